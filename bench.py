@@ -1,0 +1,351 @@
+#!/usr/bin/env python
+"""Benchmark: exact k-means assign throughput (and train time) on B200.
+
+Workload: 200,000 x 768 f32 unit rows from a 4,096-component
+Gaussian mixture (means N(0, I), noise sigma 0.5, Zipf(1.1) weights), k = 1024
+centroids, squared-L2 metric, exact FP32 labels. The centroids are the result
+of training on rank 0's rows with the engine's device loop (seed 0), so the
+assign sees trained geometry. One step = one full assign pass over a GPU's
+200,000 rows (``Device::top1`` preceded by the centroid norms, as
+``core::assign_on`` does). With N GPUs every rank assigns its own 200,000-row
+shard against the replicated centroids: weak scaling, no collective on the
+data path.
+
+Reported:
+- value: rows assigned per second over all ranks (Grows/s), device-resident
+  inputs, CUDA events on the engine's stream, max over ranks;
+- e2e: the same through ``eb_assign`` (Assigner::assign) with pinned host
+  rows/centroids in and labels/scores out, copies inside the timed region;
+- roofline of the top-1 op (2 rows k d flops per pass) against the measured
+  dense peak, cpu_baseline (the C++ oracle port of the reference CPU kernel on
+  this host's cores, bounded sample), train_s (C2 training, 1 GPU), clocks.
+
+``--impl reference`` times the reference CPU path (the oracle port; the Rust
+reference cannot be built here) on the same workload, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "assign Grows/s & k-means train s (200k×768 f32, k=1024) at 1/2/4/8 B200"
+FALLBACK_PEAK_TFLOPS = 1590.0
+
+
+def gen_rows(n, d, seed_rows, components=4096, sigma=0.5, zipf=1.1, seed_means=0):
+    """Config-2 rows: Zipf-weighted Gaussian mixture, unit-normalised."""
+    means = np.random.default_rng(seed_means).standard_normal((components, d), dtype=np.float32)
+    w = 1.0 / np.arange(1, components + 1, dtype=np.float64) ** zipf
+    rng = np.random.default_rng(1000 + seed_rows)
+    comp = rng.choice(components, n, p=w / w.sum())
+    x = means[comp]
+    x += np.float32(sigma) * rng.standard_normal((n, d), dtype=np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    return np.ascontiguousarray(x, dtype=np.float32)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return j.get("bf16_tflops", FALLBACK_PEAK_TFLOPS), "MEASURED_PEAKS.json bf16_tflops (burst)"
+    return FALLBACK_PEAK_TFLOPS, "fallback 1.59 PFLOP/s (no MEASURED_PEAKS.json)"
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    Q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 6:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if r[2 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def dist_setup(gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != gpus:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}: launch N>1 under torchrun")
+    return world, rank, local
+
+
+def cpu_baseline(x, d, cent, budget_s=8.0, chunk=16384):
+    """The oracle port of the reference CPU kernel on this host's cores."""
+    import oracle
+
+    threads = os.cpu_count() or 1
+    done, t0 = 0, time.perf_counter()
+    n = x.shape[0]
+    while done < n and time.perf_counter() - t0 < budget_s:
+        e = min(done + chunk, n)
+        oracle.top1(x[done:e].ravel(), d, cent.ravel(), oracle.L2, threads=threads)
+        done = e
+    dt = time.perf_counter() - t0
+    return {"value": done / dt / 1e9, "unit": "Grows/s", "cores": threads, "kind": "port",
+            "sample": f"first {done} of {n} rows (exact FP32 L2 top-1, k={cent.shape[0]}), "
+                      f"{dt:.1f} s, oracle/oracle.cpp AVX2+FMA, {threads} threads"}
+
+
+def run_reference(args):
+    """--impl reference: the reference CPU path (oracle port) on the host cores."""
+    world, rank, _ = dist_setup(args.gpus) if args.gpus > 1 else (1, 0, 0)
+    if rank != 0:
+        return
+    import oracle
+
+    n, d, k = args.n, args.d, args.k
+    x = gen_rows(n, d, 0)
+    cent = x[np.random.default_rng(0).permutation(n)[:k]]
+    threads = os.cpu_count() or 1
+    sample = args.ref_rows
+    for _ in range(args.warmup):
+        oracle.top1(x[:sample].ravel(), d, cent.ravel(), oracle.L2, threads=threads)
+    times = []
+    for s in range(args.steps):
+        lo = (s * sample) % (n - sample + 1)
+        t0 = time.perf_counter()
+        oracle.top1(x[lo:lo + sample].ravel(), d, cent.ravel(), oracle.L2, threads=threads)
+        times.append(time.perf_counter() - t0)
+    t = sum(times)
+    v = sample * args.steps / t / 1e9
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "Grows/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"C2 assign, bounded sample of {sample} rows per step",
+                   "rows": n, "d": d, "k": k, "metric": "L2"},
+        "cpu_baseline": {"value": v, "unit": "Grows/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample} rows x {args.steps} steps (oracle/oracle.cpp, "
+                                   "the reference cpu-fused float order; Rust reference not "
+                                   "buildable here: no cargo)"},
+        "e2e": {"value": v, "unit": "Grows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(args):
+    import torch
+
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    import emeans_b200 as eb
+
+    n, d, k = args.n, args.d, args.k
+    eng = eb.Engine(local)
+    stream = torch.cuda.ExternalStream(eng.stream())
+
+    # Centroids: train on the shared config-2 rows (identical on every rank).
+    xtrain = gen_rows(n, d, 0)
+    cfg = eb.Config(d=d, k=k, seed=0, spherical=False)
+    train_s = None
+    if not args.no_train:
+        eng.train(xtrain, cfg)  # warm-up run
+        t0 = time.perf_counter()
+        tr = eng.train(xtrain, cfg)
+        train_s = time.perf_counter() - t0
+        cent = tr.centroids
+    else:
+        cent = xtrain[np.random.default_rng(0).permutation(n)[:k]]
+    x = xtrain if rank == 0 else gen_rows(n, d, rank)
+
+    # ---- device-resident assign
+    xb = eng.bind(x, d)
+    cb = eng.upload_f32(cent)
+    cn = eng.zeros_f32(k)
+    lab = eng.zeros_u32(n)
+    sco = eng.zeros_f32(n)
+    rows = range(0, n)
+
+    def step(ev=None):
+        eng.row_norms(cb, k, d, cn)
+        if ev:
+            ev[0].record(stream)
+        eng.top1(xb, d, None, rows, cb, cn, k, eb.L2, lab, sco)
+        if ev:
+            ev[1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    eng.sync()
+    if dist:
+        dist.barrier()
+    launches0 = eng.stats()["kernel_launches"]
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        start.record(stream)
+        for s in range(args.steps):
+            step(kev[s])
+        end.record(stream)
+        end.synchronize()
+    eng.sync()
+    launches = eng.stats()["kernel_launches"] - launches0
+    ms = start.elapsed_time(end)
+    top1_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    stats = eng.stats()
+    if dist:
+        t = torch.tensor([ms, top1_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, top1_ms = t.tolist()
+        dist.barrier()
+
+    # ---- end to end through Assigner::assign (eb_assign), pinned host buffers
+    hx = torch.from_numpy(x).pin_memory()
+    hc = torch.from_numpy(np.ascontiguousarray(cent)).pin_memory()
+    hl = torch.empty(n, dtype=torch.int32).pin_memory()
+    hs = torch.empty(n, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        eng.assign_ptr(hx.data_ptr(), n, d, hc.data_ptr(), k, eb.L2, hl.data_ptr(),
+                       hs.data_ptr())
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = t.item()
+        dist.barrier()
+    # The e2e labels must equal the device-resident ones.
+    assert np.array_equal(hl.numpy().view(np.uint32), lab.read()), "e2e labels differ"
+
+    if rank == 0:
+        peak, peak_src = peaks()
+        flops = 2.0 * n * k * d
+        achieved = flops / (top1_ms * 1e-3) / 1e12
+        total_rows = n * world * args.steps
+        out = {
+            "metric": METRIC,
+            "value": total_rows / (ms * 1e-3) / 1e9,
+            "unit": "Grows/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C2 final assign: 200,000 x 768 f32 rows per GPU vs k=1024 "
+                                   "trained centroids, squared L2, exact FP32 labels+scores",
+                       "rows_per_gpu": n, "d": d, "k": k, "metric": "L2",
+                       "l2_flush": "inputs larger than L2 (rows are 614 MB per GPU)",
+                       "parallelism": f"rows sharded over {world} GPU(s), centroids replicated",
+                       "engine": eng.name()},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                         "kernel": "top-1 op (all its kernels), 2*rows*k*d useful flops",
+                         "peak_source": peak_src, "top1_ms": top1_ms},
+            "e2e": {"value": n * world * args.steps / e2e_s / 1e9, "unit": "Grows/s",
+                    "h2d_bytes_per_step": n * d * 4 + k * d * 4,
+                    "d2h_bytes_per_step": n * 8},
+            "gpu_launches": launches,
+            "screen_stats": stats,
+        }
+        if train_s is not None:
+            out["train_s"] = {"value": train_s, "unit": "s", "n_gpus": 1,
+                              "steps": tr.total_steps, "batch_size": tr.batch_size,
+                              "final_obj": tr.obj[-1]}
+        out["clocks"] = clk.summary()
+        if world == 1 and not args.no_cpu:
+            out["cpu_baseline"] = cpu_baseline(x, d, cent)
+        print(json.dumps(out), flush=True)
+    del xb, cb, cn, lab, sco
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n", type=int, default=200_000)
+    ap.add_argument("--d", type=int, default=768)
+    ap.add_argument("--k", type=int, default=1024)
+    ap.add_argument("--ref-rows", type=int, default=32768)
+    ap.add_argument("--no-train", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

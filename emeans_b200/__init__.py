@@ -1,0 +1,457 @@
+"""emeans_b200: the emeans hot path on B200 (sm_100a), from Python.
+
+A ctypes layer over libemeans_b200.so (the C ABI in include/emeans_b200.h).
+It mirrors the reference's interfaces for this path:
+
+- :class:`Engine` is the layer-1 op contract ``trait Device``
+  (crates/emeans-core/src/core/mod.rs:71-178): buffers, ``top1``, ``topk``,
+  ``scatter_add``, ``row_norms``, ``normalize_rows``, ``split``,
+  ``ema_update``; plus ``train`` (``Engine::run_train``, the device loop of
+  core/train.rs) and ``assign`` (``Assigner::assign``).
+- :class:`B200Assigner` is ``trait Assigner`` (crates/emeans-core/src/assign.rs:71-117),
+  the object ``make_assigner(Backend::Cuda)`` returns
+  (crates/emeans-cluster/src/backend.rs:126-133).
+- :func:`knn_self` / :func:`knn` follow crates/emeans-cluster/src/knn.rs:17-64.
+
+There is no CPU fallback: without the built library or a B200 the calls
+raise.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+import os
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+
+__all__ = ["Engine", "Buffer", "B200Assigner", "EngineError", "Config", "Trained",
+           "knn", "knn_self", "L2", "IP", "lib_path", "load"]
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_NAME = "libemeans_b200.so"
+
+L2, IP = 0, 1
+F32, U32 = 0, 1
+OK, INVALID_ARGUMENT, ERROR, INTERNAL = 0, 1, 2, 3
+NONE_ID = 0xFFFFFFFF
+GPU_KMAX = 16
+
+_lib = None
+
+
+class EngineError(RuntimeError):
+    """A non-OK status from the engine; ``code`` is the EB_* status."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{ {1: 'INVALID_ARGUMENT', 2: 'ERROR', 3: 'INTERNAL'}.get(code, code)}] {msg}")
+        self.code = code
+
+
+class Stats(C.Structure):
+    _fields_ = [("screened_rows", C.c_uint64), ("fallback_rows", C.c_uint64),
+                ("rescored_candidates", C.c_uint64), ("exact_rows", C.c_uint64),
+                ("kernel_launches", C.c_uint64)]
+
+
+class TrainJob(C.Structure):
+    _fields_ = [
+        ("x", C.c_void_p), ("n", C.c_size_t), ("d", C.c_size_t), ("k", C.c_size_t),
+        ("nepochs", C.c_double), ("batch_law", C.c_int32), ("spherical", C.c_int32),
+        ("batch_size", C.c_int64), ("alpha0", C.c_double), ("unused_threshold", C.c_double),
+        ("seed", C.c_uint32), ("capture", C.c_int32), ("chunk", C.c_int64),
+        ("init", C.c_void_p), ("state_positions", C.c_void_p), ("state_usage", C.c_void_p),
+        ("verbose", C.c_int32),
+    ]
+
+
+class TrainOut(C.Structure):
+    _fields_ = [
+        ("centroids", C.c_void_p), ("positions", C.c_void_p), ("usage", C.c_void_p),
+        ("labels", C.c_void_p), ("obj", C.c_double * 64), ("imbalance", C.c_double * 64),
+        ("nsplit", C.c_int64 * 64), ("epoch_time", C.c_double * 64), ("n_epochs", C.c_int32),
+        ("n_splits", C.c_int64), ("batch_size", C.c_int64), ("alpha0", C.c_double),
+        ("total_steps", C.c_int64),
+    ]
+
+
+def lib_path() -> str:
+    return os.path.join(HERE, _LIB_NAME)
+
+
+def load():
+    """Load libemeans_b200.so; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = lib_path()
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: build it with `python -m emeans_b200.build` "
+                           "(nvcc, sm_100a); there is no CPU fallback")
+    lib = C.CDLL(path)
+    P, S, I = C.c_void_p, C.c_size_t, C.c_int
+    sig = {
+        "eb_last_error": (C.c_char_p, []),
+        "eb_version": (C.c_char_p, []),
+        "eb_engine_create": (I, [I, C.POINTER(P)]),
+        "eb_engine_destroy": (I, [P]),
+        "eb_engine_name": (I, [P, C.c_char_p, S]),
+        "eb_flush": (I, [P]),
+        "eb_sync": (I, [P]),
+        "eb_get_stats": (I, [P, C.POINTER(Stats)]),
+        "eb_engine_stream": (I, [P, C.POINTER(P)]),
+        "eb_buf_alloc": (I, [P, I, S, C.POINTER(P)]),
+        "eb_buf_wrap": (I, [P, I, P, S, C.POINTER(P)]),
+        "eb_buf_free": (I, [P, P]),
+        "eb_buf_len": (S, [P]),
+        "eb_buf_ptr": (P, [P]),
+        "eb_buf_write": (I, [P, P, S, P, S]),
+        "eb_buf_read": (I, [P, P, S, S, P]),
+        "eb_buf_upload": (I, [P, I, P, S, C.POINTER(P)]),
+        "eb_bind": (I, [P, P, S, S, C.POINTER(P)]),
+        "eb_top1": (I, [P, P, S, P, S, S, P, P, S, I, P, P]),
+        "eb_topk": (I, [P, P, S, P, S, S, S, I, P, P]),
+        "eb_scatter_add": (I, [P, P, S, P, S, S, P, S, P, P, P]),
+        "eb_row_norms": (I, [P, P, S, S, P]),
+        "eb_normalize_rows": (I, [P, P, S, S, P]),
+        "eb_split": (I, [P, P, P, P, S, S]),
+        "eb_ema_update": (I, [P, P, P, P, P, S, S, C.c_float, C.c_float, I]),
+        "eb_bind_data": (I, [P, P, S, S]),
+        "eb_unbind_data": (I, [P]),
+        "eb_assign": (I, [P, P, S, S, P, S, P, S, I, P, P]),
+        "eb_train": (I, [P, C.POINTER(TrainJob), C.POINTER(TrainOut)]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def _check(rc: int):
+    if rc != OK:
+        raise EngineError(rc, load().eb_last_error().decode())
+
+
+def _ptr(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _u32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.uint32)
+
+
+class Buffer:
+    """An engine buffer (``Device::F`` / ``Device::U``); freed with the object."""
+
+    def __init__(self, engine: "Engine", handle, dtype: int, owner=None):
+        self.engine = engine
+        self.h = handle
+        self.dtype = dtype
+        self._owner = owner  # keeps wrapped memory alive
+
+    def __len__(self) -> int:
+        return load().eb_buf_len(self.h)
+
+    @property
+    def ptr(self) -> int:
+        return load().eb_buf_ptr(self.h) or 0
+
+    def read(self, lo: int = 0, hi: Optional[int] = None) -> np.ndarray:
+        """``Device::read_f32/u32``: waits for queued work."""
+        hi = len(self) if hi is None else hi
+        out = np.empty(max(hi - lo, 0), np.float32 if self.dtype == F32 else np.uint32)
+        _check(load().eb_buf_read(self.engine.h, self.h, lo, hi, _ptr(out)))
+        return out
+
+    def write(self, offset: int, values) -> None:
+        """``Device::write_f32/u32``."""
+        v = _f32(values) if self.dtype == F32 else _u32(values)
+        _check(load().eb_buf_write(self.engine.h, self.h, offset, _ptr(v), v.size))
+
+    def free(self) -> None:
+        if self.h and self.engine.h:
+            load().eb_buf_free(self.engine.h, self.h)
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+@dataclass
+class Config:
+    """The training inputs of ``model::Config`` (crates/emeans-core/src/model.rs:23-67)."""
+    d: int
+    k: int
+    nepochs: float = 5.0
+    batch_size: Optional[int] = None
+    alpha0: Optional[float] = None
+    batch_law: str = "auto"
+    seed: int = 1234
+    spherical: bool = False
+    unused_threshold: Optional[float] = None
+    assignment_chunk_size: Optional[int] = None
+    capture_assignments: bool = True
+    verbose: bool = False
+
+
+@dataclass
+class Trained:
+    """``core::train::Outcome`` (core/train.rs:51-58) with the epoch statistics."""
+    centroids: np.ndarray
+    positions: np.ndarray
+    usage: np.ndarray
+    labels: Optional[np.ndarray]
+    obj: list = field(default_factory=list)
+    imbalance: list = field(default_factory=list)
+    nsplit: list = field(default_factory=list)
+    epoch_time: list = field(default_factory=list)
+    n_splits: int = 0
+    batch_size: int = 0
+    alpha0: float = 0.0
+    total_steps: int = 0
+
+
+_LAWS = {"auto": 0, "throughput": 1, "quality": 2}
+
+
+class Engine:
+    """One engine (stream, scratch, bound data) on one CUDA device."""
+
+    def __init__(self, device: int = 0):
+        lib = load()
+        h = C.c_void_p()
+        _check(lib.eb_engine_create(device, C.byref(h)))
+        self.h = h.value
+        self.device = device
+
+    def close(self):
+        if getattr(self, "h", None):
+            load().eb_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # ---- engine
+    def name(self) -> str:
+        buf = C.create_string_buffer(64)
+        _check(load().eb_engine_name(self.h, buf, 64))
+        return buf.value.decode()
+
+    def sync(self):
+        _check(load().eb_sync(self.h))
+
+    def flush(self):
+        _check(load().eb_flush(self.h))
+
+    def stream(self) -> int:
+        """The engine's cudaStream_t, for torch.cuda.ExternalStream and events."""
+        s = C.c_void_p()
+        _check(load().eb_engine_stream(self.h, C.byref(s)))
+        return s.value or 0
+
+    def stats(self) -> dict:
+        s = Stats()
+        _check(load().eb_get_stats(self.h, C.byref(s)))
+        return {f: getattr(s, f) for f, _ in Stats._fields_}
+
+    # ---- buffers (Device::bind/upload/zeros)
+    def _new(self, fn, *args, dtype=F32, owner=None) -> Buffer:
+        h = C.c_void_p()
+        _check(fn(self.h, *args, C.byref(h)))
+        return Buffer(self, h.value, dtype, owner)
+
+    def zeros_f32(self, n: int) -> Buffer:
+        return self._new(load().eb_buf_alloc, F32, n, dtype=F32)
+
+    def zeros_u32(self, n: int) -> Buffer:
+        return self._new(load().eb_buf_alloc, U32, n, dtype=U32)
+
+    def upload_f32(self, v) -> Buffer:
+        v = _f32(v).ravel()
+        return self._new(load().eb_buf_upload, F32, _ptr(v), v.size, dtype=F32)
+
+    def upload_u32(self, v) -> Buffer:
+        v = _u32(v).ravel()
+        return self._new(load().eb_buf_upload, U32, _ptr(v), v.size, dtype=U32)
+
+    def bind(self, x, d: int) -> Buffer:
+        x = _f32(x).ravel()
+        return self._new(load().eb_bind, _ptr(x), x.size // d, d, dtype=F32)
+
+    def wrap(self, tensor) -> Buffer:
+        """A non-owning view of a torch CUDA tensor (float32 or int32/uint32)."""
+        import torch
+
+        assert tensor.is_cuda and tensor.is_contiguous()
+        dtype = F32 if tensor.dtype == torch.float32 else U32
+        assert tensor.dtype in (torch.float32, torch.int32, torch.uint32)
+        return self._new(load().eb_buf_wrap, dtype, tensor.data_ptr(), tensor.numel(), dtype=dtype,
+                         owner=tensor)
+
+    # ---- layer-1 ops (trait Device)
+    def top1(self, x: Buffer, d: int, ids: Optional[Buffer], rows: range, centroids: Buffer,
+             cnorm: Optional[Buffer], k: int, metric: int, labels: Buffer, scores: Buffer):
+        _check(load().eb_top1(self.h, x.h, d, ids.h if ids else None, rows.start, rows.stop,
+                              centroids.h, cnorm.h if cnorm else None, k, metric, labels.h,
+                              scores.h))
+
+    def topk(self, queries, data, d: int, kk: int, exclude_self: bool = False):
+        q, x = _f32(queries).ravel(), _f32(data).ravel()
+        m, n = q.size // d, x.size // d
+        ids = np.empty(m * kk, np.uint32)
+        sims = np.empty(m * kk, np.float32)
+        _check(load().eb_topk(self.h, _ptr(q), m, _ptr(x), n, d, kk, int(exclude_self),
+                              _ptr(ids), _ptr(sims)))
+        return ids, sims
+
+    def scatter_add(self, x: Buffer, d: int, ids: Optional[Buffer], rows: range, labels: Buffer,
+                    k: int, sums: Buffer, counts: Buffer, acc: Optional[Buffer] = None):
+        _check(load().eb_scatter_add(self.h, x.h, d, ids.h if ids else None, rows.start,
+                                     rows.stop, labels.h, k, sums.h, counts.h,
+                                     acc.h if acc else None))
+
+    def row_norms(self, m: Buffer, rows: int, d: int, out: Buffer):
+        _check(load().eb_row_norms(self.h, m.h, rows, d, out.h))
+
+    def normalize_rows(self, src: Buffer, rows: int, d: int, dst: Buffer):
+        _check(load().eb_normalize_rows(self.h, src.h, rows, d, dst.h))
+
+    def split(self, positions: Buffer, usage: Buffer, plan: Sequence, d: int):
+        p = _u32(np.asarray(plan, dtype=np.uint32).reshape(-1))
+        _check(load().eb_split(self.h, positions.h, usage.h, _ptr(p), p.size // 2, d))
+
+    def ema_update(self, positions: Buffer, usage: Buffer, sums: Buffer, counts: Buffer, k: int,
+                   d: int, alpha: float):
+        """``Device::ema_update`` with ``EmaStep::new(alpha)`` (core/mod.rs:189-197)."""
+        a32 = np.float32(alpha)
+        decay = np.float32(1.0 - alpha)
+        _check(load().eb_ema_update(self.h, positions.h, usage.h, sums.h, counts.h, k, d,
+                                    float(a32), float(decay), int(alpha == 1.0)))
+
+    # ---- Assigner::assign and the device loop
+    def assign(self, rows, d: int, centroids, metric: int, ids=None):
+        x = _f32(rows).ravel()
+        c = _f32(centroids).ravel()
+        n, k = x.size // d, c.size // d
+        idv = None if ids is None else _u32(ids).ravel()
+        m = n if idv is None else idv.size
+        labels = np.empty(m, np.uint32)
+        scores = np.empty(m, np.float32)
+        _check(load().eb_assign(self.h, _ptr(x), n, d, _ptr(idv), m, _ptr(c), k, metric,
+                                _ptr(labels), _ptr(scores)))
+        return labels, scores
+
+    def assign_ptr(self, x_ptr: int, n: int, d: int, c_ptr: int, k: int, metric: int,
+                   labels_ptr: int, scores_ptr: int):
+        """``eb_assign`` on caller-owned host memory (pinned buffers for the e2e bench)."""
+        _check(load().eb_assign(self.h, x_ptr, n, d, None, n, c_ptr, k, metric, labels_ptr,
+                                scores_ptr))
+
+    def bind_data(self, data, d: int):
+        x = _f32(data).ravel()
+        self._bound = x  # the host copy that indexed assign calls compare against
+        _check(load().eb_bind_data(self.h, _ptr(x), x.size // d, d))
+        return x
+
+    def unbind_data(self):
+        _check(load().eb_unbind_data(self.h))
+        self._bound = None
+
+    def train(self, x, cfg: Config, init=None, state=None) -> Trained:
+        """``Engine::run_train``: the device loop (core/train.rs:60-303)."""
+        x = _f32(x).ravel()
+        d, k = cfg.d, cfg.k
+        n = x.size // d
+        cent = np.empty(k * d, np.float32)
+        pos = np.empty(k * d, np.float32)
+        usage = np.empty(k, np.float32)
+        labels = np.empty(n, np.int32) if cfg.capture_assignments else None
+        init_a = None if init is None else _f32(init).ravel()
+        sp = su = None
+        if state is not None:
+            sp, su = _f32(state[0]).ravel(), _f32(state[1]).ravel()
+        job = TrainJob(x=_ptr(x), n=n, d=d, k=k, nepochs=float(cfg.nepochs),
+                       batch_law=_LAWS[cfg.batch_law], spherical=int(cfg.spherical),
+                       batch_size=cfg.batch_size or 0,
+                       alpha0=math.nan if cfg.alpha0 is None else float(cfg.alpha0),
+                       unused_threshold=math.nan if cfg.unused_threshold is None
+                       else float(cfg.unused_threshold),
+                       seed=cfg.seed, capture=int(cfg.capture_assignments),
+                       chunk=cfg.assignment_chunk_size or 0, init=_ptr(init_a),
+                       state_positions=_ptr(sp), state_usage=_ptr(su), verbose=int(cfg.verbose))
+        out = TrainOut(centroids=_ptr(cent), positions=_ptr(pos), usage=_ptr(usage),
+                       labels=_ptr(labels))
+        _check(load().eb_train(self.h, C.byref(job), C.byref(out)))
+        ne = out.n_epochs
+        return Trained(centroids=cent.reshape(k, d), positions=pos.reshape(k, d), usage=usage,
+                       labels=labels, obj=list(out.obj[:ne]), imbalance=list(out.imbalance[:ne]),
+                       nsplit=list(out.nsplit[:ne]), epoch_time=list(out.epoch_time[:ne]),
+                       n_splits=out.n_splits, batch_size=out.batch_size, alpha0=out.alpha0,
+                       total_steps=out.total_steps)
+
+
+class B200Assigner:
+    """``trait Assigner`` (crates/emeans-core/src/assign.rs:71-117) on the engine."""
+
+    def __init__(self, device: int = 0):
+        self.engine = Engine(device)
+        self._bound = None
+
+    def name(self) -> str:
+        return self.engine.name()
+
+    def bind_data(self, data, d: int):
+        self._bound = self.engine.bind_data(data, d)
+
+    def unbind_data(self):
+        self.engine.unbind_data()
+        self._bound = None
+
+    def with_engine(self, f):
+        return f(self.engine)
+
+    def assign(self, rows, d: int, centroids, metric: int, ids=None):
+        if ids is not None and self._bound is not None and rows is not None and \
+                np.asarray(rows).size == self._bound.size:
+            rows = self._bound
+        return self.engine.assign(rows, d, centroids, metric, ids=ids)
+
+
+def _search(queries, data, d, k, exclude_self, engine=None):
+    if k < 1 or k > GPU_KMAX:
+        raise ValueError(f"k must be 1..={GPU_KMAX} on the B200 engine")
+    eng = engine or Engine(0)
+    ids, sims = eng.topk(queries, data, d, k, exclude_self)
+    m = ids.size // k
+    return ids.reshape(m, k), sims.reshape(m, k)
+
+
+def knn_self(data, d: int, k: int, engine: Optional[Engine] = None):
+    """Neighbours of every row among the other rows (knn.rs:17-19)."""
+    return _search(data, data, d, k, True, engine)
+
+
+def knn(queries, data, d: int, k: int, engine: Optional[Engine] = None):
+    """Neighbours of every query row among the data rows (knn.rs:21-29)."""
+    return _search(queries, data, d, k, False, engine)

@@ -1,0 +1,154 @@
+// Internal declarations shared by the engine's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdio>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/emeans_b200.h"
+
+namespace eb {
+
+// An error that becomes a status code at the C ABI edge.
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+inline void ensure(bool ok, const std::string& msg) {
+  if (!ok) throw Error(EB_INVALID_ARGUMENT, msg);
+}
+
+inline void cuda_check(cudaError_t st, const char* what) {
+  if (st != cudaSuccess)
+    throw Error(EB_ERROR, std::string(what) + ": " + cudaGetErrorString(st));
+}
+#define EB_CUDA(x) ::eb::cuda_check((x), #x)
+// After every kernel launch: check the launch and count it (eb_stats).
+#define EB_LAUNCH(what)                              \
+  do {                                               \
+    ::eb::cuda_check(cudaGetLastError(), what);      \
+    e->stats.kernel_launches++;                      \
+  } while (0)
+
+// Device-side error flags (a word in device memory; read by the next sync).
+enum : uint32_t {
+  ST_BAD_LABEL = 1u,
+  ST_BAD_ROW = 2u,
+  ST_WAIT_TIMEOUT = 4u,
+};
+
+// A grow-only device scratch slot.
+struct Scratch {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+
+struct Fp16Copy;  // FP16 screen copy of a bound data set (top1_tc.cu)
+
+}  // namespace eb
+
+struct eb_buf {
+  void* ptr = nullptr;
+  size_t len = 0;
+  int dtype = EB_F32;
+  bool owned = false;
+  // Bumped by every host write; caches derived from the buffer compare it.
+  uint64_t version = 0;
+  // For bound data sets: d, the rows' squared norms (CPU float order) and the
+  // FP16 screen copy.
+  size_t d = 0;
+  float* xnorm = nullptr;
+  eb::Fp16Copy* f16 = nullptr;
+};
+
+struct eb_engine {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  uint32_t* d_status = nullptr;  // device error flags
+  uint32_t* h_status = nullptr;  // pinned mirror
+  std::unordered_map<std::string, eb::Scratch> scratch;
+  eb_stats stats{};
+  // Assigner::bind_data state.
+  eb_buf* bound = nullptr;
+  const float* bound_host = nullptr;
+  size_t bound_n = 0;
+  int num_sms = 148;
+  bool tc_enabled = true;  // tensor-core screen for top-1 (EMEANS_B200_SCREEN=0 turns it off)
+
+  template <class T>
+  T* scratch_get(const char* name, size_t count) {
+    auto& s = scratch[name];
+    size_t bytes = count * sizeof(T);
+    if (bytes == 0) bytes = 16;
+    if (s.bytes < bytes) {
+      if (s.p) EB_CUDA(cudaFreeAsync(s.p, stream));
+      size_t want = bytes + bytes / 4;
+      EB_CUDA(cudaMallocAsync(&s.p, want, stream));
+      s.bytes = want;
+    }
+    return static_cast<T*>(s.p);
+  }
+};
+
+namespace eb {
+
+eb_buf* new_buf(eb_engine* e, int dtype, size_t len);
+void free_buf(eb_engine* e, eb_buf* b);
+void sync(eb_engine* e);  // wait + status check (throws)
+void set_last_error(const std::string& msg);
+
+// ---- ops.cu: update ops, bit-equal to the CPU float order
+void row_norms(eb_engine* e, const float* m, size_t rows, size_t d, float* out);
+// Squared norms of the selected rows x[ids[p]] (or x[p]) for p in r0..r1,
+// written at out[p - r0].
+void sel_row_norms(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids,
+                   size_t r0, size_t r1, float* out);
+void normalize_rows(eb_engine* e, const float* src, size_t rows, size_t d, float* dst);
+void ema_update(eb_engine* e, float* pos, float* usage, const float* sums, const uint32_t* counts,
+                size_t k, size_t d, float alpha, float decay, bool replace);
+void split(eb_engine* e, float* pos, float* usage, const uint32_t* d_pairs, size_t npairs,
+           size_t d);
+void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids, size_t r0,
+                 size_t r1, const uint32_t* labels, size_t k, float* sums, uint32_t* counts,
+                 float* acc);
+
+// ---- top1_exact.cu: the exact FP32 SIMT kernels
+struct Top1Args {
+  const float* x;      // n x d
+  size_t n, d;
+  const uint32_t* ids; // selection ids or null
+  size_t r0, r1;       // positions
+  const float* c;      // k x d
+  const float* cnorm;  // k (L2)
+  size_t k;
+  int metric;
+  uint32_t* labels;    // indexed by position
+  float* scores;
+  const float* xnorm;  // squared norms by data row (L2), or null: computed
+};
+// Full exact scan of every selected row.
+void top1_exact(eb_engine* e, const Top1Args& a);
+// Full exact scan of the positions listed in list[0..*count) (device count).
+void top1_exact_list(eb_engine* e, const Top1Args& a, const uint32_t* list,
+                     const uint32_t* count, size_t max_count);
+
+// Screen when the tensor-core path supports the call, else the exact kernel.
+void top1_dispatch(eb_engine* e, const Top1Args& a, eb_buf* xbuf);
+
+// ---- top1_tc.cu: the tcgen05 screen + exact re-score
+bool top1_screen_supported(eb_engine* e, const Top1Args& a);
+void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf);
+void drop_f16(eb_buf* b);
+
+// ---- topk.cu
+void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, size_t d,
+          size_t kk, bool exclude_self, uint32_t* ids, float* sims);
+
+}  // namespace eb

@@ -1,0 +1,327 @@
+// The update ops of the hot path: row norms, normalisation, the EMA step,
+// revival splits and the deterministic scatter-add. Each is bit-equal to the
+// reference CPU float order (crates/emeans-core/src/core/cpu.rs): every
+// rounding is spelled with an explicit __f*_rn intrinsic, so no FMA
+// contraction can change a bit, and sums run in the reference's order.
+#include <cuda_runtime.h>
+
+#include "engine.h"
+
+namespace eb {
+namespace {
+
+constexpr int kRowThreads = 64;
+
+// Sequential sum of rounded squares of one row, in column order
+// (assign.rs:150-155: `r.iter().map(|v| v * v).sum()`).
+__device__ __forceinline__ float row_sumsq(const float* __restrict__ r, int d) {
+  float s = -0.0f;
+  if ((d & 3) == 0 && ((uintptr_t)r & 15) == 0) {
+    const float4* r4 = reinterpret_cast<const float4*>(r);
+    for (int q = 0; q < d / 4; q++) {
+      float4 v = __ldg(r4 + q);
+      s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+      s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+      s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+      s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+    }
+  } else {
+    for (int t = 0; t < d; t++) {
+      float v = __ldg(r + t);
+      s = __fadd_rn(s, __fmul_rn(v, v));
+    }
+  }
+  return s;
+}
+
+__global__ void k_row_sumsq(const float* __restrict__ m, long rows, int d, float* __restrict__ out) {
+  long r = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < rows) out[r] = row_sumsq(m + r * d, d);
+}
+
+__global__ void k_sel_sumsq(const float* __restrict__ x, long n, int d,
+                            const uint32_t* __restrict__ ids, long r0, long r1,
+                            float* __restrict__ out, uint32_t* status) {
+  long p = r0 + (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= r1) return;
+  long row = ids ? (long)ids[p] : p;
+  if (row >= n) {
+    atomicOr(status, ST_BAD_ROW);
+    out[p - r0] = 0.0f;
+    return;
+  }
+  out[p - r0] = row_sumsq(x + row * d, d);
+}
+
+// faiss normalize_into for one row per thread (core/cpu.rs:219-230):
+// divide by max |v| (zero rows keep 1), then by sqrt of the sequential sum of
+// squares of the scaled row.
+__global__ void k_normalize(const float* __restrict__ src, long rows, int d, float* __restrict__ dst) {
+  long r = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const float* a = src + r * d;
+  float mx = 0.0f;
+  for (int t = 0; t < d; t++) mx = fmaxf(mx, fabsf(a[t]));
+  float s = mx > 0.0f ? mx : 1.0f;
+  float ss = -0.0f;
+  for (int t = 0; t < d; t++) {
+    float u = __fdiv_rn(a[t], s);
+    ss = __fadd_rn(ss, __fmul_rn(u, u));
+  }
+  float nrm = __fsqrt_rn(ss);
+  float s2 = nrm > 0.0f ? nrm : 1.0f;
+  float* o = dst + r * d;
+  for (int t = 0; t < d; t++) o[t] = __fdiv_rn(__fdiv_rn(a[t], s), s2);
+}
+
+// The EMA step, one block per centroid (core/cpu.rs:389-432).
+__global__ void k_ema(float* __restrict__ pos, float* __restrict__ usage,
+                      const float* __restrict__ sums, const uint32_t* __restrict__ counts, int d,
+                      float a32, float decay, int replace) {
+  long j = blockIdx.x;
+  float u = usage[j];
+  uint32_t cnt = counts[j];
+  float ud = replace ? u : __fmul_rn(u, decay);
+  float mass = ud;
+  if (cnt != 0) {
+    float count = __uint2float_rn(cnt);
+    float retained = replace ? 0.0f : ud;
+    float step = __fmul_rn(a32, count);
+    mass = __fadd_rn(retained, step);
+    float w = __fdiv_rn(step, mass);
+    float* c = pos + j * d;
+    const float* s = sums + j * d;
+    for (int t = threadIdx.x; t < d; t += blockDim.x) {
+      float mean = __fdiv_rn(s[t], count);
+      float ct = c[t];
+      c[t] = w == 1.0f ? mean : __fadd_rn(ct, __fmul_rn(w, __fsub_rn(mean, ct)));
+    }
+  }
+  __syncthreads();  // every thread has read usage[j]
+  if (threadIdx.x == 0) usage[j] = mass;
+}
+
+// Revival splits, one block per (donor, dead) pair (core/mod.rs:374-399).
+__global__ void k_split(float* __restrict__ pos, float* __restrict__ usage,
+                        const uint32_t* __restrict__ pairs, int d) {
+  uint32_t s = pairs[2 * blockIdx.x], t = pairs[2 * blockIdx.x + 1];
+  const float eps = (float)1e-4;
+  float* cs = pos + (long)s * d;
+  float* ct = pos + (long)t * d;
+  bool same = true;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    float off = __fmul_rn(eps, (i % 2 == 0) ? 1.0f : -1.0f);
+    float c = cs[i];
+    float dn = __fmul_rn(c, __fsub_rn(1.0f, off));
+    float ch = __fmul_rn(c, __fadd_rn(1.0f, off));
+    same = same && (dn == ch);
+  }
+  int all_same = __syncthreads_and(same ? 1 : 0);
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    float off = __fmul_rn(eps, (i % 2 == 0) ? 1.0f : -1.0f);
+    float c = cs[i];
+    float dn = __fmul_rn(c, __fsub_rn(1.0f, off));
+    float ch = __fmul_rn(c, __fadd_rn(1.0f, off));
+    if (i == 0 && all_same) {
+      float up = nextafterf(ch, INFINITY);
+      ch = isfinite(up) ? up : nextafterf(ch, -INFINITY);
+    }
+    cs[i] = dn;
+    ct[i] = ch;
+  }
+  if (threadIdx.x == 0) {
+    float half = __fdiv_rn(usage[s], 2.0f);
+    usage[s] = half;
+    usage[t] = half;
+  }
+}
+
+// ---- deterministic scatter-add: a stable counting sort by label, then one
+// sequential f32 sum per (centroid, column) in selection order.
+
+constexpr int kSeg = 256;  // positions per segment (one warp ranks a segment)
+
+// In-segment stable rank of every position among positions with its label,
+// and the per-(segment, label) counts.
+__global__ void k_seg_rank(const uint32_t* __restrict__ labels, long r0, long m, uint32_t k,
+                           uint32_t* __restrict__ segcnt, uint32_t* __restrict__ rank,
+                           uint32_t* status) {
+  long seg = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  int lane = threadIdx.x & 31;
+  long segs = (m + kSeg - 1) / kSeg;
+  if (seg >= segs) return;
+  uint32_t* cnt = segcnt + seg * (long)k;
+  for (int c = 0; c < kSeg; c += 32) {
+    long p = seg * kSeg + c + lane;
+    uint32_t l = p < m ? labels[r0 + p] : 0xFFFFFFFFu;
+    bool valid = l < k;
+    if (p < m && !valid) atomicOr(status, ST_BAD_LABEL);
+    uint32_t key = valid ? l : 0xFFFFFFFFu;
+    uint32_t peers = __match_any_sync(0xFFFFFFFFu, key);
+    int leader = __ffs(peers) - 1;
+    uint32_t base = 0;
+    if (valid && lane == leader) {
+      base = cnt[l];
+      cnt[l] = base + __popc(peers);
+    }
+    base = __shfl_sync(0xFFFFFFFFu, base, leader);
+    if (valid) rank[p] = base + __popc(peers & ((1u << lane) - 1u));
+    __syncwarp();
+  }
+}
+
+// Per label: exclusive prefix of its counts over segments (in place), and
+// the label's total.
+__global__ void k_seg_scan(uint32_t* __restrict__ segcnt, long segs, uint32_t k,
+                           uint32_t* __restrict__ counts) {
+  uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
+  if (l >= k) return;
+  uint32_t run = 0;
+  for (long s = 0; s < segs; s++) {
+    uint32_t c = segcnt[s * k + l];
+    segcnt[s * k + l] = run;
+    run += c;
+  }
+  counts[l] = run;
+}
+
+// Exclusive scan of counts into start[0..k], one block.
+__global__ void k_label_scan(const uint32_t* __restrict__ counts, uint32_t k,
+                             uint32_t* __restrict__ start) {
+  __shared__ uint32_t part[1024];
+  uint32_t per = (k + blockDim.x - 1) / blockDim.x;
+  uint32_t lo = threadIdx.x * per, hi = min(lo + per, k);
+  uint32_t s = 0;
+  for (uint32_t l = lo; l < hi; l++) s += counts[l];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  for (int off = 1; off < (int)blockDim.x; off <<= 1) {
+    uint32_t v = threadIdx.x >= (unsigned)off ? part[threadIdx.x - off] : 0;
+    __syncthreads();
+    part[threadIdx.x] += v;
+    __syncthreads();
+  }
+  uint32_t run = threadIdx.x ? part[threadIdx.x - 1] : 0;
+  for (uint32_t l = lo; l < hi; l++) {
+    start[l] = run;
+    run += counts[l];
+  }
+  if (threadIdx.x == blockDim.x - 1) start[k] = part[threadIdx.x];
+}
+
+// Place every position at its sorted slot; the slot holds the data row id.
+__global__ void k_place(const uint32_t* __restrict__ labels, const uint32_t* __restrict__ ids,
+                        long r0, long m, long n, uint32_t k, const uint32_t* __restrict__ segcnt,
+                        const uint32_t* __restrict__ start, const uint32_t* __restrict__ rank,
+                        uint32_t* __restrict__ order, uint32_t* status) {
+  long p = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= m) return;
+  uint32_t l = labels[r0 + p];
+  if (l >= k) return;
+  long seg = p / kSeg;
+  uint32_t row = ids ? ids[r0 + p] : (uint32_t)(r0 + p);
+  if ((long)row >= n) {
+    atomicOr(status, ST_BAD_ROW);
+    row = 0;
+  }
+  order[start[l] + segcnt[seg * k + l] + rank[p]] = row;
+}
+
+// sums[j][t] = rows of centroid j added in selection order from +0;
+// acc[j][t] += sums[j][t]. One thread per (centroid, column).
+__global__ void k_seg_sum(const float* __restrict__ x, int d, const uint32_t* __restrict__ order,
+                          const uint32_t* __restrict__ start, float* __restrict__ sums,
+                          float* __restrict__ acc) {
+  long j = blockIdx.x;
+  int t = blockIdx.y * blockDim.x + threadIdx.x;
+  if (t >= d) return;
+  uint32_t b = start[j], e = start[j + 1];
+  float s = 0.0f;
+  uint32_t i = b;
+  for (; i + 8 <= e; i += 8) {
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) v[q] = __ldg(x + (long)order[i + q] * d + t);
+#pragma unroll
+    for (int q = 0; q < 8; q++) s = __fadd_rn(s, v[q]);
+  }
+  for (; i < e; i++) s = __fadd_rn(s, __ldg(x + (long)order[i] * d + t));
+  sums[j * d + t] = s;
+  if (acc) acc[j * d + t] = __fadd_rn(acc[j * d + t], s);
+}
+
+unsigned blocks_for(size_t n, unsigned per) { return (unsigned)((n + per - 1) / per); }
+
+}  // namespace
+
+void row_norms(eb_engine* e, const float* m, size_t rows, size_t d, float* out) {
+  if (rows == 0) return;
+  k_row_sumsq<<<blocks_for(rows, kRowThreads), kRowThreads, 0, e->stream>>>(m, (long)rows, (int)d,
+                                                                            out);
+  EB_LAUNCH("row_norms");
+}
+
+void sel_row_norms(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids,
+                   size_t r0, size_t r1, float* out) {
+  if (r1 <= r0) return;
+  k_sel_sumsq<<<blocks_for(r1 - r0, kRowThreads), kRowThreads, 0, e->stream>>>(
+      x, (long)n, (int)d, ids, (long)r0, (long)r1, out, e->d_status);
+  EB_LAUNCH("sel_row_norms");
+}
+
+void normalize_rows(eb_engine* e, const float* src, size_t rows, size_t d, float* dst) {
+  if (rows == 0) return;
+  k_normalize<<<blocks_for(rows, kRowThreads), kRowThreads, 0, e->stream>>>(src, (long)rows,
+                                                                            (int)d, dst);
+  EB_LAUNCH("normalize_rows");
+}
+
+void ema_update(eb_engine* e, float* pos, float* usage, const float* sums, const uint32_t* counts,
+                size_t k, size_t d, float alpha, float decay, bool replace) {
+  if (k == 0) return;
+  k_ema<<<(unsigned)k, 128, 0, e->stream>>>(pos, usage, sums, counts, (int)d, alpha, decay,
+                                           replace ? 1 : 0);
+  EB_LAUNCH("ema_update");
+}
+
+void split(eb_engine* e, float* pos, float* usage, const uint32_t* d_pairs, size_t npairs,
+           size_t d) {
+  if (npairs == 0) return;
+  k_split<<<(unsigned)npairs, 128, 0, e->stream>>>(pos, usage, d_pairs, (int)d);
+  EB_LAUNCH("split");
+}
+
+void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids, size_t r0,
+                 size_t r1, const uint32_t* labels, size_t k, float* sums, uint32_t* counts,
+                 float* acc) {
+  size_t m = r1 - r0;
+  size_t segs = (m + kSeg - 1) / kSeg;
+  if (segs == 0) segs = 1;
+  uint32_t* segcnt = e->scratch_get<uint32_t>("sc_segcnt", segs * k);
+  uint32_t* rank = e->scratch_get<uint32_t>("sc_rank", m ? m : 1);
+  uint32_t* start = e->scratch_get<uint32_t>("sc_start", k + 1);
+  uint32_t* order = e->scratch_get<uint32_t>("sc_order", m ? m : 1);
+  EB_CUDA(cudaMemsetAsync(segcnt, 0, segs * k * sizeof(uint32_t), e->stream));
+  if (m > 0) {
+    const int warps = 8;
+    k_seg_rank<<<blocks_for(segs, warps), warps * 32, 0, e->stream>>>(labels, (long)r0, (long)m,
+                                                                     (uint32_t)k, segcnt, rank,
+                                                                     e->d_status);
+    EB_LAUNCH("scatter rank");
+  }
+  k_seg_scan<<<blocks_for(k, 256), 256, 0, e->stream>>>(segcnt, (long)segs, (uint32_t)k, counts);
+  EB_LAUNCH("scatter seg scan");
+  k_label_scan<<<1, 1024, 0, e->stream>>>(counts, (uint32_t)k, start);
+  EB_LAUNCH("scatter label scan");
+  if (m > 0) {
+    k_place<<<blocks_for(m, 256), 256, 0, e->stream>>>(labels, ids, (long)r0, (long)m, (long)n,
+                                                       (uint32_t)k, segcnt, start, rank, order,
+                                                       e->d_status);
+    EB_LAUNCH("scatter place");
+  }
+  dim3 grid((unsigned)k, blocks_for(d, 128));
+  k_seg_sum<<<grid, 128, 0, e->stream>>>(x, (int)d, order, start, sums, acc);
+  EB_LAUNCH("scatter sum");
+}
+
+}  // namespace eb

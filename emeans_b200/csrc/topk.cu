@@ -1,0 +1,145 @@
+// Exact k-nearest rows by inner product (Device::topk, core/mod.rs:114-124):
+// every score is one sequential FMA chain over d (the top-1 float order), and
+// each query keeps the best kk by (larger score, then lower id), as knn_cpu
+// does (crates/emeans-core/src/knn.rs:53-107): a candidate enters only when
+// strictly better than the current last, so NaN and -inf never enter and
+// missing neighbours stay (0xFFFFFFFF, -inf).
+#include <cuda_runtime.h>
+
+#include "engine.h"
+
+namespace eb {
+namespace {
+
+constexpr int BM = 64, BN = 64, BK = 16, NT = 256, KMAX = 16;
+
+__global__ void __launch_bounds__(NT) k_topk_exact(const float* __restrict__ q, long m,
+                                                   const float* __restrict__ data, long n, int d,
+                                                   int kk, int exclude_self,
+                                                   uint32_t* __restrict__ out_ids,
+                                                   float* __restrict__ out_sims) {
+  __shared__ __align__(16) float As[BK][BM + 4];
+  __shared__ __align__(16) float Bs[BK][BN + 4];
+  __shared__ float S[BM][BN + 1];
+
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const long q0 = (long)blockIdx.x * BM;
+  const int lr = tid >> 2, lc = (tid & 3) * 4;
+  const bool a_live = q0 + lr < m;
+  const float* arow = q + (a_live ? q0 + lr : 0) * (long)d;
+  const bool vec = (d & 3) == 0;
+
+  // Per-query list (threads 0..63 own query q0 + tid), best first.
+  float ls[KMAX];
+  uint32_t li[KMAX];
+#pragma unroll
+  for (int i = 0; i < KMAX; i++) {
+    ls[i] = -INFINITY;
+    li[i] = 0xFFFFFFFFu;
+  }
+
+  for (long n0 = 0; n0 < n; n0 += BN) {
+    const bool b_live = n0 + lr < n;
+    const float* brow = data + (b_live ? n0 + lr : 0) * (long)d;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+    for (int k0 = 0; k0 < d; k0 += BK) {
+      float av[4], bv[4];
+      if (vec && k0 + lc + 4 <= d) {
+        float4 a4 = a_live ? __ldg(reinterpret_cast<const float4*>(arow + k0 + lc))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 b4 = b_live ? __ldg(reinterpret_cast<const float4*>(brow + k0 + lc))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        av[0] = a4.x; av[1] = a4.y; av[2] = a4.z; av[3] = a4.w;
+        bv[0] = b4.x; bv[1] = b4.y; bv[2] = b4.z; bv[3] = b4.w;
+      } else {
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+          int c = k0 + lc + t;
+          av[t] = (a_live && c < d) ? __ldg(arow + c) : 0.0f;
+          bv[t] = (b_live && c < d) ? __ldg(brow + c) : 0.0f;
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        As[lc + t][lr] = av[t];
+        Bs[lc + t][lr] = bv[t];
+      }
+      __syncthreads();
+      const int kmax = min(BK, d - k0);
+      for (int kx = 0; kx < kmax; kx++) {
+        float4 a4 = *reinterpret_cast<const float4*>(&As[kx][ty * 4]);
+        float4 b4 = *reinterpret_cast<const float4*>(&Bs[kx][tx * 4]);
+        float a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+          for (int j = 0; j < 4; j++) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) S[ty * 4 + i][tx * 4 + j] = acc[i][j];
+    __syncthreads();
+    if (tid < BM) {
+      long qi = q0 + tid;
+      int cols = (int)min((long)BN, n - n0);
+      for (int j = 0; j < cols; j++) {
+        uint32_t col = (uint32_t)(n0 + j);
+        if (exclude_self && (long)col == qi) continue;
+        float v = S[tid][j];
+        if (!(v > ls[KMAX - 1])) continue;
+        float cv = v;
+        uint32_t cj = col;
+#pragma unroll
+        for (int i = 0; i < KMAX; i++) {
+          bool b = cv > ls[i] || (cv == ls[i] && cj < li[i]);
+          float tv = ls[i];
+          uint32_t tj = li[i];
+          ls[i] = b ? cv : tv;
+          li[i] = b ? cj : tj;
+          cv = b ? tv : cv;
+          cj = b ? tj : cj;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (tid < BM && q0 + tid < m) {
+    long qi = q0 + tid;
+#pragma unroll
+    for (int i = 0; i < KMAX; i++) {
+      if (i < kk) {
+        out_ids[qi * kk + i] = li[i];
+        out_sims[qi * kk + i] = li[i] == 0xFFFFFFFFu ? -INFINITY : ls[i];
+      }
+    }
+  }
+}
+
+}  // namespace
+
+void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, size_t d,
+          size_t kk, bool exclude_self, uint32_t* ids, float* sims) {
+  float* dq = e->scratch_get<float>("tk_q", m * d);
+  float* dd = e->scratch_get<float>("tk_data", n * d);
+  uint32_t* di = e->scratch_get<uint32_t>("tk_ids", m * kk);
+  float* ds = e->scratch_get<float>("tk_sims", m * kk);
+  EB_CUDA(cudaMemcpyAsync(dq, q, m * d * 4, cudaMemcpyHostToDevice, e->stream));
+  EB_CUDA(cudaMemcpyAsync(dd, data, n * d * 4, cudaMemcpyHostToDevice, e->stream));
+  unsigned grid = (unsigned)((m + BM - 1) / BM);
+  k_topk_exact<<<grid, NT, 0, e->stream>>>(dq, (long)m, dd, (long)n, (int)d, (int)kk,
+                                           exclude_self ? 1 : 0, di, ds);
+  EB_LAUNCH("topk");
+  EB_CUDA(cudaMemcpyAsync(ids, di, m * kk * 4, cudaMemcpyDeviceToHost, e->stream));
+  EB_CUDA(cudaMemcpyAsync(sims, ds, m * kk * 4, cudaMemcpyDeviceToHost, e->stream));
+  sync(e);
+}
+
+}  // namespace eb

@@ -1,0 +1,264 @@
+// Engine::run_train on this engine: the reference device loop
+// (crates/emeans-core/src/core/train.rs:60-303), restated in C++ over the
+// engine's layer-1 ops. Per batch, queued without a host wait: readout
+// (normalize or row norms), top-1 in chunks, scatter-add (and the closing
+// sums in the last epoch), EMA. The host waits only every 5th step for the
+// masses (revival plan, MT19937 on the host), at epoch ends for the labels and
+// scores (statistics), and at the end.
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cmath>
+#include <future>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+#include "host.h"
+
+namespace eb {
+
+void top1_dispatch(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
+  if (e->tc_enabled && top1_screen_supported(e, a))
+    top1_screen(e, a, xbuf);
+  else
+    top1_exact(e, a);
+}
+
+namespace {
+
+struct DevBuf {
+  eb_engine* e;
+  eb_buf* b;
+  DevBuf(eb_engine* eng, int dtype, size_t len) : e(eng), b(new_buf(eng, dtype, len)) {}
+  ~DevBuf() { free_buf(e, b); }
+  float* f() { return static_cast<float*>(b->ptr); }
+  uint32_t* u() { return static_cast<uint32_t*>(b->ptr); }
+};
+
+void read_into(eb_engine* e, void* dst, const void* src, size_t bytes) {
+  if (bytes) EB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, e->stream));
+  sync(e);
+}
+
+struct EpochStat {
+  double obj, imbalance;
+};
+
+// Epoch statistics (train.rs:224-279): f64 objective per chunk, imbalance.
+EpochStat epoch_stats(const std::vector<uint32_t>& lab, const std::vector<float>& sc, size_t rows,
+                      size_t bsz, size_t chunk, size_t k, bool spherical,
+                      std::vector<uint64_t>& hist) {
+  double obj_epoch = 0.0;
+  for (size_t b = 0; b < rows; b += bsz) {
+    size_t e = std::min(b + bsz, rows);
+    double obj_batch = 0.0;
+    for (size_t c0 = b; c0 < e; c0 += chunk) {
+      size_t c1 = std::min(c0 + chunk, e);
+      double obj = 0.0;
+      if (spherical) {
+        obj += 2.0 * (double)(c1 - c0);
+        for (size_t i = c0; i < c1; i++) obj += (double)(-2.0f * sc[i]);
+      } else {
+        for (size_t i = c0; i < c1; i++) obj += (double)sc[i];
+      }
+      obj_batch += obj;
+    }
+    obj_epoch += obj_batch;
+  }
+  hist.assign(k, 0);
+  for (size_t i = 0; i < rows; i++) {
+    ensure(lab[i] < k, "device returned a label >= k");
+    hist[lab[i]]++;
+  }
+  double sq = 0.0;
+  for (size_t j = 0; j < k; j++) sq += (double)hist[j] * (double)hist[j];
+  return {obj_epoch, (double)k * sq / ((double)rows * (double)rows)};
+}
+
+}  // namespace
+
+void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
+  const size_t n = job->n, d = job->d, k = job->k;
+  ensure(d > 0 && k > 0, "d and k must be positive");
+  ensure(job->x != nullptr, "x is null");
+  ensure(n >= k, "need at least k = " + std::to_string(k) + " rows, got " + std::to_string(n));
+  ensure(out && out->centroids, "out->centroids is required");
+  ensure(job->batch_law >= 0 && job->batch_law <= 2, "unknown batch law");
+  ensure(!(job->state_positions == nullptr) == !(job->state_usage == nullptr),
+         "state needs positions and usage");
+  double tau = job->unused_threshold;
+  if (std::isnan(tau)) tau = d <= 2 ? 0.0 : 0.1;
+  ensure(tau >= 0.0, "unused_threshold must be >= 0 (0 disables revival)");
+  const bool spherical = job->spherical != 0;
+  host::Recipe r = host::resolve_recipe(n, k, d, job->nepochs, job->batch_law,
+                                        (size_t)std::max<int64_t>(job->batch_size, 0),
+                                        job->alpha0);
+  ensure(r.epoch_rows.size() <= 64, "at most 64 epochs");
+  for (size_t rows : r.epoch_rows) ensure(rows > 0, "nepochs gives an empty epoch");
+  const auto t0 = std::chrono::steady_clock::now();
+
+  // The epoch-0 permutation is drawn while the init runs (model.rs:781-784).
+  auto perm_of = [n, seed = job->seed](size_t epoch) {
+    return host::Mt19937(host::epoch_seed(seed, epoch)).permutation(n);
+  };
+  std::future<std::vector<uint32_t>> next_order = std::async(std::launch::async, perm_of, 0);
+
+  // Start state (model.rs:306-349, 772-797).
+  std::vector<float> pos(k * d), usage(k, 1.0f / 65536.0f);
+  if (job->state_positions) {
+    std::memcpy(pos.data(), job->state_positions, k * d * 4);
+    std::memcpy(usage.data(), job->state_usage, k * 4);
+    for (float u : usage) ensure(std::isfinite(u) && u >= 0.0f, "usage must be finite and >= 0");
+  } else {
+    if (job->init) {
+      std::memcpy(pos.data(), job->init, k * d * 4);
+    } else if (n == k) {
+      std::memcpy(pos.data(), job->x, k * d * 4);
+    } else {
+      std::vector<uint32_t> perm = host::Mt19937(job->seed).permutation(n);
+      for (size_t j = 0; j < k; j++) std::memcpy(&pos[j * d], job->x + (size_t)perm[j] * d, d * 4);
+    }
+    if (spherical)
+      for (size_t j = 0; j < k; j++) host::normalize_row(&pos[j * d], d);
+  }
+  for (float v : pos) ensure(std::isfinite(v), "initial centroids must be finite");
+
+  const size_t bsz = r.batch_size;
+  const size_t chunk = job->chunk > 0 ? (size_t)job->chunk : 65536;
+  const size_t n_epochs = r.epoch_rows.size();
+
+  // Device state (train.rs:92-101).
+  eb_buf* data = nullptr;
+  {
+    int rc = eb_bind(e, job->x, n, d, &data);
+    if (rc != EB_OK) throw Error(rc, eb_last_error());
+  }
+  struct Unbind {
+    eb_engine* e;
+    eb_buf* b;
+    ~Unbind() { free_buf(e, b); }
+  } unbind{e, data};
+  DevBuf order(e, EB_U32, n), labels_ep(e, EB_U32, n), scores_ep(e, EB_F32, n);
+  DevBuf dpos(e, EB_F32, k * d), mass(e, EB_F32, k), readout(e, EB_F32, spherical ? k * d : k);
+  DevBuf sums(e, EB_F32, k * d), counts(e, EB_U32, k), pass(e, EB_F32, k * d);
+  DevBuf pairs(e, EB_U32, 2 * k);
+  EB_CUDA(cudaMemcpyAsync(dpos.f(), pos.data(), k * d * 4, cudaMemcpyHostToDevice, e->stream));
+  EB_CUDA(cudaMemcpyAsync(mass.f(), usage.data(), k * 4, cudaMemcpyHostToDevice, e->stream));
+  if (data->d == d && !data->xnorm && !spherical) {
+    EB_CUDA(cudaMallocAsync(&data->xnorm, std::max<size_t>(n, 1) * 4, e->stream));
+    row_norms(e, static_cast<const float*>(data->ptr), n, d, data->xnorm);
+  }
+
+  host::Mt19937 split_rng(job->seed);
+  size_t n_splits = 0, step = 0;
+  std::vector<double> pass_counts(k, 0.0);
+  std::vector<uint32_t> lab(n);
+  std::vector<float> sc(n);
+  std::vector<uint64_t> hist;
+  std::vector<float> mass_h(k);
+  if (out->labels)
+    for (size_t i = 0; i < n; i++) out->labels[i] = -1;
+
+  for (size_t epoch = 0; epoch < n_epochs; epoch++) {
+    const size_t rows = r.epoch_rows[epoch];
+    std::vector<uint32_t> ord = next_order.get();
+    if (epoch + 1 < n_epochs) next_order = std::async(std::launch::async, perm_of, epoch + 1);
+    const bool last = epoch + 1 == n_epochs;
+    EB_CUDA(cudaMemcpyAsync(order.u(), ord.data(), rows * 4, cudaMemcpyHostToDevice, e->stream));
+    const size_t splits_before = n_splits;
+    for (size_t b = 0; b < rows; b += bsz) {
+      const size_t end = std::min(b + bsz, rows);
+      if (spherical)
+        normalize_rows(e, dpos.f(), k, d, readout.f());
+      else
+        row_norms(e, dpos.f(), k, d, readout.f());
+      for (size_t c0 = b; c0 < end; c0 += chunk) {
+        Top1Args a;
+        a.x = static_cast<const float*>(data->ptr);
+        a.n = n;
+        a.d = d;
+        a.ids = order.u();
+        a.r0 = c0;
+        a.r1 = std::min(c0 + chunk, end);
+        a.c = spherical ? readout.f() : dpos.f();
+        a.cnorm = spherical ? nullptr : readout.f();
+        a.k = k;
+        a.metric = spherical ? EB_IP : EB_L2;
+        a.labels = labels_ep.u();
+        a.scores = scores_ep.f();
+        a.xnorm = data->xnorm;
+        top1_dispatch(e, a, data);
+      }
+      scatter_add(e, static_cast<const float*>(data->ptr), n, d, order.u(), b, end, labels_ep.u(),
+                  k, sums.f(), counts.u(), last ? pass.f() : nullptr);
+      const double alpha = host::scheduled_alpha(r.alpha0, step, r.total_steps);
+      ema_update(e, dpos.f(), mass.f(), sums.f(), counts.u(), k, d, (float)alpha,
+                 (float)(1.0 - alpha), alpha == 1.0);
+      if ((step + 1) % 5 == 0) {
+        read_into(e, mass_h.data(), mass.f(), k * 4);
+        std::vector<uint32_t> plan = host::plan_revival(mass_h, tau, split_rng);
+        if (!plan.empty()) {
+          EB_CUDA(cudaMemcpyAsync(pairs.u(), plan.data(), plan.size() * 4, cudaMemcpyHostToDevice,
+                                  e->stream));
+          split(e, dpos.f(), mass.f(), pairs.u(), plan.size() / 2, d);
+          n_splits += plan.size() / 2;
+        }
+      }
+      step++;
+    }
+    // Epoch end: labels and scores come down for the statistics.
+    EB_CUDA(cudaMemcpyAsync(lab.data(), labels_ep.u(), rows * 4, cudaMemcpyDeviceToHost, e->stream));
+    read_into(e, sc.data(), scores_ep.f(), rows * 4);
+    EpochStat st = epoch_stats(lab, sc, rows, bsz, chunk, k, spherical, hist);
+    out->obj[epoch] = st.obj;
+    out->imbalance[epoch] = st.imbalance;
+    out->nsplit[epoch] = (int64_t)(n_splits - splits_before);
+    out->epoch_time[epoch] =
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (job->verbose)
+      fprintf(stderr, "  Epoch %zu / %zu (%zu rows), iteration %zu (%.2f s): objective=%.17g\n",
+              epoch + 1, n_epochs, rows, step, out->epoch_time[epoch], st.obj);
+    if (last) {
+      for (size_t j = 0; j < k; j++) pass_counts[j] = (double)hist[j];
+      if (out->labels)
+        for (size_t i = 0; i < rows; i++) out->labels[ord[i]] = (int32_t)lab[i];
+    }
+  }
+  std::vector<float> closing(k * d);
+  EB_CUDA(cudaMemcpyAsync(pos.data(), dpos.f(), k * d * 4, cudaMemcpyDeviceToHost, e->stream));
+  EB_CUDA(cudaMemcpyAsync(usage.data(), mass.f(), k * 4, cudaMemcpyDeviceToHost, e->stream));
+  read_into(e, closing.data(), pass.f(), k * d * 4);
+  host::closing_means(pos.data(), closing.data(), pass_counts, k, d, spherical, out->centroids);
+  if (out->positions) std::memcpy(out->positions, pos.data(), k * d * 4);
+  if (out->usage) std::memcpy(out->usage, usage.data(), k * 4);
+  out->n_epochs = (int32_t)n_epochs;
+  out->n_splits = (int64_t)n_splits;
+  out->batch_size = (int64_t)bsz;
+  out->alpha0 = r.alpha0;
+  out->total_steps = (int64_t)r.total_steps;
+}
+
+}  // namespace eb
+
+extern "C" int eb_train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
+  if (!e || !job || !out) {
+    eb::set_last_error("engine, job and out are required");
+    return EB_INVALID_ARGUMENT;
+  }
+  int prev = -1;
+  cudaGetDevice(&prev);
+  int rc = EB_OK;
+  try {
+    if (prev != e->device) EB_CUDA(cudaSetDevice(e->device));
+    eb::train(e, job, out);
+  } catch (const eb::Error& err) {
+    rc = err.code;
+    eb::set_last_error(err.what());
+  } catch (const std::exception& err) {
+    rc = EB_INTERNAL;
+    eb::set_last_error(err.what());
+  }
+  if (prev >= 0 && prev != e->device) cudaSetDevice(prev);
+  return rc;
+}

@@ -1,0 +1,222 @@
+/*
+ * emeans_b200: a B200 (sm_100a) engine for the emeans hot path, behind a C ABI.
+ *
+ * The ABI mirrors the reference's layer-1 op contract, `trait Device`
+ * (crates/emeans-core/src/core/mod.rs:71-178), one entry point per method, so
+ * that a thin Rust crate can implement `Device + Assigner` over it and plug in
+ * at `make_assigner(Backend::Cuda)` (crates/emeans-cluster/src/backend.rs:126-133).
+ * Above it, `eb_assign` is `Assigner::assign` (crates/emeans-core/src/assign.rs:71-117,
+ * core::assign_on core/mod.rs:249-330) and `eb_train` is `Engine::run_train`
+ * (core/mod.rs:229-231), the reference device loop (core/train.rs:60-303)
+ * restated in C++ on this engine.
+ *
+ * Conventions (from crates/emeans-ffi/include/emeans.h:66-80 and
+ * crates/emeans-ffi/src/lib.rs:95-126):
+ *  - every function returns a status code; on failure eb_last_error() holds a
+ *    message for the calling thread;
+ *  - ops are queued on the engine's stream and only eb_buf_read / eb_sync (and
+ *    the host-array entry points eb_assign, eb_topk, eb_train) wait; errors
+ *    that a kernel detects (a label >= k, a row id past the data) are
+ *    reported by the next call that waits, as EB_INVALID_ARGUMENT;
+ *  - an engine is owned by one thread at a time (Send, not Sync);
+ *  - outputs outside the selection rows r0..r1 are never written.
+ *
+ * Exactness (the reference contract, core/mod.rs:60-69):
+ *  - eb_top1 / eb_assign: labels and scores bit-equal to the reference CPU
+ *    kernel (`cpu-fused`, assign/fused.rs): each dot is one sequential FMA
+ *    chain over d; ties keep the lower id; L2 keys are cnorm - 2 dot (one
+ *    rounding) and scores max(sum x^2 + key, 0). The tensor-core screen only
+ *    chooses which centroids get the exact FP32 chain.
+ *  - eb_scatter_add: counts exact; sums bit-equal to adding the rows in
+ *    selection order in f32.
+ *  - eb_ema_update, eb_split, eb_row_norms, eb_normalize_rows: bit-equal to
+ *    the CPU float order (no FMA contraction, IEEE divide and sqrt).
+ *  - eb_topk: ids and scores bit-equal to the exact top-k by FMA-chain inner
+ *    product (best first, lower id on ties).
+ */
+#ifndef EMEANS_B200_H
+#define EMEANS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes: crates/emeans-ffi/include/emeans.h:66-80. */
+#define EB_OK 0
+#define EB_INVALID_ARGUMENT 1
+#define EB_ERROR 2 /* CUDA/NCCL failure, out of memory, device-wait timeout */
+#define EB_INTERNAL 3
+
+/* Element types of engine buffers. */
+#define EB_F32 0
+#define EB_U32 1
+
+/* Metric: crates/emeans-core/src/assign.rs:14-21. */
+#define EB_L2 0
+#define EB_IP 1
+
+typedef struct eb_engine eb_engine;
+typedef struct eb_buf eb_buf;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* eb_last_error(void);
+/* Library version string. */
+const char* eb_version(void);
+
+/* ---------------------------------------------------------------- engine */
+
+/* An engine on CUDA device `device` with its own stream. No device, or a
+ * device that is not sm_100, fails with EB_ERROR
+ * (crates/emeans-cuda/src/lib.rs:303-309: a missing driver is an error). */
+int eb_engine_create(int device, eb_engine** out);
+int eb_engine_destroy(eb_engine* e);
+/* Device::name (core/mod.rs:77). Writes a NUL-terminated name. */
+int eb_engine_name(eb_engine* e, char* buf, size_t cap);
+/* Device::flush (core/mod.rs:93-95): submit queued work without waiting. */
+int eb_flush(eb_engine* e);
+/* Wait for queued work; report errors detected on the device. */
+int eb_sync(eb_engine* e);
+
+/* The engine's CUDA stream (a cudaStream_t), for callers that order their own
+ * work or CUDA events against the engine's. */
+int eb_engine_stream(eb_engine* e, void** stream);
+
+/* Counters since creation: rows top-1 screened on tensor cores, rows that fell
+ * back to the exact full scan, candidates re-scored exactly, rows served by the
+ * exact SIMT kernel directly, and kernels launched. */
+typedef struct {
+  uint64_t screened_rows;
+  uint64_t fallback_rows;
+  uint64_t rescored_candidates;
+  uint64_t exact_rows;
+  uint64_t kernel_launches;
+} eb_stats;
+int eb_get_stats(eb_engine* e, eb_stats* out);
+
+/* ---------------------------------------------------------------- buffers */
+
+/* Device::zeros_f32 / zeros_u32 (core/mod.rs:84-85): a zeroed buffer of `len`
+ * elements of `dtype`. */
+int eb_buf_alloc(eb_engine* e, int dtype, size_t len, eb_buf** out);
+/* A non-owning view of `len` elements of device memory at `dev_ptr` (on the
+ * engine's device; 16-byte aligned). The memory must outlive the view. */
+int eb_buf_wrap(eb_engine* e, int dtype, void* dev_ptr, size_t len, eb_buf** out);
+int eb_buf_free(eb_engine* e, eb_buf* b);
+size_t eb_buf_len(const eb_buf* b);
+void* eb_buf_ptr(const eb_buf* b);
+/* Device::write_f32 / write_u32 (core/mod.rs:86-88): overwrite
+ * b[offset .. offset+len) from host memory, after queued work that uses b. */
+int eb_buf_write(eb_engine* e, eb_buf* b, size_t offset, const void* host, size_t len);
+/* Device::read_f32 / read_u32 (core/mod.rs:89-91): wait, copy b[lo..hi) to host. */
+int eb_buf_read(eb_engine* e, const eb_buf* b, size_t lo, size_t hi, void* host);
+/* Device::upload_f32 / upload_u32 (core/mod.rs:82-83). */
+int eb_buf_upload(eb_engine* e, int dtype, const void* host, size_t len, eb_buf** out);
+/* Device::bind (core/mod.rs:79-81): put the n x d data set on the device. The
+ * engine also keeps the data's row norms and its FP16 screen copy for top-1. */
+int eb_bind(eb_engine* e, const float* x, size_t n, size_t d, eb_buf** out);
+
+/* ---------------------------------------------------------------- layer-1 ops */
+
+/* Device::top1 (core/mod.rs:97-112). For every selection position p in
+ * r0..r1, row x[ids[p]] (or x[p] when ids is NULL) gets labels[p] = best of
+ * the k centroids and scores[p] its score. cnorm (k squared norms) is
+ * required for EB_L2. */
+int eb_top1(eb_engine* e, const eb_buf* x, size_t d, const eb_buf* ids, size_t r0, size_t r1,
+            const eb_buf* centroids, const eb_buf* cnorm, size_t k, int metric, eb_buf* labels,
+            eb_buf* scores);
+
+/* Device::topk (core/mod.rs:114-124): the best kk (1..=16) data rows of every
+ * query by inner product, best first (larger score, then lower id). With
+ * exclude_self, query i is data row i and is skipped. Missing neighbours:
+ * id 0xFFFFFFFF, score -inf. ids and sims are m*kk host arrays. */
+int eb_topk(eb_engine* e, const float* queries, size_t m, const float* data, size_t n, size_t d,
+            size_t kk, int exclude_self, uint32_t* ids, float* sims);
+
+/* Device::scatter_add (core/mod.rs:126-139): sums (k x d) = the selected rows
+ * added per label in selection order, counts (k) = rows per label; both are
+ * overwritten. labels are read at positions r0..r1. With acc, acc += sums. */
+int eb_scatter_add(eb_engine* e, const eb_buf* x, size_t d, const eb_buf* ids, size_t r0,
+                   size_t r1, const eb_buf* labels, size_t k, eb_buf* sums, eb_buf* counts,
+                   eb_buf* acc);
+
+/* Device::row_norms (core/mod.rs:141-142): squared norm of each of `rows` rows. */
+int eb_row_norms(eb_engine* e, const eb_buf* m, size_t rows, size_t d, eb_buf* out);
+
+/* Device::normalize_rows (core/mod.rs:144-151): faiss normalize_into. */
+int eb_normalize_rows(eb_engine* e, const eb_buf* src, size_t rows, size_t d, eb_buf* dst);
+
+/* Device::split (core/mod.rs:153-162): apply a revival plan of npairs
+ * (donor, dead) pairs (2*npairs host u32). The pairs must not share ids. */
+int eb_split(eb_engine* e, eb_buf* positions, eb_buf* usage, const uint32_t* pairs,
+             size_t npairs, size_t d);
+
+/* Device::ema_update (core/mod.rs:164-177) with EmaStep{alpha, decay, replace}
+ * (core/mod.rs:182-197). */
+int eb_ema_update(eb_engine* e, eb_buf* positions, eb_buf* usage, const eb_buf* sums,
+                  const eb_buf* counts, size_t k, size_t d, float alpha, float decay,
+                  int replace);
+
+/* ---------------------------------------------------------------- Assigner */
+
+/* Assigner::bind_data / unbind_data (assign.rs:75-95): keep `data` (n x d) on
+ * the device; eb_assign calls with ids into the same (pointer, n) then send
+ * only the ids. Binding always takes a fresh copy. */
+int eb_bind_data(eb_engine* e, const float* data, size_t n, size_t d);
+int eb_unbind_data(eb_engine* e);
+
+/* Assigner::assign (assign.rs:104-116; core::assign_on core/mod.rs:249-330).
+ * ids == NULL: Rows::Dense, `rows` is n x d and m == n.
+ * ids != NULL: Rows::Indexed{data: rows (n x d), ids (m)}.
+ * centroids: k x d host. labels, scores: m host. */
+int eb_assign(eb_engine* e, const float* rows, size_t n, size_t d, const uint32_t* ids,
+              size_t m, const float* centroids, size_t k, int metric, uint32_t* labels,
+              float* scores);
+
+/* ---------------------------------------------------------------- Engine::run_train */
+
+/* core::train::Job (core/train.rs:33-49) plus the recipe inputs of
+ * model::Config (model.rs:23-67). */
+typedef struct {
+  const float* x; /* n x d host rows */
+  size_t n, d, k;
+  double nepochs;
+  int32_t batch_law;     /* 0 auto, 1 throughput, 2 quality */
+  int32_t spherical;     /* inner product on the unit sphere */
+  int64_t batch_size;    /* 0: batch law */
+  double alpha0;         /* NaN: step law */
+  double unused_threshold; /* NaN: 0.1, or 0 when d <= 2 */
+  uint32_t seed;
+  int32_t capture;       /* fill labels */
+  int64_t chunk;         /* rows per top-1 call; 0: 65536 */
+  const float* init;     /* k x d initial centroids, or NULL: MT19937 draw */
+  const float* state_positions; /* resume from EMA state (k x d), or NULL */
+  const float* state_usage;     /* k, with state_positions */
+  int32_t verbose;
+} eb_train_job;
+
+/* core::train::Outcome (core/train.rs:51-58) + model::EpochStats (model.rs:77-89). */
+typedef struct {
+  float* centroids; /* k x d */
+  float* positions; /* k x d, may be NULL */
+  float* usage;     /* k, may be NULL */
+  int32_t* labels;  /* n, may be NULL */
+  double obj[64];
+  double imbalance[64];
+  int64_t nsplit[64];
+  double epoch_time[64];
+  int32_t n_epochs;
+  int64_t n_splits;
+  int64_t batch_size;
+  double alpha0;
+  int64_t total_steps;
+} eb_train_out;
+
+int eb_train(eb_engine* e, const eb_train_job* job, eb_train_out* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EMEANS_B200_H */

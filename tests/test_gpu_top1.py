@@ -1,0 +1,172 @@
+"""Top-1 on the B200 against the CPU oracle: labels and scores bit-equal.
+
+The oracle follows the reference CPU kernel's float order (one sequential FMA
+chain per dot, crates/emeans-core/src/assign/fused.rs:12-16), so the engine
+must reproduce every bit, whether a row was certified by the tensor-core
+screen or scanned exactly. Shapes follow the reference contract suite
+(crates/emeans-core/src/core/contract.rs:75-161): check() shapes with
+indexed and dense selections and a sub-range whose outside must stay
+untouched, check_production() (16,384 x 768, k 1024 / 1000 with duplicate
+centroids in other tiles), and adversarial near-ties.
+"""
+
+import numpy as np
+import pytest
+
+import emeans_b200 as eb
+import oracle
+from tests.helpers import bits, contract_centroids, mixture, near_tie_centroids, \
+    production_centroids
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(1000, 768, 64), (777, 768, 100), (513, 13, 70), (2000, 20, 300), (300, 64, 1),
+          (600, 768, 1024)]
+
+
+def run_top1(engine, x, c, metric, ids=None, lo=None, hi=None):
+    n, d = x.shape
+    k = c.shape[0]
+    m = n if ids is None else len(ids)
+    lo = 0 if lo is None else lo
+    hi = m if hi is None else hi
+    xb = engine.bind(x, d)
+    cb = engine.upload_f32(c)
+    cn = None
+    if metric == eb.L2:
+        cn = engine.zeros_f32(k)
+        engine.row_norms(cb, k, d, cn)
+    ib = engine.upload_u32(ids) if ids is not None else None
+    lab = engine.upload_u32(np.full(m, 0xFFFFFFFF, np.uint32))
+    sco = engine.upload_f32(np.full(m, np.nan, np.float32))
+    engine.top1(xb, d, ib, range(lo, hi), cb, cn, k, metric, lab, sco)
+    return lab.read(), sco.read()
+
+
+def check_against_oracle(engine, x, c, metric, ids=None, lo=None, hi=None):
+    n, d = x.shape
+    m = n if ids is None else len(ids)
+    lo = 0 if lo is None else lo
+    hi = m if hi is None else hi
+    gl, gs = run_top1(engine, x, c, metric, ids, lo, hi)
+    wl = np.full(m, 0xFFFFFFFF, np.uint32)
+    ws = np.full(m, np.nan, np.float32)
+    oracle.top1(x.ravel(), d, c.ravel(), metric, ids=ids, r0=lo, r1=hi, labels=wl, scores=ws)
+    outside = np.ones(m, bool)
+    outside[lo:hi] = False
+    assert np.all(gl[outside] == 0xFFFFFFFF) and np.all(np.isnan(gs[outside])), \
+        "top1 wrote outside the selection"
+    bad = np.flatnonzero(gl[lo:hi] != wl[lo:hi])
+    assert bad.size == 0, f"{bad.size} labels differ, first at {lo + bad[0]}"
+    assert np.array_equal(bits(gs[lo:hi]), bits(ws[lo:hi]))
+
+
+@pytest.mark.parametrize("n,d,k", SHAPES)
+@pytest.mark.parametrize("metric", [eb.IP, eb.L2])
+def test_contract_shapes(engine, n, d, k, metric):
+    x = mixture(n, d, 11, 0.6, metric == eb.IP, 3 * n + k)
+    c = contract_centroids(x, d, k)
+    perm = ((np.arange(n, dtype=np.int64) * 7919 + 13) % n).astype(np.uint32)
+    lo, hi = n // 7, n - n // 9
+    check_against_oracle(engine, x, c, metric, ids=perm, lo=lo, hi=hi)
+    check_against_oracle(engine, x, c, metric, lo=lo, hi=hi)
+
+
+@pytest.mark.parametrize("k", [1024, 1000])
+@pytest.mark.parametrize("metric", [eb.IP, eb.L2])
+def test_production_batch_with_duplicate_centroids(engine, k, metric):
+    n, d = 16384, 768
+    x = mixture(n, d, 64, 0.6, metric == eb.IP, 5 * n + k)
+    c = production_centroids(x, k)
+    check_against_oracle(engine, x, c, metric)
+    # Exact duplicates: the lower id wins.
+    gl, _ = run_top1(engine, x, c, metric)
+    assert np.all(gl < k - 256)
+
+
+@pytest.mark.parametrize("metric", [eb.IP, eb.L2])
+def test_near_ties_and_scaled_rows(engine, metric):
+    n, d, k = 4096, 256, 512
+    c = near_tie_centroids(d, k, 3)
+    rng = np.random.default_rng(8)
+    x = (c[rng.integers(0, k, n)] + np.float32(1e-3) * rng.standard_normal((n, d))).astype(np.float32)
+    scale = np.array([1.0, 1e3, 1e-3, 1e-15], np.float32)[np.arange(n) % 4]
+    x = (x * scale[:, None]).astype(np.float32)
+    check_against_oracle(engine, x, c, metric)
+
+
+@pytest.mark.parametrize("metric", [eb.IP, eb.L2])
+def test_odd_shapes(engine, metric):
+    rng = np.random.default_rng(0)
+    for n, d, k in [(1, 1, 1), (5, 3, 2), (129, 17, 257), (64, 8, 40), (200, 100, 3)]:
+        x = rng.standard_normal((n, d)).astype(np.float32)
+        c = rng.standard_normal((k, d)).astype(np.float32)
+        check_against_oracle(engine, x, c, metric)
+
+
+def test_ties_keep_the_lowest_id(engine):
+    d = 8
+    x = np.ones((3, d), np.float32)
+    c = np.zeros((40, d), np.float32)
+    for j in (5, 17, 33):
+        c[j] = 1.0
+    for metric in (eb.IP, eb.L2):
+        gl, _ = run_top1(engine, x, c, metric)
+        assert gl.tolist() == [5, 5, 5]
+
+
+def test_nonfinite_rows_follow_the_cpu_semantics(engine):
+    d, k = 16, 9
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((6, d)).astype(np.float32)
+    x[1, 3] = np.nan
+    x[2, 0] = np.inf
+    x[3] = 0.0
+    c = rng.standard_normal((k, d)).astype(np.float32)
+    c[4, 2] = np.nan
+    for metric in (eb.IP, eb.L2):
+        check_against_oracle(engine, x, c, metric)
+
+
+def test_bad_row_id_is_an_error(engine):
+    d = 4
+    x = np.ones((10, d), np.float32)
+    c = np.ones((3, d), np.float32)
+    xb = engine.bind(x, d)
+    cb = engine.upload_f32(c)
+    ib = engine.upload_u32(np.array([0, 1, 99], np.uint32))
+    lab, sco = engine.zeros_u32(3), engine.zeros_f32(3)
+    engine.top1(xb, d, ib, range(0, 3), cb, None, 3, eb.IP, lab, sco)
+    with pytest.raises(eb.EngineError) as ei:
+        engine.sync()
+    assert ei.value.code == eb.INVALID_ARGUMENT
+    engine.sync()
+
+
+def test_argument_checks(engine):
+    d = 4
+    xb = engine.bind(np.ones((10, d), np.float32), d)
+    cb = engine.upload_f32(np.ones((3, d), np.float32))
+    lab, sco = engine.zeros_u32(10), engine.zeros_f32(10)
+    with pytest.raises(eb.EngineError, match="past the data"):
+        engine.top1(xb, d, None, range(0, 11), cb, None, 3, eb.IP, lab, sco)
+    with pytest.raises(eb.EngineError, match="centroid norms"):
+        engine.top1(xb, d, None, range(0, 10), cb, None, 3, eb.L2, lab, sco)
+    with pytest.raises(eb.EngineError, match="k x d"):
+        engine.top1(xb, d, None, range(0, 10), cb, None, 4, eb.IP, lab, sco)
+
+
+@pytest.mark.parametrize("metric", [eb.IP, eb.L2])
+def test_assign_host_api(engine, metric):
+    n, d, k = 3000, 96, 130
+    x = mixture(n, d, 20, 0.5, metric == eb.IP, 77)
+    c = contract_centroids(x, d, k)
+    gl, gs = engine.assign(x, d, c, metric)
+    wl, ws = oracle.top1(x.ravel(), d, c.ravel(), metric)
+    assert np.array_equal(gl, wl) and np.array_equal(bits(gs), bits(ws))
+    ids = np.random.default_rng(2).permutation(n)[:777].astype(np.uint32)
+    engine.bind_data(x, d)
+    gl, gs = engine.assign(engine._bound, d, c, metric, ids=ids)
+    engine.unbind_data()
+    wl, ws = oracle.top1(x.ravel(), d, c.ravel(), metric, ids=ids)
+    assert np.array_equal(gl, wl) and np.array_equal(bits(gs), bits(ws))
