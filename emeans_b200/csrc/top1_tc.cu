@@ -1,18 +1,721 @@
-// Tensor-core screen for top-1 (tcgen05). Placeholder until the screen lands:
-// every call takes the exact SIMT path.
+// Exact top-1 on the tensor cores: a tcgen05 FP16 screen, then an exact FP32
+// re-score of the few centroids the screen cannot rule out.
+//
+// The labels and scores are the reference CPU kernel's bit for bit
+// (crates/emeans-core/src/assign/fused.rs:12-16: one sequential FMA chain per
+// dot, lower id on ties). The screen only decides which centroids get that
+// exact chain:
+//
+// 1. prep: rows and centroids are scaled by powers of two (per row for x, one
+//    exponent for all centroids) so that |v| < 2^14, and rounded to FP16.
+// 2. screen (tcgen05): a 128-row tile of x against 256-centroid tiles, FP32
+//    accumulators in TMEM (two buffers of 256 columns, so the epilogue reads
+//    one while the tensor cores fill the other), operands staged by TMA into
+//    128B-swizzled shared memory through a 4-stage mbarrier ring. The
+//    epilogue (one thread per row) keeps the running best screened value and
+//    every centroid within 2e of it, where e bounds |screen - exact chain|
+//    (FP16 rounding of both operands, tensor-core accumulation, the FP32 chain
+//    itself); a centroid more than 2e behind the best cannot be the exact
+//    winner. At most KSLOTS candidates are kept; more mark the row for the
+//    full exact scan.
+// 3. rescore: the exact FMA chain for each candidate; lower id on ties.
+// 4. fallback: rows with more candidates than slots, or non-finite inputs,
+//    take the exact SIMT kernel (top1_exact.cu).
+//
+// Error bound (acc units, operands scaled): with u = 2^-11 and FP16
+// subnormals (half-ulp 2^-25),
+//   |acc - x'.c'| <= (2^-10 + 2^-22) sum|x'||c'| + 2^-24 (sum|x'| + sum|c'|)
+//                    + d 2^-21 sum|x'||c'|        (accumulation, taken loose)
+// and the FP32 chain differs from the exact dot by <= gamma_d sum|x c|.
+// sum|x'||c'| <= |x'| |c'|, sum|x'| <= sqrt(d) |x'| (Cauchy-Schwarz).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <cmath>
+
 #include "engine.h"
 
 namespace eb {
 
 struct Fp16Copy {};
 
-bool top1_screen_supported(eb_engine*, const Top1Args&) { return false; }
-void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) { top1_exact(e, a); }
 void drop_f16(eb_buf* b) {
   if (b && b->f16) {
     delete b->f16;
     b->f16 = nullptr;
   }
+}
+
+namespace {
+
+constexpr int BM = 128;          // rows per CTA (TMEM lanes)
+constexpr int BN = 256;          // centroids per tile (TMEM columns per buffer)
+constexpr int BKH = 64;          // FP16 columns per k-block: one 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BKH * 2;
+constexpr int B_BYTES = BN * BKH * 2;
+constexpr int KSLOTS = 8;        // candidates kept per row
+constexpr int NTHREADS = 192;    // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr uint32_t FALLBACK = 0xFFFFFFFFu;
+constexpr int XEXP_BAD = INT_MIN;  // row with a non-finite value
+constexpr size_t CHUNK_ROWS = 131072;
+constexpr uint64_t WAIT_NS = 2000000000ull;  // bounded waits: 2 s
+
+constexpr size_t SMEM_BYTES = 1024 /* alignment slack */ + STAGES * (A_BYTES + B_BYTES) + 256;
+
+// ---------------------------------------------------------------- PTX helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase of `bar` with the given parity; false (and the CTA's
+// abort flag set) after WAIT_NS, so that no wait can spin forever.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = now_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (now_ns() - t0 > WAIT_NS) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                            int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// K-major operand tile with 128-byte rows, 128B swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;             // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: F16 x F16 -> F32, both K-major, M=128, N=256.
+constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+// 32 consecutive FP32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- prep kernels
+
+// Scaled FP16 copy of the selected rows (one warp per row), with the row's
+// exponent (XEXP_BAD for non-finite rows) and an upper bound on its norm.
+__global__ void k_prep_rows(const float* __restrict__ x, long n, int d, int dp,
+                            const uint32_t* __restrict__ ids, long p0, long m,
+                            __half* __restrict__ xh, int* __restrict__ xexp,
+                            float* __restrict__ xnrm, uint32_t* status) {
+  long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  int lane = threadIdx.x & 31;
+  if (i >= m) return;
+  long p = p0 + i;
+  long row = ids ? (long)ids[p] : p;
+  __half* out = xh + i * (long)dp;
+  if (row >= n) {
+    if (lane == 0) {
+      atomicOr(status, ST_BAD_ROW);
+      xexp[i] = XEXP_BAD;
+      xnrm[i] = 0.0f;
+    }
+    for (int t = lane; t < dp; t += 32) out[t] = __float2half_rn(0.0f);
+    return;
+  }
+  const float* r = x + row * (long)d;
+  float mx = 0.0f, ss = 0.0f;
+  bool finite = true;
+  for (int t = lane; t < d; t += 32) {
+    float v = __ldg(r + t);
+    finite = finite && isfinite(v);
+    mx = fmaxf(mx, fabsf(v));
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+  }
+  finite = __all_sync(0xFFFFFFFFu, finite);
+  int ex = 0;
+  frexpf(mx, &ex);
+  int sh = 14 - ex;
+  for (int t = lane; t < dp; t += 32) {
+    float v = t < d ? __ldg(r + t) : 0.0f;
+    out[t] = __float2half_rn(finite ? ldexpf(v, sh) : 0.0f);
+  }
+  if (lane == 0) {
+    xexp[i] = finite ? ex : XEXP_BAD;
+    // Any-order sum of squares: relative error < d 2^-24; inflate by 2^-9.
+    xnrm[i] = finite ? sqrtf(ss) * (1.0f + 1.0f / 512.0f) : 0.0f;
+  }
+}
+
+// Global max |c|, a bound on max |c_j| and a non-finite flag, over all centroids.
+// cinfo (u32): [0] bits of max|c|, [1] bits of the norm bound, [2] non-finite flag.
+__global__ void k_cent_max(const float* __restrict__ c, long k, int d, uint32_t* cinfo) {
+  long j = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  int lane = threadIdx.x & 31;
+  if (j >= k) return;
+  const float* r = c + j * (long)d;
+  float mx = 0.0f, ss = 0.0f;
+  bool finite = true;
+  for (int t = lane; t < d; t += 32) {
+    float v = __ldg(r + t);
+    finite = finite && isfinite(v);
+    mx = fmaxf(mx, fabsf(v));
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+  }
+  finite = __all_sync(0xFFFFFFFFu, finite);
+  if (lane == 0) {
+    if (!finite) {
+      atomicOr(&cinfo[2], 1u);
+      return;
+    }
+    atomicMax(&cinfo[0], __float_as_uint(mx));
+    atomicMax(&cinfo[1], __float_as_uint(sqrtf(ss) * (1.0f + 1.0f / 512.0f)));
+  }
+}
+
+// Scaled FP16 centroids: c' = c 2^(14 - ec), 2^(ec-1) <= max|c| < 2^ec.
+__global__ void k_cent_conv(const float* __restrict__ c, long k, int d, int dp,
+                            const uint32_t* __restrict__ cinfo, __half* __restrict__ ch) {
+  long j = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  int lane = threadIdx.x & 31;
+  if (j >= k) return;
+  int ec = 0;
+  frexpf(__uint_as_float(cinfo[0]), &ec);
+  int sh = 14 - ec;
+  bool bad = cinfo[2] != 0;
+  const float* r = c + j * (long)d;
+  __half* out = ch + j * (long)dp;
+  for (int t = lane; t < dp; t += 32) {
+    float v = (t < d && !bad) ? __ldg(r + t) : 0.0f;
+    out[t] = __float2half_rn(ldexpf(v, sh));
+  }
+}
+
+// ---------------------------------------------------------------- the screen
+
+struct ScreenParams {
+  long m;              // staging rows in this launch
+  int k;
+  int kblocks;         // dp / 64
+  int ntiles;          // ceil(k / 256)
+  int d;
+  const int* xexp;     // per staging row
+  const float* xnrm;   // per staging row
+  const float* cn;     // k squared centroid norms (L2) or null
+  const uint32_t* cinfo;
+  float e_rel, e_abs, e_min;  // bound coefficients (see the header comment)
+  uint32_t* cand;      // m x KSLOTS
+  uint32_t* cand_cnt;  // m: count, or FALLBACK
+  uint32_t* status;
+};
+
+template <bool IP>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_screen(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+             ScreenParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = (uint64_t*)(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long m0 = (long)blockIdx.x * BM;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int total = P.ntiles * P.kblocks;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // TMA producer: per (tile, k-block), one A box (128 x 64) and one B box (256 x 64).
+      for (int it = 0; it < total; it++) {
+        const int s = it % STAGES;
+        const uint32_t par = ((it / STAGES) & 1) ^ 1;
+        if (!mbar_wait(&empty[s], par, abort_flag)) break;
+        const int nt = it / P.kblocks, kb = it % P.kblocks;
+        mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+        tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BKH, (int)m0);
+        tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * BKH, nt * BN);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer.
+      int it = 0;
+      for (int nt = 0; nt < P.ntiles && !*abort_flag; nt++) {
+        const int a = nt & 1;
+        if (!mbar_wait(&tempty[a], ((nt >> 1) & 1) ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t dcol = tmem + (uint32_t)(a * BN);
+        bool ok = true;
+        for (int kb = 0; kb < P.kblocks; kb++, it++) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BKH / 16; kk++)
+            umma_f16(dcol, umma_desc(a0 + kk * 32), umma_desc(b0 + kk * 32),
+                     (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[a]);
+      }
+      // Every MMA this thread issued has completed once mma_done flips.
+      umma_commit(mma_done);
+      uint64_t t0 = now_ns();
+      while (!mbar_try_wait(mma_done, 0) && now_ns() - t0 < WAIT_NS) {
+      }
+    }
+  } else {
+    // Epilogue: one thread per row of the tile.
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const long i = m0 + r;
+    const bool live = i < P.m;
+    const int ex = live ? P.xexp[i] : XEXP_BAD;
+    int ec = 0;
+    frexpf(__uint_as_float(P.cinfo[0]), &ec);
+    const float cmax = __uint_as_float(P.cinfo[1]);
+    const bool c_bad = P.cinfo[2] != 0;
+    bool fallback = !live || ex == XEXP_BAD || c_bad;
+    const float xn = live ? P.xnrm[i] : 0.0f;
+    // |x'| and max |c'| in acc units, and the bound e (acc units).
+    const float xs = ldexpf(xn, 14 - (fallback ? 0 : ex));
+    const float cs = ldexpf(cmax, 14 - ec);
+    const float e_acc = fmaf(P.e_rel * xs, cs, fmaf(P.e_abs, xs + cs, P.e_min));
+    float off, m2f = 0.0f;
+    if (IP) {
+      off = 2.0f * e_acc;
+    } else {
+      const int fe = ex + ec - 28;
+      if (fe < -100 || fe > 100) fallback = true;
+      const float f = ldexpf(1.0f, fallback ? 0 : fe);
+      m2f = -2.0f * f;
+      const float e_key = fmaf(2.0f * f, e_acc, ldexpf(fmaf(cmax, cmax, 2.0f * xn * cmax), -22));
+      off = 2.0f * e_key;
+    }
+    if (!isfinite(off)) fallback = true;
+    float best = IP ? -INFINITY : INFINITY;
+    float thr = best;
+    float sv[KSLOTS];
+    uint32_t sj[KSLOTS];
+#pragma unroll
+    for (int s = 0; s < KSLOTS; s++) {
+      sv[s] = IP ? -INFINITY : INFINITY;
+      sj[s] = FALLBACK;
+    }
+    bool overflow = false;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+
+    for (int nt = 0; nt < P.ntiles; nt++) {
+      const int a = nt & 1;
+      if (!mbar_wait(&tfull[a], (nt >> 1) & 1, abort_flag)) break;
+      tc_fence_after();
+      const int col0 = nt * BN;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ch++) {
+        uint32_t v[32];
+        tmem_ld32(lane_base + (uint32_t)(a * BN + ch * 32), v);
+        const int cb = col0 + ch * 32;
+        if (cb >= P.k) break;
+        const bool partial = cb + 32 > P.k;
+        float cnv[32];
+        if (!IP) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            float4 c4 = (cb + j + 4 <= P.k) ? __ldg(reinterpret_cast<const float4*>(P.cn + cb + j))
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            cnv[j] = c4.x;
+            cnv[j + 1] = c4.y;
+            cnv[j + 2] = c4.z;
+            cnv[j + 3] = c4.w;
+          }
+          if (partial)
+            for (int j = 0; j < 32; j++) cnv[j] = (cb + j < P.k) ? __ldg(P.cn + cb + j) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          float s = IP ? __uint_as_float(v[j]) : fmaf(m2f, __uint_as_float(v[j]), cnv[j]);
+          const bool admit = IP ? (s >= thr) : (s <= thr);
+          if (admit && (!partial || cb + j < P.k)) {
+            if (IP ? (s > best) : (s < best)) {
+              best = s;
+              thr = IP ? __fsub_rd(best, off) : __fadd_ru(best, off);
+            }
+            bool placed = false;
+#pragma unroll
+            for (int q2 = 0; q2 < KSLOTS; q2++) {
+              const bool stale = IP ? !(sv[q2] >= thr) : !(sv[q2] <= thr);
+              if (!placed && stale) {
+                sv[q2] = s;
+                sj[q2] = (uint32_t)(cb + j);
+                placed = true;
+              }
+            }
+            overflow |= !placed;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[a]);
+    }
+    if (live) {
+      uint32_t cnt = 0;
+      if (!fallback && !overflow && isfinite(best) && !*abort_flag) {
+#pragma unroll
+        for (int s = 0; s < KSLOTS; s++) {
+          const bool in = IP ? (sv[s] >= thr) : (sv[s] <= thr);
+          if (in && sj[s] != FALLBACK) P.cand[i * KSLOTS + cnt++] = sj[s];
+        }
+      }
+      P.cand_cnt[i] = cnt == 0 ? FALLBACK : cnt;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512)
+                 : "memory");
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(P.status, ST_WAIT_TIMEOUT);
+}
+
+// ---------------------------------------------------------------- exact re-score
+
+// Exact FMA chain of row x against centroid c over d columns.
+__device__ __forceinline__ float chain(const float* __restrict__ x, const float* __restrict__ c,
+                                       int d) {
+  float acc = 0.0f;
+  if ((d & 3) == 0) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const float4* c4 = reinterpret_cast<const float4*>(c);
+    for (int t = 0; t < d / 4; t++) {
+      float4 a = __ldg(x4 + t), b = __ldg(c4 + t);
+      acc = __fmaf_rn(a.x, b.x, acc);
+      acc = __fmaf_rn(a.y, b.y, acc);
+      acc = __fmaf_rn(a.z, b.z, acc);
+      acc = __fmaf_rn(a.w, b.w, acc);
+    }
+  } else {
+    for (int t = 0; t < d; t++) acc = __fmaf_rn(__ldg(x + t), __ldg(c + t), acc);
+  }
+  return acc;
+}
+
+template <bool IP>
+__global__ void k_rescore(const float* __restrict__ x, long n, int d,
+                          const uint32_t* __restrict__ ids, long p0, long m,
+                          const float* __restrict__ c, const float* __restrict__ cn,
+                          const float* __restrict__ xnorm_row, const uint32_t* __restrict__ cand,
+                          const uint32_t* __restrict__ cand_cnt, uint32_t* __restrict__ labels,
+                          float* __restrict__ scores, uint32_t* __restrict__ list,
+                          uint32_t* __restrict__ list_count,
+                          unsigned long long* __restrict__ counters) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= m) return;
+  const long p = p0 + i;
+  const uint32_t cnt = cand_cnt[i];
+  if (cnt == FALLBACK) {
+    list[atomicAdd(list_count, 1u)] = (uint32_t)p;
+    atomicAdd(&counters[1], 1ull);
+    return;
+  }
+  const long row = ids ? (long)ids[p] : p;
+  const float* xr = x + row * (long)d;
+  float best = IP ? -INFINITY : INFINITY;
+  uint32_t bj = 0xFFFFFFFFu;
+  for (uint32_t s = 0; s < cnt; s++) {
+    const uint32_t j = cand[i * KSLOTS + s];
+    float v = chain(xr, c + (long)j * d, d);
+    if (!IP) v = __fsub_rn(__ldg(cn + j), __fmul_rn(2.0f, v));
+    const bool better = IP ? (v > best || (v == best && j < bj)) : (v < best || (v == best && j < bj));
+    if (better || bj == 0xFFFFFFFFu) {
+      best = v;
+      bj = j;
+    }
+  }
+  atomicAdd(&counters[2], (unsigned long long)cnt);
+  float score = best;
+  if (!IP) {
+    float xn;
+    if (xnorm_row) {
+      xn = xnorm_row[row];
+    } else {
+      xn = -0.0f;
+      for (int t = 0; t < d; t++) {
+        float v = __ldg(xr + t);
+        xn = __fadd_rn(xn, __fmul_rn(v, v));
+      }
+    }
+    score = fmaxf(__fadd_rn(xn, best), 0.0f);
+  }
+  labels[p] = bj;
+  scores[p] = score;
+}
+
+// ---------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    EB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !p)
+      throw Error(EB_ERROR, "cuTensorMapEncodeTiled is not available from the driver");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// A 2-D FP16 tensor map over rows x dp (row stride dp*2 bytes) with a
+// box of `box_rows` x 64 columns and 128-byte swizzle.
+CUtensorMap make_map(const void* base, size_t rows, size_t dp, uint32_t box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)dp, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)dp * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BKH, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(EB_ERROR, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  return m;
+}
+
+template <class K>
+void set_smem(K kernel) {
+  static bool done = false;
+  if (!done) {
+    EB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)SMEM_BYTES));
+    done = true;
+  }
+}
+
+}  // namespace
+
+bool top1_screen_supported(eb_engine* e, const Top1Args& a) {
+  if (e->screen_mode == 0) return false;
+  if (a.d > 16384 || a.k > 0x7FFFFFFF) return false;
+  if (e->screen_mode == 2) return true;
+  return a.k >= 64 && a.r1 - a.r0 >= 128 && a.d >= 16;
+}
+
+void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
+  const size_t d = a.d, k = a.k;
+  const size_t dp = (d + BKH - 1) / BKH * BKH;
+  const size_t m_all = a.r1 - a.r0;
+  const size_t chunk = std::min(m_all, CHUNK_ROWS);
+  const bool ip = a.metric == EB_IP;
+
+  // Bound coefficients for this d (see the header comment), with 1% slack.
+  const double dd = (double)d;
+  const double gamma_d = dd * std::ldexp(1.0, -24) / (1.0 - dd * std::ldexp(1.0, -24));
+  const float e_rel = (float)((std::ldexp(1.0, -10) + std::ldexp(1.0, -22) +
+                               dd * std::ldexp(1.0, -21) * (1.0 + std::ldexp(1.0, -9)) + gamma_d) *
+                              1.01);
+  const float e_abs = (float)(std::ldexp(1.0, -24) * std::sqrt(dd) * 1.01);
+  const float e_min = (float)(dd * std::ldexp(1.0, -50));
+
+  // Centroids: one exponent, FP16 copy.
+  uint32_t* cinfo = e->scratch_get<uint32_t>("tc_cinfo", 4);
+  __half* ch = e->scratch_get<__half>("tc_ch", k * dp);
+  EB_CUDA(cudaMemsetAsync(cinfo, 0, 16, e->stream));
+  const unsigned wpb = 8;
+  k_cent_max<<<(unsigned)((k + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(a.c, (long)k, (int)d,
+                                                                          cinfo);
+  EB_LAUNCH("screen centroid max");
+  k_cent_conv<<<(unsigned)((k + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(
+      a.c, (long)k, (int)d, (int)dp, cinfo, ch);
+  EB_LAUNCH("screen centroid convert");
+  const CUtensorMap mapB = make_map(ch, k, dp, BN);
+
+  __half* xh = e->scratch_get<__half>("tc_xh", chunk * dp);
+  int* xexp = e->scratch_get<int>("tc_xexp", chunk);
+  float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
+  uint32_t* cand = e->scratch_get<uint32_t>("tc_cand", chunk * KSLOTS);
+  uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", chunk);
+  uint32_t* list = e->scratch_get<uint32_t>("tc_list", chunk);
+  uint32_t* list_count = e->scratch_get<uint32_t>("tc_list_count", 4);
+  unsigned long long* counters = e->counters();
+
+  ScreenParams P;
+  P.k = (int)k;
+  P.kblocks = (int)(dp / BKH);
+  P.ntiles = (int)((k + BN - 1) / BN);
+  P.d = (int)d;
+  P.xexp = xexp;
+  P.xnrm = xnrm;
+  P.cn = a.cnorm;
+  P.cinfo = cinfo;
+  P.e_rel = e_rel;
+  P.e_abs = e_abs;
+  P.e_min = e_min;
+  P.cand = cand;
+  P.cand_cnt = cand_cnt;
+  P.status = e->d_status;
+
+  if (ip)
+    set_smem(k_screen<true>);
+  else
+    set_smem(k_screen<false>);
+
+  for (size_t c0 = a.r0; c0 < a.r1; c0 += chunk) {
+    const size_t m = std::min(chunk, a.r1 - c0);
+    k_prep_rows<<<(unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(
+        a.x, (long)a.n, (int)d, (int)dp, a.ids, (long)c0, (long)m, xh, xexp, xnrm, e->d_status);
+    EB_LAUNCH("screen row prep");
+    const CUtensorMap mapA = make_map(xh, m, dp, BM);
+    P.m = (long)m;
+    const unsigned grid = (unsigned)((m + BM - 1) / BM);
+    if (ip)
+      k_screen<true><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(mapA, mapB, P);
+    else
+      k_screen<false><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(mapA, mapB, P);
+    EB_LAUNCH("screen");
+    EB_CUDA(cudaMemsetAsync(list_count, 0, 4, e->stream));
+    const unsigned rb = 128;
+    if (ip)
+      k_rescore<true><<<(unsigned)((m + rb - 1) / rb), rb, 0, e->stream>>>(
+          a.x, (long)a.n, (int)d, a.ids, (long)c0, (long)m, a.c, a.cnorm, a.xnorm, cand, cand_cnt,
+          a.labels, a.scores, list, list_count, counters);
+    else
+      k_rescore<false><<<(unsigned)((m + rb - 1) / rb), rb, 0, e->stream>>>(
+          a.x, (long)a.n, (int)d, a.ids, (long)c0, (long)m, a.c, a.cnorm, a.xnorm, cand, cand_cnt,
+          a.labels, a.scores, list, list_count, counters);
+    EB_LAUNCH("screen rescore");
+    Top1Args fa = a;
+    fa.r0 = c0;
+    fa.r1 = c0 + m;
+    top1_exact_list(e, fa, list, list_count, m);
+  }
+  e->stats.screened_rows += m_all;
 }
 
 }  // namespace eb
