@@ -102,6 +102,7 @@ def load():
         "eb_sync": (I, [P]),
         "eb_get_stats": (I, [P, C.POINTER(Stats)]),
         "eb_engine_stream": (I, [P, C.POINTER(P)]),
+        "eb_set_screen_mode": (I, [P, I]),
         "eb_buf_alloc": (I, [P, I, S, C.POINTER(P)]),
         "eb_buf_wrap": (I, [P, I, P, S, C.POINTER(P)]),
         "eb_buf_free": (I, [P, P]),
@@ -263,6 +264,11 @@ class Engine:
 
     def flush(self):
         _check(load().eb_flush(self.h))
+
+    def set_screen_mode(self, mode: int):
+        """Top-1 path: 0 exact SIMT only, 1 auto (default), 2 tensor-core screen always.
+        Results are identical in every mode."""
+        _check(load().eb_set_screen_mode(self.h, mode))
 
     def stream(self) -> int:
         """The engine's cudaStream_t, for torch.cuda.ExternalStream and events."""

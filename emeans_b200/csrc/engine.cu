@@ -160,8 +160,11 @@ int eb_engine_create(int device, eb_engine** out) {
       EB_CUDA(cudaMemset(e->d_status, 0, 16));
       EB_CUDA(cudaMallocHost(&e->h_status, 16));
       *e->h_status = 0;
+      EB_CUDA(cudaMalloc(&e->d_counters, 4 * sizeof(unsigned long long)));
+      EB_CUDA(cudaMemset(e->d_counters, 0, 4 * sizeof(unsigned long long)));
       const char* sc = getenv("EMEANS_B200_SCREEN");
-      e->tc_enabled = !(sc && std::string(sc) == "0");
+      if (sc && (sc[0] == '0' || sc[0] == '1' || sc[0] == '2') && sc[1] == 0)
+        e->screen_mode = sc[0] - '0';
     } catch (...) {
       if (prev >= 0) cudaSetDevice(prev);
       delete e;
@@ -182,6 +185,7 @@ int eb_engine_destroy(eb_engine* e) {
       if (kv.second.p) cudaFreeAsync(kv.second.p, e->stream);
     cudaStreamSynchronize(e->stream);
     cudaFree(e->d_status);
+    cudaFree(e->d_counters);
     cudaFreeHost(e->h_status);
     cudaStreamDestroy(e->stream);
     delete e;
@@ -192,7 +196,7 @@ int eb_engine_name(eb_engine* e, char* buf, size_t cap) {
   return guard([&] {
     need(e, "engine");
     need(buf, "buf");
-    std::string name = e->tc_enabled ? "b200-exact" : "b200-exact-simt";
+    std::string name = e->screen_mode ? "b200-exact" : "b200-exact-simt";
     ensure(cap > name.size(), "name buffer too small");
     std::memcpy(buf, name.c_str(), name.size() + 1);
   });
@@ -222,7 +226,21 @@ int eb_get_stats(eb_engine* e, eb_stats* out) {
   return guard([&] {
     need(e, "engine");
     need(out, "out");
+    DeviceGuard g(e);
+    unsigned long long c[4];
+    EB_CUDA(cudaMemcpyAsync(c, e->d_counters, sizeof(c), cudaMemcpyDeviceToHost, e->stream));
+    eb::sync(e);
     *out = e->stats;
+    out->fallback_rows = c[1];
+    out->rescored_candidates = c[2];
+  });
+}
+
+int eb_set_screen_mode(eb_engine* e, int mode) {
+  return guard([&] {
+    need(e, "engine");
+    ensure(mode >= 0 && mode <= 2, "screen mode must be 0 (off), 1 (auto) or 2 (always)");
+    e->screen_mode = mode;
   });
 }
 

@@ -80,7 +80,12 @@ struct eb_engine {
   const float* bound_host = nullptr;
   size_t bound_n = 0;
   int num_sms = 148;
-  bool tc_enabled = true;  // tensor-core screen for top-1 (EMEANS_B200_SCREEN=0 turns it off)
+  // Tensor-core screen for top-1: 0 off, 1 auto (large enough calls), 2 always.
+  // EMEANS_B200_SCREEN=0/1/2 sets it at creation; eb_set_screen_mode later.
+  int screen_mode = 1;
+  // Device counters: [0] unused, [1] fallback rows, [2] re-scored candidates.
+  unsigned long long* d_counters = nullptr;
+  unsigned long long* counters() { return d_counters; }
 
   template <class T>
   T* scratch_get(const char* name, size_t count) {

@@ -40,14 +40,14 @@ __global__ void __launch_bounds__(NT) k_top1_exact(
 
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
+  const long total = list ? (long)*list_count : r1 - r0;
 
-  // Positions of this block's rows.
+  // Tiles of BM rows, grid-stride (the list length is only known on the device).
+  for (long tile = blockIdx.x; tile * BM < total; tile += gridDim.x) {
   long nrows;
   if (list) {
-    long cnt = (long)*list_count;
-    long b0 = (long)blockIdx.x * BM;
-    if (b0 >= cnt) return;
-    nrows = min((long)BM, cnt - b0);
+    long b0 = tile * BM;
+    nrows = min((long)BM, total - b0);
     if (tid < BM) {
       long p = tid < nrows ? (long)list[b0 + tid] : -1;
       pos_of[tid] = p;
@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(NT) k_top1_exact(
       row_of[tid] = row;
     }
   } else {
-    long b0 = r0 + (long)blockIdx.x * BM;
+    long b0 = r0 + tile * BM;
     nrows = min((long)BM, r1 - b0);
     if (tid < BM) {
       long p = tid < nrows ? b0 + tid : -1;
@@ -192,6 +192,8 @@ __global__ void __launch_bounds__(NT) k_top1_exact(
       scores[p] = s;
     }
   }
+  __syncthreads();  // pos_of / row_of are rewritten by the next tile
+  }
 }
 
 void launch(eb_engine* e, const Top1Args& a, const uint32_t* list, const uint32_t* count,
@@ -209,7 +211,11 @@ void launch(eb_engine* e, const Top1Args& a, const uint32_t* list, const uint32_
       xn = t;
     }
   }
-  unsigned grid = (unsigned)((rows_bound + BM - 1) / BM);
+  size_t tiles = (rows_bound + BM - 1) / BM;
+  // A list's length is known only on the device: a grid of a few blocks per SM
+  // strides over it, so an empty list costs one short launch.
+  if (list) tiles = std::min<size_t>(tiles, (size_t)e->num_sms * 4);
+  unsigned grid = (unsigned)tiles;
   if (a.metric == EB_IP)
     k_top1_exact<true><<<grid, NT, 0, e->stream>>>(a.x, (long)a.n, (int)a.d, a.ids, (long)a.r0,
                                                    (long)a.r1, list, count, a.c, a.cnorm,

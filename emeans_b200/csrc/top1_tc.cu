@@ -346,6 +346,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // TMA producer: per (tile, k-block), one A box (128 x 64) and one B box (256 x 64).
+      int issued = 0;
       for (int it = 0; it < total; it++) {
         const int s = it % STAGES;
         const uint32_t par = ((it / STAGES) & 1) ^ 1;
@@ -354,6 +355,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
         tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BKH, (int)m0);
         tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * BKH, nt * BN);
+        issued = it + 1;
+      }
+      // No copy may still be landing in shared memory when the CTA exits: wait
+      // (bounded) for the last loads issued. On the normal path they have
+      // already been consumed and these waits return at once.
+      for (int it = issued > STAGES ? issued - STAGES : 0; it < issued; it++) {
+        uint64_t t0 = now_ns();
+        while (!mbar_try_wait(&full[it % STAGES], (it / STAGES) & 1) && now_ns() - t0 < WAIT_NS) {
+        }
       }
     }
   } else if (warp == 1) {
@@ -432,7 +442,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     for (int nt = 0; nt < P.ntiles; nt++) {
       const int a = nt & 1;
-      if (!mbar_wait(&tfull[a], (nt >> 1) & 1, abort_flag)) break;
+      // Warp-uniform: the TMEM loads below are .sync.aligned.
+      const bool ready = __all_sync(0xFFFFFFFFu, mbar_wait(&tfull[a], (nt >> 1) & 1, abort_flag));
+      if (!ready) break;
       tc_fence_after();
       const int col0 = nt * BN;
 #pragma unroll 1
@@ -608,13 +620,14 @@ CUtensorMap make_map(const void* base, size_t rows, size_t dp, uint32_t box_rows
   return m;
 }
 
+// The dynamic shared memory limit is a per-device function attribute.
 template <class K>
-void set_smem(K kernel) {
-  static bool done = false;
-  if (!done) {
+void set_smem(K kernel, int device) {
+  static uint64_t done = 0;
+  if (!(done >> device & 1)) {
     EB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)SMEM_BYTES));
-    done = true;
+    done |= 1ull << device;
   }
 }
 
@@ -682,9 +695,9 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
   P.status = e->d_status;
 
   if (ip)
-    set_smem(k_screen<true>);
+    set_smem(k_screen<true>, e->device);
   else
-    set_smem(k_screen<false>);
+    set_smem(k_screen<false>, e->device);
 
   for (size_t c0 = a.r0; c0 < a.r1; c0 += chunk) {
     const size_t m = std::min(chunk, a.r1 - c0);

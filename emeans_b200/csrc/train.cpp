@@ -19,7 +19,7 @@
 namespace eb {
 
 void top1_dispatch(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
-  if (e->tc_enabled && top1_screen_supported(e, a))
+  if (top1_screen_supported(e, a))
     top1_screen(e, a, xbuf);
   else
     top1_exact(e, a);

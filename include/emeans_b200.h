@@ -96,6 +96,12 @@ typedef struct {
 } eb_stats;
 int eb_get_stats(eb_engine* e, eb_stats* out);
 
+/* Top-1 path: 0 = exact SIMT kernel only, 1 = tensor-core screen + exact
+ * re-score for calls large enough to pay (the default), 2 = screen always.
+ * Results are identical in every mode; only the speed differs. The
+ * environment variable EMEANS_B200_SCREEN=0/1/2 sets it at engine creation. */
+int eb_set_screen_mode(eb_engine* e, int mode);
+
 /* ---------------------------------------------------------------- buffers */
 
 /* Device::zeros_f32 / zeros_u32 (core/mod.rs:84-85): a zeroed buffer of `len`

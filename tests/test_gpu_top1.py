@@ -20,6 +20,14 @@ from tests.helpers import bits, contract_centroids, mixture, near_tie_centroids,
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(params=[0, 2], ids=["exact", "screen"])
+def eng(engine, request):
+    """The session engine on the exact SIMT path (0) or the tcgen05 screen (2)."""
+    engine.set_screen_mode(request.param)
+    yield engine
+    engine.set_screen_mode(1)
+
 SHAPES = [(1000, 768, 64), (777, 768, 100), (513, 13, 70), (2000, 20, 300), (300, 64, 1),
           (600, 768, 1024)]
 
@@ -63,59 +71,77 @@ def check_against_oracle(engine, x, c, metric, ids=None, lo=None, hi=None):
 
 @pytest.mark.parametrize("n,d,k", SHAPES)
 @pytest.mark.parametrize("metric", [eb.IP, eb.L2])
-def test_contract_shapes(engine, n, d, k, metric):
+def test_contract_shapes(eng, n, d, k, metric):
     x = mixture(n, d, 11, 0.6, metric == eb.IP, 3 * n + k)
     c = contract_centroids(x, d, k)
     perm = ((np.arange(n, dtype=np.int64) * 7919 + 13) % n).astype(np.uint32)
     lo, hi = n // 7, n - n // 9
-    check_against_oracle(engine, x, c, metric, ids=perm, lo=lo, hi=hi)
-    check_against_oracle(engine, x, c, metric, lo=lo, hi=hi)
+    check_against_oracle(eng, x, c, metric, ids=perm, lo=lo, hi=hi)
+    check_against_oracle(eng, x, c, metric, lo=lo, hi=hi)
 
 
 @pytest.mark.parametrize("k", [1024, 1000])
 @pytest.mark.parametrize("metric", [eb.IP, eb.L2])
-def test_production_batch_with_duplicate_centroids(engine, k, metric):
+def test_production_batch_with_duplicate_centroids(eng, k, metric):
     n, d = 16384, 768
     x = mixture(n, d, 64, 0.6, metric == eb.IP, 5 * n + k)
     c = production_centroids(x, k)
-    check_against_oracle(engine, x, c, metric)
+    check_against_oracle(eng, x, c, metric)
     # Exact duplicates: the lower id wins.
-    gl, _ = run_top1(engine, x, c, metric)
+    gl, _ = run_top1(eng, x, c, metric)
     assert np.all(gl < k - 256)
 
 
 @pytest.mark.parametrize("metric", [eb.IP, eb.L2])
-def test_near_ties_and_scaled_rows(engine, metric):
+def test_screen_runs_on_large_calls(engine, metric):
+    """Auto mode takes the tensor-core path for a production batch; few rows fall back."""
+    engine.set_screen_mode(1)
+    n, d, k = 16384, 768, 1024
+    x = mixture(n, d, 64, 0.6, metric == eb.IP, 99)
+    c = production_centroids(x, k)
+    s0 = engine.stats()
+    check_against_oracle(engine, x, c, metric)
+    s1 = engine.stats()
+    screened = s1["screened_rows"] - s0["screened_rows"]
+    fallback = s1["fallback_rows"] - s0["fallback_rows"]
+    print(f"screened {screened} rows, {fallback} fell back, "
+          f"{s1['rescored_candidates'] - s0['rescored_candidates']} candidates re-scored")
+    assert screened == n
+    assert fallback < n // 2
+
+
+@pytest.mark.parametrize("metric", [eb.IP, eb.L2])
+def test_near_ties_and_scaled_rows(eng, metric):
     n, d, k = 4096, 256, 512
     c = near_tie_centroids(d, k, 3)
     rng = np.random.default_rng(8)
     x = (c[rng.integers(0, k, n)] + np.float32(1e-3) * rng.standard_normal((n, d))).astype(np.float32)
     scale = np.array([1.0, 1e3, 1e-3, 1e-15], np.float32)[np.arange(n) % 4]
     x = (x * scale[:, None]).astype(np.float32)
-    check_against_oracle(engine, x, c, metric)
+    check_against_oracle(eng, x, c, metric)
 
 
 @pytest.mark.parametrize("metric", [eb.IP, eb.L2])
-def test_odd_shapes(engine, metric):
+def test_odd_shapes(eng, metric):
     rng = np.random.default_rng(0)
     for n, d, k in [(1, 1, 1), (5, 3, 2), (129, 17, 257), (64, 8, 40), (200, 100, 3)]:
         x = rng.standard_normal((n, d)).astype(np.float32)
         c = rng.standard_normal((k, d)).astype(np.float32)
-        check_against_oracle(engine, x, c, metric)
+        check_against_oracle(eng, x, c, metric)
 
 
-def test_ties_keep_the_lowest_id(engine):
+def test_ties_keep_the_lowest_id(eng):
     d = 8
     x = np.ones((3, d), np.float32)
     c = np.zeros((40, d), np.float32)
     for j in (5, 17, 33):
         c[j] = 1.0
     for metric in (eb.IP, eb.L2):
-        gl, _ = run_top1(engine, x, c, metric)
+        gl, _ = run_top1(eng, x, c, metric)
         assert gl.tolist() == [5, 5, 5]
 
 
-def test_nonfinite_rows_follow_the_cpu_semantics(engine):
+def test_nonfinite_rows_follow_the_cpu_semantics(eng):
     d, k = 16, 9
     rng = np.random.default_rng(1)
     x = rng.standard_normal((6, d)).astype(np.float32)
@@ -125,48 +151,48 @@ def test_nonfinite_rows_follow_the_cpu_semantics(engine):
     c = rng.standard_normal((k, d)).astype(np.float32)
     c[4, 2] = np.nan
     for metric in (eb.IP, eb.L2):
-        check_against_oracle(engine, x, c, metric)
+        check_against_oracle(eng, x, c, metric)
 
 
-def test_bad_row_id_is_an_error(engine):
+def test_bad_row_id_is_an_error(eng):
     d = 4
     x = np.ones((10, d), np.float32)
     c = np.ones((3, d), np.float32)
-    xb = engine.bind(x, d)
-    cb = engine.upload_f32(c)
-    ib = engine.upload_u32(np.array([0, 1, 99], np.uint32))
-    lab, sco = engine.zeros_u32(3), engine.zeros_f32(3)
-    engine.top1(xb, d, ib, range(0, 3), cb, None, 3, eb.IP, lab, sco)
+    xb = eng.bind(x, d)
+    cb = eng.upload_f32(c)
+    ib = eng.upload_u32(np.array([0, 1, 99], np.uint32))
+    lab, sco = eng.zeros_u32(3), eng.zeros_f32(3)
+    eng.top1(xb, d, ib, range(0, 3), cb, None, 3, eb.IP, lab, sco)
     with pytest.raises(eb.EngineError) as ei:
-        engine.sync()
+        eng.sync()
     assert ei.value.code == eb.INVALID_ARGUMENT
-    engine.sync()
+    eng.sync()
 
 
-def test_argument_checks(engine):
+def test_argument_checks(eng):
     d = 4
-    xb = engine.bind(np.ones((10, d), np.float32), d)
-    cb = engine.upload_f32(np.ones((3, d), np.float32))
-    lab, sco = engine.zeros_u32(10), engine.zeros_f32(10)
+    xb = eng.bind(np.ones((10, d), np.float32), d)
+    cb = eng.upload_f32(np.ones((3, d), np.float32))
+    lab, sco = eng.zeros_u32(10), eng.zeros_f32(10)
     with pytest.raises(eb.EngineError, match="past the data"):
-        engine.top1(xb, d, None, range(0, 11), cb, None, 3, eb.IP, lab, sco)
+        eng.top1(xb, d, None, range(0, 11), cb, None, 3, eb.IP, lab, sco)
     with pytest.raises(eb.EngineError, match="centroid norms"):
-        engine.top1(xb, d, None, range(0, 10), cb, None, 3, eb.L2, lab, sco)
+        eng.top1(xb, d, None, range(0, 10), cb, None, 3, eb.L2, lab, sco)
     with pytest.raises(eb.EngineError, match="k x d"):
-        engine.top1(xb, d, None, range(0, 10), cb, None, 4, eb.IP, lab, sco)
+        eng.top1(xb, d, None, range(0, 10), cb, None, 4, eb.IP, lab, sco)
 
 
 @pytest.mark.parametrize("metric", [eb.IP, eb.L2])
-def test_assign_host_api(engine, metric):
+def test_assign_host_api(eng, metric):
     n, d, k = 3000, 96, 130
     x = mixture(n, d, 20, 0.5, metric == eb.IP, 77)
     c = contract_centroids(x, d, k)
-    gl, gs = engine.assign(x, d, c, metric)
+    gl, gs = eng.assign(x, d, c, metric)
     wl, ws = oracle.top1(x.ravel(), d, c.ravel(), metric)
     assert np.array_equal(gl, wl) and np.array_equal(bits(gs), bits(ws))
     ids = np.random.default_rng(2).permutation(n)[:777].astype(np.uint32)
-    engine.bind_data(x, d)
-    gl, gs = engine.assign(engine._bound, d, c, metric, ids=ids)
-    engine.unbind_data()
+    eng.bind_data(x, d)
+    gl, gs = eng.assign(eng._bound, d, c, metric, ids=ids)
+    eng.unbind_data()
     wl, ws = oracle.top1(x.ravel(), d, c.ravel(), metric, ids=ids)
     assert np.array_equal(gl, wl) and np.array_equal(bits(gs), bits(ws))
