@@ -620,12 +620,12 @@ CUtensorMap make_map(const void* base, size_t rows, size_t dp, uint32_t box_rows
   return m;
 }
 
-// The dynamic shared memory limit is a per-device function attribute.
-template <class K>
-void set_smem(K kernel, int device) {
-  static uint64_t done = 0;
+// The dynamic shared memory limit is a per-device, per-kernel attribute.
+template <bool IP>
+void set_smem(int device) {
+  static uint64_t done = 0;  // one instance per kernel: IP is a template parameter
   if (!(done >> device & 1)) {
-    EB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    EB_CUDA(cudaFuncSetAttribute(k_screen<IP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)SMEM_BYTES));
     done |= 1ull << device;
   }
@@ -695,9 +695,9 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
   P.status = e->d_status;
 
   if (ip)
-    set_smem(k_screen<true>, e->device);
+    set_smem<true>(e->device);
   else
-    set_smem(k_screen<false>, e->device);
+    set_smem<false>(e->device);
 
   for (size_t c0 = a.r0; c0 < a.r1; c0 += chunk) {
     const size_t m = std::min(chunk, a.r1 - c0);
