@@ -57,7 +57,8 @@ constexpr int BKH = 64;          // FP16 columns per k-block: one 128-byte swizz
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BKH * 2;
 constexpr int B_BYTES = BN * BKH * 2;
-constexpr int KSLOTS = 8;        // candidates kept per row
+constexpr int KSLOTS = 8;        // candidates kept in registers per row
+constexpr int CAP = 128;         // per-row candidate list: KSLOTS + spilled entries
 constexpr int NTHREADS = 192;    // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr uint32_t FALLBACK = 0xFFFFFFFFu;
 constexpr int XEXP_BAD = INT_MIN;  // row with a non-finite value
@@ -294,8 +295,9 @@ struct ScreenParams {
   const float* cn;     // k squared centroid norms (L2) or null
   const uint32_t* cinfo;
   float e_rel, e_abs, e_min;  // bound coefficients (see the header comment)
-  uint32_t* cand;      // m x KSLOTS
-  uint32_t* cand_cnt;  // m: count, or FALLBACK
+  uint2* cand;         // m x CAP (id, screened value bits); entries 0..KSLOTS-1 from registers
+  uint32_t* cand_cnt;  // m: entries in use, or FALLBACK
+  float* cand_thr;     // m: the final admission threshold
   uint32_t* status;
 };
 
@@ -438,6 +440,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       sj[s] = FALLBACK;
     }
     bool overflow = false;
+    int nspill = 0;  // entries spilled to the row's list after the register slots
+    uint2* row_list = P.cand + (live ? i : 0) * (long)CAP;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
 
     for (int nt = 0; nt < P.ntiles; nt++) {
@@ -487,7 +491,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 placed = true;
               }
             }
-            overflow |= !placed;
+            if (!placed) {
+              // Registers full of live candidates: spill to the row's list.
+              if (live && nspill < CAP - KSLOTS) {
+                row_list[KSLOTS + nspill] = make_uint2((uint32_t)(cb + j), __float_as_uint(s));
+                nspill++;
+              } else {
+                overflow = true;
+              }
+            }
           }
         }
       }
@@ -495,15 +507,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_arrive(&tempty[a]);
     }
     if (live) {
-      uint32_t cnt = 0;
-      if (!fallback && !overflow && isfinite(best) && !*abort_flag) {
+      const bool ok = !fallback && !overflow && isfinite(best) && !*abort_flag;
+      if (ok) {
+        // Register slots go to entries 0..KSLOTS-1 (empty ones carry FALLBACK as id);
+        // the re-score admits entries against the final threshold.
 #pragma unroll
-        for (int s = 0; s < KSLOTS; s++) {
-          const bool in = IP ? (sv[s] >= thr) : (sv[s] <= thr);
-          if (in && sj[s] != FALLBACK) P.cand[i * KSLOTS + cnt++] = sj[s];
-        }
+        for (int s = 0; s < KSLOTS; s++) row_list[s] = make_uint2(sj[s], __float_as_uint(sv[s]));
+        P.cand_thr[i] = thr;
       }
-      P.cand_cnt[i] = cnt == 0 ? FALLBACK : cnt;
+      P.cand_cnt[i] = ok ? (uint32_t)(KSLOTS + nspill) : FALLBACK;
     }
   }
 
@@ -539,50 +551,70 @@ __device__ __forceinline__ float chain(const float* __restrict__ x, const float*
 }
 
 template <bool IP>
+__device__ __forceinline__ bool better(float v, uint32_t j, float bv, uint32_t bj) {
+  if (bj == FALLBACK) return true;
+  return IP ? (v > bv || (v == bv && j < bj)) : (v < bv || (v == bv && j < bj));
+}
+
+// One warp per row: lanes take the row's admitted candidates, each computes
+// the exact chain, and the warp keeps the best (lower id on ties). Rows the
+// screen could not certify go to the exact kernel's list.
+template <bool IP>
 __global__ void k_rescore(const float* __restrict__ x, long n, int d,
                           const uint32_t* __restrict__ ids, long p0, long m,
                           const float* __restrict__ c, const float* __restrict__ cn,
-                          const float* __restrict__ xnorm_row, const uint32_t* __restrict__ cand,
-                          const uint32_t* __restrict__ cand_cnt, uint32_t* __restrict__ labels,
+                          const float* __restrict__ xnorm_row, const float* __restrict__ xnorm_pos,
+                          const uint2* __restrict__ cand, const uint32_t* __restrict__ cand_cnt,
+                          const float* __restrict__ cand_thr, uint32_t* __restrict__ labels,
                           float* __restrict__ scores, uint32_t* __restrict__ list,
                           uint32_t* __restrict__ list_count,
                           unsigned long long* __restrict__ counters) {
-  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
   if (i >= m) return;
   const long p = p0 + i;
   const uint32_t cnt = cand_cnt[i];
-  if (cnt == FALLBACK) {
+  float best = IP ? -INFINITY : INFINITY;
+  uint32_t bj = FALLBACK;
+  uint32_t nres = 0;
+  long row = 0;
+  if (cnt != FALLBACK) {
+    const float thr = cand_thr[i];
+    row = ids ? (long)ids[p] : p;
+    const float* xr = x + row * (long)d;
+    for (uint32_t e = lane; e < cnt; e += 32) {
+      const uint2 en = cand[i * (long)CAP + e];
+      const float sv = __uint_as_float(en.y);
+      if (en.x == FALLBACK || !(IP ? sv >= thr : sv <= thr)) continue;
+      nres++;
+      float v = chain(xr, c + (long)en.x * d, d);
+      if (!IP) v = __fsub_rn(__ldg(cn + en.x), __fmul_rn(2.0f, v));
+      if (better<IP>(v, en.x, best, bj)) {
+        best = v;
+        bj = en.x;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+    const uint32_t oj = __shfl_xor_sync(0xFFFFFFFFu, bj, o);
+    nres += __shfl_xor_sync(0xFFFFFFFFu, nres, o);
+    if (oj != FALLBACK && better<IP>(ov, oj, best, bj)) {
+      best = ov;
+      bj = oj;
+    }
+  }
+  if (lane != 0) return;
+  if (bj == FALLBACK) {
     list[atomicAdd(list_count, 1u)] = (uint32_t)p;
     atomicAdd(&counters[1], 1ull);
     return;
   }
-  const long row = ids ? (long)ids[p] : p;
-  const float* xr = x + row * (long)d;
-  float best = IP ? -INFINITY : INFINITY;
-  uint32_t bj = 0xFFFFFFFFu;
-  for (uint32_t s = 0; s < cnt; s++) {
-    const uint32_t j = cand[i * KSLOTS + s];
-    float v = chain(xr, c + (long)j * d, d);
-    if (!IP) v = __fsub_rn(__ldg(cn + j), __fmul_rn(2.0f, v));
-    const bool better = IP ? (v > best || (v == best && j < bj)) : (v < best || (v == best && j < bj));
-    if (better || bj == 0xFFFFFFFFu) {
-      best = v;
-      bj = j;
-    }
-  }
-  atomicAdd(&counters[2], (unsigned long long)cnt);
+  atomicAdd(&counters[2], (unsigned long long)nres);
   float score = best;
   if (!IP) {
-    float xn;
-    if (xnorm_row) {
-      xn = xnorm_row[row];
-    } else {
-      xn = -0.0f;
-      for (int t = 0; t < d; t++) {
-        float v = __ldg(xr + t);
-        xn = __fadd_rn(xn, __fmul_rn(v, v));
-      }
-    }
+    const float xn = xnorm_row ? xnorm_row[row] : xnorm_pos[i];
     score = fmaxf(__fadd_rn(xn, best), 0.0f);
   }
   labels[p] = bj;
@@ -672,8 +704,10 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
   __half* xh = e->scratch_get<__half>("tc_xh", chunk * dp);
   int* xexp = e->scratch_get<int>("tc_xexp", chunk);
   float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
-  uint32_t* cand = e->scratch_get<uint32_t>("tc_cand", chunk * KSLOTS);
+  uint2* cand = e->scratch_get<uint2>("tc_cand", chunk * CAP);
   uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", chunk);
+  float* cand_thr = e->scratch_get<float>("tc_thr", chunk);
+  float* xnorm_pos = (!ip && !a.xnorm) ? e->scratch_get<float>("tc_xnorm_pos", chunk) : nullptr;
   uint32_t* list = e->scratch_get<uint32_t>("tc_list", chunk);
   uint32_t* list_count = e->scratch_get<uint32_t>("tc_list_count", 4);
   unsigned long long* counters = e->counters();
@@ -692,6 +726,7 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
   P.e_min = e_min;
   P.cand = cand;
   P.cand_cnt = cand_cnt;
+  P.cand_thr = cand_thr;
   P.status = e->d_status;
 
   if (ip)
@@ -713,15 +748,17 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
       k_screen<false><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(mapA, mapB, P);
     EB_LAUNCH("screen");
     EB_CUDA(cudaMemsetAsync(list_count, 0, 4, e->stream));
-    const unsigned rb = 128;
+    if (xnorm_pos) sel_row_norms(e, a.x, a.n, d, a.ids, c0, c0 + m, xnorm_pos);
+    const unsigned rw = 8;  // rows (warps) per block
+    const unsigned rgrid = (unsigned)((m + rw - 1) / rw);
     if (ip)
-      k_rescore<true><<<(unsigned)((m + rb - 1) / rb), rb, 0, e->stream>>>(
-          a.x, (long)a.n, (int)d, a.ids, (long)c0, (long)m, a.c, a.cnorm, a.xnorm, cand, cand_cnt,
-          a.labels, a.scores, list, list_count, counters);
+      k_rescore<true><<<rgrid, rw * 32, 0, e->stream>>>(
+          a.x, (long)a.n, (int)d, a.ids, (long)c0, (long)m, a.c, a.cnorm, a.xnorm, xnorm_pos,
+          cand, cand_cnt, cand_thr, a.labels, a.scores, list, list_count, counters);
     else
-      k_rescore<false><<<(unsigned)((m + rb - 1) / rb), rb, 0, e->stream>>>(
-          a.x, (long)a.n, (int)d, a.ids, (long)c0, (long)m, a.c, a.cnorm, a.xnorm, cand, cand_cnt,
-          a.labels, a.scores, list, list_count, counters);
+      k_rescore<false><<<rgrid, rw * 32, 0, e->stream>>>(
+          a.x, (long)a.n, (int)d, a.ids, (long)c0, (long)m, a.c, a.cnorm, a.xnorm, xnorm_pos,
+          cand, cand_cnt, cand_thr, a.labels, a.scores, list, list_count, counters);
     EB_LAUNCH("screen rescore");
     Top1Args fa = a;
     fa.r0 = c0;
