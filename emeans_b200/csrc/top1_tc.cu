@@ -12,15 +12,19 @@
 //    accumulators in TMEM (two buffers of 256 columns, so the epilogue reads
 //    one while the tensor cores fill the other), operands staged by TMA into
 //    128B-swizzled shared memory through a 4-stage mbarrier ring. The
-//    epilogue (one thread per row) keeps the running best screened value and
-//    every centroid within 2e of it, where e bounds |screen - exact chain|
-//    (FP16 rounding of both operands, tensor-core accumulation, the FP32 chain
-//    itself); a centroid more than 2e behind the best cannot be the exact
-//    winner. At most KSLOTS candidates are kept; more mark the row for the
-//    full exact scan.
-// 3. rescore: the exact FMA chain for each candidate; lower id on ties.
-// 4. fallback: rows with more candidates than slots, or non-finite inputs,
-//    take the exact SIMT kernel (top1_exact.cu).
+//    epilogue (one thread per row) reads each 256-column tile from TMEM twice:
+//    first for the tile's best score, which moves the row's running best, then
+//    to append every centroid within 2e of that best to the row's candidate
+//    list, where e bounds |screen - exact chain| (FP16 rounding of both
+//    operands, tensor-core accumulation, the FP32 chain itself). A centroid
+//    more than 2e behind the best cannot be the exact winner.
+// 3. refine (one warp per row): a precise FP32 dot per candidate with its own
+//    error bound (from the computed sum |x_t c_t|) leaves the candidates that
+//    could still be the exact best, usually one.
+// 4. exact (one thread per row): the exact FMA chain of each survivor; lower
+//    id on ties.
+// 5. fallback: rows with too many candidates, or non-finite inputs, take the
+//    exact SIMT kernel (top1_exact.cu).
 //
 // Error bound (acc units, operands scaled): with u = 2^-11 and FP16
 // subnormals (half-ulp 2^-25),
@@ -57,8 +61,7 @@ constexpr int BKH = 64;          // FP16 columns per k-block: one 128-byte swizz
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BKH * 2;
 constexpr int B_BYTES = BN * BKH * 2;
-constexpr int KSLOTS = 8;        // candidates kept in registers per row
-constexpr int CAP = 128;         // per-row candidate list: KSLOTS + spilled entries
+constexpr int CAP = 128;         // per-row candidate list capacity
 constexpr int NTHREADS = 192;    // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr uint32_t FALLBACK = 0xFFFFFFFFu;
 constexpr int XEXP_BAD = INT_MIN;  // row with a non-finite value
@@ -181,6 +184,41 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Screened scores of 32 columns (cb .. cb+31) of this thread's row: the raw
+// accumulator (IP), or the key cn_j - 2 f acc_j with one rounding (L2).
+// Columns past k score -inf (IP) / +inf (L2), so they never win or enter.
+template <bool IP>
+__device__ __forceinline__ void chunk_scores(uint32_t taddr, int cb, int k,
+                                             const float* __restrict__ cn, float m2f,
+                                             float (&s)[32]) {
+  uint32_t v[32];
+  tmem_ld32(taddr, v);
+  if (cb + 32 <= k) {
+    if (IP) {
+#pragma unroll
+      for (int j = 0; j < 32; j++) s[j] = __uint_as_float(v[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 c4 = __ldg(reinterpret_cast<const float4*>(cn + cb + j));
+        s[j] = __fmaf_rn(m2f, __uint_as_float(v[j]), c4.x);
+        s[j + 1] = __fmaf_rn(m2f, __uint_as_float(v[j + 1]), c4.y);
+        s[j + 2] = __fmaf_rn(m2f, __uint_as_float(v[j + 2]), c4.z);
+        s[j + 3] = __fmaf_rn(m2f, __uint_as_float(v[j + 3]), c4.w);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      const bool in = cb + j < k;
+      if (IP)
+        s[j] = in ? __uint_as_float(v[j]) : -INFINITY;
+      else
+        s[j] = in ? __fmaf_rn(m2f, __uint_as_float(v[j]), __ldg(cn + cb + j)) : INFINITY;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- prep kernels
 
 // Scaled FP16 copy of the selected rows (one warp per row), with the row's
@@ -295,7 +333,7 @@ struct ScreenParams {
   const float* cn;     // k squared centroid norms (L2) or null
   const uint32_t* cinfo;
   float e_rel, e_abs, e_min;  // bound coefficients (see the header comment)
-  uint2* cand;         // m x CAP (id, screened value bits); entries 0..KSLOTS-1 from registers
+  uint2* cand;         // m x CAP (id, screened value bits)
   uint32_t* cand_cnt;  // m: entries in use, or FALLBACK
   float* cand_thr;     // m: the final admission threshold
   uint32_t* status;
@@ -430,17 +468,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       off = 2.0f * e_key;
     }
     if (!isfinite(off)) fallback = true;
+    const bool collect = live && !fallback;
     float best = IP ? -INFINITY : INFINITY;
     float thr = best;
-    float sv[KSLOTS];
-    uint32_t sj[KSLOTS];
-#pragma unroll
-    for (int s = 0; s < KSLOTS; s++) {
-      sv[s] = IP ? -INFINITY : INFINITY;
-      sj[s] = FALLBACK;
-    }
     bool overflow = false;
-    int nspill = 0;  // entries spilled to the row's list after the register slots
+    uint32_t cnt = 0;  // entries in this row's candidate list
     uint2* row_list = P.cand + (live ? i : 0) * (long)CAP;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
 
@@ -451,55 +483,44 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!ready) break;
       tc_fence_after();
       const int col0 = nt * BN;
+      const int nch = min(BN / 32, (P.k - col0 + 31) / 32);
+      const uint32_t tbase = lane_base + (uint32_t)(a * BN);
+      // Pass 1: the tile's best score moves the threshold first, so that
+      // pass 2 admits only what can still be within 2e of the final best.
+      float tb = IP ? -INFINITY : INFINITY;
 #pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ch++) {
-        uint32_t v[32];
-        tmem_ld32(lane_base + (uint32_t)(a * BN + ch * 32), v);
-        const int cb = col0 + ch * 32;
-        if (cb >= P.k) break;
-        const bool partial = cb + 32 > P.k;
-        float cnv[32];
-        if (!IP) {
+      for (int ch = 0; ch < nch; ch++) {
+        float s[32];
+        chunk_scores<IP>(tbase + (uint32_t)(ch * 32), col0 + ch * 32, P.k, P.cn, m2f, s);
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            float4 c4 = (cb + j + 4 <= P.k) ? __ldg(reinterpret_cast<const float4*>(P.cn + cb + j))
-                                            : make_float4(0.f, 0.f, 0.f, 0.f);
-            cnv[j] = c4.x;
-            cnv[j + 1] = c4.y;
-            cnv[j + 2] = c4.z;
-            cnv[j + 3] = c4.w;
-          }
-          if (partial)
-            for (int j = 0; j < 32; j++) cnv[j] = (cb + j < P.k) ? __ldg(P.cn + cb + j) : 0.0f;
-        }
+        for (int j = 0; j < 32; j++) tb = IP ? fmaxf(tb, s[j]) : fminf(tb, s[j]);
+      }
+      if (IP ? (tb > best) : (tb < best)) {
+        best = tb;
+        thr = IP ? __fsub_rd(best, off) : __fadd_ru(best, off);
+      }
+      // Pass 2: append every score within the window to the row's list.
+#pragma unroll 1
+      for (int ch = 0; ch < nch; ch++) {
+        float s[32];
+        chunk_scores<IP>(tbase + (uint32_t)(ch * 32), col0 + ch * 32, P.k, P.cn, m2f, s);
 #pragma unroll
         for (int j = 0; j < 32; j++) {
-          float s = IP ? __uint_as_float(v[j]) : fmaf(m2f, __uint_as_float(v[j]), cnv[j]);
-          const bool admit = IP ? (s >= thr) : (s <= thr);
-          if (admit && (!partial || cb + j < P.k)) {
-            if (IP ? (s > best) : (s < best)) {
-              best = s;
-              thr = IP ? __fsub_rd(best, off) : __fadd_ru(best, off);
-            }
-            bool placed = false;
-#pragma unroll
-            for (int q2 = 0; q2 < KSLOTS; q2++) {
-              const bool stale = IP ? !(sv[q2] >= thr) : !(sv[q2] <= thr);
-              if (!placed && stale) {
-                sv[q2] = s;
-                sj[q2] = (uint32_t)(cb + j);
-                placed = true;
+          if (collect && (IP ? (s[j] >= thr) : (s[j] <= thr))) {
+            if (cnt == CAP) {
+              // Full: drop the entries the current window has left behind.
+              uint32_t w = 0;
+              for (uint32_t e2 = 0; e2 < CAP; e2++) {
+                const uint2 en = row_list[e2];
+                const float sv = __uint_as_float(en.y);
+                if (IP ? (sv >= thr) : (sv <= thr)) row_list[w++] = en;
               }
+              cnt = w;
             }
-            if (!placed) {
-              // Registers full of live candidates: spill to the row's list.
-              if (live && nspill < CAP - KSLOTS) {
-                row_list[KSLOTS + nspill] = make_uint2((uint32_t)(cb + j), __float_as_uint(s));
-                nspill++;
-              } else {
-                overflow = true;
-              }
-            }
+            if (cnt < CAP)
+              row_list[cnt++] = make_uint2((uint32_t)(col0 + ch * 32 + j), __float_as_uint(s[j]));
+            else
+              overflow = true;
           }
         }
       }
@@ -507,15 +528,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_arrive(&tempty[a]);
     }
     if (live) {
-      const bool ok = !fallback && !overflow && isfinite(best) && !*abort_flag;
-      if (ok) {
-        // Register slots go to entries 0..KSLOTS-1 (empty ones carry FALLBACK as id);
-        // the re-score admits entries against the final threshold.
-#pragma unroll
-        for (int s = 0; s < KSLOTS; s++) row_list[s] = make_uint2(sj[s], __float_as_uint(sv[s]));
-        P.cand_thr[i] = thr;
-      }
-      P.cand_cnt[i] = ok ? (uint32_t)(KSLOTS + nspill) : FALLBACK;
+      const bool ok = collect && !overflow && isfinite(best) && !*abort_flag;
+      if (ok) P.cand_thr[i] = thr;
+      P.cand_cnt[i] = ok ? cnt : FALLBACK;
     }
   }
 
@@ -529,16 +544,163 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 }
 
 // ---------------------------------------------------------------- exact re-score
+//
+// Stage 1 (k_refine, one warp per row): each admitted candidate gets a precise
+// FP32 dot with the lanes splitting d, plus the sum of |x_t c_t| that bounds
+// its error; only candidates that could still be the exact best survive.
+// Stage 2 (k_exact, one thread per row): the exact FMA chain of each survivor
+// (usually one) gives the label and the bit-exact score.
 
-// Exact FMA chain of row x against centroid c over d columns.
+constexpr int SURV = 8;  // survivors per row kept for the exact chains
+
+template <bool IP>
+__device__ __forceinline__ bool better(float v, uint32_t j, float bv, uint32_t bj) {
+  if (bj == FALLBACK) return true;
+  return IP ? (v > bv || (v == bv && j < bj)) : (v < bv || (v == bv && j < bj));
+}
+
+__device__ __forceinline__ void to_list(uint32_t p, uint32_t* list, uint32_t* list_count,
+                                        unsigned long long* counters) {
+  list[atomicAdd(list_count, 1u)] = p;
+  atomicAdd(&counters[1], 1ull);
+}
+
+template <bool IP>
+__global__ void __launch_bounds__(256) k_refine(
+    const float* __restrict__ x, int d, const uint32_t* __restrict__ ids, long p0, long m,
+    const float* __restrict__ c, const float* __restrict__ cn, const uint2* __restrict__ cand,
+    const uint32_t* __restrict__ cand_cnt, const float* __restrict__ cand_thr, float e2,
+    uint32_t* __restrict__ surv, uint32_t* __restrict__ surv_cnt, uint32_t* __restrict__ list,
+    uint32_t* __restrict__ list_count, unsigned long long* __restrict__ counters) {
+  __shared__ float pv_s[8][CAP], pe_s[8][CAP];
+  __shared__ uint32_t pj_s[8][CAP];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long i = (long)blockIdx.x * 8 + w;
+  if (i >= m) return;
+  const uint32_t cnt = cand_cnt[i];
+  if (cnt == FALLBACK) {
+    if (lane == 0) {
+      surv_cnt[i] = 0;
+      to_list((uint32_t)(p0 + i), list, list_count, counters);
+    }
+    return;
+  }
+  const float thr = cand_thr[i];
+  const long p = p0 + i;
+  const long row = ids ? (long)ids[p] : p;
+  const float* xr = x + row * (long)d;
+  float* pv = pv_s[w];
+  float* pe = pe_s[w];
+  uint32_t* pj = pj_s[w];
+  int np = 0;
+  for (uint32_t e = 0; e < cnt; e++) {
+    const uint2 en = cand[i * (long)CAP + e];
+    const float sv = __uint_as_float(en.y);
+    if (!(IP ? sv >= thr : sv <= thr)) continue;  // left behind by the window
+    const float* cr = c + (long)en.x * d;
+    float dot = 0.0f, ab = 0.0f;
+    if ((d & 3) == 0) {
+      const float4* x4 = reinterpret_cast<const float4*>(xr);
+      const float4* c4 = reinterpret_cast<const float4*>(cr);
+      for (int t = lane; t < d / 4; t += 32) {
+        const float4 xa = __ldg(x4 + t), ca = __ldg(c4 + t);
+        dot = __fmaf_rn(xa.x, ca.x, dot);
+        dot = __fmaf_rn(xa.y, ca.y, dot);
+        dot = __fmaf_rn(xa.z, ca.z, dot);
+        dot = __fmaf_rn(xa.w, ca.w, dot);
+        ab = __fmaf_rn(fabsf(xa.x), fabsf(ca.x), ab);
+        ab = __fmaf_rn(fabsf(xa.y), fabsf(ca.y), ab);
+        ab = __fmaf_rn(fabsf(xa.z), fabsf(ca.z), ab);
+        ab = __fmaf_rn(fabsf(xa.w), fabsf(ca.w), ab);
+      }
+    } else {
+      for (int t = lane; t < d; t += 32) {
+        const float xa = __ldg(xr + t), ca = __ldg(cr + t);
+        dot = __fmaf_rn(xa, ca, dot);
+        ab = __fmaf_rn(fabsf(xa), fabsf(ca), ab);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      dot = __fadd_rn(dot, __shfl_xor_sync(0xFFFFFFFFu, dot, o));
+      ab = __fadd_rn(ab, __shfl_xor_sync(0xFFFFFFFFu, ab, o));
+    }
+    float v, err;
+    if (IP) {
+      v = dot;
+      err = __fmaf_ru(e2, ab, 1e-37f);
+    } else {
+      const float cj = __ldg(cn + en.x);
+      v = __fsub_rn(cj, __fmul_rn(2.0f, dot));
+      // key error: twice the dot error plus the two key roundings.
+      err = __fmaf_ru(2.0f * e2, ab, __fmaf_ru(ldexpf(1.0f, -22), fabsf(v), 1e-37f));
+    }
+    if (lane == 0) {
+      pv[np] = v;
+      pe[np] = err;
+      pj[np] = en.x;
+    }
+    np++;
+  }
+  __syncwarp();
+  // The best provable bound over the candidates, then every candidate that
+  // could still beat it.
+  float lim = IP ? -INFINITY : INFINITY;
+  for (int e = lane; e < np; e += 32)
+    lim = IP ? fmaxf(lim, __fsub_rd(pv[e], pe[e])) : fminf(lim, __fadd_ru(pv[e], pe[e]));
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float ol = __shfl_xor_sync(0xFFFFFFFFu, lim, o);
+    lim = IP ? fmaxf(lim, ol) : fminf(lim, ol);
+  }
+  int ns = 0;
+  for (int base = 0; base < np; base += 32) {
+    const int e = base + lane;
+    const bool keep = e < np && (IP ? __fadd_ru(pv[e], pe[e]) >= lim
+                                    : __fsub_rd(pv[e], pe[e]) <= lim);
+    const uint32_t mask = __ballot_sync(0xFFFFFFFFu, keep);
+    const int slot = ns + __popc(mask & ((1u << lane) - 1u));
+    if (keep && slot < SURV) surv[i * SURV + slot] = pj[e];
+    ns += __popc(mask);
+  }
+  if (lane == 0) {
+    atomicAdd(&counters[2], (unsigned long long)np);
+    if (ns == 0 || ns > SURV) {
+      surv_cnt[i] = 0;
+      to_list((uint32_t)p, list, list_count, counters);
+    } else {
+      surv_cnt[i] = (uint32_t)ns;
+    }
+  }
+}
+
+// Exact FMA chain of row x against centroid c over d columns, loads kept
+// several steps ahead of the dependent FMAs.
 __device__ __forceinline__ float chain(const float* __restrict__ x, const float* __restrict__ c,
                                        int d) {
   float acc = 0.0f;
   if ((d & 3) == 0) {
     const float4* x4 = reinterpret_cast<const float4*>(x);
     const float4* c4 = reinterpret_cast<const float4*>(c);
-    for (int t = 0; t < d / 4; t++) {
-      float4 a = __ldg(x4 + t), b = __ldg(c4 + t);
+    const int q = d / 4;
+    int t = 0;
+    for (; t + 4 <= q; t += 4) {
+      float4 a[4], b[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        a[u] = __ldg(x4 + t + u);
+        b[u] = __ldg(c4 + t + u);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        acc = __fmaf_rn(a[u].x, b[u].x, acc);
+        acc = __fmaf_rn(a[u].y, b[u].y, acc);
+        acc = __fmaf_rn(a[u].z, b[u].z, acc);
+        acc = __fmaf_rn(a[u].w, b[u].w, acc);
+      }
+    }
+    for (; t < q; t++) {
+      const float4 a = __ldg(x4 + t), b = __ldg(c4 + t);
       acc = __fmaf_rn(a.x, b.x, acc);
       acc = __fmaf_rn(a.y, b.y, acc);
       acc = __fmaf_rn(a.z, b.z, acc);
@@ -551,72 +713,31 @@ __device__ __forceinline__ float chain(const float* __restrict__ x, const float*
 }
 
 template <bool IP>
-__device__ __forceinline__ bool better(float v, uint32_t j, float bv, uint32_t bj) {
-  if (bj == FALLBACK) return true;
-  return IP ? (v > bv || (v == bv && j < bj)) : (v < bv || (v == bv && j < bj));
-}
-
-// One warp per row: lanes take the row's admitted candidates, each computes
-// the exact chain, and the warp keeps the best (lower id on ties). Rows the
-// screen could not certify go to the exact kernel's list.
-template <bool IP>
-__global__ void k_rescore(const float* __restrict__ x, long n, int d,
-                          const uint32_t* __restrict__ ids, long p0, long m,
-                          const float* __restrict__ c, const float* __restrict__ cn,
-                          const float* __restrict__ xnorm_row, const float* __restrict__ xnorm_pos,
-                          const uint2* __restrict__ cand, const uint32_t* __restrict__ cand_cnt,
-                          const float* __restrict__ cand_thr, uint32_t* __restrict__ labels,
-                          float* __restrict__ scores, uint32_t* __restrict__ list,
-                          uint32_t* __restrict__ list_count,
-                          unsigned long long* __restrict__ counters) {
-  const long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
+__global__ void k_exact(const float* __restrict__ x, int d, const uint32_t* __restrict__ ids,
+                        long p0, long m, const float* __restrict__ c, const float* __restrict__ cn,
+                        const float* __restrict__ xnorm_row, const float* __restrict__ xnorm_pos,
+                        const uint32_t* __restrict__ surv, const uint32_t* __restrict__ surv_cnt,
+                        uint32_t* __restrict__ labels, float* __restrict__ scores) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= m) return;
+  const uint32_t ns = surv_cnt[i];
+  if (ns == 0) return;  // on the exact kernel's list
   const long p = p0 + i;
-  const uint32_t cnt = cand_cnt[i];
+  const long row = ids ? (long)ids[p] : p;
+  const float* xr = x + row * (long)d;
   float best = IP ? -INFINITY : INFINITY;
   uint32_t bj = FALLBACK;
-  uint32_t nres = 0;
-  long row = 0;
-  if (cnt != FALLBACK) {
-    const float thr = cand_thr[i];
-    row = ids ? (long)ids[p] : p;
-    const float* xr = x + row * (long)d;
-    for (uint32_t e = lane; e < cnt; e += 32) {
-      const uint2 en = cand[i * (long)CAP + e];
-      const float sv = __uint_as_float(en.y);
-      if (en.x == FALLBACK || !(IP ? sv >= thr : sv <= thr)) continue;
-      nres++;
-      float v = chain(xr, c + (long)en.x * d, d);
-      if (!IP) v = __fsub_rn(__ldg(cn + en.x), __fmul_rn(2.0f, v));
-      if (better<IP>(v, en.x, best, bj)) {
-        best = v;
-        bj = en.x;
-      }
+  for (uint32_t s = 0; s < ns; s++) {
+    const uint32_t j = surv[i * SURV + s];
+    float v = chain(xr, c + (long)j * d, d);
+    if (!IP) v = __fsub_rn(__ldg(cn + j), __fmul_rn(2.0f, v));
+    if (better<IP>(v, j, best, bj)) {
+      best = v;
+      bj = j;
     }
   }
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
-    const uint32_t oj = __shfl_xor_sync(0xFFFFFFFFu, bj, o);
-    nres += __shfl_xor_sync(0xFFFFFFFFu, nres, o);
-    if (oj != FALLBACK && better<IP>(ov, oj, best, bj)) {
-      best = ov;
-      bj = oj;
-    }
-  }
-  if (lane != 0) return;
-  if (bj == FALLBACK) {
-    list[atomicAdd(list_count, 1u)] = (uint32_t)p;
-    atomicAdd(&counters[1], 1ull);
-    return;
-  }
-  atomicAdd(&counters[2], (unsigned long long)nres);
   float score = best;
-  if (!IP) {
-    const float xn = xnorm_row ? xnorm_row[row] : xnorm_pos[i];
-    score = fmaxf(__fadd_rn(xn, best), 0.0f);
-  }
+  if (!IP) score = fmaxf(__fadd_rn(xnorm_row ? xnorm_row[row] : xnorm_pos[i], best), 0.0f);
   labels[p] = bj;
   scores[p] = score;
 }
@@ -708,6 +829,14 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
   uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", chunk);
   float* cand_thr = e->scratch_get<float>("tc_thr", chunk);
   float* xnorm_pos = (!ip && !a.xnorm) ? e->scratch_get<float>("tc_xnorm_pos", chunk) : nullptr;
+  uint32_t* surv = e->scratch_get<uint32_t>("tc_surv", chunk * SURV);
+  uint32_t* surv_cnt = e->scratch_get<uint32_t>("tc_surv_cnt", chunk);
+  // Precise-dot bound of the refine stage: each lane's FMA chain plus the
+  // 5-level shuffle tree is at most kp roundings, gamma_kp sum|x c|; the exact
+  // chain adds gamma_d sum|x c|; the computed sum|x c| is itself within gamma_kp.
+  const double kp = std::ceil(dd / 32.0) + 5.0;
+  const double gamma_kp = kp * std::ldexp(1.0, -24) / (1.0 - kp * std::ldexp(1.0, -24));
+  const float e2 = (float)((gamma_kp + gamma_d) * (1.0 + 4.0 * gamma_kp) * 1.01);
   uint32_t* list = e->scratch_get<uint32_t>("tc_list", chunk);
   uint32_t* list_count = e->scratch_get<uint32_t>("tc_list_count", 4);
   unsigned long long* counters = e->counters();
@@ -749,17 +878,26 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
     EB_LAUNCH("screen");
     EB_CUDA(cudaMemsetAsync(list_count, 0, 4, e->stream));
     if (xnorm_pos) sel_row_norms(e, a.x, a.n, d, a.ids, c0, c0 + m, xnorm_pos);
-    const unsigned rw = 8;  // rows (warps) per block
-    const unsigned rgrid = (unsigned)((m + rw - 1) / rw);
+    const unsigned rgrid = (unsigned)((m + 7) / 8);  // 8 rows (warps) per block
     if (ip)
-      k_rescore<true><<<rgrid, rw * 32, 0, e->stream>>>(
-          a.x, (long)a.n, (int)d, a.ids, (long)c0, (long)m, a.c, a.cnorm, a.xnorm, xnorm_pos,
-          cand, cand_cnt, cand_thr, a.labels, a.scores, list, list_count, counters);
+      k_refine<true><<<rgrid, 256, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
+                                                   a.cnorm, cand, cand_cnt, cand_thr, e2, surv,
+                                                   surv_cnt, list, list_count, counters);
     else
-      k_rescore<false><<<rgrid, rw * 32, 0, e->stream>>>(
-          a.x, (long)a.n, (int)d, a.ids, (long)c0, (long)m, a.c, a.cnorm, a.xnorm, xnorm_pos,
-          cand, cand_cnt, cand_thr, a.labels, a.scores, list, list_count, counters);
-    EB_LAUNCH("screen rescore");
+      k_refine<false><<<rgrid, 256, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
+                                                    a.cnorm, cand, cand_cnt, cand_thr, e2, surv,
+                                                    surv_cnt, list, list_count, counters);
+    EB_LAUNCH("screen refine");
+    const unsigned egrid = (unsigned)((m + 127) / 128);
+    if (ip)
+      k_exact<true><<<egrid, 128, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
+                                                  a.cnorm, a.xnorm, xnorm_pos, surv, surv_cnt,
+                                                  a.labels, a.scores);
+    else
+      k_exact<false><<<egrid, 128, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
+                                                   a.cnorm, a.xnorm, xnorm_pos, surv, surv_cnt,
+                                                   a.labels, a.scores);
+    EB_LAUNCH("screen exact chains");
     Top1Args fa = a;
     fa.r0 = c0;
     fa.r1 = c0 + m;
