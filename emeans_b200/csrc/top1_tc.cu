@@ -65,7 +65,8 @@ constexpr int CAP = 128;         // per-row candidate list capacity
 constexpr int NTHREADS = 192;    // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr uint32_t FALLBACK = 0xFFFFFFFFu;
 constexpr int XEXP_BAD = INT_MIN;  // row with a non-finite value
-constexpr size_t CHUNK_ROWS = 131072;
+constexpr size_t MAX_CHUNK_ROWS = 1 << 20;
+constexpr size_t L2_BUDGET = 96u << 20;  // bytes of a pass's rows meant to stay in L2
 constexpr uint64_t WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
 constexpr size_t SMEM_BYTES = 1024 /* alignment slack */ + STAGES * (A_BYTES + B_BYTES) + 256;
@@ -245,24 +246,63 @@ __global__ void k_prep_rows(const float* __restrict__ x, long n, int d, int dp,
   const float* r = x + row * (long)d;
   float mx = 0.0f, ss = 0.0f;
   bool finite = true;
-  for (int t = lane; t < d; t += 32) {
-    float v = __ldg(r + t);
-    finite = finite && isfinite(v);
-    mx = fmaxf(mx, fabsf(v));
-    ss = fmaf(v, v, ss);
-  }
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-  }
-  finite = __all_sync(0xFFFFFFFFu, finite);
   int ex = 0;
-  frexpf(mx, &ex);
-  int sh = 14 - ex;
-  for (int t = lane; t < dp; t += 32) {
-    float v = t < d ? __ldg(r + t) : 0.0f;
-    out[t] = __float2half_rn(finite ? ldexpf(v, sh) : 0.0f);
+  if ((d & 3) == 0 && d <= 2048) {
+    // One read: up to 16 float4 per lane stay in registers.
+    const float4* r4 = reinterpret_cast<const float4*>(r);
+    const int q4 = d / 4;
+    float4 v[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+      const int t = lane + 32 * u;
+      v[u] = t < q4 ? __ldg(r4 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
+      finite = finite && isfinite(v[u].x) && isfinite(v[u].y) && isfinite(v[u].z) &&
+               isfinite(v[u].w);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+      ss = fmaf(v[u].x, v[u].x, fmaf(v[u].y, v[u].y, fmaf(v[u].z, v[u].z, fmaf(v[u].w, v[u].w, ss))));
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+      ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    }
+    finite = __all_sync(0xFFFFFFFFu, finite);
+    frexpf(mx, &ex);
+    const int sh = 14 - ex;
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+      const int t = lane + 32 * u;
+      if (t < q4) {
+        __half2 h0 = finite ? __floats2half2_rn(ldexpf(v[u].x, sh), ldexpf(v[u].y, sh))
+                            : __floats2half2_rn(0.f, 0.f);
+        __half2 h1 = finite ? __floats2half2_rn(ldexpf(v[u].z, sh), ldexpf(v[u].w, sh))
+                            : __floats2half2_rn(0.f, 0.f);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&h0);
+        pk.y = *reinterpret_cast<uint32_t*>(&h1);
+        *reinterpret_cast<uint2*>(out + 4 * t) = pk;
+      }
+    }
+    for (int t = d + lane; t < dp; t += 32) out[t] = __float2half_rn(0.0f);
+  } else {
+    for (int t = lane; t < d; t += 32) {
+      float v = __ldg(r + t);
+      finite = finite && isfinite(v);
+      mx = fmaxf(mx, fabsf(v));
+      ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+      ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    }
+    finite = __all_sync(0xFFFFFFFFu, finite);
+    frexpf(mx, &ex);
+    const int sh = 14 - ex;
+    for (int t = lane; t < dp; t += 32) {
+      float v = t < d ? __ldg(r + t) : 0.0f;
+      out[t] = __float2half_rn(finite ? ldexpf(v, sh) : 0.0f);
+    }
   }
   if (lane == 0) {
     xexp[i] = finite ? ex : XEXP_BAD;
@@ -356,7 +396,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long m0 = (long)blockIdx.x * BM;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -385,17 +424,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // TMA producer: per (tile, k-block), one A box (128 x 64) and one B box (256 x 64).
-      int issued = 0;
-      for (int it = 0; it < total; it++) {
-        const int s = it % STAGES;
-        const uint32_t par = ((it / STAGES) & 1) ^ 1;
-        if (!mbar_wait(&empty[s], par, abort_flag)) break;
-        const int nt = it / P.kblocks, kb = it % P.kblocks;
-        mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
-        tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BKH, (int)m0);
-        tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * BKH, nt * BN);
-        issued = it + 1;
+      // TMA producer: per (row tile, centroid tile, k-block), one A box
+      // (128 x 64) and one B box (256 x 64). The ring runs on across row tiles.
+      int it = 0, issued = 0;
+      bool stop = false;
+      for (long rt = blockIdx.x; rt * BM < P.m && !stop; rt += gridDim.x) {
+        for (int t2 = 0; t2 < total; t2++, it++) {
+          const int s = it % STAGES;
+          const uint32_t par = ((it / STAGES) & 1) ^ 1;
+          if (!mbar_wait(&empty[s], par, abort_flag)) {
+            stop = true;
+            break;
+          }
+          const int nt = t2 / P.kblocks, kb = t2 % P.kblocks;
+          mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+          tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BKH, (int)(rt * BM));
+          tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * BKH, nt * BN);
+          issued = it + 1;
+        }
       }
       // No copy may still be landing in shared memory when the CTA exits: wait
       // (bounded) for the last loads issued. On the normal path they have
@@ -408,11 +454,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // MMA issuer.
-      int it = 0;
-      for (int nt = 0; nt < P.ntiles && !*abort_flag; nt++) {
-        const int a = nt & 1;
-        if (!mbar_wait(&tempty[a], ((nt >> 1) & 1) ^ 1, abort_flag)) break;
+      // MMA issuer; tc counts (row tile, centroid tile) pairs for the TMEM buffers.
+      int it = 0, tc = 0;
+      bool stop = false;
+      for (long rt = blockIdx.x; rt * BM < P.m && !stop; rt += gridDim.x)
+      for (int nt = 0; nt < P.ntiles; nt++, tc++) {
+        const int a = tc & 1;
+        if (!mbar_wait(&tempty[a], ((tc >> 1) & 1) ^ 1, abort_flag)) {
+          stop = true;
+          break;
+        }
         tc_fence_after();
         const uint32_t dcol = tmem + (uint32_t)(a * BN);
         bool ok = true;
@@ -430,7 +481,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                      (kb > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&empty[s]);
         }
-        if (!ok) break;
+        if (!ok) {
+          stop = true;
+          break;
+        }
         umma_commit(&tfull[a]);
       }
       // Every MMA this thread issued has completed once mma_done flips.
@@ -440,16 +494,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
   } else {
-    // Epilogue: one thread per row of the tile.
+    // Epilogue: one thread per row of each row tile.
     const int q = warp & 3;
     const int r = q * 32 + lane;
-    const long i = m0 + r;
-    const bool live = i < P.m;
-    const int ex = live ? P.xexp[i] : XEXP_BAD;
     int ec = 0;
     frexpf(__uint_as_float(P.cinfo[0]), &ec);
     const float cmax = __uint_as_float(P.cinfo[1]);
     const bool c_bad = P.cinfo[2] != 0;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    int tc = 0;  // (row tile, centroid tile) pairs, as the MMA issuer counts them
+    bool stop = false;
+    for (long rt = blockIdx.x; rt * BM < P.m && !stop; rt += gridDim.x) {
+    const long i = rt * BM + r;
+    const bool live = i < P.m;
+    const int ex = live ? P.xexp[i] : XEXP_BAD;
     bool fallback = !live || ex == XEXP_BAD || c_bad;
     const float xn = live ? P.xnrm[i] : 0.0f;
     // |x'| and max |c'| in acc units, and the bound e (acc units).
@@ -474,13 +532,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     bool overflow = false;
     uint32_t cnt = 0;  // entries in this row's candidate list
     uint2* row_list = P.cand + (live ? i : 0) * (long)CAP;
-    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
 
-    for (int nt = 0; nt < P.ntiles; nt++) {
-      const int a = nt & 1;
+    for (int nt = 0; nt < P.ntiles; nt++, tc++) {
+      const int a = tc & 1;
       // Warp-uniform: the TMEM loads below are .sync.aligned.
-      const bool ready = __all_sync(0xFFFFFFFFu, mbar_wait(&tfull[a], (nt >> 1) & 1, abort_flag));
-      if (!ready) break;
+      const bool ready = __all_sync(0xFFFFFFFFu, mbar_wait(&tfull[a], (tc >> 1) & 1, abort_flag));
+      if (!ready) {
+        stop = true;
+        break;
+      }
       tc_fence_after();
       const int col0 = nt * BN;
       const int nch = min(BN / 32, (P.k - col0 + 31) / 32);
@@ -532,6 +592,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (ok) P.cand_thr[i] = thr;
       P.cand_cnt[i] = ok ? cnt : FALLBACK;
     }
+    }  // row tiles
   }
 
   __syncthreads();
@@ -712,10 +773,111 @@ __device__ __forceinline__ float chain(const float* __restrict__ x, const float*
   return acc;
 }
 
+// Exact chains, one thread per row, for rows whose first survivor is alone
+// (the common case) and d % 32 == 0: x and the survivor's centroid stream
+// through shared memory in 32-column slices (cp.async, 4 slices in flight),
+// each 16-byte chunk q of row t stored at q ^ (t & 7) so that the per-thread
+// LDS.128 reads are free of bank conflicts. Other rows keep ns and go to
+// k_exact below.
+constexpr int EX_ROWS = 128, EX_COLS = 32, EX_STAGES = 4;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <bool IP>
+__global__ void __launch_bounds__(EX_ROWS) k_exact_staged(
+    const float* __restrict__ x, int d, const uint32_t* __restrict__ ids, long p0, long m,
+    const float* __restrict__ c, const float* __restrict__ cn, const float* __restrict__ xnorm_row,
+    const uint32_t* __restrict__ surv,
+    uint32_t* __restrict__ surv_cnt, uint32_t* __restrict__ labels, float* __restrict__ scores) {
+  extern __shared__ __align__(16) float ex_smem[];
+  float* xs = ex_smem;                                   // [stage][row][32]
+  float* cs = ex_smem + EX_STAGES * EX_ROWS * EX_COLS;   // [stage][row][32]
+  __shared__ const float* xrow_s[EX_ROWS];
+  __shared__ const float* crow_s[EX_ROWS];
+  const int t = threadIdx.x;
+  const long i = (long)blockIdx.x * EX_ROWS + t;
+  const bool mine = i < m && surv_cnt[i] == 1;
+  long row = 0;
+  uint32_t j = 0;
+  if (mine) {
+    row = ids ? (long)ids[p0 + i] : p0 + i;
+    j = surv[i * SURV];
+  }
+  // Rows not handled here read row 0 / centroid 0 harmlessly and are not written.
+  xrow_s[t] = x + row * (long)d;
+  crow_s[t] = c + (long)j * d;
+  __syncthreads();
+  const int nsl = d / EX_COLS;
+  // Each slice: 128 rows x 8 chunks for x and for c = 2048 copies, 16 per thread.
+  auto issue = [&](int sl) {
+    if (sl < nsl) {
+      const int st = sl % EX_STAGES;
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int idx = u * EX_ROWS + t;  // 0 .. 1023
+        const int r = idx >> 3, q = idx & 7;
+        const int pq = q ^ (r & 7);
+        cp_async16(xs + (st * EX_ROWS + r) * EX_COLS + pq * 4, xrow_s[r] + sl * EX_COLS + q * 4);
+        cp_async16(cs + (st * EX_ROWS + r) * EX_COLS + pq * 4, crow_s[r] + sl * EX_COLS + q * 4);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int s = 0; s < EX_STAGES - 1; s++) issue(s);
+  // The L2 score needs the row's sum of squares in the CPU order (sequential,
+  // no FMA); without cached norms it is summed here as the row streams by.
+  const bool want_xn = !IP && !xnorm_row;
+  float acc = 0.0f, xn = -0.0f;
+  for (int sl = 0; sl < nsl; sl++) {
+    issue(sl + EX_STAGES - 1);
+    cp_async_wait<EX_STAGES - 1>();
+    __syncthreads();
+    const int st = sl % EX_STAGES;
+    const float4* xr4 = reinterpret_cast<const float4*>(xs + (st * EX_ROWS + t) * EX_COLS);
+    const float4* cr4 = reinterpret_cast<const float4*>(cs + (st * EX_ROWS + t) * EX_COLS);
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      const float4 a = xr4[q ^ (t & 7)], b = cr4[q ^ (t & 7)];
+      acc = __fmaf_rn(a.x, b.x, acc);
+      acc = __fmaf_rn(a.y, b.y, acc);
+      acc = __fmaf_rn(a.z, b.z, acc);
+      acc = __fmaf_rn(a.w, b.w, acc);
+      if (want_xn) {
+        xn = __fadd_rn(xn, __fmul_rn(a.x, a.x));
+        xn = __fadd_rn(xn, __fmul_rn(a.y, a.y));
+        xn = __fadd_rn(xn, __fmul_rn(a.z, a.z));
+        xn = __fadd_rn(xn, __fmul_rn(a.w, a.w));
+      }
+    }
+    __syncthreads();  // the slot is refilled next iteration
+  }
+  cp_async_wait<0>();
+  if (!mine) return;
+  float score = acc;
+  if (!IP) {
+    const float key = __fsub_rn(__ldg(cn + j), __fmul_rn(2.0f, acc));
+    score = fmaxf(__fadd_rn(xnorm_row ? xnorm_row[row] : xn, key), 0.0f);
+  }
+  labels[p0 + i] = j;
+  scores[p0 + i] = score;
+  surv_cnt[i] = 0;  // done: k_exact skips the row
+}
+
 template <bool IP>
 __global__ void k_exact(const float* __restrict__ x, int d, const uint32_t* __restrict__ ids,
                         long p0, long m, const float* __restrict__ c, const float* __restrict__ cn,
-                        const float* __restrict__ xnorm_row, const float* __restrict__ xnorm_pos,
+                        const float* __restrict__ xnorm_row,
                         const uint32_t* __restrict__ surv, const uint32_t* __restrict__ surv_cnt,
                         uint32_t* __restrict__ labels, float* __restrict__ scores) {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -737,7 +899,19 @@ __global__ void k_exact(const float* __restrict__ x, int d, const uint32_t* __re
     }
   }
   float score = best;
-  if (!IP) score = fmaxf(__fadd_rn(xnorm_row ? xnorm_row[row] : xnorm_pos[i], best), 0.0f);
+  if (!IP) {
+    float xn;
+    if (xnorm_row) {
+      xn = xnorm_row[row];
+    } else {
+      xn = -0.0f;  // sequential sum of squares, the CPU order
+      for (int t = 0; t < d; t++) {
+        const float v = __ldg(xr + t);
+        xn = __fadd_rn(xn, __fmul_rn(v, v));
+      }
+    }
+    score = fmaxf(__fadd_rn(xn, best), 0.0f);
+  }
   labels[p] = bj;
   scores[p] = score;
 }
@@ -784,6 +958,16 @@ void set_smem(int device) {
   }
 }
 
+template <bool IP>
+void set_exact_smem(int device, size_t bytes) {
+  static uint64_t done = 0;
+  if (!(done >> device & 1)) {
+    EB_CUDA(cudaFuncSetAttribute(k_exact_staged<IP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)bytes));
+    done |= 1ull << device;
+  }
+}
+
 }  // namespace
 
 bool top1_screen_supported(eb_engine* e, const Top1Args& a) {
@@ -797,7 +981,12 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
   const size_t d = a.d, k = a.k;
   const size_t dp = (d + BKH - 1) / BKH * BKH;
   const size_t m_all = a.r1 - a.r0;
-  const size_t chunk = std::min(m_all, CHUNK_ROWS);
+  // Rows per pass: whole waves of 128-row CTAs, sized so that a pass's rows
+  // (FP32 and FP16, 6 bytes per element) stay in L2 from the conversion
+  // through the screen to the exact re-score.
+  const size_t wave = (size_t)e->num_sms * BM;
+  const size_t fit = (size_t)L2_BUDGET / (6 * dp) / wave * wave;
+  const size_t chunk = std::min(m_all, std::min(std::max(wave, fit), MAX_CHUNK_ROWS));
   const bool ip = a.metric == EB_IP;
 
   // Bound coefficients for this d (see the header comment), with 1% slack.
@@ -828,7 +1017,6 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
   uint2* cand = e->scratch_get<uint2>("tc_cand", chunk * CAP);
   uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", chunk);
   float* cand_thr = e->scratch_get<float>("tc_thr", chunk);
-  float* xnorm_pos = (!ip && !a.xnorm) ? e->scratch_get<float>("tc_xnorm_pos", chunk) : nullptr;
   uint32_t* surv = e->scratch_get<uint32_t>("tc_surv", chunk * SURV);
   uint32_t* surv_cnt = e->scratch_get<uint32_t>("tc_surv_cnt", chunk);
   // Precise-dot bound of the refine stage: each lane's FMA chain plus the
@@ -870,14 +1058,14 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
     EB_LAUNCH("screen row prep");
     const CUtensorMap mapA = make_map(xh, m, dp, BM);
     P.m = (long)m;
-    const unsigned grid = (unsigned)((m + BM - 1) / BM);
+    // Persistent: at most one CTA per SM, each looping over row tiles.
+    const unsigned grid = (unsigned)std::min<size_t>((m + BM - 1) / BM, (size_t)e->num_sms);
     if (ip)
       k_screen<true><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(mapA, mapB, P);
     else
       k_screen<false><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(mapA, mapB, P);
     EB_LAUNCH("screen");
     EB_CUDA(cudaMemsetAsync(list_count, 0, 4, e->stream));
-    if (xnorm_pos) sel_row_norms(e, a.x, a.n, d, a.ids, c0, c0 + m, xnorm_pos);
     const unsigned rgrid = (unsigned)((m + 7) / 8);  // 8 rows (warps) per block
     if (ip)
       k_refine<true><<<rgrid, 256, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
@@ -889,13 +1077,28 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
                                                     surv_cnt, list, list_count, counters);
     EB_LAUNCH("screen refine");
     const unsigned egrid = (unsigned)((m + 127) / 128);
+    if (d % EX_COLS == 0) {
+      const size_t ex_smem = 2 * EX_STAGES * EX_ROWS * EX_COLS * sizeof(float);
+      if (ip) {
+        set_exact_smem<true>(e->device, ex_smem);
+        k_exact_staged<true><<<egrid, EX_ROWS, ex_smem, e->stream>>>(
+            a.x, (int)d, a.ids, (long)c0, (long)m, a.c, a.cnorm, a.xnorm, surv,
+            surv_cnt, a.labels, a.scores);
+      } else {
+        set_exact_smem<false>(e->device, ex_smem);
+        k_exact_staged<false><<<egrid, EX_ROWS, ex_smem, e->stream>>>(
+            a.x, (int)d, a.ids, (long)c0, (long)m, a.c, a.cnorm, a.xnorm, surv,
+            surv_cnt, a.labels, a.scores);
+      }
+      EB_LAUNCH("screen exact chains (staged)");
+    }
     if (ip)
       k_exact<true><<<egrid, 128, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
-                                                  a.cnorm, a.xnorm, xnorm_pos, surv, surv_cnt,
+                                                  a.cnorm, a.xnorm, surv, surv_cnt,
                                                   a.labels, a.scores);
     else
       k_exact<false><<<egrid, 128, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
-                                                   a.cnorm, a.xnorm, xnorm_pos, surv, surv_cnt,
+                                                   a.cnorm, a.xnorm, surv, surv_cnt,
                                                    a.labels, a.scores);
     EB_LAUNCH("screen exact chains");
     Top1Args fa = a;
