@@ -185,7 +185,18 @@ __global__ void __launch_bounds__(NT) k_top1_exact(
       long p = pos_of[r];
       float s = best_v[i];
       if (!IP) {
-        float xn = xnorm_by_row ? xnorm[row_of[r]] : xnorm[p - r0];
+        float xn;
+        if (xnorm) {
+          xn = xnorm_by_row ? xnorm[row_of[r]] : xnorm[p - r0];
+        } else {
+          // Sequential sum of squares in the CPU order, for this row only.
+          const float* xr = x + row_of[r] * (long)d;
+          xn = -0.0f;
+          for (int t = 0; t < d; t++) {
+            const float v = __ldg(xr + t);
+            xn = __fadd_rn(xn, __fmul_rn(v, v));
+          }
+        }
         s = fmaxf(__fadd_rn(xn, s), 0.0f);
       }
       labels[p] = best_j[i];
@@ -205,6 +216,8 @@ void launch(eb_engine* e, const Top1Args& a, const uint32_t* list, const uint32_
     if (a.xnorm) {
       xn = a.xnorm;
       by_row = 1;
+    } else if (list) {
+      xn = nullptr;  // the kernel sums the listed rows' squares itself
     } else {
       float* t = e->scratch_get<float>("top1_xnorm", a.r1 - a.r0);
       sel_row_norms(e, a.x, a.n, a.d, a.ids, a.r0, a.r1, t);

@@ -65,11 +65,13 @@ constexpr int CAP = 128;         // per-row candidate list capacity
 constexpr int NTHREADS = 192;    // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr uint32_t FALLBACK = 0xFFFFFFFFu;
 constexpr int XEXP_BAD = INT_MIN;  // row with a non-finite value
-constexpr size_t MAX_CHUNK_ROWS = 1 << 20;
-constexpr size_t L2_BUDGET = 96u << 20;  // bytes of a pass's rows meant to stay in L2
+constexpr size_t PASS_WAVES = 8;  // row tiles per SM in one pass
 constexpr uint64_t WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
-constexpr size_t SMEM_BYTES = 1024 /* alignment slack */ + STAGES * (A_BYTES + B_BYTES) + 256;
+// Operand ring, then 256 B of barriers / TMEM slot / flags, then per epilogue
+// warp two tiles of centroid norms.
+constexpr size_t SMEM_BYTES =
+    1024 /* alignment slack */ + STAGES * (A_BYTES + B_BYTES) + 256 + 4 * 2 * BN * sizeof(float);
 
 // ---------------------------------------------------------------- PTX helpers
 
@@ -170,53 +172,54 @@ __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 
-// 32 consecutive FP32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 64 consecutive FP32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
       "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-      "%30, %31}, [%32];"
+      "%30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
         "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
         "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
-        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]),
+        "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]),
+        "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]),
+        "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]),
+        "=r"(r[63])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Screened scores of 32 columns (cb .. cb+31) of this thread's row: the raw
-// accumulator (IP), or the key cn_j - 2 f acc_j with one rounding (L2).
-// Columns past k score -inf (IP) / +inf (L2), so they never win or enter.
+// Screened scores of 64 columns of this thread's row, `lim` of them real
+// (lim >= 64: all): the raw accumulator (IP), or the key cn_j - 2 f acc_j with
+// one rounding (L2), with the norms read from shared memory. Columns past k
+// score -inf (IP) / +inf (L2), so they never win or enter.
 template <bool IP>
-__device__ __forceinline__ void chunk_scores(uint32_t taddr, int cb, int k,
-                                             const float* __restrict__ cn, float m2f,
-                                             float (&s)[32]) {
-  uint32_t v[32];
-  tmem_ld32(taddr, v);
-  if (cb + 32 <= k) {
-    if (IP) {
+__device__ __forceinline__ void group_scores(uint32_t taddr, const float* cns, float m2f, int lim,
+                                             float (&s)[64]) {
+  uint32_t v[64];
+  tmem_ld64(taddr, v);
+  if (IP) {
 #pragma unroll
-      for (int j = 0; j < 32; j++) s[j] = __uint_as_float(v[j]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 c4 = __ldg(reinterpret_cast<const float4*>(cn + cb + j));
-        s[j] = __fmaf_rn(m2f, __uint_as_float(v[j]), c4.x);
-        s[j + 1] = __fmaf_rn(m2f, __uint_as_float(v[j + 1]), c4.y);
-        s[j + 2] = __fmaf_rn(m2f, __uint_as_float(v[j + 2]), c4.z);
-        s[j + 3] = __fmaf_rn(m2f, __uint_as_float(v[j + 3]), c4.w);
-      }
-    }
+    for (int j = 0; j < 64; j++) s[j] = __uint_as_float(v[j]);
   } else {
+    const float4* c4 = reinterpret_cast<const float4*>(cns);
 #pragma unroll
-    for (int j = 0; j < 32; j++) {
-      const bool in = cb + j < k;
-      if (IP)
-        s[j] = in ? __uint_as_float(v[j]) : -INFINITY;
-      else
-        s[j] = in ? __fmaf_rn(m2f, __uint_as_float(v[j]), __ldg(cn + cb + j)) : INFINITY;
+    for (int j = 0; j < 64; j += 4) {
+      const float4 c = c4[j / 4];
+      s[j] = __fmaf_rn(m2f, __uint_as_float(v[j]), c.x);
+      s[j + 1] = __fmaf_rn(m2f, __uint_as_float(v[j + 1]), c.y);
+      s[j + 2] = __fmaf_rn(m2f, __uint_as_float(v[j + 2]), c.z);
+      s[j + 3] = __fmaf_rn(m2f, __uint_as_float(v[j + 3]), c.w);
     }
+  }
+  if (lim < 64) {
+#pragma unroll
+    for (int j = 0; j < 64; j++)
+      if (j >= lim) s[j] = IP ? -INFINITY : INFINITY;
   }
 }
 
@@ -247,13 +250,13 @@ __global__ void k_prep_rows(const float* __restrict__ x, long n, int d, int dp,
   float mx = 0.0f, ss = 0.0f;
   bool finite = true;
   int ex = 0;
-  if ((d & 3) == 0 && d <= 2048) {
-    // One read: up to 16 float4 per lane stay in registers.
+  if ((d & 3) == 0 && d <= 1024) {
+    // One read: up to 8 float4 per lane stay in registers.
     const float4* r4 = reinterpret_cast<const float4*>(r);
     const int q4 = d / 4;
-    float4 v[16];
+    float4 v[8];
 #pragma unroll
-    for (int u = 0; u < 16; u++) {
+    for (int u = 0; u < 8; u++) {
       const int t = lane + 32 * u;
       v[u] = t < q4 ? __ldg(r4 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
       finite = finite && isfinite(v[u].x) && isfinite(v[u].y) && isfinite(v[u].z) &&
@@ -270,7 +273,7 @@ __global__ void k_prep_rows(const float* __restrict__ x, long n, int d, int dp,
     frexpf(mx, &ex);
     const int sh = 14 - ex;
 #pragma unroll
-    for (int u = 0; u < 16; u++) {
+    for (int u = 0; u < 8; u++) {
       const int t = lane + 32 * u;
       if (t < q4) {
         __half2 h0 = finite ? __floats2half2_rn(ldexpf(v[u].x, sh), ldexpf(v[u].y, sh))
@@ -394,6 +397,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* mma_done = tempty + 2;
   uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  float* cn_s = (float*)(smem + STAGES * (A_BYTES + B_BYTES) + 256);  // [4 warps][2][BN] (L2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -543,29 +547,42 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       tc_fence_after();
       const int col0 = nt * BN;
-      const int nch = min(BN / 32, (P.k - col0 + 31) / 32);
       const uint32_t tbase = lane_base + (uint32_t)(a * BN);
-      // Pass 1: the tile's best score moves the threshold first, so that
-      // pass 2 admits only what can still be within 2e of the final best.
-      float tb = IP ? -INFINITY : INFINITY;
-#pragma unroll 1
-      for (int ch = 0; ch < nch; ch++) {
-        float s[32];
-        chunk_scores<IP>(tbase + (uint32_t)(ch * 32), col0 + ch * 32, P.k, P.cn, m2f, s);
+      // This tile's squared centroid norms, staged by each warp for itself (no
+      // barrier across warps, so a timed-out wait can never strand another warp).
+      float* cns = cn_s + (q * 2 + a) * BN;
+      if (!IP) {
 #pragma unroll
-        for (int j = 0; j < 32; j++) tb = IP ? fmaxf(tb, s[j]) : fminf(tb, s[j]);
+        for (int u = 0; u < BN / 32; u++) {
+          const int c = u * 32 + lane;
+          cns[c] = col0 + c < P.k ? __ldg(P.cn + col0 + c) : 0.0f;
+        }
+        __syncwarp();
       }
-      if (IP ? (tb > best) : (tb < best)) {
-        best = tb;
-        thr = IP ? __fsub_rd(best, off) : __fadd_ru(best, off);
-      }
-      // Pass 2: append every score within the window to the row's list.
+      const int ngr = min(BN / 64, (P.k - col0 + 63) / 64);
 #pragma unroll 1
-      for (int ch = 0; ch < nch; ch++) {
-        float s[32];
-        chunk_scores<IP>(tbase + (uint32_t)(ch * 32), col0 + ch * 32, P.k, P.cn, m2f, s);
+      for (int g = 0; g < ngr; g++) {
+        // One pass per 64 columns: scores, their best (which moves the
+        // threshold first), then every score within the window is appended.
+        float s[64];
+        group_scores<IP>(tbase + (uint32_t)(g * 64), cns + g * 64, m2f, P.k - (col0 + g * 64), s);
+        float gb;
+        {
+          float t[32];
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
+          for (int j = 0; j < 32; j++) t[j] = IP ? fmaxf(s[j], s[j + 32]) : fminf(s[j], s[j + 32]);
+#pragma unroll
+          for (int w2 = 16; w2 >= 1; w2 >>= 1)
+#pragma unroll
+            for (int j = 0; j < w2; j++) t[j] = IP ? fmaxf(t[j], t[j + w2]) : fminf(t[j], t[j + w2]);
+          gb = t[0];
+        }
+        if (IP ? (gb > best) : (gb < best)) {
+          best = gb;
+          thr = IP ? __fsub_rd(best, off) : __fadd_ru(best, off);
+        }
+#pragma unroll
+        for (int j = 0; j < 64; j++) {
           if (collect && (IP ? (s[j] >= thr) : (s[j] <= thr))) {
             if (cnt == CAP) {
               // Full: drop the entries the current window has left behind.
@@ -578,7 +595,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               cnt = w;
             }
             if (cnt < CAP)
-              row_list[cnt++] = make_uint2((uint32_t)(col0 + ch * 32 + j), __float_as_uint(s[j]));
+              row_list[cnt++] = make_uint2((uint32_t)(col0 + g * 64 + j), __float_as_uint(s[j]));
             else
               overflow = true;
           }
@@ -654,54 +671,105 @@ __global__ void __launch_bounds__(256) k_refine(
   float* pe = pe_s[w];
   uint32_t* pj = pj_s[w];
   int np = 0;
-  for (uint32_t e = 0; e < cnt; e++) {
-    const uint2 en = cand[i * (long)CAP + e];
-    const float sv = __uint_as_float(en.y);
-    if (!(IP ? sv >= thr : sv <= thr)) continue;  // left behind by the window
-    const float* cr = c + (long)en.x * d;
-    float dot = 0.0f, ab = 0.0f;
-    if ((d & 3) == 0) {
-      const float4* x4 = reinterpret_cast<const float4*>(xr);
-      const float4* c4 = reinterpret_cast<const float4*>(cr);
-      for (int t = lane; t < d / 4; t += 32) {
-        const float4 xa = __ldg(x4 + t), ca = __ldg(c4 + t);
-        dot = __fmaf_rn(xa.x, ca.x, dot);
-        dot = __fmaf_rn(xa.y, ca.y, dot);
-        dot = __fmaf_rn(xa.z, ca.z, dot);
-        dot = __fmaf_rn(xa.w, ca.w, dot);
-        ab = __fmaf_rn(fabsf(xa.x), fabsf(ca.x), ab);
-        ab = __fmaf_rn(fabsf(xa.y), fabsf(ca.y), ab);
-        ab = __fmaf_rn(fabsf(xa.z), fabsf(ca.z), ab);
-        ab = __fmaf_rn(fabsf(xa.w), fabsf(ca.w), ab);
+  // The row's x (a float4 per lane per 128 columns) stays in registers for
+  // every candidate when d % 4 == 0 and d <= 1024; otherwise it is re-read.
+  const bool vec = (d & 3) == 0 && d <= 1024;
+  const int q4 = d / 4;
+  float4 xv[8];
+#pragma unroll
+  for (int u = 0; u < 8; u++) {
+    const int t = lane + 32 * u;
+    xv[u] = (vec && t < q4) ? __ldg(reinterpret_cast<const float4*>(xr) + t)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  uint32_t e = 0;
+  while (true) {
+    // The next two candidates still inside the final window (the rest were
+    // left behind by it), scored together so their loads overlap.
+    uint32_t jc[2] = {FALLBACK, FALLBACK};
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      while (e < cnt) {
+        const uint2 en = cand[i * (long)CAP + e++];
+        const float sv = __uint_as_float(en.y);
+        if (IP ? sv >= thr : sv <= thr) {
+          jc[h] = en.x;
+          break;
+        }
+      }
+    }
+    if (jc[0] == FALLBACK) break;
+    float dot[2] = {0.0f, 0.0f}, ab[2] = {0.0f, 0.0f};
+    if (vec) {
+      const float4* c40 = reinterpret_cast<const float4*>(c + (long)jc[0] * d);
+      const float4* c41 = reinterpret_cast<const float4*>(
+          c + (long)(jc[1] == FALLBACK ? jc[0] : jc[1]) * d);
+      float4 ca[8], cb[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int t = lane + 32 * u;
+        ca[u] = t < q4 ? __ldg(c40 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
+        cb[u] = t < q4 ? __ldg(c41 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const float4 a = xv[u];
+        dot[0] = __fmaf_rn(a.x, ca[u].x, dot[0]);
+        dot[0] = __fmaf_rn(a.y, ca[u].y, dot[0]);
+        dot[0] = __fmaf_rn(a.z, ca[u].z, dot[0]);
+        dot[0] = __fmaf_rn(a.w, ca[u].w, dot[0]);
+        ab[0] = __fmaf_rn(fabsf(a.x), fabsf(ca[u].x), ab[0]);
+        ab[0] = __fmaf_rn(fabsf(a.y), fabsf(ca[u].y), ab[0]);
+        ab[0] = __fmaf_rn(fabsf(a.z), fabsf(ca[u].z), ab[0]);
+        ab[0] = __fmaf_rn(fabsf(a.w), fabsf(ca[u].w), ab[0]);
+        dot[1] = __fmaf_rn(a.x, cb[u].x, dot[1]);
+        dot[1] = __fmaf_rn(a.y, cb[u].y, dot[1]);
+        dot[1] = __fmaf_rn(a.z, cb[u].z, dot[1]);
+        dot[1] = __fmaf_rn(a.w, cb[u].w, dot[1]);
+        ab[1] = __fmaf_rn(fabsf(a.x), fabsf(cb[u].x), ab[1]);
+        ab[1] = __fmaf_rn(fabsf(a.y), fabsf(cb[u].y), ab[1]);
+        ab[1] = __fmaf_rn(fabsf(a.z), fabsf(cb[u].z), ab[1]);
+        ab[1] = __fmaf_rn(fabsf(a.w), fabsf(cb[u].w), ab[1]);
       }
     } else {
-      for (int t = lane; t < d; t += 32) {
-        const float xa = __ldg(xr + t), ca = __ldg(cr + t);
-        dot = __fmaf_rn(xa, ca, dot);
-        ab = __fmaf_rn(fabsf(xa), fabsf(ca), ab);
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        if (jc[h] == FALLBACK) continue;
+        const float* cr = c + (long)jc[h] * d;
+        for (int t = lane; t < d; t += 32) {
+          const float xa = __ldg(xr + t), ca = __ldg(cr + t);
+          dot[h] = __fmaf_rn(xa, ca, dot[h]);
+          ab[h] = __fmaf_rn(fabsf(xa), fabsf(ca), ab[h]);
+        }
       }
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
-      dot = __fadd_rn(dot, __shfl_xor_sync(0xFFFFFFFFu, dot, o));
-      ab = __fadd_rn(ab, __shfl_xor_sync(0xFFFFFFFFu, ab, o));
+      dot[0] = __fadd_rn(dot[0], __shfl_xor_sync(0xFFFFFFFFu, dot[0], o));
+      ab[0] = __fadd_rn(ab[0], __shfl_xor_sync(0xFFFFFFFFu, ab[0], o));
+      dot[1] = __fadd_rn(dot[1], __shfl_xor_sync(0xFFFFFFFFu, dot[1], o));
+      ab[1] = __fadd_rn(ab[1], __shfl_xor_sync(0xFFFFFFFFu, ab[1], o));
     }
-    float v, err;
-    if (IP) {
-      v = dot;
-      err = __fmaf_ru(e2, ab, 1e-37f);
-    } else {
-      const float cj = __ldg(cn + en.x);
-      v = __fsub_rn(cj, __fmul_rn(2.0f, dot));
-      // key error: twice the dot error plus the two key roundings.
-      err = __fmaf_ru(2.0f * e2, ab, __fmaf_ru(ldexpf(1.0f, -22), fabsf(v), 1e-37f));
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      if (jc[h] == FALLBACK) break;
+      float v, err;
+      if (IP) {
+        v = dot[h];
+        err = __fmaf_ru(e2, ab[h], 1e-37f);
+      } else {
+        const float cj = __ldg(cn + jc[h]);
+        v = __fsub_rn(cj, __fmul_rn(2.0f, dot[h]));
+        // key error: twice the dot error plus the two key roundings.
+        err = __fmaf_ru(2.0f * e2, ab[h], __fmaf_ru(ldexpf(1.0f, -22), fabsf(v), 1e-37f));
+      }
+      if (lane == 0) {
+        pv[np] = v;
+        pe[np] = err;
+        pj[np] = jc[h];
+      }
+      np++;
     }
-    if (lane == 0) {
-      pv[np] = v;
-      pe[np] = err;
-      pj[np] = en.x;
-    }
-    np++;
   }
   __syncwarp();
   // The best provable bound over the candidates, then every candidate that
@@ -773,12 +841,12 @@ __device__ __forceinline__ float chain(const float* __restrict__ x, const float*
   return acc;
 }
 
-// Exact chains, one thread per row, for rows whose first survivor is alone
-// (the common case) and d % 32 == 0: x and the survivor's centroid stream
-// through shared memory in 32-column slices (cp.async, 4 slices in flight),
-// each 16-byte chunk q of row t stored at q ^ (t & 7) so that the per-thread
-// LDS.128 reads are free of bank conflicts. Other rows keep ns and go to
-// k_exact below.
+// Exact chains, one thread per row, for rows with one or two survivors (two
+// are revival twins, nearly the same centroid) when d % 32 == 0: x and the
+// survivors' centroids stream through shared memory in 32-column slices
+// (cp.async, 4 slices in flight), each 16-byte chunk q of row t stored at
+// q ^ (t & 7) so that the per-thread LDS.128 reads are free of bank conflicts.
+// Rows with more survivors keep ns and go to k_exact below.
 constexpr int EX_ROWS = 128, EX_COLS = 32, EX_STAGES = 4;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -800,25 +868,33 @@ __global__ void __launch_bounds__(EX_ROWS) k_exact_staged(
     const uint32_t* __restrict__ surv,
     uint32_t* __restrict__ surv_cnt, uint32_t* __restrict__ labels, float* __restrict__ scores) {
   extern __shared__ __align__(16) float ex_smem[];
-  float* xs = ex_smem;                                   // [stage][row][32]
-  float* cs = ex_smem + EX_STAGES * EX_ROWS * EX_COLS;   // [stage][row][32]
+  constexpr int SLICE = EX_STAGES * EX_ROWS * EX_COLS;
+  float* xs = ex_smem;               // [stage][row][32]
+  float* cs0 = ex_smem + SLICE;      // first survivor
+  float* cs1 = ex_smem + 2 * SLICE;  // second survivor (revival twins)
   __shared__ const float* xrow_s[EX_ROWS];
-  __shared__ const float* crow_s[EX_ROWS];
+  __shared__ const float* crow0_s[EX_ROWS];
+  __shared__ const float* crow1_s[EX_ROWS];
+  __shared__ int two_s[EX_ROWS];
   const int t = threadIdx.x;
   const long i = (long)blockIdx.x * EX_ROWS + t;
-  const bool mine = i < m && surv_cnt[i] == 1;
+  const uint32_t ns = i < m ? surv_cnt[i] : 0;
+  const bool mine = ns == 1 || ns == 2;
   long row = 0;
-  uint32_t j = 0;
+  uint32_t j0 = 0, j1 = 0;
   if (mine) {
     row = ids ? (long)ids[p0 + i] : p0 + i;
-    j = surv[i * SURV];
+    j0 = surv[i * SURV];
+    j1 = ns == 2 ? surv[i * SURV + 1] : j0;
   }
   // Rows not handled here read row 0 / centroid 0 harmlessly and are not written.
   xrow_s[t] = x + row * (long)d;
-  crow_s[t] = c + (long)j * d;
+  crow0_s[t] = c + (long)j0 * d;
+  crow1_s[t] = c + (long)j1 * d;
+  two_s[t] = ns == 2;
   __syncthreads();
   const int nsl = d / EX_COLS;
-  // Each slice: 128 rows x 8 chunks for x and for c = 2048 copies, 16 per thread.
+  // Each slice: 128 rows x 8 16-byte chunks per operand, 8 of each per thread.
   auto issue = [&](int sl) {
     if (sl < nsl) {
       const int st = sl % EX_STAGES;
@@ -826,9 +902,11 @@ __global__ void __launch_bounds__(EX_ROWS) k_exact_staged(
       for (int u = 0; u < 8; u++) {
         const int idx = u * EX_ROWS + t;  // 0 .. 1023
         const int r = idx >> 3, q = idx & 7;
-        const int pq = q ^ (r & 7);
-        cp_async16(xs + (st * EX_ROWS + r) * EX_COLS + pq * 4, xrow_s[r] + sl * EX_COLS + q * 4);
-        cp_async16(cs + (st * EX_ROWS + r) * EX_COLS + pq * 4, crow_s[r] + sl * EX_COLS + q * 4);
+        const int off = (st * EX_ROWS + r) * EX_COLS + (q ^ (r & 7)) * 4;
+        const int g = sl * EX_COLS + q * 4;
+        cp_async16(xs + off, xrow_s[r] + g);
+        cp_async16(cs0 + off, crow0_s[r] + g);
+        if (two_s[r]) cp_async16(cs1 + off, crow1_s[r] + g);
       }
     }
     cp_async_commit();
@@ -838,21 +916,31 @@ __global__ void __launch_bounds__(EX_ROWS) k_exact_staged(
   // The L2 score needs the row's sum of squares in the CPU order (sequential,
   // no FMA); without cached norms it is summed here as the row streams by.
   const bool want_xn = !IP && !xnorm_row;
-  float acc = 0.0f, xn = -0.0f;
+  const bool two = ns == 2;
+  float acc0 = 0.0f, acc1 = 0.0f, xn = -0.0f;
   for (int sl = 0; sl < nsl; sl++) {
     issue(sl + EX_STAGES - 1);
     cp_async_wait<EX_STAGES - 1>();
     __syncthreads();
-    const int st = sl % EX_STAGES;
-    const float4* xr4 = reinterpret_cast<const float4*>(xs + (st * EX_ROWS + t) * EX_COLS);
-    const float4* cr4 = reinterpret_cast<const float4*>(cs + (st * EX_ROWS + t) * EX_COLS);
+    const int base = (sl % EX_STAGES * EX_ROWS + t) * EX_COLS;
+    const float4* xr4 = reinterpret_cast<const float4*>(xs + base);
+    const float4* c04 = reinterpret_cast<const float4*>(cs0 + base);
+    const float4* c14 = reinterpret_cast<const float4*>(cs1 + base);
 #pragma unroll
     for (int q = 0; q < 8; q++) {
-      const float4 a = xr4[q ^ (t & 7)], b = cr4[q ^ (t & 7)];
-      acc = __fmaf_rn(a.x, b.x, acc);
-      acc = __fmaf_rn(a.y, b.y, acc);
-      acc = __fmaf_rn(a.z, b.z, acc);
-      acc = __fmaf_rn(a.w, b.w, acc);
+      const int pq = q ^ (t & 7);
+      const float4 a = xr4[pq], b = c04[pq];
+      acc0 = __fmaf_rn(a.x, b.x, acc0);
+      acc0 = __fmaf_rn(a.y, b.y, acc0);
+      acc0 = __fmaf_rn(a.z, b.z, acc0);
+      acc0 = __fmaf_rn(a.w, b.w, acc0);
+      if (two) {
+        const float4 b1 = c14[pq];
+        acc1 = __fmaf_rn(a.x, b1.x, acc1);
+        acc1 = __fmaf_rn(a.y, b1.y, acc1);
+        acc1 = __fmaf_rn(a.z, b1.z, acc1);
+        acc1 = __fmaf_rn(a.w, b1.w, acc1);
+      }
       if (want_xn) {
         xn = __fadd_rn(xn, __fmul_rn(a.x, a.x));
         xn = __fadd_rn(xn, __fmul_rn(a.y, a.y));
@@ -864,12 +952,20 @@ __global__ void __launch_bounds__(EX_ROWS) k_exact_staged(
   }
   cp_async_wait<0>();
   if (!mine) return;
-  float score = acc;
+  float v0 = acc0, v1 = acc1;
   if (!IP) {
-    const float key = __fsub_rn(__ldg(cn + j), __fmul_rn(2.0f, acc));
-    score = fmaxf(__fadd_rn(xnorm_row ? xnorm_row[row] : xn, key), 0.0f);
+    v0 = __fsub_rn(__ldg(cn + j0), __fmul_rn(2.0f, acc0));
+    if (two) v1 = __fsub_rn(__ldg(cn + j1), __fmul_rn(2.0f, acc1));
   }
-  labels[p0 + i] = j;
+  uint32_t bj = j0;
+  float best = v0;
+  if (two && better<IP>(v1, j1, v0, j0)) {
+    best = v1;
+    bj = j1;
+  }
+  float score = best;
+  if (!IP) score = fmaxf(__fadd_rn(xnorm_row ? xnorm_row[row] : xn, best), 0.0f);
+  labels[p0 + i] = bj;
   scores[p0 + i] = score;
   surv_cnt[i] = 0;  // done: k_exact skips the row
 }
@@ -981,12 +1077,10 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
   const size_t d = a.d, k = a.k;
   const size_t dp = (d + BKH - 1) / BKH * BKH;
   const size_t m_all = a.r1 - a.r0;
-  // Rows per pass: whole waves of 128-row CTAs, sized so that a pass's rows
-  // (FP32 and FP16, 6 bytes per element) stay in L2 from the conversion
-  // through the screen to the exact re-score.
+  // Rows per pass: eight 128-row tiles per SM, so that each persistent CTA
+  // keeps its operand ring and TMEM buffers running across tiles.
   const size_t wave = (size_t)e->num_sms * BM;
-  const size_t fit = (size_t)L2_BUDGET / (6 * dp) / wave * wave;
-  const size_t chunk = std::min(m_all, std::min(std::max(wave, fit), MAX_CHUNK_ROWS));
+  const size_t chunk = std::min(m_all, PASS_WAVES * wave);
   const bool ip = a.metric == EB_IP;
 
   // Bound coefficients for this d (see the header comment), with 1% slack.
@@ -1078,7 +1172,7 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
     EB_LAUNCH("screen refine");
     const unsigned egrid = (unsigned)((m + 127) / 128);
     if (d % EX_COLS == 0) {
-      const size_t ex_smem = 2 * EX_STAGES * EX_ROWS * EX_COLS * sizeof(float);
+      const size_t ex_smem = 3 * EX_STAGES * EX_ROWS * EX_COLS * sizeof(float);
       if (ip) {
         set_exact_smem<true>(e->device, ex_smem);
         k_exact_staged<true><<<egrid, EX_ROWS, ex_smem, e->stream>>>(
