@@ -223,6 +223,19 @@ __device__ __forceinline__ void group_scores(uint32_t taddr, const float* cns, f
   }
 }
 
+// Keep only the entries of a row's candidate list still inside the window
+// (out of line: it runs only when a list nears its capacity).
+template <bool IP>
+__device__ __noinline__ uint32_t compact_list(uint2* list, uint32_t cnt, float thr) {
+  uint32_t w = 0;
+  for (uint32_t e = 0; e < cnt; e++) {
+    const uint2 en = list[e];
+    const float sv = __uint_as_float(en.y);
+    if (IP ? (sv >= thr) : (sv <= thr)) list[w++] = en;
+  }
+  return w;
+}
+
 // ---------------------------------------------------------------- prep kernels
 
 // Scaled FP16 copy of the selected rows (one warp per row), with the row's
@@ -581,23 +594,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           best = gb;
           thr = IP ? __fsub_rd(best, off) : __fadd_ru(best, off);
         }
+        // Straight-line admission mask; the append runs only when it is set.
+        uint32_t adm_lo = 0, adm_hi = 0;
 #pragma unroll
-        for (int j = 0; j < 64; j++) {
-          if (collect && (IP ? (s[j] >= thr) : (s[j] <= thr))) {
-            if (cnt == CAP) {
-              // Full: drop the entries the current window has left behind.
-              uint32_t w = 0;
-              for (uint32_t e2 = 0; e2 < CAP; e2++) {
-                const uint2 en = row_list[e2];
-                const float sv = __uint_as_float(en.y);
-                if (IP ? (sv >= thr) : (sv <= thr)) row_list[w++] = en;
-              }
-              cnt = w;
+        for (int j = 0; j < 32; j++) {
+          adm_lo |= (uint32_t)(IP ? (s[j] >= thr) : (s[j] <= thr)) << j;
+          adm_hi |= (uint32_t)(IP ? (s[j + 32] >= thr) : (s[j + 32] <= thr)) << j;
+        }
+        if (collect && (adm_lo | adm_hi)) {
+          if (cnt + 64 > CAP) cnt = compact_list<IP>(row_list, cnt, thr);
+          const uint32_t base = (uint32_t)(col0 + g * 64);
+#pragma unroll
+          for (int j = 0; j < 64; j++) {
+            const bool in = ((j < 32 ? adm_lo : adm_hi) >> (j & 31)) & 1u;
+            if (in) {
+              if (cnt < CAP) row_list[cnt] = make_uint2(base + j, __float_as_uint(s[j]));
+              overflow |= cnt >= CAP;
+              cnt += cnt < CAP;
             }
-            if (cnt < CAP)
-              row_list[cnt++] = make_uint2((uint32_t)(col0 + g * 64 + j), __float_as_uint(s[j]));
-            else
-              overflow = true;
           }
         }
       }
