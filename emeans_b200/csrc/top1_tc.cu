@@ -662,7 +662,8 @@ __global__ void __launch_bounds__(256) k_refine(
     const float* __restrict__ x, int d, const uint32_t* __restrict__ ids, long p0, long m,
     const float* __restrict__ c, const float* __restrict__ cn, const uint2* __restrict__ cand,
     const uint32_t* __restrict__ cand_cnt, const float* __restrict__ cand_thr, float e2,
-    uint32_t* __restrict__ surv, uint32_t* __restrict__ surv_cnt, uint32_t* __restrict__ list,
+    uint2* __restrict__ pairs, uint32_t* __restrict__ pair_count,
+    unsigned long long* __restrict__ rkey, uint32_t* __restrict__ list,
     uint32_t* __restrict__ list_count, unsigned long long* __restrict__ counters) {
   __shared__ float pv_s[8][CAP], pe_s[8][CAP];
   __shared__ uint32_t pj_s[8][CAP];
@@ -672,7 +673,7 @@ __global__ void __launch_bounds__(256) k_refine(
   const uint32_t cnt = cand_cnt[i];
   if (cnt == FALLBACK) {
     if (lane == 0) {
-      surv_cnt[i] = 0;
+      rkey[i] = IP ? 0ull : ~0ull;
       to_list((uint32_t)(p0 + i), list, list_count, counters);
     }
     return;
@@ -801,18 +802,32 @@ __global__ void __launch_bounds__(256) k_refine(
     const int e = base + lane;
     const bool keep = e < np && (IP ? __fadd_ru(pv[e], pe[e]) >= lim
                                     : __fsub_rd(pv[e], pe[e]) <= lim);
-    const uint32_t mask = __ballot_sync(0xFFFFFFFFu, keep);
-    const int slot = ns + __popc(mask & ((1u << lane) - 1u));
-    if (keep && slot < SURV) surv[i * SURV + slot] = pj[e];
-    ns += __popc(mask);
+    ns += __popc(__ballot_sync(0xFFFFFFFFu, keep));
   }
+  // Each survivor becomes a (row, centroid) pair for the exact stage; the
+  // row's result key starts at the identity of its reduction.
+  const bool ok = ns >= 1 && ns <= SURV;
+  uint32_t pbase = 0;
   if (lane == 0) {
     atomicAdd(&counters[2], (unsigned long long)np);
-    if (ns == 0 || ns > SURV) {
-      surv_cnt[i] = 0;
-      to_list((uint32_t)p, list, list_count, counters);
+    if (ok) {
+      pbase = atomicAdd(pair_count, (uint32_t)ns);
+      rkey[i] = IP ? 0ull : ~0ull;
     } else {
-      surv_cnt[i] = (uint32_t)ns;
+      rkey[i] = IP ? 0ull : ~0ull;
+      to_list((uint32_t)p, list, list_count, counters);
+    }
+  }
+  pbase = __shfl_sync(0xFFFFFFFFu, pbase, 0);
+  if (ok) {
+    int w = 0;
+    for (int base = 0; base < np; base += 32) {
+      const int e = base + lane;
+      const bool keep = e < np && (IP ? __fadd_ru(pv[e], pe[e]) >= lim
+                                      : __fsub_rd(pv[e], pe[e]) <= lim);
+      const uint32_t mask = __ballot_sync(0xFFFFFFFFu, keep);
+      if (keep) pairs[pbase + w + __popc(mask & ((1u << lane) - 1u))] = make_uint2((uint32_t)i, pj[e]);
+      w += __popc(mask);
     }
   }
 }
@@ -855,12 +870,13 @@ __device__ __forceinline__ float chain(const float* __restrict__ x, const float*
   return acc;
 }
 
-// Exact chains, one thread per row, for rows with one or two survivors (two
-// are revival twins, nearly the same centroid) when d % 32 == 0: x and the
-// survivors' centroids stream through shared memory in 32-column slices
-// (cp.async, 4 slices in flight), each 16-byte chunk q of row t stored at
-// q ^ (t & 7) so that the per-thread LDS.128 reads are free of bank conflicts.
-// Rows with more survivors keep ns and go to k_exact below.
+// Exact chains over flattened (row, survivor) pairs, one thread per pair:
+// x and the survivor's centroid stream through shared memory in 32-column
+// slices (cp.async, 4 slices in flight), each 16-byte chunk q of pair slot t
+// stored at q ^ (t & 7) so that the per-thread LDS.128 reads are free of bank
+// conflicts. Each pair folds (value, id) into its row's 64-bit key with an
+// atomic max (IP) / min (L2): the key orders by value, then by the lower id,
+// which is the CPU's strict scan (-0.0 counts as +0.0, as it compares equal).
 constexpr int EX_ROWS = 128, EX_COLS = 32, EX_STAGES = 4;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -875,157 +891,169 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Key of (v, j): larger key = better for IP (max v, then min j); smaller key
+// = better for L2 (min v, then min j).
 template <bool IP>
-__global__ void __launch_bounds__(EX_ROWS) k_exact_staged(
-    const float* __restrict__ x, int d, const uint32_t* __restrict__ ids, long p0, long m,
+__device__ __forceinline__ unsigned long long result_key(float v, uint32_t j) {
+  if (v == 0.0f) v = 0.0f;  // -0.0 == +0.0 in the CPU's comparisons
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (IP ? (uint32_t)~j : j);
+}
+
+template <bool IP>
+__global__ void __launch_bounds__(EX_ROWS) k_pairs(
+    const float* __restrict__ x, int d, const uint32_t* __restrict__ ids, long p0,
     const float* __restrict__ c, const float* __restrict__ cn, const float* __restrict__ xnorm_row,
-    const uint32_t* __restrict__ surv,
-    uint32_t* __restrict__ surv_cnt, uint32_t* __restrict__ labels, float* __restrict__ scores) {
+    const uint2* __restrict__ pairs, const uint32_t* __restrict__ pair_count,
+    unsigned long long* __restrict__ rkey, float* __restrict__ xn_pos,
+    uint32_t* __restrict__ bad) {
   extern __shared__ __align__(16) float ex_smem[];
   constexpr int SLICE = EX_STAGES * EX_ROWS * EX_COLS;
-  float* xs = ex_smem;               // [stage][row][32]
-  float* cs0 = ex_smem + SLICE;      // first survivor
-  float* cs1 = ex_smem + 2 * SLICE;  // second survivor (revival twins)
+  float* xs = ex_smem;          // [stage][pair][32]
+  float* cs = ex_smem + SLICE;  // [stage][pair][32]
   __shared__ const float* xrow_s[EX_ROWS];
-  __shared__ const float* crow0_s[EX_ROWS];
-  __shared__ const float* crow1_s[EX_ROWS];
-  __shared__ int two_s[EX_ROWS];
+  __shared__ const float* crow_s[EX_ROWS];
   const int t = threadIdx.x;
-  const long i = (long)blockIdx.x * EX_ROWS + t;
-  const uint32_t ns = i < m ? surv_cnt[i] : 0;
-  const bool mine = ns == 1 || ns == 2;
-  long row = 0;
-  uint32_t j0 = 0, j1 = 0;
-  if (mine) {
-    row = ids ? (long)ids[p0 + i] : p0 + i;
-    j0 = surv[i * SURV];
-    j1 = ns == 2 ? surv[i * SURV + 1] : j0;
-  }
-  // Rows not handled here read row 0 / centroid 0 harmlessly and are not written.
-  xrow_s[t] = x + row * (long)d;
-  crow0_s[t] = c + (long)j0 * d;
-  crow1_s[t] = c + (long)j1 * d;
-  two_s[t] = ns == 2;
-  __syncthreads();
+  const long np = (long)*pair_count;
   const int nsl = d / EX_COLS;
-  // Each slice: 128 rows x 8 16-byte chunks per operand, 8 of each per thread.
-  auto issue = [&](int sl) {
-    if (sl < nsl) {
-      const int st = sl % EX_STAGES;
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const int idx = u * EX_ROWS + t;  // 0 .. 1023
-        const int r = idx >> 3, q = idx & 7;
-        const int off = (st * EX_ROWS + r) * EX_COLS + (q ^ (r & 7)) * 4;
-        const int g = sl * EX_COLS + q * 4;
-        cp_async16(xs + off, xrow_s[r] + g);
-        cp_async16(cs0 + off, crow0_s[r] + g);
-        if (two_s[r]) cp_async16(cs1 + off, crow1_s[r] + g);
-      }
-    }
-    cp_async_commit();
-  };
-#pragma unroll
-  for (int s = 0; s < EX_STAGES - 1; s++) issue(s);
-  // The L2 score needs the row's sum of squares in the CPU order (sequential,
-  // no FMA); without cached norms it is summed here as the row streams by.
   const bool want_xn = !IP && !xnorm_row;
-  const bool two = ns == 2;
-  float acc0 = 0.0f, acc1 = 0.0f, xn = -0.0f;
-  for (int sl = 0; sl < nsl; sl++) {
-    issue(sl + EX_STAGES - 1);
-    cp_async_wait<EX_STAGES - 1>();
-    __syncthreads();
-    const int base = (sl % EX_STAGES * EX_ROWS + t) * EX_COLS;
-    const float4* xr4 = reinterpret_cast<const float4*>(xs + base);
-    const float4* c04 = reinterpret_cast<const float4*>(cs0 + base);
-    const float4* c14 = reinterpret_cast<const float4*>(cs1 + base);
-#pragma unroll
-    for (int q = 0; q < 8; q++) {
-      const int pq = q ^ (t & 7);
-      const float4 a = xr4[pq], b = c04[pq];
-      acc0 = __fmaf_rn(a.x, b.x, acc0);
-      acc0 = __fmaf_rn(a.y, b.y, acc0);
-      acc0 = __fmaf_rn(a.z, b.z, acc0);
-      acc0 = __fmaf_rn(a.w, b.w, acc0);
-      if (two) {
-        const float4 b1 = c14[pq];
-        acc1 = __fmaf_rn(a.x, b1.x, acc1);
-        acc1 = __fmaf_rn(a.y, b1.y, acc1);
-        acc1 = __fmaf_rn(a.z, b1.z, acc1);
-        acc1 = __fmaf_rn(a.w, b1.w, acc1);
-      }
-      if (want_xn) {
-        xn = __fadd_rn(xn, __fmul_rn(a.x, a.x));
-        xn = __fadd_rn(xn, __fmul_rn(a.y, a.y));
-        xn = __fadd_rn(xn, __fmul_rn(a.z, a.z));
-        xn = __fadd_rn(xn, __fmul_rn(a.w, a.w));
-      }
+  for (long tile = blockIdx.x; tile * EX_ROWS < np; tile += gridDim.x) {
+    const long pi = tile * EX_ROWS + t;
+    const bool mine = pi < np;
+    uint2 pr = make_uint2(0, 0);
+    long row = 0;
+    if (mine) {
+      pr = pairs[pi];
+      row = ids ? (long)ids[p0 + pr.x] : p0 + pr.x;
     }
-    __syncthreads();  // the slot is refilled next iteration
+    // Slots past the pair count read row 0 / centroid 0 harmlessly and write nothing.
+    xrow_s[t] = x + row * (long)d;
+    crow_s[t] = c + (long)pr.y * d;
+    __syncthreads();
+    auto issue = [&](int sl) {
+      if (sl < nsl) {
+        const int st = sl % EX_STAGES;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          const int idx = u * EX_ROWS + t;  // 0 .. 1023
+          const int r = idx >> 3, q = idx & 7;
+          const int off = (st * EX_ROWS + r) * EX_COLS + (q ^ (r & 7)) * 4;
+          const int g = sl * EX_COLS + q * 4;
+          cp_async16(xs + off, xrow_s[r] + g);
+          cp_async16(cs + off, crow_s[r] + g);
+        }
+      }
+      cp_async_commit();
+    };
+#pragma unroll
+    for (int s = 0; s < EX_STAGES - 1; s++) issue(s);
+    float acc = 0.0f, xn = -0.0f;
+    for (int sl = 0; sl < nsl; sl++) {
+      issue(sl + EX_STAGES - 1);
+      cp_async_wait<EX_STAGES - 1>();
+      __syncthreads();
+      const int base = (sl % EX_STAGES * EX_ROWS + t) * EX_COLS;
+      const float4* xr4 = reinterpret_cast<const float4*>(xs + base);
+      const float4* cr4 = reinterpret_cast<const float4*>(cs + base);
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        const int pq = q ^ (t & 7);
+        const float4 a = xr4[pq], b = cr4[pq];
+        acc = __fmaf_rn(a.x, b.x, acc);
+        acc = __fmaf_rn(a.y, b.y, acc);
+        acc = __fmaf_rn(a.z, b.z, acc);
+        acc = __fmaf_rn(a.w, b.w, acc);
+        if (want_xn) {
+          // The row's sum of squares in the CPU order (sequential, no FMA).
+          xn = __fadd_rn(xn, __fmul_rn(a.x, a.x));
+          xn = __fadd_rn(xn, __fmul_rn(a.y, a.y));
+          xn = __fadd_rn(xn, __fmul_rn(a.z, a.z));
+          xn = __fadd_rn(xn, __fmul_rn(a.w, a.w));
+        }
+      }
+      __syncthreads();  // the slot is refilled next iteration
+    }
+    cp_async_wait<0>();
+    if (mine) {
+      const float v = IP ? acc : __fsub_rn(__ldg(cn + pr.y), __fmul_rn(2.0f, acc));
+      if (!isfinite(v)) {
+        bad[pr.x] = 1;  // overflowing chains: the exact scan reproduces the CPU here
+      } else if (IP) {
+        atomicMax(rkey + pr.x, result_key<IP>(v, pr.y));
+      } else {
+        atomicMin(rkey + pr.x, result_key<IP>(v, pr.y));
+      }
+      if (want_xn) xn_pos[pr.x] = xn;  // the same value from every pair of the row
+    }
+    __syncthreads();  // row pointers are rewritten by the next tile
   }
-  cp_async_wait<0>();
-  if (!mine) return;
-  float v0 = acc0, v1 = acc1;
-  if (!IP) {
-    v0 = __fsub_rn(__ldg(cn + j0), __fmul_rn(2.0f, acc0));
-    if (two) v1 = __fsub_rn(__ldg(cn + j1), __fmul_rn(2.0f, acc1));
-  }
-  uint32_t bj = j0;
-  float best = v0;
-  if (two && better<IP>(v1, j1, v0, j0)) {
-    best = v1;
-    bj = j1;
-  }
-  float score = best;
-  if (!IP) score = fmaxf(__fadd_rn(xnorm_row ? xnorm_row[row] : xn, best), 0.0f);
-  labels[p0 + i] = bj;
-  scores[p0 + i] = score;
-  surv_cnt[i] = 0;  // done: k_exact skips the row
 }
 
+// The same for d % 32 != 0: one thread per pair reads its operands directly.
 template <bool IP>
-__global__ void k_exact(const float* __restrict__ x, int d, const uint32_t* __restrict__ ids,
-                        long p0, long m, const float* __restrict__ c, const float* __restrict__ cn,
-                        const float* __restrict__ xnorm_row,
-                        const uint32_t* __restrict__ surv, const uint32_t* __restrict__ surv_cnt,
-                        uint32_t* __restrict__ labels, float* __restrict__ scores) {
+__global__ void k_pairs_plain(const float* __restrict__ x, int d, const uint32_t* __restrict__ ids,
+                              long p0, const float* __restrict__ c, const float* __restrict__ cn,
+                              const float* __restrict__ xnorm_row, const uint2* __restrict__ pairs,
+                              const uint32_t* __restrict__ pair_count,
+                              unsigned long long* __restrict__ rkey, float* __restrict__ xn_pos,
+                              uint32_t* __restrict__ bad) {
+  const long np = (long)*pair_count;
+  for (long pi = (long)blockIdx.x * blockDim.x + threadIdx.x; pi < np;
+       pi += (long)gridDim.x * blockDim.x) {
+    const uint2 pr = pairs[pi];
+    const long row = ids ? (long)ids[p0 + pr.x] : p0 + pr.x;
+    const float* xr = x + row * (long)d;
+    const float acc = chain(xr, c + (long)pr.y * d, d);
+    const float v = IP ? acc : __fsub_rn(__ldg(cn + pr.y), __fmul_rn(2.0f, acc));
+    if (!isfinite(v)) {
+      bad[pr.x] = 1;
+    } else if (IP) {
+      atomicMax(rkey + pr.x, result_key<IP>(v, pr.y));
+    } else {
+      atomicMin(rkey + pr.x, result_key<IP>(v, pr.y));
+    }
+    if (!IP && !xnorm_row) {
+      float xn = -0.0f;
+      for (int u = 0; u < d; u++) {
+        const float a = __ldg(xr + u);
+        xn = __fadd_rn(xn, __fmul_rn(a, a));
+      }
+      xn_pos[pr.x] = xn;
+    }
+  }
+}
+
+// Labels and scores from the rows' keys; rows whose chains overflowed join
+// the exact kernel's list.
+template <bool IP>
+__global__ void k_finish(const uint32_t* __restrict__ ids, long p0, long m,
+                         const float* __restrict__ xnorm_row, const float* __restrict__ xn_pos,
+                         const unsigned long long* __restrict__ rkey, uint32_t* __restrict__ bad,
+                         uint32_t* __restrict__ labels, float* __restrict__ scores,
+                         uint32_t* __restrict__ list, uint32_t* __restrict__ list_count,
+                         unsigned long long* __restrict__ counters) {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= m) return;
-  const uint32_t ns = surv_cnt[i];
-  if (ns == 0) return;  // on the exact kernel's list
-  const long p = p0 + i;
-  const long row = ids ? (long)ids[p] : p;
-  const float* xr = x + row * (long)d;
-  float best = IP ? -INFINITY : INFINITY;
-  uint32_t bj = FALLBACK;
-  for (uint32_t s = 0; s < ns; s++) {
-    const uint32_t j = surv[i * SURV + s];
-    float v = chain(xr, c + (long)j * d, d);
-    if (!IP) v = __fsub_rn(__ldg(cn + j), __fmul_rn(2.0f, v));
-    if (better<IP>(v, j, best, bj)) {
-      best = v;
-      bj = j;
-    }
+  const unsigned long long key = rkey[i];
+  if (bad[i]) {
+    bad[i] = 0;
+    to_list((uint32_t)(p0 + i), list, list_count, counters);
+    return;
   }
-  float score = best;
+  if (key == (IP ? 0ull : ~0ull)) return;  // on the list already (or no pair)
+  const uint32_t ord = (uint32_t)(key >> 32);
+  const uint32_t u = (ord & 0x80000000u) ? (ord & 0x7FFFFFFFu) : ~ord;
+  const float v = __uint_as_float(u);
+  const uint32_t j = IP ? ~(uint32_t)key : (uint32_t)key;
+  float score = v;
   if (!IP) {
-    float xn;
-    if (xnorm_row) {
-      xn = xnorm_row[row];
-    } else {
-      xn = -0.0f;  // sequential sum of squares, the CPU order
-      for (int t = 0; t < d; t++) {
-        const float v = __ldg(xr + t);
-        xn = __fadd_rn(xn, __fmul_rn(v, v));
-      }
-    }
-    score = fmaxf(__fadd_rn(xn, best), 0.0f);
+    const long row = ids ? (long)ids[p0 + i] : p0 + i;
+    score = fmaxf(__fadd_rn(xnorm_row ? xnorm_row[row] : xn_pos[i], v), 0.0f);
   }
-  labels[p] = bj;
-  scores[p] = score;
+  labels[p0 + i] = j;
+  scores[p0 + i] = score;
 }
-
 // ---------------------------------------------------------------- host side
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1072,7 +1100,7 @@ template <bool IP>
 void set_exact_smem(int device, size_t bytes) {
   static uint64_t done = 0;
   if (!(done >> device & 1)) {
-    EB_CUDA(cudaFuncSetAttribute(k_exact_staged<IP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    EB_CUDA(cudaFuncSetAttribute(k_pairs<IP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)bytes));
     done |= 1ull << device;
   }
@@ -1125,8 +1153,11 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
   uint2* cand = e->scratch_get<uint2>("tc_cand", chunk * CAP);
   uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", chunk);
   float* cand_thr = e->scratch_get<float>("tc_thr", chunk);
-  uint32_t* surv = e->scratch_get<uint32_t>("tc_surv", chunk * SURV);
-  uint32_t* surv_cnt = e->scratch_get<uint32_t>("tc_surv_cnt", chunk);
+  uint2* pairs = e->scratch_get<uint2>("tc_pairs", chunk * SURV);
+  uint32_t* pair_count = e->scratch_get<uint32_t>("tc_pair_count", 4);
+  unsigned long long* rkey = e->scratch_get<unsigned long long>("tc_rkey", chunk);
+  uint32_t* bad = e->scratch_get<uint32_t>("tc_bad", chunk);
+  float* xn_pos = e->scratch_get<float>("tc_xn_pos", chunk);
   // Precise-dot bound of the refine stage: each lane's FMA chain plus the
   // 5-level shuffle tree is at most kp roundings, gamma_kp sum|x c|; the exact
   // chain adds gamma_d sum|x c|; the computed sum|x c| is itself within gamma_kp.
@@ -1174,41 +1205,54 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf*) {
       k_screen<false><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(mapA, mapB, P);
     EB_LAUNCH("screen");
     EB_CUDA(cudaMemsetAsync(list_count, 0, 4, e->stream));
+    EB_CUDA(cudaMemsetAsync(pair_count, 0, 4, e->stream));
+    EB_CUDA(cudaMemsetAsync(bad, 0, m * sizeof(uint32_t), e->stream));
     const unsigned rgrid = (unsigned)((m + 7) / 8);  // 8 rows (warps) per block
     if (ip)
       k_refine<true><<<rgrid, 256, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
-                                                   a.cnorm, cand, cand_cnt, cand_thr, e2, surv,
-                                                   surv_cnt, list, list_count, counters);
+                                                   a.cnorm, cand, cand_cnt, cand_thr, e2, pairs,
+                                                   pair_count, rkey, list, list_count, counters);
     else
       k_refine<false><<<rgrid, 256, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
-                                                    a.cnorm, cand, cand_cnt, cand_thr, e2, surv,
-                                                    surv_cnt, list, list_count, counters);
+                                                    a.cnorm, cand, cand_cnt, cand_thr, e2, pairs,
+                                                    pair_count, rkey, list, list_count, counters);
     EB_LAUNCH("screen refine");
-    const unsigned egrid = (unsigned)((m + 127) / 128);
+    // The pair count is known on the device only: persistent blocks stride over it.
+    const unsigned pgrid = (unsigned)e->num_sms;
     if (d % EX_COLS == 0) {
-      const size_t ex_smem = 3 * EX_STAGES * EX_ROWS * EX_COLS * sizeof(float);
+      const size_t ex_smem = 2 * EX_STAGES * EX_ROWS * EX_COLS * sizeof(float);
       if (ip) {
         set_exact_smem<true>(e->device, ex_smem);
-        k_exact_staged<true><<<egrid, EX_ROWS, ex_smem, e->stream>>>(
-            a.x, (int)d, a.ids, (long)c0, (long)m, a.c, a.cnorm, a.xnorm, surv,
-            surv_cnt, a.labels, a.scores);
+        k_pairs<true><<<pgrid, EX_ROWS, ex_smem, e->stream>>>(a.x, (int)d, a.ids, (long)c0, a.c,
+                                                              a.cnorm, a.xnorm, pairs, pair_count,
+                                                              rkey, xn_pos, bad);
       } else {
         set_exact_smem<false>(e->device, ex_smem);
-        k_exact_staged<false><<<egrid, EX_ROWS, ex_smem, e->stream>>>(
-            a.x, (int)d, a.ids, (long)c0, (long)m, a.c, a.cnorm, a.xnorm, surv,
-            surv_cnt, a.labels, a.scores);
+        k_pairs<false><<<pgrid, EX_ROWS, ex_smem, e->stream>>>(a.x, (int)d, a.ids, (long)c0, a.c,
+                                                               a.cnorm, a.xnorm, pairs, pair_count,
+                                                               rkey, xn_pos, bad);
       }
-      EB_LAUNCH("screen exact chains (staged)");
+    } else {
+      if (ip)
+        k_pairs_plain<true><<<pgrid * 4, 128, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, a.c,
+                                                              a.cnorm, a.xnorm, pairs, pair_count,
+                                                              rkey, xn_pos, bad);
+      else
+        k_pairs_plain<false><<<pgrid * 4, 128, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, a.c,
+                                                               a.cnorm, a.xnorm, pairs,
+                                                               pair_count, rkey, xn_pos, bad);
     }
-    if (ip)
-      k_exact<true><<<egrid, 128, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
-                                                  a.cnorm, a.xnorm, surv, surv_cnt,
-                                                  a.labels, a.scores);
-    else
-      k_exact<false><<<egrid, 128, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
-                                                   a.cnorm, a.xnorm, surv, surv_cnt,
-                                                   a.labels, a.scores);
     EB_LAUNCH("screen exact chains");
+    const unsigned fgrid = (unsigned)((m + 255) / 256);
+    if (ip)
+      k_finish<true><<<fgrid, 256, 0, e->stream>>>(a.ids, (long)c0, (long)m, a.xnorm, xn_pos, rkey,
+                                                   bad, a.labels, a.scores, list, list_count,
+                                                   counters);
+    else
+      k_finish<false><<<fgrid, 256, 0, e->stream>>>(a.ids, (long)c0, (long)m, a.xnorm, xn_pos,
+                                                    rkey, bad, a.labels, a.scores, list,
+                                                    list_count, counters);
+    EB_LAUNCH("screen finish");
     Top1Args fa = a;
     fa.r0 = c0;
     fa.r1 = c0 + m;
