@@ -198,19 +198,25 @@ def run_ours(args):
     eng = eb.Engine(local)
     stream = torch.cuda.ExternalStream(eng.stream())
 
-    # Centroids: train on the shared config-2 rows (identical on every rank).
-    xtrain = gen_rows(n, d, 0)
+    # Centroids: train on the shared config-2 rows (identical on every rank),
+    # always the full 200,000 rows so that smaller --n runs see the same geometry.
+    xtrain = gen_rows(200_000, d, 0)
     cfg = eb.Config(d=d, k=k, seed=0, spherical=False)
     train_s = None
-    if not args.no_train:
+    if args.load_cent:
+        cent = np.load(args.load_cent).astype(np.float32)
+    elif not args.no_train:
         eng.train(xtrain, cfg)  # warm-up run
         t0 = time.perf_counter()
         tr = eng.train(xtrain, cfg)
         train_s = time.perf_counter() - t0
         cent = tr.centroids
     else:
-        cent = xtrain[np.random.default_rng(0).permutation(n)[:k]]
-    x = xtrain if rank == 0 else gen_rows(n, d, rank)
+        cent = xtrain[np.random.default_rng(0).permutation(xtrain.shape[0])[:k]]
+    if args.save_cent and rank == 0:
+        np.save(args.save_cent, cent)
+    x = xtrain[:n] if rank == 0 and n <= xtrain.shape[0] else gen_rows(n, d, rank)
+    x = np.ascontiguousarray(x)
 
     # ---- device-resident assign
     xb = eng.bind(x, d)
@@ -338,6 +344,8 @@ def main():
     ap.add_argument("--ref-rows", type=int, default=32768)
     ap.add_argument("--no-train", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--save-cent", default=None, help="write the trained centroids (.npy)")
+    ap.add_argument("--load-cent", default=None, help="use these centroids instead of training")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -39,6 +39,57 @@ __global__ void k_row_sumsq(const float* __restrict__ m, long rows, int d, float
   if (r < rows) out[r] = row_sumsq(m + r * d, d);
 }
 
+// The same sums for d % 32 == 0, one thread per row with the row streamed
+// through shared memory: 32 rows per block, 32-column slices copied with
+// cp.async (8 slices in flight), 16-byte chunk q of row t at q ^ (t & 7) so
+// that each thread's LDS.128 reads are free of bank conflicts.
+constexpr int NS_ROWS = 32, NS_STAGES = 8;
+
+__global__ void __launch_bounds__(NS_ROWS) k_row_sumsq_staged(const float* __restrict__ m,
+                                                              long rows, int d,
+                                                              float* __restrict__ out) {
+  __shared__ __align__(16) float buf[NS_STAGES][NS_ROWS][32];
+  const int t = threadIdx.x;
+  const long r0 = (long)blockIdx.x * NS_ROWS;
+  const int nsl = d / 32;
+  auto issue = [&](int sl) {
+    if (sl < nsl) {
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int r = u * 4 + (t >> 3), q = t & 7;
+        const long row = min(r0 + r, rows - 1);
+        const float* src = m + row * d + sl * 32 + q * 4;
+        float* dst = &buf[sl % NS_STAGES][r][(q ^ (r & 7)) * 4];
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                         (uint32_t)__cvta_generic_to_shared(dst)),
+                     "l"(src)
+                     : "memory");
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+#pragma unroll
+  for (int s = 0; s < NS_STAGES - 1; s++) issue(s);
+  float s = -0.0f;
+  for (int sl = 0; sl < nsl; sl++) {
+    issue(sl + NS_STAGES - 1);
+    asm volatile("cp.async.wait_group %0;" ::"n"(NS_STAGES - 1) : "memory");
+    __syncwarp();
+    const float4* r4 = reinterpret_cast<const float4*>(buf[sl % NS_STAGES][t]);
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      const float4 v = r4[q ^ (t & 7)];
+      s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+      s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+      s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+      s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+    }
+    __syncwarp();  // the slot is refilled next iteration
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (r0 + t < rows) out[r0 + t] = s;
+}
+
 __global__ void k_sel_sumsq(const float* __restrict__ x, long n, int d,
                             const uint32_t* __restrict__ ids, long r0, long r1,
                             float* __restrict__ out, uint32_t* status) {
@@ -256,8 +307,13 @@ unsigned blocks_for(size_t n, unsigned per) { return (unsigned)((n + per - 1) / 
 
 void row_norms(eb_engine* e, const float* m, size_t rows, size_t d, float* out) {
   if (rows == 0) return;
-  k_row_sumsq<<<blocks_for(rows, kRowThreads), kRowThreads, 0, e->stream>>>(m, (long)rows, (int)d,
-                                                                            out);
+  if (d % 32 == 0 && ((uintptr_t)m & 15) == 0) {
+    k_row_sumsq_staged<<<blocks_for(rows, NS_ROWS), NS_ROWS, 0, e->stream>>>(m, (long)rows,
+                                                                             (int)d, out);
+  } else {
+    k_row_sumsq<<<blocks_for(rows, kRowThreads), kRowThreads, 0, e->stream>>>(m, (long)rows,
+                                                                              (int)d, out);
+  }
   EB_LAUNCH("row_norms");
 }
 
