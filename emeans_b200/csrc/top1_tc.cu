@@ -1,37 +1,38 @@
-// Exact top-1 on the tensor cores: a tcgen05 FP16 screen, then an exact FP32
-// re-score of the few centroids the screen cannot rule out.
+// Exact top-1 on the tensor cores: a tcgen05 screen on split FP16 operands,
+// then the exact FP32 chain for the few centroids the screen cannot rule out.
 //
 // The labels and scores are the reference CPU kernel's bit for bit
 // (crates/emeans-core/src/assign/fused.rs:12-16: one sequential FMA chain per
 // dot, lower id on ties). The screen only decides which centroids get that
 // exact chain:
 //
-// 1. prep: rows and centroids are scaled by powers of two (per row for x, one
-//    exponent for all centroids) so that |v| < 2^14, and rounded to FP16.
-// 2. screen (tcgen05): a 128-row tile of x against 256-centroid tiles, FP32
-//    accumulators in TMEM (two buffers of 256 columns, so the epilogue reads
-//    one while the tensor cores fill the other), operands staged by TMA into
-//    128B-swizzled shared memory through a 4-stage mbarrier ring. The
-//    epilogue (one thread per row) reads each 256-column tile from TMEM twice:
-//    first for the tile's best score, which moves the row's running best, then
-//    to append every centroid within 2e of that best to the row's candidate
-//    list, where e bounds |screen - exact chain| (FP16 rounding of both
-//    operands, tensor-core accumulation, the FP32 chain itself). A centroid
-//    more than 2e behind the best cannot be the exact winner.
-// 3. refine (one warp per row): a precise FP32 dot per candidate with its own
-//    error bound (from the computed sum |x_t c_t|) leaves the candidates that
-//    could still be the exact best, usually one.
-// 4. exact (one thread per row): the exact FMA chain of each survivor; lower
-//    id on ties.
-// 5. fallback: rows with too many candidates, or non-finite inputs, take the
-//    exact SIMT kernel (top1_exact.cu).
+// 1. prep: rows (per-row exponent) and centroids (one exponent) are scaled by
+//    powers of two so that |v| < 2^14, and split into two FP16 terms,
+//    v' = hi + lo + r with |r| <= 2^-22 |v'| + 2^-24. A bound data set keeps
+//    this copy across calls.
+// 2. screen (tcgen05, persistent: one CTA per SM over 128-row tiles): each
+//    256-centroid tile accumulates xh.ch in one TMEM accumulator and
+//    xh.cl + xl.ch in a second (so the small terms are not rounded against the
+//    large partial sums); operands arrive by TMA in 64-byte-swizzled shared
+//    memory through a 4-stage mbarrier ring. The epilogue (one thread per row)
+//    adds the two accumulators, tracks the running best screened score and
+//    appends every centroid within 2e of it to the row's candidate list, where
+//    e bounds |screen - exact chain|. A centroid more than 2e behind the best
+//    cannot be the exact winner.
+// 3. collect: each row's candidates still inside the final window become
+//    (row, centroid) pairs.
+// 4. pairs: one thread per pair runs the exact FMA chain (operands streamed
+//    through shared memory) and folds (score, id) into the row's 64-bit key.
+// 5. finish: labels and scores from the keys; rows with non-finite inputs or
+//    too many candidates take the exact SIMT kernel (top1_exact.cu).
 //
-// Error bound (acc units, operands scaled): with u = 2^-11 and FP16
-// subnormals (half-ulp 2^-25),
-//   |acc - x'.c'| <= (2^-10 + 2^-22) sum|x'||c'| + 2^-24 (sum|x'| + sum|c'|)
-//                    + d 2^-21 sum|x'||c'|        (accumulation, taken loose)
-// and the FP32 chain differs from the exact dot by <= gamma_d sum|x c|.
-// sum|x'||c'| <= |x'| |c'|, sum|x'| <= sqrt(d) |x'| (Cauchy-Schwarz).
+// Error bound in accumulator units (operands scaled, u = 2^-11):
+//   split operands:   3 2^-22 sum|x'||c'| + 2^-23 (sum|x'| + sum|c'|)
+//   accumulation:     d 2^-21 sum|x'||c'| (four times the per-addition
+//                     truncation bound), the lo accumulator d 2^-30, the final
+//                     add 2^-23
+//   the FP32 chain:   gamma_d sum|x c| from the exact dot
+// with sum|x'||c'| <= |x'| |c'| and sum|x'| <= sqrt(d) |x'| (Cauchy-Schwarz).
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -44,11 +45,11 @@
 
 namespace eb {
 
-// The FP16 screen copy of a bound data set (its scaled rows, exponents and
-// norm bounds), built by the first screened top-1 on the set and kept until
-// the buffer is written or freed.
+// The split FP16 screen copy of a bound data set, built by the first screened
+// top-1 on the set and kept until the buffer is written or freed.
 struct Fp16Copy {
-  __half* xh = nullptr;  // n x dp
+  __half* xh = nullptr;  // n x dp, high terms
+  __half* xl = nullptr;  // n x dp, low terms
   int* xexp = nullptr;
   float* xnrm = nullptr;
   size_t n = 0, d = 0;
@@ -60,6 +61,7 @@ void drop_f16(eb_buf* b) {
   if (b && b->f16) {
     Fp16Copy* f = b->f16;
     cudaFreeAsync(f->xh, f->stream);
+    cudaFreeAsync(f->xl, f->stream);
     cudaFreeAsync(f->xexp, f->stream);
     cudaFreeAsync(f->xnrm, f->stream);
     delete f;
@@ -69,23 +71,25 @@ void drop_f16(eb_buf* b) {
 
 namespace {
 
-constexpr int BM = 128;          // rows per CTA (TMEM lanes)
-constexpr int BN = 256;          // centroids per tile (TMEM columns per buffer)
-constexpr int BKH = 64;          // FP16 columns per k-block: one 128-byte swizzle row
+constexpr int BM = 128;          // rows per tile (TMEM lanes)
+constexpr int BN = 256;          // centroids per tile (TMEM columns per accumulator)
+constexpr int BKH = 32;          // FP16 columns per k-block: one 64-byte swizzle row
 constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BKH * 2;
-constexpr int B_BYTES = BN * BKH * 2;
-constexpr int CAP = 128;         // per-row candidate list capacity
+constexpr int A_BYTES = BM * BKH * 2;                // one of xh / xl
+constexpr int B_BYTES = BN * BKH * 2;                // one of ch / cl
+constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
+constexpr int CAP = 64;          // per-row candidate list capacity
+constexpr int SURV = 16;         // candidates per row taken to exact chains
 constexpr int NTHREADS = 192;    // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr uint32_t FALLBACK = 0xFFFFFFFFu;
 constexpr int XEXP_BAD = INT_MIN;  // row with a non-finite value
-constexpr size_t PASS_WAVES = 8;  // row tiles per SM in one pass
+constexpr size_t PASS_WAVES = 8;   // row tiles per SM in one pass
 constexpr uint64_t WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
-// Operand ring, then 256 B of barriers / TMEM slot / flags, then per epilogue
-// warp two tiles of centroid norms.
-constexpr size_t SMEM_BYTES =
-    1024 /* alignment slack */ + STAGES * (A_BYTES + B_BYTES) + 256 + 4 * 2 * BN * sizeof(float);
+// Operand ring, 256 B of barriers / TMEM slot / flags, one tile of centroid
+// norms per epilogue warp.
+constexpr size_t SMEM_BYTES = 1024 /* alignment slack */ + STAGES * STAGE_BYTES + 256 +
+                              4 * BN * sizeof(float);
 
 // ---------------------------------------------------------------- PTX helpers
 
@@ -129,7 +133,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // abort flag set) after WAIT_NS, so that no wait can spin forever.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = now_ns();
+  const uint64_t t0 = now_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
@@ -149,14 +153,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// K-major operand tile with 128-byte rows, 128B swizzle, 8-row groups 1024 B apart.
+// K-major operand tile with 64-byte rows, 64B swizzle, 8-row groups 512 B apart.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset: 8 rows x 128 B
-  d |= (uint64_t)1 << 46;             // descriptor version (sm_100)
-  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(512 >> 4) << 32;   // stride byte offset: 8 rows x 64 B
+  d |= (uint64_t)1 << 46;            // descriptor version (sm_100)
+  d |= (uint64_t)4 << 61;            // SWIZZLE_64B
   return d;
 }
 
@@ -186,55 +190,22 @@ __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 
-// 64 consecutive FP32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+// 32 consecutive FP32 columns of this thread's TMEM lane (completes with
+// tmem_wait()).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
       "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-      "%30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
-      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
+      "%30, %31}, [%32];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
         "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
         "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
-        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]),
-        "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]),
-        "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]),
-        "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
-        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]),
-        "=r"(r[63])
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-
-// Screened scores of 64 columns of this thread's row, `lim` of them real
-// (lim >= 64: all): the raw accumulator (IP), or the key cn_j - 2 f acc_j with
-// one rounding (L2), with the norms read from shared memory. Columns past k
-// score -inf (IP) / +inf (L2), so they never win or enter.
-template <bool IP>
-__device__ __forceinline__ void group_scores(uint32_t taddr, const float* cns, float m2f, int lim,
-                                             float (&s)[64]) {
-  uint32_t v[64];
-  tmem_ld64(taddr, v);
-  if (IP) {
-#pragma unroll
-    for (int j = 0; j < 64; j++) s[j] = __uint_as_float(v[j]);
-  } else {
-    const float4* c4 = reinterpret_cast<const float4*>(cns);
-#pragma unroll
-    for (int j = 0; j < 64; j += 4) {
-      const float4 c = c4[j / 4];
-      s[j] = __fmaf_rn(m2f, __uint_as_float(v[j]), c.x);
-      s[j + 1] = __fmaf_rn(m2f, __uint_as_float(v[j + 1]), c.y);
-      s[j + 2] = __fmaf_rn(m2f, __uint_as_float(v[j + 2]), c.z);
-      s[j + 3] = __fmaf_rn(m2f, __uint_as_float(v[j + 3]), c.w);
-    }
-  }
-  if (lim < 64) {
-#pragma unroll
-    for (int j = 0; j < 64; j++)
-      if (j >= lim) s[j] = IP ? -INFINITY : INFINITY;
-  }
+__device__ __forceinline__ void tmem_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // Keep only the entries of a row's candidate list still inside the window
@@ -252,25 +223,33 @@ __device__ __noinline__ uint32_t compact_list(uint2* list, uint32_t cnt, float t
 
 // ---------------------------------------------------------------- prep kernels
 
-// Scaled FP16 copy of the selected rows (one warp per row), with the row's
-// exponent (XEXP_BAD for non-finite rows) and an upper bound on its norm.
+// Split a scaled value into two FP16 terms: hi = RN(v), lo = RN(v - hi); the
+// difference v - hi is exact in FP32.
+__device__ __forceinline__ void split16(float v, __half& hi, __half& lo) {
+  hi = __float2half_rn(v);
+  lo = __float2half_rn(v - __half2float(hi));
+}
+
+// Scaled split FP16 copy of the selected rows (one warp per row), with the
+// row's exponent (XEXP_BAD for non-finite rows) and an upper bound on its norm.
 __global__ void k_prep_rows(const float* __restrict__ x, long n, int d, int dp,
                             const uint32_t* __restrict__ ids, long p0, long m,
-                            __half* __restrict__ xh, int* __restrict__ xexp,
-                            float* __restrict__ xnrm, uint32_t* status) {
-  long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  int lane = threadIdx.x & 31;
+                            __half* __restrict__ xh, __half* __restrict__ xl,
+                            int* __restrict__ xexp, float* __restrict__ xnrm, uint32_t* status) {
+  const long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
   if (i >= m) return;
-  long p = p0 + i;
-  long row = ids ? (long)ids[p] : p;
-  __half* out = xh + i * (long)dp;
+  const long p = p0 + i;
+  const long row = ids ? (long)ids[p] : p;
+  __half* oh = xh + i * (long)dp;
+  __half* ol = xl + i * (long)dp;
   if (row >= n) {
     if (lane == 0) {
       atomicOr(status, ST_BAD_ROW);
       xexp[i] = XEXP_BAD;
       xnrm[i] = 0.0f;
     }
-    for (int t = lane; t < dp; t += 32) out[t] = __float2half_rn(0.0f);
+    for (int t = lane; t < dp; t += 32) oh[t] = ol[t] = __float2half_rn(0.0f);
     return;
   }
   const float* r = x + row * (long)d;
@@ -303,20 +282,22 @@ __global__ void k_prep_rows(const float* __restrict__ x, long n, int d, int dp,
     for (int u = 0; u < 8; u++) {
       const int t = lane + 32 * u;
       if (t < q4) {
-        __half2 h0 = finite ? __floats2half2_rn(ldexpf(v[u].x, sh), ldexpf(v[u].y, sh))
-                            : __floats2half2_rn(0.f, 0.f);
-        __half2 h1 = finite ? __floats2half2_rn(ldexpf(v[u].z, sh), ldexpf(v[u].w, sh))
-                            : __floats2half2_rn(0.f, 0.f);
-        uint2 pk;
-        pk.x = *reinterpret_cast<uint32_t*>(&h0);
-        pk.y = *reinterpret_cast<uint32_t*>(&h1);
-        *reinterpret_cast<uint2*>(out + 4 * t) = pk;
+        const float a[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        __half h[4], l[4];
+#pragma unroll
+        for (int w = 0; w < 4; w++) split16(finite ? ldexpf(a[w], sh) : 0.0f, h[w], l[w]);
+        __half2 h01 = __halves2half2(h[0], h[1]), h23 = __halves2half2(h[2], h[3]);
+        __half2 l01 = __halves2half2(l[0], l[1]), l23 = __halves2half2(l[2], l[3]);
+        *reinterpret_cast<uint2*>(oh + 4 * t) =
+            make_uint2(*reinterpret_cast<uint32_t*>(&h01), *reinterpret_cast<uint32_t*>(&h23));
+        *reinterpret_cast<uint2*>(ol + 4 * t) =
+            make_uint2(*reinterpret_cast<uint32_t*>(&l01), *reinterpret_cast<uint32_t*>(&l23));
       }
     }
-    for (int t = d + lane; t < dp; t += 32) out[t] = __float2half_rn(0.0f);
+    for (int t = d + lane; t < dp; t += 32) oh[t] = ol[t] = __float2half_rn(0.0f);
   } else {
     for (int t = lane; t < d; t += 32) {
-      float v = __ldg(r + t);
+      const float v = __ldg(r + t);
       finite = finite && isfinite(v);
       mx = fmaxf(mx, fabsf(v));
       ss = fmaf(v, v, ss);
@@ -330,8 +311,8 @@ __global__ void k_prep_rows(const float* __restrict__ x, long n, int d, int dp,
     frexpf(mx, &ex);
     const int sh = 14 - ex;
     for (int t = lane; t < dp; t += 32) {
-      float v = t < d ? __ldg(r + t) : 0.0f;
-      out[t] = __float2half_rn(finite ? ldexpf(v, sh) : 0.0f);
+      const float v = t < d ? __ldg(r + t) : 0.0f;
+      split16(finite ? ldexpf(v, sh) : 0.0f, oh[t], ol[t]);
     }
   }
   if (lane == 0) {
@@ -341,21 +322,22 @@ __global__ void k_prep_rows(const float* __restrict__ x, long n, int d, int dp,
   }
 }
 
-// Rows x[ids[p]] of a cached FP16 copy gathered into the pass's staging rows
-// (one warp per row, 16-byte copies; dp * 2 bytes is a multiple of 128).
-__global__ void k_gather_rows(const __half* __restrict__ src_h, const int* __restrict__ src_e,
-                              const float* __restrict__ src_n, long n, int dp,
-                              const uint32_t* __restrict__ ids, long p0, long m,
-                              __half* __restrict__ xh, int* __restrict__ xexp,
-                              float* __restrict__ xnrm, uint32_t* status) {
+// Rows x[ids[p]] of a cached split copy gathered into the pass's staging rows
+// (one warp per row, 16-byte copies; dp * 2 bytes is a multiple of 64).
+__global__ void k_gather_rows(const __half* __restrict__ src_h, const __half* __restrict__ src_l,
+                              const int* __restrict__ src_e, const float* __restrict__ src_n,
+                              long n, int dp, const uint32_t* __restrict__ ids, long p0, long m,
+                              __half* __restrict__ xh, __half* __restrict__ xl,
+                              int* __restrict__ xexp, float* __restrict__ xnrm, uint32_t* status) {
   const long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (i >= m) return;
   const long row = ids[p0 + i];
-  uint4* out = reinterpret_cast<uint4*>(xh + i * (long)dp);
+  uint4* oh = reinterpret_cast<uint4*>(xh + i * (long)dp);
+  uint4* ol = reinterpret_cast<uint4*>(xl + i * (long)dp);
   const int q = dp / 8;
   if (row >= n) {
-    for (int t = lane; t < q; t += 32) out[t] = make_uint4(0, 0, 0, 0);
+    for (int t = lane; t < q; t += 32) oh[t] = ol[t] = make_uint4(0, 0, 0, 0);
     if (lane == 0) {
       atomicOr(status, ST_BAD_ROW);
       xexp[i] = XEXP_BAD;
@@ -363,8 +345,12 @@ __global__ void k_gather_rows(const __half* __restrict__ src_h, const int* __res
     }
     return;
   }
-  const uint4* in = reinterpret_cast<const uint4*>(src_h + row * (long)dp);
-  for (int t = lane; t < q; t += 32) out[t] = __ldg(in + t);
+  const uint4* ih = reinterpret_cast<const uint4*>(src_h + row * (long)dp);
+  const uint4* il = reinterpret_cast<const uint4*>(src_l + row * (long)dp);
+  for (int t = lane; t < q; t += 32) {
+    oh[t] = __ldg(ih + t);
+    ol[t] = __ldg(il + t);
+  }
   if (lane == 0) {
     xexp[i] = src_e[row];
     xnrm[i] = src_n[row];
@@ -374,14 +360,14 @@ __global__ void k_gather_rows(const __half* __restrict__ src_h, const int* __res
 // Global max |c|, a bound on max |c_j| and a non-finite flag, over all centroids.
 // cinfo (u32): [0] bits of max|c|, [1] bits of the norm bound, [2] non-finite flag.
 __global__ void k_cent_max(const float* __restrict__ c, long k, int d, uint32_t* cinfo) {
-  long j = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  int lane = threadIdx.x & 31;
+  const long j = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
   if (j >= k) return;
   const float* r = c + j * (long)d;
   float mx = 0.0f, ss = 0.0f;
   bool finite = true;
   for (int t = lane; t < d; t += 32) {
-    float v = __ldg(r + t);
+    const float v = __ldg(r + t);
     finite = finite && isfinite(v);
     mx = fmaxf(mx, fabsf(v));
     ss = fmaf(v, v, ss);
@@ -402,32 +388,31 @@ __global__ void k_cent_max(const float* __restrict__ c, long k, int d, uint32_t*
   }
 }
 
-// Scaled FP16 centroids: c' = c 2^(14 - ec), 2^(ec-1) <= max|c| < 2^ec.
+// Scaled split FP16 centroids: c' = c 2^(14 - ec), 2^(ec-1) <= max|c| < 2^ec.
 __global__ void k_cent_conv(const float* __restrict__ c, long k, int d, int dp,
-                            const uint32_t* __restrict__ cinfo, __half* __restrict__ ch) {
-  long j = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  int lane = threadIdx.x & 31;
+                            const uint32_t* __restrict__ cinfo, __half* __restrict__ ch,
+                            __half* __restrict__ cl) {
+  const long j = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
   if (j >= k) return;
   int ec = 0;
   frexpf(__uint_as_float(cinfo[0]), &ec);
-  int sh = 14 - ec;
-  bool bad = cinfo[2] != 0;
+  const int sh = 14 - ec;
+  const bool bad = cinfo[2] != 0;
   const float* r = c + j * (long)d;
-  __half* out = ch + j * (long)dp;
   for (int t = lane; t < dp; t += 32) {
-    float v = (t < d && !bad) ? __ldg(r + t) : 0.0f;
-    out[t] = __float2half_rn(ldexpf(v, sh));
+    const float v = (t < d && !bad) ? __ldg(r + t) : 0.0f;
+    split16(ldexpf(v, sh), ch[j * (long)dp + t], cl[j * (long)dp + t]);
   }
 }
 
 // ---------------------------------------------------------------- the screen
 
 struct ScreenParams {
-  long m;              // staging rows in this launch
+  long m;              // staging rows in this pass
   int k;
-  int kblocks;         // dp / 64
+  int kblocks;         // dp / 32
   int ntiles;          // ceil(k / 256)
-  int d;
   const int* xexp;     // per staging row
   const float* xnrm;   // per staging row
   const float* cn;     // k squared centroid norms (L2) or null
@@ -441,20 +426,19 @@ struct ScreenParams {
 
 template <bool IP>
 __global__ void __launch_bounds__(NTHREADS, 1)
-    k_screen(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    k_screen(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+             const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
              ScreenParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = (uint64_t*)(sB + STAGES * B_BYTES);
+  uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* mma_done = tempty + 2;
+  uint64_t* tempty = tfull + 1;
+  uint64_t* mma_done = tempty + 1;
   uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
-  float* cn_s = (float*)(smem + STAGES * (A_BYTES + B_BYTES) + 256);  // [4 warps][2][BN] (L2)
+  float* cn_s = (float*)(smem + STAGES * STAGE_BYTES + 256);  // [4 warps][BN]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -463,10 +447,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; a++) {
-      mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
-    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, 128);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -480,77 +462,83 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *tmem_slot;  // hi accumulator at column 0, lo at column BN
   const int total = P.ntiles * P.kblocks;
 
   if (warp == 0) {
     if (lane == 0) {
-      // TMA producer: per (row tile, centroid tile, k-block), one A box
-      // (128 x 64) and one B box (256 x 64). The ring runs on across row tiles.
+      // TMA producer: per (row tile, centroid tile, k-block) the four boxes
+      // xh, xl (128 x 32) and ch, cl (256 x 32). The ring runs on across tiles.
       int it = 0, issued = 0;
       bool stop = false;
       for (long rt = blockIdx.x; rt * BM < P.m && !stop; rt += gridDim.x) {
         for (int t2 = 0; t2 < total; t2++, it++) {
           const int s = it % STAGES;
-          const uint32_t par = ((it / STAGES) & 1) ^ 1;
-          if (!mbar_wait(&empty[s], par, abort_flag)) {
+          if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag)) {
             stop = true;
             break;
           }
           const int nt = t2 / P.kblocks, kb = t2 % P.kblocks;
-          mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
-          tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BKH, (int)(rt * BM));
-          tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * BKH, nt * BN);
+          uint8_t* st = smem + s * STAGE_BYTES;
+          mbar_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(st, &tmAh, &full[s], kb * BKH, (int)(rt * BM));
+          tma_load_2d(st + A_BYTES, &tmAl, &full[s], kb * BKH, (int)(rt * BM));
+          tma_load_2d(st + 2 * A_BYTES, &tmBh, &full[s], kb * BKH, nt * BN);
+          tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[s], kb * BKH, nt * BN);
           issued = it + 1;
         }
       }
       // No copy may still be landing in shared memory when the CTA exits: wait
       // (bounded) for the last loads issued. On the normal path they have
       // already been consumed and these waits return at once.
-      for (int it = issued > STAGES ? issued - STAGES : 0; it < issued; it++) {
-        uint64_t t0 = now_ns();
-        while (!mbar_try_wait(&full[it % STAGES], (it / STAGES) & 1) && now_ns() - t0 < WAIT_NS) {
+      for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; j++) {
+        const uint64_t t0 = now_ns();
+        while (!mbar_try_wait(&full[j % STAGES], (j / STAGES) & 1) && now_ns() - t0 < WAIT_NS) {
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // MMA issuer; tc counts (row tile, centroid tile) pairs for the TMEM buffers.
+      // MMA issuer; tc counts (row tile, centroid tile) pairs.
       int it = 0, tc = 0;
       bool stop = false;
-      for (long rt = blockIdx.x; rt * BM < P.m && !stop; rt += gridDim.x)
-      for (int nt = 0; nt < P.ntiles; nt++, tc++) {
-        const int a = tc & 1;
-        if (!mbar_wait(&tempty[a], ((tc >> 1) & 1) ^ 1, abort_flag)) {
-          stop = true;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t dcol = tmem + (uint32_t)(a * BN);
-        bool ok = true;
-        for (int kb = 0; kb < P.kblocks; kb++, it++) {
-          const int s = it % STAGES;
-          if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) {
-            ok = false;
+      for (long rt = blockIdx.x; rt * BM < P.m && !stop; rt += gridDim.x) {
+        for (int nt = 0; nt < P.ntiles; nt++, tc++) {
+          // The epilogue must have read both accumulators of the last tile.
+          if (!mbar_wait(tempty, (tc & 1) ^ 1, abort_flag)) {
+            stop = true;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+          bool ok = true;
+          for (int kb = 0; kb < P.kblocks; kb++, it++) {
+            const int s = it % STAGES;
+            if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t ah = smem_u32(smem + s * STAGE_BYTES);
+            const uint32_t al = ah + A_BYTES, bh = ah + 2 * A_BYTES, bl = bh + B_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BKH / 16; kk++)
-            umma_f16(dcol, umma_desc(a0 + kk * 32), umma_desc(b0 + kk * 32),
-                     (kb > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&empty[s]);
+            for (int kk = 0; kk < BKH / 16; kk++) {
+              const uint32_t first = (kb > 0 || kk > 0) ? 1u : 0u;
+              umma_f16(tmem, umma_desc(ah + kk * 32), umma_desc(bh + kk * 32), first);
+              umma_f16(tmem + BN, umma_desc(ah + kk * 32), umma_desc(bl + kk * 32), first);
+              umma_f16(tmem + BN, umma_desc(al + kk * 32), umma_desc(bh + kk * 32), 1u);
+            }
+            umma_commit(&empty[s]);
+          }
+          if (!ok) {
+            stop = true;
+            break;
+          }
+          umma_commit(tfull);
         }
-        if (!ok) {
-          stop = true;
-          break;
-        }
-        umma_commit(&tfull[a]);
       }
       // Every MMA this thread issued has completed once mma_done flips.
       umma_commit(mma_done);
-      uint64_t t0 = now_ns();
+      const uint64_t t0 = now_ns();
       while (!mbar_try_wait(mma_done, 0) && now_ns() - t0 < WAIT_NS) {
       }
     }
@@ -563,111 +551,118 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const float cmax = __uint_as_float(P.cinfo[1]);
     const bool c_bad = P.cinfo[2] != 0;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-    int tc = 0;  // (row tile, centroid tile) pairs, as the MMA issuer counts them
+    float* cns = cn_s + q * BN;
+    int tc = 0;
     bool stop = false;
     for (long rt = blockIdx.x; rt * BM < P.m && !stop; rt += gridDim.x) {
-    const long i = rt * BM + r;
-    const bool live = i < P.m;
-    const int ex = live ? P.xexp[i] : XEXP_BAD;
-    bool fallback = !live || ex == XEXP_BAD || c_bad;
-    const float xn = live ? P.xnrm[i] : 0.0f;
-    // |x'| and max |c'| in acc units, and the bound e (acc units).
-    const float xs = ldexpf(xn, 14 - (fallback ? 0 : ex));
-    const float cs = ldexpf(cmax, 14 - ec);
-    const float e_acc = fmaf(P.e_rel * xs, cs, fmaf(P.e_abs, xs + cs, P.e_min));
-    float off, m2f = 0.0f;
-    if (IP) {
-      off = 2.0f * e_acc;
-    } else {
-      const int fe = ex + ec - 28;
-      if (fe < -100 || fe > 100) fallback = true;
-      const float f = ldexpf(1.0f, fallback ? 0 : fe);
-      m2f = -2.0f * f;
-      const float e_key = fmaf(2.0f * f, e_acc, ldexpf(fmaf(cmax, cmax, 2.0f * xn * cmax), -22));
-      off = 2.0f * e_key;
-    }
-    if (!isfinite(off)) fallback = true;
-    const bool collect = live && !fallback;
-    float best = IP ? -INFINITY : INFINITY;
-    float thr = best;
-    bool overflow = false;
-    uint32_t cnt = 0;  // entries in this row's candidate list
-    uint2* row_list = P.cand + (live ? i : 0) * (long)CAP;
+      const long i = rt * BM + r;
+      const bool live = i < P.m;
+      const int ex = live ? P.xexp[i] : XEXP_BAD;
+      bool fallback = !live || ex == XEXP_BAD || c_bad;
+      const float xn = live ? P.xnrm[i] : 0.0f;
+      // |x'| and max |c'| in accumulator units, and the bound e there.
+      const float xs = ldexpf(xn, 14 - (fallback ? 0 : ex));
+      const float cs = ldexpf(cmax, 14 - ec);
+      const float e_acc = fmaf(P.e_rel * xs, cs, fmaf(P.e_abs, xs + cs, P.e_min));
+      float off, m2f = 0.0f;
+      if (IP) {
+        off = 2.0f * e_acc;
+      } else {
+        const int fe = ex + ec - 28;
+        if (fe < -100 || fe > 100) fallback = true;
+        const float f = ldexpf(1.0f, fallback ? 0 : fe);
+        m2f = -2.0f * f;
+        // key error: twice the dot error plus the key's two roundings.
+        const float e_key = fmaf(2.0f * f, e_acc, ldexpf(fmaf(cmax, cmax, 2.0f * xn * cmax), -22));
+        off = 2.0f * e_key;
+      }
+      if (!isfinite(off)) fallback = true;
+      const bool collect = live && !fallback;
+      float best = IP ? -INFINITY : INFINITY;
+      float thr = best;
+      bool overflow = false;
+      uint32_t cnt = 0;  // entries in this row's candidate list
+      uint2* row_list = P.cand + (live ? i : 0) * (long)CAP;
 
-    for (int nt = 0; nt < P.ntiles; nt++, tc++) {
-      const int a = tc & 1;
-      // Warp-uniform: the TMEM loads below are .sync.aligned.
-      const bool ready = __all_sync(0xFFFFFFFFu, mbar_wait(&tfull[a], (tc >> 1) & 1, abort_flag));
-      if (!ready) {
-        stop = true;
-        break;
-      }
-      tc_fence_after();
-      const int col0 = nt * BN;
-      const uint32_t tbase = lane_base + (uint32_t)(a * BN);
-      // This tile's squared centroid norms, staged by each warp for itself (no
-      // barrier across warps, so a timed-out wait can never strand another warp).
-      float* cns = cn_s + (q * 2 + a) * BN;
-      if (!IP) {
-#pragma unroll
-        for (int u = 0; u < BN / 32; u++) {
-          const int c = u * 32 + lane;
-          cns[c] = col0 + c < P.k ? __ldg(P.cn + col0 + c) : 0.0f;
+      for (int nt = 0; nt < P.ntiles; nt++, tc++) {
+        // Warp-uniform: the TMEM loads below are .sync.aligned.
+        const bool ready = __all_sync(0xFFFFFFFFu, mbar_wait(tfull, tc & 1, abort_flag));
+        if (!ready) {
+          stop = true;
+          break;
         }
-        __syncwarp();
-      }
-      const int ngr = min(BN / 64, (P.k - col0 + 63) / 64);
+        tc_fence_after();
+        const int col0 = nt * BN;
+        if (!IP) {
+          // This tile's squared centroid norms, staged by each warp for itself
+          // (no barrier across warps, so a timed-out wait strands no warp).
+#pragma unroll
+          for (int u = 0; u < BN / 32; u++) {
+            const int c = u * 32 + lane;
+            cns[c] = col0 + c < P.k ? __ldg(P.cn + col0 + c) : 0.0f;
+          }
+          __syncwarp();
+        }
+        const int ngr = min(BN / 32, (P.k - col0 + 31) / 32);
 #pragma unroll 1
-      for (int g = 0; g < ngr; g++) {
-        // One pass per 64 columns: scores, their best (which moves the
-        // threshold first), then every score within the window is appended.
-        float s[64];
-        group_scores<IP>(tbase + (uint32_t)(g * 64), cns + g * 64, m2f, P.k - (col0 + g * 64), s);
-        float gb;
-        {
-          float t[32];
+        for (int g = 0; g < ngr; g++) {
+          uint32_t vh[32], vl[32];
+          tmem_ld32(lane_base + (uint32_t)(g * 32), vh);
+          tmem_ld32(lane_base + (uint32_t)(BN + g * 32), vl);
+          tmem_wait();
+          const int lim = P.k - (col0 + g * 32);
+          float s[32];
+          const float4* c4 = reinterpret_cast<const float4*>(cns + g * 32);
 #pragma unroll
-          for (int j = 0; j < 32; j++) t[j] = IP ? fmaxf(s[j], s[j + 32]) : fminf(s[j], s[j + 32]);
+          for (int j = 0; j < 32; j += 4) {
+            const float4 cv = IP ? make_float4(0.f, 0.f, 0.f, 0.f) : c4[j / 4];
+            const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
 #pragma unroll
-          for (int w2 = 16; w2 >= 1; w2 >>= 1)
+            for (int w = 0; w < 4; w++) {
+              const float acc = __fadd_rn(__uint_as_float(vh[j + w]), __uint_as_float(vl[j + w]));
+              float v = IP ? acc : __fmaf_rn(m2f, acc, cc[w]);
+              if (j + w >= lim) v = IP ? -INFINITY : INFINITY;
+              s[j + w] = v;
+            }
+          }
+          // The group's best moves the threshold first.
+          float t[16];
+#pragma unroll
+          for (int j = 0; j < 16; j++) t[j] = IP ? fmaxf(s[j], s[j + 16]) : fminf(s[j], s[j + 16]);
+#pragma unroll
+          for (int w2 = 8; w2 >= 1; w2 >>= 1)
 #pragma unroll
             for (int j = 0; j < w2; j++) t[j] = IP ? fmaxf(t[j], t[j + w2]) : fminf(t[j], t[j + w2]);
-          gb = t[0];
-        }
-        if (IP ? (gb > best) : (gb < best)) {
-          best = gb;
-          thr = IP ? __fsub_rd(best, off) : __fadd_ru(best, off);
-        }
-        // Straight-line admission mask; the append runs only when it is set.
-        uint32_t adm_lo = 0, adm_hi = 0;
+          if (IP ? (t[0] > best) : (t[0] < best)) {
+            best = t[0];
+            thr = IP ? __fsub_rd(best, off) : __fadd_ru(best, off);
+          }
+          // Straight-line admission mask; the append runs only when it is set.
+          uint32_t adm = 0;
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-          adm_lo |= (uint32_t)(IP ? (s[j] >= thr) : (s[j] <= thr)) << j;
-          adm_hi |= (uint32_t)(IP ? (s[j + 32] >= thr) : (s[j + 32] <= thr)) << j;
-        }
-        if (collect && (adm_lo | adm_hi)) {
-          if (cnt + 64 > CAP) cnt = compact_list<IP>(row_list, cnt, thr);
-          const uint32_t base = (uint32_t)(col0 + g * 64);
+          for (int j = 0; j < 32; j++) adm |= (uint32_t)(IP ? (s[j] >= thr) : (s[j] <= thr)) << j;
+          if (collect && adm) {
+            if (cnt + 32 > CAP) cnt = compact_list<IP>(row_list, cnt, thr);
+            const uint32_t base = (uint32_t)(col0 + g * 32);
 #pragma unroll
-          for (int j = 0; j < 64; j++) {
-            const bool in = ((j < 32 ? adm_lo : adm_hi) >> (j & 31)) & 1u;
-            if (in) {
-              if (cnt < CAP) row_list[cnt] = make_uint2(base + j, __float_as_uint(s[j]));
-              overflow |= cnt >= CAP;
-              cnt += cnt < CAP;
+            for (int j = 0; j < 32; j++) {
+              if ((adm >> j) & 1u) {
+                if (cnt < CAP) row_list[cnt] = make_uint2(base + j, __float_as_uint(s[j]));
+                overflow |= cnt >= CAP;
+                cnt += cnt < CAP;
+              }
             }
           }
         }
+        tc_fence_before();
+        mbar_arrive(tempty);
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[a]);
+      if (live) {
+        const bool ok = collect && !overflow && isfinite(best) && !*abort_flag;
+        if (ok) P.cand_thr[i] = thr;
+        P.cand_cnt[i] = ok ? cnt : FALLBACK;
+      }
     }
-    if (live) {
-      const bool ok = collect && !overflow && isfinite(best) && !*abort_flag;
-      if (ok) P.cand_thr[i] = thr;
-      P.cand_cnt[i] = ok ? cnt : FALLBACK;
-    }
-    }  // row tiles
   }
 
   __syncthreads();
@@ -679,21 +674,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (threadIdx.x == 0 && *abort_flag) atomicOr(P.status, ST_WAIT_TIMEOUT);
 }
 
-// ---------------------------------------------------------------- exact re-score
-//
-// Stage 1 (k_refine, one warp per row): each admitted candidate gets a precise
-// FP32 dot with the lanes splitting d, plus the sum of |x_t c_t| that bounds
-// its error; only candidates that could still be the exact best survive.
-// Stage 2 (k_exact, one thread per row): the exact FMA chain of each survivor
-// (usually one) gives the label and the bit-exact score.
-
-constexpr int SURV = 8;  // survivors per row kept for the exact chains
-
-template <bool IP>
-__device__ __forceinline__ bool better(float v, uint32_t j, float bv, uint32_t bj) {
-  if (bj == FALLBACK) return true;
-  return IP ? (v > bv || (v == bv && j < bj)) : (v < bv || (v == bv && j < bj));
-}
+// ---------------------------------------------------------------- exact stage
 
 __device__ __forceinline__ void to_list(uint32_t p, uint32_t* list, uint32_t* list_count,
                                         unsigned long long* counters) {
@@ -701,178 +682,40 @@ __device__ __forceinline__ void to_list(uint32_t p, uint32_t* list, uint32_t* li
   atomicAdd(&counters[1], 1ull);
 }
 
+// Each row's candidates still inside its final window become (row, centroid)
+// pairs; rows with none, with more than SURV, or marked for the fallback go to
+// the exact kernel's list. The row's result key starts at the identity of its
+// reduction.
 template <bool IP>
-__global__ void __launch_bounds__(256) k_refine(
-    const float* __restrict__ x, int d, const uint32_t* __restrict__ ids, long p0, long m,
-    const float* __restrict__ c, const float* __restrict__ cn, const uint2* __restrict__ cand,
-    const uint32_t* __restrict__ cand_cnt, const float* __restrict__ cand_thr, float e2,
-    uint2* __restrict__ pairs, uint32_t* __restrict__ pair_count,
-    unsigned long long* __restrict__ rkey, uint32_t* __restrict__ list,
-    uint32_t* __restrict__ list_count, unsigned long long* __restrict__ counters) {
-  __shared__ float pv_s[8][CAP], pe_s[8][CAP];
-  __shared__ uint32_t pj_s[8][CAP];
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long i = (long)blockIdx.x * 8 + w;
+__global__ void k_collect(long p0, long m, const uint2* __restrict__ cand,
+                          const uint32_t* __restrict__ cand_cnt, const float* __restrict__ cand_thr,
+                          uint2* __restrict__ pairs, uint32_t* __restrict__ pair_count,
+                          unsigned long long* __restrict__ rkey, uint32_t* __restrict__ list,
+                          uint32_t* __restrict__ list_count,
+                          unsigned long long* __restrict__ counters) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= m) return;
+  rkey[i] = IP ? 0ull : ~0ull;
   const uint32_t cnt = cand_cnt[i];
-  if (cnt == FALLBACK) {
-    if (lane == 0) {
-      rkey[i] = IP ? 0ull : ~0ull;
-      to_list((uint32_t)(p0 + i), list, list_count, counters);
+  uint32_t ns = 0;
+  float thr = 0.0f;
+  if (cnt != FALLBACK) {
+    thr = cand_thr[i];
+    for (uint32_t e = 0; e < cnt; e++) {
+      const float sv = __uint_as_float(cand[i * (long)CAP + e].y);
+      ns += IP ? (sv >= thr) : (sv <= thr);
     }
+  }
+  if (cnt == FALLBACK || ns == 0 || ns > SURV) {
+    to_list((uint32_t)(p0 + i), list, list_count, counters);
     return;
   }
-  const float thr = cand_thr[i];
-  const long p = p0 + i;
-  const long row = ids ? (long)ids[p] : p;
-  const float* xr = x + row * (long)d;
-  float* pv = pv_s[w];
-  float* pe = pe_s[w];
-  uint32_t* pj = pj_s[w];
-  int np = 0;
-  // The row's x (a float4 per lane per 128 columns) stays in registers for
-  // every candidate when d % 4 == 0 and d <= 1024; otherwise it is re-read.
-  const bool vec = (d & 3) == 0 && d <= 1024;
-  const int q4 = d / 4;
-  float4 xv[8];
-#pragma unroll
-  for (int u = 0; u < 8; u++) {
-    const int t = lane + 32 * u;
-    xv[u] = (vec && t < q4) ? __ldg(reinterpret_cast<const float4*>(xr) + t)
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  uint32_t e = 0;
-  while (true) {
-    // The next two candidates still inside the final window (the rest were
-    // left behind by it), scored together so their loads overlap.
-    uint32_t jc[2] = {FALLBACK, FALLBACK};
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-      while (e < cnt) {
-        const uint2 en = cand[i * (long)CAP + e++];
-        const float sv = __uint_as_float(en.y);
-        if (IP ? sv >= thr : sv <= thr) {
-          jc[h] = en.x;
-          break;
-        }
-      }
-    }
-    if (jc[0] == FALLBACK) break;
-    float dot[2] = {0.0f, 0.0f}, ab[2] = {0.0f, 0.0f};
-    if (vec) {
-      const float4* c40 = reinterpret_cast<const float4*>(c + (long)jc[0] * d);
-      const float4* c41 = reinterpret_cast<const float4*>(
-          c + (long)(jc[1] == FALLBACK ? jc[0] : jc[1]) * d);
-      float4 ca[8], cb[8];
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const int t = lane + 32 * u;
-        ca[u] = t < q4 ? __ldg(c40 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
-        cb[u] = t < q4 ? __ldg(c41 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const float4 a = xv[u];
-        dot[0] = __fmaf_rn(a.x, ca[u].x, dot[0]);
-        dot[0] = __fmaf_rn(a.y, ca[u].y, dot[0]);
-        dot[0] = __fmaf_rn(a.z, ca[u].z, dot[0]);
-        dot[0] = __fmaf_rn(a.w, ca[u].w, dot[0]);
-        ab[0] = __fmaf_rn(fabsf(a.x), fabsf(ca[u].x), ab[0]);
-        ab[0] = __fmaf_rn(fabsf(a.y), fabsf(ca[u].y), ab[0]);
-        ab[0] = __fmaf_rn(fabsf(a.z), fabsf(ca[u].z), ab[0]);
-        ab[0] = __fmaf_rn(fabsf(a.w), fabsf(ca[u].w), ab[0]);
-        dot[1] = __fmaf_rn(a.x, cb[u].x, dot[1]);
-        dot[1] = __fmaf_rn(a.y, cb[u].y, dot[1]);
-        dot[1] = __fmaf_rn(a.z, cb[u].z, dot[1]);
-        dot[1] = __fmaf_rn(a.w, cb[u].w, dot[1]);
-        ab[1] = __fmaf_rn(fabsf(a.x), fabsf(cb[u].x), ab[1]);
-        ab[1] = __fmaf_rn(fabsf(a.y), fabsf(cb[u].y), ab[1]);
-        ab[1] = __fmaf_rn(fabsf(a.z), fabsf(cb[u].z), ab[1]);
-        ab[1] = __fmaf_rn(fabsf(a.w), fabsf(cb[u].w), ab[1]);
-      }
-    } else {
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        if (jc[h] == FALLBACK) continue;
-        const float* cr = c + (long)jc[h] * d;
-        for (int t = lane; t < d; t += 32) {
-          const float xa = __ldg(xr + t), ca = __ldg(cr + t);
-          dot[h] = __fmaf_rn(xa, ca, dot[h]);
-          ab[h] = __fmaf_rn(fabsf(xa), fabsf(ca), ab[h]);
-        }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-      dot[0] = __fadd_rn(dot[0], __shfl_xor_sync(0xFFFFFFFFu, dot[0], o));
-      ab[0] = __fadd_rn(ab[0], __shfl_xor_sync(0xFFFFFFFFu, ab[0], o));
-      dot[1] = __fadd_rn(dot[1], __shfl_xor_sync(0xFFFFFFFFu, dot[1], o));
-      ab[1] = __fadd_rn(ab[1], __shfl_xor_sync(0xFFFFFFFFu, ab[1], o));
-    }
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-      if (jc[h] == FALLBACK) break;
-      float v, err;
-      if (IP) {
-        v = dot[h];
-        err = __fmaf_ru(e2, ab[h], 1e-37f);
-      } else {
-        const float cj = __ldg(cn + jc[h]);
-        v = __fsub_rn(cj, __fmul_rn(2.0f, dot[h]));
-        // key error: twice the dot error plus the two key roundings.
-        err = __fmaf_ru(2.0f * e2, ab[h], __fmaf_ru(ldexpf(1.0f, -22), fabsf(v), 1e-37f));
-      }
-      if (lane == 0) {
-        pv[np] = v;
-        pe[np] = err;
-        pj[np] = jc[h];
-      }
-      np++;
-    }
-  }
-  __syncwarp();
-  // The best provable bound over the candidates, then every candidate that
-  // could still beat it.
-  float lim = IP ? -INFINITY : INFINITY;
-  for (int e = lane; e < np; e += 32)
-    lim = IP ? fmaxf(lim, __fsub_rd(pv[e], pe[e])) : fminf(lim, __fadd_ru(pv[e], pe[e]));
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    const float ol = __shfl_xor_sync(0xFFFFFFFFu, lim, o);
-    lim = IP ? fmaxf(lim, ol) : fminf(lim, ol);
-  }
-  int ns = 0;
-  for (int base = 0; base < np; base += 32) {
-    const int e = base + lane;
-    const bool keep = e < np && (IP ? __fadd_ru(pv[e], pe[e]) >= lim
-                                    : __fsub_rd(pv[e], pe[e]) <= lim);
-    ns += __popc(__ballot_sync(0xFFFFFFFFu, keep));
-  }
-  // Each survivor becomes a (row, centroid) pair for the exact stage; the
-  // row's result key starts at the identity of its reduction.
-  const bool ok = ns >= 1 && ns <= SURV;
-  uint32_t pbase = 0;
-  if (lane == 0) {
-    atomicAdd(&counters[2], (unsigned long long)np);
-    if (ok) {
-      pbase = atomicAdd(pair_count, (uint32_t)ns);
-      rkey[i] = IP ? 0ull : ~0ull;
-    } else {
-      rkey[i] = IP ? 0ull : ~0ull;
-      to_list((uint32_t)p, list, list_count, counters);
-    }
-  }
-  pbase = __shfl_sync(0xFFFFFFFFu, pbase, 0);
-  if (ok) {
-    int w = 0;
-    for (int base = 0; base < np; base += 32) {
-      const int e = base + lane;
-      const bool keep = e < np && (IP ? __fadd_ru(pv[e], pe[e]) >= lim
-                                      : __fsub_rd(pv[e], pe[e]) <= lim);
-      const uint32_t mask = __ballot_sync(0xFFFFFFFFu, keep);
-      if (keep) pairs[pbase + w + __popc(mask & ((1u << lane) - 1u))] = make_uint2((uint32_t)i, pj[e]);
-      w += __popc(mask);
-    }
+  atomicAdd(&counters[2], (unsigned long long)ns);
+  uint32_t w = atomicAdd(pair_count, ns);
+  for (uint32_t e = 0; e < cnt; e++) {
+    const uint2 en = cand[i * (long)CAP + e];
+    const float sv = __uint_as_float(en.y);
+    if (IP ? (sv >= thr) : (sv <= thr)) pairs[w++] = make_uint2((uint32_t)i, en.x);
   }
 }
 
@@ -914,13 +757,22 @@ __device__ __forceinline__ float chain(const float* __restrict__ x, const float*
   return acc;
 }
 
-// Exact chains over flattened (row, survivor) pairs, one thread per pair:
-// x and the survivor's centroid stream through shared memory in 32-column
-// slices (cp.async, 4 slices in flight), each 16-byte chunk q of pair slot t
-// stored at q ^ (t & 7) so that the per-thread LDS.128 reads are free of bank
-// conflicts. Each pair folds (value, id) into its row's 64-bit key with an
-// atomic max (IP) / min (L2): the key orders by value, then by the lower id,
-// which is the CPU's strict scan (-0.0 counts as +0.0, as it compares equal).
+// Key of (v, j): larger key = better for IP (max v, then min j); smaller key
+// = better for L2 (min v, then min j). -0.0 counts as +0.0: they compare
+// equal in the CPU's scan, so the lower id must decide.
+template <bool IP>
+__device__ __forceinline__ unsigned long long result_key(float v, uint32_t j) {
+  if (v == 0.0f) v = 0.0f;
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (IP ? (uint32_t)~j : j);
+}
+
+// Exact chains over the (row, centroid) pairs, one thread per pair: x and the
+// centroid stream through shared memory in 32-column slices (cp.async, 4
+// slices in flight), each 16-byte chunk q of pair slot t stored at
+// q ^ (t & 7) so that the per-thread LDS.128 reads are free of bank conflicts.
+// Each pair folds (value, id) into its row's key with an atomic max / min.
 constexpr int EX_ROWS = 128, EX_COLS = 32, EX_STAGES = 4;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -933,16 +785,6 @@ __device__ __forceinline__ void cp_async_commit() {
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// Key of (v, j): larger key = better for IP (max v, then min j); smaller key
-// = better for L2 (min v, then min j).
-template <bool IP>
-__device__ __forceinline__ unsigned long long result_key(float v, uint32_t j) {
-  if (v == 0.0f) v = 0.0f;  // -0.0 == +0.0 in the CPU's comparisons
-  const uint32_t u = __float_as_uint(v);
-  const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)ord << 32) | (IP ? (uint32_t)~j : j);
 }
 
 template <bool IP>
@@ -1022,7 +864,7 @@ __global__ void __launch_bounds__(EX_ROWS) k_pairs(
     if (mine) {
       const float v = IP ? acc : __fsub_rn(__ldg(cn + pr.y), __fmul_rn(2.0f, acc));
       if (!isfinite(v)) {
-        bad[pr.x] = 1;  // overflowing chains: the exact scan reproduces the CPU here
+        bad[pr.x] = 1;  // an overflowing chain: the exact scan reproduces the CPU here
       } else if (IP) {
         atomicMax(rkey + pr.x, result_key<IP>(v, pr.y));
       } else {
@@ -1081,11 +923,10 @@ __global__ void k_finish(const uint32_t* __restrict__ ids, long p0, long m,
   if (i >= m) return;
   const unsigned long long key = rkey[i];
   if (bad[i]) {
-    bad[i] = 0;
     to_list((uint32_t)(p0 + i), list, list_count, counters);
     return;
   }
-  if (key == (IP ? 0ull : ~0ull)) return;  // on the list already (or no pair)
+  if (key == (IP ? 0ull : ~0ull)) return;  // on the list already
   const uint32_t ord = (uint32_t)(key >> 32);
   const uint32_t u = (ord & 0x80000000u) ? (ord & 0x7FFFFFFFu) : ~ord;
   const float v = __uint_as_float(u);
@@ -1098,6 +939,7 @@ __global__ void k_finish(const uint32_t* __restrict__ ids, long p0, long m,
   labels[p0 + i] = j;
   scores[p0 + i] = score;
 }
+
 // ---------------------------------------------------------------- host side
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1113,23 +955,24 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// A 2-D FP16 tensor map over rows x dp (row stride dp*2 bytes) with a
-// box of `box_rows` x 64 columns and 128-byte swizzle.
+// A 2-D FP16 tensor map over rows x dp (row stride dp*2 bytes) with a box of
+// `box_rows` x 32 columns (64 bytes, 64-byte swizzle). The inner coordinate of
+// every load is a multiple of 32 elements (64 bytes).
 CUtensorMap make_map(const void* base, size_t rows, size_t dp, uint32_t box_rows) {
   CUtensorMap m;
-  cuuint64_t dims[2] = {(cuuint64_t)dp, (cuuint64_t)rows};
+  cuuint64_t dims[2] = {(cuuint64_t)dp, (cuuint64_t)std::max<size_t>(rows, 1)};
   cuuint64_t strides[1] = {(cuuint64_t)dp * 2};
   cuuint32_t box[2] = {(cuuint32_t)BKH, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw Error(EB_ERROR, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
   return m;
 }
 
-// The dynamic shared memory limit is a per-device, per-kernel attribute.
+// Dynamic shared memory limits are per-device, per-kernel attributes.
 template <bool IP>
 void set_smem(int device) {
   static uint64_t done = 0;  // one instance per kernel: IP is a template parameter
@@ -1141,13 +984,51 @@ void set_smem(int device) {
 }
 
 template <bool IP>
-void set_exact_smem(int device, size_t bytes) {
+void set_pairs_smem(int device, size_t bytes) {
   static uint64_t done = 0;
   if (!(done >> device & 1)) {
     EB_CUDA(cudaFuncSetAttribute(k_pairs<IP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)bytes));
     done |= 1ull << device;
   }
+}
+
+template <bool IP>
+void launch_screen(eb_engine* e, unsigned grid, const CUtensorMap& ah, const CUtensorMap& al,
+                   const CUtensorMap& bh, const CUtensorMap& bl, const ScreenParams& P) {
+  set_smem<IP>(e->device);
+  k_screen<IP><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(ah, al, bh, bl, P);
+}
+
+template <bool IP>
+void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const uint2* cand,
+                  const uint32_t* cand_cnt, const float* cand_thr, uint2* pairs,
+                  uint32_t* pair_count, unsigned long long* rkey, uint32_t* bad, float* xn_pos,
+                  uint32_t* list, uint32_t* list_count) {
+  unsigned long long* counters = e->counters();
+  EB_CUDA(cudaMemsetAsync(pair_count, 0, 4, e->stream));
+  EB_CUDA(cudaMemsetAsync(bad, 0, m * sizeof(uint32_t), e->stream));
+  const unsigned rgrid = (unsigned)((m + 255) / 256);
+  k_collect<IP><<<rgrid, 256, 0, e->stream>>>(c0, m, cand, cand_cnt, cand_thr, pairs, pair_count,
+                                              rkey, list, list_count, counters);
+  EB_LAUNCH("screen collect");
+  // The pair count is known on the device only: persistent blocks stride over it.
+  const unsigned pgrid = (unsigned)e->num_sms;
+  if (a.d % EX_COLS == 0) {
+    const size_t ex_smem = 2 * EX_STAGES * EX_ROWS * EX_COLS * sizeof(float);
+    set_pairs_smem<IP>(e->device, ex_smem);
+    k_pairs<IP><<<pgrid, EX_ROWS, ex_smem, e->stream>>>(a.x, (int)a.d, a.ids, c0, a.c, a.cnorm,
+                                                        a.xnorm, pairs, pair_count, rkey, xn_pos,
+                                                        bad);
+  } else {
+    k_pairs_plain<IP><<<pgrid * 4, 128, 0, e->stream>>>(a.x, (int)a.d, a.ids, c0, a.c, a.cnorm,
+                                                        a.xnorm, pairs, pair_count, rkey, xn_pos,
+                                                        bad);
+  }
+  EB_LAUNCH("screen exact chains");
+  k_finish<IP><<<rgrid, 256, 0, e->stream>>>(a.ids, c0, m, a.xnorm, xn_pos, rkey, bad, a.labels,
+                                             a.scores, list, list_count, counters);
+  EB_LAUNCH("screen finish");
 }
 
 }  // namespace
@@ -1164,61 +1045,56 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   const size_t dp = (d + BKH - 1) / BKH * BKH;
   const size_t m_all = a.r1 - a.r0;
   // Rows per pass: eight 128-row tiles per SM, so that each persistent CTA
-  // keeps its operand ring and TMEM buffers running across tiles.
+  // keeps its operand ring running across tiles.
   const size_t wave = (size_t)e->num_sms * BM;
   const size_t chunk = std::min(m_all, PASS_WAVES * wave);
   const bool ip = a.metric == EB_IP;
 
   // Bound coefficients for this d (see the header comment), with 1% slack.
   const double dd = (double)d;
-  const double gamma_d = dd * std::ldexp(1.0, -24) / (1.0 - dd * std::ldexp(1.0, -24));
-  const float e_rel = (float)((std::ldexp(1.0, -10) + std::ldexp(1.0, -22) +
-                               dd * std::ldexp(1.0, -21) * (1.0 + std::ldexp(1.0, -9)) + gamma_d) *
-                              1.01);
-  const float e_abs = (float)(std::ldexp(1.0, -24) * std::sqrt(dd) * 1.01);
-  const float e_min = (float)(dd * std::ldexp(1.0, -50));
+  const double u24 = std::ldexp(1.0, -24);
+  const double gamma_d = dd * u24 / (1.0 - dd * u24);
+  const float e_rel =
+      (float)((3.0 * std::ldexp(1.0, -22) + dd * std::ldexp(1.0, -21) * (1.0 + std::ldexp(1.0, -9)) +
+               dd * std::ldexp(1.0, -30) + std::ldexp(1.0, -23) + gamma_d) *
+              1.01);
+  const float e_abs = (float)(std::ldexp(1.0, -23) * std::sqrt(dd) * 1.01);
+  const float e_min = (float)(dd * std::ldexp(1.0, -48));
 
-  // Centroids: one exponent, FP16 copy.
+  // Centroids: one exponent, split FP16 copy.
   uint32_t* cinfo = e->scratch_get<uint32_t>("tc_cinfo", 4);
   __half* ch = e->scratch_get<__half>("tc_ch", k * dp);
+  __half* cl = e->scratch_get<__half>("tc_cl", k * dp);
   EB_CUDA(cudaMemsetAsync(cinfo, 0, 16, e->stream));
   const unsigned wpb = 8;
   k_cent_max<<<(unsigned)((k + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(a.c, (long)k, (int)d,
                                                                           cinfo);
   EB_LAUNCH("screen centroid max");
   k_cent_conv<<<(unsigned)((k + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(
-      a.c, (long)k, (int)d, (int)dp, cinfo, ch);
+      a.c, (long)k, (int)d, (int)dp, cinfo, ch, cl);
   EB_LAUNCH("screen centroid convert");
-  const CUtensorMap mapB = make_map(ch, k, dp, BN);
+  const CUtensorMap mapBh = make_map(ch, k, dp, BN);
+  const CUtensorMap mapBl = make_map(cl, k, dp, BN);
 
   __half* xh = e->scratch_get<__half>("tc_xh", chunk * dp);
+  __half* xl = e->scratch_get<__half>("tc_xl", chunk * dp);
   int* xexp = e->scratch_get<int>("tc_xexp", chunk);
   float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
   uint2* cand = e->scratch_get<uint2>("tc_cand", chunk * CAP);
   uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", chunk);
   float* cand_thr = e->scratch_get<float>("tc_thr", chunk);
+  uint32_t* list = e->scratch_get<uint32_t>("tc_list", chunk);
+  uint32_t* list_count = e->scratch_get<uint32_t>("tc_list_count", 4);
   uint2* pairs = e->scratch_get<uint2>("tc_pairs", chunk * SURV);
   uint32_t* pair_count = e->scratch_get<uint32_t>("tc_pair_count", 4);
   unsigned long long* rkey = e->scratch_get<unsigned long long>("tc_rkey", chunk);
   uint32_t* bad = e->scratch_get<uint32_t>("tc_bad", chunk);
   float* xn_pos = e->scratch_get<float>("tc_xn_pos", chunk);
-  // Precise-dot bound of the refine stage: each lane's FMA chain plus the
-  // 5-level shuffle tree is at most kp roundings, gamma_kp sum|x c|; the exact
-  // chain adds gamma_d sum|x c|; the computed sum|x c| is itself within gamma_kp.
-  const double kp = std::ceil(dd / 32.0) + 5.0;
-  const double gamma_kp = kp * std::ldexp(1.0, -24) / (1.0 - kp * std::ldexp(1.0, -24));
-  const float e2 = (float)((gamma_kp + gamma_d) * (1.0 + 4.0 * gamma_kp) * 1.01);
-  uint32_t* list = e->scratch_get<uint32_t>("tc_list", chunk);
-  uint32_t* list_count = e->scratch_get<uint32_t>("tc_list_count", 4);
-  unsigned long long* counters = e->counters();
 
   ScreenParams P;
   P.k = (int)k;
   P.kblocks = (int)(dp / BKH);
   P.ntiles = (int)((k + BN - 1) / BN);
-  P.d = (int)d;
-  P.xexp = xexp;
-  P.xnrm = xnrm;
   P.cn = a.cnorm;
   P.cinfo = cinfo;
   P.e_rel = e_rel;
@@ -1229,12 +1105,7 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   P.cand_thr = cand_thr;
   P.status = e->d_status;
 
-  if (ip)
-    set_smem<true>(e->device);
-  else
-    set_smem<false>(e->device);
-
-  // A bound data set keeps its FP16 screen copy across calls (training steps,
+  // A bound data set keeps its split copy across calls (training steps,
   // repeated assigns): converted once, then read in place or gathered by id.
   Fp16Copy* cache = nullptr;
   if (xbuf && xbuf->d == d && xbuf->len == a.n * d) {
@@ -1245,7 +1116,9 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
       f->d = d;
       f->version = xbuf->version;
       f->stream = e->stream;
-      cudaError_t st = cudaMallocAsync(&f->xh, std::max<size_t>(a.n * dp, 8) * 2, e->stream);
+      const size_t cells = std::max<size_t>(a.n * dp, 8);
+      cudaError_t st = cudaMallocAsync(&f->xh, cells * 2, e->stream);
+      if (st == cudaSuccess) st = cudaMallocAsync(&f->xl, cells * 2, e->stream);
       if (st == cudaSuccess) st = cudaMallocAsync(&f->xexp, std::max<size_t>(a.n, 1) * 4, e->stream);
       if (st == cudaSuccess) st = cudaMallocAsync(&f->xnrm, std::max<size_t>(a.n, 1) * 4, e->stream);
       xbuf->f16 = f;
@@ -1254,8 +1127,8 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
         cudaGetLastError();
       } else if (a.n) {
         k_prep_rows<<<(unsigned)((a.n + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(
-            a.x, (long)a.n, (int)d, (int)dp, nullptr, 0, (long)a.n, f->xh, f->xexp, f->xnrm,
-            e->d_status);
+            a.x, (long)a.n, (int)d, (int)dp, nullptr, 0, (long)a.n, f->xh, f->xl, f->xexp,
+            f->xnrm, e->d_status);
         EB_LAUNCH("screen copy of bound rows");
       }
     }
@@ -1264,84 +1137,45 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
 
   for (size_t c0 = a.r0; c0 < a.r1; c0 += chunk) {
     const size_t m = std::min(chunk, a.r1 - c0);
-    const __half* xa = xh;
+    const __half *ah = xh, *al = xl;
     if (cache && !a.ids) {
       // Dense rows of the bound set: the screen reads the cached copy in place.
-      xa = cache->xh + c0 * dp;
+      ah = cache->xh + c0 * dp;
+      al = cache->xl + c0 * dp;
       P.xexp = cache->xexp + c0;
       P.xnrm = cache->xnrm + c0;
     } else if (cache) {
       k_gather_rows<<<(unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(
-          cache->xh, cache->xexp, cache->xnrm, (long)a.n, (int)dp, a.ids, (long)c0, (long)m, xh,
-          xexp, xnrm, e->d_status);
+          cache->xh, cache->xl, cache->xexp, cache->xnrm, (long)a.n, (int)dp, a.ids, (long)c0,
+          (long)m, xh, xl, xexp, xnrm, e->d_status);
       EB_LAUNCH("screen row gather");
       P.xexp = xexp;
       P.xnrm = xnrm;
     } else {
       k_prep_rows<<<(unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(
-          a.x, (long)a.n, (int)d, (int)dp, a.ids, (long)c0, (long)m, xh, xexp, xnrm, e->d_status);
+          a.x, (long)a.n, (int)d, (int)dp, a.ids, (long)c0, (long)m, xh, xl, xexp, xnrm,
+          e->d_status);
       EB_LAUNCH("screen row prep");
       P.xexp = xexp;
       P.xnrm = xnrm;
     }
-    const CUtensorMap mapA = make_map(xa, m, dp, BM);
+    const CUtensorMap mapAh = make_map(ah, m, dp, BM);
+    const CUtensorMap mapAl = make_map(al, m, dp, BM);
     P.m = (long)m;
     // Persistent: at most one CTA per SM, each looping over row tiles.
     const unsigned grid = (unsigned)std::min<size_t>((m + BM - 1) / BM, (size_t)e->num_sms);
     if (ip)
-      k_screen<true><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(mapA, mapB, P);
+      launch_screen<true>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
     else
-      k_screen<false><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(mapA, mapB, P);
+      launch_screen<false>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
     EB_LAUNCH("screen");
     EB_CUDA(cudaMemsetAsync(list_count, 0, 4, e->stream));
-    EB_CUDA(cudaMemsetAsync(pair_count, 0, 4, e->stream));
-    EB_CUDA(cudaMemsetAsync(bad, 0, m * sizeof(uint32_t), e->stream));
-    const unsigned rgrid = (unsigned)((m + 7) / 8);  // 8 rows (warps) per block
     if (ip)
-      k_refine<true><<<rgrid, 256, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
-                                                   a.cnorm, cand, cand_cnt, cand_thr, e2, pairs,
-                                                   pair_count, rkey, list, list_count, counters);
+      launch_exact<true>(e, a, (long)c0, (long)m, cand, cand_cnt, cand_thr, pairs, pair_count,
+                         rkey, bad, xn_pos, list, list_count);
     else
-      k_refine<false><<<rgrid, 256, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, (long)m, a.c,
-                                                    a.cnorm, cand, cand_cnt, cand_thr, e2, pairs,
-                                                    pair_count, rkey, list, list_count, counters);
-    EB_LAUNCH("screen refine");
-    // The pair count is known on the device only: persistent blocks stride over it.
-    const unsigned pgrid = (unsigned)e->num_sms;
-    if (d % EX_COLS == 0) {
-      const size_t ex_smem = 2 * EX_STAGES * EX_ROWS * EX_COLS * sizeof(float);
-      if (ip) {
-        set_exact_smem<true>(e->device, ex_smem);
-        k_pairs<true><<<pgrid, EX_ROWS, ex_smem, e->stream>>>(a.x, (int)d, a.ids, (long)c0, a.c,
-                                                              a.cnorm, a.xnorm, pairs, pair_count,
-                                                              rkey, xn_pos, bad);
-      } else {
-        set_exact_smem<false>(e->device, ex_smem);
-        k_pairs<false><<<pgrid, EX_ROWS, ex_smem, e->stream>>>(a.x, (int)d, a.ids, (long)c0, a.c,
-                                                               a.cnorm, a.xnorm, pairs, pair_count,
-                                                               rkey, xn_pos, bad);
-      }
-    } else {
-      if (ip)
-        k_pairs_plain<true><<<pgrid * 4, 128, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, a.c,
-                                                              a.cnorm, a.xnorm, pairs, pair_count,
-                                                              rkey, xn_pos, bad);
-      else
-        k_pairs_plain<false><<<pgrid * 4, 128, 0, e->stream>>>(a.x, (int)d, a.ids, (long)c0, a.c,
-                                                               a.cnorm, a.xnorm, pairs,
-                                                               pair_count, rkey, xn_pos, bad);
-    }
-    EB_LAUNCH("screen exact chains");
-    const unsigned fgrid = (unsigned)((m + 255) / 256);
-    if (ip)
-      k_finish<true><<<fgrid, 256, 0, e->stream>>>(a.ids, (long)c0, (long)m, a.xnorm, xn_pos, rkey,
-                                                   bad, a.labels, a.scores, list, list_count,
-                                                   counters);
-    else
-      k_finish<false><<<fgrid, 256, 0, e->stream>>>(a.ids, (long)c0, (long)m, a.xnorm, xn_pos,
-                                                    rkey, bad, a.labels, a.scores, list,
-                                                    list_count, counters);
-    EB_LAUNCH("screen finish");
+      launch_exact<false>(e, a, (long)c0, (long)m, cand, cand_cnt, cand_thr, pairs, pair_count,
+                          rkey, bad, xn_pos, list, list_count);
     Top1Args fa = a;
     fa.r0 = c0;
     fa.r1 = c0 + m;
