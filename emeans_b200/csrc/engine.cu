@@ -119,6 +119,7 @@ void sync(eb_engine* e) {
     if (st & ST_BAD_LABEL) throw Error(EB_INVALID_ARGUMENT, "label out of range");
     if (st & ST_BAD_ROW) throw Error(EB_INVALID_ARGUMENT, "row id out of range");
     if (st & ST_WAIT_TIMEOUT) throw Error(EB_ERROR, "device-side wait timed out");
+    if (st & ST_BAD_STATE) throw Error(EB_INTERNAL, "device-side consistency check failed");
     throw Error(EB_INTERNAL, "device reported status " + std::to_string(st));
   }
 }

@@ -42,6 +42,7 @@ enum : uint32_t {
   ST_BAD_LABEL = 1u,
   ST_BAD_ROW = 2u,
   ST_WAIT_TIMEOUT = 4u,
+  ST_BAD_STATE = 8u,  // a kernel found an index its producer should never write
 };
 
 // A grow-only device scratch slot.
@@ -140,9 +141,6 @@ struct Top1Args {
 };
 // Full exact scan of every selected row.
 void top1_exact(eb_engine* e, const Top1Args& a);
-// Full exact scan of the positions listed in list[0..*count) (device count).
-void top1_exact_list(eb_engine* e, const Top1Args& a, const uint32_t* list,
-                     const uint32_t* count, size_t max_count);
 
 // Screen when the tensor-core path supports the call, else the exact kernel.
 void top1_dispatch(eb_engine* e, const Top1Args& a, eb_buf* xbuf);

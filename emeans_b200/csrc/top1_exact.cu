@@ -4,9 +4,9 @@
 // lower id on ties (assign.rs:423-443); L2 keys are cnorm - 2 dot with one
 // rounding and scores max(sum x^2 + key, 0) (assign.rs:497-502).
 //
-// This kernel serves small problems, the rows the tensor-core screen cannot
-// certify, and the checks of that screen. Tile: 64 rows x 64 centroids per
-// block of 256 threads (4x4 per thread), 16 columns of d per stage.
+// This kernel serves the calls the tensor-core screen does not take (small
+// problems, the exact mode). Tile: 64 rows x 64 centroids per block of 256
+// threads (4x4 per thread), 16 columns of d per stage.
 #include <cuda_runtime.h>
 
 #include "engine.h"
@@ -29,7 +29,6 @@ __device__ __forceinline__ bool better(float av, uint32_t aj, float bv, uint32_t
 template <bool IP>
 __global__ void __launch_bounds__(NT) k_top1_exact(
     const float* __restrict__ x, long n, int d, const uint32_t* __restrict__ ids, long r0, long r1,
-    const uint32_t* __restrict__ list, const uint32_t* __restrict__ list_count,
     const float* __restrict__ c, const float* __restrict__ cnorm, long k,
     const float* __restrict__ xnorm, int xnorm_by_row, uint32_t* __restrict__ labels,
     float* __restrict__ scores, uint32_t* status) {
@@ -40,37 +39,21 @@ __global__ void __launch_bounds__(NT) k_top1_exact(
 
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
-  const long total = list ? (long)*list_count : r1 - r0;
+  const long total = r1 - r0;
 
-  // Tiles of BM rows, grid-stride (the list length is only known on the device).
+  // Tiles of BM rows, grid-stride.
   for (long tile = blockIdx.x; tile * BM < total; tile += gridDim.x) {
-  long nrows;
-  if (list) {
-    long b0 = tile * BM;
-    nrows = min((long)BM, total - b0);
-    if (tid < BM) {
-      long p = tid < nrows ? (long)list[b0 + tid] : -1;
-      pos_of[tid] = p;
-      long row = p < 0 ? 0 : (ids ? (long)ids[p] : p);
-      if (row >= n) {
-        atomicOr(status, ST_BAD_ROW);
-        row = 0;
-      }
-      row_of[tid] = row;
+  const long b0 = r0 + tile * BM;
+  const long nrows = min((long)BM, r1 - b0);
+  if (tid < BM) {
+    long p = tid < nrows ? b0 + tid : -1;
+    pos_of[tid] = p;
+    long row = p < 0 ? 0 : (ids ? (long)ids[p] : p);
+    if (row >= n) {
+      atomicOr(status, ST_BAD_ROW);
+      row = 0;
     }
-  } else {
-    long b0 = r0 + tile * BM;
-    nrows = min((long)BM, r1 - b0);
-    if (tid < BM) {
-      long p = tid < nrows ? b0 + tid : -1;
-      pos_of[tid] = p;
-      long row = p < 0 ? 0 : (ids ? (long)ids[p] : p);
-      if (row >= n) {
-        atomicOr(status, ST_BAD_ROW);
-        row = 0;
-      }
-      row_of[tid] = row;
-    }
+    row_of[tid] = row;
   }
   __syncthreads();
 
@@ -207,51 +190,36 @@ __global__ void __launch_bounds__(NT) k_top1_exact(
   }
 }
 
-void launch(eb_engine* e, const Top1Args& a, const uint32_t* list, const uint32_t* count,
-            size_t rows_bound) {
-  if (rows_bound == 0) return;
+}  // namespace
+
+void top1_exact(eb_engine* e, const Top1Args& a) {
+  const size_t rows = a.r1 - a.r0;
+  if (rows == 0) return;
   const float* xn = nullptr;
   int by_row = 0;
   if (a.metric == EB_L2) {
     if (a.xnorm) {
       xn = a.xnorm;
       by_row = 1;
-    } else if (list) {
-      xn = nullptr;  // the kernel sums the listed rows' squares itself
     } else {
       float* t = e->scratch_get<float>("top1_xnorm", a.r1 - a.r0);
       sel_row_norms(e, a.x, a.n, a.d, a.ids, a.r0, a.r1, t);
       xn = t;
     }
   }
-  size_t tiles = (rows_bound + BM - 1) / BM;
-  // A list's length is known only on the device: a grid of a few blocks per SM
-  // strides over it, so an empty list costs one short launch.
-  if (list) tiles = std::min<size_t>(tiles, (size_t)e->num_sms * 4);
-  unsigned grid = (unsigned)tiles;
+  const unsigned grid = (unsigned)((rows + BM - 1) / BM);
   if (a.metric == EB_IP)
     k_top1_exact<true><<<grid, NT, 0, e->stream>>>(a.x, (long)a.n, (int)a.d, a.ids, (long)a.r0,
-                                                   (long)a.r1, list, count, a.c, a.cnorm,
+                                                   (long)a.r1, a.c, a.cnorm,
                                                    (long)a.k, xn, by_row, a.labels, a.scores,
                                                    e->d_status);
   else
     k_top1_exact<false><<<grid, NT, 0, e->stream>>>(a.x, (long)a.n, (int)a.d, a.ids, (long)a.r0,
-                                                    (long)a.r1, list, count, a.c, a.cnorm,
+                                                    (long)a.r1, a.c, a.cnorm,
                                                     (long)a.k, xn, by_row, a.labels, a.scores,
                                                     e->d_status);
   EB_LAUNCH("top1_exact");
-}
-
-}  // namespace
-
-void top1_exact(eb_engine* e, const Top1Args& a) {
-  launch(e, a, nullptr, nullptr, a.r1 - a.r0);
-  e->stats.exact_rows += a.r1 - a.r0;
-}
-
-void top1_exact_list(eb_engine* e, const Top1Args& a, const uint32_t* list,
-                     const uint32_t* count, size_t max_count) {
-  launch(e, a, list, count, max_count);
+  e->stats.exact_rows += rows;
 }
 
 }  // namespace eb

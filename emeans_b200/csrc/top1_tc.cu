@@ -23,8 +23,10 @@
 //    (row, centroid) pairs.
 // 4. pairs: one thread per pair runs the exact FMA chain (operands streamed
 //    through shared memory) and folds (score, id) into the row's 64-bit key.
-// 5. finish: labels and scores from the keys; rows with non-finite inputs or
-//    too many candidates take the exact SIMT kernel (top1_exact.cu).
+// 5. finish: labels and scores from the keys.
+// 6. list: rows with non-finite inputs, too many candidates, or a screen that
+//    gave up are scanned exactly against every centroid, parallel over
+//    (row, block of centroids) with the same keyed reduction.
 //
 // Error bound in accumulator units (operands scaled, u = 2^-11):
 //   split operands:   3 2^-22 sum|x'||c'| + 2^-23 (sum|x'| + sum|c'|)
@@ -554,9 +556,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float* cns = cn_s + q * BN;
     int tc = 0;
     bool stop = false;
-    for (long rt = blockIdx.x; rt * BM < P.m && !stop; rt += gridDim.x) {
+    for (long rt = blockIdx.x; rt * BM < P.m; rt += gridDim.x) {
       const long i = rt * BM + r;
       const bool live = i < P.m;
+      if (stop) {
+        // A wait gave up: this CTA's remaining rows go to the exact fallback.
+        if (live) P.cand_cnt[i] = FALLBACK;
+        continue;
+      }
       const int ex = live ? P.xexp[i] : XEXP_BAD;
       bool fallback = !live || ex == XEXP_BAD || c_bad;
       const float xn = live ? P.xnrm[i] : 0.0f;
@@ -658,7 +665,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_arrive(tempty);
       }
       if (live) {
-        const bool ok = collect && !overflow && isfinite(best) && !*abort_flag;
+        const bool ok = collect && !stop && !overflow && isfinite(best) && !*abort_flag;
         if (ok) P.cand_thr[i] = thr;
         P.cand_cnt[i] = ok ? cnt : FALLBACK;
       }
@@ -676,46 +683,97 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
 // ---------------------------------------------------------------- exact stage
 
-__device__ __forceinline__ void to_list(uint32_t p, uint32_t* list, uint32_t* list_count,
-                                        unsigned long long* counters) {
-  list[atomicAdd(list_count, 1u)] = p;
-  atomicAdd(&counters[1], 1ull);
+// Warp-aggregated append: every lane of a full warp calls this with its own
+// count n (possibly 0); one atomic per warp reserves the slots, and each lane
+// gets the first of its own.
+__device__ __forceinline__ uint32_t warp_append(uint32_t* counter, uint32_t n) {
+  const int lane = threadIdx.x & 31;
+  uint32_t incl = n;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  uint32_t base = 0;
+  if (lane == 31 && incl) base = atomicAdd(counter, incl);
+  return __shfl_sync(0xFFFFFFFFu, base, 31) + incl - n;
+}
+
+// Key of (v, j): larger key = better for IP (max v, then min j); smaller key
+// = better for L2 (min v, then min j). -0.0 counts as +0.0: they compare
+// equal in the CPU's scan, so the lower id must decide.
+template <bool IP>
+__device__ __forceinline__ unsigned long long result_key(float v, uint32_t j) {
+  if (v == 0.0f) v = 0.0f;
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (IP ? (uint32_t)~j : j);
+}
+
+// The key of the CPU scan's starting point (-inf / +inf with id 0): only a
+// strictly better value replaces it, exactly as in the sequential scan.
+template <bool IP>
+__device__ __forceinline__ unsigned long long scan_start_key() {
+  return result_key<IP>(IP ? -INFINITY : INFINITY, 0u);
 }
 
 // Each row's candidates still inside its final window become (row, centroid)
 // pairs; rows with none, with more than SURV, or marked for the fallback go to
-// the exact kernel's list. The row's result key starts at the identity of its
-// reduction.
+// the exact list, whose key starts at the scan's starting point. The row's
+// pair key starts at the identity of its reduction. Launched with whole warps.
 template <bool IP>
-__global__ void k_collect(long p0, long m, const uint2* __restrict__ cand,
-                          const uint32_t* __restrict__ cand_cnt, const float* __restrict__ cand_thr,
-                          uint2* __restrict__ pairs, uint32_t* __restrict__ pair_count,
-                          unsigned long long* __restrict__ rkey, uint32_t* __restrict__ list,
-                          uint32_t* __restrict__ list_count,
-                          unsigned long long* __restrict__ counters) {
+__global__ void __launch_bounds__(256) k_collect(
+    long p0, long m, uint32_t k, const uint2* __restrict__ cand,
+    const uint32_t* __restrict__ cand_cnt, const float* __restrict__ cand_thr,
+    uint2* __restrict__ pairs, uint32_t* __restrict__ pair_count,
+    unsigned long long* __restrict__ rkey, uint32_t* __restrict__ list,
+    uint32_t* __restrict__ list_count, unsigned long long* __restrict__ lkey,
+    unsigned long long* __restrict__ counters, uint32_t* __restrict__ status) {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= m) return;
-  rkey[i] = IP ? 0ull : ~0ull;
-  const uint32_t cnt = cand_cnt[i];
+  const bool live = i < m;
+  const uint32_t cnt = live ? cand_cnt[i] : FALLBACK;
+  bool fb = cnt == FALLBACK;
+  if (!fb && cnt > CAP) {
+    atomicOr(status, ST_BAD_STATE);
+    fb = true;
+  }
   uint32_t ns = 0;
   float thr = 0.0f;
-  if (cnt != FALLBACK) {
+  if (!fb) {
     thr = cand_thr[i];
     for (uint32_t e = 0; e < cnt; e++) {
-      const float sv = __uint_as_float(cand[i * (long)CAP + e].y);
+      const uint2 en = cand[i * (long)CAP + e];
+      const float sv = __uint_as_float(en.y);
+      if (en.x >= k) {
+        atomicOr(status, ST_BAD_STATE);
+        fb = true;
+        break;
+      }
       ns += IP ? (sv >= thr) : (sv <= thr);
     }
   }
-  if (cnt == FALLBACK || ns == 0 || ns > SURV) {
-    to_list((uint32_t)(p0 + i), list, list_count, counters);
-    return;
+  fb = fb || ns == 0 || ns > SURV;
+  const bool listed = live && fb;
+  const uint32_t np = live && !fb ? ns : 0;
+  if (live) rkey[i] = IP ? 0ull : ~0ull;
+  const uint32_t lp = warp_append(list_count, listed ? 1u : 0u);
+  if (listed) {
+    list[lp] = (uint32_t)(p0 + i);
+    lkey[lp] = scan_start_key<IP>();
   }
-  atomicAdd(&counters[2], (unsigned long long)ns);
-  uint32_t w = atomicAdd(pair_count, ns);
-  for (uint32_t e = 0; e < cnt; e++) {
-    const uint2 en = cand[i * (long)CAP + e];
-    const float sv = __uint_as_float(en.y);
-    if (IP ? (sv >= thr) : (sv <= thr)) pairs[w++] = make_uint2((uint32_t)i, en.x);
+  uint32_t w = warp_append(pair_count, np);
+  if (np) {
+    for (uint32_t e = 0; e < cnt; e++) {
+      const uint2 en = cand[i * (long)CAP + e];
+      const float sv = __uint_as_float(en.y);
+      if (IP ? (sv >= thr) : (sv <= thr)) pairs[w++] = make_uint2((uint32_t)i, en.x);
+    }
+  }
+  const uint32_t nl = __reduce_add_sync(0xFFFFFFFFu, listed ? 1u : 0u);
+  const uint32_t nps = __reduce_add_sync(0xFFFFFFFFu, np);
+  if ((threadIdx.x & 31) == 0) {
+    if (nl) atomicAdd(&counters[1], (unsigned long long)nl);
+    if (nps) atomicAdd(&counters[2], (unsigned long long)nps);
   }
 }
 
@@ -757,17 +815,6 @@ __device__ __forceinline__ float chain(const float* __restrict__ x, const float*
   return acc;
 }
 
-// Key of (v, j): larger key = better for IP (max v, then min j); smaller key
-// = better for L2 (min v, then min j). -0.0 counts as +0.0: they compare
-// equal in the CPU's scan, so the lower id must decide.
-template <bool IP>
-__device__ __forceinline__ unsigned long long result_key(float v, uint32_t j) {
-  if (v == 0.0f) v = 0.0f;
-  const uint32_t u = __float_as_uint(v);
-  const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)ord << 32) | (IP ? (uint32_t)~j : j);
-}
-
 // Exact chains over the (row, centroid) pairs, one thread per pair: x and the
 // centroid stream through shared memory in 32-column slices (cp.async, 4
 // slices in flight), each 16-byte chunk q of pair slot t stored at
@@ -791,9 +838,9 @@ template <bool IP>
 __global__ void __launch_bounds__(EX_ROWS) k_pairs(
     const float* __restrict__ x, int d, const uint32_t* __restrict__ ids, long p0,
     const float* __restrict__ c, const float* __restrict__ cn, const float* __restrict__ xnorm_row,
-    const uint2* __restrict__ pairs, const uint32_t* __restrict__ pair_count,
+    const uint2* __restrict__ pairs, const uint32_t* __restrict__ pair_count, long m, uint32_t k,
     unsigned long long* __restrict__ rkey, float* __restrict__ xn_pos,
-    uint32_t* __restrict__ bad) {
+    uint32_t* __restrict__ bad, uint32_t* __restrict__ status) {
   extern __shared__ __align__(16) float ex_smem[];
   constexpr int SLICE = EX_STAGES * EX_ROWS * EX_COLS;
   float* xs = ex_smem;          // [stage][pair][32]
@@ -806,11 +853,16 @@ __global__ void __launch_bounds__(EX_ROWS) k_pairs(
   const bool want_xn = !IP && !xnorm_row;
   for (long tile = blockIdx.x; tile * EX_ROWS < np; tile += gridDim.x) {
     const long pi = tile * EX_ROWS + t;
-    const bool mine = pi < np;
+    bool mine = pi < np;
     uint2 pr = make_uint2(0, 0);
     long row = 0;
     if (mine) {
       pr = pairs[pi];
+      if (pr.x >= m || pr.y >= k) {
+        atomicOr(status, ST_BAD_STATE);
+        pr = make_uint2(0, 0);
+        mine = false;
+      }
       row = ids ? (long)ids[p0 + pr.x] : p0 + pr.x;
     }
     // Slots past the pair count read row 0 / centroid 0 harmlessly and write nothing.
@@ -881,13 +933,17 @@ template <bool IP>
 __global__ void k_pairs_plain(const float* __restrict__ x, int d, const uint32_t* __restrict__ ids,
                               long p0, const float* __restrict__ c, const float* __restrict__ cn,
                               const float* __restrict__ xnorm_row, const uint2* __restrict__ pairs,
-                              const uint32_t* __restrict__ pair_count,
+                              const uint32_t* __restrict__ pair_count, long m, uint32_t k,
                               unsigned long long* __restrict__ rkey, float* __restrict__ xn_pos,
-                              uint32_t* __restrict__ bad) {
+                              uint32_t* __restrict__ bad, uint32_t* __restrict__ status) {
   const long np = (long)*pair_count;
   for (long pi = (long)blockIdx.x * blockDim.x + threadIdx.x; pi < np;
        pi += (long)gridDim.x * blockDim.x) {
     const uint2 pr = pairs[pi];
+    if (pr.x >= m || pr.y >= k) {
+      atomicOr(status, ST_BAD_STATE);
+      continue;
+    }
     const long row = ids ? (long)ids[p0 + pr.x] : p0 + pr.x;
     const float* xr = x + row * (long)d;
     const float acc = chain(xr, c + (long)pr.y * d, d);
@@ -910,27 +966,40 @@ __global__ void k_pairs_plain(const float* __restrict__ x, int d, const uint32_t
   }
 }
 
-// Labels and scores from the rows' keys; rows whose chains overflowed join
-// the exact kernel's list.
+// Decode a result key back to (value, id).
 template <bool IP>
-__global__ void k_finish(const uint32_t* __restrict__ ids, long p0, long m,
-                         const float* __restrict__ xnorm_row, const float* __restrict__ xn_pos,
-                         const unsigned long long* __restrict__ rkey, uint32_t* __restrict__ bad,
-                         uint32_t* __restrict__ labels, float* __restrict__ scores,
-                         uint32_t* __restrict__ list, uint32_t* __restrict__ list_count,
-                         unsigned long long* __restrict__ counters) {
-  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= m) return;
-  const unsigned long long key = rkey[i];
-  if (bad[i]) {
-    to_list((uint32_t)(p0 + i), list, list_count, counters);
-    return;
-  }
-  if (key == (IP ? 0ull : ~0ull)) return;  // on the list already
+__device__ __forceinline__ float key_value(unsigned long long key, uint32_t& j) {
   const uint32_t ord = (uint32_t)(key >> 32);
   const uint32_t u = (ord & 0x80000000u) ? (ord & 0x7FFFFFFFu) : ~ord;
-  const float v = __uint_as_float(u);
-  const uint32_t j = IP ? ~(uint32_t)key : (uint32_t)key;
+  j = IP ? ~(uint32_t)key : (uint32_t)key;
+  return __uint_as_float(u);
+}
+
+// Labels and scores from the rows' keys; rows whose chains overflowed join
+// the exact list. Launched with whole warps.
+template <bool IP>
+__global__ void __launch_bounds__(256) k_finish(
+    const uint32_t* __restrict__ ids, long p0, long m, const float* __restrict__ xnorm_row,
+    const float* __restrict__ xn_pos, const unsigned long long* __restrict__ rkey,
+    const uint32_t* __restrict__ bad, uint32_t* __restrict__ labels, float* __restrict__ scores,
+    uint32_t* __restrict__ list, uint32_t* __restrict__ list_count,
+    unsigned long long* __restrict__ lkey, unsigned long long* __restrict__ counters) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool live = i < m;
+  const bool listed = live && bad[i];
+  const uint32_t lp = warp_append(list_count, listed ? 1u : 0u);
+  const uint32_t nl = __reduce_add_sync(0xFFFFFFFFu, listed ? 1u : 0u);
+  if ((threadIdx.x & 31) == 0 && nl) atomicAdd(&counters[1], (unsigned long long)nl);
+  if (listed) {
+    list[lp] = (uint32_t)(p0 + i);
+    lkey[lp] = scan_start_key<IP>();
+    return;
+  }
+  if (!live) return;
+  const unsigned long long key = rkey[i];
+  if (key == (IP ? 0ull : ~0ull)) return;  // on the list already
+  uint32_t j;
+  const float v = key_value<IP>(key, j);
   float score = v;
   if (!IP) {
     const long row = ids ? (long)ids[p0 + i] : p0 + i;
@@ -938,6 +1007,170 @@ __global__ void k_finish(const uint32_t* __restrict__ ids, long p0, long m,
   }
   labels[p0 + i] = j;
   scores[p0 + i] = score;
+}
+
+// The exact list: rows the screen could not certify, scanned against every
+// centroid. Work items are (listed row, block of LS_C centroids), one thread
+// per centroid: the row's 32-column slice and the centroids' slices stream
+// through shared memory (cp.async, LS_STAGES slices in flight; the same XOR
+// layout as the pair kernel), each thread runs its centroid's FMA chain over
+// all d columns, and the block folds its best (value, id) into the row's key.
+// Keys start at the scan's starting point and skip NaN values, so the atomic
+// reduction reproduces the sequential strict scan with its lower-id rule.
+constexpr int LS_C = 128, LS_STAGES = 4;
+constexpr size_t LS_SMEM = (size_t)LS_STAGES * (LS_C + 1) * EX_COLS * sizeof(float);
+
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+
+template <bool IP>
+__global__ void __launch_bounds__(LS_C) k_list(
+    const float* __restrict__ x, long n, int d, const uint32_t* __restrict__ ids,
+    const float* __restrict__ c, const float* __restrict__ cn, long k,
+    const uint32_t* __restrict__ list, const uint32_t* __restrict__ list_count,
+    unsigned long long* __restrict__ lkey, uint32_t* __restrict__ status) {
+  extern __shared__ __align__(16) float ls_smem[];
+  float* cs = ls_smem;                                 // [stage][LS_C][32]
+  float* xs = ls_smem + LS_STAGES * LS_C * EX_COLS;    // [stage][32]
+  __shared__ unsigned long long red[LS_C / 32];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const long kch = (k + LS_C - 1) / LS_C;
+  const long total = (long)*list_count * kch;
+  const int nsl = (d + EX_COLS - 1) / EX_COLS;
+  const bool v16 = (d & 3) == 0;  // rows start on 16-byte boundaries
+  for (long w = blockIdx.x; w < total; w += gridDim.x) {
+    const long ent = w / kch;
+    const long j0 = (w - ent * kch) * LS_C;
+    long row = list[ent];
+    if (ids) row = ids[row];
+    if (row >= n) {
+      atomicOr(status, ST_BAD_ROW);
+      row = 0;
+    }
+    const float* xr = x + row * (long)d;
+    auto issue = [&](int sl) {
+      if (sl < nsl) {
+        const int st = sl % LS_STAGES;
+        const int g0 = sl * EX_COLS;
+        float* cst = cs + st * LS_C * EX_COLS;
+        if (v16) {
+#pragma unroll
+          for (int u = 0; u < 8; u++) {
+            const int idx = u * LS_C + t;  // 0 .. 1023
+            const int r = idx >> 3, q = idx & 7;
+            const int g = g0 + q * 4;
+            if (j0 + r < k && g < d)
+              cp_async16(cst + r * EX_COLS + (q ^ (r & 7)) * 4, c + (j0 + r) * (long)d + g);
+          }
+          if (t < 8 && g0 + t * 4 < d) cp_async16(xs + st * EX_COLS + t * 4, xr + g0 + t * 4);
+        } else {
+#pragma unroll 4
+          for (int u = 0; u < 32; u++) {
+            const int idx = u * LS_C + t;  // 0 .. 4095
+            const int r = idx >> 5, cc = idx & 31;
+            const int g = g0 + cc;
+            if (j0 + r < k && g < d)
+              cp_async4(cst + r * EX_COLS + (((cc >> 2) ^ (r & 7)) << 2) + (cc & 3),
+                        c + (j0 + r) * (long)d + g);
+          }
+          if (t < 32 && g0 + t < d) cp_async4(xs + st * EX_COLS + t, xr + g0 + t);
+        }
+      }
+      cp_async_commit();
+    };
+#pragma unroll
+    for (int s = 0; s < LS_STAGES - 1; s++) issue(s);
+    float acc = 0.0f;
+    for (int sl = 0; sl < nsl; sl++) {
+      issue(sl + LS_STAGES - 1);
+      cp_async_wait<LS_STAGES - 1>();
+      __syncthreads();
+      const int st = sl % LS_STAGES;
+      const float* crow = cs + (st * LS_C + t) * EX_COLS;
+      const float* xsl = xs + st * EX_COLS;
+      const int kmax = min(EX_COLS, d - sl * EX_COLS);
+      if (kmax == EX_COLS) {
+        const float4* x4 = reinterpret_cast<const float4*>(xsl);
+        const float4* c4 = reinterpret_cast<const float4*>(crow);
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          const float4 a = x4[q], b = c4[q ^ (t & 7)];
+          acc = __fmaf_rn(a.x, b.x, acc);
+          acc = __fmaf_rn(a.y, b.y, acc);
+          acc = __fmaf_rn(a.z, b.z, acc);
+          acc = __fmaf_rn(a.w, b.w, acc);
+        }
+      } else {
+        for (int cc = 0; cc < kmax; cc++)
+          acc = __fmaf_rn(xsl[cc], crow[(((cc >> 2) ^ (t & 7)) << 2) + (cc & 3)], acc);
+      }
+      __syncthreads();  // the slot is refilled next iteration
+    }
+    cp_async_wait<0>();
+    const long j = j0 + t;
+    unsigned long long key = scan_start_key<IP>();
+    if (j < k) {
+      const float v = IP ? acc : __fsub_rn(__ldg(cn + j), __fmul_rn(2.0f, acc));
+      if (!isnan(v)) key = result_key<IP>(v, (uint32_t)j);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, key, o);
+      key = IP ? max(key, other) : min(key, other);
+    }
+    if (lane == 0) red[warp] = key;
+    __syncthreads();
+    if (t == 0) {
+#pragma unroll
+      for (int u = 1; u < LS_C / 32; u++) key = IP ? max(key, red[u]) : min(key, red[u]);
+      if (key != scan_start_key<IP>()) {
+        if (IP)
+          atomicMax(lkey + ent, key);
+        else
+          atomicMin(lkey + ent, key);
+      }
+    }
+  }
+}
+
+// Labels and scores of the listed rows from their keys.
+template <bool IP>
+__global__ void k_list_finish(const float* __restrict__ x, long n, int d,
+                              const uint32_t* __restrict__ ids,
+                              const uint32_t* __restrict__ list,
+                              const uint32_t* __restrict__ list_count,
+                              const unsigned long long* __restrict__ lkey,
+                              const float* __restrict__ xnorm_row, uint32_t* __restrict__ labels,
+                              float* __restrict__ scores) {
+  const long cnt = (long)*list_count;
+  for (long ent = (long)blockIdx.x * blockDim.x + threadIdx.x; ent < cnt;
+       ent += (long)gridDim.x * blockDim.x) {
+    const long p = list[ent];
+    uint32_t j;
+    const float v = key_value<IP>(lkey[ent], j);
+    float score = v;
+    if (!IP) {
+      long row = ids ? (long)ids[p] : p;
+      if (row >= n) row = 0;  // reported by the scan kernel
+      float xn;
+      if (xnorm_row) {
+        xn = xnorm_row[row];
+      } else {
+        // Sequential sum of squares in the CPU order, for this row only.
+        const float* xr = x + row * (long)d;
+        xn = -0.0f;
+        for (int u = 0; u < d; u++) {
+          const float a = __ldg(xr + u);
+          xn = __fadd_rn(xn, __fmul_rn(a, a));
+        }
+      }
+      score = fmaxf(__fadd_rn(xn, v), 0.0f);
+    }
+    labels[p] = j;
+    scores[p] = score;
+  }
 }
 
 // ---------------------------------------------------------------- host side
@@ -994,41 +1227,79 @@ void set_pairs_smem(int device, size_t bytes) {
 }
 
 template <bool IP>
+void set_list_smem(int device) {
+  static uint64_t done = 0;
+  if (!(done >> device & 1)) {
+    EB_CUDA(cudaFuncSetAttribute(k_list<IP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)LS_SMEM));
+    done |= 1ull << device;
+  }
+}
+
+template <bool IP>
 void launch_screen(eb_engine* e, unsigned grid, const CUtensorMap& ah, const CUtensorMap& al,
                    const CUtensorMap& bh, const CUtensorMap& bl, const ScreenParams& P) {
   set_smem<IP>(e->device);
   k_screen<IP><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(ah, al, bh, bl, P);
 }
 
+// Scratch of the exact stage of one pass of m rows.
+struct ExactScratch {
+  const uint2* cand;
+  const uint32_t* cand_cnt;
+  const float* cand_thr;
+  uint2* pairs;
+  uint32_t* pair_count;
+  unsigned long long* rkey;
+  uint32_t* bad;
+  float* xn_pos;
+  uint32_t* list;
+  uint32_t* list_count;
+  unsigned long long* lkey;
+};
+
 template <bool IP>
-void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const uint2* cand,
-                  const uint32_t* cand_cnt, const float* cand_thr, uint2* pairs,
-                  uint32_t* pair_count, unsigned long long* rkey, uint32_t* bad, float* xn_pos,
-                  uint32_t* list, uint32_t* list_count) {
+void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const ExactScratch& S) {
   unsigned long long* counters = e->counters();
-  EB_CUDA(cudaMemsetAsync(pair_count, 0, 4, e->stream));
-  EB_CUDA(cudaMemsetAsync(bad, 0, m * sizeof(uint32_t), e->stream));
+  EB_CUDA(cudaMemsetAsync(S.pair_count, 0, 4, e->stream));
+  EB_CUDA(cudaMemsetAsync(S.list_count, 0, 4, e->stream));
+  EB_CUDA(cudaMemsetAsync(S.bad, 0, m * sizeof(uint32_t), e->stream));
   const unsigned rgrid = (unsigned)((m + 255) / 256);
-  k_collect<IP><<<rgrid, 256, 0, e->stream>>>(c0, m, cand, cand_cnt, cand_thr, pairs, pair_count,
-                                              rkey, list, list_count, counters);
+  k_collect<IP><<<rgrid, 256, 0, e->stream>>>(c0, m, (uint32_t)a.k, S.cand, S.cand_cnt, S.cand_thr,
+                                              S.pairs, S.pair_count, S.rkey, S.list, S.list_count,
+                                              S.lkey, counters, e->d_status);
   EB_LAUNCH("screen collect");
   // The pair count is known on the device only: persistent blocks stride over it.
   const unsigned pgrid = (unsigned)e->num_sms;
   if (a.d % EX_COLS == 0) {
     const size_t ex_smem = 2 * EX_STAGES * EX_ROWS * EX_COLS * sizeof(float);
     set_pairs_smem<IP>(e->device, ex_smem);
-    k_pairs<IP><<<pgrid, EX_ROWS, ex_smem, e->stream>>>(a.x, (int)a.d, a.ids, c0, a.c, a.cnorm,
-                                                        a.xnorm, pairs, pair_count, rkey, xn_pos,
-                                                        bad);
+    k_pairs<IP><<<pgrid, EX_ROWS, ex_smem, e->stream>>>(
+        a.x, (int)a.d, a.ids, c0, a.c, a.cnorm, a.xnorm, S.pairs, S.pair_count, m,
+        (uint32_t)a.k, S.rkey, S.xn_pos, S.bad, e->d_status);
   } else {
-    k_pairs_plain<IP><<<pgrid * 4, 128, 0, e->stream>>>(a.x, (int)a.d, a.ids, c0, a.c, a.cnorm,
-                                                        a.xnorm, pairs, pair_count, rkey, xn_pos,
-                                                        bad);
+    k_pairs_plain<IP><<<pgrid * 4, 128, 0, e->stream>>>(
+        a.x, (int)a.d, a.ids, c0, a.c, a.cnorm, a.xnorm, S.pairs, S.pair_count, m,
+        (uint32_t)a.k, S.rkey, S.xn_pos, S.bad, e->d_status);
   }
   EB_LAUNCH("screen exact chains");
-  k_finish<IP><<<rgrid, 256, 0, e->stream>>>(a.ids, c0, m, a.xnorm, xn_pos, rkey, bad, a.labels,
-                                             a.scores, list, list_count, counters);
+  k_finish<IP><<<rgrid, 256, 0, e->stream>>>(a.ids, c0, m, a.xnorm, S.xn_pos, S.rkey, S.bad,
+                                             a.labels, a.scores, S.list, S.list_count, S.lkey,
+                                             counters);
   EB_LAUNCH("screen finish");
+  // The list's length is known on the device only: a grid of a few blocks per
+  // SM strides over its (row, centroid block) items; an empty list costs two
+  // short launches.
+  const long kch = ((long)a.k + LS_C - 1) / LS_C;
+  const unsigned lgrid = (unsigned)std::min<long>(m * kch, (long)e->num_sms * 3);
+  set_list_smem<IP>(e->device);
+  k_list<IP><<<lgrid, LS_C, LS_SMEM, e->stream>>>(a.x, (long)a.n, (int)a.d, a.ids, a.c, a.cnorm,
+                                                 (long)a.k, S.list, S.list_count, S.lkey,
+                                                 e->d_status);
+  EB_LAUNCH("screen exact list");
+  k_list_finish<IP><<<(unsigned)std::min<long>((m + 255) / 256, e->num_sms), 256, 0, e->stream>>>(
+      a.x, (long)a.n, (int)a.d, a.ids, S.list, S.list_count, S.lkey, a.xnorm, a.labels, a.scores);
+  EB_LAUNCH("screen exact list finish");
 }
 
 }  // namespace
@@ -1090,6 +1361,9 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   unsigned long long* rkey = e->scratch_get<unsigned long long>("tc_rkey", chunk);
   uint32_t* bad = e->scratch_get<uint32_t>("tc_bad", chunk);
   float* xn_pos = e->scratch_get<float>("tc_xn_pos", chunk);
+  unsigned long long* lkey = e->scratch_get<unsigned long long>("tc_lkey", chunk);
+  const ExactScratch S{cand, cand_cnt, cand_thr, pairs, pair_count, rkey, bad, xn_pos, list,
+                       list_count, lkey};
 
   ScreenParams P;
   P.k = (int)k;
@@ -1169,17 +1443,10 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
     else
       launch_screen<false>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
     EB_LAUNCH("screen");
-    EB_CUDA(cudaMemsetAsync(list_count, 0, 4, e->stream));
     if (ip)
-      launch_exact<true>(e, a, (long)c0, (long)m, cand, cand_cnt, cand_thr, pairs, pair_count,
-                         rkey, bad, xn_pos, list, list_count);
+      launch_exact<true>(e, a, (long)c0, (long)m, S);
     else
-      launch_exact<false>(e, a, (long)c0, (long)m, cand, cand_cnt, cand_thr, pairs, pair_count,
-                          rkey, bad, xn_pos, list, list_count);
-    Top1Args fa = a;
-    fa.r0 = c0;
-    fa.r1 = c0 + m;
-    top1_exact_list(e, fa, list, list_count, m);
+      launch_exact<false>(e, a, (long)c0, (long)m, S);
   }
   e->stats.screened_rows += m_all;
 }
