@@ -213,12 +213,12 @@ __device__ __forceinline__ void tmem_wait() {
 // Keep only the entries of a row's candidate list still inside the window
 // (out of line: it runs only when a list nears its capacity).
 template <bool IP>
-__device__ __noinline__ uint32_t compact_list(uint2* list, uint32_t cnt, float thr) {
+__device__ __noinline__ uint32_t compact_list(uint2* list, long stride, uint32_t cnt, float thr) {
   uint32_t w = 0;
   for (uint32_t e = 0; e < cnt; e++) {
-    const uint2 en = list[e];
+    const uint2 en = list[e * stride];
     const float sv = __uint_as_float(en.y);
-    if (IP ? (sv >= thr) : (sv <= thr)) list[w++] = en;
+    if (IP ? (sv >= thr) : (sv <= thr)) list[(w++) * stride] = en;
   }
   return w;
 }
@@ -361,18 +361,34 @@ __global__ void k_gather_rows(const __half* __restrict__ src_h, const __half* __
 
 // Global max |c|, a bound on max |c_j| and a non-finite flag, over all centroids.
 // cinfo (u32): [0] bits of max|c|, [1] bits of the norm bound, [2] non-finite flag.
-__global__ void k_cent_max(const float* __restrict__ c, long k, int d, uint32_t* cinfo) {
-  const long j = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+// One warp per centroid, two per block; 16-byte loads when the rows allow.
+__global__ void __launch_bounds__(64) k_cent_max(const float* __restrict__ c, long k, int d,
+                                                 uint32_t* cinfo) {
+  const long j = (long)blockIdx.x * 2 + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (j >= k) return;
   const float* r = c + j * (long)d;
   float mx = 0.0f, ss = 0.0f;
   bool finite = true;
-  for (int t = lane; t < d; t += 32) {
-    const float v = __ldg(r + t);
-    finite = finite && isfinite(v);
-    mx = fmaxf(mx, fabsf(v));
-    ss = fmaf(v, v, ss);
+  if ((d & 3) == 0 && ((uintptr_t)c & 15) == 0) {
+    const float4* r4 = reinterpret_cast<const float4*>(r);
+#pragma unroll 4
+    for (int t = lane; t < d / 4; t += 32) {
+      const float4 v = __ldg(r4 + t);
+      finite = finite && isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      ss = fmaf(v.x, v.x, ss);
+      ss = fmaf(v.y, v.y, ss);
+      ss = fmaf(v.z, v.z, ss);
+      ss = fmaf(v.w, v.w, ss);
+    }
+  } else {
+    for (int t = lane; t < d; t += 32) {
+      const float v = __ldg(r + t);
+      finite = finite && isfinite(v);
+      mx = fmaxf(mx, fabsf(v));
+      ss = fmaf(v, v, ss);
+    }
   }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) {
@@ -391,10 +407,14 @@ __global__ void k_cent_max(const float* __restrict__ c, long k, int d, uint32_t*
 }
 
 // Scaled split FP16 centroids: c' = c 2^(14 - ec), 2^(ec-1) <= max|c| < 2^ec.
-__global__ void k_cent_conv(const float* __restrict__ c, long k, int d, int dp,
-                            const uint32_t* __restrict__ cinfo, __half* __restrict__ ch,
-                            __half* __restrict__ cl) {
-  const long j = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+// One warp per centroid, two per block; four columns per lane step when the
+// rows allow 16-byte loads (dp is a multiple of 32, so the padding is whole
+// groups of four).
+__global__ void __launch_bounds__(64) k_cent_conv(const float* __restrict__ c, long k, int d,
+                                                  int dp, const uint32_t* __restrict__ cinfo,
+                                                  __half* __restrict__ ch,
+                                                  __half* __restrict__ cl) {
+  const long j = (long)blockIdx.x * 2 + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (j >= k) return;
   int ec = 0;
@@ -402,9 +422,27 @@ __global__ void k_cent_conv(const float* __restrict__ c, long k, int d, int dp,
   const int sh = 14 - ec;
   const bool bad = cinfo[2] != 0;
   const float* r = c + j * (long)d;
-  for (int t = lane; t < dp; t += 32) {
-    const float v = (t < d && !bad) ? __ldg(r + t) : 0.0f;
-    split16(ldexpf(v, sh), ch[j * (long)dp + t], cl[j * (long)dp + t]);
+  __half* oh = ch + j * (long)dp;
+  __half* ol = cl + j * (long)dp;
+  if ((d & 3) == 0 && ((uintptr_t)c & 15) == 0) {
+    const float4* r4 = reinterpret_cast<const float4*>(r);
+#pragma unroll 2
+    for (int t = lane; t < dp / 4; t += 32) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (4 * t < d && !bad) v = __ldg(r4 + t);
+      __align__(8) __half h[4], l[4];
+      split16(ldexpf(v.x, sh), h[0], l[0]);
+      split16(ldexpf(v.y, sh), h[1], l[1]);
+      split16(ldexpf(v.z, sh), h[2], l[2]);
+      split16(ldexpf(v.w, sh), h[3], l[3]);
+      *reinterpret_cast<uint2*>(oh + 4 * t) = *reinterpret_cast<const uint2*>(h);
+      *reinterpret_cast<uint2*>(ol + 4 * t) = *reinterpret_cast<const uint2*>(l);
+    }
+  } else {
+    for (int t = lane; t < dp; t += 32) {
+      const float v = (t < d && !bad) ? __ldg(r + t) : 0.0f;
+      split16(ldexpf(v, sh), oh[t], ol[t]);
+    }
   }
 }
 
@@ -420,7 +458,7 @@ struct ScreenParams {
   const float* cn;     // k squared centroid norms (L2) or null
   const uint32_t* cinfo;
   float e_rel, e_abs, e_min;  // bound coefficients (see the header comment)
-  uint2* cand;         // m x CAP (id, screened value bits)
+  uint2* cand;         // CAP x m (id, screened value bits): entry e of row i at e m + i
   uint32_t* cand_cnt;  // m: entries in use, or FALLBACK
   float* cand_thr;     // m: the final admission threshold
   uint32_t* status;
@@ -589,7 +627,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       float thr = best;
       bool overflow = false;
       uint32_t cnt = 0;  // entries in this row's candidate list
-      uint2* row_list = P.cand + (live ? i : 0) * (long)CAP;
+      uint2* row_list = P.cand + (live ? i : 0);  // entries P.m apart
 
       for (int nt = 0; nt < P.ntiles; nt++, tc++) {
         // Warp-uniform: the TMEM loads below are .sync.aligned.
@@ -649,12 +687,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
           for (int j = 0; j < 32; j++) adm |= (uint32_t)(IP ? (s[j] >= thr) : (s[j] <= thr)) << j;
           if (collect && adm) {
-            if (cnt + 32 > CAP) cnt = compact_list<IP>(row_list, cnt, thr);
+            if (cnt + 32 > CAP) cnt = compact_list<IP>(row_list, P.m, cnt, thr);
             const uint32_t base = (uint32_t)(col0 + g * 32);
 #pragma unroll
             for (int j = 0; j < 32; j++) {
               if ((adm >> j) & 1u) {
-                if (cnt < CAP) row_list[cnt] = make_uint2(base + j, __float_as_uint(s[j]));
+                if (cnt < CAP) row_list[cnt * P.m] = make_uint2(base + j, __float_as_uint(s[j]));
                 overflow |= cnt >= CAP;
                 cnt += cnt < CAP;
               }
@@ -742,7 +780,7 @@ __global__ void __launch_bounds__(256) k_collect(
   if (!fb) {
     thr = cand_thr[i];
     for (uint32_t e = 0; e < cnt; e++) {
-      const uint2 en = cand[i * (long)CAP + e];
+      const uint2 en = cand[e * m + i];
       const float sv = __uint_as_float(en.y);
       if (en.x >= k) {
         atomicOr(status, ST_BAD_STATE);
@@ -764,7 +802,7 @@ __global__ void __launch_bounds__(256) k_collect(
   uint32_t w = warp_append(pair_count, np);
   if (np) {
     for (uint32_t e = 0; e < cnt; e++) {
-      const uint2 en = cand[i * (long)CAP + e];
+      const uint2 en = cand[e * m + i];
       const float sv = __uint_as_float(en.y);
       if (IP ? (sv >= thr) : (sv <= thr)) pairs[w++] = make_uint2((uint32_t)i, en.x);
     }
@@ -815,12 +853,17 @@ __device__ __forceinline__ float chain(const float* __restrict__ x, const float*
   return acc;
 }
 
-// Exact chains over the (row, centroid) pairs, one thread per pair: x and the
-// centroid stream through shared memory in 32-column slices (cp.async, 4
-// slices in flight), each 16-byte chunk q of pair slot t stored at
-// q ^ (t & 7) so that the per-thread LDS.128 reads are free of bank conflicts.
-// Each pair folds (value, id) into its row's key with an atomic max / min.
-constexpr int EX_ROWS = 128, EX_COLS = 32, EX_STAGES = 4;
+// Exact chains over the (row, centroid) pairs, one thread per pair. Each warp
+// runs its own pipeline over its 32 pairs, with no barrier across warps: x
+// and the centroid stream through the warp's shared memory in 32-column
+// slices (cp.async, EX_STAGES slices in flight; each copy instruction moves
+// four whole 128-byte row segments), and each 16-byte chunk q of pair slot r
+// is stored at q ^ (r & 7) so that the per-lane LDS.128 reads are free of
+// bank conflicts. Each pair folds (value, id) into its row's key with an
+// atomic max / min.
+constexpr int EX_COLS = 32, EX_STAGES = 3, EX_WARPS = 8;
+constexpr int EX_WARP_FLOATS = EX_STAGES * 2 * 32 * EX_COLS;  // x and c slices of one warp
+constexpr size_t EX_SMEM = (size_t)EX_WARPS * EX_WARP_FLOATS * sizeof(float);
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem)
@@ -835,24 +878,23 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 template <bool IP>
-__global__ void __launch_bounds__(EX_ROWS) k_pairs(
+__global__ void __launch_bounds__(EX_WARPS * 32) k_pairs(
     const float* __restrict__ x, int d, const uint32_t* __restrict__ ids, long p0,
     const float* __restrict__ c, const float* __restrict__ cn, const float* __restrict__ xnorm_row,
     const uint2* __restrict__ pairs, const uint32_t* __restrict__ pair_count, long m, uint32_t k,
     unsigned long long* __restrict__ rkey, float* __restrict__ xn_pos,
     uint32_t* __restrict__ bad, uint32_t* __restrict__ status) {
   extern __shared__ __align__(16) float ex_smem[];
-  constexpr int SLICE = EX_STAGES * EX_ROWS * EX_COLS;
-  float* xs = ex_smem;          // [stage][pair][32]
-  float* cs = ex_smem + SLICE;  // [stage][pair][32]
-  __shared__ const float* xrow_s[EX_ROWS];
-  __shared__ const float* crow_s[EX_ROWS];
-  const int t = threadIdx.x;
+  __shared__ const float* rows_s[EX_WARPS][2][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* xs = ex_smem + warp * EX_WARP_FLOATS;  // [stage][pair][32]
+  float* cs = xs + EX_STAGES * 32 * EX_COLS;     // [stage][pair][32]
   const long np = (long)*pair_count;
   const int nsl = d / EX_COLS;
   const bool want_xn = !IP && !xnorm_row;
-  for (long tile = blockIdx.x; tile * EX_ROWS < np; tile += gridDim.x) {
-    const long pi = tile * EX_ROWS + t;
+  const long stride = (long)gridDim.x * EX_WARPS;
+  for (long wt = (long)blockIdx.x * EX_WARPS + warp; wt * 32 < np; wt += stride) {
+    const long pi = wt * 32 + lane;
     bool mine = pi < np;
     uint2 pr = make_uint2(0, 0);
     long row = 0;
@@ -866,20 +908,20 @@ __global__ void __launch_bounds__(EX_ROWS) k_pairs(
       row = ids ? (long)ids[p0 + pr.x] : p0 + pr.x;
     }
     // Slots past the pair count read row 0 / centroid 0 harmlessly and write nothing.
-    xrow_s[t] = x + row * (long)d;
-    crow_s[t] = c + (long)pr.y * d;
-    __syncthreads();
+    rows_s[warp][0][lane] = x + row * (long)d;
+    rows_s[warp][1][lane] = c + (long)pr.y * d;
+    __syncwarp();
     auto issue = [&](int sl) {
       if (sl < nsl) {
         const int st = sl % EX_STAGES;
+        const int q = lane & 7;
 #pragma unroll
         for (int u = 0; u < 8; u++) {
-          const int idx = u * EX_ROWS + t;  // 0 .. 1023
-          const int r = idx >> 3, q = idx & 7;
-          const int off = (st * EX_ROWS + r) * EX_COLS + (q ^ (r & 7)) * 4;
+          const int r = u * 4 + (lane >> 3);
+          const int off = (st * 32 + r) * EX_COLS + ((q ^ (r & 7)) << 2);
           const int g = sl * EX_COLS + q * 4;
-          cp_async16(xs + off, xrow_s[r] + g);
-          cp_async16(cs + off, crow_s[r] + g);
+          cp_async16(xs + off, rows_s[warp][0][r] + g);
+          cp_async16(cs + off, rows_s[warp][1][r] + g);
         }
       }
       cp_async_commit();
@@ -890,13 +932,13 @@ __global__ void __launch_bounds__(EX_ROWS) k_pairs(
     for (int sl = 0; sl < nsl; sl++) {
       issue(sl + EX_STAGES - 1);
       cp_async_wait<EX_STAGES - 1>();
-      __syncthreads();
-      const int base = (sl % EX_STAGES * EX_ROWS + t) * EX_COLS;
+      __syncwarp();
+      const int base = (sl % EX_STAGES * 32 + lane) * EX_COLS;
       const float4* xr4 = reinterpret_cast<const float4*>(xs + base);
       const float4* cr4 = reinterpret_cast<const float4*>(cs + base);
 #pragma unroll
       for (int q = 0; q < 8; q++) {
-        const int pq = q ^ (t & 7);
+        const int pq = q ^ (lane & 7);
         const float4 a = xr4[pq], b = cr4[pq];
         acc = __fmaf_rn(a.x, b.x, acc);
         acc = __fmaf_rn(a.y, b.y, acc);
@@ -910,13 +952,13 @@ __global__ void __launch_bounds__(EX_ROWS) k_pairs(
           xn = __fadd_rn(xn, __fmul_rn(a.w, a.w));
         }
       }
-      __syncthreads();  // the slot is refilled next iteration
+      __syncwarp();  // the slot is refilled next iteration
     }
     cp_async_wait<0>();
     if (mine) {
       const float v = IP ? acc : __fsub_rn(__ldg(cn + pr.y), __fmul_rn(2.0f, acc));
       if (!isfinite(v)) {
-        bad[pr.x] = 1;  // an overflowing chain: the exact scan reproduces the CPU here
+        bad[pr.x] = 1;  // an overflowing chain: the exact list reproduces the CPU here
       } else if (IP) {
         atomicMax(rkey + pr.x, result_key<IP>(v, pr.y));
       } else {
@@ -924,7 +966,7 @@ __global__ void __launch_bounds__(EX_ROWS) k_pairs(
       }
       if (want_xn) xn_pos[pr.x] = xn;  // the same value from every pair of the row
     }
-    __syncthreads();  // row pointers are rewritten by the next tile
+    __syncwarp();  // row pointers are rewritten by the next tile
   }
 }
 
@@ -1030,7 +1072,8 @@ __global__ void __launch_bounds__(LS_C) k_list(
     const float* __restrict__ x, long n, int d, const uint32_t* __restrict__ ids,
     const float* __restrict__ c, const float* __restrict__ cn, long k,
     const uint32_t* __restrict__ list, const uint32_t* __restrict__ list_count,
-    unsigned long long* __restrict__ lkey, uint32_t* __restrict__ status) {
+    unsigned long long* __restrict__ lkey, const float* __restrict__ xnorm_row,
+    float* __restrict__ lxn, uint32_t* __restrict__ status) {
   extern __shared__ __align__(16) float ls_smem[];
   float* cs = ls_smem;                                 // [stage][LS_C][32]
   float* xs = ls_smem + LS_STAGES * LS_C * EX_COLS;    // [stage][32]
@@ -1043,6 +1086,9 @@ __global__ void __launch_bounds__(LS_C) k_list(
   for (long w = blockIdx.x; w < total; w += gridDim.x) {
     const long ent = w / kch;
     const long j0 = (w - ent * kch) * LS_C;
+    // The first centroid block's thread 0 also sums the row's squares in the
+    // CPU order (sequential, no FMA) when the caller has no row norms.
+    const bool sum_xn = !IP && !xnorm_row && j0 == 0 && t == 0;
     long row = list[ent];
     if (ids) row = ids[row];
     if (row >= n) {
@@ -1082,7 +1128,7 @@ __global__ void __launch_bounds__(LS_C) k_list(
     };
 #pragma unroll
     for (int s = 0; s < LS_STAGES - 1; s++) issue(s);
-    float acc = 0.0f;
+    float acc = 0.0f, xn = -0.0f;
     for (int sl = 0; sl < nsl; sl++) {
       issue(sl + LS_STAGES - 1);
       cp_async_wait<LS_STAGES - 1>();
@@ -1091,6 +1137,8 @@ __global__ void __launch_bounds__(LS_C) k_list(
       const float* crow = cs + (st * LS_C + t) * EX_COLS;
       const float* xsl = xs + st * EX_COLS;
       const int kmax = min(EX_COLS, d - sl * EX_COLS);
+      if (sum_xn)
+        for (int cc = 0; cc < kmax; cc++) xn = __fadd_rn(xn, __fmul_rn(xsl[cc], xsl[cc]));
       if (kmax == EX_COLS) {
         const float4* x4 = reinterpret_cast<const float4*>(xsl);
         const float4* c4 = reinterpret_cast<const float4*>(crow);
@@ -1109,6 +1157,7 @@ __global__ void __launch_bounds__(LS_C) k_list(
       __syncthreads();  // the slot is refilled next iteration
     }
     cp_async_wait<0>();
+    if (sum_xn) lxn[ent] = xn;
     const long j = j0 + t;
     unsigned long long key = scan_start_key<IP>();
     if (j < k) {
@@ -1142,8 +1191,8 @@ __global__ void k_list_finish(const float* __restrict__ x, long n, int d,
                               const uint32_t* __restrict__ list,
                               const uint32_t* __restrict__ list_count,
                               const unsigned long long* __restrict__ lkey,
-                              const float* __restrict__ xnorm_row, uint32_t* __restrict__ labels,
-                              float* __restrict__ scores) {
+                              const float* __restrict__ xnorm_row, const float* __restrict__ lxn,
+                              uint32_t* __restrict__ labels, float* __restrict__ scores) {
   const long cnt = (long)*list_count;
   for (long ent = (long)blockIdx.x * blockDim.x + threadIdx.x; ent < cnt;
        ent += (long)gridDim.x * blockDim.x) {
@@ -1154,18 +1203,7 @@ __global__ void k_list_finish(const float* __restrict__ x, long n, int d,
     if (!IP) {
       long row = ids ? (long)ids[p] : p;
       if (row >= n) row = 0;  // reported by the scan kernel
-      float xn;
-      if (xnorm_row) {
-        xn = xnorm_row[row];
-      } else {
-        // Sequential sum of squares in the CPU order, for this row only.
-        const float* xr = x + row * (long)d;
-        xn = -0.0f;
-        for (int u = 0; u < d; u++) {
-          const float a = __ldg(xr + u);
-          xn = __fadd_rn(xn, __fmul_rn(a, a));
-        }
-      }
+      const float xn = xnorm_row ? xnorm_row[row] : lxn[ent];
       score = fmaxf(__fadd_rn(xn, v), 0.0f);
     }
     labels[p] = j;
@@ -1256,6 +1294,7 @@ struct ExactScratch {
   uint32_t* list;
   uint32_t* list_count;
   unsigned long long* lkey;
+  float* lxn;
 };
 
 template <bool IP>
@@ -1272,9 +1311,8 @@ void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const ExactS
   // The pair count is known on the device only: persistent blocks stride over it.
   const unsigned pgrid = (unsigned)e->num_sms;
   if (a.d % EX_COLS == 0) {
-    const size_t ex_smem = 2 * EX_STAGES * EX_ROWS * EX_COLS * sizeof(float);
-    set_pairs_smem<IP>(e->device, ex_smem);
-    k_pairs<IP><<<pgrid, EX_ROWS, ex_smem, e->stream>>>(
+    set_pairs_smem<IP>(e->device, EX_SMEM);
+    k_pairs<IP><<<pgrid, EX_WARPS * 32, EX_SMEM, e->stream>>>(
         a.x, (int)a.d, a.ids, c0, a.c, a.cnorm, a.xnorm, S.pairs, S.pair_count, m,
         (uint32_t)a.k, S.rkey, S.xn_pos, S.bad, e->d_status);
   } else {
@@ -1295,10 +1333,11 @@ void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const ExactS
   set_list_smem<IP>(e->device);
   k_list<IP><<<lgrid, LS_C, LS_SMEM, e->stream>>>(a.x, (long)a.n, (int)a.d, a.ids, a.c, a.cnorm,
                                                  (long)a.k, S.list, S.list_count, S.lkey,
-                                                 e->d_status);
+                                                 a.xnorm, S.lxn, e->d_status);
   EB_LAUNCH("screen exact list");
   k_list_finish<IP><<<(unsigned)std::min<long>((m + 255) / 256, e->num_sms), 256, 0, e->stream>>>(
-      a.x, (long)a.n, (int)a.d, a.ids, S.list, S.list_count, S.lkey, a.xnorm, a.labels, a.scores);
+      a.x, (long)a.n, (int)a.d, a.ids, S.list, S.list_count, S.lkey, a.xnorm, S.lxn, a.labels,
+      a.scores);
   EB_LAUNCH("screen exact list finish");
 }
 
@@ -1338,11 +1377,10 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   __half* cl = e->scratch_get<__half>("tc_cl", k * dp);
   EB_CUDA(cudaMemsetAsync(cinfo, 0, 16, e->stream));
   const unsigned wpb = 8;
-  k_cent_max<<<(unsigned)((k + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(a.c, (long)k, (int)d,
-                                                                          cinfo);
+  k_cent_max<<<(unsigned)((k + 1) / 2), 64, 0, e->stream>>>(a.c, (long)k, (int)d, cinfo);
   EB_LAUNCH("screen centroid max");
-  k_cent_conv<<<(unsigned)((k + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(
-      a.c, (long)k, (int)d, (int)dp, cinfo, ch, cl);
+  k_cent_conv<<<(unsigned)((k + 1) / 2), 64, 0, e->stream>>>(a.c, (long)k, (int)d, (int)dp, cinfo,
+                                                            ch, cl);
   EB_LAUNCH("screen centroid convert");
   const CUtensorMap mapBh = make_map(ch, k, dp, BN);
   const CUtensorMap mapBl = make_map(cl, k, dp, BN);
@@ -1362,8 +1400,9 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   uint32_t* bad = e->scratch_get<uint32_t>("tc_bad", chunk);
   float* xn_pos = e->scratch_get<float>("tc_xn_pos", chunk);
   unsigned long long* lkey = e->scratch_get<unsigned long long>("tc_lkey", chunk);
+  float* lxn = e->scratch_get<float>("tc_lxn", chunk);
   const ExactScratch S{cand, cand_cnt, cand_thr, pairs, pair_count, rkey, bad, xn_pos, list,
-                       list_count, lkey};
+                       list_count, lkey, lxn};
 
   ScreenParams P;
   P.k = (int)k;
