@@ -9,6 +9,9 @@
 // threads (4x4 per thread), 16 columns of d per stage.
 #include <cuda_runtime.h>
 
+#include <mutex>
+#include <string>
+
 #include "engine.h"
 
 namespace eb {
@@ -222,4 +225,106 @@ void top1_exact(eb_engine* e, const Top1Args& a) {
   e->stats.exact_rows += rows;
 }
 
+// ---------------------------------------------------------------- no-alloc entry
+//
+// eb_top1_exact_noalloc runs the kernel above for callers that may not
+// allocate device memory while a call is in progress: a serving process that
+// reserves its device memory once at start-up and must keep its footprint
+// fixed per request, or a caller on a latency budget that cannot take the
+// pause (or the failure) a pool allocation may bring under memory pressure.
+// The engine's top-1 keeps its L2 row norms in grow-only scratch, which can
+// allocate on a larger call; this entry keeps them in the fixed device array
+// below instead, so the call itself allocates nothing.
+//
+// The first call on a device does the set-up (looking up this device's copy
+// of the array, which may load the module): make it before any stream
+// capture. The array is one per device and shared by every engine on it, so
+// two calls in flight at once on one device (different streams or engines)
+// race on it; calls on one stream are ordered and safe. Nothing in it needs
+// to start at zero: every norm a call reads is written earlier in that call.
+namespace {
+
+constexpr size_t kNoAllocRows = EB_NOALLOC_MAX_ROWS;  // 4 MiB of row norms
+static __device__ __align__(256) float g_noalloc_xnorm[kNoAllocRows];
+
+constexpr int kNoAllocDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_addr[kNoAllocDevices] = {};
+
+// This device's copy of the array; the caller has made the device current.
+float* noalloc_scratch(int device) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (device < 0 || device >= kNoAllocDevices)
+    throw Error(EB_ERROR, "device ordinal out of range for the no-alloc scratch");
+  if (!g_noalloc_addr[device]) {
+    void* p = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&p, g_noalloc_xnorm);
+    if (rc != cudaSuccess || p == nullptr)
+      throw Error(EB_ERROR, std::string("cudaGetSymbolAddress(no-alloc scratch): ") +
+                                cudaGetErrorString(rc));
+    g_noalloc_addr[device] = static_cast<float*>(p);
+  }
+  return g_noalloc_addr[device];
+}
+
+struct CurrentDevice {
+  int prev = -1;
+  explicit CurrentDevice(int device) {
+    cudaGetDevice(&prev);
+    if (prev != device) EB_CUDA(cudaSetDevice(device));
+  }
+  ~CurrentDevice() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
 }  // namespace eb
+
+extern "C" int eb_top1_exact_noalloc(eb_engine* e, const float* x, size_t n, size_t d,
+                                     const uint32_t* ids, size_t r0, size_t r1, const float* c,
+                                     const float* cnorm, size_t k, int metric, uint32_t* labels,
+                                     float* scores) {
+  using namespace eb;
+  try {
+    ensure(e != nullptr, "engine is null");
+    ensure(x && c && labels && scores, "a device pointer is null");
+    ensure(d > 0, "d must be positive");
+    ensure(metric == EB_L2 || metric == EB_IP, "unknown metric");
+    ensure(r0 <= r1, "bad row range");
+    if (!ids) ensure(r1 <= n, "row range past the data");
+    ensure(k > 0 && k <= 0xFFFFFFFFull, "k must be in 1 .. 2^32 - 1");
+    if (metric == EB_L2) ensure(cnorm != nullptr, "L2 needs centroid norms");
+    ensure(r1 - r0 <= kNoAllocRows,
+           "the no-alloc top-1 takes at most " + std::to_string(kNoAllocRows) +
+               " rows per call (got " + std::to_string(r1 - r0) + ")");
+    CurrentDevice dev(e->device);
+    float* xn = noalloc_scratch(e->device);
+    const size_t rows = r1 - r0;
+    if (rows > 0) {
+      if (metric == EB_L2) sel_row_norms(e, x, n, d, ids, r0, r1, xn);
+      const unsigned grid = (unsigned)((rows + BM - 1) / BM);
+      if (metric == EB_IP)
+        k_top1_exact<true><<<grid, NT, 0, e->stream>>>(x, (long)n, (int)d, ids, (long)r0,
+                                                       (long)r1, c, cnorm, (long)k, nullptr, 0,
+                                                       labels, scores, e->d_status);
+      else
+        k_top1_exact<false><<<grid, NT, 0, e->stream>>>(x, (long)n, (int)d, ids, (long)r0,
+                                                        (long)r1, c, cnorm, (long)k, xn, 0,
+                                                        labels, scores, e->d_status);
+      EB_LAUNCH("top1_exact_noalloc");
+      e->stats.exact_rows += rows;
+    }
+    set_last_error("");
+    return EB_OK;
+  } catch (const Error& err) {
+    set_last_error(err.what());
+    return err.code;
+  } catch (const std::exception& err) {
+    set_last_error(std::string("internal: ") + err.what());
+    return EB_INTERNAL;
+  }
+}

@@ -222,6 +222,29 @@ typedef struct {
 
 int eb_train(eb_engine* e, const eb_train_job* job, eb_train_out* out);
 
+/* ---------------------------------------------------------------- no-alloc top-1 */
+
+/* No counterpart in the reference: its CPU path has no device memory to
+ * allocate. The exact top-1 of eb_top1 (the SIMT kernel, same labels and
+ * scores bit for bit) over raw device pointers, for callers that may not
+ * allocate device memory during a call (a fixed per-request memory
+ * footprint, no allocation pauses on a latency budget). Its one scratch, the
+ * L2 row norms of the selection, is a fixed device array of
+ * EB_NOALLOC_MAX_ROWS floats per device; larger selections are rejected with
+ * EB_INVALID_ARGUMENT. x is n x d (rows x[ids[p]] or x[p]), c is k x d,
+ * cnorm k squared norms (EB_L2 only), labels and scores are indexed by
+ * position p in r0..r1; pointer sizes are the caller's to guarantee. The
+ * first call on a device sets up the scratch's address and must come before
+ * any stream capture. The array is shared by all engines on a device: calls
+ * in flight at the same time on one device race; calls on one stream do not.
+ * Asynchronous on the engine's stream; errors found on the device surface at
+ * the next eb_sync. */
+#define EB_NOALLOC_MAX_ROWS 1048576
+int eb_top1_exact_noalloc(eb_engine* e, const float* x, size_t n, size_t d,
+                          const uint32_t* ids, size_t r0, size_t r1, const float* c,
+                          const float* cnorm, size_t k, int metric, uint32_t* labels,
+                          float* scores);
+
 #ifdef __cplusplus
 }
 #endif
