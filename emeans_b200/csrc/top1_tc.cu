@@ -82,16 +82,18 @@ constexpr int B_BYTES = BN * BKH * 2;                // one of ch / cl
 constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
 constexpr int CAP = 64;          // per-row candidate list capacity
 constexpr int SURV = 16;         // candidates per row taken to exact chains
-constexpr int NTHREADS = 192;    // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int NTHREADS = 320;    // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int HALF = BN / 2;     // tile columns per epilogue warp (two warps per TMEM lane quadrant)
 constexpr uint32_t FALLBACK = 0xFFFFFFFFu;
 constexpr int XEXP_BAD = INT_MIN;  // row with a non-finite value
 constexpr size_t PASS_WAVES = 8;   // row tiles per SM in one pass
 constexpr uint64_t WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
-// Operand ring, 256 B of barriers / TMEM slot / flags, one tile of centroid
-// norms per epilogue warp.
+// Operand ring, 256 B of barriers / TMEM slot / flags, the centroid norms of
+// each epilogue warp's half tile, and each epilogue warp's slab of one
+// group's screened values ([16 columns][32 rows]) for the appends.
 constexpr size_t SMEM_BYTES = 1024 /* alignment slack */ + STAGES * STAGE_BYTES + 256 +
-                              4 * BN * sizeof(float);
+                              8 * HALF * sizeof(float) + 8 * 16 * 32 * sizeof(float);
 
 // ---------------------------------------------------------------- PTX helpers
 
@@ -192,22 +194,31 @@ __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 
-// 32 consecutive FP32 columns of this thread's TMEM lane (completes with
-// tmem_wait()).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 16 consecutive FP32 columns of this thread's TMEM lane (valid after
+// tmem_wait_tied()).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-      "%30, %31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
-        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
-        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_wait() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+// Wait for this thread's TMEM loads. The registers of the group just loaded
+// are tied to the wait (and to an empty statement after it), so the compiler
+// cannot move their first use above the point where they are valid.
+__device__ __forceinline__ void tmem_wait_tied(uint32_t (&a)[16], uint32_t (&b)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]),
+                 "+r"(a[6]), "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]),
+                 "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15])
+               :
+               : "memory");
+  asm volatile(""
+               : "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]),
+                 "+r"(b[6]), "+r"(b[7]), "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]),
+                 "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15]));
 }
 
 // Keep only the entries of a row's candidate list still inside the window
@@ -458,9 +469,11 @@ struct ScreenParams {
   const float* cn;     // k squared centroid norms (L2) or null
   const uint32_t* cinfo;
   float e_rel, e_abs, e_min;  // bound coefficients (see the header comment)
-  uint2* cand;         // CAP x m (id, screened value bits): entry e of row i at e m + i
-  uint32_t* cand_cnt;  // m: entries in use, or FALLBACK
-  float* cand_thr;     // m: the final admission threshold
+  // Candidate lists, one per (half tile, row): half h, entry e of row i at
+  // (h CAP + e) m + i (id, screened value bits).
+  uint2* cand;
+  uint32_t* cand_cnt;  // 2 m: entries in use per (half, row), or FALLBACK
+  float* cand_thr;     // 2 m: the final admission threshold per (half, row)
   uint32_t* status;
 };
 
@@ -478,7 +491,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* mma_done = tempty + 1;
   uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
-  float* cn_s = (float*)(smem + STAGES * STAGE_BYTES + 256);  // [4 warps][BN]
+  float* cn_s = (float*)(smem + STAGES * STAGE_BYTES + 256);  // [8 warps][HALF]
+  float* sv_s = cn_s + 8 * HALF;                               // [8 warps][16][32]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -488,7 +502,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(tfull, 1);
-    mbar_init(tempty, 128);
+    mbar_init(tempty, 256);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -583,15 +597,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
   } else {
-    // Epilogue: one thread per row of each row tile.
+    // Epilogue: warps 2-9. Warp w reads TMEM lanes 32 (w % 4) .. + 31 (one
+    // row per thread) and half (w - 2) / 4 of every tile's columns; each
+    // (row, half) keeps its own running best and candidate list.
     const int q = warp & 3;
+    const int hf = (warp - 2) >> 2;
     const int r = q * 32 + lane;
     int ec = 0;
     frexpf(__uint_as_float(P.cinfo[0]), &ec);
     const float cmax = __uint_as_float(P.cinfo[1]);
     const bool c_bad = P.cinfo[2] != 0;
-    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-    float* cns = cn_s + q * BN;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(hf * HALF);
+    float* cns = cn_s + (warp - 2) * HALF;
+    float* svs = sv_s + (warp - 2) * 16 * 32 + lane;  // this lane's column of the slab
     int tc = 0;
     bool stop = false;
     for (long rt = blockIdx.x; rt * BM < P.m; rt += gridDim.x) {
@@ -599,7 +617,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const bool live = i < P.m;
       if (stop) {
         // A wait gave up: this CTA's remaining rows go to the exact fallback.
-        if (live) P.cand_cnt[i] = FALLBACK;
+        if (live) P.cand_cnt[hf * P.m + i] = FALLBACK;
         continue;
       }
       const int ex = live ? P.xexp[i] : XEXP_BAD;
@@ -626,8 +644,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       float best = IP ? -INFINITY : INFINITY;
       float thr = best;
       bool overflow = false;
-      uint32_t cnt = 0;  // entries in this row's candidate list
-      uint2* row_list = P.cand + (live ? i : 0);  // entries P.m apart
+      uint32_t cnt = 0;  // entries in this (row, half)'s candidate list
+      uint2* row_list = P.cand + (long)hf * CAP * P.m + (live ? i : 0);  // entries P.m apart
 
       for (int nt = 0; nt < P.ntiles; nt++, tc++) {
         // Warp-uniform: the TMEM loads below are .sync.aligned.
@@ -637,75 +655,101 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           break;
         }
         tc_fence_after();
-        const int col0 = nt * BN;
+        const int col0 = nt * BN + hf * HALF;  // first centroid of this warp's half tile
         if (!IP) {
-          // This tile's squared centroid norms, staged by each warp for itself
-          // (no barrier across warps, so a timed-out wait strands no warp).
+          // This half tile's squared centroid norms, staged by each warp for
+          // itself (no barrier across warps, so a timed-out wait strands no warp).
 #pragma unroll
-          for (int u = 0; u < BN / 32; u++) {
+          for (int u = 0; u < HALF / 32; u++) {
             const int c = u * 32 + lane;
             cns[c] = col0 + c < P.k ? __ldg(P.cn + col0 + c) : 0.0f;
           }
           __syncwarp();
         }
-        const int ngr = min(BN / 32, (P.k - col0 + 31) / 32);
-#pragma unroll 1
-        for (int g = 0; g < ngr; g++) {
-          uint32_t vh[32], vl[32];
-          tmem_ld32(lane_base + (uint32_t)(g * 32), vh);
-          tmem_ld32(lane_base + (uint32_t)(BN + g * 32), vl);
-          tmem_wait();
-          const int lim = P.k - (col0 + g * 32);
-          float s[32];
-          const float4* c4 = reinterpret_cast<const float4*>(cns + g * 32);
+        const int ngr = max(0, min(HALF / 16, (P.k - col0 + 15) / 16));
+        // Software pipeline over 16-column groups: group g + 1's TMEM loads are
+        // in flight while group g is scored.
+        uint32_t vh[2][16], vl[2][16];
+        if (ngr > 0) {
+          tmem_ld16(lane_base, vh[0]);
+          tmem_ld16(lane_base + BN, vl[0]);
+        }
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
+        for (int g = 0; g < HALF / 16; g++) {
+          if (g >= ngr) break;
+          uint32_t(&h)[16] = vh[g & 1];
+          uint32_t(&l)[16] = vl[g & 1];
+          tmem_wait_tied(h, l);
+          if (g + 1 < ngr) {
+            tmem_ld16(lane_base + (uint32_t)((g + 1) * 16), vh[(g + 1) & 1]);
+            tmem_ld16(lane_base + (uint32_t)(BN + (g + 1) * 16), vl[(g + 1) & 1]);
+          }
+          float s[16];
+          const float4* c4 = reinterpret_cast<const float4*>(cns + g * 16);
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
             const float4 cv = IP ? make_float4(0.f, 0.f, 0.f, 0.f) : c4[j / 4];
             const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
 #pragma unroll
             for (int w = 0; w < 4; w++) {
-              const float acc = __fadd_rn(__uint_as_float(vh[j + w]), __uint_as_float(vl[j + w]));
-              float v = IP ? acc : __fmaf_rn(m2f, acc, cc[w]);
-              if (j + w >= lim) v = IP ? -INFINITY : INFINITY;
-              s[j + w] = v;
+              const float acc = __fadd_rn(__uint_as_float(h[j + w]), __uint_as_float(l[j + w]));
+              s[j + w] = IP ? acc : __fmaf_rn(m2f, acc, cc[w]);
             }
           }
+          const int lim = P.k - (col0 + g * 16);
+          if (lim < 16) {  // warp-uniform: only the last, partial group of the centroids
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+              if (j >= lim) s[j] = IP ? -INFINITY : INFINITY;
+          }
           // The group's best moves the threshold first.
-          float t[16];
+          float t[8];
 #pragma unroll
-          for (int j = 0; j < 16; j++) t[j] = IP ? fmaxf(s[j], s[j + 16]) : fminf(s[j], s[j + 16]);
+          for (int j = 0; j < 8; j++) t[j] = IP ? fmaxf(s[j], s[j + 8]) : fminf(s[j], s[j + 8]);
 #pragma unroll
-          for (int w2 = 8; w2 >= 1; w2 >>= 1)
+          for (int w2 = 4; w2 >= 1; w2 >>= 1)
 #pragma unroll
             for (int j = 0; j < w2; j++) t[j] = IP ? fmaxf(t[j], t[j + w2]) : fminf(t[j], t[j + w2]);
           if (IP ? (t[0] > best) : (t[0] < best)) {
             best = t[0];
             thr = IP ? __fsub_rd(best, off) : __fadd_ru(best, off);
           }
-          // Straight-line admission mask; the append runs only when it is set.
           uint32_t adm = 0;
 #pragma unroll
-          for (int j = 0; j < 32; j++) adm |= (uint32_t)(IP ? (s[j] >= thr) : (s[j] <= thr)) << j;
-          if (collect && adm) {
-            if (cnt + 32 > CAP) cnt = compact_list<IP>(row_list, P.m, cnt, thr);
-            const uint32_t base = (uint32_t)(col0 + g * 32);
+          for (int j = 0; j < 16; j++) adm |= (uint32_t)(IP ? (s[j] >= thr) : (s[j] <= thr)) << j;
+          if (!collect) adm = 0;
+          // Appends: the warp stages the group's values in its slab only when
+          // some lane admits a column; each admitting lane then walks its set
+          // bits (usually one or two) and reads the values back by index.
+          if (__any_sync(0xFFFFFFFFu, adm != 0)) {
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-              if ((adm >> j) & 1u) {
-                if (cnt < CAP) row_list[cnt * P.m] = make_uint2(base + j, __float_as_uint(s[j]));
+            for (int j = 0; j < 16; j++) svs[j * 32] = s[j];
+            __syncwarp();
+            if (adm) {
+              if (cnt + (uint32_t)__popc(adm) > CAP) cnt = compact_list<IP>(row_list, P.m, cnt, thr);
+              const uint32_t base = (uint32_t)(col0 + g * 16);
+              while (adm) {
+                const int j = __ffs(adm) - 1;
+                adm &= adm - 1;
+                if (cnt < CAP) row_list[cnt * P.m] = make_uint2(base + j, __float_as_uint(svs[j * 32]));
                 overflow |= cnt >= CAP;
                 cnt += cnt < CAP;
               }
             }
+            __syncwarp();
           }
         }
         tc_fence_before();
         mbar_arrive(tempty);
       }
       if (live) {
-        const bool ok = collect && !stop && !overflow && isfinite(best) && !*abort_flag;
-        if (ok) P.cand_thr[i] = thr;
-        P.cand_cnt[i] = ok ? cnt : FALLBACK;
+        // With k <= HALF the second half tile holds no centroid at all: its
+        // list is empty and its threshold the identity, not a fallback.
+        const bool no_columns = hf * HALF >= P.k;
+        const bool ok = collect && !stop && !overflow && !*abort_flag &&
+                        (isfinite(best) || no_columns);
+        if (ok) P.cand_thr[hf * P.m + i] = thr;
+        P.cand_cnt[hf * P.m + i] = ok ? cnt : FALLBACK;
       }
     }
   }
@@ -755,10 +799,12 @@ __device__ __forceinline__ unsigned long long scan_start_key() {
   return result_key<IP>(IP ? -INFINITY : INFINITY, 0u);
 }
 
-// Each row's candidates still inside its final window become (row, centroid)
-// pairs; rows with none, with more than SURV, or marked for the fallback go to
-// the exact list, whose key starts at the scan's starting point. The row's
-// pair key starts at the identity of its reduction. Launched with whole warps.
+// Each row's candidates (from both half-tile lists) still inside its final
+// window become (row, centroid) pairs; the window is the tighter of the two
+// halves' thresholds, the one of the row's overall best. Rows with none, with
+// more than SURV, or marked for the fallback go to the exact list, whose key
+// starts at the scan's starting point. The row's pair key starts at the
+// identity of its reduction. Launched with whole warps.
 template <bool IP>
 __global__ void __launch_bounds__(256) k_collect(
     long p0, long m, uint32_t k, const uint2* __restrict__ cand,
@@ -769,26 +815,41 @@ __global__ void __launch_bounds__(256) k_collect(
     unsigned long long* __restrict__ counters, uint32_t* __restrict__ status) {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const bool live = i < m;
-  const uint32_t cnt = live ? cand_cnt[i] : FALLBACK;
-  bool fb = cnt == FALLBACK;
-  if (!fb && cnt > CAP) {
-    atomicOr(status, ST_BAD_STATE);
-    fb = true;
+  uint32_t cnt[2];
+  bool fb = !live;
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    cnt[h] = live ? cand_cnt[h * m + i] : 0;
+    if (cnt[h] == FALLBACK) {
+      fb = true;
+    } else if (cnt[h] > CAP) {
+      atomicOr(status, ST_BAD_STATE);
+      fb = true;
+    }
   }
   uint32_t ns = 0;
   float thr = 0.0f;
   if (!fb) {
-    thr = cand_thr[i];
-    for (uint32_t e = 0; e < cnt; e++) {
-      const uint2 en = cand[e * m + i];
-      const float sv = __uint_as_float(en.y);
-      if (en.x >= k) {
-        atomicOr(status, ST_BAD_STATE);
-        fb = true;
-        break;
+    const float t0 = cand_thr[i], t1 = cand_thr[m + i];
+    thr = IP ? fmaxf(t0, t1) : fminf(t0, t1);
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const uint2* lst = cand + (long)h * CAP * m + i;
+      // Loads in batches of eight, so that they are in flight together.
+      for (uint32_t e0 = 0; e0 < cnt[h]; e0 += 8) {
+        uint2 en[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          en[u] = e0 + u < cnt[h] ? lst[(e0 + u) * m] : make_uint2(0u, __float_as_uint(NAN));
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          const float sv = __uint_as_float(en[u].y);
+          if (en[u].x >= k) fb = true;
+          ns += IP ? (sv >= thr) : (sv <= thr);
+        }
       }
-      ns += IP ? (sv >= thr) : (sv <= thr);
     }
+    if (fb) atomicOr(status, ST_BAD_STATE);
   }
   fb = fb || ns == 0 || ns > SURV;
   const bool listed = live && fb;
@@ -801,10 +862,20 @@ __global__ void __launch_bounds__(256) k_collect(
   }
   uint32_t w = warp_append(pair_count, np);
   if (np) {
-    for (uint32_t e = 0; e < cnt; e++) {
-      const uint2 en = cand[e * m + i];
-      const float sv = __uint_as_float(en.y);
-      if (IP ? (sv >= thr) : (sv <= thr)) pairs[w++] = make_uint2((uint32_t)i, en.x);
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const uint2* lst = cand + (long)h * CAP * m + i;
+      for (uint32_t e0 = 0; e0 < cnt[h]; e0 += 8) {
+        uint2 en[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          en[u] = e0 + u < cnt[h] ? lst[(e0 + u) * m] : make_uint2(0u, __float_as_uint(NAN));
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          const float sv = __uint_as_float(en[u].y);
+          if (IP ? (sv >= thr) : (sv <= thr)) pairs[w++] = make_uint2((uint32_t)i, en[u].x);
+        }
+      }
     }
   }
   const uint32_t nl = __reduce_add_sync(0xFFFFFFFFu, listed ? 1u : 0u);
@@ -1389,9 +1460,9 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   __half* xl = e->scratch_get<__half>("tc_xl", chunk * dp);
   int* xexp = e->scratch_get<int>("tc_xexp", chunk);
   float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
-  uint2* cand = e->scratch_get<uint2>("tc_cand", chunk * CAP);
-  uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", chunk);
-  float* cand_thr = e->scratch_get<float>("tc_thr", chunk);
+  uint2* cand = e->scratch_get<uint2>("tc_cand", 2 * chunk * CAP);
+  uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", 2 * chunk);
+  float* cand_thr = e->scratch_get<float>("tc_thr", 2 * chunk);
   uint32_t* list = e->scratch_get<uint32_t>("tc_list", chunk);
   uint32_t* list_count = e->scratch_get<uint32_t>("tc_list_count", 4);
   uint2* pairs = e->scratch_get<uint2>("tc_pairs", chunk * SURV);
