@@ -170,8 +170,10 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"C2 assign, bounded sample of {sample} rows per step",
-                   "rows": n, "d": d, "k": k, "metric": "L2"},
+        "config": {"workload": "C2 final assign: 200,000 x 768 f32 rows per GPU vs k=1024 "
+                               "centroids, squared L2, exact FP32 labels+scores",
+                   "rows_per_gpu": n, "d": d, "k": k, "metric": "L2",
+                   "sample_rows_per_step": sample},
         "cpu_baseline": {"value": v, "unit": "Grows/s", "cores": threads, "kind": "port",
                          "sample": f"{sample} rows x {args.steps} steps (oracle/oracle.cpp, "
                                    "the reference cpu-fused float order; Rust reference not "
@@ -197,6 +199,10 @@ def run_ours(args):
     n, d, k = args.n, args.d, args.k
     eng = eb.Engine(local)
     stream = torch.cuda.ExternalStream(eng.stream())
+    if world > 1:
+        # Training runs as one group: each batch's top-1 split over the ranks,
+        # labels and scores all-gathered over NCCL (eb_engine_join).
+        eng.join_torch_group()
 
     # Centroids: train on the shared config-2 rows (identical on every rank),
     # always the full 200,000 rows so that smaller --n runs see the same geometry.
@@ -207,15 +213,22 @@ def run_ours(args):
         cent = np.load(args.load_cent).astype(np.float32)
     elif not args.no_train:
         eng.train(xtrain, cfg)  # warm-up run
+        if dist:
+            dist.barrier()
         t0 = time.perf_counter()
         tr = eng.train(xtrain, cfg)
         train_s = time.perf_counter() - t0
         cent = tr.centroids
+        if dist:
+            t = torch.tensor([train_s], device="cuda", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            train_s = t.item()
     else:
         cent = xtrain[np.random.default_rng(0).permutation(xtrain.shape[0])[:k]]
     if args.save_cent and rank == 0:
         np.save(args.save_cent, cent)
-    x = xtrain[:n] if rank == 0 and n <= xtrain.shape[0] else gen_rows(n, d, rank)
+    rows_seed = rank if args.rows_seed is None else args.rows_seed + rank
+    x = xtrain[:n] if rows_seed == 0 and n <= xtrain.shape[0] else gen_rows(n, d, rows_seed)
     x = np.ascontiguousarray(x)
 
     # ---- device-resident assign
@@ -256,7 +269,12 @@ def run_ours(args):
     ms = start.elapsed_time(end)
     top1_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
     stats = eng.stats()
+    rank_ms = [ms / args.steps]
     if dist:
+        mine = torch.tensor([ms / args.steps], device="cuda")
+        every = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        rank_ms = [float(v.item()) for v in every]
         t = torch.tensor([ms, top1_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, top1_ms = t.tolist()
@@ -315,10 +333,14 @@ def run_ours(args):
                     "h2d_bytes_per_step": n * d * 4 + k * d * 4,
                     "d2h_bytes_per_step": n * 8},
             "gpu_launches": launches,
+            "rank_ms_per_step": rank_ms,
             "screen_stats": stats,
         }
         if train_s is not None:
-            out["train_s"] = {"value": train_s, "unit": "s", "n_gpus": 1,
+            out["train_s"] = {"value": train_s, "unit": "s", "n_gpus": world,
+                              "mode": "group: batch top-1 split over the ranks, labels and "
+                                      "scores all-gathered (NCCL); result equal to one GPU"
+                                      if world > 1 else "one GPU",
                               "steps": tr.total_steps, "batch_size": tr.batch_size,
                               "final_obj": tr.obj[-1]}
         out["clocks"] = clk.summary()
@@ -346,6 +368,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--save-cent", default=None, help="write the trained centroids (.npy)")
     ap.add_argument("--load-cent", default=None, help="use these centroids instead of training")
+    ap.add_argument("--rows-seed", type=int, default=None,
+                    help="draw rank r's rows with seed rows_seed + r (default: rank 0 assigns "
+                         "the training rows, rank r > 0 fresh rows drawn with seed r)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -123,6 +123,9 @@ def load():
         "eb_unbind_data": (I, [P]),
         "eb_assign": (I, [P, P, S, S, P, S, P, S, I, P, P]),
         "eb_train": (I, [P, C.POINTER(TrainJob), C.POINTER(TrainOut)]),
+        "eb_group_unique_id": (I, [C.c_char_p]),
+        "eb_engine_join": (I, [P, I, I, C.c_char_p]),
+        "eb_engine_group": (I, [P, C.POINTER(I), C.POINTER(I)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -384,6 +387,26 @@ class Engine:
         _check(load().eb_unbind_data(self.h))
         self._bound = None
 
+    def join(self, rank: int, world: int, group_id: bytes):
+        """Join a multi-GPU group (eb_engine_join); collective over the ranks."""
+        if len(group_id) != GROUP_ID_BYTES:
+            raise ValueError(f"group id must be {GROUP_ID_BYTES} bytes")
+        _check(load().eb_engine_join(self.h, rank, world, group_id))
+
+    def join_torch_group(self):
+        """Join with every rank of the default torch.distributed group: rank 0
+        draws the id and broadcasts it (as bytes) over that group."""
+        import torch.distributed as dist
+        rank, world = dist.get_rank(), dist.get_world_size()
+        box = [group_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        self.join(rank, world, box[0])
+
+    def group(self):
+        r, w = C.c_int(), C.c_int()
+        _check(load().eb_engine_group(self.h, C.byref(r), C.byref(w)))
+        return r.value, w.value
+
     def train(self, x, cfg: Config, init=None, state=None) -> Trained:
         """``Engine::run_train``: the device loop (core/train.rs:60-303)."""
         x = _f32(x).ravel()
@@ -415,6 +438,26 @@ class Engine:
                        nsplit=list(out.nsplit[:ne]), epoch_time=list(out.epoch_time[:ne]),
                        n_splits=out.n_splits, batch_size=out.batch_size, alpha0=out.alpha0,
                        total_steps=out.total_steps)
+
+
+GROUP_ID_BYTES = 128
+
+
+def group_unique_id() -> bytes:
+    """A fresh multi-GPU group id (eb_group_unique_id), made on rank 0."""
+    buf = C.create_string_buffer(GROUP_ID_BYTES)
+    _check(load().eb_group_unique_id(buf))
+    return buf.raw
+
+
+def shard_bounds(b: int, end: int, rank: int, world: int):
+    """The positions [lo, hi) of batch [b, end) that `rank` scores in a group
+    of `world` engines (the split eb_train uses: equal slices of ceil(B/world),
+    the last ones shorter or empty)."""
+    sh = (end - b + world - 1) // world
+    lo = min(b + rank * sh, end)
+    hi = min(lo + sh, end) if world > 1 else end
+    return lo, hi
 
 
 class B200Assigner:

@@ -67,7 +67,7 @@ def build(verbose: bool = False) -> str:
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: compile_one(s, verbose), srcs))
     if not os.path.exists(OUT) or os.path.getmtime(OUT) < max(os.path.getmtime(o) for o in objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-o", OUT, *objs, "-lpthread"]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", OUT, *objs, "-lpthread", "-ldl"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

@@ -181,6 +181,7 @@ int eb_engine_destroy(eb_engine* e) {
   return guard([&] {
     DeviceGuard g(e);
     cudaStreamSynchronize(e->stream);
+    eb::group_leave(e);
     if (e->bound) eb::free_buf(e, e->bound);
     for (auto& kv : e->scratch)
       if (kv.second.p) cudaFreeAsync(kv.second.p, e->stream);

@@ -86,6 +86,10 @@ struct eb_engine {
   int screen_mode = 1;
   // Device counters: [0] unused, [1] fallback rows, [2] re-scored candidates.
   unsigned long long* d_counters = nullptr;
+  // Multi-GPU group (eb_engine_join): an NCCL communicator over one engine per
+  // GPU, or null for a single-GPU engine.
+  void* comm = nullptr;
+  int rank = 0, world = 1;
   unsigned long long* counters() { return d_counters; }
 
   template <class T>
@@ -109,6 +113,19 @@ eb_buf* new_buf(eb_engine* e, int dtype, size_t len);
 void free_buf(eb_engine* e, eb_buf* b);
 void sync(eb_engine* e);  // wait + status check (throws)
 void set_last_error(const std::string& msg);
+
+// Group exchange (nccl.cpp): in-place all-gather of `words` 32-bit words per
+// rank in buf[0 .. world * words) on the engine's stream; rank r's share is
+// buf[r * words ..). Release of the engine's communicator.
+void group_allgather(eb_engine* e, uint32_t* buf, size_t words);
+void group_leave(eb_engine* e);
+// Pack this rank's (labels, scores) slice of len <= s entries into
+// stage[rank * 2s ..) and unpack every rank's slice after the exchange into
+// labels / scores at p0 + q s (ops.cu).
+void shard_pack(eb_engine* e, const uint32_t* labels, const float* scores, size_t len, size_t s,
+                uint32_t* stage);
+void shard_unpack(eb_engine* e, const uint32_t* stage, size_t total, size_t s, int world,
+                  uint32_t* labels, float* scores);
 
 // ---- ops.cu: update ops, bit-equal to the CPU float order
 void row_norms(eb_engine* e, const float* m, size_t rows, size_t d, float* out);

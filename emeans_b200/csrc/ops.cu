@@ -381,3 +381,47 @@ void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_
 }
 
 }  // namespace eb
+
+// ---- multi-GPU batch exchange: (labels, scores) slices through one staging
+// buffer of world x 2s words, all-gathered in place between pack and unpack.
+
+namespace eb {
+namespace {
+
+__global__ void k_shard_pack(const uint32_t* __restrict__ labels, const float* __restrict__ scores,
+                             long len, long s, uint32_t* __restrict__ stage) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= s) return;
+  stage[i] = i < len ? labels[i] : 0u;
+  stage[s + i] = i < len ? __float_as_uint(scores[i]) : 0u;
+}
+
+__global__ void k_shard_unpack(const uint32_t* __restrict__ stage, long total, long s,
+                               uint32_t* __restrict__ labels, float* __restrict__ scores) {
+  const long p = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= total) return;
+  const long q = p / s, i = p - q * s;
+  labels[p] = stage[q * 2 * s + i];
+  scores[p] = __uint_as_float(stage[q * 2 * s + s + i]);
+}
+
+}  // namespace
+
+void shard_pack(eb_engine* e, const uint32_t* labels, const float* scores, size_t len, size_t s,
+                uint32_t* stage) {
+  if (s == 0) return;
+  k_shard_pack<<<blocks_for(s, 256), 256, 0, e->stream>>>(labels, scores, (long)len, (long)s,
+                                                         stage + (size_t)e->rank * 2 * s);
+  EB_LAUNCH("shard_pack");
+}
+
+void shard_unpack(eb_engine* e, const uint32_t* stage, size_t total, size_t s, int world,
+                  uint32_t* labels, float* scores) {
+  (void)world;
+  if (total == 0) return;
+  k_shard_unpack<<<blocks_for(total, 256), 256, 0, e->stream>>>(stage, (long)total, (long)s,
+                                                                labels, scores);
+  EB_LAUNCH("shard_unpack");
+}
+
+}  // namespace eb

@@ -81,7 +81,7 @@ constexpr int A_BYTES = BM * BKH * 2;                // one of xh / xl
 constexpr int B_BYTES = BN * BKH * 2;                // one of ch / cl
 constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
 constexpr int CAP = 64;          // per-row candidate list capacity
-constexpr int SURV = 16;         // candidates per row taken to exact chains
+constexpr int SURV = 64;         // candidates per row taken to exact chains (more: full scan)
 constexpr int NTHREADS = 320;    // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int HALF = BN / 2;     // tile columns per epilogue warp (two warps per TMEM lane quadrant)
 constexpr uint32_t FALLBACK = 0xFFFFFFFFu;

@@ -143,6 +143,8 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   DevBuf dpos(e, EB_F32, k * d), mass(e, EB_F32, k), readout(e, EB_F32, spherical ? k * d : k);
   DevBuf sums(e, EB_F32, k * d), counts(e, EB_U32, k), pass(e, EB_F32, k * d);
   DevBuf pairs(e, EB_U32, 2 * k);
+  // Group exchange staging: world x (labels, scores) slices of a batch.
+  DevBuf stage(e, EB_U32, e->world > 1 ? 2 * ((bsz + e->world - 1) / e->world) * e->world : 1);
   EB_CUDA(cudaMemcpyAsync(dpos.f(), pos.data(), k * d * 4, cudaMemcpyHostToDevice, e->stream));
   EB_CUDA(cudaMemcpyAsync(mass.f(), usage.data(), k * 4, cudaMemcpyHostToDevice, e->stream));
   if (data->d == d && !data->xnorm && !spherical) {
@@ -173,14 +175,19 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
         normalize_rows(e, dpos.f(), k, d, readout.f());
       else
         row_norms(e, dpos.f(), k, d, readout.f());
-      for (size_t c0 = b; c0 < end; c0 += chunk) {
+      // In a group, rank q scores positions [b + q s, b + (q + 1) s) of the
+      // batch and the slices are all-gathered; alone, the whole batch.
+      const size_t sh = (end - b + e->world - 1) / e->world;
+      const size_t lo = std::min(b + (size_t)e->rank * sh, end);
+      const size_t hi = e->world > 1 ? std::min(lo + sh, end) : end;
+      for (size_t c0 = lo; c0 < hi; c0 += chunk) {
         Top1Args a;
         a.x = static_cast<const float*>(data->ptr);
         a.n = n;
         a.d = d;
         a.ids = order.u();
         a.r0 = c0;
-        a.r1 = std::min(c0 + chunk, end);
+        a.r1 = std::min(c0 + chunk, hi);
         a.c = spherical ? readout.f() : dpos.f();
         a.cnorm = spherical ? nullptr : readout.f();
         a.k = k;
@@ -189,6 +196,11 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
         a.scores = scores_ep.f();
         a.xnorm = data->xnorm;
         top1_dispatch(e, a, data);
+      }
+      if (e->world > 1) {
+        shard_pack(e, labels_ep.u() + lo, scores_ep.f() + lo, hi - lo, sh, stage.u());
+        group_allgather(e, stage.u(), 2 * sh);
+        shard_unpack(e, stage.u(), end - b, sh, e->world, labels_ep.u() + b, scores_ep.f() + b);
       }
       scatter_add(e, static_cast<const float*>(data->ptr), n, d, order.u(), b, end, labels_ep.u(),
                   k, sums.f(), counts.u(), last ? pass.f() : nullptr);

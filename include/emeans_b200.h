@@ -222,6 +222,22 @@ typedef struct {
 
 int eb_train(eb_engine* e, const eb_train_job* job, eb_train_out* out);
 
+/* ---------------------------------------------------------------- multi-GPU groups */
+
+/* No counterpart in the reference (its engine is one device). Engines on
+ * several GPUs, one per process or thread, form a group over NCCL: rank 0
+ * calls eb_group_unique_id, the host hands the id to every rank by its own
+ * means, and every rank calls eb_engine_join with it (collectively; it blocks
+ * until all ranks joined). eb_train on a joined engine splits each batch's
+ * top-1 across the ranks and all-gathers the labels and scores, so every rank
+ * computes the same model as one engine alone, bit for bit; all ranks must
+ * call it with the same job. NCCL is loaded when a group is formed. The group
+ * is left when the engine is destroyed. */
+#define EB_GROUP_ID_BYTES 128
+int eb_group_unique_id(unsigned char* id);
+int eb_engine_join(eb_engine* e, int rank, int world, const unsigned char* id);
+int eb_engine_group(eb_engine* e, int* rank, int* world);
+
 /* ---------------------------------------------------------------- no-alloc top-1 */
 
 /* No counterpart in the reference: its CPU path has no device memory to

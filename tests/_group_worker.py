@@ -1,0 +1,51 @@
+"""One rank of the multi-GPU group test (launched by tests/test_gpu_group.py
+under torch.distributed.run): a joined engine trains with the batch top-1
+split across the ranks and the labels/scores all-gathered over NCCL; the
+result must equal, bit for bit, a lone engine's training on the same GPU."""
+
+import datetime
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+import emeans_b200 as eb  # noqa: E402
+from tests.helpers import mixture  # noqa: E402
+
+
+def main():
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+    cases = [
+        # (n, d, k, spherical, seed): the C1 shape and an L2 case with revival
+        (20000, 64, 32, True, 7),
+        (30000, 96, 200, False, 3),
+    ]
+    group = eb.Engine(local)
+    group.join_torch_group()
+    assert group.group() == (rank, world)
+    solo = eb.Engine(local)
+    for n, d, k, spherical, seed in cases:
+        x = mixture(n, d, 24, 0.4, spherical, seed)
+        cfg = eb.Config(d=d, k=k, seed=seed, spherical=spherical, nepochs=2.0)
+        a = group.train(x, cfg)
+        b = solo.train(x, cfg)
+        assert np.array_equal(a.centroids.view(np.uint32), b.centroids.view(np.uint32)), \
+            f"rank {rank}: centroids differ (n={n}, k={k})"
+        assert np.array_equal(a.labels, b.labels), f"rank {rank}: labels differ"
+        assert a.obj == b.obj and a.nsplit == b.nsplit, f"rank {rank}: statistics differ"
+    group.close()
+    solo.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    print(f"rank {rank}: group training equals the lone engine", flush=True)
+
+
+if __name__ == "__main__":
+    main()
