@@ -123,6 +123,10 @@ def load():
         "eb_unbind_data": (I, [P]),
         "eb_assign": (I, [P, P, S, S, P, S, P, S, I, P, P]),
         "eb_train": (I, [P, C.POINTER(TrainJob), C.POINTER(TrainOut)]),
+        "eb_set_kernel_timing": (I, [P, I]),
+        "eb_screen_timing": (I, [P, C.POINTER(C.c_double), C.POINTER(C.c_uint64),
+                                 C.POINTER(C.c_uint64)]),
+        "eb_topk_group": (I, [P, P, S, P, S, S, S, S, S, I, P, P]),
         "eb_group_unique_id": (I, [C.c_char_p]),
         "eb_engine_join": (I, [P, I, I, C.c_char_p]),
         "eb_engine_group": (I, [P, C.POINTER(I), C.POINTER(I)]),
@@ -334,6 +338,18 @@ class Engine:
                               _ptr(ids), _ptr(sims)))
         return ids, sims
 
+    def topk_group(self, queries, shard, shard_offset: int, n_total: int, d: int, kk: int,
+                   exclude_self: bool = False):
+        """eb_topk_group: top-kk over a database sharded across the engine's
+        group (this rank holds rows shard_offset .. + len(shard)); collective."""
+        q, x = _f32(queries).ravel(), _f32(shard).ravel()
+        m, n = q.size // d, x.size // d
+        ids = np.empty(m * kk, np.uint32)
+        sims = np.empty(m * kk, np.float32)
+        _check(load().eb_topk_group(self.h, _ptr(q), m, _ptr(x) if n else None, n, shard_offset,
+                                    n_total, d, kk, int(exclude_self), _ptr(ids), _ptr(sims)))
+        return ids, sims
+
     def scatter_add(self, x: Buffer, d: int, ids: Optional[Buffer], rows: range, labels: Buffer,
                     k: int, sums: Buffer, counts: Buffer, acc: Optional[Buffer] = None):
         _check(load().eb_scatter_add(self.h, x.h, d, ids.h if ids else None, rows.start,
@@ -386,6 +402,17 @@ class Engine:
     def unbind_data(self):
         _check(load().eb_unbind_data(self.h))
         self._bound = None
+
+    def set_kernel_timing(self, on: bool):
+        """Bracket every top-1 screen launch with CUDA events (measurement)."""
+        _check(load().eb_set_kernel_timing(self.h, int(bool(on))))
+
+    def screen_timing(self):
+        """(summed device ms, launches, rows) of the screen launches since the
+        last call; waits for queued work."""
+        ms, n, r = C.c_double(), C.c_uint64(), C.c_uint64()
+        _check(load().eb_screen_timing(self.h, C.byref(ms), C.byref(n), C.byref(r)))
+        return ms.value, n.value, r.value
 
     def join(self, rank: int, world: int, group_id: bytes):
         """Join a multi-GPU group (eb_engine_join); collective over the ranks."""
@@ -448,6 +475,23 @@ def group_unique_id() -> bytes:
     buf = C.create_string_buffer(GROUP_ID_BYTES)
     _check(load().eb_group_unique_id(buf))
     return buf.raw
+
+
+def merge_topk(lists, kk: int):
+    """The group top-k merge rule (k_topk_merge) on the host: per query, the
+    best kk of the ranks' (ids, sims) lists by (larger score, then lower id),
+    missing entries (id 0xFFFFFFFF) dropped and padded back at the end."""
+    m = lists[0][0].size // kk
+    ids = np.full(m * kk, 0xFFFFFFFF, np.uint32)
+    sims = np.full(m * kk, -np.inf, np.float32)
+    for qi in range(m):
+        cand = [(float(s[qi * kk + t]), int(i[qi * kk + t])) for i, s in lists for t in range(kk)
+                if i[qi * kk + t] != 0xFFFFFFFF]
+        cand.sort(key=lambda c: (-c[0], c[1]))
+        for t, (v, j) in enumerate(cand[:kk]):
+            ids[qi * kk + t] = j
+            sims[qi * kk + t] = v
+    return ids, sims
 
 
 def shard_bounds(b: int, end: int, rank: int, world: int):

@@ -182,6 +182,10 @@ int eb_engine_destroy(eb_engine* e) {
     DeviceGuard g(e);
     cudaStreamSynchronize(e->stream);
     eb::group_leave(e);
+    for (auto& ev : e->screen_ev) {
+      cudaEventDestroy(ev.first);
+      cudaEventDestroy(ev.second);
+    }
     if (e->bound) eb::free_buf(e, e->bound);
     for (auto& kv : e->scratch)
       if (kv.second.p) cudaFreeAsync(kv.second.p, e->stream);
@@ -235,6 +239,36 @@ int eb_get_stats(eb_engine* e, eb_stats* out) {
     *out = e->stats;
     out->fallback_rows = c[1];
     out->rescored_candidates = c[2];
+  });
+}
+
+int eb_set_kernel_timing(eb_engine* e, int on) {
+  return guard([&] {
+    need(e, "engine");
+    e->time_screen = on != 0;
+  });
+}
+
+int eb_screen_timing(eb_engine* e, double* total_ms, uint64_t* launches, uint64_t* rows) {
+  return guard([&] {
+    need(e, "engine");
+    need(total_ms, "total_ms");
+    need(launches, "launches");
+    need(rows, "rows");
+    DeviceGuard g(e);
+    eb::sync(e);
+    double ms = 0.0;
+    uint64_t r = 0;
+    for (size_t u = 0; u < e->screen_ev_used; u++) {
+      float t = 0.0f;
+      EB_CUDA(cudaEventElapsedTime(&t, e->screen_ev[u].first, e->screen_ev[u].second));
+      ms += t;
+      r += e->screen_ev_rows[u];
+    }
+    *total_ms = ms;
+    *launches = e->screen_ev_used;
+    *rows = r;
+    e->screen_ev_used = 0;
   });
 }
 
@@ -421,6 +455,27 @@ int eb_topk(eb_engine* e, const float* queries, size_t m, const float* data, siz
     need(sims, "sims");
     DeviceGuard g(e);
     eb::topk(e, queries, m, data, n, d, kk, exclude_self != 0, ids, sims);
+  });
+}
+
+int eb_topk_group(eb_engine* e, const float* queries, size_t m, const float* shard,
+                  size_t n_shard, size_t shard_offset, size_t n_total, size_t d, size_t kk,
+                  int exclude_self, uint32_t* ids, float* sims) {
+  return guard([&] {
+    need(e, "engine");
+    ensure(d > 0, "d must be positive");
+    ensure(kk >= 1 && kk <= 16, "kk must be 1..=16");
+    ensure(n_total > 0 && n_total <= 0xFFFFFFFEull, "n_total must be in 1 .. 2^32 - 2");
+    ensure(shard_offset + n_shard <= n_total, "shard past the data");
+    ensure(!exclude_self || m == n_total, "exclude_self needs queries == data");
+    if (m == 0) return;
+    need(queries, "queries");
+    if (n_shard) need(shard, "shard");
+    need(ids, "ids");
+    need(sims, "sims");
+    DeviceGuard g(e);
+    eb::topk(e, queries, m, shard, n_shard, d, kk, exclude_self != 0, ids, sims, shard_offset,
+             true);
   });
 }
 

@@ -90,6 +90,13 @@ struct eb_engine {
   // GPU, or null for a single-GPU engine.
   void* comm = nullptr;
   int rank = 0, world = 1;
+  // Optional CUDA-event timing of the top-1 screen kernel (eb_set_kernel_timing):
+  // one (start, end) pair per launch since the last eb_screen_timing read,
+  // with the rows of that launch.
+  bool time_screen = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> screen_ev;
+  std::vector<size_t> screen_ev_rows;
+  size_t screen_ev_used = 0;
   unsigned long long* counters() { return d_counters; }
 
   template <class T>
@@ -169,6 +176,7 @@ void drop_f16(eb_buf* b);
 
 // ---- topk.cu
 void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, size_t d,
-          size_t kk, bool exclude_self, uint32_t* ids, float* sims);
+          size_t kk, bool exclude_self, uint32_t* ids, float* sims, size_t id0 = 0,
+          bool collective = false);
 
 }  // namespace eb

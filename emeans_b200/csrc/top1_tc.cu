@@ -1548,11 +1548,26 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
     P.m = (long)m;
     // Persistent: at most one CTA per SM, each looping over row tiles.
     const unsigned grid = (unsigned)std::min<size_t>((m + BM - 1) / BM, (size_t)e->num_sms);
+    cudaEvent_t ev_end = nullptr;
+    if (e->time_screen) {
+      if (e->screen_ev_used == e->screen_ev.size()) {
+        cudaEvent_t a, b;
+        EB_CUDA(cudaEventCreate(&a));
+        EB_CUDA(cudaEventCreate(&b));
+        e->screen_ev.emplace_back(a, b);
+        e->screen_ev_rows.push_back(0);
+      }
+      const size_t u = e->screen_ev_used++;
+      e->screen_ev_rows[u] = m;
+      EB_CUDA(cudaEventRecord(e->screen_ev[u].first, e->stream));
+      ev_end = e->screen_ev[u].second;
+    }
     if (ip)
       launch_screen<true>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
     else
       launch_screen<false>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
     EB_LAUNCH("screen");
+    if (ev_end) EB_CUDA(cudaEventRecord(ev_end, e->stream));
     if (ip)
       launch_exact<true>(e, a, (long)c0, (long)m, S);
     else

@@ -15,7 +15,7 @@ constexpr int BM = 64, BN = 64, BK = 16, NT = 256, KMAX = 16;
 
 __global__ void __launch_bounds__(NT) k_topk_exact(const float* __restrict__ q, long m,
                                                    const float* __restrict__ data, long n, int d,
-                                                   int kk, int exclude_self,
+                                                   int kk, int exclude_self, long id0,
                                                    uint32_t* __restrict__ out_ids,
                                                    float* __restrict__ out_sims) {
   __shared__ __align__(16) float As[BK][BM + 4];
@@ -91,7 +91,8 @@ __global__ void __launch_bounds__(NT) k_topk_exact(const float* __restrict__ q, 
       long qi = q0 + tid;
       int cols = (int)min((long)BN, n - n0);
       for (int j = 0; j < cols; j++) {
-        uint32_t col = (uint32_t)(n0 + j);
+        // Data row n0 + j has the global id id0 + n0 + j (a shard's offset).
+        uint32_t col = (uint32_t)(id0 + n0 + j);
         if (exclude_self && (long)col == qi) continue;
         float v = S[tid][j];
         if (!(v > ls[KMAX - 1])) continue;
@@ -123,20 +124,79 @@ __global__ void __launch_bounds__(NT) k_topk_exact(const float* __restrict__ q, 
   }
 }
 
+// Merge of the ranks' lists after the all-gather: per query, the best kk of
+// world x kk candidates by (larger score, then lower id); the shards' ids are
+// disjoint, and missing entries (0xFFFFFFFF) never enter.
+__global__ void k_topk_merge(const uint32_t* __restrict__ stage, long m, int kk, int world,
+                             uint32_t* __restrict__ out_ids, float* __restrict__ out_sims) {
+  const long qi = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (qi >= m) return;
+  float ls[KMAX];
+  uint32_t li[KMAX];
+#pragma unroll
+  for (int i = 0; i < KMAX; i++) {
+    ls[i] = -INFINITY;
+    li[i] = 0xFFFFFFFFu;
+  }
+  const long per = 2 * m * (long)kk;  // words per rank: ids then sims
+  for (int r = 0; r < world; r++) {
+    const uint32_t* ids = stage + r * per;
+    const float* sims = reinterpret_cast<const float*>(stage + r * per + m * (long)kk);
+    for (int t = 0; t < kk; t++) {
+      const uint32_t cj0 = ids[qi * kk + t];
+      if (cj0 == 0xFFFFFFFFu) break;  // lists are best first: the rest are missing too
+      float cv = sims[qi * kk + t];
+      uint32_t cj = cj0;
+#pragma unroll
+      for (int i = 0; i < KMAX; i++) {
+        const bool b = cv > ls[i] || (cv == ls[i] && cj < li[i]);
+        const float tv = ls[i];
+        const uint32_t tj = li[i];
+        ls[i] = b ? cv : tv;
+        li[i] = b ? cj : tj;
+        cv = b ? tv : cv;
+        cj = b ? tj : cj;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < KMAX; i++) {
+    if (i < kk) {
+      out_ids[qi * kk + i] = li[i];
+      out_sims[qi * kk + i] = li[i] == 0xFFFFFFFFu ? -INFINITY : ls[i];
+    }
+  }
+}
+
 }  // namespace
 
 void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, size_t d,
-          size_t kk, bool exclude_self, uint32_t* ids, float* sims) {
+          size_t kk, bool exclude_self, uint32_t* ids, float* sims, size_t id0,
+          bool collective) {
   float* dq = e->scratch_get<float>("tk_q", m * d);
   float* dd = e->scratch_get<float>("tk_data", n * d);
-  uint32_t* di = e->scratch_get<uint32_t>("tk_ids", m * kk);
-  float* ds = e->scratch_get<float>("tk_sims", m * kk);
+  const bool group = collective && e->world > 1;
+  // In a group the local lists land in this rank's share of the exchange
+  // buffer (ids, then sims), which is all-gathered and merged.
+  uint32_t* stage = group ? e->scratch_get<uint32_t>("tk_stage", (size_t)e->world * 2 * m * kk)
+                          : nullptr;
+  uint32_t* di = group ? stage + (size_t)e->rank * 2 * m * kk
+                       : e->scratch_get<uint32_t>("tk_ids", m * kk);
+  float* ds = group ? reinterpret_cast<float*>(di + m * kk) : e->scratch_get<float>("tk_sims", m * kk);
   EB_CUDA(cudaMemcpyAsync(dq, q, m * d * 4, cudaMemcpyHostToDevice, e->stream));
-  EB_CUDA(cudaMemcpyAsync(dd, data, n * d * 4, cudaMemcpyHostToDevice, e->stream));
+  if (n) EB_CUDA(cudaMemcpyAsync(dd, data, n * d * 4, cudaMemcpyHostToDevice, e->stream));
   unsigned grid = (unsigned)((m + BM - 1) / BM);
   k_topk_exact<<<grid, NT, 0, e->stream>>>(dq, (long)m, dd, (long)n, (int)d, (int)kk,
-                                           exclude_self ? 1 : 0, di, ds);
+                                           exclude_self ? 1 : 0, (long)id0, di, ds);
   EB_LAUNCH("topk");
+  if (group) {
+    group_allgather(e, stage, 2 * m * kk);
+    di = e->scratch_get<uint32_t>("tk_ids", m * kk);
+    ds = e->scratch_get<float>("tk_sims", m * kk);
+    k_topk_merge<<<(unsigned)((m + 127) / 128), 128, 0, e->stream>>>(stage, (long)m, (int)kk,
+                                                                     e->world, di, ds);
+    EB_LAUNCH("topk merge");
+  }
   EB_CUDA(cudaMemcpyAsync(ids, di, m * kk * 4, cudaMemcpyDeviceToHost, e->stream));
   EB_CUDA(cudaMemcpyAsync(sims, ds, m * kk * 4, cudaMemcpyDeviceToHost, e->stream));
   sync(e);

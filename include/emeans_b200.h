@@ -102,6 +102,13 @@ int eb_get_stats(eb_engine* e, eb_stats* out);
  * environment variable EMEANS_B200_SCREEN=0/1/2 sets it at engine creation. */
 int eb_set_screen_mode(eb_engine* e, int mode);
 
+/* No counterpart in the reference (measurement only). With timing on, every
+ * launch of the top-1 tensor-core screen kernel is bracketed by CUDA events on
+ * the engine's stream; eb_screen_timing waits for queued work and returns the
+ * launches since the last read, their summed device time and their rows. */
+int eb_set_kernel_timing(eb_engine* e, int on);
+int eb_screen_timing(eb_engine* e, double* total_ms, uint64_t* launches, uint64_t* rows);
+
 /* ---------------------------------------------------------------- buffers */
 
 /* Device::zeros_f32 / zeros_u32 (core/mod.rs:84-85): a zeroed buffer of `len`
@@ -237,6 +244,18 @@ int eb_train(eb_engine* e, const eb_train_job* job, eb_train_out* out);
 int eb_group_unique_id(unsigned char* id);
 int eb_engine_join(eb_engine* e, int rank, int world, const unsigned char* id);
 int eb_engine_group(eb_engine* e, int* rank, int* world);
+
+/* Device::topk over a database sharded across a group (knn_self over several
+ * GPUs, crates/emeans-cluster/src/knn.rs:17-64): every rank passes the same m
+ * queries and its own shard, rows shard_offset .. shard_offset + n_shard of an
+ * n_total-row database; each ranks its shard (global ids), the lists are
+ * all-gathered over NCCL and merged on the device by (larger score, then lower
+ * id), so every rank gets the top-kk of eb_topk over the whole database. With
+ * exclude_self, query i is database row i. Collective: all ranks call it. On
+ * an engine that is not in a group it ranks the one shard alone. */
+int eb_topk_group(eb_engine* e, const float* queries, size_t m, const float* shard,
+                  size_t n_shard, size_t shard_offset, size_t n_total, size_t d, size_t kk,
+                  int exclude_self, uint32_t* ids, float* sims);
 
 /* ---------------------------------------------------------------- no-alloc top-1 */
 

@@ -1,7 +1,8 @@
 """One rank of the multi-GPU group test (launched by tests/test_gpu_group.py
 under torch.distributed.run): a joined engine trains with the batch top-1
-split across the ranks and the labels/scores all-gathered over NCCL; the
-result must equal, bit for bit, a lone engine's training on the same GPU."""
+split across the ranks and the labels/scores all-gathered over NCCL, and
+ranks a sharded database with eb_topk_group; both must equal, bit for bit, a
+lone engine's results on the same GPU."""
 
 import datetime
 import os
@@ -40,6 +41,18 @@ def main():
             f"rank {rank}: centroids differ (n={n}, k={k})"
         assert np.array_equal(a.labels, b.labels), f"rank {rank}: labels differ"
         assert a.obj == b.obj and a.nsplit == b.nsplit, f"rank {rank}: statistics differ"
+    # knn_self over a database sharded across the ranks, against one engine
+    # ranking the whole database.
+    rng = np.random.default_rng(11)
+    n, d, kk = 5003, 48, 10
+    data = rng.standard_normal((n, d)).astype(np.float32)
+    data[4000:4010] = data[10:20]  # duplicates across the shards
+    lo, hi = eb.shard_bounds(0, n, rank, world)
+    for exclude_self in (True, False):
+        gi, gs = group.topk_group(data, data[lo:hi], lo, n, d, kk, exclude_self)
+        si, ss = solo.topk(data, data, d, kk, exclude_self)
+        assert np.array_equal(gi, si), f"rank {rank}: knn ids differ"
+        assert np.array_equal(gs.view(np.uint32), ss.view(np.uint32)), f"rank {rank}: knn sims differ"
     group.close()
     solo.close()
     dist.barrier()

@@ -1,10 +1,17 @@
-"""The multi-GPU split and exchange, checked on CPU with two gloo ranks.
+"""The multi-GPU split, exchange and merge, checked on CPU with two gloo ranks.
 
 eb_train in a group splits every batch's top-1 into equal slices of
 ceil(B / world) positions (emeans_b200.shard_bounds mirrors that split) and
 all-gathers the slices' labels and scores. Here each gloo rank scores its
 slice with the CPU oracle and all-gathers it; the assembled batch must equal
 the oracle over the whole batch, for batch sizes that do not divide evenly.
+
+eb_topk_group ranks each rank's database shard with global ids, all-gathers
+the lists and merges them by (larger score, then lower id); here each rank
+ranks its shard with the oracle, the lists are all-gathered over gloo and
+merged by the same rule (emeans_b200.merge_topk), and the result must equal
+the oracle's top-k over the whole database, duplicate rows across the shards
+included (equal scores: the lower id wins).
 """
 
 import datetime
@@ -70,16 +77,58 @@ def _rank(rank, world, port, q):
         q.put((rank, repr(exc)))
 
 
-@pytest.mark.timeout(180)
-def test_two_gloo_ranks_assemble_the_batch():
-    world = 2
+def _knn_rank(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        rng = np.random.default_rng(9)
+        n, d, m, kk = 2001, 16, 150, 10
+        data = rng.standard_normal((n, d)).astype(np.float32)
+        data[1500:1520] = data[100:120]  # exact duplicates in the other shard
+        queries = np.concatenate([data[:50], rng.standard_normal((m - 50, d)).astype(np.float32)])
+        lo, hi = eb.shard_bounds(0, n, rank, world)
+        ids, sims = oracle.topk(queries.ravel(), data[lo:hi].ravel(), d, kk)
+        ids = np.where(ids == 0xFFFFFFFF, ids, ids + np.uint32(lo)).astype(np.uint32)
+        mine = torch.from_numpy(np.concatenate([ids.astype(np.int64),
+                                                sims.view(np.uint32).astype(np.int64)]))
+        parts = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(parts, mine)
+        lists = []
+        for p in parts:
+            a = p.numpy()
+            lists.append((a[:m * kk].astype(np.uint32),
+                          a[m * kk:].astype(np.uint32).view(np.float32)))
+        got_i, got_s = eb.merge_topk(lists, kk)
+        want_i, want_s = oracle.topk(queries.ravel(), data.ravel(), d, kk)
+        ok = np.array_equal(got_i, want_i) and np.array_equal(got_s.view(np.uint32),
+                                                              want_s.view(np.uint32))
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, bool(ok)))
+    except Exception as exc:  # report instead of hanging the parent
+        q.put((rank, repr(exc)))
+
+
+def _run_ranks(target, world=2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=150) for _ in range(world))
     for p in procs:
         p.join(timeout=30)
+    return results
+
+
+@pytest.mark.timeout(180)
+def test_two_gloo_ranks_merge_sharded_topk():
+    assert _run_ranks(_knn_rank) == {0: True, 1: True}
+
+
+@pytest.mark.timeout(180)
+def test_two_gloo_ranks_assemble_the_batch():
+    results = _run_ranks(_rank)
     assert results == {0: True, 1: True}, results
