@@ -82,7 +82,12 @@ constexpr int B_BYTES = BN * BKH * 2;                // one of ch / cl
 constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
 constexpr int CAP = 64;          // per-row candidate list capacity
 constexpr int SURV = 64;         // candidates per row taken to exact chains (more: full scan)
-constexpr int NTHREADS = 320;    // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+// Three warpgroups: warp 0 TMA, warp 1 MMA (warps 2-3 idle), warps 4-11 epilogue.
+// Launched at 168 registers a thread; the first warpgroup gives its registers
+// to the epilogue (setmaxnreg: 128 x 56 + 256 x 224 = 384 x 168).
+constexpr int NTHREADS = 384;
+constexpr int REG_PRODUCER = 56, REG_EPILOGUE = 224;
+static_assert(128 * REG_PRODUCER + 256 * REG_EPILOGUE <= NTHREADS * 168, "register split");
 constexpr int HALF = BN / 2;     // tile columns per epilogue warp (two warps per TMEM lane quadrant)
 constexpr uint32_t FALLBACK = 0xFFFFFFFFu;
 constexpr int XEXP_BAD = INT_MIN;  // row with a non-finite value
@@ -204,6 +209,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
         "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// An empty statement that takes registers loaded from TMEM as operands: placed
+// after tmem_wait(), it keeps the compiler from moving their uses above it.
+__device__ __forceinline__ void tmem_tie(uint32_t (&a)[16]) {
+  asm volatile(""
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]),
+                 "+r"(a[6]), "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]),
+                 "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]));
 }
 // Wait for this thread's TMEM loads. The registers of the group just loaded
 // are tied to the wait (and to an empty statement after it), so the compiler
@@ -518,7 +534,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;  // hi accumulator at column 0, lo at column BN
   const int total = P.ntiles * P.kblocks;
-
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_PRODUCER));
   if (warp == 0) {
     if (lane == 0) {
       // TMA producer: per (row tile, centroid tile, k-block) the four boxes
@@ -596,20 +613,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       while (!mbar_try_wait(mma_done, 0) && now_ns() - t0 < WAIT_NS) {
       }
     }
+  }
   } else {
-    // Epilogue: warps 2-9. Warp w reads TMEM lanes 32 (w % 4) .. + 31 (one
-    // row per thread) and half (w - 2) / 4 of every tile's columns; each
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_EPILOGUE));
+    // Epilogue: warps 4-11. Warp w reads TMEM lanes 32 (w % 4) .. + 31 (one
+    // row per thread) and half (w - 4) / 4 of every tile's columns; each
     // (row, half) keeps its own running best and candidate list.
     const int q = warp & 3;
-    const int hf = (warp - 2) >> 2;
+    const int hf = (warp - 4) >> 2;
     const int r = q * 32 + lane;
     int ec = 0;
     frexpf(__uint_as_float(P.cinfo[0]), &ec);
     const float cmax = __uint_as_float(P.cinfo[1]);
     const bool c_bad = P.cinfo[2] != 0;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(hf * HALF);
-    float* cns = cn_s + (warp - 2) * HALF;
-    float* svs = sv_s + (warp - 2) * 16 * 32 + lane;  // this lane's column of the slab
+    float* cns = cn_s + (warp - 4) * HALF;
+    float* svs = sv_s + (warp - 4) * 16 * 32 + lane;  // this lane's column of the slab
     int tc = 0;
     bool stop = false;
     for (long rt = blockIdx.x; rt * BM < P.m; rt += gridDim.x) {
@@ -667,23 +686,43 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           __syncwarp();
         }
         const int ngr = max(0, min(HALF / 16, (P.k - col0 + 15) / 16));
-        // Software pipeline over 16-column groups: group g + 1's TMEM loads are
-        // in flight while group g is scored.
-        uint32_t vh[2][16], vl[2][16];
-        if (ngr > 0) {
-          tmem_ld16(lane_base, vh[0]);
-          tmem_ld16(lane_base + BN, vl[0]);
+        // Drain: this thread's half-tile row (hi in acc, lo added group pair by
+        // group pair) comes into registers and the accumulators are released
+        // at once, so that the next tile's products run while this one is
+        // scored.
+        uint32_t acc[HALF / 16][16];
+        {
+          uint32_t lo[2][16];
+#pragma unroll
+          for (int g = 0; g < HALF / 16; g++)
+            if (g < ngr) tmem_ld16(lane_base + (uint32_t)(g * 16), acc[g]);
+#pragma unroll
+          for (int p2 = 0; p2 < HALF / 32; p2++) {
+#pragma unroll
+            for (int h2 = 0; h2 < 2; h2++)
+              if (2 * p2 + h2 < ngr)
+                tmem_ld16(lane_base + (uint32_t)(BN + (2 * p2 + h2) * 16), lo[h2]);
+            tmem_wait();
+            if (p2 == 0) {
+#pragma unroll
+              for (int g = 0; g < HALF / 16; g++) tmem_tie(acc[g]);
+            }
+            tmem_tie(lo[0]);
+            tmem_tie(lo[1]);
+#pragma unroll
+            for (int h2 = 0; h2 < 2; h2++)
+#pragma unroll
+              for (int j = 0; j < 16; j++)
+                acc[2 * p2 + h2][j] = __float_as_uint(
+                    __fadd_rn(__uint_as_float(acc[2 * p2 + h2][j]), __uint_as_float(lo[h2][j])));
+          }
         }
+        tc_fence_before();
+        mbar_arrive(tempty);
 #pragma unroll
         for (int g = 0; g < HALF / 16; g++) {
           if (g >= ngr) break;
-          uint32_t(&h)[16] = vh[g & 1];
-          uint32_t(&l)[16] = vl[g & 1];
-          tmem_wait_tied(h, l);
-          if (g + 1 < ngr) {
-            tmem_ld16(lane_base + (uint32_t)((g + 1) * 16), vh[(g + 1) & 1]);
-            tmem_ld16(lane_base + (uint32_t)(BN + (g + 1) * 16), vl[(g + 1) & 1]);
-          }
+          const uint32_t(&h)[16] = acc[g];
           float s[16];
           const float4* c4 = reinterpret_cast<const float4*>(cns + g * 16);
 #pragma unroll
@@ -692,8 +731,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
 #pragma unroll
             for (int w = 0; w < 4; w++) {
-              const float acc = __fadd_rn(__uint_as_float(h[j + w]), __uint_as_float(l[j + w]));
-              s[j + w] = IP ? acc : __fmaf_rn(m2f, acc, cc[w]);
+              const float v = __uint_as_float(h[j + w]);  // hi + lo, added in the drain
+              s[j + w] = IP ? v : __fmaf_rn(m2f, v, cc[w]);
             }
           }
           const int lim = P.k - (col0 + g * 16);
@@ -739,8 +778,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             __syncwarp();
           }
         }
-        tc_fence_before();
-        mbar_arrive(tempty);
       }
       if (live) {
         // With k <= HALF the second half tile holds no centroid at all: its
