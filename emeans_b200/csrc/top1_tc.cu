@@ -646,7 +646,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const float xs = ldexpf(xn, 14 - (fallback ? 0 : ex));
       const float cs = ldexpf(cmax, 14 - ec);
       const float e_acc = fmaf(P.e_rel * xs, cs, fmaf(P.e_abs, xs + cs, P.e_min));
-      float off, m2f = 0.0f;
+      float off, m2f = 1.0f;  // screened value = m2f acc + cn (IP: acc + 0)
       if (IP) {
         off = 2.0f * e_acc;
       } else {
@@ -690,31 +690,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // group pair) comes into registers and the accumulators are released
         // at once, so that the next tile's products run while this one is
         // scored.
+        constexpr int LOG = 2;  // lo groups per TMEM wait
         uint32_t acc[HALF / 16][16];
         {
-          uint32_t lo[2][16];
+          uint32_t lo[LOG][16];
 #pragma unroll
           for (int g = 0; g < HALF / 16; g++)
             if (g < ngr) tmem_ld16(lane_base + (uint32_t)(g * 16), acc[g]);
 #pragma unroll
-          for (int p2 = 0; p2 < HALF / 32; p2++) {
+          for (int p2 = 0; p2 < HALF / 16 / LOG; p2++) {
 #pragma unroll
-            for (int h2 = 0; h2 < 2; h2++)
-              if (2 * p2 + h2 < ngr)
-                tmem_ld16(lane_base + (uint32_t)(BN + (2 * p2 + h2) * 16), lo[h2]);
+            for (int h2 = 0; h2 < LOG; h2++)
+              if (LOG * p2 + h2 < ngr)
+                tmem_ld16(lane_base + (uint32_t)(BN + (LOG * p2 + h2) * 16), lo[h2]);
             tmem_wait();
             if (p2 == 0) {
 #pragma unroll
               for (int g = 0; g < HALF / 16; g++) tmem_tie(acc[g]);
             }
-            tmem_tie(lo[0]);
-            tmem_tie(lo[1]);
 #pragma unroll
-            for (int h2 = 0; h2 < 2; h2++)
+            for (int h2 = 0; h2 < LOG; h2++) tmem_tie(lo[h2]);
+#pragma unroll
+            for (int h2 = 0; h2 < LOG; h2++)
 #pragma unroll
               for (int j = 0; j < 16; j++)
-                acc[2 * p2 + h2][j] = __float_as_uint(
-                    __fadd_rn(__uint_as_float(acc[2 * p2 + h2][j]), __uint_as_float(lo[h2][j])));
+                acc[LOG * p2 + h2][j] = __float_as_uint(__fadd_rn(
+                    __uint_as_float(acc[LOG * p2 + h2][j]), __uint_as_float(lo[h2][j])));
           }
         }
         tc_fence_before();
@@ -732,7 +733,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int w = 0; w < 4; w++) {
               const float v = __uint_as_float(h[j + w]);  // hi + lo, added in the drain
-              s[j + w] = IP ? v : __fmaf_rn(m2f, v, cc[w]);
+              s[j + w] = __fmaf_rn(m2f, v, cc[w]);
             }
           }
           const int lim = P.k - (col0 + g * 16);

@@ -196,3 +196,21 @@ def test_assign_host_api(eng, metric):
     eng.unbind_data()
     wl, ws = oracle.top1(x.ravel(), d, c.ravel(), metric, ids=ids)
     assert np.array_equal(gl, wl) and np.array_equal(bits(gs), bits(ws))
+
+
+@pytest.mark.parametrize("metric", [eb.IP, eb.L2])
+def test_assign_only_config_shape(engine, metric):
+    """The assign-only config's shape, scaled in rows: unit rows and k = 65,536
+    unit centroids drawn the same way, d = 1024 (256 centroid tiles per row
+    tile, candidate lists compacted many times)."""
+    engine.set_screen_mode(1)
+    d, k, n = 1024, 65536, 3000
+    rng = np.random.default_rng(1)
+    c = rng.standard_normal((k, d), dtype=np.float32)
+    c /= np.linalg.norm(c, axis=1, keepdims=True)
+    x = rng.standard_normal((n, d), dtype=np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    s0 = engine.stats()
+    check_against_oracle(engine, x, c, metric)
+    s1 = engine.stats()
+    assert s1["screened_rows"] - s0["screened_rows"] == n
