@@ -178,5 +178,15 @@ void drop_f16(eb_buf* b);
 void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, size_t d,
           size_t kk, bool exclude_self, uint32_t* ids, float* sims, size_t id0 = 0,
           bool collective = false);
+// Exact top-kk of L device-resident queries against n device-resident data
+// rows, results on the device (topk.cu).
+void topk_exact_device(eb_engine* e, const float* q, size_t L, const uint32_t* qids,
+                       const float* data, size_t n, size_t d, size_t kk, bool exclude_self,
+                       uint32_t* ids, float* sims, size_t id0);
+// Top-kk on the tensor-core screen (top1_tc.cu): queries and data on the
+// device, data row j with global id id0 + j; results (global ids) on the
+// device. False when the call is not one it takes.
+bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size_t n, size_t d,
+                 size_t kk, bool exclude_self, uint32_t* ids, float* sims, size_t id0);
 
 }  // namespace eb

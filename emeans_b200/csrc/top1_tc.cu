@@ -82,6 +82,7 @@ constexpr int B_BYTES = BN * BKH * 2;                // one of ch / cl
 constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
 constexpr int CAP = 64;          // per-row candidate list capacity
 constexpr int SURV = 64;         // candidates per row taken to exact chains (more: full scan)
+constexpr int KMAX = 16;         // largest k of the top-k mode
 // Three warpgroups: warp 0 TMA, warp 1 MMA (warps 2-3 idle), warps 4-11 epilogue.
 // Launched at 168 registers a thread; the first warpgroup gives its registers
 // to the epilogue (setmaxnreg: 128 x 56 + 256 x 224 = 384 x 168).
@@ -491,9 +492,17 @@ struct ScreenParams {
   uint32_t* cand_cnt;  // 2 m: entries in use per (half, row), or FALLBACK
   float* cand_thr;     // 2 m: the final admission threshold per (half, row)
   uint32_t* status;
+  // Top-k mode (k_screen<true, true>): each (row, half) keeps its best kk
+  // screened values and admits every column within the window of the kk-th.
+  int kk;
+  int exclude_self;    // skip the column whose id is the row's global id
+  long row_gid0;       // global id of staging row 0
+  long col_gid0;       // global id of column 0 (a database shard's offset)
+  float* kvals;        // 2 m x KMAX: each (half, row)'s best kk values, descending
+  float* roff;         // m: each row's window 2e
 };
 
-template <bool IP>
+template <bool IP, bool TOPK = false>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_screen(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
              const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
@@ -665,6 +674,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool overflow = false;
       uint32_t cnt = 0;  // entries in this (row, half)'s candidate list
       uint2* row_list = P.cand + (long)hf * CAP * P.m + (live ? i : 0);  // entries P.m apart
+      // Top-k mode: the best kk screened values so far, descending (slots past
+      // kk stay -inf), and the kk-th of them.
+      float kv[TOPK ? KMAX : 1];
+#pragma unroll
+      for (int a = 0; a < (TOPK ? KMAX : 1); a++) kv[a] = -INFINITY;
+      float kth = -INFINITY;
+      const long gid = P.row_gid0 + i;
 
       for (int nt = 0; nt < P.ntiles; nt++, tc++) {
         // Warp-uniform: the TMEM loads below are .sync.aligned.
@@ -742,6 +758,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int j = 0; j < 16; j++)
               if (j >= lim) s[j] = IP ? -INFINITY : INFINITY;
           }
+          if (TOPK && P.exclude_self) {
+            const long rel = gid - (P.col_gid0 + col0 + g * 16);  // the row's own column
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+              if (rel == j) s[j] = -INFINITY;
+          }
           // The group's best moves the threshold first.
           float t[8];
 #pragma unroll
@@ -750,13 +772,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int w2 = 4; w2 >= 1; w2 >>= 1)
 #pragma unroll
             for (int j = 0; j < w2; j++) t[j] = IP ? fmaxf(t[j], t[j + w2]) : fminf(t[j], t[j + w2]);
-          if (IP ? (t[0] > best) : (t[0] < best)) {
+          if constexpr (TOPK) {
+            // Columns above the kk-th best enter the best-kk values (rare once
+            // the row has seen a few tiles), read back from the warp's slab.
+            const bool upd = collect && t[0] > kth;
+            if (__any_sync(0xFFFFFFFFu, upd)) {
+#pragma unroll
+              for (int j = 0; j < 16; j++) svs[j * 32] = s[j];
+              __syncwarp();
+              if (upd) {
+                uint32_t m_up = 0;
+#pragma unroll
+                for (int j = 0; j < 16; j++) m_up |= (uint32_t)(s[j] > kth) << j;
+                while (m_up) {
+                  const int j = __ffs(m_up) - 1;
+                  m_up &= m_up - 1;
+                  float cv = svs[j * 32];
+                  if (!(cv > kth)) continue;
+#pragma unroll
+                  for (int a = 0; a < KMAX; a++) {
+                    const bool b = a < P.kk && cv > kv[a];
+                    const float tv = kv[a];
+                    kv[a] = b ? cv : tv;
+                    cv = b ? tv : cv;
+                  }
+                  float kt = kv[0];
+#pragma unroll
+                  for (int a = 1; a < KMAX; a++)
+                    if (a == P.kk - 1) kt = kv[a];
+                  kth = kt;
+                }
+              }
+              __syncwarp();
+            }
+            thr = kth > -INFINITY ? __fsub_rd(kth, off) : -INFINITY;
+          } else if (IP ? (t[0] > best) : (t[0] < best)) {
             best = t[0];
             thr = IP ? __fsub_rd(best, off) : __fadd_ru(best, off);
           }
           uint32_t adm = 0;
 #pragma unroll
-          for (int j = 0; j < 16; j++) adm |= (uint32_t)(IP ? (s[j] >= thr) : (s[j] <= thr)) << j;
+          for (int j = 0; j < 16; j++)
+            adm |= (uint32_t)(TOPK ? (s[j] >= thr && s[j] > -INFINITY)
+                                   : (IP ? (s[j] >= thr) : (s[j] <= thr))) << j;
           if (!collect) adm = 0;
           // Appends: the warp stages the group's values in its slab only when
           // some lane admits a column; each admitting lane then walks its set
@@ -785,9 +843,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // list is empty and its threshold the identity, not a fallback.
         const bool no_columns = hf * HALF >= P.k;
         const bool ok = collect && !stop && !overflow && !*abort_flag &&
-                        (isfinite(best) || no_columns);
+                        (TOPK || isfinite(best) || no_columns);
         if (ok) P.cand_thr[hf * P.m + i] = thr;
         P.cand_cnt[hf * P.m + i] = ok ? cnt : FALLBACK;
+        if constexpr (TOPK) {
+          float* kvo = P.kvals + (hf * P.m + i) * KMAX;
+#pragma unroll
+          for (int a = 0; a < KMAX; a++) kvo[a] = kv[a];
+          if (hf == 0) P.roff[i] = off;
+        }
       }
     }
   }
@@ -992,7 +1056,7 @@ __global__ void __launch_bounds__(EX_WARPS * 32) k_pairs(
     const float* __restrict__ c, const float* __restrict__ cn, const float* __restrict__ xnorm_row,
     const uint2* __restrict__ pairs, const uint32_t* __restrict__ pair_count, long m, uint32_t k,
     unsigned long long* __restrict__ rkey, float* __restrict__ xn_pos,
-    uint32_t* __restrict__ bad, uint32_t* __restrict__ status) {
+    uint32_t* __restrict__ bad, uint32_t* __restrict__ status, float* __restrict__ pval) {
   extern __shared__ __align__(16) float ex_smem[];
   __shared__ const float* rows_s[EX_WARPS][2][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1064,7 +1128,9 @@ __global__ void __launch_bounds__(EX_WARPS * 32) k_pairs(
       __syncwarp();  // the slot is refilled next iteration
     }
     cp_async_wait<0>();
-    if (mine) {
+    if (mine && pval) {
+      pval[pi] = acc;  // top-k mode: every pair's exact inner product
+    } else if (mine) {
       const float v = IP ? acc : __fsub_rn(__ldg(cn + pr.y), __fmul_rn(2.0f, acc));
       if (!isfinite(v)) {
         bad[pr.x] = 1;  // an overflowing chain: the exact list reproduces the CPU here
@@ -1086,7 +1152,8 @@ __global__ void k_pairs_plain(const float* __restrict__ x, int d, const uint32_t
                               const float* __restrict__ xnorm_row, const uint2* __restrict__ pairs,
                               const uint32_t* __restrict__ pair_count, long m, uint32_t k,
                               unsigned long long* __restrict__ rkey, float* __restrict__ xn_pos,
-                              uint32_t* __restrict__ bad, uint32_t* __restrict__ status) {
+                              uint32_t* __restrict__ bad, uint32_t* __restrict__ status,
+                              float* __restrict__ pval) {
   const long np = (long)*pair_count;
   for (long pi = (long)blockIdx.x * blockDim.x + threadIdx.x; pi < np;
        pi += (long)gridDim.x * blockDim.x) {
@@ -1098,6 +1165,10 @@ __global__ void k_pairs_plain(const float* __restrict__ x, int d, const uint32_t
     const long row = ids ? (long)ids[p0 + pr.x] : p0 + pr.x;
     const float* xr = x + row * (long)d;
     const float acc = chain(xr, c + (long)pr.y * d, d);
+    if (pval) {
+      pval[pi] = acc;  // top-k mode
+      continue;
+    }
     const float v = IP ? acc : __fsub_rn(__ldg(cn + pr.y), __fmul_rn(2.0f, acc));
     if (!isfinite(v)) {
       bad[pr.x] = 1;
@@ -1320,6 +1391,164 @@ __global__ void k_list_finish(const float* __restrict__ x, long n, int d,
   }
 }
 
+// ---------------------------------------------------------------- top-k stage
+
+// Top-k mode: a row's window is 2e below the kk-th best of the union of its
+// two halves' best-kk values (the row's screened kk-th best). Its listed
+// columns still inside become (row, column) pairs, contiguous per row
+// (pstart, pcnt); rows with none, more than SURV, or marked for the fallback
+// go to the full scan (pcnt 0). Launched with whole warps.
+__global__ void __launch_bounds__(256) k_collect_topk(
+    long p0, long m, uint32_t n, int kk, const uint2* __restrict__ cand,
+    const uint32_t* __restrict__ cand_cnt, const float* __restrict__ kvals,
+    const float* __restrict__ roff, uint2* __restrict__ pairs, uint32_t* __restrict__ pair_count,
+    uint32_t* __restrict__ pstart, uint32_t* __restrict__ pcnt, uint32_t* __restrict__ list,
+    uint32_t* __restrict__ list_count, unsigned long long* __restrict__ counters,
+    uint32_t* __restrict__ status) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool live = i < m;
+  uint32_t cnt[2] = {0, 0};
+  bool fb = !live;
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    cnt[h] = live ? cand_cnt[h * m + i] : 0;
+    if (cnt[h] == FALLBACK) {
+      fb = true;
+      cnt[h] = 0;
+    } else if (cnt[h] > CAP) {
+      atomicOr(status, ST_BAD_STATE);
+      fb = true;
+      cnt[h] = 0;
+    }
+  }
+  float thr = -INFINITY;
+  uint32_t ns = 0;
+  if (!fb) {
+    // The kk-th largest of the two descending lists.
+    const float* a = kvals + i * KMAX;
+    const float* b = kvals + (m + i) * KMAX;
+    int ia = 0, ib = 0;
+    float kth = -INFINITY;
+    for (int t = 0; t < kk; t++) {
+      const float va = ia < kk ? a[ia] : -INFINITY;
+      const float vb = ib < kk ? b[ib] : -INFINITY;
+      if (va >= vb) {
+        kth = va;
+        ia++;
+      } else {
+        kth = vb;
+        ib++;
+      }
+    }
+    thr = kth > -INFINITY ? __fsub_rd(kth, roff[i]) : -INFINITY;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const uint2* lst = cand + (long)h * CAP * m + i;
+      for (uint32_t e = 0; e < cnt[h]; e++) {
+        const uint2 en = lst[e * m];
+        const float sv = __uint_as_float(en.y);
+        if (en.x >= n) fb = true;
+        ns += sv >= thr && sv > -INFINITY;
+      }
+    }
+    if (fb) atomicOr(status, ST_BAD_STATE);
+  }
+  fb = fb || ns == 0 || ns > SURV;
+  const bool listed = live && fb;
+  const uint32_t np = live && !fb ? ns : 0;
+  const uint32_t lp = warp_append(list_count, listed ? 1u : 0u);
+  if (listed) list[lp] = (uint32_t)(p0 + i);
+  uint32_t w = warp_append(pair_count, np);
+  if (live) {
+    pstart[i] = w;
+    pcnt[i] = np;
+  }
+  if (np) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const uint2* lst = cand + (long)h * CAP * m + i;
+      for (uint32_t e = 0; e < cnt[h]; e++) {
+        const uint2 en = lst[e * m];
+        const float sv = __uint_as_float(en.y);
+        if (sv >= thr && sv > -INFINITY) pairs[w++] = make_uint2((uint32_t)i, en.x);
+      }
+    }
+  }
+  const uint32_t nl = __reduce_add_sync(0xFFFFFFFFu, listed ? 1u : 0u);
+  const uint32_t nps = __reduce_add_sync(0xFFFFFFFFu, np);
+  if ((threadIdx.x & 31) == 0) {
+    if (nl) atomicAdd(&counters[1], (unsigned long long)nl);
+    if (nps) atomicAdd(&counters[2], (unsigned long long)nps);
+  }
+}
+
+// Each row's best kk of its pairs' exact inner products by (larger score,
+// then lower id); NaN and -inf never enter, missing entries stay
+// (0xFFFFFFFF, -inf). Rows of the full scan (pcnt 0) are written there.
+__global__ void k_topk_finish(long p0, long m, int kk, uint32_t id0,
+                              const uint32_t* __restrict__ pstart,
+                              const uint32_t* __restrict__ pcnt, const uint2* __restrict__ pairs,
+                              const float* __restrict__ pval, uint32_t* __restrict__ ids,
+                              float* __restrict__ sims) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= m) return;
+  const uint32_t np = pcnt[i];
+  if (np == 0) return;
+  float ls[KMAX];
+  uint32_t li[KMAX];
+#pragma unroll
+  for (int a = 0; a < KMAX; a++) {
+    ls[a] = -INFINITY;
+    li[a] = 0xFFFFFFFFu;
+  }
+  const uint32_t s0 = pstart[i];
+  for (uint32_t t = 0; t < np; t++) {
+    float cv = pval[s0 + t];
+    uint32_t cj = pairs[s0 + t].y;
+    if (!(cv > -INFINITY)) continue;
+#pragma unroll
+    for (int a = 0; a < KMAX; a++) {
+      const bool b = a < kk && (cv > ls[a] || (cv == ls[a] && cj < li[a]));
+      const float tv = ls[a];
+      const uint32_t tj = li[a];
+      ls[a] = b ? cv : tv;
+      li[a] = b ? cj : tj;
+      cv = b ? tv : cv;
+      cj = b ? tj : cj;
+    }
+  }
+  const long o = (p0 + i) * (long)kk;
+#pragma unroll
+  for (int a = 0; a < KMAX; a++) {
+    if (a < kk) {
+      ids[o + a] = li[a] == 0xFFFFFFFFu ? li[a] : li[a] + id0;  // global ids
+      sims[o + a] = li[a] == 0xFFFFFFFFu ? -INFINITY : ls[a];
+    }
+  }
+}
+
+// Gather the rows of listed queries (global positions) into a dense block.
+__global__ void k_gather_queries(const float* __restrict__ q, int d, const uint32_t* __restrict__ list,
+                                 long L, float* __restrict__ out) {
+  const long t = (long)blockIdx.y * gridDim.x + blockIdx.x;
+  if (t >= L) return;
+  const float* src = q + (long)list[t] * d;
+  float* dst = out + t * d;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) dst[c] = src[c];
+}
+
+// Scatter the full scan's results of the listed queries into place.
+__global__ void k_scatter_topk(const uint32_t* __restrict__ list, long L, int kk,
+                               const uint32_t* __restrict__ tids, const float* __restrict__ tsims,
+                               uint32_t* __restrict__ ids, float* __restrict__ sims) {
+  const long u = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= L * kk) return;
+  const long t = u / kk, a = u - t * kk;
+  const long o = (long)list[t] * kk + a;
+  ids[o] = tids[u];
+  sims[o] = tsims[u];
+}
+
 // ---------------------------------------------------------------- host side
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1353,11 +1582,11 @@ CUtensorMap make_map(const void* base, size_t rows, size_t dp, uint32_t box_rows
 }
 
 // Dynamic shared memory limits are per-device, per-kernel attributes.
-template <bool IP>
+template <bool IP, bool TOPK>
 void set_smem(int device) {
-  static uint64_t done = 0;  // one instance per kernel: IP is a template parameter
+  static uint64_t done = 0;  // one instance per kernel: IP, TOPK are template parameters
   if (!(done >> device & 1)) {
-    EB_CUDA(cudaFuncSetAttribute(k_screen<IP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    EB_CUDA(cudaFuncSetAttribute(k_screen<IP, TOPK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)SMEM_BYTES));
     done |= 1ull << device;
   }
@@ -1383,11 +1612,11 @@ void set_list_smem(int device) {
   }
 }
 
-template <bool IP>
+template <bool IP, bool TOPK = false>
 void launch_screen(eb_engine* e, unsigned grid, const CUtensorMap& ah, const CUtensorMap& al,
                    const CUtensorMap& bh, const CUtensorMap& bl, const ScreenParams& P) {
-  set_smem<IP>(e->device);
-  k_screen<IP><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(ah, al, bh, bl, P);
+  set_smem<IP, TOPK>(e->device);
+  k_screen<IP, TOPK><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(ah, al, bh, bl, P);
 }
 
 // Scratch of the exact stage of one pass of m rows.
@@ -1423,11 +1652,11 @@ void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const ExactS
     set_pairs_smem<IP>(e->device, EX_SMEM);
     k_pairs<IP><<<pgrid, EX_WARPS * 32, EX_SMEM, e->stream>>>(
         a.x, (int)a.d, a.ids, c0, a.c, a.cnorm, a.xnorm, S.pairs, S.pair_count, m,
-        (uint32_t)a.k, S.rkey, S.xn_pos, S.bad, e->d_status);
+        (uint32_t)a.k, S.rkey, S.xn_pos, S.bad, e->d_status, nullptr);
   } else {
     k_pairs_plain<IP><<<pgrid * 4, 128, 0, e->stream>>>(
         a.x, (int)a.d, a.ids, c0, a.c, a.cnorm, a.xnorm, S.pairs, S.pair_count, m,
-        (uint32_t)a.k, S.rkey, S.xn_pos, S.bad, e->d_status);
+        (uint32_t)a.k, S.rkey, S.xn_pos, S.bad, e->d_status, nullptr);
   }
   EB_LAUNCH("screen exact chains");
   k_finish<IP><<<rgrid, 256, 0, e->stream>>>(a.ids, c0, m, a.xnorm, S.xn_pos, S.rkey, S.bad,
@@ -1612,6 +1841,149 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
       launch_exact<false>(e, a, (long)c0, (long)m, S);
   }
   e->stats.screened_rows += m_all;
+}
+
+namespace {
+
+// The bound coefficients of the header comment for this d, with 1% slack.
+void screen_bound(size_t d, float& e_rel, float& e_abs, float& e_min) {
+  const double dd = (double)d;
+  const double u24 = std::ldexp(1.0, -24);
+  const double gamma_d = dd * u24 / (1.0 - dd * u24);
+  e_rel = (float)((3.0 * std::ldexp(1.0, -22) + dd * std::ldexp(1.0, -21) * (1.0 + std::ldexp(1.0, -9)) +
+                   dd * std::ldexp(1.0, -30) + std::ldexp(1.0, -23) + gamma_d) *
+                  1.01);
+  e_abs = (float)(std::ldexp(1.0, -23) * std::sqrt(dd) * 1.01);
+  e_min = (float)(dd * std::ldexp(1.0, -48));
+}
+
+}  // namespace
+
+// Top-kk by inner product on the tensor cores: the screen in top-k mode keeps
+// every column within 2e of each row's screened kk-th best (a column of the
+// exact top kk cannot lie further below it), the exact FP32 chains score
+// those candidates, and each row takes its best kk by (larger score, then
+// lower id); rows with too many candidates are scanned exactly in full.
+bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size_t n, size_t d,
+                 size_t kk, bool exclude_self, uint32_t* ids, float* sims, size_t id0) {
+  if (e->screen_mode == 0 || d > 16384 || n > 0x7FFFFFFFull || kk > (size_t)KMAX) return false;
+  if (e->screen_mode == 1 && (n < 256 || m < 128 || d < 16)) return false;
+  const size_t dp = (d + BKH - 1) / BKH * BKH;
+  const size_t wave = (size_t)e->num_sms * BM;
+  const size_t chunk = std::min(m, PASS_WAVES * wave);
+  float e_rel, e_abs, e_min;
+  screen_bound(d, e_rel, e_abs, e_min);
+
+  // The data rows play the centroids: one exponent, split FP16 copy.
+  uint32_t* cinfo = e->scratch_get<uint32_t>("tc_cinfo", 4);
+  __half* ch = e->scratch_get<__half>("tc_ch", n * dp);
+  __half* cl = e->scratch_get<__half>("tc_cl", n * dp);
+  EB_CUDA(cudaMemsetAsync(cinfo, 0, 16, e->stream));
+  k_cent_max<<<(unsigned)((n + 1) / 2), 64, 0, e->stream>>>(data, (long)n, (int)d, cinfo);
+  EB_LAUNCH("topk data max");
+  k_cent_conv<<<(unsigned)((n + 1) / 2), 64, 0, e->stream>>>(data, (long)n, (int)d, (int)dp, cinfo,
+                                                            ch, cl);
+  EB_LAUNCH("topk data convert");
+  const CUtensorMap mapBh = make_map(ch, n, dp, BN);
+  const CUtensorMap mapBl = make_map(cl, n, dp, BN);
+
+  const unsigned wpb = 8;
+  __half* xh = e->scratch_get<__half>("tc_xh", chunk * dp);
+  __half* xl = e->scratch_get<__half>("tc_xl", chunk * dp);
+  int* xexp = e->scratch_get<int>("tc_xexp", chunk);
+  float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
+  uint2* cand = e->scratch_get<uint2>("tc_cand", 2 * chunk * CAP);
+  uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", 2 * chunk);
+  float* cand_thr = e->scratch_get<float>("tc_thr", 2 * chunk);
+  float* kvals = e->scratch_get<float>("tk_kvals", 2 * chunk * KMAX);
+  float* roff = e->scratch_get<float>("tk_roff", chunk);
+  uint2* pairs = e->scratch_get<uint2>("tc_pairs", chunk * SURV);
+  float* pval = e->scratch_get<float>("tk_pval", chunk * SURV);
+  uint32_t* pair_count = e->scratch_get<uint32_t>("tc_pair_count", 4);
+  uint32_t* pstart = e->scratch_get<uint32_t>("tk_pstart", chunk);
+  uint32_t* pcnt = e->scratch_get<uint32_t>("tk_pcnt", chunk);
+  uint32_t* list = e->scratch_get<uint32_t>("tc_list", chunk);
+  uint32_t* list_count = e->scratch_get<uint32_t>("tc_list_count", 4);
+  uint32_t* h_list_count = e->h_status + 1;  // pinned word beside the status mirror
+  unsigned long long* counters = e->counters();
+
+  ScreenParams P{};
+  P.k = (int)n;
+  P.kblocks = (int)(dp / BKH);
+  P.ntiles = (int)((n + BN - 1) / BN);
+  P.cn = nullptr;
+  P.cinfo = cinfo;
+  P.e_rel = e_rel;
+  P.e_abs = e_abs;
+  P.e_min = e_min;
+  P.cand = cand;
+  P.cand_cnt = cand_cnt;
+  P.cand_thr = cand_thr;
+  P.status = e->d_status;
+  P.kk = (int)kk;
+  P.exclude_self = exclude_self ? 1 : 0;
+  P.col_gid0 = (long)id0;
+  P.kvals = kvals;
+  P.roff = roff;
+
+  for (size_t c0 = 0; c0 < m; c0 += chunk) {
+    const size_t mc = std::min(chunk, m - c0);
+    k_prep_rows<<<(unsigned)((mc + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(
+        q, (long)m, (int)d, (int)dp, nullptr, (long)c0, (long)mc, xh, xl, xexp, xnrm,
+        e->d_status);
+    EB_LAUNCH("topk query prep");
+    const CUtensorMap mapAh = make_map(xh, mc, dp, BM);
+    const CUtensorMap mapAl = make_map(xl, mc, dp, BM);
+    P.m = (long)mc;
+    P.xexp = xexp;
+    P.xnrm = xnrm;
+    P.row_gid0 = (long)c0;
+    const unsigned grid = (unsigned)std::min<size_t>((mc + BM - 1) / BM, (size_t)e->num_sms);
+    launch_screen<true, true>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
+    EB_LAUNCH("topk screen");
+    EB_CUDA(cudaMemsetAsync(pair_count, 0, 4, e->stream));
+    EB_CUDA(cudaMemsetAsync(list_count, 0, 4, e->stream));
+    const unsigned rgrid = (unsigned)((mc + 255) / 256);
+    k_collect_topk<<<rgrid, 256, 0, e->stream>>>((long)c0, (long)mc, (uint32_t)n, (int)kk, cand,
+                                                 cand_cnt, kvals, roff, pairs, pair_count, pstart,
+                                                 pcnt, list, list_count, counters, e->d_status);
+    EB_LAUNCH("topk collect");
+    const unsigned pgrid = (unsigned)e->num_sms;
+    if (d % EX_COLS == 0) {
+      set_pairs_smem<true>(e->device, EX_SMEM);
+      k_pairs<true><<<pgrid, EX_WARPS * 32, EX_SMEM, e->stream>>>(
+          q, (int)d, nullptr, (long)c0, data, nullptr, nullptr, pairs, pair_count, (long)mc,
+          (uint32_t)n, nullptr, nullptr, nullptr, e->d_status, pval);
+    } else {
+      k_pairs_plain<true><<<pgrid * 4, 128, 0, e->stream>>>(
+          q, (int)d, nullptr, (long)c0, data, nullptr, nullptr, pairs, pair_count, (long)mc,
+          (uint32_t)n, nullptr, nullptr, nullptr, e->d_status, pval);
+    }
+    EB_LAUNCH("topk exact chains");
+    k_topk_finish<<<rgrid, 256, 0, e->stream>>>((long)c0, (long)mc, (int)kk, (uint32_t)id0,
+                                                pstart, pcnt, pairs, pval, ids, sims);
+    EB_LAUNCH("topk finish");
+    // Rows of the full scan: their count comes to the host (this call ends
+    // with a copy to the host anyway), then a chunked exact scan.
+    EB_CUDA(cudaMemcpyAsync(h_list_count, list_count, 4, cudaMemcpyDeviceToHost, e->stream));
+    EB_CUDA(cudaStreamSynchronize(e->stream));
+    const size_t L = *h_list_count;
+    if (L) {
+      float* gq = e->scratch_get<float>("tk_gq", L * d);
+      uint32_t* tids = e->scratch_get<uint32_t>("tk_tids", L * kk);
+      float* tsims = e->scratch_get<float>("tk_tsims", L * kk);
+      const unsigned gx = (unsigned)std::min<size_t>(L, 65535);
+      const unsigned gy = (unsigned)((L + gx - 1) / gx);
+      k_gather_queries<<<dim3(gx, gy), 128, 0, e->stream>>>(q, (int)d, list, (long)L, gq);
+      EB_LAUNCH("topk gather");
+      topk_exact_device(e, gq, L, list, data, n, d, kk, exclude_self, tids, tsims, id0);
+      k_scatter_topk<<<(unsigned)((L * kk + 255) / 256), 256, 0, e->stream>>>(
+          list, (long)L, (int)kk, tids, tsims, ids, sims);
+      EB_LAUNCH("topk scatter");
+    }
+  }
+  e->stats.screened_rows += m;
+  return true;
 }
 
 }  // namespace eb

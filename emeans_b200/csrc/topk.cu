@@ -6,6 +6,8 @@
 // missing neighbours stay (0xFFFFFFFF, -inf).
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "engine.h"
 
 namespace eb {
@@ -13,11 +15,23 @@ namespace {
 
 constexpr int BM = 64, BN = 64, BK = 16, NT = 256, KMAX = 16;
 
+// Block (x, y): queries 64 x .. 64 x + 63 against data rows of chunk y,
+// y chunk .. min(n, (y + 1) chunk) (all rows when gridDim.y is 1), whose
+// global ids start at id0. Chunk y's lists go to out_ids / out_sims + y per.
+// With exclude_self, query qi is skipped against the data row whose global
+// id is qids[qi] (qi when qids is null).
 __global__ void __launch_bounds__(NT) k_topk_exact(const float* __restrict__ q, long m,
-                                                   const float* __restrict__ data, long n, int d,
-                                                   int kk, int exclude_self, long id0,
-                                                   uint32_t* __restrict__ out_ids,
-                                                   float* __restrict__ out_sims) {
+                                                   const float* __restrict__ data_all, long n_all,
+                                                   int d, int kk, int exclude_self, long id0,
+                                                   const uint32_t* __restrict__ qids, long chunk,
+                                                   long per, uint32_t* __restrict__ out_ids_all,
+                                                   float* __restrict__ out_sims_all) {
+  const long c0 = (long)blockIdx.y * chunk;
+  const float* data = data_all + c0 * (long)d;
+  const long n = gridDim.y == 1 ? n_all : min(chunk, n_all - c0);
+  uint32_t* out_ids = out_ids_all + (long)blockIdx.y * per;
+  float* out_sims = out_sims_all + (long)blockIdx.y * per;
+  id0 += c0;
   __shared__ __align__(16) float As[BK][BM + 4];
   __shared__ __align__(16) float Bs[BK][BN + 4];
   __shared__ float S[BM][BN + 1];
@@ -88,12 +102,13 @@ __global__ void __launch_bounds__(NT) k_topk_exact(const float* __restrict__ q, 
       for (int j = 0; j < 4; j++) S[ty * 4 + i][tx * 4 + j] = acc[i][j];
     __syncthreads();
     if (tid < BM) {
-      long qi = q0 + tid;
+      const long qi = q0 + tid;
+      const long qg = q0 + tid < m ? (qids ? (long)qids[q0 + tid] : qi) : -1;
       int cols = (int)min((long)BN, n - n0);
       for (int j = 0; j < cols; j++) {
         // Data row n0 + j has the global id id0 + n0 + j (a shard's offset).
         uint32_t col = (uint32_t)(id0 + n0 + j);
-        if (exclude_self && (long)col == qi) continue;
+        if (exclude_self && (long)col == qg) continue;
         float v = S[tid][j];
         if (!(v > ls[KMAX - 1])) continue;
         float cv = v;
@@ -185,10 +200,13 @@ void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, s
   float* ds = group ? reinterpret_cast<float*>(di + m * kk) : e->scratch_get<float>("tk_sims", m * kk);
   EB_CUDA(cudaMemcpyAsync(dq, q, m * d * 4, cudaMemcpyHostToDevice, e->stream));
   if (n) EB_CUDA(cudaMemcpyAsync(dd, data, n * d * 4, cudaMemcpyHostToDevice, e->stream));
-  unsigned grid = (unsigned)((m + BM - 1) / BM);
-  k_topk_exact<<<grid, NT, 0, e->stream>>>(dq, (long)m, dd, (long)n, (int)d, (int)kk,
-                                           exclude_self ? 1 : 0, (long)id0, di, ds);
-  EB_LAUNCH("topk");
+  if (!topk_screen(e, dq, m, dd, n, d, kk, exclude_self, di, ds, id0)) {
+    unsigned grid = (unsigned)((m + BM - 1) / BM);
+    k_topk_exact<<<grid, NT, 0, e->stream>>>(dq, (long)m, dd, (long)n, (int)d, (int)kk,
+                                             exclude_self ? 1 : 0, (long)id0, nullptr, (long)n, 0,
+                                             di, ds);
+    EB_LAUNCH("topk");
+  }
   if (group) {
     group_allgather(e, stage, 2 * m * kk);
     di = e->scratch_get<uint32_t>("tk_ids", m * kk);
@@ -200,6 +218,29 @@ void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, s
   EB_CUDA(cudaMemcpyAsync(ids, di, m * kk * 4, cudaMemcpyDeviceToHost, e->stream));
   EB_CUDA(cudaMemcpyAsync(sims, ds, m * kk * 4, cudaMemcpyDeviceToHost, e->stream));
   sync(e);
+}
+
+// Exact top-kk of L device-resident queries (global ids qids, for
+// exclude_self) against n device-resident data rows: the data is split into
+// up to one chunk per SM, every (64 queries, chunk) pair is a block, and the
+// chunks' lists are merged; results (L x kk) stay on the device.
+void topk_exact_device(eb_engine* e, const float* q, size_t L, const uint32_t* qids,
+                       const float* data, size_t n, size_t d, size_t kk, bool exclude_self,
+                       uint32_t* ids, float* sims, size_t id0) {
+  if (L == 0) return;
+  const size_t nch = std::max<size_t>(1, std::min<size_t>((size_t)e->num_sms, (n + 4095) / 4096));
+  const size_t chunk = (n + nch - 1) / nch;
+  const size_t per = 2 * L * kk;
+  uint32_t* stage = e->scratch_get<uint32_t>("tk_chunks", nch * per);
+  dim3 grid((unsigned)((L + BM - 1) / BM), (unsigned)nch);
+  k_topk_exact<<<grid, NT, 0, e->stream>>>(q, (long)L, data, (long)n, (int)d, (int)kk,
+                                           exclude_self ? 1 : 0, (long)id0, qids, (long)chunk,
+                                           (long)per,
+                                           stage, reinterpret_cast<float*>(stage + L * kk));
+  EB_LAUNCH("topk chunks");
+  k_topk_merge<<<(unsigned)((L + 127) / 128), 128, 0, e->stream>>>(stage, (long)L, (int)kk,
+                                                                   (int)nch, ids, sims);
+  EB_LAUNCH("topk chunk merge");
 }
 
 }  // namespace eb
