@@ -239,14 +239,23 @@ __device__ __forceinline__ void tmem_wait_tied(uint32_t (&a)[16], uint32_t (&b)[
 }
 
 // Keep only the entries of a row's candidate list still inside the window
-// (out of line: it runs only when a list nears its capacity).
+// (out of line: it runs only when a list nears its capacity). Entries are
+// read eight at a time before any of them is written back: every write goes
+// to a slot at or below one already read, so the batch's loads can all be in
+// flight together.
 template <bool IP>
 __device__ __noinline__ uint32_t compact_list(uint2* list, long stride, uint32_t cnt, float thr) {
   uint32_t w = 0;
-  for (uint32_t e = 0; e < cnt; e++) {
-    const uint2 en = list[e * stride];
-    const float sv = __uint_as_float(en.y);
-    if (IP ? (sv >= thr) : (sv <= thr)) list[(w++) * stride] = en;
+  for (uint32_t e0 = 0; e0 < cnt; e0 += 8) {
+    uint2 en[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+      en[u] = e0 + u < cnt ? list[(e0 + u) * stride] : make_uint2(0u, __float_as_uint(NAN));
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const float sv = __uint_as_float(en[u].y);
+      if (IP ? (sv >= thr) : (sv <= thr)) list[(w++) * stride] = en[u];
+    }
   }
   return w;
 }
@@ -498,7 +507,7 @@ struct ScreenParams {
   int exclude_self;    // skip the column whose id is the row's global id
   long row_gid0;       // global id of staging row 0
   long col_gid0;       // global id of column 0 (a database shard's offset)
-  float* kvals;        // 2 m x KMAX: each (half, row)'s best kk values, descending
+  float* kvals;        // 2 m x KMAX: each (half, row)'s best kk values, ascending
   float* roff;         // m: each row's window 2e
 };
 
@@ -674,11 +683,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool overflow = false;
       uint32_t cnt = 0;  // entries in this (row, half)'s candidate list
       uint2* row_list = P.cand + (long)hf * CAP * P.m + (live ? i : 0);  // entries P.m apart
-      // Top-k mode: the best kk screened values so far, descending (slots past
-      // kk stay -inf), and the kk-th of them.
+      // Top-k mode: the best kk screened values so far in slots 0 .. kk - 1,
+      // ascending (the kk-th best in slot 0), slots kk .. KMAX - 1 held at +inf.
       float kv[TOPK ? KMAX : 1];
 #pragma unroll
-      for (int a = 0; a < (TOPK ? KMAX : 1); a++) kv[a] = -INFINITY;
+      for (int a = 0; a < (TOPK ? KMAX : 1); a++) kv[a] = a < P.kk ? -INFINITY : INFINITY;
       float kth = -INFINITY;
       const long gid = P.row_gid0 + i;
 
@@ -787,20 +796,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 while (m_up) {
                   const int j = __ffs(m_up) - 1;
                   m_up &= m_up - 1;
-                  float cv = svs[j * 32];
-                  if (!(cv > kth)) continue;
+                  const float cv = svs[j * 32];
+                  if (!(cv > kv[0])) continue;
+                  // Replace the smallest and let it rise to its place.
+                  kv[0] = cv;
 #pragma unroll
-                  for (int a = 0; a < KMAX; a++) {
-                    const bool b = a < P.kk && cv > kv[a];
-                    const float tv = kv[a];
-                    kv[a] = b ? cv : tv;
-                    cv = b ? tv : cv;
+                  for (int a = 0; a + 1 < KMAX; a++) {
+                    const float lo_v = fminf(kv[a], kv[a + 1]), hi_v = fmaxf(kv[a], kv[a + 1]);
+                    kv[a] = lo_v;
+                    kv[a + 1] = hi_v;
                   }
-                  float kt = kv[0];
-#pragma unroll
-                  for (int a = 1; a < KMAX; a++)
-                    if (a == P.kk - 1) kt = kv[a];
-                  kth = kt;
+                  kth = kv[0];
                 }
               }
               __syncwarp();
@@ -1424,20 +1430,21 @@ __global__ void __launch_bounds__(256) k_collect_topk(
   float thr = -INFINITY;
   uint32_t ns = 0;
   if (!fb) {
-    // The kk-th largest of the two descending lists.
+    // The kk-th largest of the two halves' best-kk values (each ascending in
+    // slots 0 .. kk - 1): a merge from the top.
     const float* a = kvals + i * KMAX;
     const float* b = kvals + (m + i) * KMAX;
-    int ia = 0, ib = 0;
+    int ia = kk - 1, ib = kk - 1;
     float kth = -INFINITY;
     for (int t = 0; t < kk; t++) {
-      const float va = ia < kk ? a[ia] : -INFINITY;
-      const float vb = ib < kk ? b[ib] : -INFINITY;
+      const float va = ia >= 0 ? a[ia] : -INFINITY;
+      const float vb = ib >= 0 ? b[ib] : -INFINITY;
       if (va >= vb) {
         kth = va;
-        ia++;
+        ia--;
       } else {
         kth = vb;
-        ib++;
+        ib--;
       }
     }
     thr = kth > -INFINITY ? __fsub_rd(kth, roff[i]) : -INFINITY;
