@@ -345,6 +345,7 @@ def run_ours(args):
                                    "events); executed tensor work is 3x (three FP16 products)",
                          "launch_ms": per_launch_ms, "rows_per_launch": rows_per_launch,
                          "executed_tflops": 3.0 * achieved,
+                         "executed_frac": 3.0 * achieved / peak,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum "
                                            "of one 65,536-row screen launch, scaled by rows",
                          "peak_source": peak_src, "top1_op_ms": top1_ms,

@@ -193,6 +193,7 @@ int eb_engine_destroy(eb_engine* e) {
     cudaFree(e->d_status);
     cudaFree(e->d_counters);
     cudaFreeHost(e->h_status);
+    if (e->copy_stream) cudaStreamDestroy(e->copy_stream);
     cudaStreamDestroy(e->stream);
     delete e;
   });
@@ -651,21 +652,60 @@ int eb_assign(eb_engine* e, const float* rows, size_t n, size_t d, const uint32_
       ib.ptr = di; ib.len = m; ib.dtype = EB_U32;
       rc = eb_top1(e, e->bound, d, &ib, 0, m, &cb, metric == EB_L2 ? &cnb : nullptr, k, metric,
                    &lb, &sb);
-    } else {
-      // Dense rows, or indexed rows gathered on the host (core/mod.rs:299-325).
+    } else if (ids) {
+      // Indexed rows gathered on the host (core/mod.rs:299-325).
       float* xd = e->scratch_get<float>("as_x", m * d);
-      if (ids) {
-        std::vector<float> gbuf(m * d);
-        for (size_t i = 0; i < m; i++)
-          std::memcpy(&gbuf[i * d], rows + (size_t)ids[i] * d, d * 4);
-        EB_CUDA(cudaMemcpyAsync(xd, gbuf.data(), m * d * 4, cudaMemcpyHostToDevice, e->stream));
-      } else {
-        EB_CUDA(cudaMemcpyAsync(xd, rows, m * d * 4, cudaMemcpyHostToDevice, e->stream));
-      }
+      std::vector<float> gbuf(m * d);
+      for (size_t i = 0; i < m; i++)
+        std::memcpy(&gbuf[i * d], rows + (size_t)ids[i] * d, d * 4);
+      EB_CUDA(cudaMemcpyAsync(xd, gbuf.data(), m * d * 4, cudaMemcpyHostToDevice, e->stream));
       eb_buf xb;
       xb.ptr = xd; xb.len = m * d; xb.dtype = EB_F32;
       rc = eb_top1(e, &xb, d, nullptr, 0, m, &cb, metric == EB_L2 ? &cnb : nullptr, k, metric,
                    &lb, &sb);
+    } else {
+      // Dense rows: copied in slices on the copy stream, each slice's top-1
+      // queued on the engine's stream behind its own copy, so that the copy
+      // of slice j + 1 overlaps the top-1 of slice j. The centroids'
+      // screen copy is made once, by the first slice that takes the screen.
+      float* xd = e->scratch_get<float>("as_x", m * d);
+      if (!e->copy_stream) EB_CUDA(cudaStreamCreateWithFlags(&e->copy_stream, cudaStreamNonBlocking));
+      const size_t slice = std::max<size_t>(16384, (m + 3) / 4);
+      cudaEvent_t ready;
+      EB_CUDA(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
+      EB_CUDA(cudaEventRecord(ready, e->stream));  // earlier work on the staging buffer
+      EB_CUDA(cudaStreamWaitEvent(e->copy_stream, ready, 0));
+      EB_CUDA(cudaEventDestroy(ready));
+      bool converted = false;
+      for (size_t r0 = 0; r0 < m; r0 += slice) {
+        const size_t r1 = std::min(m, r0 + slice);
+        EB_CUDA(cudaMemcpyAsync(xd + r0 * d, rows + r0 * d, (r1 - r0) * d * 4,
+                                cudaMemcpyHostToDevice, e->copy_stream));
+        cudaEvent_t landed;
+        EB_CUDA(cudaEventCreateWithFlags(&landed, cudaEventDisableTiming));
+        EB_CUDA(cudaEventRecord(landed, e->copy_stream));
+        EB_CUDA(cudaStreamWaitEvent(e->stream, landed, 0));
+        EB_CUDA(cudaEventDestroy(landed));
+        eb::Top1Args a;
+        a.x = xd;
+        a.n = m;
+        a.d = d;
+        a.ids = nullptr;
+        a.r0 = r0;
+        a.r1 = r1;
+        a.c = c;
+        a.cnorm = cn;
+        a.k = k;
+        a.metric = metric;
+        a.labels = lab;
+        a.scores = sco;
+        a.xnorm = nullptr;
+        a.centroids_ready = converted;
+        const bool screened = eb::top1_screen_supported(e, a);
+        eb::top1_dispatch(e, a, nullptr);
+        converted = converted || screened;
+      }
+      rc = EB_OK;
     }
     if (rc != EB_OK) throw eb::Error(rc, g_last_error);
     EB_CUDA(cudaMemcpyAsync(labels, lab, m * 4, cudaMemcpyDeviceToHost, e->stream));

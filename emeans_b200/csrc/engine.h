@@ -93,6 +93,9 @@ struct eb_engine {
   // Optional CUDA-event timing of the top-1 screen kernel (eb_set_kernel_timing):
   // one (start, end) pair per launch since the last eb_screen_timing read,
   // with the rows of that launch.
+  // Second stream for host-to-device copies that overlap compute (eb_assign),
+  // created on first use.
+  cudaStream_t copy_stream = nullptr;
   bool time_screen = false;
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> screen_ev;
   std::vector<size_t> screen_ev_rows;
@@ -162,6 +165,9 @@ struct Top1Args {
   uint32_t* labels;    // indexed by position
   float* scores;
   const float* xnorm;  // squared norms by data row (L2), or null: computed
+  // The tensor-core screen's split copy of these centroids is already in its
+  // scratch (a later slice of the same call): skip the conversion.
+  bool centroids_ready = false;
 };
 // Full exact scan of every selected row.
 void top1_exact(eb_engine* e, const Top1Args& a);

@@ -1720,13 +1720,15 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   uint32_t* cinfo = e->scratch_get<uint32_t>("tc_cinfo", 4);
   __half* ch = e->scratch_get<__half>("tc_ch", k * dp);
   __half* cl = e->scratch_get<__half>("tc_cl", k * dp);
-  EB_CUDA(cudaMemsetAsync(cinfo, 0, 16, e->stream));
   const unsigned wpb = 8;
-  k_cent_max<<<(unsigned)((k + 1) / 2), 64, 0, e->stream>>>(a.c, (long)k, (int)d, cinfo);
-  EB_LAUNCH("screen centroid max");
-  k_cent_conv<<<(unsigned)((k + 1) / 2), 64, 0, e->stream>>>(a.c, (long)k, (int)d, (int)dp, cinfo,
-                                                            ch, cl);
-  EB_LAUNCH("screen centroid convert");
+  if (!a.centroids_ready) {
+    EB_CUDA(cudaMemsetAsync(cinfo, 0, 16, e->stream));
+    k_cent_max<<<(unsigned)((k + 1) / 2), 64, 0, e->stream>>>(a.c, (long)k, (int)d, cinfo);
+    EB_LAUNCH("screen centroid max");
+    k_cent_conv<<<(unsigned)((k + 1) / 2), 64, 0, e->stream>>>(a.c, (long)k, (int)d, (int)dp,
+                                                              cinfo, ch, cl);
+    EB_LAUNCH("screen centroid convert");
+  }
   const CUtensorMap mapBh = make_map(ch, k, dp, BN);
   const CUtensorMap mapBl = make_map(cl, k, dp, BN);
 
