@@ -128,17 +128,24 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   const size_t chunk = job->chunk > 0 ? (size_t)job->chunk : 65536;
   const size_t n_epochs = r.epoch_rows.size();
 
-  // Device state (train.rs:92-101).
+  // Device state (train.rs:92-101). Data bound with Assigner::bind_data
+  // (the same host rows) is used in place, with its row norms and screen
+  // copy; otherwise the rows are uploaded for this run.
   eb_buf* data = nullptr;
-  {
+  const bool reuse = e->bound && e->bound_host == job->x && e->bound_n == n && e->bound->d == d;
+  if (reuse) {
+    data = e->bound;
+  } else {
     int rc = eb_bind(e, job->x, n, d, &data);
     if (rc != EB_OK) throw Error(rc, eb_last_error());
   }
   struct Unbind {
     eb_engine* e;
     eb_buf* b;
-    ~Unbind() { free_buf(e, b); }
-  } unbind{e, data};
+    ~Unbind() {
+      if (b) free_buf(e, b);
+    }
+  } unbind{e, reuse ? nullptr : data};
   DevBuf order(e, EB_U32, n), labels_ep(e, EB_U32, n), scores_ep(e, EB_F32, n);
   DevBuf dpos(e, EB_F32, k * d), mass(e, EB_F32, k), readout(e, EB_F32, spherical ? k * d : k);
   DevBuf sums(e, EB_F32, k * d), counts(e, EB_U32, k), pass(e, EB_F32, k * d);

@@ -94,3 +94,20 @@ def test_train_argument_errors(engine):
         engine.train(x, eb.Config(d=4, k=11))
     with pytest.raises(eb.EngineError, match="finite"):
         engine.train(x, eb.Config(d=4, k=2), init=np.full((2, 4), np.nan, np.float32))
+
+
+def test_training_on_bound_rows(engine):
+    """Rows bound with Assigner::bind_data are trained on in place (no upload
+    inside the run); the result is the same as a run that uploads them."""
+    x = mixture(12000, 96, 30, 0.4, False, 21)
+    cfg = eb.Config(d=96, k=120, seed=4, spherical=False, nepochs=3.0)
+    want = engine.train(x, cfg)
+    engine.bind_data(x, 96)
+    try:
+        got = engine.train(x, cfg)
+        again = engine.train(x, cfg)
+    finally:
+        engine.unbind_data()
+    for g in (got, again):
+        assert np.array_equal(bits(g.centroids.ravel()), bits(want.centroids.ravel()))
+        assert np.array_equal(g.labels, want.labels) and g.obj == want.obj
