@@ -40,22 +40,23 @@ __global__ void k_row_sumsq(const float* __restrict__ m, long rows, int d, float
 }
 
 // The same sums for d % 32 == 0, one thread per row with the row streamed
-// through shared memory: 32 rows per block, 32-column slices copied with
-// cp.async (8 slices in flight), 16-byte chunk q of row t at q ^ (t & 7) so
-// that each thread's LDS.128 reads are free of bank conflicts.
+// through shared memory: R rows per one-warp block (32, or 8 when there are
+// few rows, so that more warps keep loads in flight), 32-column slices copied
+// with cp.async (8 slices in flight), 16-byte chunk q of row t at q ^ (t & 7)
+// so that each thread's LDS.128 reads are free of bank conflicts.
 constexpr int NS_ROWS = 32, NS_STAGES = 8;
 
-__global__ void __launch_bounds__(NS_ROWS) k_row_sumsq_staged(const float* __restrict__ m,
-                                                              long rows, int d,
-                                                              float* __restrict__ out) {
-  __shared__ __align__(16) float buf[NS_STAGES][NS_ROWS][32];
+template <int R>
+__global__ void __launch_bounds__(32) k_row_sumsq_staged(const float* __restrict__ m, long rows,
+                                                         int d, float* __restrict__ out) {
+  __shared__ __align__(16) float buf[NS_STAGES][R][32];
   const int t = threadIdx.x;
-  const long r0 = (long)blockIdx.x * NS_ROWS;
+  const long r0 = (long)blockIdx.x * R;
   const int nsl = d / 32;
   auto issue = [&](int sl) {
     if (sl < nsl) {
 #pragma unroll
-      for (int u = 0; u < 8; u++) {
+      for (int u = 0; u < R / 4; u++) {
         const int r = u * 4 + (t >> 3), q = t & 7;
         const long row = min(r0 + r, rows - 1);
         const float* src = m + row * d + sl * 32 + q * 4;
@@ -71,14 +72,15 @@ __global__ void __launch_bounds__(NS_ROWS) k_row_sumsq_staged(const float* __res
 #pragma unroll
   for (int s = 0; s < NS_STAGES - 1; s++) issue(s);
   float s = -0.0f;
+  const int tr = t < R ? t : 0;  // lanes past R rows idle
   for (int sl = 0; sl < nsl; sl++) {
     issue(sl + NS_STAGES - 1);
     asm volatile("cp.async.wait_group %0;" ::"n"(NS_STAGES - 1) : "memory");
     __syncwarp();
-    const float4* r4 = reinterpret_cast<const float4*>(buf[sl % NS_STAGES][t]);
+    const float4* r4 = reinterpret_cast<const float4*>(buf[sl % NS_STAGES][tr]);
 #pragma unroll
     for (int q = 0; q < 8; q++) {
-      const float4 v = r4[q ^ (t & 7)];
+      const float4 v = r4[q ^ (tr & 7)];
       s = __fadd_rn(s, __fmul_rn(v.x, v.x));
       s = __fadd_rn(s, __fmul_rn(v.y, v.y));
       s = __fadd_rn(s, __fmul_rn(v.z, v.z));
@@ -87,7 +89,7 @@ __global__ void __launch_bounds__(NS_ROWS) k_row_sumsq_staged(const float* __res
     __syncwarp();  // the slot is refilled next iteration
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
-  if (r0 + t < rows) out[r0 + t] = s;
+  if (t < R && r0 + t < rows) out[r0 + t] = s;
 }
 
 __global__ void k_sel_sumsq(const float* __restrict__ x, long n, int d,
@@ -228,10 +230,17 @@ __global__ void k_seg_scan(uint32_t* __restrict__ segcnt, long segs, uint32_t k,
   uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
   if (l >= k) return;
   uint32_t run = 0;
-  for (long s = 0; s < segs; s++) {
-    uint32_t c = segcnt[s * k + l];
-    segcnt[s * k + l] = run;
-    run += c;
+  // Sixteen segments' counts are read before any is rewritten, so that their
+  // loads are in flight together.
+  for (long s0 = 0; s0 < segs; s0 += 16) {
+    uint32_t c[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) c[u] = s0 + u < segs ? segcnt[(s0 + u) * k + l] : 0u;
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+      if (s0 + u < segs) segcnt[(s0 + u) * k + l] = run;
+      run += c[u];
+    }
   }
   counts[l] = run;
 }
@@ -308,8 +317,11 @@ unsigned blocks_for(size_t n, unsigned per) { return (unsigned)((n + per - 1) / 
 void row_norms(eb_engine* e, const float* m, size_t rows, size_t d, float* out) {
   if (rows == 0) return;
   if (d % 32 == 0 && ((uintptr_t)m & 15) == 0) {
-    k_row_sumsq_staged<<<blocks_for(rows, NS_ROWS), NS_ROWS, 0, e->stream>>>(m, (long)rows,
-                                                                             (int)d, out);
+    if (rows <= (size_t)e->num_sms * 32)
+      k_row_sumsq_staged<8><<<blocks_for(rows, 8), 32, 0, e->stream>>>(m, (long)rows, (int)d, out);
+    else
+      k_row_sumsq_staged<NS_ROWS><<<blocks_for(rows, NS_ROWS), 32, 0, e->stream>>>(m, (long)rows,
+                                                                                  (int)d, out);
   } else {
     k_row_sumsq<<<blocks_for(rows, kRowThreads), kRowThreads, 0, e->stream>>>(m, (long)rows,
                                                                               (int)d, out);
