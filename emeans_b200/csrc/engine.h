@@ -24,6 +24,11 @@ struct Error : std::runtime_error {
 inline void ensure(bool ok, const std::string& msg) {
   if (!ok) throw Error(EB_INVALID_ARGUMENT, msg);
 }
+// A literal message builds no string unless the check fails (checks run in
+// per-element loops).
+inline void ensure(bool ok, const char* msg) {
+  if (!ok) throw Error(EB_INVALID_ARGUMENT, msg);
+}
 
 inline void cuda_check(cudaError_t st, const char* what) {
   if (st != cudaSuccess)
