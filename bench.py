@@ -381,6 +381,47 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def gen_knn_rows(n, d, seed=4, components=10_000, sigma=0.4, dup_frac=0.05):
+    """kNN self-join config rows: unit rows from a mixture (means N(0, I),
+    noise sigma), with a fraction replaced by near-duplicates of random rows
+    (plus N(0, 0.01^2 I), renormalised)."""
+    rng = np.random.default_rng(seed)
+    means = rng.standard_normal((components, d), dtype=np.float32)
+    x = means[rng.integers(0, components, n)]
+    x += np.float32(sigma) * rng.standard_normal((n, d), dtype=np.float32)
+    nd = int(n * dup_frac)
+    dup = rng.choice(n, nd, replace=False)
+    x[dup] = x[rng.integers(0, n, nd)] + np.float32(0.01) * rng.standard_normal((nd, d),
+                                                                                dtype=np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    return np.ascontiguousarray(x, dtype=np.float32)
+
+
+def run_knn(args):
+    """--knn N: the kNN self-join config's shape on N rows (d 384, kk 10, inner
+    product, self excluded) through eb_topk with host arrays; one JSON line."""
+    import emeans_b200 as eb
+
+    n, d, kk = args.knn, 384, 10
+    x = gen_knn_rows(n, d)
+    eng = eb.Engine(0)
+    eng.topk(x[:2048], x, d, kk)  # warm-up
+    times = []
+    for _ in range(max(1, args.steps)):
+        t0 = time.perf_counter()
+        eng.topk(x, x, d, kk, exclude_self=True)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    print(json.dumps({"metric": "kNN self-join (d 384, kk 10, IP) queries/s", "value": n / t,
+                      "unit": "queries/s", "n_gpus": 1, "steps": len(times),
+                      "higher_is_better": True, "data": "synthetic",
+                      "config": {"workload": f"kNN self-join config shape, {n} rows", "rows": n,
+                                 "d": d, "kk": kk},
+                      "s_per_join": t, "useful_tflops": 2.0 * n * n * d / t / 1e12,
+                      "stats": eng.stats()}), flush=True)
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -398,10 +439,15 @@ def main():
     ap.add_argument("--rows-seed", type=int, default=None,
                     help="draw rank r's rows with seed rows_seed + r (default: rank 0 assigns "
                          "the training rows, rank r > 0 fresh rows drawn with seed r)")
+    ap.add_argument("--knn", type=int, default=0,
+                    help="instead of the headline: the kNN self-join config's shape on this "
+                         "many rows (one GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.knn:
+        run_knn(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
