@@ -222,22 +222,6 @@ __device__ __forceinline__ void tmem_tie(uint32_t (&a)[16]) {
                  "+r"(a[6]), "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]),
                  "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]));
 }
-// Wait for this thread's TMEM loads. The registers of the group just loaded
-// are tied to the wait (and to an empty statement after it), so the compiler
-// cannot move their first use above the point where they are valid.
-__device__ __forceinline__ void tmem_wait_tied(uint32_t (&a)[16], uint32_t (&b)[16]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]),
-                 "+r"(a[6]), "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]),
-                 "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15])
-               :
-               : "memory");
-  asm volatile(""
-               : "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]),
-                 "+r"(b[6]), "+r"(b[7]), "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]),
-                 "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15]));
-}
-
 // Keep only the entries of a row's candidate list still inside the window
 // (out of line: it runs only when a list nears its capacity). Entries are
 // read eight at a time before any of them is written back: every write goes
