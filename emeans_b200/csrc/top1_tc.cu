@@ -766,17 +766,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int j = 0; j < w2; j++) t[j] = IP ? fmaxf(t[j], t[j + w2]) : fminf(t[j], t[j + w2]);
           if constexpr (TOPK) {
-            // Columns above the kk-th best enter the best-kk values (rare once
-            // the row has seen a few tiles), read back from the warp's slab.
+            // Columns above the kk-th best enter the best-kk values. One such
+            // column in the group (the usual case once the row has seen a few
+            // tiles) is the group's best, t[0]; two or more are read back from
+            // the warp's slab.
             const bool upd = collect && t[0] > kth;
-            if (__any_sync(0xFFFFFFFFu, upd)) {
+            uint32_t m_up = 0;
+            if (upd) {
+#pragma unroll
+              for (int j = 0; j < 16; j++) m_up |= (uint32_t)(s[j] > kth) << j;
+            }
+            const int nup = __popc(m_up);
+            if (nup == 1) {
+              kv[0] = t[0];
+#pragma unroll
+              for (int a = 0; a + 1 < KMAX; a++) {
+                const float lo_v = fminf(kv[a], kv[a + 1]), hi_v = fmaxf(kv[a], kv[a + 1]);
+                kv[a] = lo_v;
+                kv[a + 1] = hi_v;
+              }
+              kth = kv[0];
+            }
+            if (__any_sync(0xFFFFFFFFu, nup > 1)) {
 #pragma unroll
               for (int j = 0; j < 16; j++) svs[j * 32] = s[j];
               __syncwarp();
-              if (upd) {
-                uint32_t m_up = 0;
-#pragma unroll
-                for (int j = 0; j < 16; j++) m_up |= (uint32_t)(s[j] > kth) << j;
+              if (nup > 1) {
                 while (m_up) {
                   const int j = __ffs(m_up) - 1;
                   m_up &= m_up - 1;
@@ -806,15 +821,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             adm |= (uint32_t)(TOPK ? (s[j] >= thr && s[j] > -INFINITY)
                                    : (IP ? (s[j] >= thr) : (s[j] <= thr))) << j;
           if (!collect) adm = 0;
-          // Appends: the warp stages the group's values in its slab only when
-          // some lane admits a column; each admitting lane then walks its set
-          // bits (usually one or two) and reads the values back by index.
-          if (__any_sync(0xFFFFFFFFu, adm != 0)) {
+          // Appends. A single admitted column is the group's best, t[0], and
+          // is appended directly; for two or more the warp stages the group's
+          // values in its slab and each such lane walks its set bits, reading
+          // the values back by index.
+          const int na = __popc(adm);
+          if (TOPK && na == 1) {
+            if (cnt + 1 > CAP) cnt = compact_list<IP>(row_list, P.m, cnt, thr);
+            if (cnt < CAP)
+              row_list[cnt * P.m] =
+                  make_uint2((uint32_t)(col0 + g * 16 + __ffs(adm) - 1), __float_as_uint(t[0]));
+            overflow |= cnt >= CAP;
+            cnt += cnt < CAP;
+          }
+          if (__any_sync(0xFFFFFFFFu, TOPK ? na > 1 : na > 0)) {
 #pragma unroll
             for (int j = 0; j < 16; j++) svs[j * 32] = s[j];
             __syncwarp();
-            if (adm) {
-              if (cnt + (uint32_t)__popc(adm) > CAP) cnt = compact_list<IP>(row_list, P.m, cnt, thr);
+            if (TOPK ? na > 1 : na > 0) {
+              if (cnt + (uint32_t)na > CAP) cnt = compact_list<IP>(row_list, P.m, cnt, thr);
               const uint32_t base = (uint32_t)(col0 + g * 16);
               while (adm) {
                 const int j = __ffs(adm) - 1;
