@@ -144,10 +144,23 @@ __global__ void k_ema(float* __restrict__ pos, float* __restrict__ usage,
     float w = __fdiv_rn(step, mass);
     float* c = pos + j * d;
     const float* s = sums + j * d;
-    for (int t = threadIdx.x; t < d; t += blockDim.x) {
-      float mean = __fdiv_rn(s[t], count);
-      float ct = c[t];
-      c[t] = w == 1.0f ? mean : __fadd_rn(ct, __fmul_rn(w, __fsub_rn(mean, ct)));
+    // Four elements per thread per round, their loads issued together.
+    for (int t0 = threadIdx.x; t0 < d; t0 += 4 * blockDim.x) {
+      float sv[4], cv[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int t = t0 + u * blockDim.x;
+        sv[u] = t < d ? s[t] : 0.0f;
+        cv[u] = t < d ? c[t] : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int t = t0 + u * blockDim.x;
+        if (t < d) {
+          const float mean = __fdiv_rn(sv[u], count);
+          c[t] = w == 1.0f ? mean : __fadd_rn(cv[u], __fmul_rn(w, __fsub_rn(mean, cv[u])));
+        }
+      }
     }
   }
   __syncthreads();  // every thread has read usage[j]
@@ -195,15 +208,27 @@ __global__ void k_split(float* __restrict__ pos, float* __restrict__ usage,
 constexpr int kSeg = 256;  // positions per segment (one warp ranks a segment)
 
 // In-segment stable rank of every position among positions with its label,
-// and the per-(segment, label) counts.
-__global__ void k_seg_rank(const uint32_t* __restrict__ labels, long r0, long m, uint32_t k,
-                           uint32_t* __restrict__ segcnt, uint32_t* __restrict__ rank,
-                           uint32_t* status) {
+// and the per-(segment, label) counts. With SMEM (k <= kRankSmem) each warp
+// counts in its own shared-memory histogram and writes it out whole at the
+// end (no zeroing pass over segcnt, no global read-modify-writes); otherwise
+// it counts in segcnt, which the caller zeroes.
+constexpr uint32_t kRankSmem = 1024;
+
+template <bool SMEM>
+__global__ void __launch_bounds__(256) k_seg_rank(const uint32_t* __restrict__ labels, long r0,
+                                                  long m, uint32_t k,
+                                                  uint32_t* __restrict__ segcnt,
+                                                  uint32_t* __restrict__ rank, uint32_t* status) {
+  __shared__ uint32_t hist[SMEM ? 8 : 1][SMEM ? kRankSmem : 1];
   long seg = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   int lane = threadIdx.x & 31;
   long segs = (m + kSeg - 1) / kSeg;
   if (seg >= segs) return;
-  uint32_t* cnt = segcnt + seg * (long)k;
+  uint32_t* cnt = SMEM ? hist[threadIdx.x / 32] : segcnt + seg * (long)k;
+  if (SMEM) {
+    for (uint32_t l = lane; l < k; l += 32) cnt[l] = 0;
+    __syncwarp();
+  }
   for (int c = 0; c < kSeg; c += 32) {
     long p = seg * kSeg + c + lane;
     uint32_t l = p < m ? labels[r0 + p] : 0xFFFFFFFFu;
@@ -221,6 +246,8 @@ __global__ void k_seg_rank(const uint32_t* __restrict__ labels, long r0, long m,
     if (valid) rank[p] = base + __popc(peers & ((1u << lane) - 1u));
     __syncwarp();
   }
+  if (SMEM)
+    for (uint32_t l = lane; l < k; l += 32) segcnt[seg * (long)k + l] = cnt[l];
 }
 
 // Per label: exclusive prefix of its counts over segments (in place), and
@@ -369,12 +396,16 @@ void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_
   uint32_t* rank = e->scratch_get<uint32_t>("sc_rank", m ? m : 1);
   uint32_t* start = e->scratch_get<uint32_t>("sc_start", k + 1);
   uint32_t* order = e->scratch_get<uint32_t>("sc_order", m ? m : 1);
-  EB_CUDA(cudaMemsetAsync(segcnt, 0, segs * k * sizeof(uint32_t), e->stream));
+  const bool smem_rank = m > 0 && k <= kRankSmem;
+  if (!smem_rank) EB_CUDA(cudaMemsetAsync(segcnt, 0, segs * k * sizeof(uint32_t), e->stream));
   if (m > 0) {
     const int warps = 8;
-    k_seg_rank<<<blocks_for(segs, warps), warps * 32, 0, e->stream>>>(labels, (long)r0, (long)m,
-                                                                     (uint32_t)k, segcnt, rank,
-                                                                     e->d_status);
+    if (smem_rank)
+      k_seg_rank<true><<<blocks_for(segs, warps), warps * 32, 0, e->stream>>>(
+          labels, (long)r0, (long)m, (uint32_t)k, segcnt, rank, e->d_status);
+    else
+      k_seg_rank<false><<<blocks_for(segs, warps), warps * 32, 0, e->stream>>>(
+          labels, (long)r0, (long)m, (uint32_t)k, segcnt, rank, e->d_status);
     EB_LAUNCH("scatter rank");
   }
   k_seg_scan<<<blocks_for(k, 256), 256, 0, e->stream>>>(segcnt, (long)segs, (uint32_t)k, counts);

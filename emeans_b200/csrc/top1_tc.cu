@@ -1049,9 +1049,13 @@ __device__ __forceinline__ float chain(const float* __restrict__ x, const float*
 // is stored at q ^ (r & 7) so that the per-lane LDS.128 reads are free of
 // bank conflicts. Each pair folds (value, id) into its row's key with an
 // atomic max / min.
-constexpr int EX_COLS = 32, EX_STAGES = 3, EX_WARPS = 8;
-constexpr int EX_WARP_FLOATS = EX_STAGES * 2 * 32 * EX_COLS;  // x and c slices of one warp
-constexpr size_t EX_SMEM = (size_t)EX_WARPS * EX_WARP_FLOATS * sizeof(float);
+// 8 warps x 3 stages per SM (measured: a 2 warps x 12 stages shape was more
+// than twice as slow on a training batch's pairs).
+constexpr int EX_COLS = 32;
+template <int WARPS, int STAGES>
+constexpr size_t ex_smem() {
+  return (size_t)WARPS * STAGES * 2 * 32 * EX_COLS * sizeof(float);
+}
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem)
@@ -1065,7 +1069,7 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <bool IP>
+template <bool IP, int EX_WARPS = 8, int EX_STAGES = 3>
 __global__ void __launch_bounds__(EX_WARPS * 32) k_pairs(
     const float* __restrict__ x, int d, const uint32_t* __restrict__ ids, long p0,
     const float* __restrict__ c, const float* __restrict__ cn, const float* __restrict__ xnorm_row,
@@ -1075,6 +1079,7 @@ __global__ void __launch_bounds__(EX_WARPS * 32) k_pairs(
   extern __shared__ __align__(16) float ex_smem[];
   __shared__ const float* rows_s[EX_WARPS][2][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int EX_WARP_FLOATS = EX_STAGES * 2 * 32 * EX_COLS;  // x and c slices of one warp
   float* xs = ex_smem + warp * EX_WARP_FLOATS;  // [stage][pair][32]
   float* cs = xs + EX_STAGES * 32 * EX_COLS;     // [stage][pair][32]
   const long np = (long)*pair_count;
@@ -1608,14 +1613,27 @@ void set_smem(int device) {
   }
 }
 
-template <bool IP>
-void set_pairs_smem(int device, size_t bytes) {
-  static uint64_t done = 0;
+template <bool IP, int WARPS, int STAGES>
+void set_pairs_smem(int device) {
+  static uint64_t done = 0;  // one instance per kernel shape
   if (!(done >> device & 1)) {
-    EB_CUDA(cudaFuncSetAttribute(k_pairs<IP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)bytes));
+    EB_CUDA(cudaFuncSetAttribute(k_pairs<IP, WARPS, STAGES>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)ex_smem<WARPS, STAGES>()));
     done |= 1ull << device;
   }
+}
+
+// The exact chains of the pairs of a pass of m rows (d % 32 == 0).
+template <bool IP>
+void launch_pairs(eb_engine* e, long m, const float* x, int d, const uint32_t* ids, long p0,
+                  const float* c, const float* cn, const float* xnorm, const uint2* pairs,
+                  const uint32_t* pair_count, uint32_t k, unsigned long long* rkey,
+                  float* xn_pos, uint32_t* bad, float* pval) {
+  const unsigned grid = (unsigned)e->num_sms;
+  set_pairs_smem<IP, 8, 3>(e->device);
+  k_pairs<IP, 8, 3><<<grid, 256, ex_smem<8, 3>(), e->stream>>>(
+      x, d, ids, p0, c, cn, xnorm, pairs, pair_count, m, k, rkey, xn_pos, bad, e->d_status, pval);
 }
 
 template <bool IP>
@@ -1665,10 +1683,8 @@ void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const ExactS
   // The pair count is known on the device only: persistent blocks stride over it.
   const unsigned pgrid = (unsigned)e->num_sms;
   if (a.d % EX_COLS == 0) {
-    set_pairs_smem<IP>(e->device, EX_SMEM);
-    k_pairs<IP><<<pgrid, EX_WARPS * 32, EX_SMEM, e->stream>>>(
-        a.x, (int)a.d, a.ids, c0, a.c, a.cnorm, a.xnorm, S.pairs, S.pair_count, m,
-        (uint32_t)a.k, S.rkey, S.xn_pos, S.bad, e->d_status, nullptr);
+    launch_pairs<IP>(e, m, a.x, (int)a.d, a.ids, c0, a.c, a.cnorm, a.xnorm, S.pairs,
+                     S.pair_count, (uint32_t)a.k, S.rkey, S.xn_pos, S.bad, nullptr);
   } else {
     k_pairs_plain<IP><<<pgrid * 4, 128, 0, e->stream>>>(
         a.x, (int)a.d, a.ids, c0, a.c, a.cnorm, a.xnorm, S.pairs, S.pair_count, m,
@@ -1968,10 +1984,8 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
     EB_LAUNCH("topk collect");
     const unsigned pgrid = (unsigned)e->num_sms;
     if (d % EX_COLS == 0) {
-      set_pairs_smem<true>(e->device, EX_SMEM);
-      k_pairs<true><<<pgrid, EX_WARPS * 32, EX_SMEM, e->stream>>>(
-          q, (int)d, nullptr, (long)c0, data, nullptr, nullptr, pairs, pair_count, (long)mc,
-          (uint32_t)n, nullptr, nullptr, nullptr, e->d_status, pval);
+      launch_pairs<true>(e, (long)mc, q, (int)d, nullptr, (long)c0, data, nullptr, nullptr, pairs,
+                         pair_count, (uint32_t)n, nullptr, nullptr, nullptr, pval);
     } else {
       k_pairs_plain<true><<<pgrid * 4, 128, 0, e->stream>>>(
           q, (int)d, nullptr, (long)c0, data, nullptr, nullptr, pairs, pair_count, (long)mc,
