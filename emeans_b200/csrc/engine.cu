@@ -190,6 +190,8 @@ int eb_engine_destroy(eb_engine* e) {
     for (auto& kv : e->scratch)
       if (kv.second.p) cudaFreeAsync(kv.second.p, e->stream);
     cudaStreamSynchronize(e->stream);
+    for (auto& kv : e->pinned)
+      if (kv.second.p) cudaFreeHost(kv.second.p);
     cudaFree(e->d_status);
     cudaFree(e->d_counters);
     cudaFreeHost(e->h_status);

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <memory>
 #include <stdexcept>
@@ -105,10 +106,35 @@ struct eb_engine {
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> screen_ev;
   std::vector<size_t> screen_ev_rows;
   size_t screen_ev_used = 0;
+  // Generation of the screen's centroid summary (max |c|, norm bound,
+  // non-finite flag): each conversion of a centroid set tags its atomics with
+  // a new generation, so the summary needs no zeroing pass per call.
+  uint32_t cinfo_gen = 0;
   unsigned long long* counters() { return d_counters; }
-
+  // Pinned host buffers (training read-backs), grown on demand, freed with
+  // the engine.
+  std::unordered_map<std::string, eb::Scratch> pinned;
   template <class T>
-  T* scratch_get(const char* name, size_t count) {
+  T* pinned_get(const char* name, size_t count) {
+    auto& s = pinned[name];
+    size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    if (s.bytes < bytes) {
+      if (s.p) {
+        EB_CUDA(cudaStreamSynchronize(stream));  // no copy may still target it
+        cudaFreeHost(s.p);
+        s.p = nullptr;
+        s.bytes = 0;
+      }
+      EB_CUDA(cudaMallocHost(&s.p, bytes));
+      s.bytes = bytes;
+    }
+    return static_cast<T*>(s.p);
+  }
+
+  // Scratch that grows on demand; with `zeroed`, a new allocation is zeroed
+  // (on the stream) before first use.
+  template <class T>
+  T* scratch_get(const char* name, size_t count, bool zeroed = false) {
     auto& s = scratch[name];
     size_t bytes = count * sizeof(T);
     if (bytes == 0) bytes = 16;
@@ -117,12 +143,44 @@ struct eb_engine {
       size_t want = bytes + bytes / 4;
       EB_CUDA(cudaMallocAsync(&s.p, want, stream));
       s.bytes = want;
+      if (zeroed) EB_CUDA(cudaMemsetAsync(s.p, 0, want, stream));
     }
     return static_cast<T*>(s.p);
   }
 };
 
 namespace eb {
+
+#ifndef EB_PDL
+#define EB_PDL 1
+#endif
+#ifdef __CUDACC__
+// Programmatic dependent launch: kernels on the hot paths are launched with
+// launch_pdl, which lets the device schedule a kernel while its predecessor on
+// the stream drains (no launch gap); every such kernel begins with pdl_wait(),
+// which returns once the predecessor has completed and its writes are
+// visible. In a kernel launched without the attribute it returns at once.
+// (Measured: also letting the next kernel be scheduled as soon as every
+// block of this one has started, griddepcontrol.launch_dependents, made the
+// training loop slower.)
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+void launch_pdl(eb_engine* e, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = e->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = EB_PDL;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cuda_check(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), "kernel launch");
+}
+#endif
 
 eb_buf* new_buf(eb_engine* e, int dtype, size_t len);
 void free_buf(eb_engine* e, eb_buf* b);
@@ -156,6 +214,12 @@ void split(eb_engine* e, float* pos, float* usage, const uint32_t* d_pairs, size
 void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids, size_t r0,
                  size_t r1, const uint32_t* labels, size_t k, float* sums, uint32_t* counts,
                  float* acc);
+// cnt[l] = occurrences of label l in labels[0 .. m).
+void label_counts(eb_engine* e, const uint32_t* labels, size_t m, size_t k, uint32_t* cnt);
+// out = sums / count per centroid, pos where the count is 0 (closing means
+// before any renormalisation).
+void closing_means(eb_engine* e, const float* pos, const float* sums, const uint32_t* cnt,
+                   size_t k, size_t d, float* out);
 
 // ---- top1_exact.cu: the exact FP32 SIMT kernels
 struct Top1Args {

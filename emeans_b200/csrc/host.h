@@ -28,12 +28,8 @@ class Mt19937 {
     idx_ = 624;
   }
   uint32_t u32() {
-    if (idx_ == 624) refill();
-    uint32_t y = st_[idx_++];
-    y ^= y >> 11;
-    y ^= (y << 7) & 0x9d2c5680u;
-    y ^= (y << 15) & 0xefc60000u;
-    return y ^ (y >> 18);
+    if (__builtin_expect(idx_ == 624, 0)) refill();
+    return out_[idx_++];
   }
   // random_sample(): a 53-bit double in [0, 1) (rng.rs:63-67).
   double sample() {
@@ -67,14 +63,28 @@ class Mt19937 {
   }
 
  private:
+  static uint32_t twist(uint32_t a, uint32_t b, uint32_t c) {
+    const uint32_t y = (a & 0x80000000u) | (b & 0x7fffffffu);
+    return c ^ (y >> 1) ^ ((0u - (y & 1u)) & 0x9908b0dfu);
+  }
+  // The next 624 words of state, then all 624 outputs tempered at once (the
+  // loops carry no modulo and the tempering vectorises).
   void refill() {
-    for (int i = 0; i < 624; i++) {
-      uint32_t y = (st_[i] & 0x80000000u) | (st_[(i + 1) % 624] & 0x7fffffffu);
-      st_[i] = st_[(i + 397) % 624] ^ (y >> 1) ^ ((y & 1u) ? 0x9908b0dfu : 0u);
+    int i = 0;
+    for (; i < 227; i++) st_[i] = twist(st_[i], st_[i + 1], st_[i + 397]);
+    for (; i < 623; i++) st_[i] = twist(st_[i], st_[i + 1], st_[i - 227]);
+    st_[623] = twist(st_[623], st_[0], st_[396]);
+    for (int j = 0; j < 624; j++) {
+      uint32_t y = st_[j];
+      y ^= y >> 11;
+      y ^= (y << 7) & 0x9d2c5680u;
+      y ^= (y << 15) & 0xefc60000u;
+      out_[j] = y ^ (y >> 18);
     }
     idx_ = 0;
   }
   uint32_t st_[624];
+  uint32_t out_[624];
   int idx_;
 };
 

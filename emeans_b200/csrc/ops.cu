@@ -35,6 +35,7 @@ __device__ __forceinline__ float row_sumsq(const float* __restrict__ r, int d) {
 }
 
 __global__ void k_row_sumsq(const float* __restrict__ m, long rows, int d, float* __restrict__ out) {
+  pdl_wait();
   long r = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (r < rows) out[r] = row_sumsq(m + r * d, d);
 }
@@ -49,6 +50,7 @@ constexpr int NS_ROWS = 32, NS_STAGES = 8;
 template <int R>
 __global__ void __launch_bounds__(32) k_row_sumsq_staged(const float* __restrict__ m, long rows,
                                                          int d, float* __restrict__ out) {
+  pdl_wait();
   __shared__ __align__(16) float buf[NS_STAGES][R][32];
   const int t = threadIdx.x;
   const long r0 = (long)blockIdx.x * R;
@@ -95,6 +97,7 @@ __global__ void __launch_bounds__(32) k_row_sumsq_staged(const float* __restrict
 __global__ void k_sel_sumsq(const float* __restrict__ x, long n, int d,
                             const uint32_t* __restrict__ ids, long r0, long r1,
                             float* __restrict__ out, uint32_t* status) {
+  pdl_wait();
   long p = r0 + (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= r1) return;
   long row = ids ? (long)ids[p] : p;
@@ -110,6 +113,7 @@ __global__ void k_sel_sumsq(const float* __restrict__ x, long n, int d,
 // divide by max |v| (zero rows keep 1), then by sqrt of the sequential sum of
 // squares of the scaled row.
 __global__ void k_normalize(const float* __restrict__ src, long rows, int d, float* __restrict__ dst) {
+  pdl_wait();
   long r = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
   const float* a = src + r * d;
@@ -131,6 +135,7 @@ __global__ void k_normalize(const float* __restrict__ src, long rows, int d, flo
 __global__ void k_ema(float* __restrict__ pos, float* __restrict__ usage,
                       const float* __restrict__ sums, const uint32_t* __restrict__ counts, int d,
                       float a32, float decay, int replace) {
+  pdl_wait();
   long j = blockIdx.x;
   float u = usage[j];
   uint32_t cnt = counts[j];
@@ -170,6 +175,7 @@ __global__ void k_ema(float* __restrict__ pos, float* __restrict__ usage,
 // Revival splits, one block per (donor, dead) pair (core/mod.rs:374-399).
 __global__ void k_split(float* __restrict__ pos, float* __restrict__ usage,
                         const uint32_t* __restrict__ pairs, int d) {
+  pdl_wait();
   uint32_t s = pairs[2 * blockIdx.x], t = pairs[2 * blockIdx.x + 1];
   const float eps = (float)1e-4;
   float* cs = pos + (long)s * d;
@@ -219,6 +225,7 @@ __global__ void __launch_bounds__(256) k_seg_rank(const uint32_t* __restrict__ l
                                                   long m, uint32_t k,
                                                   uint32_t* __restrict__ segcnt,
                                                   uint32_t* __restrict__ rank, uint32_t* status) {
+  pdl_wait();
   __shared__ uint32_t hist[SMEM ? 8 : 1][SMEM ? kRankSmem : 1];
   long seg = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   int lane = threadIdx.x & 31;
@@ -254,6 +261,7 @@ __global__ void __launch_bounds__(256) k_seg_rank(const uint32_t* __restrict__ l
 // the label's total.
 __global__ void k_seg_scan(uint32_t* __restrict__ segcnt, long segs, uint32_t k,
                            uint32_t* __restrict__ counts) {
+  pdl_wait();
   uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
   if (l >= k) return;
   uint32_t run = 0;
@@ -275,6 +283,7 @@ __global__ void k_seg_scan(uint32_t* __restrict__ segcnt, long segs, uint32_t k,
 // Exclusive scan of counts into start[0..k], one block.
 __global__ void k_label_scan(const uint32_t* __restrict__ counts, uint32_t k,
                              uint32_t* __restrict__ start) {
+  pdl_wait();
   __shared__ uint32_t part[1024];
   uint32_t per = (k + blockDim.x - 1) / blockDim.x;
   uint32_t lo = threadIdx.x * per, hi = min(lo + per, k);
@@ -301,6 +310,7 @@ __global__ void k_place(const uint32_t* __restrict__ labels, const uint32_t* __r
                         long r0, long m, long n, uint32_t k, const uint32_t* __restrict__ segcnt,
                         const uint32_t* __restrict__ start, const uint32_t* __restrict__ rank,
                         uint32_t* __restrict__ order, uint32_t* status) {
+  pdl_wait();
   long p = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= m) return;
   uint32_t l = labels[r0 + p];
@@ -319,6 +329,7 @@ __global__ void k_place(const uint32_t* __restrict__ labels, const uint32_t* __r
 __global__ void k_seg_sum(const float* __restrict__ x, int d, const uint32_t* __restrict__ order,
                           const uint32_t* __restrict__ start, float* __restrict__ sums,
                           float* __restrict__ acc) {
+  pdl_wait();
   long j = blockIdx.x;
   int t = blockIdx.y * blockDim.x + threadIdx.x;
   if (t >= d) return;
@@ -337,6 +348,47 @@ __global__ void k_seg_sum(const float* __restrict__ x, int d, const uint32_t* __
   if (acc) acc[j * d + t] = __fadd_rn(acc[j * d + t], s);
 }
 
+// Count of every label among labels[0 .. m) into cnt (zeroed by the caller);
+// per-block shared-memory histograms when k is small. Integer counts: the
+// order of the additions does not matter.
+constexpr uint32_t kHistSmem = 4096;
+__global__ void k_label_hist(const uint32_t* __restrict__ labels, long m, uint32_t k,
+                             uint32_t* __restrict__ cnt) {
+  pdl_wait();
+  __shared__ uint32_t h[kHistSmem];
+  const bool sm = k <= kHistSmem;
+  if (sm) {
+    for (uint32_t l = threadIdx.x; l < k; l += blockDim.x) h[l] = 0;
+    __syncthreads();
+  }
+  for (long p = (long)blockIdx.x * blockDim.x + threadIdx.x; p < m;
+       p += (long)gridDim.x * blockDim.x) {
+    const uint32_t l = labels[p];
+    if (l < k) atomicAdd(sm ? &h[l] : &cnt[l], 1u);
+  }
+  if (sm) {
+    __syncthreads();
+    for (uint32_t l = threadIdx.x; l < k; l += blockDim.x)
+      if (h[l]) atomicAdd(&cnt[l], h[l]);
+  }
+}
+
+// closing_means before the spherical renormalisation (core/mod.rs:404-429):
+// a centroid with rows in the closing pass takes sums / (float)count, one
+// without keeps its position.
+__global__ void k_closing(const float* __restrict__ pos, const float* __restrict__ sums,
+                          const uint32_t* __restrict__ cnt, long k, int d,
+                          float* __restrict__ out) {
+  pdl_wait();
+  const long j = blockIdx.x;
+  const uint32_t c = cnt[j];
+  const float nf = __uint2float_rn(c);
+  for (int t = threadIdx.x; t < d; t += blockDim.x) {
+    const long q = j * d + t;
+    out[q] = c > 0 ? __fdiv_rn(sums[q], nf) : pos[q];
+  }
+}
+
 unsigned blocks_for(size_t n, unsigned per) { return (unsigned)((n + per - 1) / per); }
 
 }  // namespace
@@ -345,12 +397,12 @@ void row_norms(eb_engine* e, const float* m, size_t rows, size_t d, float* out) 
   if (rows == 0) return;
   if (d % 32 == 0 && ((uintptr_t)m & 15) == 0) {
     if (rows <= (size_t)e->num_sms * 32)
-      k_row_sumsq_staged<8><<<blocks_for(rows, 8), 32, 0, e->stream>>>(m, (long)rows, (int)d, out);
+      launch_pdl(e, k_row_sumsq_staged<8>, blocks_for(rows, 8), 32, 0, m, (long)rows, (int)d, out);
     else
-      k_row_sumsq_staged<NS_ROWS><<<blocks_for(rows, NS_ROWS), 32, 0, e->stream>>>(m, (long)rows,
+      launch_pdl(e, k_row_sumsq_staged<NS_ROWS>, blocks_for(rows, NS_ROWS), 32, 0, m, (long)rows,
                                                                                   (int)d, out);
   } else {
-    k_row_sumsq<<<blocks_for(rows, kRowThreads), kRowThreads, 0, e->stream>>>(m, (long)rows,
+    launch_pdl(e, k_row_sumsq, blocks_for(rows, kRowThreads), kRowThreads, 0, m, (long)rows,
                                                                               (int)d, out);
   }
   EB_LAUNCH("row_norms");
@@ -359,22 +411,36 @@ void row_norms(eb_engine* e, const float* m, size_t rows, size_t d, float* out) 
 void sel_row_norms(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids,
                    size_t r0, size_t r1, float* out) {
   if (r1 <= r0) return;
-  k_sel_sumsq<<<blocks_for(r1 - r0, kRowThreads), kRowThreads, 0, e->stream>>>(
-      x, (long)n, (int)d, ids, (long)r0, (long)r1, out, e->d_status);
+  launch_pdl(e, k_sel_sumsq, blocks_for(r1 - r0, kRowThreads), kRowThreads, 0, x, (long)n, (int)d, ids, (long)r0, (long)r1, out, e->d_status);
   EB_LAUNCH("sel_row_norms");
 }
 
 void normalize_rows(eb_engine* e, const float* src, size_t rows, size_t d, float* dst) {
   if (rows == 0) return;
-  k_normalize<<<blocks_for(rows, kRowThreads), kRowThreads, 0, e->stream>>>(src, (long)rows,
+  launch_pdl(e, k_normalize, blocks_for(rows, kRowThreads), kRowThreads, 0, src, (long)rows,
                                                                             (int)d, dst);
   EB_LAUNCH("normalize_rows");
+}
+
+void label_counts(eb_engine* e, const uint32_t* labels, size_t m, size_t k, uint32_t* cnt) {
+  EB_CUDA(cudaMemsetAsync(cnt, 0, k * sizeof(uint32_t), e->stream));
+  if (m == 0) return;
+  const unsigned grid = (unsigned)std::min<size_t>(blocks_for(m, 256), (size_t)e->num_sms * 2);
+  launch_pdl(e, k_label_hist, grid, 256, 0, labels, (long)m, (uint32_t)k, cnt);
+  EB_LAUNCH("label_counts");
+}
+
+void closing_means(eb_engine* e, const float* pos, const float* sums, const uint32_t* cnt,
+                   size_t k, size_t d, float* out) {
+  if (k == 0) return;
+  launch_pdl(e, k_closing, (unsigned)k, 128, 0, pos, sums, cnt, (long)k, (int)d, out);
+  EB_LAUNCH("closing_means");
 }
 
 void ema_update(eb_engine* e, float* pos, float* usage, const float* sums, const uint32_t* counts,
                 size_t k, size_t d, float alpha, float decay, bool replace) {
   if (k == 0) return;
-  k_ema<<<(unsigned)k, 128, 0, e->stream>>>(pos, usage, sums, counts, (int)d, alpha, decay,
+  launch_pdl(e, k_ema, (unsigned)k, 128, 0, pos, usage, sums, counts, (int)d, alpha, decay,
                                            replace ? 1 : 0);
   EB_LAUNCH("ema_update");
 }
@@ -382,7 +448,7 @@ void ema_update(eb_engine* e, float* pos, float* usage, const float* sums, const
 void split(eb_engine* e, float* pos, float* usage, const uint32_t* d_pairs, size_t npairs,
            size_t d) {
   if (npairs == 0) return;
-  k_split<<<(unsigned)npairs, 128, 0, e->stream>>>(pos, usage, d_pairs, (int)d);
+  launch_pdl(e, k_split, (unsigned)npairs, 128, 0, pos, usage, d_pairs, (int)d);
   EB_LAUNCH("split");
 }
 
@@ -401,25 +467,23 @@ void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_
   if (m > 0) {
     const int warps = 8;
     if (smem_rank)
-      k_seg_rank<true><<<blocks_for(segs, warps), warps * 32, 0, e->stream>>>(
-          labels, (long)r0, (long)m, (uint32_t)k, segcnt, rank, e->d_status);
+      launch_pdl(e, k_seg_rank<true>, blocks_for(segs, warps), warps * 32, 0, labels, (long)r0, (long)m, (uint32_t)k, segcnt, rank, e->d_status);
     else
-      k_seg_rank<false><<<blocks_for(segs, warps), warps * 32, 0, e->stream>>>(
-          labels, (long)r0, (long)m, (uint32_t)k, segcnt, rank, e->d_status);
+      launch_pdl(e, k_seg_rank<false>, blocks_for(segs, warps), warps * 32, 0, labels, (long)r0, (long)m, (uint32_t)k, segcnt, rank, e->d_status);
     EB_LAUNCH("scatter rank");
   }
-  k_seg_scan<<<blocks_for(k, 256), 256, 0, e->stream>>>(segcnt, (long)segs, (uint32_t)k, counts);
+  launch_pdl(e, k_seg_scan, blocks_for(k, 256), 256, 0, segcnt, (long)segs, (uint32_t)k, counts);
   EB_LAUNCH("scatter seg scan");
-  k_label_scan<<<1, 1024, 0, e->stream>>>(counts, (uint32_t)k, start);
+  launch_pdl(e, k_label_scan, 1, 1024, 0, counts, (uint32_t)k, start);
   EB_LAUNCH("scatter label scan");
   if (m > 0) {
-    k_place<<<blocks_for(m, 256), 256, 0, e->stream>>>(labels, ids, (long)r0, (long)m, (long)n,
+    launch_pdl(e, k_place, blocks_for(m, 256), 256, 0, labels, ids, (long)r0, (long)m, (long)n,
                                                        (uint32_t)k, segcnt, start, rank, order,
                                                        e->d_status);
     EB_LAUNCH("scatter place");
   }
   dim3 grid((unsigned)k, blocks_for(d, 128));
-  k_seg_sum<<<grid, 128, 0, e->stream>>>(x, (int)d, order, start, sums, acc);
+  launch_pdl(e, k_seg_sum, grid, 128, 0, x, (int)d, order, start, sums, acc);
   EB_LAUNCH("scatter sum");
 }
 
@@ -433,6 +497,7 @@ namespace {
 
 __global__ void k_shard_pack(const uint32_t* __restrict__ labels, const float* __restrict__ scores,
                              long len, long s, uint32_t* __restrict__ stage) {
+  pdl_wait();
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= s) return;
   stage[i] = i < len ? labels[i] : 0u;
@@ -441,6 +506,7 @@ __global__ void k_shard_pack(const uint32_t* __restrict__ labels, const float* _
 
 __global__ void k_shard_unpack(const uint32_t* __restrict__ stage, long total, long s,
                                uint32_t* __restrict__ labels, float* __restrict__ scores) {
+  pdl_wait();
   const long p = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= total) return;
   const long q = p / s, i = p - q * s;
@@ -453,7 +519,7 @@ __global__ void k_shard_unpack(const uint32_t* __restrict__ stage, long total, l
 void shard_pack(eb_engine* e, const uint32_t* labels, const float* scores, size_t len, size_t s,
                 uint32_t* stage) {
   if (s == 0) return;
-  k_shard_pack<<<blocks_for(s, 256), 256, 0, e->stream>>>(labels, scores, (long)len, (long)s,
+  launch_pdl(e, k_shard_pack, blocks_for(s, 256), 256, 0, labels, scores, (long)len, (long)s,
                                                          stage + (size_t)e->rank * 2 * s);
   EB_LAUNCH("shard_pack");
 }
@@ -462,7 +528,7 @@ void shard_unpack(eb_engine* e, const uint32_t* stage, size_t total, size_t s, i
                   uint32_t* labels, float* scores) {
   (void)world;
   if (total == 0) return;
-  k_shard_unpack<<<blocks_for(total, 256), 256, 0, e->stream>>>(stage, (long)total, (long)s,
+  launch_pdl(e, k_shard_unpack, blocks_for(total, 256), 256, 0, stage, (long)total, (long)s,
                                                                 labels, scores);
   EB_LAUNCH("shard_unpack");
 }

@@ -259,6 +259,7 @@ __global__ void k_prep_rows(const float* __restrict__ x, long n, int d, int dp,
                             const uint32_t* __restrict__ ids, long p0, long m,
                             __half* __restrict__ xh, __half* __restrict__ xl,
                             int* __restrict__ xexp, float* __restrict__ xnrm, uint32_t* status) {
+  pdl_wait();
   const long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (i >= m) return;
@@ -352,6 +353,7 @@ __global__ void k_gather_rows(const __half* __restrict__ src_h, const __half* __
                               long n, int dp, const uint32_t* __restrict__ ids, long p0, long m,
                               __half* __restrict__ xh, __half* __restrict__ xl,
                               int* __restrict__ xexp, float* __restrict__ xnrm, uint32_t* status) {
+  pdl_wait();
   const long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (i >= m) return;
@@ -380,11 +382,22 @@ __global__ void k_gather_rows(const __half* __restrict__ src_h, const __half* __
   }
 }
 
-// Global max |c|, a bound on max |c_j| and a non-finite flag, over all centroids.
-// cinfo (u32): [0] bits of max|c|, [1] bits of the norm bound, [2] non-finite flag.
-// One warp per centroid, two per block; 16-byte loads when the rows allow.
+// The centroid summary: u64 words (generation << 32 | payload), [0] bits of
+// max |c|, [1] bits of a bound on max |c_j|, [2] non-finite flag. The words
+// are atomic maxima, so a word from an older generation (a smaller tag) is
+// replaced by the first write of this one; a reader takes a word whose tag is
+// not the current generation as 0.
+__device__ __forceinline__ uint32_t cinfo_word(const unsigned long long* ci, int w, uint32_t gen) {
+  const unsigned long long v = ci[w];
+  return (uint32_t)(v >> 32) == gen ? (uint32_t)v : 0u;
+}
+
+// Global max |c|, a bound on max |c_j| and a non-finite flag, over all
+// centroids, into the summary of generation gen. One warp per centroid, two
+// per block; 16-byte loads when the rows allow.
 __global__ void __launch_bounds__(64) k_cent_max(const float* __restrict__ c, long k, int d,
-                                                 uint32_t* cinfo) {
+                                                 unsigned long long* cinfo, uint32_t gen) {
+  pdl_wait();
   const long j = (long)blockIdx.x * 2 + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (j >= k) return;
@@ -418,12 +431,13 @@ __global__ void __launch_bounds__(64) k_cent_max(const float* __restrict__ c, lo
   }
   finite = __all_sync(0xFFFFFFFFu, finite);
   if (lane == 0) {
+    const unsigned long long tag = (unsigned long long)gen << 32;
     if (!finite) {
-      atomicOr(&cinfo[2], 1u);
+      atomicMax(&cinfo[2], tag | 1ull);
       return;
     }
-    atomicMax(&cinfo[0], __float_as_uint(mx));
-    atomicMax(&cinfo[1], __float_as_uint(sqrtf(ss) * (1.0f + 1.0f / 512.0f)));
+    atomicMax(&cinfo[0], tag | __float_as_uint(mx));
+    atomicMax(&cinfo[1], tag | __float_as_uint(sqrtf(ss) * (1.0f + 1.0f / 512.0f)));
   }
 }
 
@@ -432,16 +446,18 @@ __global__ void __launch_bounds__(64) k_cent_max(const float* __restrict__ c, lo
 // rows allow 16-byte loads (dp is a multiple of 32, so the padding is whole
 // groups of four).
 __global__ void __launch_bounds__(64) k_cent_conv(const float* __restrict__ c, long k, int d,
-                                                  int dp, const uint32_t* __restrict__ cinfo,
-                                                  __half* __restrict__ ch,
+                                                  int dp,
+                                                  const unsigned long long* __restrict__ cinfo,
+                                                  uint32_t gen, __half* __restrict__ ch,
                                                   __half* __restrict__ cl) {
+  pdl_wait();
   const long j = (long)blockIdx.x * 2 + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (j >= k) return;
   int ec = 0;
-  frexpf(__uint_as_float(cinfo[0]), &ec);
+  frexpf(__uint_as_float(cinfo_word(cinfo, 0, gen)), &ec);
   const int sh = 14 - ec;
-  const bool bad = cinfo[2] != 0;
+  const bool bad = cinfo_word(cinfo, 2, gen) != 0;
   const float* r = c + j * (long)d;
   __half* oh = ch + j * (long)dp;
   __half* ol = cl + j * (long)dp;
@@ -477,7 +493,8 @@ struct ScreenParams {
   const int* xexp;     // per staging row
   const float* xnrm;   // per staging row
   const float* cn;     // k squared centroid norms (L2) or null
-  const uint32_t* cinfo;
+  const unsigned long long* cinfo;  // the centroid summary of generation cgen
+  uint32_t cgen;
   float e_rel, e_abs, e_min;  // bound coefficients (see the header comment)
   // Candidate lists, one per (half tile, row): half h, entry e of row i at
   // (h CAP + e) m + i (id, screened value bits).
@@ -493,6 +510,10 @@ struct ScreenParams {
   long col_gid0;       // global id of column 0 (a database shard's offset)
   float* kvals;        // 2 m x KMAX: each (half, row)'s best kk values, ascending
   float* roff;         // m: each row's window 2e
+  // Counters of the exact stage that follows (pairs, exact list), zeroed by
+  // the screen's first thread.
+  uint32_t* zero0;
+  uint32_t* zero1;
 };
 
 template <bool IP, bool TOPK = false>
@@ -500,6 +521,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     k_screen(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
              const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
              ScreenParams P) {
+  pdl_wait();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
@@ -515,6 +537,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) {
+      if (P.zero0) *P.zero0 = 0u;
+      if (P.zero1) *P.zero1 = 0u;
+    }
     for (int s = 0; s < STAGES; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -625,9 +651,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int hf = (warp - 4) >> 2;
     const int r = q * 32 + lane;
     int ec = 0;
-    frexpf(__uint_as_float(P.cinfo[0]), &ec);
-    const float cmax = __uint_as_float(P.cinfo[1]);
-    const bool c_bad = P.cinfo[2] != 0;
+    frexpf(__uint_as_float(cinfo_word(P.cinfo, 0, P.cgen)), &ec);
+    const float cmax = __uint_as_float(cinfo_word(P.cinfo, 1, P.cgen));
+    const bool c_bad = cinfo_word(P.cinfo, 2, P.cgen) != 0;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(hf * HALF);
     float* cns = cn_s + (warp - 4) * HALF;
     float* svs = sv_s + (warp - 4) * 16 * 32 + lane;  // this lane's column of the slab
@@ -929,7 +955,9 @@ __global__ void __launch_bounds__(256) k_collect(
     uint2* __restrict__ pairs, uint32_t* __restrict__ pair_count,
     unsigned long long* __restrict__ rkey, uint32_t* __restrict__ list,
     uint32_t* __restrict__ list_count, unsigned long long* __restrict__ lkey,
-    unsigned long long* __restrict__ counters, uint32_t* __restrict__ status) {
+    uint32_t* __restrict__ bad, unsigned long long* __restrict__ counters,
+    uint32_t* __restrict__ status) {
+  pdl_wait();
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const bool live = i < m;
   uint32_t cnt[2];
@@ -971,7 +999,10 @@ __global__ void __launch_bounds__(256) k_collect(
   fb = fb || ns == 0 || ns > SURV;
   const bool listed = live && fb;
   const uint32_t np = live && !fb ? ns : 0;
-  if (live) rkey[i] = IP ? 0ull : ~0ull;
+  if (live) {
+    rkey[i] = IP ? 0ull : ~0ull;
+    bad[i] = 0u;
+  }
   const uint32_t lp = warp_append(list_count, listed ? 1u : 0u);
   if (listed) {
     list[lp] = (uint32_t)(p0 + i);
@@ -1076,6 +1107,7 @@ __global__ void __launch_bounds__(EX_WARPS * 32) k_pairs(
     const uint2* __restrict__ pairs, const uint32_t* __restrict__ pair_count, long m, uint32_t k,
     unsigned long long* __restrict__ rkey, float* __restrict__ xn_pos,
     uint32_t* __restrict__ bad, uint32_t* __restrict__ status, float* __restrict__ pval) {
+  pdl_wait();
   extern __shared__ __align__(16) float ex_smem[];
   __shared__ const float* rows_s[EX_WARPS][2][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1086,7 +1118,10 @@ __global__ void __launch_bounds__(EX_WARPS * 32) k_pairs(
   const int nsl = d / EX_COLS;
   const bool want_xn = !IP && !xnorm_row;
   const long stride = (long)gridDim.x * EX_WARPS;
-  for (long wt = (long)blockIdx.x * EX_WARPS + warp; wt * 32 < np; wt += stride) {
+  // Consecutive 32-pair tiles go to different SMs, so that a small pass
+  // (a training batch) spreads over all of them. (Measured: an L2 prefetch of
+  // each tile's whole rows made large passes slower.)
+  for (long wt = (long)warp * gridDim.x + blockIdx.x; wt * 32 < np; wt += stride) {
     const long pi = wt * 32 + lane;
     bool mine = pi < np;
     uint2 pr = make_uint2(0, 0);
@@ -1174,6 +1209,7 @@ __global__ void k_pairs_plain(const float* __restrict__ x, int d, const uint32_t
                               unsigned long long* __restrict__ rkey, float* __restrict__ xn_pos,
                               uint32_t* __restrict__ bad, uint32_t* __restrict__ status,
                               float* __restrict__ pval) {
+  pdl_wait();
   const long np = (long)*pair_count;
   for (long pi = (long)blockIdx.x * blockDim.x + threadIdx.x; pi < np;
        pi += (long)gridDim.x * blockDim.x) {
@@ -1226,6 +1262,7 @@ __global__ void __launch_bounds__(256) k_finish(
     const uint32_t* __restrict__ bad, uint32_t* __restrict__ labels, float* __restrict__ scores,
     uint32_t* __restrict__ list, uint32_t* __restrict__ list_count,
     unsigned long long* __restrict__ lkey, unsigned long long* __restrict__ counters) {
+  pdl_wait();
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const bool live = i < m;
   const bool listed = live && bad[i];
@@ -1274,6 +1311,7 @@ __global__ void __launch_bounds__(LS_C) k_list(
     const uint32_t* __restrict__ list, const uint32_t* __restrict__ list_count,
     unsigned long long* __restrict__ lkey, const float* __restrict__ xnorm_row,
     float* __restrict__ lxn, uint32_t* __restrict__ status) {
+  pdl_wait();
   extern __shared__ __align__(16) float ls_smem[];
   float* cs = ls_smem;                                 // [stage][LS_C][32]
   float* xs = ls_smem + LS_STAGES * LS_C * EX_COLS;    // [stage][32]
@@ -1393,6 +1431,7 @@ __global__ void k_list_finish(const float* __restrict__ x, long n, int d,
                               const unsigned long long* __restrict__ lkey,
                               const float* __restrict__ xnorm_row, const float* __restrict__ lxn,
                               uint32_t* __restrict__ labels, float* __restrict__ scores) {
+  pdl_wait();
   const long cnt = (long)*list_count;
   for (long ent = (long)blockIdx.x * blockDim.x + threadIdx.x; ent < cnt;
        ent += (long)gridDim.x * blockDim.x) {
@@ -1425,6 +1464,7 @@ __global__ void __launch_bounds__(256) k_collect_topk(
     uint32_t* __restrict__ pstart, uint32_t* __restrict__ pcnt, uint32_t* __restrict__ list,
     uint32_t* __restrict__ list_count, unsigned long long* __restrict__ counters,
     uint32_t* __restrict__ status) {
+  pdl_wait();
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const bool live = i < m;
   uint32_t cnt[2] = {0, 0};
@@ -1511,6 +1551,7 @@ __global__ void k_topk_finish(long p0, long m, int kk, uint32_t id0,
                               const uint32_t* __restrict__ pcnt, const uint2* __restrict__ pairs,
                               const float* __restrict__ pval, uint32_t* __restrict__ ids,
                               float* __restrict__ sims) {
+  pdl_wait();
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= m) return;
   const uint32_t np = pcnt[i];
@@ -1551,6 +1592,7 @@ __global__ void k_topk_finish(long p0, long m, int kk, uint32_t id0,
 // Gather the rows of listed queries (global positions) into a dense block.
 __global__ void k_gather_queries(const float* __restrict__ q, int d, const uint32_t* __restrict__ list,
                                  long L, float* __restrict__ out) {
+  pdl_wait();
   const long t = (long)blockIdx.y * gridDim.x + blockIdx.x;
   if (t >= L) return;
   const float* src = q + (long)list[t] * d;
@@ -1562,6 +1604,7 @@ __global__ void k_gather_queries(const float* __restrict__ q, int d, const uint3
 __global__ void k_scatter_topk(const uint32_t* __restrict__ list, long L, int kk,
                                const uint32_t* __restrict__ tids, const float* __restrict__ tsims,
                                uint32_t* __restrict__ ids, float* __restrict__ sims) {
+  pdl_wait();
   const long u = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (u >= L * kk) return;
   const long t = u / kk, a = u - t * kk;
@@ -1632,8 +1675,7 @@ void launch_pairs(eb_engine* e, long m, const float* x, int d, const uint32_t* i
                   float* xn_pos, uint32_t* bad, float* pval) {
   const unsigned grid = (unsigned)e->num_sms;
   set_pairs_smem<IP, 8, 3>(e->device);
-  k_pairs<IP, 8, 3><<<grid, 256, ex_smem<8, 3>(), e->stream>>>(
-      x, d, ids, p0, c, cn, xnorm, pairs, pair_count, m, k, rkey, xn_pos, bad, e->d_status, pval);
+  launch_pdl(e, k_pairs<IP, 8, 3>, grid, 256, ex_smem<8, 3>(), x, d, ids, p0, c, cn, xnorm, pairs, pair_count, m, k, rkey, xn_pos, bad, e->d_status, pval);
 }
 
 template <bool IP>
@@ -1650,7 +1692,7 @@ template <bool IP, bool TOPK = false>
 void launch_screen(eb_engine* e, unsigned grid, const CUtensorMap& ah, const CUtensorMap& al,
                    const CUtensorMap& bh, const CUtensorMap& bl, const ScreenParams& P) {
   set_smem<IP, TOPK>(e->device);
-  k_screen<IP, TOPK><<<grid, NTHREADS, SMEM_BYTES, e->stream>>>(ah, al, bh, bl, P);
+  launch_pdl(e, k_screen<IP, TOPK>, grid, NTHREADS, SMEM_BYTES, ah, al, bh, bl, P);
 }
 
 // Scratch of the exact stage of one pass of m rows.
@@ -1672,13 +1714,11 @@ struct ExactScratch {
 template <bool IP>
 void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const ExactScratch& S) {
   unsigned long long* counters = e->counters();
-  EB_CUDA(cudaMemsetAsync(S.pair_count, 0, 4, e->stream));
-  EB_CUDA(cudaMemsetAsync(S.list_count, 0, 4, e->stream));
-  EB_CUDA(cudaMemsetAsync(S.bad, 0, m * sizeof(uint32_t), e->stream));
+  // pair_count and list_count were zeroed by the screen; k_collect zeroes bad.
   const unsigned rgrid = (unsigned)((m + 255) / 256);
-  k_collect<IP><<<rgrid, 256, 0, e->stream>>>(c0, m, (uint32_t)a.k, S.cand, S.cand_cnt, S.cand_thr,
+  launch_pdl(e, k_collect<IP>, rgrid, 256, 0, c0, m, (uint32_t)a.k, S.cand, S.cand_cnt, S.cand_thr,
                                               S.pairs, S.pair_count, S.rkey, S.list, S.list_count,
-                                              S.lkey, counters, e->d_status);
+                                              S.lkey, S.bad, counters, e->d_status);
   EB_LAUNCH("screen collect");
   // The pair count is known on the device only: persistent blocks stride over it.
   const unsigned pgrid = (unsigned)e->num_sms;
@@ -1686,12 +1726,11 @@ void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const ExactS
     launch_pairs<IP>(e, m, a.x, (int)a.d, a.ids, c0, a.c, a.cnorm, a.xnorm, S.pairs,
                      S.pair_count, (uint32_t)a.k, S.rkey, S.xn_pos, S.bad, nullptr);
   } else {
-    k_pairs_plain<IP><<<pgrid * 4, 128, 0, e->stream>>>(
-        a.x, (int)a.d, a.ids, c0, a.c, a.cnorm, a.xnorm, S.pairs, S.pair_count, m,
+    launch_pdl(e, k_pairs_plain<IP>, pgrid * 4, 128, 0, a.x, (int)a.d, a.ids, c0, a.c, a.cnorm, a.xnorm, S.pairs, S.pair_count, m,
         (uint32_t)a.k, S.rkey, S.xn_pos, S.bad, e->d_status, nullptr);
   }
   EB_LAUNCH("screen exact chains");
-  k_finish<IP><<<rgrid, 256, 0, e->stream>>>(a.ids, c0, m, a.xnorm, S.xn_pos, S.rkey, S.bad,
+  launch_pdl(e, k_finish<IP>, rgrid, 256, 0, a.ids, c0, m, a.xnorm, S.xn_pos, S.rkey, S.bad,
                                              a.labels, a.scores, S.list, S.list_count, S.lkey,
                                              counters);
   EB_LAUNCH("screen finish");
@@ -1701,14 +1740,47 @@ void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const ExactS
   const long kch = ((long)a.k + LS_C - 1) / LS_C;
   const unsigned lgrid = (unsigned)std::min<long>(m * kch, (long)e->num_sms * 3);
   set_list_smem<IP>(e->device);
-  k_list<IP><<<lgrid, LS_C, LS_SMEM, e->stream>>>(a.x, (long)a.n, (int)a.d, a.ids, a.c, a.cnorm,
+  launch_pdl(e, k_list<IP>, lgrid, LS_C, LS_SMEM, a.x, (long)a.n, (int)a.d, a.ids, a.c, a.cnorm,
                                                  (long)a.k, S.list, S.list_count, S.lkey,
                                                  a.xnorm, S.lxn, e->d_status);
   EB_LAUNCH("screen exact list");
-  k_list_finish<IP><<<(unsigned)std::min<long>((m + 255) / 256, e->num_sms), 256, 0, e->stream>>>(
-      a.x, (long)a.n, (int)a.d, a.ids, S.list, S.list_count, S.lkey, a.xnorm, S.lxn, a.labels,
+  launch_pdl(e, k_list_finish<IP>, (unsigned)std::min<long>((m + 255) / 256, e->num_sms), 256, 0, a.x, (long)a.n, (int)a.d, a.ids, S.list, S.list_count, S.lkey, a.xnorm, S.lxn, a.labels,
       a.scores);
   EB_LAUNCH("screen exact list finish");
+}
+
+}  // namespace
+
+namespace {
+
+// The bound coefficients of the header comment for this d, with 1% slack.
+void screen_bound(size_t d, float& e_rel, float& e_abs, float& e_min) {
+  const double dd = (double)d;
+  const double u24 = std::ldexp(1.0, -24);
+  const double gamma_d = dd * u24 / (1.0 - dd * u24);
+  e_rel = (float)((3.0 * std::ldexp(1.0, -22) + dd * std::ldexp(1.0, -21) * (1.0 + std::ldexp(1.0, -9)) +
+                   dd * std::ldexp(1.0, -30) + std::ldexp(1.0, -23) + gamma_d) *
+                  1.01);
+  e_abs = (float)(std::ldexp(1.0, -23) * std::sqrt(dd) * 1.01);
+  e_min = (float)(dd * std::ldexp(1.0, -48));
+}
+
+
+// The scaled split FP16 copy of k rows of c (centroids, or data rows playing
+// them) and their summary under a new generation, which is returned.
+uint32_t convert_centroids(eb_engine* e, const float* c, size_t k, size_t d, size_t dp,
+                           unsigned long long* cinfo, __half* ch, __half* cl) {
+  if (++e->cinfo_gen == 0) {  // wrapped: older tags could compare higher
+    EB_CUDA(cudaMemsetAsync(cinfo, 0, 4 * sizeof(unsigned long long), e->stream));
+    e->cinfo_gen = 1;
+  }
+  const uint32_t gen = e->cinfo_gen;
+  launch_pdl(e, k_cent_max, (unsigned)((k + 1) / 2), 64, 0, c, (long)k, (int)d, cinfo, gen);
+  EB_LAUNCH("screen centroid max");
+  launch_pdl(e, k_cent_conv, (unsigned)((k + 1) / 2), 64, 0, c, (long)k, (int)d, (int)dp, cinfo,
+                                                            gen, ch, cl);
+  EB_LAUNCH("screen centroid convert");
+  return gen;
 }
 
 }  // namespace
@@ -1730,30 +1802,17 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   const size_t chunk = std::min(m_all, PASS_WAVES * wave);
   const bool ip = a.metric == EB_IP;
 
-  // Bound coefficients for this d (see the header comment), with 1% slack.
-  const double dd = (double)d;
-  const double u24 = std::ldexp(1.0, -24);
-  const double gamma_d = dd * u24 / (1.0 - dd * u24);
-  const float e_rel =
-      (float)((3.0 * std::ldexp(1.0, -22) + dd * std::ldexp(1.0, -21) * (1.0 + std::ldexp(1.0, -9)) +
-               dd * std::ldexp(1.0, -30) + std::ldexp(1.0, -23) + gamma_d) *
-              1.01);
-  const float e_abs = (float)(std::ldexp(1.0, -23) * std::sqrt(dd) * 1.01);
-  const float e_min = (float)(dd * std::ldexp(1.0, -48));
+  float e_rel, e_abs, e_min;
+  screen_bound(d, e_rel, e_abs, e_min);
 
-  // Centroids: one exponent, split FP16 copy.
-  uint32_t* cinfo = e->scratch_get<uint32_t>("tc_cinfo", 4);
+  // Centroids: one exponent, split FP16 copy (kept from the last call when
+  // the caller says the centroids are unchanged).
+  unsigned long long* cinfo = e->scratch_get<unsigned long long>("tc_cinfo", 4, true);
   __half* ch = e->scratch_get<__half>("tc_ch", k * dp);
   __half* cl = e->scratch_get<__half>("tc_cl", k * dp);
   const unsigned wpb = 8;
-  if (!a.centroids_ready) {
-    EB_CUDA(cudaMemsetAsync(cinfo, 0, 16, e->stream));
-    k_cent_max<<<(unsigned)((k + 1) / 2), 64, 0, e->stream>>>(a.c, (long)k, (int)d, cinfo);
-    EB_LAUNCH("screen centroid max");
-    k_cent_conv<<<(unsigned)((k + 1) / 2), 64, 0, e->stream>>>(a.c, (long)k, (int)d, (int)dp,
-                                                              cinfo, ch, cl);
-    EB_LAUNCH("screen centroid convert");
-  }
+  const uint32_t cgen =
+      a.centroids_ready ? e->cinfo_gen : convert_centroids(e, a.c, k, d, dp, cinfo, ch, cl);
   const CUtensorMap mapBh = make_map(ch, k, dp, BN);
   const CUtensorMap mapBl = make_map(cl, k, dp, BN);
 
@@ -1776,12 +1835,13 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   const ExactScratch S{cand, cand_cnt, cand_thr, pairs, pair_count, rkey, bad, xn_pos, list,
                        list_count, lkey, lxn};
 
-  ScreenParams P;
+  ScreenParams P{};
   P.k = (int)k;
   P.kblocks = (int)(dp / BKH);
   P.ntiles = (int)((k + BN - 1) / BN);
   P.cn = a.cnorm;
   P.cinfo = cinfo;
+  P.cgen = cgen;
   P.e_rel = e_rel;
   P.e_abs = e_abs;
   P.e_min = e_min;
@@ -1789,6 +1849,8 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   P.cand_cnt = cand_cnt;
   P.cand_thr = cand_thr;
   P.status = e->d_status;
+  P.zero0 = pair_count;
+  P.zero1 = list_count;
 
   // A bound data set keeps its split copy across calls (training steps,
   // repeated assigns): converted once, then read in place or gathered by id.
@@ -1811,8 +1873,7 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
         drop_f16(xbuf);  // no room for the copy: convert per pass instead
         cudaGetLastError();
       } else if (a.n) {
-        k_prep_rows<<<(unsigned)((a.n + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(
-            a.x, (long)a.n, (int)d, (int)dp, nullptr, 0, (long)a.n, f->xh, f->xl, f->xexp,
+        launch_pdl(e, k_prep_rows, (unsigned)((a.n + wpb - 1) / wpb), wpb * 32, 0, a.x, (long)a.n, (int)d, (int)dp, nullptr, 0, (long)a.n, f->xh, f->xl, f->xexp,
             f->xnrm, e->d_status);
         EB_LAUNCH("screen copy of bound rows");
       }
@@ -1830,15 +1891,13 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
       P.xexp = cache->xexp + c0;
       P.xnrm = cache->xnrm + c0;
     } else if (cache) {
-      k_gather_rows<<<(unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(
-          cache->xh, cache->xl, cache->xexp, cache->xnrm, (long)a.n, (int)dp, a.ids, (long)c0,
+      launch_pdl(e, k_gather_rows, (unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, cache->xh, cache->xl, cache->xexp, cache->xnrm, (long)a.n, (int)dp, a.ids, (long)c0,
           (long)m, xh, xl, xexp, xnrm, e->d_status);
       EB_LAUNCH("screen row gather");
       P.xexp = xexp;
       P.xnrm = xnrm;
     } else {
-      k_prep_rows<<<(unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(
-          a.x, (long)a.n, (int)d, (int)dp, a.ids, (long)c0, (long)m, xh, xl, xexp, xnrm,
+      launch_pdl(e, k_prep_rows, (unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, a.x, (long)a.n, (int)d, (int)dp, a.ids, (long)c0, (long)m, xh, xl, xexp, xnrm,
           e->d_status);
       EB_LAUNCH("screen row prep");
       P.xexp = xexp;
@@ -1877,21 +1936,6 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   e->stats.screened_rows += m_all;
 }
 
-namespace {
-
-// The bound coefficients of the header comment for this d, with 1% slack.
-void screen_bound(size_t d, float& e_rel, float& e_abs, float& e_min) {
-  const double dd = (double)d;
-  const double u24 = std::ldexp(1.0, -24);
-  const double gamma_d = dd * u24 / (1.0 - dd * u24);
-  e_rel = (float)((3.0 * std::ldexp(1.0, -22) + dd * std::ldexp(1.0, -21) * (1.0 + std::ldexp(1.0, -9)) +
-                   dd * std::ldexp(1.0, -30) + std::ldexp(1.0, -23) + gamma_d) *
-                  1.01);
-  e_abs = (float)(std::ldexp(1.0, -23) * std::sqrt(dd) * 1.01);
-  e_min = (float)(dd * std::ldexp(1.0, -48));
-}
-
-}  // namespace
 
 // Top-kk by inner product on the tensor cores: the screen in top-k mode keeps
 // every column within 2e of each row's screened kk-th best (a column of the
@@ -1909,15 +1953,10 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
   screen_bound(d, e_rel, e_abs, e_min);
 
   // The data rows play the centroids: one exponent, split FP16 copy.
-  uint32_t* cinfo = e->scratch_get<uint32_t>("tc_cinfo", 4);
+  unsigned long long* cinfo = e->scratch_get<unsigned long long>("tc_cinfo", 4, true);
   __half* ch = e->scratch_get<__half>("tc_ch", n * dp);
   __half* cl = e->scratch_get<__half>("tc_cl", n * dp);
-  EB_CUDA(cudaMemsetAsync(cinfo, 0, 16, e->stream));
-  k_cent_max<<<(unsigned)((n + 1) / 2), 64, 0, e->stream>>>(data, (long)n, (int)d, cinfo);
-  EB_LAUNCH("topk data max");
-  k_cent_conv<<<(unsigned)((n + 1) / 2), 64, 0, e->stream>>>(data, (long)n, (int)d, (int)dp, cinfo,
-                                                            ch, cl);
-  EB_LAUNCH("topk data convert");
+  const uint32_t cgen = convert_centroids(e, data, n, d, dp, cinfo, ch, cl);
   const CUtensorMap mapBh = make_map(ch, n, dp, BN);
   const CUtensorMap mapBl = make_map(cl, n, dp, BN);
 
@@ -1947,6 +1986,7 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
   P.ntiles = (int)((n + BN - 1) / BN);
   P.cn = nullptr;
   P.cinfo = cinfo;
+  P.cgen = cgen;
   P.e_rel = e_rel;
   P.e_abs = e_abs;
   P.e_min = e_min;
@@ -1954,6 +1994,8 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
   P.cand_cnt = cand_cnt;
   P.cand_thr = cand_thr;
   P.status = e->d_status;
+  P.zero0 = pair_count;
+  P.zero1 = list_count;
   P.kk = (int)kk;
   P.exclude_self = exclude_self ? 1 : 0;
   P.col_gid0 = (long)id0;
@@ -1962,8 +2004,7 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
 
   for (size_t c0 = 0; c0 < m; c0 += chunk) {
     const size_t mc = std::min(chunk, m - c0);
-    k_prep_rows<<<(unsigned)((mc + wpb - 1) / wpb), wpb * 32, 0, e->stream>>>(
-        q, (long)m, (int)d, (int)dp, nullptr, (long)c0, (long)mc, xh, xl, xexp, xnrm,
+    launch_pdl(e, k_prep_rows, (unsigned)((mc + wpb - 1) / wpb), wpb * 32, 0, q, (long)m, (int)d, (int)dp, nullptr, (long)c0, (long)mc, xh, xl, xexp, xnrm,
         e->d_status);
     EB_LAUNCH("topk query prep");
     const CUtensorMap mapAh = make_map(xh, mc, dp, BM);
@@ -1975,10 +2016,8 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
     const unsigned grid = (unsigned)std::min<size_t>((mc + BM - 1) / BM, (size_t)e->num_sms);
     launch_screen<true, true>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
     EB_LAUNCH("topk screen");
-    EB_CUDA(cudaMemsetAsync(pair_count, 0, 4, e->stream));
-    EB_CUDA(cudaMemsetAsync(list_count, 0, 4, e->stream));
     const unsigned rgrid = (unsigned)((mc + 255) / 256);
-    k_collect_topk<<<rgrid, 256, 0, e->stream>>>((long)c0, (long)mc, (uint32_t)n, (int)kk, cand,
+    launch_pdl(e, k_collect_topk, rgrid, 256, 0, (long)c0, (long)mc, (uint32_t)n, (int)kk, cand,
                                                  cand_cnt, kvals, roff, pairs, pair_count, pstart,
                                                  pcnt, list, list_count, counters, e->d_status);
     EB_LAUNCH("topk collect");
@@ -1987,12 +2026,11 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
       launch_pairs<true>(e, (long)mc, q, (int)d, nullptr, (long)c0, data, nullptr, nullptr, pairs,
                          pair_count, (uint32_t)n, nullptr, nullptr, nullptr, pval);
     } else {
-      k_pairs_plain<true><<<pgrid * 4, 128, 0, e->stream>>>(
-          q, (int)d, nullptr, (long)c0, data, nullptr, nullptr, pairs, pair_count, (long)mc,
+      launch_pdl(e, k_pairs_plain<true>, pgrid * 4, 128, 0, q, (int)d, nullptr, (long)c0, data, nullptr, nullptr, pairs, pair_count, (long)mc,
           (uint32_t)n, nullptr, nullptr, nullptr, e->d_status, pval);
     }
     EB_LAUNCH("topk exact chains");
-    k_topk_finish<<<rgrid, 256, 0, e->stream>>>((long)c0, (long)mc, (int)kk, (uint32_t)id0,
+    launch_pdl(e, k_topk_finish, rgrid, 256, 0, (long)c0, (long)mc, (int)kk, (uint32_t)id0,
                                                 pstart, pcnt, pairs, pval, ids, sims);
     EB_LAUNCH("topk finish");
     // Rows of the full scan: their count comes to the host (this call ends
@@ -2006,11 +2044,10 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
       float* tsims = e->scratch_get<float>("tk_tsims", L * kk);
       const unsigned gx = (unsigned)std::min<size_t>(L, 65535);
       const unsigned gy = (unsigned)((L + gx - 1) / gx);
-      k_gather_queries<<<dim3(gx, gy), 128, 0, e->stream>>>(q, (int)d, list, (long)L, gq);
+      launch_pdl(e, k_gather_queries, dim3(gx, gy), 128, 0, q, (int)d, list, (long)L, gq);
       EB_LAUNCH("topk gather");
       topk_exact_device(e, gq, L, list, data, n, d, kk, exclude_self, tids, tsims, id0);
-      k_scatter_topk<<<(unsigned)((L * kk + 255) / 256), 256, 0, e->stream>>>(
-          list, (long)L, (int)kk, tids, tsims, ids, sims);
+      launch_pdl(e, k_scatter_topk, (unsigned)((L * kk + 255) / 256), 256, 0, list, (long)L, (int)kk, tids, tsims, ids, sims);
       EB_LAUNCH("topk scatter");
     }
   }

@@ -3,8 +3,10 @@
 // engine's layer-1 ops. Per batch, queued without a host wait: readout
 // (normalize or row norms), top-1 in chunks, scatter-add (and the closing
 // sums in the last epoch), EMA. The host waits only every 5th step for the
-// masses (revival plan, MT19937 on the host), at epoch ends for the labels and
-// scores (statistics), and at the end.
+// masses (revival plan, MT19937 on the host) and at the end. Each epoch's
+// labels and scores are copied into pinned memory behind the epoch's work,
+// and its statistics are computed on a helper thread while the next epoch
+// runs; the closing means are computed on the device.
 #include <cuda_runtime.h>
 
 #include <chrono>
@@ -46,9 +48,8 @@ struct EpochStat {
 };
 
 // Epoch statistics (train.rs:224-279): f64 objective per chunk, imbalance.
-EpochStat epoch_stats(const std::vector<uint32_t>& lab, const std::vector<float>& sc, size_t rows,
-                      size_t bsz, size_t chunk, size_t k, bool spherical,
-                      std::vector<uint64_t>& hist) {
+EpochStat epoch_stats(const uint32_t* lab, const float* sc, size_t rows, size_t bsz, size_t chunk,
+                      size_t k, bool spherical) {
   double obj_epoch = 0.0;
   for (size_t b = 0; b < rows; b += bsz) {
     size_t e = std::min(b + bsz, rows);
@@ -66,7 +67,7 @@ EpochStat epoch_stats(const std::vector<uint32_t>& lab, const std::vector<float>
     }
     obj_epoch += obj_batch;
   }
-  hist.assign(k, 0);
+  std::vector<uint64_t> hist(k, 0);
   for (size_t i = 0; i < rows; i++) {
     ensure(lab[i] < k, "device returned a label >= k");
     hist[lab[i]]++;
@@ -105,16 +106,19 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   std::future<std::vector<uint32_t>> next_order = std::async(std::launch::async, perm_of, 0);
 
   // Start state (model.rs:306-349, 772-797).
-  std::vector<float> pos(k * d), usage(k, 1.0f / 65536.0f);
+  // The start positions are assembled in pinned memory, so that their upload
+  // runs as a DMA behind the host's remaining set-up.
+  float* pos = e->pinned_get<float>("tr_pos", k * d);
+  std::vector<float> usage(k, 1.0f / 65536.0f);
   if (job->state_positions) {
-    std::memcpy(pos.data(), job->state_positions, k * d * 4);
+    std::memcpy(pos, job->state_positions, k * d * 4);
     std::memcpy(usage.data(), job->state_usage, k * 4);
     for (float u : usage) ensure(std::isfinite(u) && u >= 0.0f, "usage must be finite and >= 0");
   } else {
     if (job->init) {
-      std::memcpy(pos.data(), job->init, k * d * 4);
+      std::memcpy(pos, job->init, k * d * 4);
     } else if (n == k) {
-      std::memcpy(pos.data(), job->x, k * d * 4);
+      std::memcpy(pos, job->x, k * d * 4);
     } else {
       std::vector<uint32_t> perm = host::Mt19937(job->seed).permutation(n);
       for (size_t j = 0; j < k; j++) std::memcpy(&pos[j * d], job->x + (size_t)perm[j] * d, d * 4);
@@ -122,7 +126,7 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
     if (spherical)
       for (size_t j = 0; j < k; j++) host::normalize_row(&pos[j * d], d);
   }
-  for (float v : pos) ensure(std::isfinite(v), "initial centroids must be finite");
+  for (size_t q = 0; q < k * d; q++) ensure(std::isfinite(pos[q]), "initial centroids must be finite");
 
   const size_t bsz = r.batch_size;
   const size_t chunk = job->chunk > 0 ? (size_t)job->chunk : 65536;
@@ -152,7 +156,7 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   DevBuf pairs(e, EB_U32, 2 * k);
   // Group exchange staging: world x (labels, scores) slices of a batch.
   DevBuf stage(e, EB_U32, e->world > 1 ? 2 * ((bsz + e->world - 1) / e->world) * e->world : 1);
-  EB_CUDA(cudaMemcpyAsync(dpos.f(), pos.data(), k * d * 4, cudaMemcpyHostToDevice, e->stream));
+  EB_CUDA(cudaMemcpyAsync(dpos.f(), pos, k * d * 4, cudaMemcpyHostToDevice, e->stream));
   EB_CUDA(cudaMemcpyAsync(mass.f(), usage.data(), k * 4, cudaMemcpyHostToDevice, e->stream));
   if (data->d == d && !data->xnorm && !spherical) {
     EB_CUDA(cudaMallocAsync(&data->xnorm, std::max<size_t>(n, 1) * 4, e->stream));
@@ -161,11 +165,25 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
 
   host::Mt19937 split_rng(job->seed);
   size_t n_splits = 0, step = 0;
-  std::vector<double> pass_counts(k, 0.0);
-  std::vector<uint32_t> lab(n);
-  std::vector<float> sc(n);
-  std::vector<uint64_t> hist;
-  std::vector<float> mass_h(k);
+  // Pinned read-backs: two (labels, scores) sets, so that an epoch's copy
+  // never overwrites the set whose statistics are still being computed, and
+  // the masses and revival plan.
+  uint32_t* h_lab[2] = {e->pinned_get<uint32_t>("tr_lab0", n), e->pinned_get<uint32_t>("tr_lab1", n)};
+  float* h_sc[2] = {e->pinned_get<float>("tr_sc0", n), e->pinned_get<float>("tr_sc1", n)};
+  float* mass_h = e->pinned_get<float>("tr_mass", k);
+  float* h_cent = e->pinned_get<float>("tr_cent", k * d);
+  uint32_t* plan_h = e->pinned_get<uint32_t>("tr_plan", 2 * k);
+  std::vector<float> mass_v(k);
+  struct Events {
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    ~Events() {
+      for (cudaEvent_t v : ev)
+        if (v) cudaEventDestroy(v);
+    }
+  } done;
+  for (auto& v : done.ev) EB_CUDA(cudaEventCreateWithFlags(&v, cudaEventDisableTiming));
+  // Declared after the events, so destroyed (joined) before them.
+  std::vector<std::future<void>> stats(n_epochs);
   if (out->labels)
     for (size_t i = 0; i < n; i++) out->labels[i] = -1;
 
@@ -215,10 +233,12 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
       ema_update(e, dpos.f(), mass.f(), sums.f(), counts.u(), k, d, (float)alpha,
                  (float)(1.0 - alpha), alpha == 1.0);
       if ((step + 1) % 5 == 0) {
-        read_into(e, mass_h.data(), mass.f(), k * 4);
-        std::vector<uint32_t> plan = host::plan_revival(mass_h, tau, split_rng);
+        read_into(e, mass_h, mass.f(), k * 4);
+        std::memcpy(mass_v.data(), mass_h, k * 4);
+        std::vector<uint32_t> plan = host::plan_revival(mass_v, tau, split_rng);
         if (!plan.empty()) {
-          EB_CUDA(cudaMemcpyAsync(pairs.u(), plan.data(), plan.size() * 4, cudaMemcpyHostToDevice,
+          std::memcpy(plan_h, plan.data(), plan.size() * 4);
+          EB_CUDA(cudaMemcpyAsync(pairs.u(), plan_h, plan.size() * 4, cudaMemcpyHostToDevice,
                                   e->stream));
           split(e, dpos.f(), mass.f(), pairs.u(), plan.size() / 2, d);
           n_splits += plan.size() / 2;
@@ -226,31 +246,60 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
       }
       step++;
     }
-    // Epoch end: labels and scores come down for the statistics.
-    EB_CUDA(cudaMemcpyAsync(lab.data(), labels_ep.u(), rows * 4, cudaMemcpyDeviceToHost, e->stream));
-    read_into(e, sc.data(), scores_ep.f(), rows * 4);
-    EpochStat st = epoch_stats(lab, sc, rows, bsz, chunk, k, spherical, hist);
-    out->obj[epoch] = st.obj;
-    out->imbalance[epoch] = st.imbalance;
+    // Epoch end: labels and scores come down behind the epoch's work; a
+    // helper thread computes the statistics once they have landed.
+    const int par = (int)(epoch & 1);
+    if (epoch >= 2) stats[epoch - 2].get();  // the set it read is reused now
+    EB_CUDA(cudaMemcpyAsync(h_lab[par], labels_ep.u(), rows * 4, cudaMemcpyDeviceToHost, e->stream));
+    EB_CUDA(cudaMemcpyAsync(h_sc[par], scores_ep.f(), rows * 4, cudaMemcpyDeviceToHost, e->stream));
+    EB_CUDA(cudaEventRecord(done.ev[par], e->stream));
     out->nsplit[epoch] = (int64_t)(n_splits - splits_before);
-    out->epoch_time[epoch] =
-        std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-    if (job->verbose)
-      fprintf(stderr, "  Epoch %zu / %zu (%zu rows), iteration %zu (%.2f s): objective=%.17g\n",
-              epoch + 1, n_epochs, rows, step, out->epoch_time[epoch], st.obj);
+    const int dev = e->device;
+    const cudaEvent_t ev = done.ev[par];
+    const uint32_t* hl = h_lab[par];
+    const float* hs = h_sc[par];
+    const bool verbose = job->verbose != 0;
+    stats[epoch] = std::async(std::launch::async, [=, ord = std::move(ord)]() {
+      EB_CUDA(cudaSetDevice(dev));
+      EB_CUDA(cudaEventSynchronize(ev));
+      const EpochStat st = epoch_stats(hl, hs, rows, bsz, chunk, k, spherical);
+      out->obj[epoch] = st.obj;
+      out->imbalance[epoch] = st.imbalance;
+      out->epoch_time[epoch] =
+          std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+      if (verbose)
+        fprintf(stderr, "  Epoch %zu / %zu (%zu rows), iteration %zu (%.2f s): objective=%.17g\n",
+                epoch + 1, n_epochs, rows, step, out->epoch_time[epoch], st.obj);
+      if (last && out->labels)
+        for (size_t i = 0; i < rows; i++) out->labels[ord[i]] = (int32_t)hl[i];
+    });
     if (last) {
-      for (size_t j = 0; j < k; j++) pass_counts[j] = (double)hist[j];
-      if (out->labels)
-        for (size_t i = 0; i < rows; i++) out->labels[ord[i]] = (int32_t)lab[i];
+      // Closing means (core/mod.rs:404-429) on the device: the closing pass's
+      // label counts, sums / count, renormalised when spherical.
+      label_counts(e, labels_ep.u(), rows, k, counts.u());
+      closing_means(e, dpos.f(), pass.f(), counts.u(), k, d, sums.f());
+      const float* closing = sums.f();
+      if (spherical) {
+        normalize_rows(e, sums.f(), k, d, pass.f());
+        closing = pass.f();
+      }
+      EB_CUDA(cudaMemcpyAsync(h_cent, closing, k * d * 4, cudaMemcpyDeviceToHost, e->stream));
     }
   }
-  std::vector<float> closing(k * d);
-  EB_CUDA(cudaMemcpyAsync(pos.data(), dpos.f(), k * d * 4, cudaMemcpyDeviceToHost, e->stream));
-  EB_CUDA(cudaMemcpyAsync(usage.data(), mass.f(), k * 4, cudaMemcpyDeviceToHost, e->stream));
-  read_into(e, closing.data(), pass.f(), k * d * 4);
-  host::closing_means(pos.data(), closing.data(), pass_counts, k, d, spherical, out->centroids);
-  if (out->positions) std::memcpy(out->positions, pos.data(), k * d * 4);
-  if (out->usage) std::memcpy(out->usage, usage.data(), k * 4);
+  // Results through pinned staging (a DMA at full speed), then into the
+  // caller's buffers on two threads.
+  EB_CUDA(cudaMemcpyAsync(pos, dpos.f(), k * d * 4, cudaMemcpyDeviceToHost, e->stream));
+  EB_CUDA(cudaMemcpyAsync(mass_h, mass.f(), k * 4, cudaMemcpyDeviceToHost, e->stream));
+  sync(e);
+  {
+    auto cp = std::async(std::launch::async,
+                         [&] { std::memcpy(out->centroids, h_cent, k * d * 4); });
+    if (out->positions) std::memcpy(out->positions, pos, k * d * 4);
+    if (out->usage) std::memcpy(out->usage, mass_h, k * 4);
+    cp.get();
+  }
+  for (auto& f : stats)
+    if (f.valid()) f.get();
   out->n_epochs = (int32_t)n_epochs;
   out->n_splits = (int64_t)n_splits;
   out->batch_size = (int64_t)bsz;
