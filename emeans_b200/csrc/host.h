@@ -55,11 +55,29 @@ class Mt19937 {
     }
   }
   // permutation(n) (rng.rs:95-102).
+  // The same draws as swapping p[i] with p[interval(i)] for i = n-1 .. 1,
+  // written without the rejection branch: each output either lands (swap,
+  // next i) or is rejected (a swap of p[i] with itself, same i).
   std::vector<uint32_t> permutation(size_t n) {
     std::vector<uint32_t> p(n);
-    for (size_t i = 0; i < n; i++) p[i] = (uint32_t)i;
-    for (size_t i = n; i-- > 1;) std::swap(p[i], p[(size_t)interval(i)]);
+    permutation_into(p.data(), n);
     return p;
+  }
+  void permutation_into(uint32_t* a, size_t n) {
+    for (size_t i = 0; i < n; i++) a[i] = (uint32_t)i;
+    if (n - 1 > 0xffffffffull) {
+      for (size_t i = n; i-- > 1;) std::swap(a[i], a[(size_t)interval(i)]);
+      return;
+    }
+    for (uint32_t i = n ? (uint32_t)(n - 1) : 0u; i > 0;) {
+      const uint32_t v = u32() & (0xffffffffu >> __builtin_clz(i));
+      const uint32_t take = v <= i;
+      const uint32_t j = take ? v : i;
+      const uint32_t t = a[i];
+      a[i] = a[j];
+      a[j] = t;
+      i -= take;
+    }
   }
 
  private:
@@ -172,9 +190,26 @@ inline float numpy_sum(const float* a, size_t n) {
   return numpy_sum(a, h) + numpy_sum(a + h, n - h);
 }
 
-// plan_revival (core/mod.rs:339-370): (donor, dead) pairs, flattened.
+// The random part of a revival plan: g[j] = log(-log(u_j)) for k uniforms
+// u_j (floored at the smallest normal double), and the generator after
+// drawing them. They depend only on the generator's state, so they can be
+// drawn ahead, while the device runs the steps before the revival.
+struct RevivalDraws {
+  std::vector<double> g;
+  Mt19937 after;
+};
+inline RevivalDraws revival_draws(Mt19937 rng, size_t k) {
+  std::vector<double> g(k);
+  for (auto& v : g) v = std::log(-std::log(std::max(rng.sample(), 2.2250738585072014e-308)));
+  return {std::move(g), rng};
+}
+
+// plan_revival (core/mod.rs:339-370): (donor, dead) pairs, flattened. The
+// uniforms are drawn only when there is something to split; `pre`, if given,
+// holds them drawn ahead from rng's current state (rng then jumps to the state
+// after them).
 inline std::vector<uint32_t> plan_revival(const std::vector<float>& usage, double tau,
-                                          Mt19937& rng) {
+                                          Mt19937& rng, const RevivalDraws* pre = nullptr) {
   const size_t k = usage.size();
   std::vector<uint32_t> plan;
   float threshold = (numpy_sum(usage.data(), k) * (float)tau) / (float)k;
@@ -186,15 +221,20 @@ inline std::vector<uint32_t> plan_revival(const std::vector<float>& usage, doubl
   }
   size_t nsplit = std::min(n_dead, n_donor);
   if (nsplit == 0) return plan;
-  std::vector<double> uni(k);
-  for (auto& u : uni) u = std::max(rng.sample(), 2.2250738585072014e-308);
+  RevivalDraws own{{}, rng};
+  if (!pre || pre->g.size() != k) {
+    own = revival_draws(rng, k);
+    pre = &own;
+  }
+  rng = pre->after;
   std::vector<std::pair<double, uint32_t>> keys;
   for (size_t j = 0; j < k; j++) {
     float u = usage[j];
-    if (!(u < threshold) && u > 0.0f)
-      keys.emplace_back((double)std::log(u) - std::log(-std::log(uni[j])), (uint32_t)j);
+    if (!(u < threshold) && u > 0.0f) keys.emplace_back((double)std::log(u) - pre->g[j], (uint32_t)j);
   }
-  std::stable_sort(keys.begin(), keys.end(), [](const auto& a, const auto& b) {
+  // Larger key first, then larger index: a strict order (indices differ), so
+  // the first nsplit of a partial sort equal those of a stable sort.
+  std::partial_sort(keys.begin(), keys.begin() + nsplit, keys.end(), [](const auto& a, const auto& b) {
     return a.first != b.first ? a.first > b.first : a.second > b.second;
   });
   size_t t = 0;

@@ -99,11 +99,30 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   for (size_t rows : r.epoch_rows) ensure(rows > 0, "nepochs gives an empty epoch");
   const auto t0 = std::chrono::steady_clock::now();
 
-  // The epoch-0 permutation is drawn while the init runs (model.rs:781-784).
-  auto perm_of = [n, seed = job->seed](size_t epoch) {
-    return host::Mt19937(host::epoch_seed(seed, epoch)).permutation(n);
+  // Events: [0, 1] an epoch's labels and scores landed in pinned set 0 / 1;
+  // [2, 3] an epoch's order left pinned buffer 0 / 1 for the device.
+  struct Events {
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    ~Events() {
+      for (cudaEvent_t v : ev)
+        if (v) cudaEventDestroy(v);
+    }
+  } done;
+  for (auto& v : done.ev) EB_CUDA(cudaEventCreateWithFlags(&v, cudaEventDisableTiming));
+  // Each epoch's permutation is drawn on a helper thread, straight into one of
+  // two pinned buffers (so that its upload is a plain DMA), while the previous
+  // epoch runs; the epoch-0 one while the init runs (model.rs:781-784).
+  uint32_t* h_ord[2] = {e->pinned_get<uint32_t>("tr_ord0", n), e->pinned_get<uint32_t>("tr_ord1", n)};
+  const int dev = e->device;
+  auto perm_of = [n, seed = job->seed, dev, &h_ord, &done](size_t epoch) {
+    const int par = (int)(epoch & 1);
+    if (epoch >= 2) {  // the buffer's last upload (epoch - 2) must have left it
+      EB_CUDA(cudaSetDevice(dev));
+      EB_CUDA(cudaEventSynchronize(done.ev[2 + par]));
+    }
+    host::Mt19937(host::epoch_seed(seed, epoch)).permutation_into(h_ord[par], n);
   };
-  std::future<std::vector<uint32_t>> next_order = std::async(std::launch::async, perm_of, 0);
+  std::future<void> next_order = std::async(std::launch::async, perm_of, 0);
 
   // Start state (model.rs:306-349, 772-797).
   // The start positions are assembled in pinned memory, so that their upload
@@ -126,7 +145,13 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
     if (spherical)
       for (size_t j = 0; j < k; j++) host::normalize_row(&pos[j * d], d);
   }
-  for (size_t q = 0; q < k * d; q++) ensure(std::isfinite(pos[q]), "initial centroids must be finite");
+  {
+    // Exponent field all ones = inf or NaN; one pass without branches.
+    uint32_t nonfinite = 0;
+    const uint32_t* pb = reinterpret_cast<const uint32_t*>(pos);
+    for (size_t q = 0; q < k * d; q++) nonfinite |= (uint32_t)((pb[q] & 0x7f800000u) == 0x7f800000u);
+    ensure(nonfinite == 0, "initial centroids must be finite");
+  }
 
   const size_t bsz = r.batch_size;
   const size_t chunk = job->chunk > 0 ? (size_t)job->chunk : 65536;
@@ -164,6 +189,11 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   }
 
   host::Mt19937 split_rng(job->seed);
+  // The next revival's uniforms, drawn ahead on a helper thread from
+  // split_rng's current state (it changes only when a revival splits).
+  std::future<host::RevivalDraws> draws_next;
+  std::unique_ptr<host::RevivalDraws> draws;
+  if (tau > 0.0) draws_next = std::async(std::launch::async, host::revival_draws, split_rng, k);
   size_t n_splits = 0, step = 0;
   // Pinned read-backs: two (labels, scores) sets, so that an epoch's copy
   // never overwrites the set whose statistics are still being computed, and
@@ -174,14 +204,6 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   float* h_cent = e->pinned_get<float>("tr_cent", k * d);
   uint32_t* plan_h = e->pinned_get<uint32_t>("tr_plan", 2 * k);
   std::vector<float> mass_v(k);
-  struct Events {
-    cudaEvent_t ev[2] = {nullptr, nullptr};
-    ~Events() {
-      for (cudaEvent_t v : ev)
-        if (v) cudaEventDestroy(v);
-    }
-  } done;
-  for (auto& v : done.ev) EB_CUDA(cudaEventCreateWithFlags(&v, cudaEventDisableTiming));
   // Declared after the events, so destroyed (joined) before them.
   std::vector<std::future<void>> stats(n_epochs);
   if (out->labels)
@@ -189,10 +211,12 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
 
   for (size_t epoch = 0; epoch < n_epochs; epoch++) {
     const size_t rows = r.epoch_rows[epoch];
-    std::vector<uint32_t> ord = next_order.get();
+    next_order.get();
+    const uint32_t* ord = h_ord[epoch & 1];
     if (epoch + 1 < n_epochs) next_order = std::async(std::launch::async, perm_of, epoch + 1);
     const bool last = epoch + 1 == n_epochs;
-    EB_CUDA(cudaMemcpyAsync(order.u(), ord.data(), rows * 4, cudaMemcpyHostToDevice, e->stream));
+    EB_CUDA(cudaMemcpyAsync(order.u(), ord, rows * 4, cudaMemcpyHostToDevice, e->stream));
+    EB_CUDA(cudaEventRecord(done.ev[2 + (epoch & 1)], e->stream));
     const size_t splits_before = n_splits;
     for (size_t b = 0; b < rows; b += bsz) {
       const size_t end = std::min(b + bsz, rows);
@@ -235,8 +259,10 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
       if ((step + 1) % 5 == 0) {
         read_into(e, mass_h, mass.f(), k * 4);
         std::memcpy(mass_v.data(), mass_h, k * 4);
-        std::vector<uint32_t> plan = host::plan_revival(mass_v, tau, split_rng);
+        if (draws_next.valid()) draws.reset(new host::RevivalDraws(draws_next.get()));
+        std::vector<uint32_t> plan = host::plan_revival(mass_v, tau, split_rng, draws.get());
         if (!plan.empty()) {
+          draws_next = std::async(std::launch::async, host::revival_draws, split_rng, k);
           std::memcpy(plan_h, plan.data(), plan.size() * 4);
           EB_CUDA(cudaMemcpyAsync(pairs.u(), plan_h, plan.size() * 4, cudaMemcpyHostToDevice,
                                   e->stream));
@@ -254,12 +280,11 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
     EB_CUDA(cudaMemcpyAsync(h_sc[par], scores_ep.f(), rows * 4, cudaMemcpyDeviceToHost, e->stream));
     EB_CUDA(cudaEventRecord(done.ev[par], e->stream));
     out->nsplit[epoch] = (int64_t)(n_splits - splits_before);
-    const int dev = e->device;
     const cudaEvent_t ev = done.ev[par];
     const uint32_t* hl = h_lab[par];
     const float* hs = h_sc[par];
     const bool verbose = job->verbose != 0;
-    stats[epoch] = std::async(std::launch::async, [=, ord = std::move(ord)]() {
+    stats[epoch] = std::async(std::launch::async, [=]() {
       EB_CUDA(cudaSetDevice(dev));
       EB_CUDA(cudaEventSynchronize(ev));
       const EpochStat st = epoch_stats(hl, hs, rows, bsz, chunk, k, spherical);
