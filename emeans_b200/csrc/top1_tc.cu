@@ -1109,7 +1109,6 @@ __global__ void __launch_bounds__(EX_WARPS * 32) k_pairs(
     uint32_t* __restrict__ bad, uint32_t* __restrict__ status, float* __restrict__ pval) {
   pdl_wait();
   extern __shared__ __align__(16) float ex_smem[];
-  __shared__ const float* rows_s[EX_WARPS][2][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   constexpr int EX_WARP_FLOATS = EX_STAGES * 2 * 32 * EX_COLS;  // x and c slices of one warp
   float* xs = ex_smem + warp * EX_WARP_FLOATS;  // [stage][pair][32]
@@ -1135,21 +1134,32 @@ __global__ void __launch_bounds__(EX_WARPS * 32) k_pairs(
       }
       row = ids ? (long)ids[p0 + pr.x] : p0 + pr.x;
     }
-    // Slots past the pair count read row 0 / centroid 0 harmlessly and write nothing.
-    rows_s[warp][0][lane] = x + row * (long)d;
-    rows_s[warp][1][lane] = c + (long)pr.y * d;
-    __syncwarp();
+    // Slots past the pair count read row 0 / centroid 0 harmlessly and write
+    // nothing. This lane copies 16-byte chunk q = lane % 8 of pair slots
+    // r = 4 u + lane / 8 (u = 0 .. 7) of every x and c slice; the slots' row
+    // addresses come from their lanes by shuffle, once per tile, and stay in
+    // registers with the chunks' shared-memory offsets.
+    const unsigned long long xrow = (unsigned long long)(x + row * (long)d);
+    const unsigned long long crow = (unsigned long long)(c + (long)pr.y * d);
+    const int q = lane & 7;
+    const float* xsrc[8];
+    const float* csrc[8];
+    int soff[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int r = u * 4 + (lane >> 3);
+      xsrc[u] = reinterpret_cast<const float*>(__shfl_sync(0xFFFFFFFFu, xrow, r)) + q * 4;
+      csrc[u] = reinterpret_cast<const float*>(__shfl_sync(0xFFFFFFFFu, crow, r)) + q * 4;
+      soff[u] = r * EX_COLS + ((q ^ (r & 7)) << 2);
+    }
     auto issue = [&](int sl) {
       if (sl < nsl) {
-        const int st = sl % EX_STAGES;
-        const int q = lane & 7;
+        const int sbase = (sl % EX_STAGES) * 32 * EX_COLS;
+        const int g = sl * EX_COLS;
 #pragma unroll
         for (int u = 0; u < 8; u++) {
-          const int r = u * 4 + (lane >> 3);
-          const int off = (st * 32 + r) * EX_COLS + ((q ^ (r & 7)) << 2);
-          const int g = sl * EX_COLS + q * 4;
-          cp_async16(xs + off, rows_s[warp][0][r] + g);
-          cp_async16(cs + off, rows_s[warp][1][r] + g);
+          cp_async16(xs + sbase + soff[u], xsrc[u] + g);
+          cp_async16(cs + sbase + soff[u], csrc[u] + g);
         }
       }
       cp_async_commit();
@@ -1164,10 +1174,17 @@ __global__ void __launch_bounds__(EX_WARPS * 32) k_pairs(
       const int base = (sl % EX_STAGES * 32 + lane) * EX_COLS;
       const float4* xr4 = reinterpret_cast<const float4*>(xs + base);
       const float4* cr4 = reinterpret_cast<const float4*>(cs + base);
+      // All sixteen loads first, so that their latencies overlap.
+      float4 av[8], bv[8];
 #pragma unroll
       for (int q = 0; q < 8; q++) {
         const int pq = q ^ (lane & 7);
-        const float4 a = xr4[pq], b = cr4[pq];
+        av[q] = xr4[pq];
+        bv[q] = cr4[pq];
+      }
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        const float4 a = av[q], b = bv[q];
         acc = __fmaf_rn(a.x, b.x, acc);
         acc = __fmaf_rn(a.y, b.y, acc);
         acc = __fmaf_rn(a.z, b.z, acc);
@@ -1196,7 +1213,7 @@ __global__ void __launch_bounds__(EX_WARPS * 32) k_pairs(
       }
       if (want_xn) xn_pos[pr.x] = xn;  // the same value from every pair of the row
     }
-    __syncwarp();  // row pointers are rewritten by the next tile
+    __syncwarp();  // the next tile refills the slices
   }
 }
 
@@ -1674,8 +1691,9 @@ void launch_pairs(eb_engine* e, long m, const float* x, int d, const uint32_t* i
                   const uint32_t* pair_count, uint32_t k, unsigned long long* rkey,
                   float* xn_pos, uint32_t* bad, float* pval) {
   const unsigned grid = (unsigned)e->num_sms;
-  set_pairs_smem<IP, 8, 3>(e->device);
-  launch_pdl(e, k_pairs<IP, 8, 3>, grid, 256, ex_smem<8, 3>(), x, d, ids, p0, c, cn, xnorm, pairs, pair_count, m, k, rkey, xn_pos, bad, e->d_status, pval);
+  constexpr int W = 8, S = 3;  // measured against 4-12 warps x 2-6 stages
+  set_pairs_smem<IP, W, S>(e->device);
+  launch_pdl(e, k_pairs<IP, W, S>, grid, W * 32, ex_smem<W, S>(), x, d, ids, p0, c, cn, xnorm, pairs, pair_count, m, k, rkey, xn_pos, bad, e->d_status, pval);
 }
 
 template <bool IP>
