@@ -726,8 +726,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // at once, so that the next tile's products run while this one is
         // scored.
         constexpr int LOG = 2;  // lo groups per TMEM wait
-        uint32_t acc[HALF / 16][16];
-        {
+        uint32_t acc[TOPK ? 1 : HALF / 16][16];
+        if constexpr (!TOPK) {
           uint32_t lo[LOG][16];
 #pragma unroll
           for (int g = 0; g < HALF / 16; g++)
@@ -752,13 +752,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 acc[LOG * p2 + h2][j] = __float_as_uint(__fadd_rn(
                     __uint_as_float(acc[LOG * p2 + h2][j]), __uint_as_float(lo[h2][j])));
           }
+          tc_fence_before();
+          mbar_arrive(tempty);
         }
-        tc_fence_before();
-        mbar_arrive(tempty);
-#pragma unroll
+        // Top-k mode scores each group straight from TMEM in a rolled loop
+        // (its group code is long: unrolled eight times it no longer fits the
+        // instruction cache) and frees TMEM after the tile.
+        constexpr int GUNROLL = TOPK ? 1 : HALF / 16;
+#pragma unroll GUNROLL
         for (int g = 0; g < HALF / 16; g++) {
           if (g >= ngr) break;
-          const uint32_t(&h)[16] = acc[g];
+          if constexpr (TOPK) {
+            uint32_t lo1[16];
+            tmem_ld16(lane_base + (uint32_t)(g * 16), acc[0]);
+            tmem_ld16(lane_base + (uint32_t)(BN + g * 16), lo1);
+            tmem_wait();
+            tmem_tie(acc[0]);
+            tmem_tie(lo1);
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+              acc[0][j] = __float_as_uint(
+                  __fadd_rn(__uint_as_float(acc[0][j]), __uint_as_float(lo1[j])));
+          }
+          const uint32_t(&h)[16] = acc[TOPK ? 0 : g];
           float s[16];
           const float4* c4 = reinterpret_cast<const float4*>(cns + g * 16);
 #pragma unroll
@@ -878,6 +894,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             __syncwarp();
           }
         }
+        if constexpr (TOPK) {
+          tc_fence_before();
+          mbar_arrive(tempty);
+        }
       }
       if (live) {
         // With k <= HALF the second half tile holds no centroid at all: its
@@ -947,7 +967,10 @@ __device__ __forceinline__ unsigned long long scan_start_key() {
 // halves' thresholds, the one of the row's overall best. Rows with none, with
 // more than SURV, or marked for the fallback go to the exact list, whose key
 // starts at the scan's starting point. The row's pair key starts at the
-// identity of its reduction. Launched with whole warps.
+// identity of its reduction. Launched with 256 threads a block. The first
+// eight entries of each half stay in registers between the counting and the
+// writing pass; the pair slots are reserved with one atomic per block (the
+// per-warp atomics on one counter serialised).
 template <bool IP>
 __global__ void __launch_bounds__(256) k_collect(
     long p0, long m, uint32_t k, const uint2* __restrict__ cand,
@@ -958,6 +981,8 @@ __global__ void __launch_bounds__(256) k_collect(
     uint32_t* __restrict__ bad, unsigned long long* __restrict__ counters,
     uint32_t* __restrict__ status) {
   pdl_wait();
+  __shared__ uint32_t wsum[8], wbase[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const bool live = i < m;
   uint32_t cnt[2];
@@ -972,30 +997,33 @@ __global__ void __launch_bounds__(256) k_collect(
       fb = true;
     }
   }
+  if (fb) cnt[0] = cnt[1] = 0;
   uint32_t ns = 0;
   float thr = 0.0f;
+  uint2 first[2][8];
   if (!fb) {
     const float t0 = cand_thr[i], t1 = cand_thr[m + i];
     thr = IP ? fmaxf(t0, t1) : fminf(t0, t1);
+  }
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const uint2* lst = cand + (long)h * CAP * m + i;
-      // Loads in batches of eight, so that they are in flight together.
-      for (uint32_t e0 = 0; e0 < cnt[h]; e0 += 8) {
-        uint2 en[8];
+  for (int h = 0; h < 2; h++) {
+    const uint2* lst = cand + (long)h * CAP * m + i;
+    // Loads in batches of eight, so that they are in flight together.
+    for (uint32_t e0 = 0; e0 < cnt[h]; e0 += 8) {
+      uint2 en[8];
 #pragma unroll
-        for (int u = 0; u < 8; u++)
-          en[u] = e0 + u < cnt[h] ? lst[(e0 + u) * m] : make_uint2(0u, __float_as_uint(NAN));
+      for (int u = 0; u < 8; u++)
+        en[u] = e0 + u < cnt[h] ? lst[(e0 + u) * m] : make_uint2(0u, __float_as_uint(NAN));
 #pragma unroll
-        for (int u = 0; u < 8; u++) {
-          const float sv = __uint_as_float(en[u].y);
-          if (en[u].x >= k) fb = true;
-          ns += IP ? (sv >= thr) : (sv <= thr);
-        }
+      for (int u = 0; u < 8; u++) {
+        const float sv = __uint_as_float(en[u].y);
+        if (en[u].x >= k) fb = true;
+        ns += IP ? (sv >= thr) : (sv <= thr);
+        if (e0 == 0) first[h][u] = en[u];
       }
     }
-    if (fb) atomicOr(status, ST_BAD_STATE);
   }
+  if (fb && live && cnt[0] + cnt[1] > 0) atomicOr(status, ST_BAD_STATE);
   fb = fb || ns == 0 || ns > SURV;
   const bool listed = live && fb;
   const uint32_t np = live && !fb ? ns : 0;
@@ -1008,7 +1036,30 @@ __global__ void __launch_bounds__(256) k_collect(
     list[lp] = (uint32_t)(p0 + i);
     lkey[lp] = scan_start_key<IP>();
   }
-  uint32_t w = warp_append(pair_count, np);
+  // Pair slots: this lane's offset in its warp, the warp's in the block, and
+  // the block's from one atomic.
+  uint32_t incl = np;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t run = 0;
+    const int nw = (int)(blockDim.x >> 5);
+    for (int w2 = 0; w2 < nw; w2++) {
+      const uint32_t v = wsum[w2];
+      wbase[w2] = run;
+      run += v;
+    }
+    const uint32_t base = run ? atomicAdd(pair_count, run) : 0u;
+    for (int w2 = 0; w2 < nw; w2++) wbase[w2] += base;
+    if (run) atomicAdd(&counters[2], (unsigned long long)run);
+  }
+  __syncthreads();
+  uint32_t w = wbase[warp] + incl - np;
   if (np) {
 #pragma unroll
     for (int h = 0; h < 2; h++) {
@@ -1017,7 +1068,8 @@ __global__ void __launch_bounds__(256) k_collect(
         uint2 en[8];
 #pragma unroll
         for (int u = 0; u < 8; u++)
-          en[u] = e0 + u < cnt[h] ? lst[(e0 + u) * m] : make_uint2(0u, __float_as_uint(NAN));
+          en[u] = e0 == 0 ? first[h][u]
+                          : (e0 + u < cnt[h] ? lst[(e0 + u) * m] : make_uint2(0u, __float_as_uint(NAN)));
 #pragma unroll
         for (int u = 0; u < 8; u++) {
           const float sv = __uint_as_float(en[u].y);
@@ -1027,11 +1079,7 @@ __global__ void __launch_bounds__(256) k_collect(
     }
   }
   const uint32_t nl = __reduce_add_sync(0xFFFFFFFFu, listed ? 1u : 0u);
-  const uint32_t nps = __reduce_add_sync(0xFFFFFFFFu, np);
-  if ((threadIdx.x & 31) == 0) {
-    if (nl) atomicAdd(&counters[1], (unsigned long long)nl);
-    if (nps) atomicAdd(&counters[2], (unsigned long long)nps);
-  }
+  if (lane == 0 && nl) atomicAdd(&counters[1], (unsigned long long)nl);
 }
 
 // Exact FMA chain of row x against centroid c over d columns, loads kept
