@@ -757,23 +757,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         // Top-k mode scores each group straight from TMEM in a rolled loop
         // (its group code is long: unrolled eight times it no longer fits the
-        // instruction cache) and frees TMEM after the tile.
-        constexpr int GUNROLL = TOPK ? 1 : HALF / 16;
-#pragma unroll GUNROLL
-        for (int g = 0; g < HALF / 16; g++) {
-          if (g >= ngr) break;
-          if constexpr (TOPK) {
-            uint32_t lo1[16];
-            tmem_ld16(lane_base + (uint32_t)(g * 16), acc[0]);
-            tmem_ld16(lane_base + (uint32_t)(BN + g * 16), lo1);
-            tmem_wait();
-            tmem_tie(acc[0]);
-            tmem_tie(lo1);
-#pragma unroll
-            for (int j = 0; j < 16; j++)
-              acc[0][j] = __float_as_uint(
-                  __fadd_rn(__uint_as_float(acc[0][j]), __uint_as_float(lo1[j])));
-          }
+        // instruction cache) and frees TMEM after the tile; top-1 mode scores
+        // the drained registers in an unrolled loop.
+        // The scoring of group g of this half tile (its 16 values in acc[g],
+        // or acc[0] in top-k mode).
+        auto score_group = [&](const int g) {
           const uint32_t(&h)[16] = acc[TOPK ? 0 : g];
           float s[16];
           const float4* c4 = reinterpret_cast<const float4*>(cns + g * 16);
@@ -893,10 +881,31 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             __syncwarp();
           }
-        }
+        };
         if constexpr (TOPK) {
+#pragma unroll 1
+          for (int g = 0; g < HALF / 16; g++) {
+            if (g >= ngr) break;
+            uint32_t lo1[16];
+            tmem_ld16(lane_base + (uint32_t)(g * 16), acc[0]);
+            tmem_ld16(lane_base + (uint32_t)(BN + g * 16), lo1);
+            tmem_wait();
+            tmem_tie(acc[0]);
+            tmem_tie(lo1);
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+              acc[0][j] = __float_as_uint(
+                  __fadd_rn(__uint_as_float(acc[0][j]), __uint_as_float(lo1[j])));
+            score_group(g);
+          }
           tc_fence_before();
           mbar_arrive(tempty);
+        } else {
+#pragma unroll
+          for (int g = 0; g < HALF / 16; g++) {
+            if (g >= ngr) break;
+            score_group(g);
+          }
         }
       }
       if (live) {

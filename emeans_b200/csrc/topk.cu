@@ -188,8 +188,10 @@ __global__ void k_topk_merge(const uint32_t* __restrict__ stage, long m, int kk,
 void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, size_t d,
           size_t kk, bool exclude_self, uint32_t* ids, float* sims, size_t id0,
           bool collective) {
+  // A self-join (queries and data the same host rows) copies the rows once.
+  const bool self_join = q == data && m == n;
   float* dq = e->scratch_get<float>("tk_q", m * d);
-  float* dd = e->scratch_get<float>("tk_data", n * d);
+  float* dd = self_join ? dq : e->scratch_get<float>("tk_data", n * d);
   const bool group = collective && e->world > 1;
   // In a group the local lists land in this rank's share of the exchange
   // buffer (ids, then sims), which is all-gathered and merged.
@@ -199,7 +201,8 @@ void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, s
                        : e->scratch_get<uint32_t>("tk_ids", m * kk);
   float* ds = group ? reinterpret_cast<float*>(di + m * kk) : e->scratch_get<float>("tk_sims", m * kk);
   EB_CUDA(cudaMemcpyAsync(dq, q, m * d * 4, cudaMemcpyHostToDevice, e->stream));
-  if (n) EB_CUDA(cudaMemcpyAsync(dd, data, n * d * 4, cudaMemcpyHostToDevice, e->stream));
+  if (n && !self_join)
+    EB_CUDA(cudaMemcpyAsync(dd, data, n * d * 4, cudaMemcpyHostToDevice, e->stream));
   if (!topk_screen(e, dq, m, dd, n, d, kk, exclude_self, di, ds, id0)) {
     unsigned grid = (unsigned)((m + BM - 1) / BM);
     k_topk_exact<<<grid, NT, 0, e->stream>>>(dq, (long)m, dd, (long)n, (int)d, (int)kk,
