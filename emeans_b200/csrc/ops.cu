@@ -325,27 +325,56 @@ __global__ void k_place(const uint32_t* __restrict__ labels, const uint32_t* __r
 }
 
 // sums[j][t] = rows of centroid j added in selection order from +0;
-// acc[j][t] += sums[j][t]. One thread per (centroid, column).
-__global__ void k_seg_sum(const float* __restrict__ x, int d, const uint32_t* __restrict__ order,
-                          const uint32_t* __restrict__ start, float* __restrict__ sums,
-                          float* __restrict__ acc) {
+// acc[j][t] += sums[j][t]. One thread per (centroid, column). The block stages
+// its centroid's row ids in shared memory, kSumStage at a time, and each
+// thread keeps the next 16 rows' loads in flight while it adds the current 16
+// in order (the adds of one column form one sequential chain).
+constexpr uint32_t kSumStage = 1024;
+__global__ void __launch_bounds__(128) k_seg_sum(const float* __restrict__ x, int d,
+                                                 const uint32_t* __restrict__ order,
+                                                 const uint32_t* __restrict__ start,
+                                                 float* __restrict__ sums,
+                                                 float* __restrict__ acc) {
   pdl_wait();
-  long j = blockIdx.x;
-  int t = blockIdx.y * blockDim.x + threadIdx.x;
-  if (t >= d) return;
-  uint32_t b = start[j], e = start[j + 1];
+  __shared__ uint32_t ord_s[kSumStage];
+  const long j = blockIdx.x;
+  const int t = blockIdx.y * blockDim.x + threadIdx.x;
+  const bool active = t < d;
+  const float* xt = x + (active ? t : 0);
+  const uint32_t b = start[j], e = start[j + 1];
   float s = 0.0f;
-  uint32_t i = b;
-  for (; i + 8 <= e; i += 8) {
-    float v[8];
+  for (uint32_t c0 = b; c0 < e; c0 += kSumStage) {
+    const uint32_t n = min(e - c0, kSumStage);
+    __syncthreads();  // the last chunk's ids are no longer read
+    for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) ord_s[u] = order[c0 + u];
+    __syncthreads();
+    if (!active) continue;
+    uint32_t i = 0;
+    float v[16];
+    if (n >= 16) {
 #pragma unroll
-    for (int q = 0; q < 8; q++) v[q] = __ldg(x + (long)order[i + q] * d + t);
+      for (int q = 0; q < 16; q++) v[q] = __ldg(xt + (long)ord_s[q] * d);
+    }
+    for (; i + 32 <= n; i += 16) {
+      float w[16];
 #pragma unroll
-    for (int q = 0; q < 8; q++) s = __fadd_rn(s, v[q]);
+      for (int q = 0; q < 16; q++) w[q] = __ldg(xt + (long)ord_s[i + 16 + q] * d);
+#pragma unroll
+      for (int q = 0; q < 16; q++) s = __fadd_rn(s, v[q]);
+#pragma unroll
+      for (int q = 0; q < 16; q++) v[q] = w[q];
+    }
+    if (i + 16 <= n) {
+#pragma unroll
+      for (int q = 0; q < 16; q++) s = __fadd_rn(s, v[q]);
+      i += 16;
+    }
+    for (; i < n; i++) s = __fadd_rn(s, __ldg(xt + (long)ord_s[i] * d));
   }
-  for (; i < e; i++) s = __fadd_rn(s, __ldg(x + (long)order[i] * d + t));
-  sums[j * d + t] = s;
-  if (acc) acc[j * d + t] = __fadd_rn(acc[j * d + t], s);
+  if (active) {
+    sums[j * d + t] = s;
+    if (acc) acc[j * d + t] = __fadd_rn(acc[j * d + t], s);
+  }
 }
 
 // Count of every label among labels[0 .. m) into cnt (zeroed by the caller);
