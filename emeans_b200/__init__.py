@@ -130,6 +130,7 @@ def load():
         "eb_group_unique_id": (I, [C.c_char_p]),
         "eb_engine_join": (I, [P, I, I, C.c_char_p]),
         "eb_engine_group": (I, [P, C.POINTER(I), C.POINTER(I)]),
+        "eb_set_group_shard": (I, [P, I]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -428,6 +429,11 @@ class Engine:
         box = [group_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         self.join(rank, world, box[0])
+
+    def set_group_shard(self, mode: int):
+        """eb_set_group_shard: 0 auto (split a training batch across the group
+        only when that shortens it), 1 always, 2 never; same on every rank."""
+        _check(load().eb_set_group_shard(self.h, int(mode)))
 
     def group(self):
         r, w = C.c_int(), C.c_int()

@@ -96,6 +96,9 @@ struct eb_engine {
   // GPU, or null for a single-GPU engine.
   void* comm = nullptr;
   int rank = 0, world = 1;
+  // Group training: 0 splits a batch's top-1 across the ranks only when that
+  // shortens it, 1 always, 2 never (eb_set_group_shard).
+  int group_shard = 0;
   // Optional CUDA-event timing of the top-1 screen kernel (eb_set_kernel_timing):
   // one (start, end) pair per launch since the last eb_screen_timing read,
   // with the rows of that launch.

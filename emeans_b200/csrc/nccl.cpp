@@ -118,6 +118,15 @@ extern "C" int eb_engine_join(eb_engine* e, int rank, int world, const unsigned 
   }
 }
 
+extern "C" int eb_set_group_shard(eb_engine* e, int mode) {
+  if (!e || mode < 0 || mode > 2) {
+    eb::set_last_error("engine required; mode must be 0, 1 or 2");
+    return EB_INVALID_ARGUMENT;
+  }
+  e->group_shard = mode;
+  return EB_OK;
+}
+
 extern "C" int eb_engine_group(eb_engine* e, int* rank, int* world) {
   if (!e || !rank || !world) {
     eb::set_last_error("engine, rank and world are required");

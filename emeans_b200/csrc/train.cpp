@@ -225,10 +225,20 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
       else
         row_norms(e, dpos.f(), k, d, readout.f());
       // In a group, rank q scores positions [b + q s, b + (q + 1) s) of the
-      // batch and the slices are all-gathered; alone, the whole batch.
+      // batch and the slices are all-gathered; alone, the whole batch. By
+      // default (group_shard 0) a batch is split only when that cuts the
+      // screen's waves of row tiles: a batch of one wave or less takes as
+      // long on one GPU as on several, so every rank scores all of it and
+      // nothing is exchanged (the same result either way).
       const size_t sh = (end - b + e->world - 1) / e->world;
-      const size_t lo = std::min(b + (size_t)e->rank * sh, end);
-      const size_t hi = e->world > 1 ? std::min(lo + sh, end) : end;
+      auto waves = [&](size_t rows) {
+        return ((rows + 127) / 128 + (size_t)e->num_sms - 1) / (size_t)e->num_sms;
+      };
+      const bool split_batch =
+          e->world > 1 &&
+          (e->group_shard == 1 || (e->group_shard == 0 && waves(sh) < waves(end - b)));
+      const size_t lo = split_batch ? std::min(b + (size_t)e->rank * sh, end) : b;
+      const size_t hi = split_batch ? std::min(lo + sh, end) : end;
       for (size_t c0 = lo; c0 < hi; c0 += chunk) {
         Top1Args a;
         a.x = static_cast<const float*>(data->ptr);
@@ -246,7 +256,7 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
         a.xnorm = data->xnorm;
         top1_dispatch(e, a, data);
       }
-      if (e->world > 1) {
+      if (split_batch) {
         shard_pack(e, labels_ep.u() + lo, scores_ep.f() + lo, hi - lo, sh, stage.u());
         group_allgather(e, stage.u(), 2 * sh);
         shard_unpack(e, stage.u(), end - b, sh, e->world, labels_ep.u() + b, scores_ep.f() + b);

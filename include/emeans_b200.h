@@ -244,6 +244,12 @@ int eb_train(eb_engine* e, const eb_train_job* job, eb_train_out* out);
 int eb_group_unique_id(unsigned char* id);
 int eb_engine_join(eb_engine* e, int rank, int world, const unsigned char* id);
 int eb_engine_group(eb_engine* e, int* rank, int* world);
+/* No counterpart in the reference. How eb_train on a joined engine divides a
+ * batch's top-1: 0 (default) splits it across the ranks only when that cuts
+ * the screen's waves of 128-row tiles (a batch of one wave or less is scored
+ * whole by every rank, with no exchange), 1 always splits it, 2 never does.
+ * Every mode gives the same model; all ranks must use the same mode. */
+int eb_set_group_shard(eb_engine* e, int mode);
 
 /* Device::topk over a database sharded across a group (knn_self over several
  * GPUs, crates/emeans-cluster/src/knn.rs:17-64): every rank passes the same m

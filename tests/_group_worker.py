@@ -32,15 +32,19 @@ def main():
     group.join_torch_group()
     assert group.group() == (rank, world)
     solo = eb.Engine(local)
-    for n, d, k, spherical, seed in cases:
-        x = mixture(n, d, 24, 0.4, spherical, seed)
-        cfg = eb.Config(d=d, k=k, seed=seed, spherical=spherical, nepochs=2.0)
-        a = group.train(x, cfg)
-        b = solo.train(x, cfg)
-        assert np.array_equal(a.centroids.view(np.uint32), b.centroids.view(np.uint32)), \
-            f"rank {rank}: centroids differ (n={n}, k={k})"
-        assert np.array_equal(a.labels, b.labels), f"rank {rank}: labels differ"
-        assert a.obj == b.obj and a.nsplit == b.nsplit, f"rank {rank}: statistics differ"
+    # Every batch split and exchanged (mode 1), and the default (mode 0: these
+    # batches are one wave of row tiles or less, so every rank scores them whole).
+    for mode in (1, 0):
+        group.set_group_shard(mode)
+        for n, d, k, spherical, seed in cases:
+            x = mixture(n, d, 24, 0.4, spherical, seed)
+            cfg = eb.Config(d=d, k=k, seed=seed, spherical=spherical, nepochs=2.0)
+            a = group.train(x, cfg)
+            b = solo.train(x, cfg)
+            assert np.array_equal(a.centroids.view(np.uint32), b.centroids.view(np.uint32)), \
+                f"rank {rank}: centroids differ (n={n}, k={k}, mode {mode})"
+            assert np.array_equal(a.labels, b.labels), f"rank {rank}: labels differ"
+            assert a.obj == b.obj and a.nsplit == b.nsplit, f"rank {rank}: statistics differ"
     # knn_self over a database sharded across the ranks, against one engine
     # ranking the whole database.
     rng = np.random.default_rng(11)
