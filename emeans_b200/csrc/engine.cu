@@ -668,19 +668,42 @@ int eb_assign(eb_engine* e, const float* rows, size_t n, size_t d, const uint32_
     } else {
       // Dense rows: copied in slices on the copy stream, each slice's top-1
       // queued on the engine's stream behind its own copy, so that the copy
-      // of slice j + 1 overlaps the top-1 of slice j. The centroids'
-      // screen copy is made once, by the first slice that takes the screen.
+      // of slice j + 1 overlaps the top-1 of slice j. The last slice is
+      // small (16,384 rows when there are at least 65,536), so that little
+      // compute remains once the last copy has landed; with pinned output
+      // buffers each slice's labels and scores go back as soon as they are
+      // ready. The centroids' screen copy is made once, by the first slice
+      // that takes the screen.
       float* xd = e->scratch_get<float>("as_x", m * d);
       if (!e->copy_stream) EB_CUDA(cudaStreamCreateWithFlags(&e->copy_stream, cudaStreamNonBlocking));
-      const size_t slice = std::max<size_t>(16384, (m + 3) / 4);
+      std::vector<size_t> cut{0};
+      if (m >= 65536) {
+        const size_t body = m - 16384, third = (body + 2) / 3;
+        for (size_t r = third; r < body; r += third) cut.push_back(r);
+        cut.push_back(body);
+      } else {
+        const size_t slice = std::max<size_t>(16384, (m + 3) / 4);
+        for (size_t r = slice; r < m; r += slice) cut.push_back(r);
+      }
+      cut.push_back(m);
+      auto pinned = [](const void* p) {
+        cudaPointerAttributes at{};
+        if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+          cudaGetLastError();
+          return false;
+        }
+        return at.type == cudaMemoryTypeHost;
+      };
+      const bool early_out = pinned(labels) && pinned(scores);
       cudaEvent_t ready;
       EB_CUDA(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
       EB_CUDA(cudaEventRecord(ready, e->stream));  // earlier work on the staging buffer
       EB_CUDA(cudaStreamWaitEvent(e->copy_stream, ready, 0));
       EB_CUDA(cudaEventDestroy(ready));
       bool converted = false;
-      for (size_t r0 = 0; r0 < m; r0 += slice) {
-        const size_t r1 = std::min(m, r0 + slice);
+      for (size_t j = 0; j + 1 < cut.size(); j++) {
+        const size_t r0 = cut[j], r1 = cut[j + 1];
+        if (r1 == r0) continue;
         EB_CUDA(cudaMemcpyAsync(xd + r0 * d, rows + r0 * d, (r1 - r0) * d * 4,
                                 cudaMemcpyHostToDevice, e->copy_stream));
         cudaEvent_t landed;
@@ -706,6 +729,16 @@ int eb_assign(eb_engine* e, const float* rows, size_t n, size_t d, const uint32_
         const bool screened = eb::top1_screen_supported(e, a);
         eb::top1_dispatch(e, a, nullptr);
         converted = converted || screened;
+        if (early_out) {
+          EB_CUDA(cudaMemcpyAsync(labels + r0, lab + r0, (r1 - r0) * 4, cudaMemcpyDeviceToHost,
+                                  e->stream));
+          EB_CUDA(cudaMemcpyAsync(scores + r0, sco + r0, (r1 - r0) * 4, cudaMemcpyDeviceToHost,
+                                  e->stream));
+        }
+      }
+      if (early_out) {
+        eb::sync(e);
+        return;
       }
       rc = EB_OK;
     }

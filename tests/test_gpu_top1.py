@@ -199,6 +199,29 @@ def test_assign_host_api(eng, metric):
 
 
 @pytest.mark.parametrize("metric", [eb.IP, eb.L2])
+def test_assign_pinned_buffers_in_slices(engine, metric):
+    """eb_assign with pinned host buffers and enough rows (70,000) for the
+    sliced path: three large slices and a small last one, each slice's labels
+    and scores copied back as soon as they are ready."""
+    import torch
+
+    n, d, k = 70000, 64, 300
+    x = mixture(n, d, 40, 0.5, metric == eb.IP, 91)
+    c = contract_centroids(x, d, k)
+    hx = torch.from_numpy(x).pin_memory()
+    hc = torch.from_numpy(np.ascontiguousarray(c)).pin_memory()
+    hl = torch.empty(n, dtype=torch.int32).pin_memory()
+    hs = torch.empty(n, dtype=torch.float32).pin_memory()
+    engine.assign_ptr(hx.data_ptr(), n, d, hc.data_ptr(), k, metric, hl.data_ptr(),
+                      hs.data_ptr())
+    wl, ws = oracle.top1(x.ravel(), d, c.ravel(), metric)
+    assert np.array_equal(hl.numpy().view(np.uint32), wl)
+    assert np.array_equal(bits(hs.numpy()), bits(ws))
+    gl, gs = engine.assign(x, d, c, metric)  # pageable buffers: results at the end
+    assert np.array_equal(gl, wl) and np.array_equal(bits(gs), bits(ws))
+
+
+@pytest.mark.parametrize("metric", [eb.IP, eb.L2])
 def test_assign_only_config_shape(engine, metric):
     """The assign-only config's shape, scaled in rows: unit rows and k = 65,536
     unit centroids drawn the same way, d = 1024 (256 centroid tiles per row
