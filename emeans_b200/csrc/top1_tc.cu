@@ -529,7 +529,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 1;
   uint64_t* mma_done = tempty + 1;
-  uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
+  // Top-k mode: the second accumulator buffer's pair.
+  uint64_t* tfull1 = mma_done + 1;
+  uint64_t* tempty1 = tfull1 + 1;
+  uint32_t* tmem_slot = (uint32_t*)(tempty1 + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   float* cn_s = (float*)(smem + STAGES * STAGE_BYTES + 256);  // [8 warps][HALF]
   float* sv_s = cn_s + 8 * HALF;                               // [8 warps][16][32]
@@ -548,6 +551,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(tfull, 1);
     mbar_init(tempty, 256);
     mbar_init(mma_done, 1);
+    mbar_init(tfull1, 1);
+    mbar_init(tempty1, 256);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -603,8 +608,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool stop = false;
       for (long rt = blockIdx.x; rt * BM < P.m && !stop; rt += gridDim.x) {
         for (int nt = 0; nt < P.ntiles; nt++, tc++) {
-          // The epilogue must have read both accumulators of the last tile.
-          if (!mbar_wait(tempty, (tc & 1) ^ 1, abort_flag)) {
+          // Top-1 mode: the epilogue must have read both accumulators of the
+          // last tile. Top-k mode: one accumulator per tile, two buffers in
+          // turn; the epilogue must have read this buffer's last tile.
+          const int buf = TOPK ? (tc & 1) : 0;
+          const uint32_t use = TOPK ? (uint32_t)(tc >> 1) : (uint32_t)tc;
+          if (!mbar_wait(buf ? tempty1 : tempty, (use & 1) ^ 1, abort_flag)) {
             stop = true;
             break;
           }
@@ -622,9 +631,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int kk = 0; kk < BKH / 16; kk++) {
               const uint32_t first = (kb > 0 || kk > 0) ? 1u : 0u;
-              umma_f16(tmem, umma_desc(ah + kk * 32), umma_desc(bh + kk * 32), first);
-              umma_f16(tmem + BN, umma_desc(ah + kk * 32), umma_desc(bl + kk * 32), first);
-              umma_f16(tmem + BN, umma_desc(al + kk * 32), umma_desc(bh + kk * 32), 1u);
+              if constexpr (TOPK) {
+                // All three products into the buffer's one accumulator.
+                const uint32_t dacc = tmem + (uint32_t)(buf * BN);
+                umma_f16(dacc, umma_desc(ah + kk * 32), umma_desc(bh + kk * 32), first);
+                umma_f16(dacc, umma_desc(ah + kk * 32), umma_desc(bl + kk * 32), 1u);
+                umma_f16(dacc, umma_desc(al + kk * 32), umma_desc(bh + kk * 32), 1u);
+              } else {
+                umma_f16(tmem, umma_desc(ah + kk * 32), umma_desc(bh + kk * 32), first);
+                umma_f16(tmem + BN, umma_desc(ah + kk * 32), umma_desc(bl + kk * 32), first);
+                umma_f16(tmem + BN, umma_desc(al + kk * 32), umma_desc(bh + kk * 32), 1u);
+              }
             }
             umma_commit(&empty[s]);
           }
@@ -632,7 +649,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             stop = true;
             break;
           }
-          umma_commit(tfull);
+          umma_commit(buf ? tfull1 : tfull);
         }
       }
       // Every MMA this thread issued has completed once mma_done flips.
@@ -703,7 +720,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
       for (int nt = 0; nt < P.ntiles; nt++, tc++) {
         // Warp-uniform: the TMEM loads below are .sync.aligned.
-        const bool ready = __all_sync(0xFFFFFFFFu, mbar_wait(tfull, tc & 1, abort_flag));
+        const int buf = TOPK ? (tc & 1) : 0;
+        const uint32_t use = TOPK ? (uint32_t)(tc >> 1) : (uint32_t)tc;
+        const bool ready =
+            __all_sync(0xFFFFFFFFu, mbar_wait(buf ? tfull1 : tfull, use & 1, abort_flag));
         if (!ready) {
           stop = true;
           break;
@@ -883,23 +903,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         };
         if constexpr (TOPK) {
+          // One accumulator per tile (all three products), in buffer buf.
 #pragma unroll 1
           for (int g = 0; g < HALF / 16; g++) {
             if (g >= ngr) break;
-            uint32_t lo1[16];
-            tmem_ld16(lane_base + (uint32_t)(g * 16), acc[0]);
-            tmem_ld16(lane_base + (uint32_t)(BN + g * 16), lo1);
+            tmem_ld16(lane_base + (uint32_t)(buf * BN + g * 16), acc[0]);
             tmem_wait();
             tmem_tie(acc[0]);
-            tmem_tie(lo1);
-#pragma unroll
-            for (int j = 0; j < 16; j++)
-              acc[0][j] = __float_as_uint(
-                  __fadd_rn(__uint_as_float(acc[0][j]), __uint_as_float(lo1[j])));
             score_group(g);
           }
           tc_fence_before();
-          mbar_arrive(tempty);
+          mbar_arrive(buf ? tempty1 : tempty);
         } else {
 #pragma unroll
           for (int g = 0; g < HALF / 16; g++) {
@@ -1829,15 +1843,19 @@ void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const ExactS
 namespace {
 
 // The bound coefficients of the header comment for this d, with 1% slack.
-void screen_bound(size_t d, float& e_rel, float& e_abs, float& e_min) {
+// With one accumulator (top-k mode) all 3d products are added into it, so
+// the accumulation term counts 3d additions and the lo accumulator's term
+// falls away.
+void screen_bound(size_t d, float& e_rel, float& e_abs, float& e_min, bool one_acc = false) {
   const double dd = (double)d;
+  const double adds = one_acc ? 3.0 * dd : dd;
   const double u24 = std::ldexp(1.0, -24);
   const double gamma_d = dd * u24 / (1.0 - dd * u24);
-  e_rel = (float)((3.0 * std::ldexp(1.0, -22) + dd * std::ldexp(1.0, -21) * (1.0 + std::ldexp(1.0, -9)) +
-                   dd * std::ldexp(1.0, -30) + std::ldexp(1.0, -23) + gamma_d) *
+  e_rel = (float)((3.0 * std::ldexp(1.0, -22) + adds * std::ldexp(1.0, -21) * (1.0 + std::ldexp(1.0, -9)) +
+                   (one_acc ? 0.0 : dd * std::ldexp(1.0, -30)) + std::ldexp(1.0, -23) + gamma_d) *
                   1.01);
   e_abs = (float)(std::ldexp(1.0, -23) * std::sqrt(dd) * 1.01);
-  e_min = (float)(dd * std::ldexp(1.0, -48));
+  e_min = (float)(adds * std::ldexp(1.0, -48));
 }
 
 
@@ -2025,7 +2043,7 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
   const size_t wave = (size_t)e->num_sms * BM;
   const size_t chunk = std::min(m, PASS_WAVES * wave);
   float e_rel, e_abs, e_min;
-  screen_bound(d, e_rel, e_abs, e_min);
+  screen_bound(d, e_rel, e_abs, e_min, true);
 
   // The data rows play the centroids: one exponent, split FP16 copy.
   unsigned long long* cinfo = e->scratch_get<unsigned long long>("tc_cinfo", 4, true);
