@@ -35,6 +35,11 @@
 //                     add 2^-23
 //   the FP32 chain:   gamma_d sum|x c| from the exact dot
 // with sum|x'||c'| <= |x'| |c'| and sum|x'| <= sqrt(d) |x'| (Cauchy-Schwarz).
+//
+// Top-k mode (k_screen<true, true>) gives each tile one accumulator that takes
+// all three products and alternates two accumulator buffers, so that the MMAs
+// of the next tile overlap the scoring of this one; its accumulation term
+// counts 3d additions (3 d 2^-21) and has no lo accumulator term.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
