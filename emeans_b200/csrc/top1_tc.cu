@@ -86,6 +86,7 @@ constexpr int A_BYTES = BM * BKH * 2;                // one of xh / xl
 constexpr int B_BYTES = BN * BKH * 2;                // one of ch / cl
 constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
 constexpr int CAP = 64;          // per-row candidate list capacity
+constexpr int CAP_TOPK = 128;    // the same in top-k mode (lists there grow further)
 constexpr int SURV = 64;         // candidates per row taken to exact chains (more: full scan)
 constexpr int KMAX = 16;         // largest k of the top-k mode
 // Three warpgroups: warp 0 TMA, warp 1 MMA (warps 2-3 idle), warps 4-11 epilogue.
@@ -488,6 +489,22 @@ __global__ void __launch_bounds__(64) k_cent_conv(const float* __restrict__ c, l
   }
 }
 
+// Top-k mode: v (> kv[0]) replaces the smallest of the ascending kv[0 .. KMAX)
+// and takes its place in the order. The slots below v's place each take the
+// next slot's value: independent selects instead of a chain of KMAX - 1
+// compare-exchanges.
+__device__ __forceinline__ void kv_insert(float (&kv)[KMAX], float v) {
+  float nk[KMAX];
+#pragma unroll
+  for (int a = 0; a < KMAX; a++) {
+    const bool shift = a + 1 < KMAX && kv[a + 1] < v;          // a is below v's place
+    const bool here = !shift && (a == 0 || kv[a] < v);           // v's place
+    nk[a] = shift ? kv[a + 1] : (here ? v : kv[a]);
+  }
+#pragma unroll
+  for (int a = 0; a < KMAX; a++) kv[a] = nk[a];
+}
+
 // ---------------------------------------------------------------- the screen
 
 struct ScreenParams {
@@ -502,7 +519,7 @@ struct ScreenParams {
   uint32_t cgen;
   float e_rel, e_abs, e_min;  // bound coefficients (see the header comment)
   // Candidate lists, one per (half tile, row): half h, entry e of row i at
-  // (h CAP + e) m + i (id, screened value bits).
+  // (h C + e) m + i (id, screened value bits), C = CAP (CAP_TOPK in top-k mode).
   uint2* cand;
   uint32_t* cand_cnt;  // 2 m: entries in use per (half, row), or FALLBACK
   float* cand_thr;     // 2 m: the final admission threshold per (half, row)
@@ -714,7 +731,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       float thr = best;
       bool overflow = false;
       uint32_t cnt = 0;  // entries in this (row, half)'s candidate list
-      uint2* row_list = P.cand + (long)hf * CAP * P.m + (live ? i : 0);  // entries P.m apart
+      constexpr int LCAP = TOPK ? CAP_TOPK : CAP;
+      uint2* row_list = P.cand + (long)hf * LCAP * P.m + (live ? i : 0);  // entries P.m apart
       // Top-k mode: the best kk screened values so far in slots 0 .. kk - 1,
       // ascending (the kk-th best in slot 0), slots kk .. KMAX - 1 held at +inf.
       float kv[TOPK ? KMAX : 1];
@@ -789,15 +807,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         auto score_group = [&](const int g) {
           const uint32_t(&h)[16] = acc[TOPK ? 0 : g];
           float s[16];
-          const float4* c4 = reinterpret_cast<const float4*>(cns + g * 16);
+          if constexpr (TOPK) {
+            // Inner product: the accumulator is the screened value.
 #pragma unroll
-          for (int j = 0; j < 16; j += 4) {
-            const float4 cv = IP ? make_float4(0.f, 0.f, 0.f, 0.f) : c4[j / 4];
-            const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
+            for (int j = 0; j < 16; j++) s[j] = __uint_as_float(h[j]);
+          } else {
+            const float4* c4 = reinterpret_cast<const float4*>(cns + g * 16);
 #pragma unroll
-            for (int w = 0; w < 4; w++) {
-              const float v = __uint_as_float(h[j + w]);  // hi + lo, added in the drain
-              s[j + w] = __fmaf_rn(m2f, v, cc[w]);
+            for (int j = 0; j < 16; j += 4) {
+              const float4 cv = IP ? make_float4(0.f, 0.f, 0.f, 0.f) : c4[j / 4];
+              const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
+#pragma unroll
+              for (int w = 0; w < 4; w++) {
+                const float v = __uint_as_float(h[j + w]);  // hi + lo, added in the drain
+                s[j + w] = __fmaf_rn(m2f, v, cc[w]);
+              }
             }
           }
           const int lim = P.k - (col0 + g * 16);
@@ -808,9 +832,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           if (TOPK && P.exclude_self) {
             const long rel = gid - (P.col_gid0 + col0 + g * 16);  // the row's own column
+            if ((unsigned long)rel < 16ul) {
 #pragma unroll
-            for (int j = 0; j < 16; j++)
-              if (rel == j) s[j] = -INFINITY;
+              for (int j = 0; j < 16; j++)
+                if (rel == j) s[j] = -INFINITY;
+            }
           }
           // The group's best moves the threshold first.
           float t[8];
@@ -833,13 +859,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             const int nup = __popc(m_up);
             if (nup == 1) {
-              kv[0] = t[0];
-#pragma unroll
-              for (int a = 0; a + 1 < KMAX; a++) {
-                const float lo_v = fminf(kv[a], kv[a + 1]), hi_v = fmaxf(kv[a], kv[a + 1]);
-                kv[a] = lo_v;
-                kv[a + 1] = hi_v;
-              }
+              kv_insert(kv, t[0]);
               kth = kv[0];
             }
             if (__any_sync(0xFFFFFFFFu, nup > 1)) {
@@ -852,14 +872,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                   m_up &= m_up - 1;
                   const float cv = svs[j * 32];
                   if (!(cv > kv[0])) continue;
-                  // Replace the smallest and let it rise to its place.
-                  kv[0] = cv;
-#pragma unroll
-                  for (int a = 0; a + 1 < KMAX; a++) {
-                    const float lo_v = fminf(kv[a], kv[a + 1]), hi_v = fmaxf(kv[a], kv[a + 1]);
-                    kv[a] = lo_v;
-                    kv[a + 1] = hi_v;
-                  }
+                  kv_insert(kv, cv);
                   kth = kv[0];
                 }
               }
@@ -882,26 +895,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           // the values back by index.
           const int na = __popc(adm);
           if (TOPK && na == 1) {
-            if (cnt + 1 > CAP) cnt = compact_list<IP>(row_list, P.m, cnt, thr);
-            if (cnt < CAP)
+            if (cnt + 1 > LCAP) cnt = compact_list<IP>(row_list, P.m, cnt, thr);
+            if (cnt < LCAP)
               row_list[cnt * P.m] =
                   make_uint2((uint32_t)(col0 + g * 16 + __ffs(adm) - 1), __float_as_uint(t[0]));
-            overflow |= cnt >= CAP;
-            cnt += cnt < CAP;
+            overflow |= cnt >= LCAP;
+            cnt += cnt < LCAP;
           }
           if (__any_sync(0xFFFFFFFFu, TOPK ? na > 1 : na > 0)) {
 #pragma unroll
             for (int j = 0; j < 16; j++) svs[j * 32] = s[j];
             __syncwarp();
             if (TOPK ? na > 1 : na > 0) {
-              if (cnt + (uint32_t)na > CAP) cnt = compact_list<IP>(row_list, P.m, cnt, thr);
+              if (cnt + (uint32_t)na > LCAP) cnt = compact_list<IP>(row_list, P.m, cnt, thr);
               const uint32_t base = (uint32_t)(col0 + g * 16);
               while (adm) {
                 const int j = __ffs(adm) - 1;
                 adm &= adm - 1;
-                if (cnt < CAP) row_list[cnt * P.m] = make_uint2(base + j, __float_as_uint(svs[j * 32]));
-                overflow |= cnt >= CAP;
-                cnt += cnt < CAP;
+                if (cnt < LCAP) row_list[cnt * P.m] = make_uint2(base + j, __float_as_uint(svs[j * 32]));
+                overflow |= cnt >= LCAP;
+                cnt += cnt < LCAP;
               }
             }
             __syncwarp();
@@ -1568,7 +1581,7 @@ __global__ void __launch_bounds__(256) k_collect_topk(
     if (cnt[h] == FALLBACK) {
       fb = true;
       cnt[h] = 0;
-    } else if (cnt[h] > CAP) {
+    } else if (cnt[h] > CAP_TOPK) {
       atomicOr(status, ST_BAD_STATE);
       fb = true;
       cnt[h] = 0;
@@ -1597,7 +1610,7 @@ __global__ void __launch_bounds__(256) k_collect_topk(
     thr = kth > -INFINITY ? __fsub_rd(kth, roff[i]) : -INFINITY;
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-      const uint2* lst = cand + (long)h * CAP * m + i;
+      const uint2* lst = cand + (long)h * CAP_TOPK * m + i;
       for (uint32_t e = 0; e < cnt[h]; e++) {
         const uint2 en = lst[e * m];
         const float sv = __uint_as_float(en.y);
@@ -1620,7 +1633,7 @@ __global__ void __launch_bounds__(256) k_collect_topk(
   if (np) {
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-      const uint2* lst = cand + (long)h * CAP * m + i;
+      const uint2* lst = cand + (long)h * CAP_TOPK * m + i;
       for (uint32_t e = 0; e < cnt[h]; e++) {
         const uint2 en = lst[e * m];
         const float sv = __uint_as_float(en.y);
@@ -2063,7 +2076,7 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
   __half* xl = e->scratch_get<__half>("tc_xl", chunk * dp);
   int* xexp = e->scratch_get<int>("tc_xexp", chunk);
   float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
-  uint2* cand = e->scratch_get<uint2>("tc_cand", 2 * chunk * CAP);
+  uint2* cand = e->scratch_get<uint2>("tc_cand", 2 * chunk * CAP_TOPK);
   uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", 2 * chunk);
   float* cand_thr = e->scratch_get<float>("tc_thr", 2 * chunk);
   float* kvals = e->scratch_get<float>("tk_kvals", 2 * chunk * KMAX);
