@@ -190,6 +190,9 @@ int eb_engine_destroy(eb_engine* e) {
     for (auto& kv : e->scratch)
       if (kv.second.p) cudaFreeAsync(kv.second.p, e->stream);
     cudaStreamSynchronize(e->stream);
+    if (e->copy_stream) cudaStreamSynchronize(e->copy_stream);
+    for (cudaEvent_t v : e->stage_ev)
+      if (v) cudaEventDestroy(v);
     for (auto& kv : e->pinned)
       if (kv.second.p) cudaFreeHost(kv.second.p);
     cudaFree(e->d_status);
@@ -338,8 +341,7 @@ int eb_buf_write(eb_engine* e, eb_buf* b, size_t offset, const void* host, size_
     if (len == 0) return;
     need(host, "host");
     DeviceGuard g(e);
-    EB_CUDA(cudaMemcpyAsync(static_cast<char*>(b->ptr) + offset * 4, host, len * 4,
-                            cudaMemcpyHostToDevice, e->stream));
+    eb::h2d(e, static_cast<char*>(b->ptr) + offset * 4, host, len * 4, e->stream);
     b->version++;
     eb::drop_f16(b);
     if (b->xnorm) {
@@ -357,8 +359,7 @@ int eb_buf_read(eb_engine* e, const eb_buf* b, size_t lo, size_t hi, void* host)
     DeviceGuard g(e);
     if (hi > lo) {
       need(host, "host");
-      EB_CUDA(cudaMemcpyAsync(host, static_cast<const char*>(b->ptr) + lo * 4, (hi - lo) * 4,
-                              cudaMemcpyDeviceToHost, e->stream));
+      eb::d2h(e, host, static_cast<const char*>(b->ptr) + lo * 4, (hi - lo) * 4, e->stream);
     }
     eb::sync(e);
   });
@@ -372,8 +373,7 @@ int eb_buf_upload(eb_engine* e, int dtype, const void* host, size_t len, eb_buf*
     ensure(host != nullptr || len == 0, "host is null");
     DeviceGuard g(e);
     eb_buf* b = eb::new_buf(e, dtype, len);
-    if (len)
-      EB_CUDA(cudaMemcpyAsync(b->ptr, host, len * 4, cudaMemcpyHostToDevice, e->stream));
+    if (len) eb::h2d(e, b->ptr, host, len * 4, e->stream);
     *out = b;
   });
 }
@@ -386,7 +386,7 @@ int eb_bind(eb_engine* e, const float* x, size_t n, size_t d, eb_buf** out) {
     ensure(x != nullptr || n == 0, "x is null");
     DeviceGuard g(e);
     eb_buf* b = eb::new_buf(e, EB_F32, n * d);
-    if (n) EB_CUDA(cudaMemcpyAsync(b->ptr, x, n * d * 4, cudaMemcpyHostToDevice, e->stream));
+    if (n) eb::h2d(e, b->ptr, x, n * d * 4, e->stream);
     b->d = d;
     *out = b;
   });
@@ -632,7 +632,7 @@ int eb_assign(eb_engine* e, const float* rows, size_t n, size_t d, const uint32_
     need(scores, "scores");
     DeviceGuard g(e);
     float* c = e->scratch_get<float>("as_c", k * d);
-    EB_CUDA(cudaMemcpyAsync(c, centroids, k * d * 4, cudaMemcpyHostToDevice, e->stream));
+    eb::h2d(e, c, centroids, k * d * 4, e->stream);
     float* cn = nullptr;
     if (metric == EB_L2) {
       cn = e->scratch_get<float>("as_cn", k);
@@ -660,7 +660,7 @@ int eb_assign(eb_engine* e, const float* rows, size_t n, size_t d, const uint32_
       std::vector<float> gbuf(m * d);
       for (size_t i = 0; i < m; i++)
         std::memcpy(&gbuf[i * d], rows + (size_t)ids[i] * d, d * 4);
-      EB_CUDA(cudaMemcpyAsync(xd, gbuf.data(), m * d * 4, cudaMemcpyHostToDevice, e->stream));
+      eb::h2d(e, xd, gbuf.data(), m * d * 4, e->stream);
       eb_buf xb;
       xb.ptr = xd; xb.len = m * d; xb.dtype = EB_F32;
       rc = eb_top1(e, &xb, d, nullptr, 0, m, &cb, metric == EB_L2 ? &cnb : nullptr, k, metric,
@@ -686,15 +686,7 @@ int eb_assign(eb_engine* e, const float* rows, size_t n, size_t d, const uint32_
         for (size_t r = slice; r < m; r += slice) cut.push_back(r);
       }
       cut.push_back(m);
-      auto pinned = [](const void* p) {
-        cudaPointerAttributes at{};
-        if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
-          cudaGetLastError();
-          return false;
-        }
-        return at.type == cudaMemoryTypeHost;
-      };
-      const bool early_out = pinned(labels) && pinned(scores);
+      const bool early_out = eb::host_pinned(labels) && eb::host_pinned(scores);
       cudaEvent_t ready;
       EB_CUDA(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
       EB_CUDA(cudaEventRecord(ready, e->stream));  // earlier work on the staging buffer
@@ -704,8 +696,7 @@ int eb_assign(eb_engine* e, const float* rows, size_t n, size_t d, const uint32_
       for (size_t j = 0; j + 1 < cut.size(); j++) {
         const size_t r0 = cut[j], r1 = cut[j + 1];
         if (r1 == r0) continue;
-        EB_CUDA(cudaMemcpyAsync(xd + r0 * d, rows + r0 * d, (r1 - r0) * d * 4,
-                                cudaMemcpyHostToDevice, e->copy_stream));
+        eb::h2d(e, xd + r0 * d, rows + r0 * d, (r1 - r0) * d * 4, e->copy_stream);
         cudaEvent_t landed;
         EB_CUDA(cudaEventCreateWithFlags(&landed, cudaEventDisableTiming));
         EB_CUDA(cudaEventRecord(landed, e->copy_stream));
@@ -743,8 +734,8 @@ int eb_assign(eb_engine* e, const float* rows, size_t n, size_t d, const uint32_
       rc = EB_OK;
     }
     if (rc != EB_OK) throw eb::Error(rc, g_last_error);
-    EB_CUDA(cudaMemcpyAsync(labels, lab, m * 4, cudaMemcpyDeviceToHost, e->stream));
-    EB_CUDA(cudaMemcpyAsync(scores, sco, m * 4, cudaMemcpyDeviceToHost, e->stream));
+    eb::d2h(e, labels, lab, m * 4, e->stream);
+    eb::d2h(e, scores, sco, m * 4, e->stream);
     eb::sync(e);
   });
 }

@@ -114,8 +114,10 @@ struct eb_engine {
   // a new generation, so the summary needs no zeroing pass per call.
   uint32_t cinfo_gen = 0;
   unsigned long long* counters() { return d_counters; }
-  // Pinned host buffers (training read-backs), grown on demand, freed with
-  // the engine.
+  // Events of the two pinned staging buffers of caller copies (hostcopy.cpp).
+  cudaEvent_t stage_ev[2] = {nullptr, nullptr};
+  // Pinned host buffers (training read-backs, staging), grown on demand,
+  // freed with the engine.
   std::unordered_map<std::string, eb::Scratch> pinned;
   template <class T>
   T* pinned_get(const char* name, size_t count) {
@@ -186,6 +188,13 @@ void launch_pdl(eb_engine* e, void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 #endif
 
 eb_buf* new_buf(eb_engine* e, int dtype, size_t len);
+// Copies of caller host memory (hostcopy.cpp): pinned memory directly,
+// pageable memory through the engine's pinned staging buffers. h2d returns
+// once the source may be reused (the last DMA may still be in flight on st);
+// d2h returns once dst holds the data.
+bool host_pinned(const void* p);
+void h2d(eb_engine* e, void* dst, const void* src, size_t bytes, cudaStream_t st);
+void d2h(eb_engine* e, void* dst, const void* src, size_t bytes, cudaStream_t st);
 void free_buf(eb_engine* e, eb_buf* b);
 void sync(eb_engine* e);  // wait + status check (throws)
 void set_last_error(const std::string& msg);

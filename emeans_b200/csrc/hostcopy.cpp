@@ -1,0 +1,119 @@
+// Host <-> device copies of caller memory that may be pageable.
+//
+// A cudaMemcpyAsync from pageable memory goes through the driver's own
+// staging at a few GB/s (7.4 GB/s measured for 154 MB on a B200 host) and
+// synchronises the stream first. Here pageable memory is copied through two
+// pinned staging buffers of the engine: the host fills one (its copy split
+// over several threads) while the DMA of the other runs, so the transfer
+// moves at the host's memory bandwidth. Pinned caller memory is copied
+// directly.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+#include "engine.h"
+
+namespace eb {
+
+namespace {
+
+constexpr size_t kStage = 32u << 20;  // bytes per staging buffer
+
+// memcpy over up to 8 threads for large copies.
+void par_memcpy(void* dst, const void* src, size_t bytes) {
+  const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+  const size_t nt = bytes >= (4u << 20) ? std::min<size_t>(8, std::max<size_t>(1, hw / 2)) : 1;
+  if (nt <= 1) {
+    std::memcpy(dst, src, bytes);
+    return;
+  }
+  const size_t per = (bytes / nt + 63) & ~(size_t)63;
+  std::vector<std::thread> th;
+  for (size_t t = 1; t < nt; t++) {
+    const size_t lo = std::min(bytes, t * per), hi = std::min(bytes, lo + per);
+    if (hi > lo)
+      th.emplace_back([=] {
+        std::memcpy(static_cast<char*>(dst) + lo, static_cast<const char*>(src) + lo, hi - lo);
+      });
+  }
+  std::memcpy(dst, src, std::min(bytes, per));
+  for (auto& t : th) t.join();
+}
+
+struct Staging {
+  char* buf[2];
+  cudaEvent_t done[2];
+};
+
+// The engine's two staging buffers and their events (created on first use).
+Staging staging(eb_engine* e) {
+  Staging s;
+  s.buf[0] = e->pinned_get<char>("hc_stage0", kStage);
+  s.buf[1] = e->pinned_get<char>("hc_stage1", kStage);
+  for (int i = 0; i < 2; i++) {
+    if (!e->stage_ev[i]) EB_CUDA(cudaEventCreateWithFlags(&e->stage_ev[i], cudaEventDisableTiming));
+    s.done[i] = e->stage_ev[i];
+  }
+  return s;
+}
+
+}  // namespace
+
+bool host_pinned(const void* p) {
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return at.type == cudaMemoryTypeHost;
+}
+
+void h2d(eb_engine* e, void* dst, const void* src, size_t bytes, cudaStream_t st) {
+  if (!bytes) return;
+  if (bytes < (1u << 20) || host_pinned(src)) {
+    EB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, st));
+    return;
+  }
+  Staging s = staging(e);
+  for (size_t off = 0, j = 0; off < bytes; off += kStage, j++) {
+    const int b = (int)(j & 1);
+    const size_t len = std::min(kStage, bytes - off);
+    EB_CUDA(cudaEventSynchronize(s.done[b]));  // the buffer's last DMA has finished
+    par_memcpy(s.buf[b], static_cast<const char*>(src) + off, len);
+    EB_CUDA(cudaMemcpyAsync(static_cast<char*>(dst) + off, s.buf[b], len, cudaMemcpyHostToDevice, st));
+    EB_CUDA(cudaEventRecord(s.done[b], st));
+  }
+}
+
+void d2h(eb_engine* e, void* dst, const void* src, size_t bytes, cudaStream_t st) {
+  if (!bytes) return;
+  if (bytes < (1u << 20) || host_pinned(dst)) {
+    EB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, st));
+    EB_CUDA(cudaStreamSynchronize(st));
+    return;
+  }
+  Staging s = staging(e);
+  size_t pend_off[2] = {0, 0}, pend_len[2] = {0, 0};
+  auto drain = [&](int b) {
+    if (!pend_len[b]) return;
+    EB_CUDA(cudaEventSynchronize(s.done[b]));
+    par_memcpy(static_cast<char*>(dst) + pend_off[b], s.buf[b], pend_len[b]);
+    pend_len[b] = 0;
+  };
+  for (size_t off = 0, j = 0; off < bytes; off += kStage, j++) {
+    const int b = (int)(j & 1);
+    const size_t len = std::min(kStage, bytes - off);
+    drain(b);  // the buffer's last chunk has been copied out
+    EB_CUDA(cudaMemcpyAsync(s.buf[b], static_cast<const char*>(src) + off, len, cudaMemcpyDeviceToHost, st));
+    EB_CUDA(cudaEventRecord(s.done[b], st));
+    pend_off[b] = off;
+    pend_len[b] = len;
+  }
+  drain(0);
+  drain(1);
+}
+
+}  // namespace eb

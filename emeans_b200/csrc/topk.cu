@@ -200,9 +200,9 @@ void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, s
   uint32_t* di = group ? stage + (size_t)e->rank * 2 * m * kk
                        : e->scratch_get<uint32_t>("tk_ids", m * kk);
   float* ds = group ? reinterpret_cast<float*>(di + m * kk) : e->scratch_get<float>("tk_sims", m * kk);
-  EB_CUDA(cudaMemcpyAsync(dq, q, m * d * 4, cudaMemcpyHostToDevice, e->stream));
+  h2d(e, dq, q, m * d * 4, e->stream);
   if (n && !self_join)
-    EB_CUDA(cudaMemcpyAsync(dd, data, n * d * 4, cudaMemcpyHostToDevice, e->stream));
+    h2d(e, dd, data, n * d * 4, e->stream);
   if (!topk_screen(e, dq, m, dd, n, d, kk, exclude_self, di, ds, id0)) {
     unsigned grid = (unsigned)((m + BM - 1) / BM);
     k_topk_exact<<<grid, NT, 0, e->stream>>>(dq, (long)m, dd, (long)n, (int)d, (int)kk,
@@ -218,8 +218,8 @@ void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, s
                                                                      e->world, di, ds);
     EB_LAUNCH("topk merge");
   }
-  EB_CUDA(cudaMemcpyAsync(ids, di, m * kk * 4, cudaMemcpyDeviceToHost, e->stream));
-  EB_CUDA(cudaMemcpyAsync(sims, ds, m * kk * 4, cudaMemcpyDeviceToHost, e->stream));
+  d2h(e, ids, di, m * kk * 4, e->stream);
+  d2h(e, sims, ds, m * kk * 4, e->stream);
   sync(e);
 }
 
