@@ -31,16 +31,21 @@ void par_memcpy(void* dst, const void* src, size_t bytes) {
     return;
   }
   const size_t per = (bytes / nt + 63) & ~(size_t)63;
-  std::vector<std::thread> th;
-  for (size_t t = 1; t < nt; t++) {
+  auto part = [=](size_t t) {
     const size_t lo = std::min(bytes, t * per), hi = std::min(bytes, lo + per);
     if (hi > lo)
-      th.emplace_back([=] {
-        std::memcpy(static_cast<char*>(dst) + lo, static_cast<const char*>(src) + lo, hi - lo);
-      });
+      std::memcpy(static_cast<char*>(dst) + lo, static_cast<const char*>(src) + lo, hi - lo);
+  };
+  std::vector<std::thread> th;
+  size_t t = 1;
+  try {
+    for (; t < nt; t++) th.emplace_back(part, t);
+  } catch (...) {
+    // No more threads: this thread copies the parts that have none.
   }
-  std::memcpy(dst, src, std::min(bytes, per));
-  for (auto& t : th) t.join();
+  for (size_t u = t; u < nt; u++) part(u);
+  part(0);
+  for (auto& w : th) w.join();
 }
 
 struct Staging {
