@@ -847,6 +847,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int j = 0; j < w2; j++) t[j] = IP ? fmaxf(t[j], t[j + w2]) : fminf(t[j], t[j + w2]);
           if constexpr (TOPK) {
+            // Nothing in the group reaches any lane's window (thr <= kth): no
+            // best-kk update and no admission, the usual case once the rows
+            // have seen a few tiles.
+            if (!__any_sync(0xFFFFFFFFu, collect && t[0] >= thr)) return;
             // Columns above the kk-th best enter the best-kk values. One such
             // column in the group (the usual case once the row has seen a few
             // tiles) is the group's best, t[0]; two or more are read back from
