@@ -236,9 +236,17 @@ __global__ void __launch_bounds__(256) k_seg_rank(const uint32_t* __restrict__ l
     for (uint32_t l = lane; l < k; l += 32) cnt[l] = 0;
     __syncwarp();
   }
+  // The segment's labels for this lane, all loads in flight together.
+  uint32_t lab[kSeg / 32];
+#pragma unroll
+  for (int c = 0; c < kSeg / 32; c++) {
+    const long p = seg * kSeg + c * 32 + lane;
+    lab[c] = p < m ? labels[r0 + p] : 0xFFFFFFFFu;
+  }
+#pragma unroll
   for (int c = 0; c < kSeg; c += 32) {
     long p = seg * kSeg + c + lane;
-    uint32_t l = p < m ? labels[r0 + p] : 0xFFFFFFFFu;
+    uint32_t l = lab[c / 32];
     bool valid = l < k;
     if (p < m && !valid) atomicOr(status, ST_BAD_LABEL);
     uint32_t key = valid ? l : 0xFFFFFFFFu;
