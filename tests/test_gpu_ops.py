@@ -129,3 +129,27 @@ def test_norms_and_normalize_bit_equal(engine, n, d):
     ub = engine.zeros_f32(rows * d)
     engine.normalize_rows(mb, rows, d, ub)
     assert np.array_equal(bits(ub.read()), bits(oracle.normalize_rows(m.ravel(), d)))
+
+
+def test_host_copies_large_pageable_and_pinned(engine):
+    """Uploads, writes and reads of host arrays from 1 MB up (the staged path
+    for pageable memory: two pinned buffers of 32 MB, several chunks, odd
+    offsets and lengths) and of pinned arrays return the bytes unchanged."""
+    import torch
+
+    rng = np.random.default_rng(12)
+    n = 70 * 1024 * 1024 // 4 + 13  # 70 MB and a ragged tail: three staging chunks
+    v = rng.standard_normal(n).astype(np.float32)
+    b = engine.upload_f32(v)
+    assert np.array_equal(b.read().view(np.uint32), v.view(np.uint32))
+    lo, hi = 1_000_003, n - 777
+    assert np.array_equal(b.read(lo, hi).view(np.uint32), v[lo:hi].view(np.uint32))
+    w = rng.standard_normal(9_000_001).astype(np.float32)
+    b.write(123_457, w)
+    v[123_457:123_457 + w.size] = w
+    assert np.array_equal(b.read().view(np.uint32), v.view(np.uint32))
+    pv = torch.from_numpy(v.copy()).pin_memory()
+    b2 = engine.upload_f32(pv.numpy())
+    assert np.array_equal(b2.read().view(np.uint32), v.view(np.uint32))
+    b.free()
+    b2.free()
