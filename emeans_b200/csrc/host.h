@@ -57,7 +57,10 @@ class Mt19937 {
   // permutation(n) (rng.rs:95-102).
   // The same draws as swapping p[i] with p[interval(i)] for i = n-1 .. 1,
   // written without the rejection branch: each output either lands (swap,
-  // next i) or is rejected (a swap of p[i] with itself, same i).
+  // next i) or is rejected (a swap of p[i] with itself, same i). The mask
+  // only changes when i drops below a power of two, so it is computed once
+  // per such range, which leaves a compare and a subtract between one draw's
+  // i and the next.
   std::vector<uint32_t> permutation(size_t n) {
     std::vector<uint32_t> p(n);
     permutation_into(p.data(), n);
@@ -69,14 +72,18 @@ class Mt19937 {
       for (size_t i = n; i-- > 1;) std::swap(a[i], a[(size_t)interval(i)]);
       return;
     }
-    for (uint32_t i = n ? (uint32_t)(n - 1) : 0u; i > 0;) {
-      const uint32_t v = u32() & (0xffffffffu >> __builtin_clz(i));
-      const uint32_t take = v <= i;
-      const uint32_t j = take ? v : i;
-      const uint32_t t = a[i];
-      a[i] = a[j];
-      a[j] = t;
-      i -= take;
+    uint32_t i = n ? (uint32_t)(n - 1) : 0u;
+    while (i > 0) {
+      const uint32_t mask = 0xffffffffu >> __builtin_clz(i);
+      for (const uint32_t low = mask >> 1; i > low;) {
+        const uint32_t v = u32() & mask;
+        const uint32_t take = v <= i;
+        const uint32_t j = take ? v : i;
+        const uint32_t t = a[i];
+        a[i] = a[j];
+        a[j] = t;
+        i -= take;
+      }
     }
   }
 
