@@ -1,0 +1,179 @@
+"""libemeans.so, the reference's C FFI for assign (include/emeans.h) over the
+B200 engine: the reference's symbols, status codes and error rules
+(crates/emeans-ffi/src/lib.rs:124-219, 387-408, 784-825), and on a GPU its
+results against the oracle.
+
+The CPU tests call only paths that fail before any device work (or, with no
+GPU, the engine's own no-device error)."""
+import ctypes as C
+import json
+import os
+import pathlib
+import re
+
+import numpy as np
+import pytest
+
+import emeans_b200
+from tests.conftest import has_gpu
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "emeans.h"
+OK, INVALID, ERROR = 0, 1, 2
+F32, U32 = 0, 1
+
+
+class Array(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("len", C.c_size_t), ("dtype", C.c_int32)]
+
+
+@pytest.fixture(scope="module")
+def ffi():
+    emeans_b200.load()  # builds nothing; fails loudly if the engine library is missing
+    path = os.path.join(os.path.dirname(emeans_b200.__file__), "libemeans.so")
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: run emeans_b200.build.build()")
+    lib = C.CDLL(path)
+    lib.emeans_abi_version.restype = C.c_uint32
+    lib.emeans_version.restype = C.c_char_p
+    lib.emeans_last_error.restype = C.c_char_p
+    lib.emeans_result_json.restype = C.c_char_p
+    lib.emeans_result_json.argtypes = [C.c_void_p]
+    lib.emeans_result_free.argtypes = [C.c_void_p]
+    lib.emeans_string_free.argtypes = [C.c_void_p]
+    lib.emeans_backends.argtypes = [C.POINTER(C.c_void_p)]
+    lib.emeans_assign.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
+                                  C.c_char_p, C.c_char_p, C.POINTER(C.c_void_p)]
+    lib.emeans_result_array.argtypes = [C.c_void_p, C.c_char_p, C.POINTER(Array)]
+    return lib
+
+
+def declared():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(emeans_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_exports_every_declared_symbol(ffi):
+    names = declared()
+    assert "emeans_assign" in names and "emeans_result_array" in names
+    assert [n for n in names if not hasattr(ffi, n)] == []
+
+
+def test_version_and_abi(ffi):
+    assert ffi.emeans_abi_version() == 1
+    assert re.fullmatch(rb"\d+\.\d+\.\d+", ffi.emeans_version())
+
+
+def assign(ffi, x, c, d, metric=b"l2", backend=None, n=None, k=None, xp=None, cp=None):
+    out = C.c_void_p()
+    n = len(x) // d if n is None else n
+    k = len(c) // d if k is None else k
+    xp = x.ctypes.data if xp is None else xp
+    cp = c.ctypes.data if cp is None else cp
+    rc = ffi.emeans_assign(xp, n, d, cp, k, metric, backend, C.byref(out))
+    return rc, out
+
+
+def test_argument_errors_are_invalid_argument(ffi):
+    x = np.zeros(64, np.float32)
+    c = np.zeros(16, np.float32)
+    assert ffi.emeans_assign(x.ctypes.data, 4, 16, c.ctypes.data, 1, b"l2", None, None) == INVALID
+    assert b"out_result is NULL" in ffi.emeans_last_error()
+    rc, _ = assign(ffi, x, c, 16, xp=0)
+    assert rc == INVALID and b"data is NULL" in ffi.emeans_last_error()
+    rc, _ = assign(ffi, x, c, 16, cp=0)
+    assert rc == INVALID and b"centroids is NULL" in ffi.emeans_last_error()
+    rc, _ = assign(ffi, x, c, 16, xp=x.ctypes.data + 2)
+    assert rc == INVALID and b"not aligned" in ffi.emeans_last_error()
+    rc, _ = assign(ffi, x, c, 16, n=2**62)
+    assert rc == INVALID and b"overflows" in ffi.emeans_last_error()
+    rc, _ = assign(ffi, x, c, 16, metric=None)
+    assert rc == INVALID and b"metric is NULL" in ffi.emeans_last_error()
+
+
+def test_shape_metric_and_backend_errors(ffi):
+    x = np.zeros(64, np.float32)
+    c = np.zeros(16, np.float32)
+    rc, _ = assign(ffi, x, c, 0, n=4, k=1)
+    assert rc == ERROR and b"d must be positive" in ffi.emeans_last_error()
+    rc, _ = assign(ffi, x, c, 16, k=0)
+    assert rc == ERROR and b"centroids is empty" in ffi.emeans_last_error()
+    rc, _ = assign(ffi, x, c, 16, metric=b"manhattan")
+    assert rc == ERROR and b"unknown metric" in ffi.emeans_last_error()
+    rc, _ = assign(ffi, x, c, 16, backend=b"cpu")
+    assert rc == ERROR and b"not in this library" in ffi.emeans_last_error()
+    rc, _ = assign(ffi, x, c, 16, backend=b"tpu")
+    assert rc == ERROR and b"unknown backend" in ffi.emeans_last_error()
+
+
+def test_null_handles(ffi):
+    arr = Array()
+    assert ffi.emeans_result_array(None, b"labels", C.byref(arr)) == INVALID
+    assert ffi.emeans_result_json(None) is None
+    ffi.emeans_result_free(None)
+    ffi.emeans_string_free(None)
+
+
+@pytest.mark.skipif(has_gpu(), reason="checks the no-device error path")
+def test_no_device_is_an_error_not_a_fallback(ffi):
+    x = np.ones(64, np.float32)
+    c = np.ones(16, np.float32)
+    rc, out = assign(ffi, x, c, 16)
+    assert rc == ERROR and b"no B200 engine" in ffi.emeans_last_error()
+    assert not out.value
+    s = C.c_void_p()
+    assert ffi.emeans_backends(C.byref(s)) == OK
+    assert ffi.emeans_last_error() is None
+    assert json.loads(C.string_at(s.value)) == []
+    ffi.emeans_string_free(s)
+
+
+def read(ffi, r, name):
+    arr = Array()
+    assert ffi.emeans_result_array(r, name, C.byref(arr)) == OK
+    if arr.len == 0:
+        assert arr.data is None
+        return np.zeros(0), arr.dtype
+    ct = C.c_float if arr.dtype == F32 else C.c_uint32
+    return np.ctypeslib.as_array(C.cast(arr.data, C.POINTER(ct)), (arr.len,)).copy(), arr.dtype
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("metric,code", [(b"l2", 0), (b"inner_product", 1), (b"cosine", 1)])
+def test_assign_matches_oracle(ffi, metric, code):
+    import oracle
+
+    rng = np.random.default_rng(11)
+    n, d, k = 3000, 72, 257
+    x = rng.standard_normal((n, d)).astype(np.float32)
+    c = x[rng.permutation(n)[:k]] * np.float32(1.01)
+    c[5] = c[4]  # a duplicate centroid: ties keep the lower id
+    for backend in (None, b"cuda"):
+        rc, r = assign(ffi, x.ravel(), c.ravel(), d, metric=metric, backend=backend)
+        assert rc == OK, ffi.emeans_last_error()
+        assert ffi.emeans_last_error() is None
+        labels, lt = read(ffi, r, b"labels")
+        scores, st = read(ffi, r, b"scores")
+        assert (lt, st) == (U32, F32)
+        assert json.loads(ffi.emeans_result_json(r)) == {}
+        arr = Array()
+        assert ffi.emeans_result_array(r, b"centroids", C.byref(arr)) == ERROR
+        assert b"has: labels, scores" in ffi.emeans_last_error()
+        ffi.emeans_result_free(r)
+        wl, ws = oracle.top1(x.ravel(), d, c.ravel(), code)
+        assert np.array_equal(labels, wl)
+        assert np.array_equal(scores.astype(np.float32).view(np.uint32), ws.view(np.uint32))
+
+
+@pytest.mark.gpu
+def test_assign_empty_and_backends(ffi):
+    c = np.ones(32, np.float32)
+    out = C.c_void_p()
+    assert ffi.emeans_assign(None, 0, 16, c.ctypes.data, 2, b"l2", None, C.byref(out)) == OK
+    labels, _ = read(ffi, out, b"labels")
+    assert labels.size == 0
+    ffi.emeans_result_free(out)
+    s = C.c_void_p()
+    assert ffi.emeans_backends(C.byref(s)) == OK
+    assert json.loads(C.string_at(s.value)) == ["cuda"]
+    ffi.emeans_string_free(s)
