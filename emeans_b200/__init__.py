@@ -42,6 +42,13 @@ GPU_KMAX = 16
 _lib = None
 
 
+class _Internal(C.Structure):
+    """eb_internal (include/emeans_b200.h)."""
+    _fields_ = [("k_eff", C.c_uint64), ("silhouette", C.c_double),
+                ("calinski_harabasz", C.c_double), ("davies_bouldin", C.c_double),
+                ("objective", C.c_double)]
+
+
 class EngineError(RuntimeError):
     """A non-OK status from the engine; ``code`` is the EB_* status."""
 
@@ -114,6 +121,7 @@ def load():
         "eb_bind": (I, [P, P, S, S, C.POINTER(P)]),
         "eb_top1": (I, [P, P, S, P, S, S, P, P, S, I, P, P]),
         "eb_topk": (I, [P, P, S, P, S, S, S, I, P, P]),
+        "eb_internal_scores": (I, [P, P, S, S, P, S, P, P]),
         "eb_scatter_add": (I, [P, P, S, P, S, S, P, S, P, P, P]),
         "eb_row_norms": (I, [P, P, S, S, P]),
         "eb_normalize_rows": (I, [P, P, S, S, P]),
@@ -338,6 +346,24 @@ class Engine:
         _check(load().eb_topk(self.h, _ptr(q), m, _ptr(x), n, d, kk, int(exclude_self),
                               _ptr(ids), _ptr(sims)))
         return ids, sims
+
+    def internal_scores(self, x, d: int, labels, k: int) -> dict:
+        """``metrics::internal_scores`` (crates/emeans-cluster/src/metrics.rs:115-274)
+        on the device: silhouette, Calinski-Harabasz, Davies-Bouldin, objective,
+        k_eff and the cluster sizes of ``labels`` (values < k) on unit rows x."""
+        xa, la = _f32(x).ravel(), _u32(np.asarray(labels, dtype=np.uint32).ravel())
+        n = la.size
+        if xa.size != n * d:
+            raise ValueError("x must be n x d with one label per row")
+        out = _Internal()
+        sizes = np.zeros(k, np.uint64)
+        _check(load().eb_internal_scores(self.h, _ptr(xa) if xa.size else None, n, d,
+                                         _ptr(la) if n else None, k, C.byref(out),
+                                         _ptr(sizes) if k else None))
+        return {"k_eff": int(out.k_eff), "silhouette": out.silhouette,
+                "calinski_harabasz": out.calinski_harabasz,
+                "davies_bouldin": out.davies_bouldin, "objective": out.objective,
+                "sizes": sizes}
 
     def topk_group(self, queries, shard, shard_offset: int, n_total: int, d: int, kk: int,
                    exclude_self: bool = False):

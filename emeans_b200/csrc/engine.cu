@@ -461,6 +461,25 @@ int eb_topk(eb_engine* e, const float* queries, size_t m, const float* data, siz
   });
 }
 
+int eb_internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* labels,
+                       size_t k, eb_internal* out, uint64_t* sizes) {
+  return guard([&] {
+    need(e, "engine");
+    need(out, "out");
+    ensure(d > 0, "x must be n x d");  // metrics.rs:116
+    ensure(k <= 0x7FFFFFFFull, "k too large");
+    if (n > 0) {
+      need(x, "x");
+      need(labels, "labels");
+    }
+    uint32_t bad = 0;
+    for (size_t i = 0; i < n; i++) bad |= (uint32_t)(labels[i] >= k);
+    ensure(bad == 0, "label out of range");  // metrics.rs:119-122
+    DeviceGuard g(e);
+    eb::internal_scores(e, x, n, d, labels, k, out, sizes);
+  });
+}
+
 int eb_topk_group(eb_engine* e, const float* queries, size_t m, const float* shard,
                   size_t n_shard, size_t shard_offset, size_t n_total, size_t d, size_t kk,
                   int exclude_self, uint32_t* ids, float* sims) {

@@ -226,6 +226,15 @@ void split(eb_engine* e, float* pos, float* usage, const uint32_t* d_pairs, size
 void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids, size_t r0,
                  size_t r1, const uint32_t* labels, size_t k, float* sums, uint32_t* counts,
                  float* acc);
+// Stable counting sort of the selected positions r0..r1 by label: counts[l]
+// (device), start[0..k] (exclusive prefix, engine scratch) and order[start[l]
+// ..] = the data rows of label l in selection order (engine scratch).
+void label_order(eb_engine* e, const uint32_t* ids, size_t r0, size_t r1, size_t n,
+                 const uint32_t* labels, size_t k, uint32_t* counts, const uint32_t** order,
+                 const uint32_t** start);
+// ---- metrics.cu: internal quality scores of a labelling
+void internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* labels,
+                     size_t k, eb_internal* out, uint64_t* sizes);
 // cnt[l] = occurrences of label l in labels[0 .. m).
 void label_counts(eb_engine* e, const uint32_t* labels, size_t m, size_t k, uint32_t* cnt);
 // out = sums / count per centroid, pos where the count is 0 (closing means

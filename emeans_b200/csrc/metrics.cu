@@ -1,0 +1,437 @@
+// Internal quality scores of a labelling (crates/emeans-cluster/src/metrics.rs:
+// 115-274) on the device: cosine silhouette, Calinski-Harabasz,
+// Davies-Bouldin and the spherical objective of unit rows.
+//
+// The reference forms the cluster sums in f64 in row order, takes one n x k_eff
+// product of the rows with the f32-rounded sums (gemm_nt, crates/emeans-core/
+// src/assign.rs:813-825, in row blocks) and scores every row from its row of
+// that product. Here:
+//  - k_sum64: the f64 sums, one thread per (cluster, column), the cluster's
+//    rows in row order (the stable sort by label of the scatter-add);
+//  - k_cluster_prep: f32 sums, sum of squares and size of the live clusters;
+//  - k_silhouette: the product as FP32 FMA chains in 64 x 64 tiles, and in its
+//    epilogue each row's own-cluster product and the best other cluster's
+//    product / size, so that the n x k_eff matrix never reaches memory; the
+//    row's silhouette, objective term and distance to its cluster mean are
+//    written in f64 with the reference's operation order (no contraction);
+//  - k_db: Davies-Bouldin's worst ratio per cluster over the cluster means.
+// The host adds the per-row terms in row order and forms Calinski-Harabasz as
+// metrics.rs:189-216 does.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <vector>
+
+#include "engine.h"
+
+namespace eb {
+namespace {
+
+unsigned nblocks(size_t n, unsigned per) { return (unsigned)((n + per - 1) / per); }
+
+// sums[j][t] = sum of (double)x[row][t] over the rows of cluster j in row
+// order, from +0 (metrics.rs:127-134).
+constexpr uint32_t kStage = 1024;
+__global__ void __launch_bounds__(128) k_sum64(const float* __restrict__ x, int d,
+                                               const uint32_t* __restrict__ order,
+                                               const uint32_t* __restrict__ start,
+                                               double* __restrict__ sums) {
+  pdl_wait();
+  __shared__ uint32_t ord_s[kStage];
+  const long j = blockIdx.x;
+  const int t = blockIdx.y * blockDim.x + threadIdx.x;
+  const bool active = t < d;
+  const float* xt = x + (active ? t : 0);
+  const uint32_t b = start[j], en = start[j + 1];
+  double s = 0.0;
+  for (uint32_t c0 = b; c0 < en; c0 += kStage) {
+    const uint32_t m = min(en - c0, kStage);
+    __syncthreads();  // the previous chunk's ids are no longer read
+    for (uint32_t u = threadIdx.x; u < m; u += blockDim.x) ord_s[u] = order[c0 + u];
+    __syncthreads();
+    if (!active) continue;
+    uint32_t i = 0;
+    for (; i + 16 <= m; i += 16) {
+      float v[16];
+#pragma unroll
+      for (int q = 0; q < 16; q++) v[q] = __ldg(xt + (long)ord_s[i + q] * d);
+#pragma unroll
+      for (int q = 0; q < 16; q++) s = __dadd_rn(s, (double)v[q]);
+    }
+    for (; i < m; i++) s = __dadd_rn(s, (double)__ldg(xt + (long)ord_s[i] * d));
+  }
+  if (active) sums[j * d + t] = s;
+}
+
+// For live cluster s (label live[s]): c32 = (float)sums, sq = sequential sum
+// of sums^2 (metrics.rs:141-148), size = its count, and its f64 mean
+// sums / size (metrics.rs:218-227). One block per live cluster.
+__global__ void k_cluster_prep(const double* __restrict__ sums, const uint32_t* __restrict__ live,
+                               const uint32_t* __restrict__ counts, int d,
+                               float* __restrict__ c32, double* __restrict__ sq,
+                               double* __restrict__ size, double* __restrict__ mean) {
+  pdl_wait();
+  const long s = blockIdx.x;
+  const long j = live[s];
+  const double nj = (double)counts[j];
+  const double* row = sums + j * d;
+  for (int t = threadIdx.x; t < d; t += blockDim.x) {
+    const double v = row[t];
+    c32[s * d + t] = (float)v;
+    mean[s * d + t] = __ddiv_rn(v, nj);
+  }
+  if (threadIdx.x == 0) {
+    double a = -0.0;
+    for (int t = 0; t < d; t++) a = __dadd_rn(a, __dmul_rn(row[t], row[t]));
+    sq[s] = a;
+    size[s] = nj;
+  }
+}
+
+// Per row i with live cluster o = slot[labels[i]] (metrics.rs:160-185):
+//   g_s  = x_i . c32_s (FP32 FMA chain over the columns)
+//   xx   = sequential sum of x^2 in f64
+//   dist = sqrt(max(xx - 2 g_o / n_o + sq_o / n_o^2, 0))
+//   obj  = 2 - 2 g_o / max(sqrt(sq_o), 1e-30)
+//   sil  = (b - a) / max(a, b) with a = 1 - (g_o - xx) / (n_o - 1) and
+//          b = min over s != o of 1 - g_s / n_s (= 1 - max of g_s / n_s: the
+//          rounding of 1 - q is monotone), 0 when k_eff < 2 or n_o < 2.
+// Tile: 64 rows x 64 clusters per block of 256 threads (4 x 4 per thread),
+// 16 columns per stage; rows in tiles, grid-stride.
+constexpr int BM = 64, BN = 64, BK = 16, NT = 256;
+
+__global__ void __launch_bounds__(NT) k_silhouette(
+    const float* __restrict__ x, long n, int d, const uint32_t* __restrict__ labels,
+    const uint32_t* __restrict__ slot, const float* __restrict__ c32,
+    const double* __restrict__ size, const double* __restrict__ sq, long keff,
+    double* __restrict__ sil, double* __restrict__ obj, double* __restrict__ dist,
+    double* __restrict__ xx_out) {
+  pdl_wait();
+  __shared__ __align__(16) float As[BK][BM + 4];
+  __shared__ __align__(16) float Bs[BK][BN + 4];
+  __shared__ int own_of[BM];
+
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int lr = tid >> 2, lc = (tid & 3) * 4;
+  const bool vec = (d & 3) == 0;
+
+  for (long tile = blockIdx.x; tile * BM < n; tile += gridDim.x) {
+    const long b0 = tile * BM;
+    const long nrows = min((long)BM, n - b0);
+    if (tid < BM) own_of[tid] = tid < nrows ? (int)slot[labels[b0 + tid]] : 0;
+    __syncthreads();
+    const float* arow = x + (b0 + min((long)lr, nrows - 1)) * (long)d;
+    const bool a_live = lr < nrows;
+
+    int own[4];
+    double vmax[4], xxr[4];
+    float dot[4];
+    bool have[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      own[i] = own_of[ty * 4 + i];
+      vmax[i] = -INFINITY;
+      xxr[i] = -0.0;
+      dot[i] = 0.0f;
+      have[i] = false;
+    }
+
+    for (long n0 = 0; n0 < keff; n0 += BN) {
+      const long cj = n0 + lr;
+      const bool b_live = cj < keff;
+      const float* brow = c32 + (b_live ? cj : 0) * (long)d;
+      float acc[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+
+      for (int k0 = 0; k0 < d; k0 += BK) {
+        float av[4], bv[4];
+        if (vec && k0 + lc + 4 <= d) {
+          const float4 a4 = a_live ? __ldg(reinterpret_cast<const float4*>(arow + k0 + lc))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 b4 = b_live ? __ldg(reinterpret_cast<const float4*>(brow + k0 + lc))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+          av[0] = a4.x; av[1] = a4.y; av[2] = a4.z; av[3] = a4.w;
+          bv[0] = b4.x; bv[1] = b4.y; bv[2] = b4.z; bv[3] = b4.w;
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const int t = k0 + lc + q;
+            av[q] = (a_live && t < d) ? __ldg(arow + t) : 0.0f;
+            bv[q] = (b_live && t < d) ? __ldg(brow + t) : 0.0f;
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          As[lc + q][lr] = av[q];
+          Bs[lc + q][lr] = bv[q];
+        }
+        __syncthreads();
+        const int kmax = min(BK, d - k0);
+        if (n0 == 0 && tx == 0) {
+          // The rows' sums of squares, once per tile, in column order.
+          for (int kk = 0; kk < kmax; kk++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              const double v = (double)As[kk][ty * 4 + i];
+              xxr[i] = __dadd_rn(xxr[i], __dmul_rn(v, v));
+            }
+        }
+        if (kmax == BK) {
+#pragma unroll
+          for (int kk = 0; kk < BK; kk++) {
+            const float4 a4 = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+            const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+            const float a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+              for (int j = 0; j < 4; j++) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+          }
+        } else {
+          for (int kk = 0; kk < kmax; kk++) {
+            const float4 a4 = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+            const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+            const float a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+              for (int j = 0; j < 4; j++) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+          }
+        }
+        __syncthreads();
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const long col = n0 + tx * 4 + j;
+        if (col >= keff) break;
+        const double nc = __ldg(size + col);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          if (col == own[i]) {
+            dot[i] = acc[i][j];
+            have[i] = true;
+          } else {
+            vmax[i] = fmax(vmax[i], __ddiv_rn((double)acc[i][j], nc));
+          }
+        }
+      }
+    }
+
+    // Merge the 16 threads of each row group (a half-warp).
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+#pragma unroll
+      for (int off = 8; off >= 1; off >>= 1) {
+        const double ov = __shfl_xor_sync(0xFFFFFFFFu, vmax[i], off);
+        const float od = __shfl_xor_sync(0xFFFFFFFFu, dot[i], off);
+        const int oh = __shfl_xor_sync(0xFFFFFFFFu, (int)have[i], off);
+        vmax[i] = fmax(vmax[i], ov);
+        if (!have[i] && oh) {
+          dot[i] = od;
+          have[i] = true;
+        }
+      }
+    }
+    if (tx == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int r = ty * 4 + i;
+        if (r >= nrows) continue;
+        const long row = b0 + r;
+        const int o = own[i];
+        const double na = size[o], sqo = sq[o];
+        const double g = (double)dot[i], xv = xxr[i];
+        const double t1 = __ddiv_rn(__dmul_rn(2.0, g), na);
+        const double t2 = __ddiv_rn(sqo, __dmul_rn(na, na));
+        dist[row] = __dsqrt_rn(fmax(__dadd_rn(__dsub_rn(xv, t1), t2), 0.0));
+        const double cosc = __ddiv_rn(g, fmax(__dsqrt_rn(sqo), 1e-30));
+        obj[row] = __dsub_rn(2.0, __dmul_rn(2.0, cosc));
+        double sv = 0.0;
+        if (keff >= 2 && na >= 2.0) {
+          const double a = __dsub_rn(1.0, __ddiv_rn(__dsub_rn(g, xv), __dsub_rn(na, 1.0)));
+          const double bb = __dsub_rn(1.0, vmax[i]);
+          const double m = fmax(a, bb);
+          sv = m > 0.0 ? __ddiv_rn(__dsub_rn(bb, a), m) : 0.0;
+        }
+        sil[row] = sv;
+        xx_out[row] = xv;
+      }
+    }
+    __syncthreads();  // own_of is rewritten by the next tile
+  }
+}
+
+// worst[a] = max over b != a of (spread_a + spread_b) / |mean_a - mean_b|
+// (infinite for equal means), folded from 0 (metrics.rs:233-256). One block
+// per cluster a, one thread per b at a time; each distance is a sequential
+// f64 chain over the columns.
+__global__ void __launch_bounds__(256) k_db(const double* __restrict__ mean,
+                                            const double* __restrict__ spread, long keff, int d,
+                                            double* __restrict__ worst) {
+  pdl_wait();
+  __shared__ double red[256];
+  const long a = blockIdx.x;
+  const double* ma = mean + a * d;
+  double w = 0.0;
+  for (long b = threadIdx.x; b < keff; b += blockDim.x) {
+    if (b == a) continue;
+    const double* mb = mean + b * d;
+    double s = -0.0;
+    for (int t = 0; t < d; t++) {
+      const double df = __dsub_rn(__ldg(ma + t), __ldg(mb + t));
+      s = __dadd_rn(s, __dmul_rn(df, df));
+    }
+    const double m = __dsqrt_rn(s);
+    const double v = m > 0.0 ? __ddiv_rn(__dadd_rn(spread[a], spread[b]), m) : INFINITY;
+    w = fmax(w, v);
+  }
+  red[threadIdx.x] = w;
+  __syncthreads();
+  for (int off = blockDim.x / 2; off > 0; off >>= 1) {
+    if (threadIdx.x < off) red[threadIdx.x] = fmax(red[threadIdx.x], red[threadIdx.x + off]);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) worst[a] = red[0];
+}
+
+// Device memory for one call, released on the engine's stream.
+struct Tmp {
+  eb_engine* e;
+  void* p = nullptr;
+  Tmp(eb_engine* eng, size_t bytes) : e(eng) {
+    EB_CUDA(cudaMallocAsync(&p, std::max<size_t>(bytes, 16), e->stream));
+  }
+  ~Tmp() {
+    if (p) cudaFreeAsync(p, e->stream);
+  }
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(p);
+  }
+};
+
+}  // namespace
+
+void internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* labels,
+                     size_t k, eb_internal* out, uint64_t* sizes) {
+  *out = eb_internal{};
+  if (sizes)
+    for (size_t j = 0; j < k; j++) sizes[j] = 0;
+  if (n == 0) return;  // no clusters: every score 0 (metrics.rs:258-273 with n = 0)
+
+  // Rows on the device: bound data in place, else one copy for this call.
+  const bool reuse = e->bound && e->bound_host == x && e->bound_n == n && e->bound->d == d;
+  std::unique_ptr<Tmp> xcopy;
+  const float* xd;
+  if (reuse) {
+    xd = static_cast<const float*>(e->bound->ptr);
+  } else {
+    xcopy.reset(new Tmp(e, n * d * 4));
+    h2d(e, xcopy->p, x, n * d * 4, e->stream);
+    xd = xcopy->as<float>();
+  }
+  Tmp lab(e, n * 4), cnt(e, k * 4), sums(e, k * d * 8);
+  h2d(e, lab.p, labels, n * 4, e->stream);
+  const uint32_t *order, *start;
+  label_order(e, nullptr, 0, n, n, lab.as<uint32_t>(), k, cnt.as<uint32_t>(), &order, &start);
+  launch_pdl(e, k_sum64, dim3((unsigned)k, nblocks(d, 128)), 128, 0, xd, (int)d, order, start,
+             sums.as<double>());
+  EB_LAUNCH("metrics sums");
+
+  std::vector<uint32_t> counts(k);
+  d2h(e, counts.data(), cnt.p, k * 4, e->stream);
+  sync(e);
+  std::vector<uint32_t> live, slot(k, 0);
+  for (size_t j = 0; j < k; j++) {
+    if (sizes) sizes[j] = counts[j];
+    if (counts[j] > 0) {
+      slot[j] = (uint32_t)live.size();
+      live.push_back((uint32_t)j);
+    }
+  }
+  const size_t keff = live.size();
+  Tmp dlive(e, keff * 4), dslot(e, k * 4), c32(e, keff * d * 4), sq(e, keff * 8),
+      size(e, keff * 8), mean(e, keff * d * 8);
+  h2d(e, dlive.p, live.data(), keff * 4, e->stream);
+  h2d(e, dslot.p, slot.data(), k * 4, e->stream);
+  launch_pdl(e, k_cluster_prep, (unsigned)keff, 128, 0, sums.as<double>(), dlive.as<uint32_t>(),
+             cnt.as<uint32_t>(), (int)d, c32.as<float>(), sq.as<double>(), size.as<double>(),
+             mean.as<double>());
+  EB_LAUNCH("metrics cluster prep");
+
+  Tmp sil(e, n * 8), obj(e, n * 8), dist(e, n * 8), xx(e, n * 8);
+  const unsigned tiles = nblocks(n, BM);
+  const unsigned grid = std::min<unsigned>(tiles, (unsigned)e->num_sms * 8);
+  launch_pdl(e, k_silhouette, grid, NT, 0, xd, (long)n, (int)d, lab.as<uint32_t>(),
+             dslot.as<uint32_t>(), c32.as<float>(), size.as<double>(), sq.as<double>(),
+             (long)keff, sil.as<double>(), obj.as<double>(), dist.as<double>(), xx.as<double>());
+  EB_LAUNCH("metrics silhouette");
+
+  std::vector<double> h_sil(n), h_obj(n), h_dist(n), h_xx(n), h_sums(k * d), h_sq(keff);
+  d2h(e, h_sil.data(), sil.p, n * 8, e->stream);
+  d2h(e, h_obj.data(), obj.p, n * 8, e->stream);
+  d2h(e, h_dist.data(), dist.p, n * 8, e->stream);
+  d2h(e, h_xx.data(), xx.p, n * 8, e->stream);
+  d2h(e, h_sums.data(), sums.p, k * d * 8, e->stream);
+  d2h(e, h_sq.data(), sq.p, keff * 8, e->stream);
+  sync(e);
+
+  // Row-order sums (metrics.rs:178-184).
+  double sil_sum = 0.0, obj_sum = 0.0;
+  std::vector<double> scatter(keff, 0.0);
+  for (size_t i = 0; i < n; i++) {
+    sil_sum += h_sil[i];
+    obj_sum += h_obj[i];
+    scatter[slot[labels[i]]] += h_dist[i];
+  }
+  const double nf = (double)n;
+
+  // Calinski-Harabasz (metrics.rs:189-216).
+  double total_xx = -0.0;
+  for (size_t i = 0; i < n; i++) total_xx += h_xx[i];
+  double wsum = -0.0;
+  for (size_t s = 0; s < keff; s++) wsum += h_sq[s] / (double)counts[live[s]];
+  const double within = total_xx - wsum;
+  std::vector<double> grand(d, 0.0);
+  for (size_t s = 0; s < keff; s++) {
+    const double* row = &h_sums[(size_t)live[s] * d];
+    for (size_t t = 0; t < d; t++) grand[t] += row[t];
+  }
+  double gsq = -0.0;
+  for (size_t t = 0; t < d; t++) gsq += grand[t] * grand[t];
+  const double total = total_xx - gsq / nf;
+  const double between = total - within;
+  double ch = 0.0;
+  if (!(keff < 2 || n <= keff || within <= 0.0))
+    ch = (between / (double)(keff - 1)) / (within / (double)(n - keff));
+
+  // Davies-Bouldin (metrics.rs:217-256).
+  double db = 0.0;
+  if (keff >= 2) {
+    std::vector<double> spread(keff);
+    for (size_t s = 0; s < keff; s++) spread[s] = scatter[s] / (double)counts[live[s]];
+    Tmp dspread(e, keff * 8), dworst(e, keff * 8);
+    h2d(e, dspread.p, spread.data(), keff * 8, e->stream);
+    launch_pdl(e, k_db, (unsigned)keff, 256, 0, mean.as<double>(), dspread.as<double>(),
+               (long)keff, (int)d, dworst.as<double>());
+    EB_LAUNCH("metrics davies-bouldin");
+    std::vector<double> worst(keff);
+    d2h(e, worst.data(), dworst.p, keff * 8, e->stream);
+    sync(e);
+    double acc = -0.0;
+    for (size_t s = 0; s < keff; s++) acc += worst[s];
+    db = acc / (double)keff;
+  }
+
+  out->k_eff = keff;
+  out->silhouette = sil_sum / nf;
+  out->calinski_harabasz = ch;
+  out->davies_bouldin = db;
+  out->objective = obj_sum / nf;
+}
+
+}  // namespace eb

@@ -516,9 +516,9 @@ void split(eb_engine* e, float* pos, float* usage, const uint32_t* d_pairs, size
   EB_LAUNCH("split");
 }
 
-void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids, size_t r0,
-                 size_t r1, const uint32_t* labels, size_t k, float* sums, uint32_t* counts,
-                 float* acc) {
+void label_order(eb_engine* e, const uint32_t* ids, size_t r0, size_t r1, size_t n,
+                 const uint32_t* labels, size_t k, uint32_t* counts, const uint32_t** order_out,
+                 const uint32_t** start_out) {
   size_t m = r1 - r0;
   size_t segs = (m + kSeg - 1) / kSeg;
   if (segs == 0) segs = 1;
@@ -546,6 +546,15 @@ void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_
                                                        e->d_status);
     EB_LAUNCH("scatter place");
   }
+  *order_out = order;
+  *start_out = start;
+}
+
+void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids, size_t r0,
+                 size_t r1, const uint32_t* labels, size_t k, float* sums, uint32_t* counts,
+                 float* acc) {
+  const uint32_t *order, *start;
+  label_order(e, ids, r0, r1, n, labels, k, counts, &order, &start);
   dim3 grid((unsigned)k, blocks_for(d, 128));
   launch_pdl(e, k_seg_sum, grid, 128, 0, x, (int)d, order, start, sums, acc);
   EB_LAUNCH("scatter sum");

@@ -286,6 +286,28 @@ int eb_top1_exact_noalloc(eb_engine* e, const float* x, size_t n, size_t d,
                           const float* cnorm, size_t k, int metric, uint32_t* labels,
                           float* scores);
 
+/* ---------------------------------------------------------------- metrics */
+
+/* metrics::Internal (crates/emeans-cluster/src/metrics.rs:94-112). */
+typedef struct {
+  uint64_t k_eff;           /* non-empty clusters */
+  double silhouette;        /* mean cosine-distance silhouette; 0 when k_eff < 2 */
+  double calinski_harabasz; /* variance ratio on the rows (Euclidean) */
+  double davies_bouldin;    /* Davies-Bouldin index on the rows (Euclidean) */
+  double objective;         /* mean 2 - 2 cos to the normalised cluster sum */
+} eb_internal;
+
+/* metrics::internal_scores (metrics.rs:115-274), the metrics' gemm_nt
+ * (crates/emeans-core/src/assign.rs:813-825) on the device: rows x (n x d
+ * host, unit rows), labels (n host, each < k). Cluster sums in f64 in row
+ * order and every per-row, per-cluster and final formula in the reference's
+ * f64 order; the n x k_eff products are FP32 FMA chains (the reference's
+ * gemm crate adds in its own order, so results agree to rounding, not
+ * bitwise). Rows bound with eb_bind_data (the same host pointer) are used in
+ * place. sizes: k counts out, or NULL. */
+int eb_internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* labels,
+                       size_t k, eb_internal* out, uint64_t* sizes);
+
 #ifdef __cplusplus
 }
 #endif
