@@ -359,6 +359,15 @@ def run_ours(args):
     # reads positions, sums, counts and masses and writes positions and masses.
     upd_bytes = n * d * 4 + n * 4 + k * d * 4 + k * 4 + 3 * k * d * 4 + 4 * k * 4
 
+    # ---- internal scores of the final labels (metrics::internal_scores):
+    # wall time of one call through the host API, after one warm-up call (rows
+    # bound by the training run are read in place).
+    hlab = lab.read()
+    eng.internal_scores(x, d, hlab, k)
+    t0 = time.perf_counter()
+    mres = eng.internal_scores(x, d, hlab, k)
+    met_ms = (time.perf_counter() - t0) * 1e3
+
     if rank == 0:
         peak, peak_src = peaks()
         # The dominant kernel, the tcgen05 screen, timed by CUDA events around
@@ -407,6 +416,13 @@ def run_ours(args):
                        "peak_source": hbm_peak()[1],
                        "bytes_source": "algorithmic: rows + labels read, sums + counts "
                                        "written; EMA 3 k d floats + 4 k"},
+            "metrics": {"op": f"internal_scores (silhouette, Calinski-Harabasz, "
+                              f"Davies-Bouldin, objective) of the {n:,} final labels, "
+                              "wall time through the host API",
+                        "ms": met_ms, "k_eff": mres["k_eff"],
+                        "product_tflops": 2.0 * n * mres["k_eff"] * d / (met_ms * 1e-3) / 1e12,
+                        "silhouette": mres["silhouette"],
+                        "davies_bouldin": mres["davies_bouldin"]},
             "gpu_launches": launches,
             "rank_ms_per_step": rank_ms,
             "screen_stats": stats,
