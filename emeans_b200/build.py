@@ -83,13 +83,14 @@ def build_ffi(verbose: bool = False) -> str:
     """libemeans.so: the reference's C FFI for assign (include/emeans.h), host
     code over libemeans_b200.so, found next to it through the run path."""
     deps = [FFI_SRC, OUT, os.path.join(ROOT, "include", "emeans.h"),
-            os.path.join(ROOT, "include", "emeans_b200.h")]
+            os.path.join(ROOT, "include", "emeans_b200.h"), os.path.join(CSRC, "host.h")]
     if os.path.exists(FFI_OUT) and os.path.getmtime(FFI_OUT) >= max(os.path.getmtime(p) for p in deps):
         return FFI_OUT
     # nvcc drives the host compiler and linker as for libemeans_b200.so (the
     # same C++ runtime); the library makes no CUDA calls of its own.
     cmd = [nvcc(), *ARCH, "-O2", "-std=c++17", "-cudart", "none", "-Xcompiler", "-fPIC", "-shared",
-           "-I" + os.path.join(ROOT, "include"), FFI_SRC, "-o", FFI_OUT, "-L" + HERE,
+           "-Xcompiler", "-ffp-contract=off", "-I" + os.path.join(ROOT, "include"), "-I" + CSRC,
+           FFI_SRC, "-o", FFI_OUT, "-L" + HERE,
            "-lemeans_b200", "-Xlinker", "-rpath,$ORIGIN"]
     if verbose:
         print(" ".join(cmd), flush=True)

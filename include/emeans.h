@@ -1,22 +1,26 @@
 /*
  * emeans.h for libemeans.so built by emeans_b200: the reference's C FFI
  * (crates/emeans-ffi/include/emeans.h, crates/emeans-ffi/src/lib.rs) for its
- * assign call, on the B200 engine.
+ * assign, train and in-memory model calls, on the B200 engine.
  *
  * A C, Go (cgo) or Python (ctypes) program written against the reference's
  * header links this libemeans.so instead and keeps its calls: the names,
  * signatures, status codes, result handles and error rules below are the
- * reference's. Only the subset listed here is provided; the model, hierarchy,
- * dedup and one-shot train calls of the reference header are not in this
- * library (a program that uses them does not link against it).
+ * reference's. Only the subset listed here is provided; model files and bytes
+ * (save, load, to/from bytes), the hierarchy, auto-clustering and dedup calls
+ * of the reference header are not in this library (a program that uses them
+ * does not link against it).
  *
  * Differences, by design:
- *  - `backend` NULL selects this library's one backend, the B200 engine on the
- *    calling thread's current CUDA device (the reference's default is "cpu").
- *    "cuda", "cuda-fused" and "b200" name it too; the reference's other
- *    backend names are EMEANS_ERROR ("not in this library").
- *  - There is no CPU fallback: with no usable GPU, emeans_assign is
- *    EMEANS_ERROR.
+ *  - `backend` NULL (and a config without "backend") selects this library's
+ *    one backend, the B200 engine on device EMEANS_B200_DEVICE (environment,
+ *    default 0); the reference's default is "cpu". "cuda", "cuda-fused" and
+ *    "b200" name it too; the reference's other backend names are
+ *    EMEANS_ERROR ("not in this library").
+ *  - There is no CPU fallback: with no usable GPU, every call that computes
+ *    is EMEANS_ERROR.
+ *  - Result JSON numbers are written with 17 significant digits (the same
+ *    doubles as the reference's shortest form).
  * Results are bit-equal to the reference's CPU assign (`cpu-fused` order:
  * one FMA chain per dot, ties to the lower id).
  */
@@ -43,6 +47,9 @@
 
 /* emeans.h:106-109: named arrays and a JSON object of scalars; caller-owned. */
 typedef struct EmeansResult EmeansResult;
+
+/* emeans.h:101-104: a trained model (its centroids and metric), in memory. */
+typedef struct EmeansModel EmeansModel;
 
 /* emeans.h:114-121: a borrowed view into a result. */
 typedef struct EmeansArray {
@@ -73,6 +80,52 @@ void emeans_string_free(char *s);
  * can run on this machine: ["cuda"] with a usable GPU, [] without.
  * Free *out_json with emeans_string_free. */
 int32_t emeans_backends(char **out_json);
+
+/* emeans.h:144-147 (lib.rs:315-323). The default config of kind "train" as
+ * JSON ("backend": "cuda"); "auto" and "dedup" are EMEANS_ERROR here. Free
+ * *out_json with emeans_string_free. */
+int32_t emeans_default_config(const char *kind, char **out_json);
+
+/* emeans.h:155-179 (lib.rs:361-378, bindings/common/src/lib.rs:189-231).
+ * Trains k centroids on data (n * d floats) with the reference's device loop
+ * (bit-equal to the reference's CPU training with the same config).
+ * config_json: overrides of emeans_default_config("train") or NULL; keys
+ * nepochs, batch_size, alpha0, batch_law, seed, spherical, unused_threshold,
+ * max_points_per_centroid, assignment_chunk_size, capture_assignments,
+ * verbose, exact_objective, backend. Result arrays: "centroids" (EMEANS_F32,
+ * k * d) and, with capture_assignments, "labels" (EMEANS_I32, n; -1 outside
+ * the training subset). Result JSON: k, d, objective, exact_objective, stats
+ * (obj, time, imbalance_factor, nsplit per epoch), backend. */
+int32_t emeans_train(const float *data, size_t n, size_t d, size_t k, const char *config_json,
+                     EmeansResult **out_result);
+
+/* emeans.h:214-225 (lib.rs:457-480). emeans_train that also returns the
+ * model; out_result may be NULL. Free the model with emeans_model_free. */
+int32_t emeans_model_train(const float *data, size_t n, size_t d, size_t k,
+                           const char *config_json, EmeansModel **out_model,
+                           EmeansResult **out_result);
+
+/* emeans.h:227-234 (lib.rs:484-499). The model's nearest centroid for each
+ * row (n * d floats): inner product when spherical, else squared L2. Result
+ * arrays as emeans_assign. */
+int32_t emeans_model_assign(const EmeansModel *m, const float *data, size_t n,
+                            EmeansResult **out_result);
+
+/* emeans.h:236-242 (lib.rs:503-517). Mean squared distance, or mean 2 - 2 cos
+ * when spherical, of the rows to their nearest centroid. */
+int32_t emeans_model_objective(const EmeansModel *m, const float *data, size_t n,
+                               double *out_objective);
+
+/* emeans.h:244-248 (lib.rs:521-534). A view of the k * d centroids, valid
+ * until the model is freed. */
+int32_t emeans_model_centroids(const EmeansModel *m, EmeansArray *out_array);
+
+/* emeans.h:250-252 (lib.rs:539-548). JSON: d, k, metric, spherical, backend,
+ * epochs. Free *out_json with emeans_string_free. */
+int32_t emeans_model_info(const EmeansModel *m, char **out_json);
+
+/* emeans.h:274-275 (lib.rs:620-625). NULL is a no-op. */
+void emeans_model_free(EmeansModel *m);
 
 /* emeans.h:189-196 (lib.rs:387-408, bindings/common/src/lib.rs:327-346).
  * The nearest of k centroids (k * d floats) for every row of data (n * d

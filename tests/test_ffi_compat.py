@@ -45,6 +45,17 @@ def ffi():
     lib.emeans_assign.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
                                   C.c_char_p, C.c_char_p, C.POINTER(C.c_void_p)]
     lib.emeans_result_array.argtypes = [C.c_void_p, C.c_char_p, C.POINTER(Array)]
+    lib.emeans_default_config.argtypes = [C.c_char_p, C.POINTER(C.c_void_p)]
+    lib.emeans_train.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_char_p,
+                                 C.POINTER(C.c_void_p)]
+    lib.emeans_model_train.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
+                                       C.c_char_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]
+    lib.emeans_model_assign.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p)]
+    lib.emeans_model_objective.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t,
+                                           C.POINTER(C.c_double)]
+    lib.emeans_model_centroids.argtypes = [C.c_void_p, C.POINTER(Array)]
+    lib.emeans_model_info.argtypes = [C.c_void_p, C.POINTER(C.c_void_p)]
+    lib.emeans_model_free.argtypes = [C.c_void_p]
     return lib
 
 
@@ -177,3 +188,149 @@ def test_assign_empty_and_backends(ffi):
     assert ffi.emeans_backends(C.byref(s)) == OK
     assert json.loads(C.string_at(s.value)) == ["cuda"]
     ffi.emeans_string_free(s)
+
+
+def take_string(ffi, p):
+    v = C.string_at(p.value).decode()
+    ffi.emeans_string_free(p)
+    return v
+
+
+def test_default_config(ffi):
+    s = C.c_void_p()
+    assert ffi.emeans_default_config(b"train", C.byref(s)) == OK
+    cfg = json.loads(take_string(ffi, s))
+    assert cfg["nepochs"] == 5.0 and cfg["seed"] == 1234 and cfg["batch_law"] == "auto"
+    assert cfg["capture_assignments"] is True and cfg["exact_objective"] is False
+    assert cfg["backend"] == "cuda" and "d" not in cfg and "k" not in cfg
+    assert ffi.emeans_default_config(b"auto", C.byref(s)) == ERROR
+    assert b"not in this library" in ffi.emeans_last_error()
+    assert ffi.emeans_default_config(b"nope", C.byref(s)) == ERROR
+    assert ffi.emeans_default_config(None, C.byref(s)) == INVALID
+
+
+def train_call(ffi, x, n, d, k, cfg):
+    out = C.c_void_p()
+    rc = ffi.emeans_train(x.ctypes.data, n, d, k, cfg, C.byref(out))
+    return rc, out
+
+
+def test_train_config_errors_before_any_device_work(ffi):
+    x = np.zeros(64 * 4, np.float32)
+    cases = [
+        (b"{nope", INVALID, b"not valid JSON"),
+        (b"[1, 2]", ERROR, b"config must be an object"),
+        (b'{"d": 4}', ERROR, b"pass d as an argument"),
+        (b'{"epochs": 3}', ERROR, b"unknown config key \"epochs\" (known: alpha0,"),
+        (b'{"exact_objective": 1}', ERROR, b"exact_objective\" must be true or false"),
+        (b'{"backend": "cpu"}', ERROR, b"not in this library"),
+        (b'{"backend": 3}', ERROR, b"must be a string"),
+        (b'{"seed": -1}', ERROR, b"bad train config"),
+        (b'{"batch_size": 2.5}', ERROR, b"bad train config"),
+        (b'{"batch_law": "fast"}', ERROR, b"bad train config"),
+        (b'{"spherical": "yes"}', ERROR, b"bad train config"),
+    ]
+    for cfg, code, msg in cases:
+        rc, out = train_call(ffi, x, 64, 4, 8, cfg)
+        assert rc == code, (cfg, rc, ffi.emeans_last_error())
+        assert msg in ffi.emeans_last_error(), (cfg, ffi.emeans_last_error())
+        assert not out.value
+    rc, _ = train_call(ffi, x, 64, 0, 8, None)
+    assert rc == ERROR and b"d must be positive" in ffi.emeans_last_error()
+    rc, _ = train_call(ffi, x, 64, 4, 0, None)
+    assert rc == ERROR and b"k must be positive" in ffi.emeans_last_error()
+    rc, _ = train_call(ffi, x, 4, 4, 8, None)
+    assert rc == ERROR and b"need at least k = 8 rows, got 4" in ffi.emeans_last_error()
+    assert ffi.emeans_train(x.ctypes.data, 64, 4, 8, None, None) == INVALID
+    m = C.c_void_p()
+    assert ffi.emeans_model_train(x.ctypes.data, 64, 4, 8, None, None, None) == INVALID
+    assert ffi.emeans_model_assign(None, x.ctypes.data, 1, C.byref(m)) == INVALID
+    assert b"model is NULL" in ffi.emeans_last_error()
+    d_ = C.c_double()
+    assert ffi.emeans_model_objective(None, x.ctypes.data, 1, C.byref(d_)) == INVALID
+    ffi.emeans_model_free(None)
+
+
+def blobs(seed, n, d, k):
+    rng = np.random.default_rng(seed)
+    means = rng.standard_normal((k, d)).astype(np.float32) * 3
+    return (means[rng.integers(0, k, n)] + rng.standard_normal((n, d))).astype(np.float32)
+
+
+def unit(x):
+    return (x / np.linalg.norm(x, axis=1, keepdims=True)).astype(np.float32)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("spherical", [False, True])
+def test_train_matches_oracle(ffi, spherical):
+    import oracle
+
+    n, d, k = 6000, 24, 40
+    x = blobs(3, n, d, k)
+    if spherical:
+        x = unit(x)
+    cfg = {"nepochs": 3.0, "seed": 77, "spherical": spherical, "exact_objective": True}
+    rc, r = train_call(ffi, x, n, d, k, json.dumps(cfg).encode())
+    assert rc == OK, ffi.emeans_last_error()
+    cent, ct = read(ffi, r, b"centroids")
+    arr = Array()
+    assert ffi.emeans_result_array(r, b"labels", C.byref(arr)) == OK and arr.dtype == 2
+    labels = np.ctypeslib.as_array(C.cast(arr.data, C.POINTER(C.c_int32)), (arr.len,)).copy()
+    meta = json.loads(ffi.emeans_result_json(r))
+    ffi.emeans_result_free(r)
+    want = oracle.train(x, d, k, nepochs=3.0, seed=77, spherical=spherical)
+    assert ct == F32
+    assert np.array_equal(cent.astype(np.float32).view(np.uint32), want["centroids"].view(np.uint32))
+    assert np.array_equal(labels, want["labels"])
+    assert meta["k"] == k and meta["d"] == d and meta["backend"] == "b200"
+    assert [s["obj"] for s in meta["stats"]] == want["obj"]
+    assert [s["nsplit"] for s in meta["stats"]] == want["nsplit"]
+    rec = oracle.recipe(n, k, d, 3.0)
+    assert meta["objective"] == want["obj"][-1] / rec["epoch_rows"][-1]
+    _, scores = oracle.top1(x, d, want["centroids"], oracle.IP if spherical else oracle.L2)
+    s64 = scores.astype(np.float64)
+    terms = 2.0 - 2.0 * s64 if spherical else s64
+    assert meta["exact_objective"] == float(np.cumsum(terms)[-1] / n)
+
+
+@pytest.mark.gpu
+def test_model_calls_and_training_subset(ffi):
+    import oracle
+
+    n, d, k = 5000, 16, 20
+    x = blobs(4, n, d, k)
+    cfg = json.dumps({"nepochs": 2.0, "seed": 5, "max_points_per_centroid": 100}).encode()
+    m, r = C.c_void_p(), C.c_void_p()
+    assert ffi.emeans_model_train(x.ctypes.data, n, d, k, cfg, C.byref(m), C.byref(r)) == OK, \
+        ffi.emeans_last_error()
+    # The subset: the first 100 k of an MT19937 permutation (seed ^ 0x9E3779B9), sorted.
+    keep = np.sort(oracle.permutation(5 ^ 0x9E3779B9, n)[:100 * k].astype(np.int64))
+    want = oracle.train(x[keep], d, k, nepochs=2.0, seed=5)
+    arr = Array()
+    assert ffi.emeans_model_centroids(m, C.byref(arr)) == OK and arr.len == k * d
+    cent = np.ctypeslib.as_array(C.cast(arr.data, C.POINTER(C.c_float)), (arr.len,)).copy()
+    assert np.array_equal(cent.view(np.uint32), want["centroids"].view(np.uint32))
+    assert ffi.emeans_result_array(r, b"labels", C.byref(arr)) == OK and arr.len == n
+    labels = np.ctypeslib.as_array(C.cast(arr.data, C.POINTER(C.c_int32)), (n,)).copy()
+    expect = np.full(n, -1, np.int32)
+    expect[keep] = want["labels"]
+    assert np.array_equal(labels, expect)
+    ffi.emeans_result_free(r)
+    s = C.c_void_p()
+    assert ffi.emeans_model_info(m, C.byref(s)) == OK
+    info = json.loads(take_string(ffi, s))
+    assert info == {"d": d, "k": k, "metric": "l2", "spherical": False, "backend": "b200",
+                    "epochs": len(want["obj"])}
+    out = C.c_void_p()
+    assert ffi.emeans_model_assign(m, x.ctypes.data, n, C.byref(out)) == OK
+    got_l, _ = read(ffi, out, b"labels")
+    got_s, _ = read(ffi, out, b"scores")
+    ffi.emeans_result_free(out)
+    wl, ws = oracle.top1(x, d, want["centroids"], oracle.L2)
+    assert np.array_equal(got_l, wl)
+    assert np.array_equal(got_s.astype(np.float32).view(np.uint32), ws.view(np.uint32))
+    obj = C.c_double()
+    assert ffi.emeans_model_objective(m, x.ctypes.data, n, C.byref(obj)) == OK
+    assert obj.value == float(np.cumsum(ws.astype(np.float64))[-1] / n)
+    ffi.emeans_model_free(m)
