@@ -9,7 +9,7 @@
 //  - k_sum64: the f64 sums, one thread per (cluster, column), the cluster's
 //    rows in row order (the stable sort by label of the scatter-add);
 //  - k_cluster_prep: f32 sums, sum of squares and size of the live clusters;
-//  - k_silhouette: the product as FP32 FMA chains in 64 x 64 tiles, and in its
+//  - k_silhouette: the product as FP32 FMA chains in 128 x 128 tiles, and in its
 //    epilogue each row's own-cluster product and the best other cluster's
 //    product / size, so that the n x k_eff matrix never reaches memory; the
 //    row's silhouette, objective term and distance to its cluster mean are
@@ -65,11 +65,12 @@ __global__ void __launch_bounds__(128) k_sum64(const float* __restrict__ x, int 
 
 // For live cluster s (label live[s]): c32 = (float)sums, sq = sequential sum
 // of sums^2 (metrics.rs:141-148), size = its count, and its f64 mean
-// sums / size (metrics.rs:218-227). One block per live cluster.
+// sums / size (metrics.rs:218-227), stored column-major (meanT[t][s]) for
+// k_db. One block per live cluster.
 __global__ void k_cluster_prep(const double* __restrict__ sums, const uint32_t* __restrict__ live,
-                               const uint32_t* __restrict__ counts, int d,
+                               const uint32_t* __restrict__ counts, int d, long keff,
                                float* __restrict__ c32, double* __restrict__ sq,
-                               double* __restrict__ size, double* __restrict__ mean) {
+                               double* __restrict__ size, double* __restrict__ meanT) {
   pdl_wait();
   const long s = blockIdx.x;
   const long j = live[s];
@@ -78,7 +79,7 @@ __global__ void k_cluster_prep(const double* __restrict__ sums, const uint32_t* 
   for (int t = threadIdx.x; t < d; t += blockDim.x) {
     const double v = row[t];
     c32[s * d + t] = (float)v;
-    mean[s * d + t] = __ddiv_rn(v, nj);
+    meanT[(long)t * keff + s] = __ddiv_rn(v, nj);
   }
   if (threadIdx.x == 0) {
     double a = -0.0;
@@ -96,9 +97,13 @@ __global__ void k_cluster_prep(const double* __restrict__ sums, const uint32_t* 
 //   sil  = (b - a) / max(a, b) with a = 1 - (g_o - xx) / (n_o - 1) and
 //          b = min over s != o of 1 - g_s / n_s (= 1 - max of g_s / n_s: the
 //          rounding of 1 - q is monotone), 0 when k_eff < 2 or n_o < 2.
-// Tile: 64 rows x 64 clusters per block of 256 threads (4 x 4 per thread),
-// 16 columns per stage; rows in tiles, grid-stride.
-constexpr int BM = 64, BN = 64, BK = 16, NT = 256;
+// Tile: 128 rows x 128 clusters per block of 256 threads, 8 x 8 per thread
+// (rows ty*4 + {0..3} and 64 + ty*4 + {0..3}, clusters likewise by tx), so
+// that four 16-byte shared-memory reads feed 64 FMAs; 8 columns per stage;
+// rows in tiles, grid-stride.
+constexpr int BM = 128, BN = 128, BK = 8, NT = 256;
+
+__device__ __forceinline__ int half_idx(int base, int q) { return (q < 4 ? 0 : 64) + base + (q & 3); }
 
 __global__ void __launch_bounds__(NT) k_silhouette(
     const float* __restrict__ x, long n, int d, const uint32_t* __restrict__ labels,
@@ -113,7 +118,7 @@ __global__ void __launch_bounds__(NT) k_silhouette(
 
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
-  const int lr = tid >> 2, lc = (tid & 3) * 4;
+  const int lr = tid >> 1, lc = (tid & 1) * 4;  // loader: row (cluster) lr, columns lc..lc+3
   const bool vec = (d & 3) == 0;
 
   for (long tile = blockIdx.x; tile * BM < n; tile += gridDim.x) {
@@ -124,13 +129,13 @@ __global__ void __launch_bounds__(NT) k_silhouette(
     const float* arow = x + (b0 + min((long)lr, nrows - 1)) * (long)d;
     const bool a_live = lr < nrows;
 
-    int own[4];
-    double vmax[4], xxr[4];
-    float dot[4];
-    bool have[4];
+    int own[8];
+    double vmax[8], xxr[8];
+    float dot[8];
+    bool have[8];
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      own[i] = own_of[ty * 4 + i];
+    for (int i = 0; i < 8; i++) {
+      own[i] = own_of[half_idx(ty * 4, i)];
       vmax[i] = -INFINITY;
       xxr[i] = -0.0;
       dot[i] = 0.0f;
@@ -141,11 +146,11 @@ __global__ void __launch_bounds__(NT) k_silhouette(
       const long cj = n0 + lr;
       const bool b_live = cj < keff;
       const float* brow = c32 + (b_live ? cj : 0) * (long)d;
-      float acc[4][4];
+      float acc[8][8];
 #pragma unroll
-      for (int i = 0; i < 4; i++)
+      for (int i = 0; i < 8; i++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
 
       for (int k0 = 0; k0 < d; k0 += BK) {
         float av[4], bv[4];
@@ -175,42 +180,38 @@ __global__ void __launch_bounds__(NT) k_silhouette(
           // The rows' sums of squares, once per tile, in column order.
           for (int kk = 0; kk < kmax; kk++)
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-              const double v = (double)As[kk][ty * 4 + i];
+            for (int i = 0; i < 8; i++) {
+              const double v = (double)As[kk][half_idx(ty * 4, i)];
               xxr[i] = __dadd_rn(xxr[i], __dmul_rn(v, v));
             }
         }
+        auto step = [&](int kk) {
+          const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+          const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][64 + ty * 4]);
+          const float4 b0v = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+          const float4 b1v = *reinterpret_cast<const float4*>(&Bs[kk][64 + tx * 4]);
+          const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+          const float b[8] = {b0v.x, b0v.y, b0v.z, b0v.w, b1v.x, b1v.y, b1v.z, b1v.w};
+#pragma unroll
+          for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+        };
         if (kmax == BK) {
 #pragma unroll
-          for (int kk = 0; kk < BK; kk++) {
-            const float4 a4 = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
-            const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
-            const float a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-              for (int j = 0; j < 4; j++) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
-          }
+          for (int kk = 0; kk < BK; kk++) step(kk);
         } else {
-          for (int kk = 0; kk < kmax; kk++) {
-            const float4 a4 = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
-            const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
-            const float a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-              for (int j = 0; j < 4; j++) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
-          }
+          for (int kk = 0; kk < kmax; kk++) step(kk);
         }
         __syncthreads();
       }
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const long col = n0 + tx * 4 + j;
-        if (col >= keff) break;
+      for (int j = 0; j < 8; j++) {
+        const long col = n0 + half_idx(tx * 4, j);
+        if (col >= keff) continue;
         const double nc = __ldg(size + col);
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
+        for (int i = 0; i < 8; i++) {
           if (col == own[i]) {
             dot[i] = acc[i][j];
             have[i] = true;
@@ -223,7 +224,7 @@ __global__ void __launch_bounds__(NT) k_silhouette(
 
     // Merge the 16 threads of each row group (a half-warp).
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
+    for (int i = 0; i < 8; i++) {
 #pragma unroll
       for (int off = 8; off >= 1; off >>= 1) {
         const double ov = __shfl_xor_sync(0xFFFFFFFFu, vmax[i], off);
@@ -238,8 +239,8 @@ __global__ void __launch_bounds__(NT) k_silhouette(
     }
     if (tx == 0) {
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int r = ty * 4 + i;
+      for (int i = 0; i < 8; i++) {
+        const int r = half_idx(ty * 4, i);
         if (r >= nrows) continue;
         const long row = b0 + r;
         const int o = own[i];
@@ -266,36 +267,57 @@ __global__ void __launch_bounds__(NT) k_silhouette(
 }
 
 // worst[a] = max over b != a of (spread_a + spread_b) / |mean_a - mean_b|
-// (infinite for equal means), folded from 0 (metrics.rs:233-256). One block
-// per cluster a, one thread per b at a time; each distance is a sequential
-// f64 chain over the columns.
-__global__ void __launch_bounds__(256) k_db(const double* __restrict__ mean,
+// (infinite for equal means), folded from 0 (metrics.rs:233-256). Each block
+// takes kDbA clusters a, each thread a cluster b at a time; each distance is
+// a sequential f64 chain over the columns. The means are column-major, so a
+// warp's loads of its 32 b's at one column are one coalesced read, and the
+// kDbA a's share every load of b.
+constexpr int kDbA = 4;
+__global__ void __launch_bounds__(256) k_db(const double* __restrict__ meanT,
                                             const double* __restrict__ spread, long keff, int d,
                                             double* __restrict__ worst) {
   pdl_wait();
-  __shared__ double red[256];
-  const long a = blockIdx.x;
-  const double* ma = mean + a * d;
-  double w = 0.0;
+  __shared__ double red[kDbA][256];
+  const long a0 = (long)blockIdx.x * kDbA;
+  double w[kDbA];
+#pragma unroll
+  for (int q = 0; q < kDbA; q++) w[q] = 0.0;
   for (long b = threadIdx.x; b < keff; b += blockDim.x) {
-    if (b == a) continue;
-    const double* mb = mean + b * d;
-    double s = -0.0;
+    double s[kDbA];
+#pragma unroll
+    for (int q = 0; q < kDbA; q++) s[q] = -0.0;
+#pragma unroll 4
     for (int t = 0; t < d; t++) {
-      const double df = __dsub_rn(__ldg(ma + t), __ldg(mb + t));
-      s = __dadd_rn(s, __dmul_rn(df, df));
+      const double* col = meanT + (long)t * keff;
+      const double mb = __ldg(col + b);
+#pragma unroll
+      for (int q = 0; q < kDbA; q++) {
+        const long a = min(a0 + q, keff - 1);
+        const double df = __dsub_rn(__ldg(col + a), mb);
+        s[q] = __dadd_rn(s[q], __dmul_rn(df, df));
+      }
     }
-    const double m = __dsqrt_rn(s);
-    const double v = m > 0.0 ? __ddiv_rn(__dadd_rn(spread[a], spread[b]), m) : INFINITY;
-    w = fmax(w, v);
+    const double sb = spread[b];
+#pragma unroll
+    for (int q = 0; q < kDbA; q++) {
+      const long a = a0 + q;
+      if (a >= keff || b == a) continue;
+      const double m = __dsqrt_rn(s[q]);
+      const double v = m > 0.0 ? __ddiv_rn(__dadd_rn(spread[a], sb), m) : INFINITY;
+      w[q] = fmax(w[q], v);
+    }
   }
-  red[threadIdx.x] = w;
+#pragma unroll
+  for (int q = 0; q < kDbA; q++) red[q][threadIdx.x] = w[q];
   __syncthreads();
   for (int off = blockDim.x / 2; off > 0; off >>= 1) {
-    if (threadIdx.x < off) red[threadIdx.x] = fmax(red[threadIdx.x], red[threadIdx.x + off]);
+    if (threadIdx.x < off)
+#pragma unroll
+      for (int q = 0; q < kDbA; q++)
+        red[q][threadIdx.x] = fmax(red[q][threadIdx.x], red[q][threadIdx.x + off]);
     __syncthreads();
   }
-  if (threadIdx.x == 0) worst[a] = red[0];
+  if (threadIdx.x < kDbA && a0 + threadIdx.x < keff) worst[a0 + threadIdx.x] = red[threadIdx.x][0];
 }
 
 // Device memory for one call, released on the engine's stream.
@@ -359,13 +381,13 @@ void internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uin
   h2d(e, dlive.p, live.data(), keff * 4, e->stream);
   h2d(e, dslot.p, slot.data(), k * 4, e->stream);
   launch_pdl(e, k_cluster_prep, (unsigned)keff, 128, 0, sums.as<double>(), dlive.as<uint32_t>(),
-             cnt.as<uint32_t>(), (int)d, c32.as<float>(), sq.as<double>(), size.as<double>(),
-             mean.as<double>());
+             cnt.as<uint32_t>(), (int)d, (long)keff, c32.as<float>(), sq.as<double>(),
+             size.as<double>(), mean.as<double>());
   EB_LAUNCH("metrics cluster prep");
 
   Tmp sil(e, n * 8), obj(e, n * 8), dist(e, n * 8), xx(e, n * 8);
   const unsigned tiles = nblocks(n, BM);
-  const unsigned grid = std::min<unsigned>(tiles, (unsigned)e->num_sms * 8);
+  const unsigned grid = std::min<unsigned>(tiles, (unsigned)e->num_sms * 4);
   launch_pdl(e, k_silhouette, grid, NT, 0, xd, (long)n, (int)d, lab.as<uint32_t>(),
              dslot.as<uint32_t>(), c32.as<float>(), size.as<double>(), sq.as<double>(),
              (long)keff, sil.as<double>(), obj.as<double>(), dist.as<double>(), xx.as<double>());
@@ -416,7 +438,7 @@ void internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uin
     for (size_t s = 0; s < keff; s++) spread[s] = scatter[s] / (double)counts[live[s]];
     Tmp dspread(e, keff * 8), dworst(e, keff * 8);
     h2d(e, dspread.p, spread.data(), keff * 8, e->stream);
-    launch_pdl(e, k_db, (unsigned)keff, 256, 0, mean.as<double>(), dspread.as<double>(),
+    launch_pdl(e, k_db, nblocks(keff, kDbA), 256, 0, mean.as<double>(), dspread.as<double>(),
                (long)keff, (int)d, dworst.as<double>());
     EB_LAUNCH("metrics davies-bouldin");
     std::vector<double> worst(keff);
