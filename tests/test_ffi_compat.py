@@ -334,3 +334,49 @@ def test_model_calls_and_training_subset(ffi):
     assert ffi.emeans_model_objective(m, x.ctypes.data, n, C.byref(obj)) == OK
     assert obj.value == float(np.cumsum(ws.astype(np.float64))[-1] / n)
     ffi.emeans_model_free(m)
+
+
+C_PROGRAM = r"""
+#include <stdio.h>
+#include <string.h>
+#include "emeans.h"
+
+int main(void) {
+  if (emeans_abi_version() != EMEANS_ABI_VERSION) return 1;
+  char* cfg = NULL;
+  if (emeans_default_config("train", &cfg) != EMEANS_OK || !strstr(cfg, "\"nepochs\"")) return 2;
+  emeans_string_free(cfg);
+  float rows[8] = {0}, cents[4] = {0};
+  EmeansResult* r = NULL;
+  if (emeans_assign(rows, 2, 4, cents, 1, "hamming", NULL, &r) != EMEANS_ERROR) return 3;
+  if (!emeans_last_error() || !strstr(emeans_last_error(), "unknown metric")) return 4;
+  if (emeans_train(rows, 2, 4, 1, "{\"epochs\": 1}", &r) != EMEANS_ERROR) return 5;
+  EmeansModel* m = NULL;
+  if (emeans_model_train(rows, 2, 4, 1, "not json", &m, NULL) != EMEANS_INVALID_ARGUMENT) return 6;
+  EmeansArray a;
+  if (emeans_model_centroids(NULL, &a) != EMEANS_INVALID_ARGUMENT) return 7;
+  emeans_result_free(NULL);
+  emeans_model_free(NULL);
+  printf("ok %s\n", emeans_version());
+  return 0;
+}
+"""
+
+
+def test_c_program_against_the_header_links_and_runs(tmp_path):
+    """A C11 program written against include/emeans.h compiles, links against
+    libemeans.so and gets the reference's status codes (no device work)."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    libdir = os.path.dirname(emeans_b200.__file__)
+    src, exe = tmp_path / "app.c", tmp_path / "app"
+    src.write_text(C_PROGRAM)
+    subprocess.run([cc, "-std=c11", "-Wall", "-Werror", "-I", str(ROOT / "include"), str(src),
+                    "-o", str(exe), "-L", libdir, "-lemeans", f"-Wl,-rpath,{libdir}"], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, (out.returncode, out.stderr)
+    assert out.stdout.startswith("ok 0.1.0")
