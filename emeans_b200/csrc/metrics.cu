@@ -152,8 +152,9 @@ __global__ void __launch_bounds__(NT) k_silhouette(
 #pragma unroll
         for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
 
-      for (int k0 = 0; k0 < d; k0 += BK) {
-        float av[4], bv[4];
+      // Stage k0's columns lc..lc+3 of the loader's row and cluster (zeros
+      // past d; never used in the chain).
+      auto load = [&](int k0, float* av, float* bv) {
         if (vec && k0 + lc + 4 <= d) {
           const float4 a4 = a_live ? __ldg(reinterpret_cast<const float4*>(arow + k0 + lc))
                                    : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -169,12 +170,19 @@ __global__ void __launch_bounds__(NT) k_silhouette(
             bv[q] = (b_live && t < d) ? __ldg(brow + t) : 0.0f;
           }
         }
+      };
+      float av[4], bv[4];
+      load(0, av, bv);
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-          As[lc + q][lr] = av[q];
-          Bs[lc + q][lr] = bv[q];
-        }
-        __syncthreads();
+      for (int q = 0; q < 4; q++) {
+        As[lc + q][lr] = av[q];
+        Bs[lc + q][lr] = bv[q];
+      }
+      __syncthreads();
+      for (int k0 = 0; k0 < d; k0 += BK) {
+        // The next stage's loads are in flight while this stage is computed.
+        const bool more = k0 + BK < d;
+        if (more) load(k0 + BK, av, bv);
         const int kmax = min(BK, d - k0);
         if (n0 == 0 && tx == 0) {
           // The rows' sums of squares, once per tile, in column order.
@@ -202,6 +210,14 @@ __global__ void __launch_bounds__(NT) k_silhouette(
           for (int kk = 0; kk < BK; kk++) step(kk);
         } else {
           for (int kk = 0; kk < kmax; kk++) step(kk);
+        }
+        __syncthreads();  // every thread is done with this stage
+        if (more) {
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            As[lc + q][lr] = av[q];
+            Bs[lc + q][lr] = bv[q];
+          }
         }
         __syncthreads();
       }
