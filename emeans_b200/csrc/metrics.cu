@@ -336,6 +336,18 @@ __global__ void __launch_bounds__(256) k_db(const double* __restrict__ meanT,
   if (threadIdx.x < kDbA && a0 + threadIdx.x < keff) worst[a0 + threadIdx.x] = red[threadIdx.x][0];
 }
 
+// grand[t] = sum over the live clusters, in label order, of sums[j][t] from
+// +0 (metrics.rs:204-209). One thread per column.
+__global__ void k_grand(const double* __restrict__ sums, const uint32_t* __restrict__ live,
+                        long keff, int d, double* __restrict__ grand) {
+  pdl_wait();
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= d) return;
+  double g = 0.0;
+  for (long s = 0; s < keff; s++) g = __dadd_rn(g, sums[(long)live[s] * d + t]);
+  grand[t] = g;
+}
+
 // Device memory for one call, released on the engine's stream.
 struct Tmp {
   eb_engine* e;
@@ -409,13 +421,24 @@ void internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uin
              (long)keff, sil.as<double>(), obj.as<double>(), dist.as<double>(), xx.as<double>());
   EB_LAUNCH("metrics silhouette");
 
-  std::vector<double> h_sil(n), h_obj(n), h_dist(n), h_xx(n), h_sums(k * d), h_sq(keff);
-  d2h(e, h_sil.data(), sil.p, n * 8, e->stream);
-  d2h(e, h_obj.data(), obj.p, n * 8, e->stream);
-  d2h(e, h_dist.data(), dist.p, n * 8, e->stream);
-  d2h(e, h_xx.data(), xx.p, n * 8, e->stream);
-  d2h(e, h_sums.data(), sums.p, k * d * 8, e->stream);
-  d2h(e, h_sq.data(), sq.p, keff * 8, e->stream);
+  Tmp grand_d(e, d * 8);
+  launch_pdl(e, k_grand, nblocks(d, 128), 128, 0, sums.as<double>(), dlive.as<uint32_t>(),
+             (long)keff, (int)d, grand_d.as<double>());
+  EB_LAUNCH("metrics grand");
+
+  // Read-back into the engine's pinned buffers (one DMA each, no staging).
+  double* h_sil = e->pinned_get<double>("met_sil", n);
+  double* h_obj = e->pinned_get<double>("met_obj", n);
+  double* h_dist = e->pinned_get<double>("met_dist", n);
+  double* h_xx = e->pinned_get<double>("met_xx", n);
+  double* h_grand = e->pinned_get<double>("met_grand", d);
+  double* h_sq = e->pinned_get<double>("met_sq", keff);
+  EB_CUDA(cudaMemcpyAsync(h_sil, sil.p, n * 8, cudaMemcpyDeviceToHost, e->stream));
+  EB_CUDA(cudaMemcpyAsync(h_obj, obj.p, n * 8, cudaMemcpyDeviceToHost, e->stream));
+  EB_CUDA(cudaMemcpyAsync(h_dist, dist.p, n * 8, cudaMemcpyDeviceToHost, e->stream));
+  EB_CUDA(cudaMemcpyAsync(h_xx, xx.p, n * 8, cudaMemcpyDeviceToHost, e->stream));
+  EB_CUDA(cudaMemcpyAsync(h_grand, grand_d.p, d * 8, cudaMemcpyDeviceToHost, e->stream));
+  EB_CUDA(cudaMemcpyAsync(h_sq, sq.p, keff * 8, cudaMemcpyDeviceToHost, e->stream));
   sync(e);
 
   // Row-order sums (metrics.rs:178-184).
@@ -434,13 +457,8 @@ void internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uin
   double wsum = -0.0;
   for (size_t s = 0; s < keff; s++) wsum += h_sq[s] / (double)counts[live[s]];
   const double within = total_xx - wsum;
-  std::vector<double> grand(d, 0.0);
-  for (size_t s = 0; s < keff; s++) {
-    const double* row = &h_sums[(size_t)live[s] * d];
-    for (size_t t = 0; t < d; t++) grand[t] += row[t];
-  }
   double gsq = -0.0;
-  for (size_t t = 0; t < d; t++) gsq += grand[t] * grand[t];
+  for (size_t t = 0; t < d; t++) gsq += h_grand[t] * h_grand[t];
   const double total = total_xx - gsq / nf;
   const double between = total - within;
   double ch = 0.0;
