@@ -103,13 +103,19 @@ int parse_metric(const std::string& m) {
 }
 
 // The reference's backend names (crates/emeans-cluster/src/backend.rs:72-101).
+// "cpu" is the reference's default; on x86_64 it resolves to the fused kernel
+// (CpuKernel::fastest, crates/emeans-core/src/assign.rs:250-260), whose float
+// order (one FMA chain per dot, lower id on ties) this engine reproduces bit
+// for bit, so "cpu" and "cpu-fused" are served here with identical results.
+// The other CPU kernels, Metal and cuda-bf16 add in other orders: refused.
 void check_backend(const std::string& s) {
-  if (s == "cuda" || s == "cuda-fused" || s == "b200") return;
-  static const char* known[] = {"cpu",       "cpu-blocked", "cpu-gemm",    "cpu-accelerate",
-                                "cpu-fused", "metal",       "metal-fused", "cuda-bf16"};
+  if (s == "cuda" || s == "cuda-fused" || s == "b200" || s == "cpu" || s == "cpu-fused") return;
+  static const char* known[] = {"cpu-blocked", "cpu-gemm", "cpu-accelerate", "metal",
+                                "metal-fused", "cuda-bf16"};
   for (const char* k : known)
-    if (s == k) throw Refused("backend \"" + s + "\" is not in this library (it runs: cuda, b200)");
-  throw Refused("unknown backend \"" + s + "\" (this library runs: cuda, b200)");
+    if (s == k)
+      throw Refused("backend \"" + s + "\" is not in this library (it runs: cpu, cpu-fused, cuda, b200)");
+  throw Refused("unknown backend \"" + s + "\" (this library runs: cpu, cpu-fused, cuda, b200)");
 }
 
 // One engine for the process, on device EMEANS_B200_DEVICE (default 0),
@@ -158,6 +164,20 @@ struct Reader {
     }
     return false;
   }
+  // The four hex digits of a \\u escape (p at the u); p ends on the last digit.
+  unsigned hex4() {
+    if (end - p < 5) fail();
+    unsigned v = 0;
+    for (int i = 1; i <= 4; i++) {
+      const char c = p[i];
+      v = v * 16 + (c >= '0' && c <= '9' ? c - '0'
+                    : c >= 'a' && c <= 'f' ? c - 'a' + 10
+                    : c >= 'A' && c <= 'F' ? c - 'A' + 10
+                                           : (fail(), 0));
+    }
+    p += 4;
+    return v;
+  }
   std::string string() {
     if (p >= end || *p != '"') fail();
     p++;
@@ -176,16 +196,17 @@ struct Reader {
           case 'r': out += '\r'; break;
           case 't': out += '\t'; break;
           case 'u': {
-            if (end - p < 5) fail();
-            unsigned v = 0;
-            for (int i = 1; i <= 4; i++) {
-              char c = p[i];
-              v = v * 16 + (c >= '0' && c <= '9' ? c - '0'
-                            : c >= 'a' && c <= 'f' ? c - 'a' + 10
-                            : c >= 'A' && c <= 'F' ? c - 'A' + 10
-                                                   : (fail(), 0));
+            unsigned v = hex4();
+            // A UTF-16 surrogate pair is one code point; a lone surrogate is
+            // not valid JSON text (serde_json refuses it too).
+            if (v >= 0xDC00 && v <= 0xDFFF) fail();
+            if (v >= 0xD800 && v <= 0xDBFF) {
+              if (end - p < 7 || p[1] != '\\' || p[2] != 'u') fail();
+              p += 2;
+              const unsigned lo = hex4();
+              if (lo < 0xDC00 || lo > 0xDFFF) fail();
+              v = 0x10000 + ((v - 0xD800) << 10) + (lo - 0xDC00);
             }
-            p += 4;
             // Config keys and values are ASCII; other code points keep their
             // UTF-8 form only for messages.
             if (v < 0x80) {
@@ -193,8 +214,13 @@ struct Reader {
             } else if (v < 0x800) {
               out += (char)(0xC0 | (v >> 6));
               out += (char)(0x80 | (v & 0x3F));
-            } else {
+            } else if (v < 0x10000) {
               out += (char)(0xE0 | (v >> 12));
+              out += (char)(0x80 | ((v >> 6) & 0x3F));
+              out += (char)(0x80 | (v & 0x3F));
+            } else {
+              out += (char)(0xF0 | (v >> 18));
+              out += (char)(0x80 | ((v >> 12) & 0x3F));
               out += (char)(0x80 | ((v >> 6) & 0x3F));
               out += (char)(0x80 | (v & 0x3F));
             }
@@ -361,7 +387,9 @@ std::string default_train_config() {
 }
 
 uint64_t as_uint(const Json& v, const std::string& key, double max) {
-  if (v.kind != Json::Num || !v.integral || v.num < 0 || v.num > (double)max)
+  // (double)UINT64_MAX rounds up to 2^64, which does not convert: refused.
+  if (v.kind != Json::Num || !v.integral || v.num < 0 || v.num > (double)max ||
+      v.num >= 18446744073709551616.0)
     bad_config(key, "a non-negative integer");
   return (uint64_t)v.num;
 }
@@ -534,7 +562,9 @@ void train_model(const float* data, size_t n, size_t d, size_t k, const char* co
   const float* x = data;
   size_t rows = n;
   if (cfg.mppc_set) {
-    const uint64_t limit = cfg.max_points_per_centroid * k;
+    // A product past 2^64 - 1 keeps every row (the limit is above any n).
+    uint64_t limit = 0;
+    if (__builtin_mul_overflow(cfg.max_points_per_centroid, (uint64_t)k, &limit)) limit = UINT64_MAX;
     if (n > limit) {
       if (cfg.verbose)
         std::fprintf(stderr, "WARNING clustering %zu points to %zu centroids: sampling %llu points\n",

@@ -13,7 +13,7 @@ Writes:
   g_e8.f32, g_s24.f32   the seeded training inputs of the runs
 
 Usage: python tests/golden/make_golden.py [/path/to/reference]
-The reference path defaults to $EMEANS_REFERENCE or /root/reference.
+The reference checkout is the first argument, or $EMEANS_REFERENCE.
 """
 
 from __future__ import annotations
@@ -81,8 +81,10 @@ def tiny(n, d, centers, spherical, seed):
 
 
 def main():
-    ref = pathlib.Path(sys.argv[1] if len(sys.argv) > 1 else
-                       os.environ.get("EMEANS_REFERENCE", "/root/reference"))
+    src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("EMEANS_REFERENCE")
+    if not src:
+        raise SystemExit("usage: make_golden.py <reference checkout> (or set EMEANS_REFERENCE)")
+    ref = pathlib.Path(src)
     sys.modules["faiss"] = faiss_standin()
     sys.path.insert(0, str(ref / "reference"))
     from faiss_e_means import NumpyEmeans  # noqa: E402

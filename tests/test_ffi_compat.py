@@ -111,7 +111,7 @@ def test_shape_metric_and_backend_errors(ffi):
     assert rc == ERROR and b"centroids is empty" in ffi.emeans_last_error()
     rc, _ = assign(ffi, x, c, 16, metric=b"manhattan")
     assert rc == ERROR and b"unknown metric" in ffi.emeans_last_error()
-    rc, _ = assign(ffi, x, c, 16, backend=b"cpu")
+    rc, _ = assign(ffi, x, c, 16, backend=b"cpu-gemm")
     assert rc == ERROR and b"not in this library" in ffi.emeans_last_error()
     rc, _ = assign(ffi, x, c, 16, backend=b"tpu")
     assert rc == ERROR and b"unknown backend" in ffi.emeans_last_error()
@@ -159,7 +159,9 @@ def test_assign_matches_oracle(ffi, metric, code):
     x = rng.standard_normal((n, d)).astype(np.float32)
     c = x[rng.permutation(n)[:k]] * np.float32(1.01)
     c[5] = c[4]  # a duplicate centroid: ties keep the lower id
-    for backend in (None, b"cuda"):
+    # "cpu" (the reference default, the fused kernel on x86_64) and
+    # "cpu-fused" are served by the engine with the same bits.
+    for backend in (None, b"cuda", b"cpu", b"cpu-fused"):
         rc, r = assign(ffi, x.ravel(), c.ravel(), d, metric=metric, backend=backend)
         assert rc == OK, ffi.emeans_last_error()
         assert ffi.emeans_last_error() is None
@@ -223,7 +225,11 @@ def test_train_config_errors_before_any_device_work(ffi):
         (b'{"d": 4}', ERROR, b"pass d as an argument"),
         (b'{"epochs": 3}', ERROR, b"unknown config key \"epochs\" (known: alpha0,"),
         (b'{"exact_objective": 1}', ERROR, b"exact_objective\" must be true or false"),
-        (b'{"backend": "cpu"}', ERROR, b"not in this library"),
+        (b'{"backend": "cpu-accelerate"}', ERROR, b"not in this library"),
+        (b'{"backend": "\\ud800"}', INVALID, b"not valid JSON"),
+        (b'{"backend": "\\udc00x"}', INVALID, b"not valid JSON"),
+        (b'{"backend": "\\ud83d\\u0041"}', INVALID, b"not valid JSON"),
+        (b'{"backend": "\\ud83d\\ude00"}', ERROR, "unknown backend \"\U0001F600\"".encode()),
         (b'{"backend": 3}', ERROR, b"must be a string"),
         (b'{"seed": -1}', ERROR, b"bad train config"),
         (b'{"batch_size": 2.5}', ERROR, b"bad train config"),
@@ -334,6 +340,15 @@ def test_model_calls_and_training_subset(ffi):
     assert ffi.emeans_model_objective(m, x.ctypes.data, n, C.byref(obj)) == OK
     assert obj.value == float(np.cumsum(ws.astype(np.float64))[-1] / n)
     ffi.emeans_model_free(m)
+    # max_points_per_centroid * k past 2^64 - 1: the limit is above any n, so
+    # every row trains (no wrap-around to a small sample).
+    big = json.dumps({"nepochs": 2.0, "seed": 5, "max_points_per_centroid": 2 ** 62}).encode()
+    rc, r = train_call(ffi, x, n, d, k, big)
+    assert rc == OK, ffi.emeans_last_error()
+    cent, _ = read(ffi, r, b"centroids")
+    ffi.emeans_result_free(r)
+    full = oracle.train(x, d, k, nepochs=2.0, seed=5)
+    assert np.array_equal(cent.astype(np.float32).view(np.uint32), full["centroids"].view(np.uint32))
 
 
 C_PROGRAM = r"""
