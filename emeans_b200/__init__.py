@@ -139,6 +139,8 @@ def load():
         "eb_engine_join": (I, [P, I, I, C.c_char_p]),
         "eb_engine_group": (I, [P, C.POINTER(I), C.POINTER(I)]),
         "eb_set_group_shard": (I, [P, I]),
+        "eb_device_allocations": (I, [P, C.POINTER(C.c_uint64)]),
+        "eb_group_allgather": (I, [P, P, S]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -291,6 +293,12 @@ class Engine:
         s = C.c_void_p()
         _check(load().eb_engine_stream(self.h, C.byref(s)))
         return s.value or 0
+
+    def device_allocations(self) -> int:
+        """Device allocations the engine has made since creation."""
+        c = C.c_uint64()
+        _check(load().eb_device_allocations(self.h, C.byref(c)))
+        return c.value
 
     def stats(self) -> dict:
         s = Stats()
@@ -457,9 +465,17 @@ class Engine:
         self.join(rank, world, box[0])
 
     def set_group_shard(self, mode: int):
-        """eb_set_group_shard: 0 auto (split a training batch across the group
-        only when that shortens it), 1 always, 2 never; same on every rank."""
+        """eb_set_group_shard: 0 auto (split a training batch's top-1 across
+        the group only when that shortens it), 1 always, 2 never (all three
+        equal one engine bit for bit); 3 splits the top-1 and the scatter-add
+        and adds the ranks' partial sums in rank order (one all-gather per
+        step; equal to one engine to rounding). Same on every rank."""
         _check(load().eb_set_group_shard(self.h, int(mode)))
+
+    def group_allgather(self, buf: "Buffer", words_per_rank: int):
+        """eb_group_allgather: in-place all-gather of buf's rank shares
+        (words_per_rank 32-bit words each); collective over the group."""
+        _check(load().eb_group_allgather(self.h, buf.h, int(words_per_rank)))
 
     def group(self):
         r, w = C.c_int(), C.c_int()
@@ -534,6 +550,17 @@ def shard_bounds(b: int, end: int, rank: int, world: int):
     lo = min(b + rank * sh, end)
     hi = min(lo + sh, end) if world > 1 else end
     return lo, hi
+
+
+def reduce_layout(batch: int, world: int, k: int, d: int):
+    """The per-rank share of eb_train's exchange buffer in group mode 3 (the
+    split top-1 and scatter-add): (s, s4, k4, share) with s = ceil(batch /
+    world) positions per rank; labels at [0, s4), scores at [s4, 2 s4),
+    partial counts at [2 s4, 2 s4 + k), partial sums (k x d) at
+    [2 s4 + k4, share), all in 32-bit words (s4, k4: s and k rounded up to 4)."""
+    s = (batch + world - 1) // world
+    s4, k4 = (s + 3) // 4 * 4, (k + 3) // 4 * 4
+    return s, s4, k4, 2 * s4 + k4 + k * d
 
 
 class B200Assigner:

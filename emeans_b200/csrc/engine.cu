@@ -89,6 +89,7 @@ eb_buf* new_buf(eb_engine* e, int dtype, size_t len) {
   b->owned = true;
   size_t bytes = std::max<size_t>(len * 4, 16);
   cudaError_t st = cudaMallocAsync(&b->ptr, bytes, e->stream);
+  e->device_allocs++;
   if (st != cudaSuccess) {
     delete b;
     throw Error(EB_ERROR, std::string("device allocation of ") + std::to_string(bytes) +
@@ -245,6 +246,14 @@ int eb_get_stats(eb_engine* e, eb_stats* out) {
     *out = e->stats;
     out->fallback_rows = c[1];
     out->rescored_candidates = c[2];
+  });
+}
+
+int eb_device_allocations(eb_engine* e, uint64_t* count) {
+  return guard([&] {
+    need(e, "engine");
+    need(count, "count");
+    *count = e->device_allocs;
   });
 }
 
@@ -434,6 +443,7 @@ int eb_top1(eb_engine* e, const eb_buf* x, size_t d, const eb_buf* ids, size_t r
       // Bound data: keep its row norms (CPU float order) for every later call.
       float* xn = nullptr;
       EB_CUDA(cudaMallocAsync(&xn, std::max<size_t>(a.n, 1) * 4, e->stream));
+      e->device_allocs++;
       eb::row_norms(e, a.x, a.n, d, xn);
       const_cast<eb_buf*>(x)->xnorm = xn;
       a.xnorm = xn;

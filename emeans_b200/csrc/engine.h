@@ -87,6 +87,9 @@ struct eb_engine {
   const float* bound_host = nullptr;
   size_t bound_n = 0;
   int num_sms = 148;
+  // Device allocations the engine has made since creation (buffers, scratch,
+  // cached copies), for callers that check a call allocated nothing.
+  uint64_t device_allocs = 0;
   // Tensor-core screen for top-1: 0 off, 1 auto (large enough calls), 2 always.
   // EMEANS_B200_SCREEN=0/1/2 sets it at creation; eb_set_screen_mode later.
   int screen_mode = 1;
@@ -97,7 +100,8 @@ struct eb_engine {
   void* comm = nullptr;
   int rank = 0, world = 1;
   // Group training: 0 splits a batch's top-1 across the ranks only when that
-  // shortens it, 1 always, 2 never (eb_set_group_shard).
+  // shortens it, 1 always, 2 never, 3 splits the top-1 and the scatter-add
+  // and sums the ranks' partial sums (eb_set_group_shard).
   int group_shard = 0;
   // Optional CUDA-event timing of the top-1 screen kernel (eb_set_kernel_timing):
   // one (start, end) pair per launch since the last eb_screen_timing read,
@@ -147,6 +151,7 @@ struct eb_engine {
       if (s.p) EB_CUDA(cudaFreeAsync(s.p, stream));
       size_t want = bytes + bytes / 4;
       EB_CUDA(cudaMallocAsync(&s.p, want, stream));
+      device_allocs++;
       s.bytes = want;
       if (zeroed) EB_CUDA(cudaMemsetAsync(s.p, 0, want, stream));
     }
@@ -204,13 +209,22 @@ void set_last_error(const std::string& msg);
 // buf[r * words ..). Release of the engine's communicator.
 void group_allgather(eb_engine* e, uint32_t* buf, size_t words);
 void group_leave(eb_engine* e);
-// Pack this rank's (labels, scores) slice of len <= s entries into
-// stage[rank * 2s ..) and unpack every rank's slice after the exchange into
-// labels / scores at p0 + q s (ops.cu).
-void shard_pack(eb_engine* e, const uint32_t* labels, const float* scores, size_t len, size_t s,
-                uint32_t* stage);
-void shard_unpack(eb_engine* e, const uint32_t* stage, size_t total, size_t s, int world,
-                  uint32_t* labels, float* scores);
+// Pack this rank's (labels, scores) slice of len <= soff entries into
+// stage[rank * stride ..) (labels, then scores soff words later; the words
+// past len zero) and unpack every rank's slice after the exchange into
+// labels / scores at p0 + q s, rank q's slice being positions q s .. (q + 1) s
+// of the batch (ops.cu). stride >= 2 soff words separates the ranks' shares.
+void shard_pack(eb_engine* e, const uint32_t* labels, const float* scores, size_t len,
+                size_t soff, size_t stride, uint32_t* stage);
+void shard_unpack(eb_engine* e, const uint32_t* stage, size_t total, size_t s, size_t soff,
+                  size_t stride, uint32_t* labels, float* scores);
+// The group's partial scatter-adds summed in rank order: every rank's share of
+// stage (stride words apart) holds its counts (k words at cnt_off) and sums
+// (k x d floats at sum_off); sums = ((p_0 + p_1) + p_2) + ..., counts = the
+// total, and acc += sums when acc is given (ops.cu).
+void reduce_partials(eb_engine* e, const uint32_t* stage, size_t stride, int world,
+                     size_t cnt_off, size_t sum_off, size_t k, size_t d, float* sums,
+                     uint32_t* counts, float* acc);
 
 // ---- ops.cu: update ops, bit-equal to the CPU float order
 void row_norms(eb_engine* e, const float* m, size_t rows, size_t d, float* out);
@@ -228,10 +242,11 @@ void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_
                  float* acc);
 // Stable counting sort of the selected positions r0..r1 by label: counts[l]
 // (device), start[0..k] (exclusive prefix, engine scratch) and order[start[l]
-// ..] = the data rows of label l in selection order (engine scratch).
+// ..] = the data rows of label l in selection order (engine scratch); with
+// by_size, the labels by count, largest first (engine scratch).
 void label_order(eb_engine* e, const uint32_t* ids, size_t r0, size_t r1, size_t n,
                  const uint32_t* labels, size_t k, uint32_t* counts, const uint32_t** order,
-                 const uint32_t** start);
+                 const uint32_t** start, const uint32_t** by_size = nullptr);
 // ---- metrics.cu: internal quality scores of a labelling
 void internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* labels,
                      size_t k, eb_internal* out, uint64_t* sizes);

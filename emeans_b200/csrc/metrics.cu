@@ -32,14 +32,17 @@ unsigned nblocks(size_t n, unsigned per) { return (unsigned)((n + per - 1) / per
 // sums[j][t] = sum of (double)x[row][t] over the rows of cluster j in row
 // order, from +0 (metrics.rs:127-134).
 constexpr uint32_t kStage = 1024;
-__global__ void __launch_bounds__(128) k_sum64(const float* __restrict__ x, int d,
+// Block b takes the b / cb-th largest cluster (by_size) and its column block
+// b % cb, so that the longest chains start first.
+__global__ void __launch_bounds__(128) k_sum64(const float* __restrict__ x, int d, int cb,
                                                const uint32_t* __restrict__ order,
                                                const uint32_t* __restrict__ start,
+                                               const uint32_t* __restrict__ by_size,
                                                double* __restrict__ sums) {
   pdl_wait();
   __shared__ uint32_t ord_s[kStage];
-  const long j = blockIdx.x;
-  const int t = blockIdx.y * blockDim.x + threadIdx.x;
+  const long j = by_size[blockIdx.x / cb];
+  const int t = (blockIdx.x % cb) * blockDim.x + threadIdx.x;
   const bool active = t < d;
   const float* xt = x + (active ? t : 0);
   const uint32_t b = start[j], en = start[j + 1];
@@ -354,6 +357,7 @@ struct Tmp {
   void* p = nullptr;
   Tmp(eb_engine* eng, size_t bytes) : e(eng) {
     EB_CUDA(cudaMallocAsync(&p, std::max<size_t>(bytes, 16), e->stream));
+    e->device_allocs++;
   }
   ~Tmp() {
     if (p) cudaFreeAsync(p, e->stream);
@@ -386,9 +390,11 @@ void internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uin
   }
   Tmp lab(e, n * 4), cnt(e, k * 4), sums(e, k * d * 8);
   h2d(e, lab.p, labels, n * 4, e->stream);
-  const uint32_t *order, *start;
-  label_order(e, nullptr, 0, n, n, lab.as<uint32_t>(), k, cnt.as<uint32_t>(), &order, &start);
-  launch_pdl(e, k_sum64, dim3((unsigned)k, nblocks(d, 128)), 128, 0, xd, (int)d, order, start,
+  const uint32_t *order, *start, *by_size;
+  label_order(e, nullptr, 0, n, n, lab.as<uint32_t>(), k, cnt.as<uint32_t>(), &order, &start,
+              &by_size);
+  const unsigned cb = nblocks(d, 128);
+  launch_pdl(e, k_sum64, (unsigned)(k * cb), 128, 0, xd, (int)d, (int)cb, order, start, by_size,
              sums.as<double>());
   EB_LAUNCH("metrics sums");
 

@@ -119,12 +119,37 @@ extern "C" int eb_engine_join(eb_engine* e, int rank, int world, const unsigned 
 }
 
 extern "C" int eb_set_group_shard(eb_engine* e, int mode) {
-  if (!e || mode < 0 || mode > 2) {
-    eb::set_last_error("engine required; mode must be 0, 1 or 2");
+  if (!e || mode < 0 || mode > 3) {
+    eb::set_last_error("engine required; mode must be 0, 1, 2 or 3");
     return EB_INVALID_ARGUMENT;
   }
   e->group_shard = mode;
   return EB_OK;
+}
+
+extern "C" int eb_group_allgather(eb_engine* e, eb_buf* b, size_t words_per_rank) {
+  try {
+    eb::ensure(e != nullptr && b != nullptr, "engine and buffer are required");
+    eb::ensure(b->len / (size_t)e->world >= words_per_rank,
+               "the buffer holds fewer than world x words_per_rank elements");
+    if (e->world > 1 && words_per_rank > 0) {
+      int prev = -1;
+      cudaGetDevice(&prev);
+      if (prev != e->device) EB_CUDA(cudaSetDevice(e->device));
+      try {
+        eb::group_allgather(e, static_cast<uint32_t*>(b->ptr), words_per_rank);
+      } catch (...) {
+        if (prev >= 0 && prev != e->device) cudaSetDevice(prev);
+        throw;
+      }
+      if (prev >= 0 && prev != e->device) cudaSetDevice(prev);
+    }
+    eb::set_last_error("");
+    return EB_OK;
+  } catch (const eb::Error& err) {
+    eb::set_last_error(err.what());
+    return err.code;
+  }
 }
 
 extern "C" int eb_engine_group(eb_engine* e, int* rank, int* world) {

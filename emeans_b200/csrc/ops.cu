@@ -303,11 +303,19 @@ __global__ void __launch_bounds__(256) k_seg_scan(uint32_t* __restrict__ segcnt,
   if (lane == 0) counts[l] = carry;
 }
 
-// Exclusive scan of counts into start[0..k], one block.
-__global__ void k_label_scan(const uint32_t* __restrict__ counts, uint32_t k,
-                             uint32_t* __restrict__ start) {
+// Exclusive scan of counts into start[0..k], one block of 1024 threads; and
+// the labels by count, largest first (ties: lower label first), into
+// by_size[0..k), so that the segment sums start the longest chains in the
+// first wave (a chain is sequential, and the largest one sets the kernel's
+// length). Bitonic sort of (count, ~label) keys in shared memory for k up to
+// kSortMax; larger k keep the label order.
+constexpr uint32_t kSortMax = 4096;
+__global__ void __launch_bounds__(1024) k_label_scan(const uint32_t* __restrict__ counts,
+                                                     uint32_t k, uint32_t* __restrict__ start,
+                                                     uint32_t* __restrict__ by_size) {
   pdl_wait();
   __shared__ uint32_t part[1024];
+  __shared__ unsigned long long keys[kSortMax];
   uint32_t per = (k + blockDim.x - 1) / blockDim.x;
   uint32_t lo = threadIdx.x * per, hi = min(lo + per, k);
   uint32_t s = 0;
@@ -326,6 +334,30 @@ __global__ void k_label_scan(const uint32_t* __restrict__ counts, uint32_t k,
     run += counts[l];
   }
   if (threadIdx.x == blockDim.x - 1) start[k] = part[threadIdx.x];
+  if (k > kSortMax) {
+    for (uint32_t l = threadIdx.x; l < k; l += blockDim.x) by_size[l] = l;
+    return;
+  }
+  uint32_t n2 = 2;
+  while (n2 < k) n2 <<= 1;
+  for (uint32_t l = threadIdx.x; l < n2; l += blockDim.x)
+    keys[l] = l < k ? ((unsigned long long)counts[l] << 32) | (uint32_t)~l : 0ull;
+  __syncthreads();
+  for (uint32_t size = 2; size <= n2; size <<= 1) {
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      for (uint32_t i = threadIdx.x; i < n2 / 2; i += blockDim.x) {
+        const uint32_t a = 2 * i - (i & (stride - 1)), b = a + stride;
+        const bool desc = (a & size) == 0;
+        const unsigned long long ka = keys[a], kb = keys[b];
+        if (desc ? ka < kb : ka > kb) {
+          keys[a] = kb;
+          keys[b] = ka;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (uint32_t l = threadIdx.x; l < k; l += blockDim.x) by_size[l] = ~(uint32_t)keys[l];
 }
 
 // Place every position at its sorted slot; the slot holds the data row id.
@@ -378,22 +410,25 @@ __device__ __forceinline__ float chain_sum(const float* __restrict__ xt, const u
 }
 
 // sums[j][t] = rows of centroid j added in selection order from +0;
-// acc[j][t] += sums[j][t]. One thread per (centroid, column). The block stages
+// acc[j][t] += sums[j][t]. One thread per (centroid, column); block b takes
+// the b / cb-th largest centroid (by_size) and its column block b % cb, so
+// that the longest chains are scheduled first. The block stages
 // its centroid's row ids in shared memory, kSumStage at a time, and each
 // thread keeps the next 32 rows' loads in flight while it adds the current 32
 // in order (the adds of one column form one sequential chain, and the
 // largest centroid's chain sets the kernel's length: measured on C2's full
 // pass, 0.24 ms with 16-row batches, 0.20 ms with 32, 0.21 ms with 64).
 constexpr uint32_t kSumStage = 1024;
-__global__ void __launch_bounds__(128) k_seg_sum(const float* __restrict__ x, int d,
+__global__ void __launch_bounds__(128) k_seg_sum(const float* __restrict__ x, int d, int cb,
                                                  const uint32_t* __restrict__ order,
                                                  const uint32_t* __restrict__ start,
+                                                 const uint32_t* __restrict__ by_size,
                                                  float* __restrict__ sums,
                                                  float* __restrict__ acc) {
   pdl_wait();
   __shared__ uint32_t ord_s[kSumStage];
-  const long j = blockIdx.x;
-  const int t = blockIdx.y * blockDim.x + threadIdx.x;
+  const long j = by_size[blockIdx.x / cb];
+  const int t = (blockIdx.x % cb) * blockDim.x + threadIdx.x;
   const bool active = t < d;
   const float* xt = x + (active ? t : 0);
   const uint32_t b = start[j], e = start[j + 1];
@@ -518,7 +553,7 @@ void split(eb_engine* e, float* pos, float* usage, const uint32_t* d_pairs, size
 
 void label_order(eb_engine* e, const uint32_t* ids, size_t r0, size_t r1, size_t n,
                  const uint32_t* labels, size_t k, uint32_t* counts, const uint32_t** order_out,
-                 const uint32_t** start_out) {
+                 const uint32_t** start_out, const uint32_t** by_size_out) {
   size_t m = r1 - r0;
   size_t segs = (m + kSeg - 1) / kSeg;
   if (segs == 0) segs = 1;
@@ -526,6 +561,7 @@ void label_order(eb_engine* e, const uint32_t* ids, size_t r0, size_t r1, size_t
   uint32_t* rank = e->scratch_get<uint32_t>("sc_rank", m ? m : 1);
   uint32_t* start = e->scratch_get<uint32_t>("sc_start", k + 1);
   uint32_t* order = e->scratch_get<uint32_t>("sc_order", m ? m : 1);
+  uint32_t* by_size = e->scratch_get<uint32_t>("sc_by_size", k);
   const bool smem_rank = m > 0 && k <= kRankSmem;
   if (!smem_rank) EB_CUDA(cudaMemsetAsync(segcnt, 0, segs * k * sizeof(uint32_t), e->stream));
   if (m > 0) {
@@ -538,7 +574,7 @@ void label_order(eb_engine* e, const uint32_t* ids, size_t r0, size_t r1, size_t
   }
   launch_pdl(e, k_seg_scan, blocks_for(k * 32, 256), 256, 0, segcnt, (long)segs, (uint32_t)k, counts);
   EB_LAUNCH("scatter seg scan");
-  launch_pdl(e, k_label_scan, 1, 1024, 0, counts, (uint32_t)k, start);
+  launch_pdl(e, k_label_scan, 1, 1024, 0, counts, (uint32_t)k, start, by_size);
   EB_LAUNCH("scatter label scan");
   if (m > 0) {
     launch_pdl(e, k_place, blocks_for(m, 256), 256, 0, labels, ids, (long)r0, (long)m, (long)n,
@@ -548,15 +584,17 @@ void label_order(eb_engine* e, const uint32_t* ids, size_t r0, size_t r1, size_t
   }
   *order_out = order;
   *start_out = start;
+  if (by_size_out) *by_size_out = by_size;
 }
 
 void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids, size_t r0,
                  size_t r1, const uint32_t* labels, size_t k, float* sums, uint32_t* counts,
                  float* acc) {
-  const uint32_t *order, *start;
-  label_order(e, ids, r0, r1, n, labels, k, counts, &order, &start);
-  dim3 grid((unsigned)k, blocks_for(d, 128));
-  launch_pdl(e, k_seg_sum, grid, 128, 0, x, (int)d, order, start, sums, acc);
+  const uint32_t *order, *start, *by_size;
+  label_order(e, ids, r0, r1, n, labels, k, counts, &order, &start, &by_size);
+  const unsigned cb = blocks_for(d, 128);
+  launch_pdl(e, k_seg_sum, (unsigned)(k * cb), 128, 0, x, (int)d, (int)cb, order, start, by_size,
+             sums, acc);
   EB_LAUNCH("scatter sum");
 }
 
@@ -578,32 +616,96 @@ __global__ void k_shard_pack(const uint32_t* __restrict__ labels, const float* _
 }
 
 __global__ void k_shard_unpack(const uint32_t* __restrict__ stage, long total, long s,
-                               uint32_t* __restrict__ labels, float* __restrict__ scores) {
+                               long soff, long stride, uint32_t* __restrict__ labels,
+                               float* __restrict__ scores) {
   pdl_wait();
   const long p = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= total) return;
   const long q = p / s, i = p - q * s;
-  labels[p] = stage[q * 2 * s + i];
-  scores[p] = __uint_as_float(stage[q * 2 * s + s + i]);
+  labels[p] = stage[q * stride + i];
+  scores[p] = __uint_as_float(stage[q * stride + soff + i]);
+}
+
+// The ranks' partial sums added in rank order, one thread per (centroid,
+// column) word of the k x d block (plus the k counts); 16-byte loads and
+// stores where the shares allow.
+template <bool V4>
+__global__ void k_reduce_partials(const uint32_t* __restrict__ stage, long stride, int world,
+                                  long cnt_off, long sum_off, long k, long kd,
+                                  float* __restrict__ sums, uint32_t* __restrict__ counts,
+                                  float* __restrict__ acc) {
+  pdl_wait();
+  const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (V4) {
+    const long q = t * 4;
+    if (q < kd) {
+      float4 s = *reinterpret_cast<const float4*>(stage + sum_off + q);
+      for (int r = 1; r < world; r++) {
+        const float4 v = *reinterpret_cast<const float4*>(stage + r * stride + sum_off + q);
+        s.x = __fadd_rn(s.x, v.x);
+        s.y = __fadd_rn(s.y, v.y);
+        s.z = __fadd_rn(s.z, v.z);
+        s.w = __fadd_rn(s.w, v.w);
+      }
+      *reinterpret_cast<float4*>(sums + q) = s;
+      if (acc) {
+        float4 a = *reinterpret_cast<float4*>(acc + q);
+        a.x = __fadd_rn(a.x, s.x);
+        a.y = __fadd_rn(a.y, s.y);
+        a.z = __fadd_rn(a.z, s.z);
+        a.w = __fadd_rn(a.w, s.w);
+        *reinterpret_cast<float4*>(acc + q) = a;
+      }
+    }
+  } else {
+    for (long q = t; q < kd; q += (long)gridDim.x * blockDim.x) {
+      float s = __uint_as_float(stage[sum_off + q]);
+      for (int r = 1; r < world; r++) s = __fadd_rn(s, __uint_as_float(stage[r * stride + sum_off + q]));
+      sums[q] = s;
+      if (acc) acc[q] = __fadd_rn(acc[q], s);
+    }
+  }
+  if (t < k) {
+    uint32_t c = 0;
+    for (int r = 0; r < world; r++) c += stage[r * stride + cnt_off + t];
+    counts[t] = c;
+  }
 }
 
 }  // namespace
 
-void shard_pack(eb_engine* e, const uint32_t* labels, const float* scores, size_t len, size_t s,
-                uint32_t* stage) {
-  if (s == 0) return;
-  launch_pdl(e, k_shard_pack, blocks_for(s, 256), 256, 0, labels, scores, (long)len, (long)s,
-                                                         stage + (size_t)e->rank * 2 * s);
+void shard_pack(eb_engine* e, const uint32_t* labels, const float* scores, size_t len,
+                size_t soff, size_t stride, uint32_t* stage) {
+  if (soff == 0) return;
+  launch_pdl(e, k_shard_pack, blocks_for(soff, 256), 256, 0, labels, scores, (long)len,
+             (long)soff, stage + (size_t)e->rank * stride);
   EB_LAUNCH("shard_pack");
 }
 
-void shard_unpack(eb_engine* e, const uint32_t* stage, size_t total, size_t s, int world,
-                  uint32_t* labels, float* scores) {
-  (void)world;
+void shard_unpack(eb_engine* e, const uint32_t* stage, size_t total, size_t s, size_t soff,
+                  size_t stride, uint32_t* labels, float* scores) {
   if (total == 0) return;
   launch_pdl(e, k_shard_unpack, blocks_for(total, 256), 256, 0, stage, (long)total, (long)s,
-                                                                labels, scores);
+             (long)soff, (long)stride, labels, scores);
   EB_LAUNCH("shard_unpack");
+}
+
+void reduce_partials(eb_engine* e, const uint32_t* stage, size_t stride, int world,
+                     size_t cnt_off, size_t sum_off, size_t k, size_t d, float* sums,
+                     uint32_t* counts, float* acc) {
+  const size_t kd = k * d;
+  if (kd == 0) return;
+  const bool v4 = kd % 4 == 0 && stride % 4 == 0 && sum_off % 4 == 0 &&
+                  ((uintptr_t)stage & 15) == 0 && ((uintptr_t)sums & 15) == 0 &&
+                  (!acc || ((uintptr_t)acc & 15) == 0);
+  const size_t threads = std::max(v4 ? kd / 4 : std::min<size_t>(kd, (size_t)e->num_sms * 1024), k);
+  if (v4)
+    launch_pdl(e, k_reduce_partials<true>, blocks_for(threads, 256), 256, 0, stage, (long)stride,
+               world, (long)cnt_off, (long)sum_off, (long)k, (long)kd, sums, counts, acc);
+  else
+    launch_pdl(e, k_reduce_partials<false>, blocks_for(threads, 256), 256, 0, stage, (long)stride,
+               world, (long)cnt_off, (long)sum_off, (long)k, (long)kd, sums, counts, acc);
+  EB_LAUNCH("reduce_partials");
 }
 
 }  // namespace eb

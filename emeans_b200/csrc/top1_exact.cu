@@ -9,6 +9,7 @@
 // threads (4x4 per thread), 16 columns of d per stage.
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <mutex>
 #include <string>
 
@@ -293,6 +294,10 @@ extern "C" int eb_top1_exact_noalloc(eb_engine* e, const float* x, size_t n, siz
     ensure(e != nullptr, "engine is null");
     ensure(x && c && labels && scores, "a device pointer is null");
     ensure(d > 0, "d must be positive");
+    // The kernel indexes columns with int and rows with long.
+    ensure(d <= (size_t)INT_MAX, "d must be at most 2^31 - 1");
+    ensure(n <= (size_t)LONG_MAX / d, "n * d overflows");
+    ensure(k <= (size_t)LONG_MAX / d, "k * d overflows");
     ensure(metric == EB_L2 || metric == EB_IP, "unknown metric");
     ensure(r0 <= r1, "bad row range");
     if (!ids) ensure(r1 <= n, "row range past the data");

@@ -1983,6 +1983,7 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
       if (st == cudaSuccess) st = cudaMallocAsync(&f->xl, cells * 2, e->stream);
       if (st == cudaSuccess) st = cudaMallocAsync(&f->xexp, std::max<size_t>(a.n, 1) * 4, e->stream);
       if (st == cudaSuccess) st = cudaMallocAsync(&f->xnrm, std::max<size_t>(a.n, 1) * 4, e->stream);
+      e->device_allocs += 4;
       xbuf->f16 = f;
       if (st != cudaSuccess) {
         drop_f16(xbuf);  // no room for the copy: convert per pass instead

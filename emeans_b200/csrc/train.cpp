@@ -179,12 +179,21 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   DevBuf dpos(e, EB_F32, k * d), mass(e, EB_F32, k), readout(e, EB_F32, spherical ? k * d : k);
   DevBuf sums(e, EB_F32, k * d), counts(e, EB_U32, k), pass(e, EB_F32, k * d);
   DevBuf pairs(e, EB_U32, 2 * k);
-  // Group exchange staging: world x (labels, scores) slices of a batch.
-  DevBuf stage(e, EB_U32, e->world > 1 ? 2 * ((bsz + e->world - 1) / e->world) * e->world : 1);
+  // Group exchange staging, one share per rank. Parity mode (group_shard
+  // 0-2): the (labels, scores) slices of a batch. Reduce mode (3): the slice's
+  // labels and scores, then its partial counts (k words) and sums (k x d), so
+  // that one all-gather carries the step's whole exchange; offsets are
+  // rounded to 4 words for 16-byte access.
+  const bool reduce_mode = e->world > 1 && e->group_shard == 3;
+  const size_t sh_max = (bsz + e->world - 1) / e->world;
+  const size_t s4 = (sh_max + 3) / 4 * 4, k4 = (k + 3) / 4 * 4;
+  const size_t share = reduce_mode ? 2 * s4 + k4 + k * d : 2 * sh_max;
+  DevBuf stage(e, EB_U32, e->world > 1 ? share * e->world : 1);
   EB_CUDA(cudaMemcpyAsync(dpos.f(), pos, k * d * 4, cudaMemcpyHostToDevice, e->stream));
   EB_CUDA(cudaMemcpyAsync(mass.f(), usage.data(), k * 4, cudaMemcpyHostToDevice, e->stream));
   if (data->d == d && !data->xnorm && !spherical) {
     EB_CUDA(cudaMallocAsync(&data->xnorm, std::max<size_t>(n, 1) * 4, e->stream));
+    e->device_allocs++;
     row_norms(e, static_cast<const float*>(data->ptr), n, d, data->xnorm);
   }
 
@@ -235,8 +244,8 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
         return ((rows + 127) / 128 + (size_t)e->num_sms - 1) / (size_t)e->num_sms;
       };
       const bool split_batch =
-          e->world > 1 &&
-          (e->group_shard == 1 || (e->group_shard == 0 && waves(sh) < waves(end - b)));
+          e->world > 1 && (reduce_mode || e->group_shard == 1 ||
+                           (e->group_shard == 0 && waves(sh) < waves(end - b)));
       const size_t lo = split_batch ? std::min(b + (size_t)e->rank * sh, end) : b;
       const size_t hi = split_batch ? std::min(lo + sh, end) : end;
       for (size_t c0 = lo; c0 < hi; c0 += chunk) {
@@ -256,13 +265,31 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
         a.xnorm = data->xnorm;
         top1_dispatch(e, a, data);
       }
-      if (split_batch) {
-        shard_pack(e, labels_ep.u() + lo, scores_ep.f() + lo, hi - lo, sh, stage.u());
-        group_allgather(e, stage.u(), 2 * sh);
-        shard_unpack(e, stage.u(), end - b, sh, e->world, labels_ep.u() + b, scores_ep.f() + b);
+      if (reduce_mode) {
+        // The north-star step: this rank's slice is scatter-added into its
+        // share of the staging buffer (partial counts and sums), one
+        // all-gather exchanges every rank's labels, scores and partials, and
+        // every rank adds the partials in rank order (the same bits on every
+        // rank for a given group size; not the single-engine row order).
+        uint32_t* mine = stage.u() + (size_t)e->rank * share;
+        shard_pack(e, labels_ep.u() + lo, scores_ep.f() + lo, hi - lo, s4, share, stage.u());
+        scatter_add(e, static_cast<const float*>(data->ptr), n, d, order.u(), lo, hi,
+                    labels_ep.u(), k, reinterpret_cast<float*>(mine + 2 * s4 + k4),
+                    mine + 2 * s4, nullptr);
+        group_allgather(e, stage.u(), share);
+        shard_unpack(e, stage.u(), end - b, sh, s4, share, labels_ep.u() + b, scores_ep.f() + b);
+        reduce_partials(e, stage.u(), share, e->world, 2 * s4, 2 * s4 + k4, k, d, sums.f(),
+                        counts.u(), last ? pass.f() : nullptr);
+      } else {
+        if (split_batch) {
+          shard_pack(e, labels_ep.u() + lo, scores_ep.f() + lo, hi - lo, sh, 2 * sh, stage.u());
+          group_allgather(e, stage.u(), 2 * sh);
+          shard_unpack(e, stage.u(), end - b, sh, sh, 2 * sh, labels_ep.u() + b,
+                       scores_ep.f() + b);
+        }
+        scatter_add(e, static_cast<const float*>(data->ptr), n, d, order.u(), b, end,
+                    labels_ep.u(), k, sums.f(), counts.u(), last ? pass.f() : nullptr);
       }
-      scatter_add(e, static_cast<const float*>(data->ptr), n, d, order.u(), b, end, labels_ep.u(),
-                  k, sums.f(), counts.u(), last ? pass.f() : nullptr);
       const double alpha = host::scheduled_alpha(r.alpha0, step, r.total_steps);
       ema_update(e, dpos.f(), mass.f(), sums.f(), counts.u(), k, d, (float)alpha,
                  (float)(1.0 - alpha), alpha == 1.0);

@@ -96,6 +96,11 @@ typedef struct {
 } eb_stats;
 int eb_get_stats(eb_engine* e, eb_stats* out);
 
+/* No counterpart in the reference. The number of device allocations the
+ * engine has made since creation (buffers, grow-only scratch, cached copies of
+ * bound data); a call that allocated nothing leaves it unchanged. */
+int eb_device_allocations(eb_engine* e, uint64_t* count);
+
 /* Top-1 path: 0 = exact SIMT kernel only, 1 = tensor-core screen + exact
  * re-score for calls large enough to pay (the default), 2 = screen always.
  * Results are identical in every mode; only the speed differs. The
@@ -245,11 +250,29 @@ int eb_group_unique_id(unsigned char* id);
 int eb_engine_join(eb_engine* e, int rank, int world, const unsigned char* id);
 int eb_engine_group(eb_engine* e, int* rank, int* world);
 /* No counterpart in the reference. How eb_train on a joined engine divides a
- * batch's top-1: 0 (default) splits it across the ranks only when that cuts
- * the screen's waves of 128-row tiles (a batch of one wave or less is scored
- * whole by every rank, with no exchange), 1 always splits it, 2 never does.
- * Every mode gives the same model; all ranks must use the same mode. */
+ * batch (the data-parallel step of core/train.rs:60-303 over several GPUs):
+ *  0 (default) splits its top-1 across the ranks only when that cuts the
+ *    screen's waves of 128-row tiles (a batch of one wave or less is scored
+ *    whole by every rank, with no exchange); 1 always splits it; 2 never
+ *    does. Modes 0-2 exchange (label, score) slices and give the model of one
+ *    engine alone, bit for bit.
+ *  3 splits the top-1 and the scatter-add: each rank sums its slice's rows
+ *    into partial k x d sums and k counts, one all-gather per step carries
+ *    every rank's slice results and partials, and every rank adds the
+ *    partials in rank order. All ranks get the same model, deterministic for
+ *    a given group size, but the sums are not added in the single engine's
+ *    row order, so the model agrees with it to rounding, not bit for bit.
+ * All ranks must use the same mode. */
 int eb_set_group_shard(eb_engine* e, int mode);
+
+/* No counterpart in the reference. In-place all-gather over the engine's group
+ * (NCCL, on the engine's stream): rank r's share is b[r * words_per_rank ..
+ * (r + 1) * words_per_rank) of 32-bit words; afterwards every rank holds every
+ * share. Collective: all ranks call it with the same words_per_rank. With a
+ * sharded assign (each rank's eb_top1 over its rows r * s .. (r + 1) * s of
+ * labels and scores) it gives every rank the labels and scores of all rows.
+ * A no-op on an engine that is not in a group. */
+int eb_group_allgather(eb_engine* e, eb_buf* b, size_t words_per_rank);
 
 /* Device::topk over a database sharded across a group (knn_self over several
  * GPUs, crates/emeans-cluster/src/knn.rs:17-64): every rank passes the same m

@@ -2,7 +2,10 @@
 under torch.distributed.run): a joined engine trains with the batch top-1
 split across the ranks and the labels/scores all-gathered over NCCL, and
 ranks a sharded database with eb_topk_group; both must equal, bit for bit, a
-lone engine's results on the same GPU."""
+lone engine's results on the same GPU. In group mode 3 (the top-1 and the
+scatter-add split, partial sums exchanged) every rank must hold the same
+model, within rounding of the lone engine's; and a sharded assign with its
+labels and scores all-gathered (eb_group_allgather) equals one engine's."""
 
 import datetime
 import os
@@ -45,6 +48,21 @@ def main():
                 f"rank {rank}: centroids differ (n={n}, k={k}, mode {mode})"
             assert np.array_equal(a.labels, b.labels), f"rank {rank}: labels differ"
             assert a.obj == b.obj and a.nsplit == b.nsplit, f"rank {rank}: statistics differ"
+    # Mode 3, the north-star step: the top-1 and the scatter-add split, partial
+    # sums exchanged and added in rank order. Every rank ends with the same
+    # bits; the model agrees with the lone engine's to rounding.
+    group.set_group_shard(3)
+    for n, d, k, spherical, seed in cases:
+        x = mixture(n, d, 24, 0.4, spherical, seed)
+        cfg = eb.Config(d=d, k=k, seed=seed, spherical=spherical, nepochs=2.0)
+        a = group.train(x, cfg)
+        b = solo.train(x, cfg)
+        every = [None] * world
+        dist.all_gather_object(every, a.centroids.tobytes())
+        assert all(v == every[0] for v in every), f"rank {rank}: ranks differ in mode 3"
+        assert abs(a.obj[-1] - b.obj[-1]) <= 1e-3 * abs(b.obj[-1]), \
+            f"rank {rank}: mode-3 objective {a.obj[-1]} vs {b.obj[-1]}"
+    group.set_group_shard(0)
     # knn_self over a database sharded across the ranks, against one engine
     # ranking the whole database.
     rng = np.random.default_rng(11)
@@ -57,6 +75,24 @@ def main():
         si, ss = solo.topk(data, data, d, kk, exclude_self)
         assert np.array_equal(gi, si), f"rank {rank}: knn ids differ"
         assert np.array_equal(gs.view(np.uint32), ss.view(np.uint32)), f"rank {rank}: knn sims differ"
+    # A sharded assign: each rank's top-1 over its rows, then the labels and
+    # scores all-gathered so that every rank holds all of them.
+    n, d, k = 9001, 64, 300
+    x = mixture(n, d, 24, 0.4, False, 5)
+    c = x[:k] * np.float32(0.97)
+    s = (n + world - 1) // world
+    lo, hi = min(rank * s, n), min(rank * s + s, n)
+    xb, cb, cn = group.bind(x, d), group.upload_f32(c), group.zeros_f32(k)
+    group.row_norms(cb, k, d, cn)
+    lab, sco = group.zeros_u32(s * world), group.zeros_f32(s * world)
+    group.top1(xb, d, None, range(lo, hi), cb, cn, k, eb.L2, lab, sco)
+    group.group_allgather(lab, s)
+    group.group_allgather(sco, s)
+    sl, ss = solo.assign(x, d, c, eb.L2)
+    assert np.array_equal(lab.read(0, n), sl), f"rank {rank}: gathered labels differ"
+    assert np.array_equal(sco.read(0, n).view(np.uint32), ss.view(np.uint32)), \
+        f"rank {rank}: gathered scores differ"
+    del xb, cb, cn, lab, sco
     group.close()
     solo.close()
     dist.barrier()

@@ -111,3 +111,28 @@ def test_training_on_bound_rows(engine):
     for g in (got, again):
         assert np.array_equal(bits(g.centroids.ravel()), bits(want.centroids.ravel()))
         assert np.array_equal(g.labels, want.labels) and g.obj == want.obj
+
+
+def test_config2_training_and_final_assign(engine):
+    """BASELINE config 2, the headline run at full size: 200,000 x 768 L2,
+    k = 1024, seed 0, the reference schedule (65 steps of 16,384 rows), then
+    the full-data final assign. Labels, centroids, masses and every epoch's
+    objective are bit-equal to the oracle's training, and the final assign's
+    labels and scores to the oracle's top-1."""
+    from bench import gen_rows
+
+    n, d, k = 200_000, 768, 1024
+    x = gen_rows(n, d, 0)
+    cfg = eb.Config(d=d, k=k, seed=0, spherical=False)
+    engine.bind_data(x, d)
+    try:
+        got = engine.train(x, cfg)
+        lab, sco = engine.assign(x, d, got.centroids, eb.L2)
+    finally:
+        engine.unbind_data()
+    want = oracle.train(x, d, k, seed=0)
+    assert got.total_steps == 65 and got.batch_size == 16384
+    same_run(got, want)
+    wl, ws = oracle.top1(x.ravel(), d, want["centroids"], oracle.L2)
+    assert np.array_equal(lab, wl)
+    assert np.array_equal(bits(sco), bits(ws))
