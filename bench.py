@@ -438,6 +438,12 @@ def run_ours(args):
         mres = eng.internal_scores(x, d, glab, k)
         met_ms = (time.perf_counter() - t0) * 1e3
 
+    c3 = c4 = None
+    if not args.no_c3:
+        c3 = c3_leg(eng, args, world, rank, local, dist)
+    if not args.no_c4:
+        c4 = c4_leg(eng, args, world, rank, dist)
+
     if rank == 0:
         peak, peak_src = peaks()
         # The dominant kernel, the tcgen05 screen, timed by CUDA events around
@@ -521,6 +527,10 @@ def run_ours(args):
                     "obj_rel_delta_vs_parity": dlt,
                     "centroids_max_abs_diff": float(np.max(np.abs(tr_red.centroids -
                                                                   tr.centroids)))}
+        if c3:
+            out["c3"] = c3
+        if c4:
+            out["c4"] = c4
         out["clocks"] = clk.summary()
         if not args.no_cpu:
             # Parity of the scored run: the oracle's labels and scores over the
@@ -572,6 +582,155 @@ def gen_knn_rows(n, d, seed=4, components=10_000, sigma=0.4, dup_frac=0.05):
     return np.ascontiguousarray(x, dtype=np.float32)
 
 
+def c3_rows(lo, hi, d, device, seed=3, chunk=65536):
+    """Config-3 rows lo .. hi on the device: N(0, I) rows normalised, drawn in
+    fixed 65,536-row chunks (chunk c from a generator seeded seed * 2^20 + c),
+    so that any shard of the 10M rows is the same on any number of GPUs."""
+    import torch
+
+    out = torch.empty((hi - lo, d), dtype=torch.float32, device=device)
+    g = torch.Generator(device=device)
+    for c in range(lo // chunk, (hi + chunk - 1) // chunk if hi > lo else lo // chunk):
+        g.manual_seed(seed * (1 << 20) + c)
+        blk = torch.randn((chunk, d), generator=g, device=device, dtype=torch.float32)
+        blk /= torch.linalg.vector_norm(blk, dim=1, keepdim=True)
+        a, b = max(lo, c * chunk), min(hi, (c + 1) * chunk)
+        out[a - lo:b - lo] = blk[a - c * chunk:b - c * chunk]
+    return out
+
+
+def c3_leg(eng, args, world, rank, local, dist):
+    """assign-only throughput, 10M x 1024 unit rows vs
+    k = 65,536 unit centroids (seed 1), inner product, label + score per row;
+    rows sharded over the ranks (generated on the device), centroids
+    replicated. Rank 0 checks its first rows against the oracle."""
+    import torch
+
+    import emeans_b200 as eb
+
+    n, d, k = args.c3_n, 1024, 65536
+    lo, hi, _ = shard(n, world, rank)
+    m = hi - lo
+    dev = torch.device("cuda", local)
+    x = c3_rows(lo, hi, d, dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    cent = torch.randn((k, d), generator=g, device=dev, dtype=torch.float32)
+    cent /= torch.linalg.vector_norm(cent, dim=1, keepdim=True)
+    lab_t = torch.empty(max(m, 1), dtype=torch.int32, device=dev)
+    sco_t = torch.empty(max(m, 1), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+    xb, cb, lab, sco = eng.wrap(x), eng.wrap(cent), eng.wrap(lab_t), eng.wrap(sco_t)
+    stream = torch.cuda.ExternalStream(eng.stream())
+
+    def step():
+        if m:
+            eng.top1(xb, d, None, range(0, m), cb, None, k, eb.IP, lab, sco)
+
+    step()
+    eng.sync()
+    if dist:
+        dist.barrier()
+    eng.set_kernel_timing(True)
+    eng.screen_timing()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.c3_steps):
+        step()
+    t1.record(stream)
+    t1.synchronize()
+    eng.sync()
+    screen_ms, launches, srows = eng.screen_timing()
+    eng.set_kernel_timing(False)
+    ms = _max_over_ranks(dist, [t0.elapsed_time(t1) / args.c3_steps])[0]
+    res = {"workload": f"C3 assign: {n:,} x {d} unit rows vs k={k} unit centroids (seed 1), "
+                       "inner product, label u32 + score f32 per row, rows on the device",
+           "rows": n, "d": d, "k": k, "n_gpus": world, "steps": args.c3_steps,
+           "ms_per_pass": ms, "grows_per_s": n / (ms * 1e-3) / 1e9,
+           "useful_tflops": 2.0 * n * k * d / (ms * 1e-3) / 1e12,
+           "screen_useful_tflops_rank0": 2.0 * srows * k * d / max(screen_ms * 1e-3, 1e-12) / 1e12,
+           "parallelism": f"rows sharded over {world} GPU(s), centroids replicated, results "
+                          "stay on each rank"}
+    if rank == 0 and m:
+        import oracle
+
+        chk = min(args.c3_check, m)
+        xs = x[:chk].cpu().numpy()
+        cs = cent.cpu().numpy()
+        gl = lab_t[:chk].cpu().numpy().view(np.uint32)
+        gs = sco_t[:chk].cpu().numpy()
+        threads = os.cpu_count() or 1
+        done, t = 0, time.perf_counter()
+        ok_l = ok_s = True
+        while done < chk and time.perf_counter() - t < args.cpu_budget:
+            e = min(done + 4096, chk)
+            ol, osc = oracle.top1(xs[done:e].ravel(), d, cs.ravel(), oracle.IP, threads=threads)
+            ok_l &= bool(np.array_equal(ol, gl[done:e]))
+            ok_s &= bool(np.array_equal(osc.view(np.uint32), gs[done:e].view(np.uint32)))
+            done = e
+        dt = time.perf_counter() - t
+        res["parity"] = {"rows": done, "labels_equal": ok_l, "scores_equal": ok_s}
+        res["cpu_baseline"] = {"value": done / dt / 1e9, "unit": "Grows/s", "cores": threads,
+                               "kind": "port", "sample": f"first {done:,} rows, {dt:.1f} s"}
+    del xb, cb, lab, sco, x, cent, lab_t, sco_t
+    torch.cuda.empty_cache()
+    return res
+
+
+def c4_leg(eng, args, world, rank, dist):
+    """exact kNN self-join, 1M x 384, kk = 10, inner
+    product, self excluded, through the host-array API; with N GPUs the
+    database is sharded, queries replicated, per-shard lists merged on the
+    device (eb_topk_group). Rank 0 checks its first queries against the
+    oracle's self-join."""
+    n, d, kk = args.c4_n, 384, 10
+    x = gen_knn_rows(n, d)
+    lo, hi, _ = shard(n, world, rank)
+
+    def call():
+        if world > 1:
+            return eng.topk_group(x, x[lo:hi], lo, n, d, kk, exclude_self=True)
+        return eng.topk(x, x, d, kk, exclude_self=True)
+
+    call()  # warm-up (screen scratch, the data's copy)
+    times = []
+    for _ in range(args.c4_steps):
+        if dist:
+            dist.barrier()
+        t = time.perf_counter()
+        ids, sims = call()
+        times.append(time.perf_counter() - t)
+    t = _max_over_ranks(dist, [statistics.median(times)])[0]
+    res = {"workload": f"C4 kNN self-join: {n:,} x {d} unit rows (10,000-component mixture, "
+                       "5% near-duplicates), kk=10, inner product, self excluded; host arrays "
+                       "in and out (eb_topk / eb_topk_group)",
+           "rows": n, "d": d, "kk": kk, "n_gpus": world, "steps": args.c4_steps,
+           "s_per_join": t, "queries_per_s": n / t,
+           "useful_tflops": 2.0 * n * n * d / t / 1e12,
+           "parallelism": f"database sharded over {world} GPU(s), queries replicated, lists "
+                          "all-gathered and merged on the device" if world > 1 else "one GPU"}
+    if rank == 0:
+        import oracle
+
+        chk = min(args.c4_check, n)
+        threads = os.cpu_count() or 1
+        done, t0 = 0, time.perf_counter()
+        ok_i = ok_s = True
+        while done < chk and time.perf_counter() - t0 < args.cpu_budget:
+            e = min(done + 1000, chk)
+            oi, osm = oracle.topk_self_rows(x, d, done, e - done, kk, threads=threads)
+            ok_i &= bool(np.array_equal(oi, ids[done * kk:e * kk]))
+            ok_s &= bool(np.array_equal(osm.view(np.uint32), sims[done * kk:e * kk].view(np.uint32)))
+            done = e
+        dt = time.perf_counter() - t0
+        res["parity"] = {"queries": done, "ids_equal": ok_i, "sims_equal": ok_s,
+                         "oracle": "FMA-chain exact top-k (oracle/oracle.cpp)"}
+        res["cpu_baseline"] = {"value": done / dt, "unit": "queries/s", "cores": threads,
+                               "kind": "port", "sample": f"first {done:,} queries x all {n:,} "
+                                                          f"rows, {dt:.1f} s"}
+    return res
+
+
 def run_knn(args):
     """--knn N: the kNN self-join config's shape on N rows (d 384, kk 10, inner
     product, self excluded) through eb_topk with host arrays; one JSON line."""
@@ -614,6 +773,16 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--save-cent", default=None, help="write the trained centroids (.npy)")
     ap.add_argument("--load-cent", default=None, help="use these centroids instead of training")
+    ap.add_argument("--no-c3", action="store_true", help="skip the config-3 assign leg")
+    ap.add_argument("--no-c4", action="store_true", help="skip the config-4 kNN leg")
+    ap.add_argument("--c3-n", type=int, default=10_000_000)
+    ap.add_argument("--c3-steps", type=int, default=2)
+    ap.add_argument("--c3-check", type=int, default=100_000,
+                    help="config-3 rows checked against the oracle (time-bounded)")
+    ap.add_argument("--c4-n", type=int, default=1_000_000)
+    ap.add_argument("--c4-steps", type=int, default=2)
+    ap.add_argument("--c4-check", type=int, default=10_000,
+                    help="config-4 queries checked against the oracle (time-bounded)")
     ap.add_argument("--knn", type=int, default=0,
                     help="instead of the headline: the kNN self-join config's shape on this "
                          "many rows (one GPU)")

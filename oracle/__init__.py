@@ -260,6 +260,20 @@ def topk(q, data, d, kk, exclude_self=False, threads=None):
     return ids, sims
 
 
+def topk_self_rows(data, d, q0, m, kk, threads=None):
+    """The self-join's top-kk (self excluded) of the queries data[q0 .. q0 + m)
+    against all of data."""
+    data = f32(data)
+    n = data.size // d
+    ids = np.empty(m * kk, np.uint32)
+    sims = np.empty(m * kk, np.float32)
+    threads = threads or os.cpu_count() or 1
+    _check(lib().orc_topk_self_rows(_p(data), C.c_size_t(n), C.c_size_t(d), C.c_size_t(q0),
+                                    C.c_size_t(m), C.c_size_t(kk), _p(ids), _p(sims),
+                                    C.c_int(threads)))
+    return ids, sims
+
+
 def train(x, d, k, nepochs=5.0, batch_law="auto", batch_size=None, alpha0=None, seed=1234,
           spherical=False, unused_threshold=None, chunk=None, init=None, state=None,
           threads=None):

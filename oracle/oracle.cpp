@@ -559,10 +559,10 @@ void orc_closing_means(const float* pos, const float* sums, const double* counts
   closing(pos, sums, counts, k, d, spherical != 0, out);
 }
 
-int orc_topk(const float* q, size_t m, const float* data, size_t n, size_t d, size_t kk,
-             int exclude_self, uint32_t* ids, float* sims, int threads) {
-  if (d == 0 || kk == 0) return fail("d and kk must be positive");
-  if (exclude_self && m != n) return fail("exclude_self needs queries == data");
+namespace {
+// Query i's own column is self0 + i when exclude_self.
+int topk_impl(const float* q, size_t m, const float* data, size_t n, size_t d, size_t kk,
+              int exclude_self, size_t self0, uint32_t* ids, float* sims, int threads) {
   std::vector<float> packed;
   pack_panels(data, n, d, packed);
   size_t panels = (n + NR - 1) / NR;
@@ -590,7 +590,7 @@ int orc_topk(const float* q, size_t m, const float* data, size_t n, size_t d, si
         uint32_t* id = bi.data() + i * kk;
         for (int j = 0; j < nc; j++) {
           uint32_t col = (uint32_t)(p * NR + j);
-          if (exclude_self && col == i0 + i) continue;
+          if (exclude_self && col == self0 + i0 + i) continue;
           float v = dots[i * NR + j];
           // Columns arrive in increasing id, so an equal score never displaces
           // (knn.rs:86: strict '>'); NaN and -inf never enter.
@@ -614,6 +614,23 @@ int orc_topk(const float* q, size_t m, const float* data, size_t n, size_t d, si
       }
   });
   return 0;
+}
+}  // namespace
+
+int orc_topk(const float* q, size_t m, const float* data, size_t n, size_t d, size_t kk,
+             int exclude_self, uint32_t* ids, float* sims, int threads) {
+  if (d == 0 || kk == 0) return fail("d and kk must be positive");
+  if (exclude_self && m != n) return fail("exclude_self needs queries == data");
+  return topk_impl(q, m, data, n, d, kk, exclude_self, 0, ids, sims, threads);
+}
+
+// knn_self restricted to the queries data[q0 .. q0 + m): the self-join's
+// results for those rows (each skips its own column q0 + i).
+int orc_topk_self_rows(const float* data, size_t n, size_t d, size_t q0, size_t m, size_t kk,
+                       uint32_t* ids, float* sims, int threads) {
+  if (d == 0 || kk == 0) return fail("d and kk must be positive");
+  if (q0 + m > n) return fail("query rows past the data");
+  return topk_impl(data + q0 * d, m, data, n, d, kk, 1, q0, ids, sims, threads);
 }
 
 // The device loop (core/train.rs:60-303) on the oracle's ops.

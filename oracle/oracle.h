@@ -78,6 +78,9 @@ void orc_closing_means(const float* pos, const float* sums, const double* counts
 /* ---- exact top-k by inner product (FMA-chain scores; best first, lower id on ties) ---- */
 int orc_topk(const float* q, size_t m, const float* data, size_t n, size_t d, size_t kk,
              int exclude_self, uint32_t* ids, float* sims, int threads);
+// knn_self for the queries data[q0 .. q0 + m) only (each skips its own row).
+int orc_topk_self_rows(const float* data, size_t n, size_t d, size_t q0, size_t m, size_t kk,
+                       uint32_t* ids, float* sims, int threads);
 
 /* ---- layer 2: the training loop (crates/emeans-core/src/core/train.rs:60-303) ---- */
 typedef struct {

@@ -277,3 +277,17 @@ def test_normalize_and_norms_float_order():
     assert np.all(u[0] == 0)
     n64 = np.linalg.norm(m[2:].astype(np.float64), axis=1)
     assert np.allclose(u[2:], m[2:] / n64[:, None], rtol=1e-5, atol=1e-6)
+
+
+def test_self_join_rows_equal_the_full_self_join():
+    """oracle.topk_self_rows (the self-join for a block of query rows, the
+    bench's subsample check) equals those rows of the full self-join."""
+    rng = np.random.default_rng(4)
+    n, d, kk = 700, 24, 7
+    x = rng.standard_normal((n, d)).astype(np.float32)
+    x[600:610] = x[5:15]  # duplicates: equal scores keep the lower id
+    ids, sims = oracle.topk(x, x, d, kk, exclude_self=True)
+    for q0, m in ((0, 50), (333, 120), (650, 50)):
+        si, ss = oracle.topk_self_rows(x, d, q0, m, kk)
+        assert np.array_equal(si, ids[q0 * kk:(q0 + m) * kk])
+        assert np.array_equal(ss.view(np.uint32), sims[q0 * kk:(q0 + m) * kk].view(np.uint32))
