@@ -582,6 +582,27 @@ def gen_knn_rows(n, d, seed=4, components=10_000, sigma=0.4, dup_frac=0.05):
     return np.ascontiguousarray(x, dtype=np.float32)
 
 
+def gen_c5_rows(n, d, seed=5, tops=64, subs=32, sub_sigma=0.3, row_sigma=0.2, dup_frac=0.02,
+                dup_sigma=0.005):
+    """Config-5 rows: a nested mixture (64 top means N(0, I), 32 sub-means per
+    top = top + N(0, 0.3^2 I), rows = sub-mean + N(0, 0.2^2 I)), unit rows, with
+    a fraction replaced by near-duplicates (a random row + N(0, 0.005^2 I),
+    renormalised)."""
+    rng = np.random.default_rng(seed)
+    top = rng.standard_normal((tops, d), dtype=np.float32)
+    sub = (np.repeat(top, subs, axis=0) +
+           np.float32(sub_sigma) * rng.standard_normal((tops * subs, d), dtype=np.float32))
+    x = sub[rng.integers(0, tops * subs, n)]
+    x += np.float32(row_sigma) * rng.standard_normal((n, d), dtype=np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    nd = int(n * dup_frac)
+    dup = rng.choice(n, nd, replace=False)
+    x[dup] = x[rng.integers(0, n, nd)] + np.float32(dup_sigma) * rng.standard_normal(
+        (nd, d), dtype=np.float32)
+    x[dup] /= np.linalg.norm(x[dup], axis=1, keepdims=True)
+    return np.ascontiguousarray(x, dtype=np.float32)
+
+
 def c3_rows(lo, hi, d, device, seed=3, chunk=65536):
     """Config-3 rows lo .. hi on the device: N(0, I) rows normalised, drawn in
     fixed 65,536-row chunks (chunk c from a generator seeded seed * 2^20 + c),

@@ -28,6 +28,7 @@ from typing import Optional, Sequence
 import numpy as np
 
 __all__ = ["Engine", "Buffer", "B200Assigner", "EngineError", "Config", "Trained",
+           "DedupConfig", "DedupResult", "dedup", "dedup_with_neighbors",
            "knn", "knn_self", "L2", "IP", "lib_path", "load"]
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -47,6 +48,20 @@ class _Internal(C.Structure):
     _fields_ = [("k_eff", C.c_uint64), ("silhouette", C.c_double),
                 ("calinski_harabasz", C.c_double), ("davies_bouldin", C.c_double),
                 ("objective", C.c_double)]
+
+
+class _DedupConfig(C.Structure):
+    """eb_dedup_config (include/emeans_b200.h)."""
+    _fields_ = [("k", C.c_size_t), ("sim_threshold", C.c_float), ("rep_threshold", C.c_float),
+                ("max_gap_secs", C.c_double)]
+
+
+class _DedupOut(C.Structure):
+    """eb_dedup_out (include/emeans_b200.h)."""
+    _fields_ = [("group_of", C.c_void_p), ("representatives", C.c_void_p),
+                ("anchors", C.c_void_p), ("sizes", C.c_void_p), ("nn_sim", C.c_void_p),
+                ("n_groups", C.c_uint64), ("linked_pairs", C.c_uint64),
+                ("split_components", C.c_uint64)]
 
 
 class EngineError(RuntimeError):
@@ -141,6 +156,10 @@ def load():
         "eb_set_group_shard": (I, [P, I]),
         "eb_device_allocations": (I, [P, C.POINTER(C.c_uint64)]),
         "eb_group_allgather": (I, [P, P, S]),
+        "eb_test_screen_dead_wait": (I, [P, I]),
+        "eb_dedup_with_neighbors": (I, [P, S, S, P, P, S, P, P, P, C.POINTER(_DedupConfig),
+                                        C.POINTER(_DedupOut)]),
+        "eb_dedup": (I, [P, P, S, S, P, P, P, C.POINTER(_DedupConfig), C.POINTER(_DedupOut)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -373,6 +392,17 @@ class Engine:
                 "davies_bouldin": out.davies_bouldin, "objective": out.objective,
                 "sizes": sizes}
 
+    def dedup(self, x, d: int, created=None, burst=None, priority=None,
+              cfg: Optional[DedupConfig] = None) -> "DedupResult":
+        """``dedup::dedup`` (crates/emeans-cluster/src/dedup.rs:160-183): the
+        exact kNN self-join on the engine, then the grouping stages."""
+        cfg = cfg or DedupConfig()
+        xa = _f32(x).ravel()
+        n = xa.size // d
+        t, b, p = _dedup_side(n, created, burst, priority)
+        return _dedup_call(lambda c, o: load().eb_dedup(
+            self.h, _ptr(xa), n, d, _ptr(t), _ptr(b), _ptr(p), c, o), n, cfg)
+
     def topk_group(self, queries, shard, shard_offset: int, n_total: int, d: int, kk: int,
                    exclude_self: bool = False):
         """eb_topk_group: top-kk over a database sharded across the engine's
@@ -552,6 +582,83 @@ def shard_bounds(b: int, end: int, rank: int, world: int):
     return lo, hi
 
 
+@dataclass
+class DedupConfig:
+    """``dedup::DedupConfig`` (crates/emeans-cluster/src/dedup.rs:39-62)."""
+    k: int = 10
+    sim_threshold: float = 0.95
+    rep_threshold: Optional[float] = None
+    max_gap_secs: Optional[float] = None
+
+
+@dataclass
+class DedupResult:
+    """``dedup::DedupResult`` (dedup.rs:77-130)."""
+    group_of: np.ndarray
+    representatives: np.ndarray
+    anchors: np.ndarray
+    sizes: np.ndarray
+    nn_sim: np.ndarray
+    linked_pairs: int
+    split_components: int
+
+    def n_groups(self) -> int:
+        return int(self.representatives.size)
+
+    def expand(self, rep_labels):
+        """Every row gets its group representative's label (dedup.rs:113-120)."""
+        rep_labels = np.asarray(rep_labels)
+        assert rep_labels.shape[0] == self.n_groups()
+        return rep_labels[self.group_of]
+
+    def gather(self, x, d: int):
+        """The representative rows, in group order (dedup.rs:123-129)."""
+        return np.asarray(x, np.float32).reshape(-1, d)[self.representatives]
+
+
+def _dedup_side(n, created, burst, priority):
+    t = None if created is None else np.ascontiguousarray(created, np.float64)
+    b = None
+    if burst is not None:
+        b = np.array([NONE_ID if v is None else int(v) for v in burst], np.uint32)
+        if np.any(np.array([v is not None and int(v) == NONE_ID for v in burst])):
+            raise ValueError("burst id 0xFFFFFFFF is reserved for no burst")
+    p = None if priority is None else np.ascontiguousarray(priority, np.float32)
+    for a in (t, b, p):
+        if a is not None and a.size != n:
+            raise ValueError("one timestamp / burst id / priority per row")
+    return t, b, p
+
+
+def _dedup_call(fn, n, cfg: DedupConfig):
+    c = _DedupConfig(k=cfg.k, sim_threshold=cfg.sim_threshold,
+                     rep_threshold=math.nan if cfg.rep_threshold is None else cfg.rep_threshold,
+                     max_gap_secs=math.nan if cfg.max_gap_secs is None else cfg.max_gap_secs)
+    arrs = [np.zeros(max(n, 1), np.uint32) for _ in range(4)] + [np.zeros(max(n, 1), np.float32)]
+    out = _DedupOut(*[a.ctypes.data for a in arrs])
+    _check(fn(C.byref(c), C.byref(out)))
+    g = int(out.n_groups)
+    return DedupResult(group_of=arrs[0][:n].copy(), representatives=arrs[1][:g].copy(),
+                       anchors=arrs[2][:g].copy(), sizes=arrs[3][:g].copy(),
+                       nn_sim=arrs[4][:n].copy(), linked_pairs=int(out.linked_pairs),
+                       split_components=int(out.split_components))
+
+
+def dedup_with_neighbors(x, d: int, ids, sims, kk: int, created=None, burst=None, priority=None,
+                         cfg: Optional[DedupConfig] = None) -> DedupResult:
+    """``dedup::dedup_with_neighbors`` (dedup.rs:186-358) on the host (C++):
+    groups from the self-join neighbours ids / sims (n x kk)."""
+    cfg = cfg or DedupConfig()
+    xa = _f32(x).ravel()
+    n = xa.size // d
+    ia, sa = _u32(ids).ravel(), _f32(sims).ravel()
+    if ia.size != n * kk or sa.size != n * kk:
+        raise ValueError("ids and sims must be n x kk")
+    t, b, p = _dedup_side(n, created, burst, priority)
+    return _dedup_call(lambda c, o: load().eb_dedup_with_neighbors(
+        _ptr(xa), n, d, _ptr(ia), _ptr(sa), kk, _ptr(t), _ptr(b), _ptr(p), c, o), n, cfg)
+
+
 def reduce_layout(batch: int, world: int, k: int, d: int):
     """The per-rank share of eb_train's exchange buffer in group mode 3 (the
     split top-1 and scatter-add): (s, s4, k4, share) with s = ceil(batch /
@@ -597,6 +704,12 @@ def _search(queries, data, d, k, exclude_self, engine=None):
     ids, sims = eng.topk(queries, data, d, k, exclude_self)
     m = ids.size // k
     return ids.reshape(m, k), sims.reshape(m, k)
+
+
+def dedup(x, d: int, created=None, burst=None, priority=None,
+          cfg: Optional[DedupConfig] = None, engine: Optional[Engine] = None) -> DedupResult:
+    """Near-duplicate groups of the unit rows x (dedup.rs:160-183) on the B200."""
+    return (engine or Engine(0)).dedup(x, d, created, burst, priority, cfg)
 
 
 def knn_self(data, d: int, k: int, engine: Optional[Engine] = None):

@@ -249,6 +249,13 @@ int eb_get_stats(eb_engine* e, eb_stats* out) {
   });
 }
 
+int eb_test_screen_dead_wait(eb_engine* e, int on) {
+  return guard([&] {
+    need(e, "engine");
+    e->screen_dead_wait = on != 0;
+  });
+}
+
 int eb_device_allocations(eb_engine* e, uint64_t* count) {
   return guard([&] {
     need(e, "engine");

@@ -90,6 +90,9 @@ struct eb_engine {
   // Device allocations the engine has made since creation (buffers, scratch,
   // cached copies), for callers that check a call allocated nothing.
   uint64_t device_allocs = 0;
+  // Failure-detection test: the next top-1 screen launch makes one wait run
+  // out (eb_test_screen_dead_wait); cleared by that launch.
+  int screen_dead_wait = 0;
   // Tensor-core screen for top-1: 0 off, 1 auto (large enough calls), 2 always.
   // EMEANS_B200_SCREEN=0/1/2 sets it at creation; eb_set_screen_mode later.
   int screen_mode = 1;

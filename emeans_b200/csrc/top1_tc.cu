@@ -536,6 +536,10 @@ struct ScreenParams {
   // the screen's first thread.
   uint32_t* zero0;
   uint32_t* zero1;
+  // Failure-detection test (eb_test_screen_dead_wait): CTA 0's epilogue waits
+  // for its second tile on a barrier that nothing arrives at, so that the
+  // wait runs out and the give-up path runs. 0 in normal use.
+  int dead_wait;
 };
 
 template <bool IP, bool TOPK = false>
@@ -554,7 +558,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   // Top-k mode: the second accumulator buffer's pair.
   uint64_t* tfull1 = mma_done + 1;
   uint64_t* tempty1 = tfull1 + 1;
-  uint32_t* tmem_slot = (uint32_t*)(tempty1 + 1);
+  uint64_t* dead = tempty1 + 1;  // never arrived at (the dead_wait test)
+  uint32_t* tmem_slot = (uint32_t*)(dead + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   float* cn_s = (float*)(smem + STAGES * STAGE_BYTES + 256);  // [8 warps][HALF]
   float* sv_s = cn_s + 8 * HALF;                               // [8 warps][16][32]
@@ -575,6 +580,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(mma_done, 1);
     mbar_init(tfull1, 1);
     mbar_init(tempty1, 256);
+    mbar_init(dead, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -745,8 +751,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // Warp-uniform: the TMEM loads below are .sync.aligned.
         const int buf = TOPK ? (tc & 1) : 0;
         const uint32_t use = TOPK ? (uint32_t)(tc >> 1) : (uint32_t)tc;
-        const bool ready =
-            __all_sync(0xFFFFFFFFu, mbar_wait(buf ? tfull1 : tfull, use & 1, abort_flag));
+        uint64_t* wbar = buf ? tfull1 : tfull;
+        uint32_t wpar = use & 1;
+        if (P.dead_wait && blockIdx.x == 0 && tc == 1) {
+          wbar = dead;  // phase 0 never completes: the wait runs out after WAIT_NS
+          wpar = 0;
+        }
+        const bool ready = __all_sync(0xFFFFFFFFu, mbar_wait(wbar, wpar, abort_flag));
         if (!ready) {
           stop = true;
           break;
@@ -1966,6 +1977,7 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   P.status = e->d_status;
   P.zero0 = pair_count;
   P.zero1 = list_count;
+  P.dead_wait = e->screen_dead_wait;
 
   // A bound data set keeps its split copy across calls (training steps,
   // repeated assigns): converted once, then read in place or gathered by id.
@@ -2043,6 +2055,7 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
     else
       launch_screen<false>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
     EB_LAUNCH("screen");
+    P.dead_wait = e->screen_dead_wait = 0;  // one launch only
     if (ev_end) EB_CUDA(cudaEventRecord(ev_end, e->stream));
     if (ip)
       launch_exact<true>(e, a, (long)c0, (long)m, S);

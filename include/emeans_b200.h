@@ -96,6 +96,17 @@ typedef struct {
 } eb_stats;
 int eb_get_stats(eb_engine* e, eb_stats* out);
 
+/* No counterpart in the reference: a failure-detection test hook. With on,
+ * the next launch of the top-1 tensor-core screen has its first CTA's
+ * epilogue wait, at its second centroid tile, on a device barrier that
+ * nothing arrives at; the wait gives up after its limit (2 s), the CTA's
+ * other roles see the abort, wait for their own copies and products in flight
+ * and free their tensor memory, its rows go to the exact full scan, and the
+ * next synchronising call reports EB_ERROR ("device-side wait timed out").
+ * The labels and scores are still exact; the engine stays usable. The hook
+ * clears itself at that launch. */
+int eb_test_screen_dead_wait(eb_engine* e, int on);
+
 /* No counterpart in the reference. The number of device allocations the
  * engine has made since creation (buffers, grow-only scratch, cached copies of
  * bound data); a call that allocated nothing leaves it unchanged. */
@@ -308,6 +319,50 @@ int eb_top1_exact_noalloc(eb_engine* e, const float* x, size_t n, size_t d,
                           const uint32_t* ids, size_t r0, size_t r1, const float* c,
                           const float* cnorm, size_t k, int metric, uint32_t* labels,
                           float* scores);
+
+/* ---------------------------------------------------------------- dedup */
+
+/* dedup::DedupConfig (crates/emeans-cluster/src/dedup.rs:39-62). */
+typedef struct {
+  size_t k;              /* neighbours searched per row; 1 ..= 16 on this engine */
+  float sim_threshold;   /* cosine at or above which two rows link, in [-1, 1] */
+  float rep_threshold;   /* cosine to the star's anchor to stay; NaN: sim_threshold */
+  double max_gap_secs;   /* largest time gap of a link; NaN: no time rule */
+} eb_dedup_config;
+
+/* dedup::DedupResult (dedup.rs:77-96). The caller provides every array with
+ * room for n entries; the first n_groups entries of representatives, anchors
+ * and sizes are written. */
+typedef struct {
+  uint32_t* group_of;        /* n: group of every row (groups by lowest row) */
+  uint32_t* representatives; /* the row that stands for each group */
+  uint32_t* anchors;         /* each group's star center */
+  uint32_t* sizes;           /* members per group */
+  float* nn_sim;             /* n: similarity to the nearest other row */
+  uint64_t n_groups;
+  uint64_t linked_pairs;     /* links that passed (each pair once) */
+  uint64_t split_components; /* components the star cover cut */
+} eb_dedup_out;
+
+/* dedup::dedup_with_neighbors (dedup.rs:186-358), host code: near-duplicate
+ * groups of the n x d unit rows x from their self-join neighbours (ids, sims:
+ * n x kk, best first, 0xFFFFFFFF / -inf padding, the row itself excluded).
+ * created_unix (n, NaN = unknown), burst (n, 0xFFFFFFFF = no burst) and
+ * priority (n, not NaN) are optional (NULL). Bursts are always one group;
+ * links need sim >= sim_threshold (and the time rule); each component is cut
+ * into stars around the best-linked rows; the representative is the member of
+ * highest priority, then highest mean similarity, then lowest id. Dots are
+ * f32 products added in column order, as the reference's. Needs no device. */
+int eb_dedup_with_neighbors(const float* x, size_t n, size_t d, const uint32_t* ids,
+                            const float* sims, size_t kk, const double* created_unix,
+                            const uint32_t* burst, const float* priority,
+                            const eb_dedup_config* cfg, eb_dedup_out* out);
+
+/* dedup::dedup (dedup.rs:160-183): the exact kNN self-join on the engine
+ * (eb_topk, min(k, n - 1) neighbours) followed by eb_dedup_with_neighbors. */
+int eb_dedup(eb_engine* e, const float* x, size_t n, size_t d, const double* created_unix,
+             const uint32_t* burst, const float* priority, const eb_dedup_config* cfg,
+             eb_dedup_out* out);
 
 /* ---------------------------------------------------------------- metrics */
 

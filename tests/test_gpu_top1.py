@@ -237,3 +237,39 @@ def test_assign_only_config_shape(engine, metric):
     check_against_oracle(engine, x, c, metric)
     s1 = engine.stats()
     assert s1["screened_rows"] - s0["screened_rows"] == n
+
+
+def test_a_screen_wait_that_runs_out_is_reported_and_results_stay_exact(engine):
+    """Failure detection without a fault: the test hook makes the screen's
+    first CTA wait, at its second centroid tile, on a device barrier that
+    nothing arrives at. The wait gives up after its limit (2 s); the CTA's
+    copies and products in flight land before it frees its tensor memory and
+    exits; its rows take the exact full scan. The next synchronising call
+    reports the timeout (EB_ERROR), the labels and scores still equal the
+    oracle's, and the engine keeps working."""
+    n, d, k = 3000, 96, 700  # 24 row tiles, three 256-centroid tiles each
+    x = mixture(n, d, 16, 0.5, False, 12)
+    c = contract_centroids(x, d, k)
+    wl, ws = oracle.top1(x.ravel(), d, c.ravel(), oracle.L2)
+    engine.set_screen_mode(2)
+    try:
+        xb, cb, cn = engine.bind(x, d), engine.upload_f32(c), engine.zeros_f32(k)
+        engine.row_norms(cb, k, d, cn)
+        lab, sco = engine.zeros_u32(n), engine.zeros_f32(n)
+        fb0 = engine.stats()["fallback_rows"]
+        assert eb.load().eb_test_screen_dead_wait(engine.h, 1) == eb.OK
+        engine.top1(xb, d, None, range(0, n), cb, cn, k, eb.L2, lab, sco)
+        with pytest.raises(eb.EngineError, match="wait timed out") as err:
+            engine.sync()
+        assert err.value.code == eb.ERROR
+        assert np.array_equal(lab.read(), wl)
+        assert np.array_equal(bits(sco.read()), bits(ws))
+        assert engine.stats()["fallback_rows"] - fb0 >= 128  # CTA 0's row tile
+        # The hook cleared itself: the same call again is clean and exact.
+        lab2, sco2 = engine.zeros_u32(n), engine.zeros_f32(n)
+        engine.top1(xb, d, None, range(0, n), cb, cn, k, eb.L2, lab2, sco2)
+        engine.sync()
+        assert np.array_equal(lab2.read(), wl)
+        assert np.array_equal(bits(sco2.read()), bits(ws))
+    finally:
+        engine.set_screen_mode(1)
