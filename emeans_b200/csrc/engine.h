@@ -284,6 +284,10 @@ void top1_exact(eb_engine* e, const Top1Args& a);
 void top1_dispatch(eb_engine* e, const Top1Args& a, eb_buf* xbuf);
 
 // ---- top1_tc.cu: the tcgen05 screen + exact re-score
+// Parts per row tile of a screen pass over rtiles row tiles, and the screen's
+// estimated length in centroid-tile times for `rows` rows against k centroids.
+int screen_parts(size_t rtiles, int ntiles, int sms);
+size_t screen_tile_times(size_t rows, size_t k, int sms);
 bool top1_screen_supported(eb_engine* e, const Top1Args& a);
 void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf);
 void drop_f16(eb_buf* b);

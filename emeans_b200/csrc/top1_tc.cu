@@ -512,17 +512,25 @@ struct ScreenParams {
   int k;
   int kblocks;         // dp / 32
   int ntiles;          // ceil(k / 256)
+  // Work units: (row tile, part) pairs, unit u = row tile u / parts, part
+  // u % parts, which covers centroid tiles part * tpp .. min(+ tpp, ntiles).
+  // Splitting a row tile's centroid tiles over parts fills the SMs when there
+  // are few row tiles (a training batch's slice on one of several GPUs).
+  int parts;
+  int tpp;             // centroid tiles per part
+  int units;           // ceil(m / 128) * parts
   const int* xexp;     // per staging row
   const float* xnrm;   // per staging row
   const float* cn;     // k squared centroid norms (L2) or null
   const unsigned long long* cinfo;  // the centroid summary of generation cgen
   uint32_t cgen;
   float e_rel, e_abs, e_min;  // bound coefficients (see the header comment)
-  // Candidate lists, one per (half tile, row): half h, entry e of row i at
-  // (h C + e) m + i (id, screened value bits), C = CAP (CAP_TOPK in top-k mode).
+  // Candidate lists, one per (part, half tile, row): list L = 2 part + half,
+  // entry e of row i at (L C + e) m + i (id, screened value bits), C = CAP
+  // (CAP_TOPK in top-k mode; top-k mode has one part).
   uint2* cand;
-  uint32_t* cand_cnt;  // 2 m: entries in use per (half, row), or FALLBACK
-  float* cand_thr;     // 2 m: the final admission threshold per (half, row)
+  uint32_t* cand_cnt;  // 2 parts m: entries in use per (list, row), or FALLBACK
+  float* cand_thr;     // 2 parts m: the final admission threshold per (list, row)
   uint32_t* status;
   // Top-k mode (k_screen<true, true>): each (row, half) keeps its best kk
   // screened values and admits every column within the window of the kk-th.
@@ -594,7 +602,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;  // hi accumulator at column 0, lo at column BN
-  const int total = P.ntiles * P.kblocks;
   if (warp < 4) {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_PRODUCER));
   if (warp == 0) {
@@ -603,8 +610,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // xh, xl (128 x 32) and ch, cl (256 x 32). The ring runs on across tiles.
       int it = 0, issued = 0;
       bool stop = false;
-      for (long rt = blockIdx.x; rt * BM < P.m && !stop; rt += gridDim.x) {
-        for (int t2 = 0; t2 < total; t2++, it++) {
+      for (int u = blockIdx.x; u < P.units && !stop; u += gridDim.x) {
+        const int rt = u / P.parts;
+        const int nt0 = (u % P.parts) * P.tpp, nt1 = min(nt0 + P.tpp, P.ntiles);
+        for (int t2 = nt0 * P.kblocks; t2 < nt1 * P.kblocks; t2++, it++) {
           const int s = it % STAGES;
           if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag)) {
             stop = true;
@@ -634,8 +643,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // MMA issuer; tc counts (row tile, centroid tile) pairs.
       int it = 0, tc = 0;
       bool stop = false;
-      for (long rt = blockIdx.x; rt * BM < P.m && !stop; rt += gridDim.x) {
-        for (int nt = 0; nt < P.ntiles; nt++, tc++) {
+      for (int u = blockIdx.x; u < P.units && !stop; u += gridDim.x) {
+        const int nt0 = (u % P.parts) * P.tpp, nt1 = min(nt0 + P.tpp, P.ntiles);
+        for (int nt = nt0; nt < nt1; nt++, tc++) {
           // Top-1 mode: the epilogue must have read both accumulators of the
           // last tile. Top-k mode: one accumulator per tile, two buffers in
           // turn; the epilogue must have read this buffer's last tile.
@@ -704,12 +714,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float* svs = sv_s + (warp - 4) * 16 * 32 + lane;  // this lane's column of the slab
     int tc = 0;
     bool stop = false;
-    for (long rt = blockIdx.x; rt * BM < P.m; rt += gridDim.x) {
+    for (int u = blockIdx.x; u < P.units; u += gridDim.x) {
+      const long rt = u / P.parts;
+      const int part = u % P.parts;
+      const int nt0 = part * P.tpp, nt1 = min(nt0 + P.tpp, P.ntiles);
+      const int L = 2 * part + hf;  // this (part, half)'s candidate list
       const long i = rt * BM + r;
       const bool live = i < P.m;
       if (stop) {
         // A wait gave up: this CTA's remaining rows go to the exact fallback.
-        if (live) P.cand_cnt[hf * P.m + i] = FALLBACK;
+        if (live) P.cand_cnt[L * P.m + i] = FALLBACK;
         continue;
       }
       const int ex = live ? P.xexp[i] : XEXP_BAD;
@@ -738,7 +752,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool overflow = false;
       uint32_t cnt = 0;  // entries in this (row, half)'s candidate list
       constexpr int LCAP = TOPK ? CAP_TOPK : CAP;
-      uint2* row_list = P.cand + (long)hf * LCAP * P.m + (live ? i : 0);  // entries P.m apart
+      uint2* row_list = P.cand + (long)L * LCAP * P.m + (live ? i : 0);  // entries P.m apart
       // Top-k mode: the best kk screened values so far in slots 0 .. kk - 1,
       // ascending (the kk-th best in slot 0), slots kk .. KMAX - 1 held at +inf.
       float kv[TOPK ? KMAX : 1];
@@ -747,7 +761,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       float kth = -INFINITY;
       const long gid = P.row_gid0 + i;
 
-      for (int nt = 0; nt < P.ntiles; nt++, tc++) {
+      for (int nt = nt0; nt < nt1; nt++, tc++) {
         // Warp-uniform: the TMEM loads below are .sync.aligned.
         const int buf = TOPK ? (tc & 1) : 0;
         const uint32_t use = TOPK ? (uint32_t)(tc >> 1) : (uint32_t)tc;
@@ -956,15 +970,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       }
       if (live) {
-        // With k <= HALF the second half tile holds no centroid at all: its
-        // list is empty and its threshold the identity, not a fallback.
-        const bool no_columns = hf * HALF >= P.k;
+        // A half tile past the last centroid (k <= HALF, or a last part
+        // whose one tile has HALF centroids or fewer) holds no centroid at
+        // all: its list is empty and its threshold the identity, not a
+        // fallback.
+        const bool no_columns = nt0 * BN + hf * HALF >= P.k;
         const bool ok = collect && !stop && !overflow && !*abort_flag &&
                         (TOPK || isfinite(best) || no_columns);
-        if (ok) P.cand_thr[hf * P.m + i] = thr;
-        P.cand_cnt[hf * P.m + i] = ok ? cnt : FALLBACK;
+        if (ok) P.cand_thr[L * P.m + i] = thr;
+        P.cand_cnt[L * P.m + i] = ok ? cnt : FALLBACK;
         if constexpr (TOPK) {
-          float* kvo = P.kvals + (hf * P.m + i) * KMAX;
+          float* kvo = P.kvals + (L * P.m + i) * KMAX;
 #pragma unroll
           for (int a = 0; a < KMAX; a++) kvo[a] = kv[a];
           if (hf == 0) P.roff[i] = off;
@@ -1018,18 +1034,20 @@ __device__ __forceinline__ unsigned long long scan_start_key() {
   return result_key<IP>(IP ? -INFINITY : INFINITY, 0u);
 }
 
-// Each row's candidates (from both half-tile lists) still inside its final
-// window become (row, centroid) pairs; the window is the tighter of the two
-// halves' thresholds, the one of the row's overall best. Rows with none, with
-// more than SURV, or marked for the fallback go to the exact list, whose key
-// starts at the scan's starting point. The row's pair key starts at the
-// identity of its reduction. Launched with 256 threads a block. The first
-// eight entries of each half stay in registers between the counting and the
-// writing pass; the pair slots are reserved with one atomic per block (the
-// per-warp atomics on one counter serialised).
+// Each row's candidates (from its nl = 2 parts lists, one per part and half
+// tile) still inside its final window become (row, centroid) pairs; the
+// window is the tightest of the lists' thresholds, the one of the row's
+// overall best. Rows with none, with more than SURV, or marked for the
+// fallback go to the exact list, whose key starts at the scan's starting
+// point. The row's pair key starts at the identity of its reduction. Launched
+// with 256 threads a block. The first eight entries of the first two lists
+// stay in registers between the counting and the writing pass; the pair slots
+// are reserved with one atomic per block (the per-warp atomics on one counter
+// serialised).
+constexpr int MAX_PARTS = 4;
 template <bool IP>
 __global__ void __launch_bounds__(256) k_collect(
-    long p0, long m, uint32_t k, const uint2* __restrict__ cand,
+    long p0, long m, uint32_t k, int nl, const uint2* __restrict__ cand,
     const uint32_t* __restrict__ cand_cnt, const float* __restrict__ cand_thr,
     uint2* __restrict__ pairs, uint32_t* __restrict__ pair_count,
     unsigned long long* __restrict__ rkey, uint32_t* __restrict__ list,
@@ -1041,11 +1059,11 @@ __global__ void __launch_bounds__(256) k_collect(
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const bool live = i < m;
-  uint32_t cnt[2];
+  uint32_t cnt[2 * MAX_PARTS];
   bool fb = !live;
 #pragma unroll
-  for (int h = 0; h < 2; h++) {
-    cnt[h] = live ? cand_cnt[h * m + i] : 0;
+  for (int h = 0; h < 2 * MAX_PARTS; h++) {
+    cnt[h] = live && h < nl ? cand_cnt[h * m + i] : 0;
     if (cnt[h] == FALLBACK) {
       fb = true;
     } else if (cnt[h] > CAP) {
@@ -1053,16 +1071,19 @@ __global__ void __launch_bounds__(256) k_collect(
       fb = true;
     }
   }
-  if (fb) cnt[0] = cnt[1] = 0;
-  uint32_t ns = 0;
-  float thr = 0.0f;
-  uint2 first[2][8];
-  if (!fb) {
-    const float t0 = cand_thr[i], t1 = cand_thr[m + i];
-    thr = IP ? fmaxf(t0, t1) : fminf(t0, t1);
-  }
+  if (fb)
 #pragma unroll
-  for (int h = 0; h < 2; h++) {
+    for (int h = 0; h < 2 * MAX_PARTS; h++) cnt[h] = 0;
+  uint32_t ns = 0;
+  float thr = IP ? -INFINITY : INFINITY;
+  uint2 first[2][8];
+  if (!fb)
+    for (int h = 0; h < nl; h++) {
+      const float th = cand_thr[h * m + i];
+      thr = IP ? fmaxf(thr, th) : fminf(thr, th);
+    }
+#pragma unroll
+  for (int h = 0; h < 2 * MAX_PARTS; h++) {
     const uint2* lst = cand + (long)h * CAP * m + i;
     // Loads in batches of eight, so that they are in flight together.
     for (uint32_t e0 = 0; e0 < cnt[h]; e0 += 8) {
@@ -1075,11 +1096,14 @@ __global__ void __launch_bounds__(256) k_collect(
         const float sv = __uint_as_float(en[u].y);
         if (en[u].x >= k) fb = true;
         ns += IP ? (sv >= thr) : (sv <= thr);
-        if (e0 == 0) first[h][u] = en[u];
+        if (h < 2 && e0 == 0) first[h < 2 ? h : 0][u] = en[u];
       }
     }
   }
-  if (fb && live && cnt[0] + cnt[1] > 0) atomicOr(status, ST_BAD_STATE);
+  uint32_t listed_entries = 0;
+#pragma unroll
+  for (int h = 0; h < 2 * MAX_PARTS; h++) listed_entries += cnt[h];
+  if (fb && live && listed_entries > 0) atomicOr(status, ST_BAD_STATE);
   fb = fb || ns == 0 || ns > SURV;
   const bool listed = live && fb;
   const uint32_t np = live && !fb ? ns : 0;
@@ -1118,14 +1142,15 @@ __global__ void __launch_bounds__(256) k_collect(
   uint32_t w = wbase[warp] + incl - np;
   if (np) {
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
+    for (int h = 0; h < 2 * MAX_PARTS; h++) {
       const uint2* lst = cand + (long)h * CAP * m + i;
       for (uint32_t e0 = 0; e0 < cnt[h]; e0 += 8) {
         uint2 en[8];
 #pragma unroll
         for (int u = 0; u < 8; u++)
-          en[u] = e0 == 0 ? first[h][u]
-                          : (e0 + u < cnt[h] ? lst[(e0 + u) * m] : make_uint2(0u, __float_as_uint(NAN)));
+          en[u] = (h < 2 && e0 == 0)
+                      ? first[h < 2 ? h : 0][u]
+                      : (e0 + u < cnt[h] ? lst[(e0 + u) * m] : make_uint2(0u, __float_as_uint(NAN)));
 #pragma unroll
         for (int u = 0; u < 8; u++) {
           const float sv = __uint_as_float(en[u].y);
@@ -1134,8 +1159,8 @@ __global__ void __launch_bounds__(256) k_collect(
       }
     }
   }
-  const uint32_t nl = __reduce_add_sync(0xFFFFFFFFu, listed ? 1u : 0u);
-  if (lane == 0 && nl) atomicAdd(&counters[1], (unsigned long long)nl);
+  const uint32_t nlisted = __reduce_add_sync(0xFFFFFFFFu, listed ? 1u : 0u);
+  if (lane == 0 && nlisted) atomicAdd(&counters[1], (unsigned long long)nlisted);
 }
 
 // Exact FMA chain of row x against centroid c over d columns, loads kept
@@ -1819,6 +1844,7 @@ void launch_screen(eb_engine* e, unsigned grid, const CUtensorMap& ah, const CUt
 
 // Scratch of the exact stage of one pass of m rows.
 struct ExactScratch {
+  int nl;  // candidate lists per row (2 per part)
   const uint2* cand;
   const uint32_t* cand_cnt;
   const float* cand_thr;
@@ -1838,7 +1864,7 @@ void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const ExactS
   unsigned long long* counters = e->counters();
   // pair_count and list_count were zeroed by the screen; k_collect zeroes bad.
   const unsigned rgrid = (unsigned)((m + 255) / 256);
-  launch_pdl(e, k_collect<IP>, rgrid, 256, 0, c0, m, (uint32_t)a.k, S.cand, S.cand_cnt, S.cand_thr,
+  launch_pdl(e, k_collect<IP>, rgrid, 256, 0, c0, m, (uint32_t)a.k, S.nl, S.cand, S.cand_cnt, S.cand_thr,
                                               S.pairs, S.pair_count, S.rkey, S.list, S.list_count,
                                               S.lkey, S.bad, counters, e->d_status);
   EB_LAUNCH("screen collect");
@@ -1911,6 +1937,35 @@ uint32_t convert_centroids(eb_engine* e, const float* c, size_t k, size_t d, siz
 
 }  // namespace
 
+// Parts per row tile: the count (1, 2 or 4, at most the centroid tiles) that
+// minimises the screen's length in centroid-tile times, waves of units times
+// tiles per part (a unit per SM at a time); ties keep fewer parts. With many
+// row tiles every SM is busy at one part; a slice of a few dozen row tiles
+// (a training batch split over GPUs, or a pass's ragged last wave) spreads
+// each row tile's centroid tiles over several SMs.
+int screen_parts(size_t rtiles, int ntiles, int sms) {
+  int best = 1;
+  size_t best_t = (size_t)-1;
+  for (int p = 1; p <= MAX_PARTS && p <= ntiles; p *= 2) {
+    const int tpp = (ntiles + p - 1) / p;
+    if ((ntiles + tpp - 1) / tpp != p) continue;  // a part would be empty
+    const size_t t = (rtiles * (size_t)p + (size_t)sms - 1) / (size_t)sms * (size_t)tpp;
+    if (t < best_t) {
+      best_t = t;
+      best = p;
+    }
+  }
+  return best;
+}
+
+size_t screen_tile_times(size_t rows, size_t k, int sms) {
+  const size_t rtiles = (rows + BM - 1) / BM;
+  const int ntiles = (int)((k + BN - 1) / BN);
+  const int p = screen_parts(rtiles, ntiles, sms);
+  const size_t tpp = (size_t)((ntiles + p - 1) / p);
+  return (rtiles * (size_t)p + (size_t)sms - 1) / (size_t)sms * tpp;
+}
+
 bool top1_screen_supported(eb_engine* e, const Top1Args& a) {
   if (e->screen_mode == 0) return false;
   if (a.d > 16384 || a.k > 0x7FFFFFFF) return false;
@@ -1946,9 +2001,15 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   __half* xl = e->scratch_get<__half>("tc_xl", chunk * dp);
   int* xexp = e->scratch_get<int>("tc_xexp", chunk);
   float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
-  uint2* cand = e->scratch_get<uint2>("tc_cand", 2 * chunk * CAP);
-  uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", 2 * chunk);
-  float* cand_thr = e->scratch_get<float>("tc_thr", 2 * chunk);
+  // Parts per row tile for each pass (the pass's row tiles decide them).
+  const int ntiles = (int)((k + BN - 1) / BN);
+  int max_parts = 1;
+  for (size_t c0 = a.r0; c0 < a.r1; c0 += chunk)
+    max_parts = std::max(max_parts, screen_parts((std::min(chunk, a.r1 - c0) + BM - 1) / BM,
+                                                 ntiles, e->num_sms));
+  uint2* cand = e->scratch_get<uint2>("tc_cand", 2 * (size_t)max_parts * chunk * CAP);
+  uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", 2 * (size_t)max_parts * chunk);
+  float* cand_thr = e->scratch_get<float>("tc_thr", 2 * (size_t)max_parts * chunk);
   uint32_t* list = e->scratch_get<uint32_t>("tc_list", chunk);
   uint32_t* list_count = e->scratch_get<uint32_t>("tc_list_count", 4);
   uint2* pairs = e->scratch_get<uint2>("tc_pairs", chunk * SURV);
@@ -1958,13 +2019,13 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   float* xn_pos = e->scratch_get<float>("tc_xn_pos", chunk);
   unsigned long long* lkey = e->scratch_get<unsigned long long>("tc_lkey", chunk);
   float* lxn = e->scratch_get<float>("tc_lxn", chunk);
-  const ExactScratch S{cand, cand_cnt, cand_thr, pairs, pair_count, rkey, bad, xn_pos, list,
-                       list_count, lkey, lxn};
+  ExactScratch S{1, cand, cand_cnt, cand_thr, pairs, pair_count, rkey, bad, xn_pos, list,
+                 list_count, lkey, lxn};
 
   ScreenParams P{};
   P.k = (int)k;
   P.kblocks = (int)(dp / BKH);
-  P.ntiles = (int)((k + BN - 1) / BN);
+  P.ntiles = ntiles;
   P.cn = a.cnorm;
   P.cinfo = cinfo;
   P.cgen = cgen;
@@ -2034,8 +2095,13 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
     const CUtensorMap mapAh = make_map(ah, m, dp, BM);
     const CUtensorMap mapAl = make_map(al, m, dp, BM);
     P.m = (long)m;
-    // Persistent: at most one CTA per SM, each looping over row tiles.
-    const unsigned grid = (unsigned)std::min<size_t>((m + BM - 1) / BM, (size_t)e->num_sms);
+    const size_t rtiles = (m + BM - 1) / BM;
+    P.parts = screen_parts(rtiles, ntiles, e->num_sms);
+    P.tpp = (ntiles + P.parts - 1) / P.parts;
+    P.units = (int)(rtiles * P.parts);
+    S.nl = 2 * P.parts;
+    // Persistent: at most one CTA per SM, each looping over work units.
+    const unsigned grid = (unsigned)std::min<size_t>((size_t)P.units, (size_t)e->num_sms);
     cudaEvent_t ev_end = nullptr;
     if (e->time_screen) {
       if (e->screen_ev_used == e->screen_ev.size()) {
@@ -2113,6 +2179,8 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
   P.k = (int)n;
   P.kblocks = (int)(dp / BKH);
   P.ntiles = (int)((n + BN - 1) / BN);
+  P.parts = 1;  // the top-k collect merges the two halves' best-kk lists
+  P.tpp = P.ntiles;
   P.cn = nullptr;
   P.cinfo = cinfo;
   P.cgen = cgen;
@@ -2139,6 +2207,7 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
     const CUtensorMap mapAh = make_map(xh, mc, dp, BM);
     const CUtensorMap mapAl = make_map(xl, mc, dp, BM);
     P.m = (long)mc;
+    P.units = (int)((mc + BM - 1) / BM);
     P.xexp = xexp;
     P.xnrm = xnrm;
     P.row_gid0 = (long)c0;

@@ -235,17 +235,17 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
         row_norms(e, dpos.f(), k, d, readout.f());
       // In a group, rank q scores positions [b + q s, b + (q + 1) s) of the
       // batch and the slices are all-gathered; alone, the whole batch. By
-      // default (group_shard 0) a batch is split only when that cuts the
-      // screen's waves of row tiles: a batch of one wave or less takes as
-      // long on one GPU as on several, so every rank scores all of it and
-      // nothing is exchanged (the same result either way).
+      // default (group_shard 0) a batch is split only when that shortens
+      // the screen (its length in centroid-tile times, the slice's row tiles
+      // spread over the SMs with their centroid tiles in parts); otherwise
+      // every rank scores all of it and nothing is exchanged (the same
+      // result either way).
       const size_t sh = (end - b + e->world - 1) / e->world;
-      auto waves = [&](size_t rows) {
-        return ((rows + 127) / 128 + (size_t)e->num_sms - 1) / (size_t)e->num_sms;
-      };
       const bool split_batch =
-          e->world > 1 && (reduce_mode || e->group_shard == 1 ||
-                           (e->group_shard == 0 && waves(sh) < waves(end - b)));
+          e->world > 1 &&
+          (reduce_mode || e->group_shard == 1 ||
+           (e->group_shard == 0 &&
+            screen_tile_times(sh, k, e->num_sms) < screen_tile_times(end - b, k, e->num_sms)));
       const size_t lo = split_batch ? std::min(b + (size_t)e->rank * sh, end) : b;
       const size_t hi = split_batch ? std::min(lo + sh, end) : end;
       for (size_t c0 = lo; c0 < hi; c0 += chunk) {

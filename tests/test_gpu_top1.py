@@ -273,3 +273,24 @@ def test_a_screen_wait_that_runs_out_is_reported_and_results_stay_exact(engine):
         assert np.array_equal(bits(sco2.read()), bits(ws))
     finally:
         engine.set_screen_mode(1)
+
+
+@pytest.mark.parametrize("m,k", [(6000, 1024), (600, 1024), (3000, 700), (2000, 1300),
+                                 (9000, 1024), (300, 257)])
+@pytest.mark.parametrize("metric", [eb.L2, eb.IP])
+def test_row_tiles_split_over_centroid_parts(engine, m, k, metric):
+    """Calls with few row tiles spread each row tile's centroid tiles over 2
+    or 4 parts (each part keeps its own candidate lists, merged by the
+    collect step); uneven parts (3 and 6 centroid tiles) included. Labels and
+    scores stay bit-equal to the oracle."""
+    d = 96
+    x = mixture(m, d, 20, 0.4, metric == eb.IP, m + k)
+    c = contract_centroids(x, d, k)
+    engine.set_screen_mode(2)
+    try:
+        gl, gs = run_top1(engine, x, c, metric)
+    finally:
+        engine.set_screen_mode(1)
+    wl, ws = oracle.top1(x.ravel(), d, c.ravel(), metric)
+    assert np.array_equal(gl, wl)
+    assert np.array_equal(bits(gs), bits(ws))
