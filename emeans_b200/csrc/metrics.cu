@@ -73,7 +73,8 @@ __global__ void __launch_bounds__(128) k_sum64(const float* __restrict__ x, int 
 __global__ void k_cluster_prep(const double* __restrict__ sums, const uint32_t* __restrict__ live,
                                const uint32_t* __restrict__ counts, int d, long keff,
                                float* __restrict__ c32, double* __restrict__ sq,
-                               double* __restrict__ size, double* __restrict__ meanT) {
+                               double* __restrict__ size, double* __restrict__ meanT,
+                               float* __restrict__ inv) {
   pdl_wait();
   const long s = blockIdx.x;
   const long j = live[s];
@@ -89,7 +90,73 @@ __global__ void k_cluster_prep(const double* __restrict__ sums, const uint32_t* 
     for (int t = 0; t < d; t++) a = __dadd_rn(a, __dmul_rn(row[t], row[t]));
     sq[s] = a;
     size[s] = nj;
+    inv[s] = 1.0f / (float)nj;  // the tensor-core product's column weight
   }
+}
+
+// The per-row terms with the tensor-core product (screen_products): vmax =
+// max over s != o of x_i . c32_s / n_s from it; the own cluster's product
+// x_i . c32_o as one FP32 FMA chain in column order (the distance and the
+// silhouette's a cancel it against the row's norm, so it stays the SIMT
+// kernel's exact chain) and the row's f64 sum of squares in column order;
+// then the same formulas as k_silhouette's epilogue. One warp per 32 rows:
+// each 32-column slice of the warp's rows is read coalesced (a row per load,
+// a column per lane) into shared memory, and each lane runs its own row's
+// chains.
+__global__ void __launch_bounds__(128) k_row_terms(
+    const float* __restrict__ x, long n, int d, const uint32_t* __restrict__ labels,
+    const uint32_t* __restrict__ slot, const float* __restrict__ c32,
+    const float* __restrict__ vmax_g, const double* __restrict__ size,
+    const double* __restrict__ sq, long keff, double* __restrict__ sil, double* __restrict__ obj,
+    double* __restrict__ dist, double* __restrict__ xx_out) {
+  pdl_wait();
+  __shared__ float tile[4][32][33];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long r0 = ((long)blockIdx.x * 4 + w) * 32;
+  if (r0 >= n) return;
+  float(*t)[33] = tile[w];
+  const long myrow = min(r0 + lane, n - 1);
+  const float* crow = c32 + (long)slot[labels[myrow]] * d;
+  double xv = -0.0;
+  float gf = 0.0f;
+  for (int c0 = 0; c0 < d; c0 += 32) {
+    float v[32];
+#pragma unroll
+    for (int r = 0; r < 32; r++) {
+      const long row = r0 + r;
+      v[r] = (row < n && c0 + lane < d) ? __ldg(x + row * d + c0 + lane) : 0.0f;
+    }
+#pragma unroll
+    for (int r = 0; r < 32; r++) t[r][lane] = v[r];
+    __syncwarp();
+    const int cmax = min(32, d - c0);
+    for (int c = 0; c < cmax; c++) {
+      const float a = t[lane][c];
+      const double q = (double)a;
+      xv = __dadd_rn(xv, __dmul_rn(q, q));
+      gf = __fmaf_rn(a, __ldg(crow + c0 + c), gf);
+    }
+    __syncwarp();
+  }
+  const long row = r0 + lane;
+  if (row >= n) return;
+  const uint32_t o = slot[labels[row]];
+  const double na = size[o], sqo = sq[o];
+  const double g = (double)gf;
+  const double t1 = __ddiv_rn(__dmul_rn(2.0, g), na);
+  const double t2 = __ddiv_rn(sqo, __dmul_rn(na, na));
+  dist[row] = __dsqrt_rn(fmax(__dadd_rn(__dsub_rn(xv, t1), t2), 0.0));
+  const double cosc = __ddiv_rn(g, fmax(__dsqrt_rn(sqo), 1e-30));
+  obj[row] = __dsub_rn(2.0, __dmul_rn(2.0, cosc));
+  double sv = 0.0;
+  if (keff >= 2 && na >= 2.0) {
+    const double a = __dsub_rn(1.0, __ddiv_rn(__dsub_rn(g, xv), __dsub_rn(na, 1.0)));
+    const double bb = __dsub_rn(1.0, (double)vmax_g[row]);
+    const double m = fmax(a, bb);
+    sv = m > 0.0 ? __ddiv_rn(__dsub_rn(bb, a), m) : 0.0;
+  }
+  sil[row] = sv;
+  xx_out[row] = xv;
 }
 
 // Per row i with live cluster o = slot[labels[i]] (metrics.rs:160-185):
@@ -411,21 +478,38 @@ void internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uin
   }
   const size_t keff = live.size();
   Tmp dlive(e, keff * 4), dslot(e, k * 4), c32(e, keff * d * 4), sq(e, keff * 8),
-      size(e, keff * 8), mean(e, keff * d * 8);
+      size(e, keff * 8), mean(e, keff * d * 8), inv(e, keff * 4);
   h2d(e, dlive.p, live.data(), keff * 4, e->stream);
   h2d(e, dslot.p, slot.data(), k * 4, e->stream);
   launch_pdl(e, k_cluster_prep, (unsigned)keff, 128, 0, sums.as<double>(), dlive.as<uint32_t>(),
              cnt.as<uint32_t>(), (int)d, (long)keff, c32.as<float>(), sq.as<double>(),
-             size.as<double>(), mean.as<double>());
+             size.as<double>(), mean.as<double>(), inv.as<float>());
   EB_LAUNCH("metrics cluster prep");
 
   Tmp sil(e, n * 8), obj(e, n * 8), dist(e, n * 8), xx(e, n * 8);
-  const unsigned tiles = nblocks(n, BM);
-  const unsigned grid = std::min<unsigned>(tiles, (unsigned)e->num_sms * 4);
-  launch_pdl(e, k_silhouette, grid, NT, 0, xd, (long)n, (int)d, lab.as<uint32_t>(),
-             dslot.as<uint32_t>(), c32.as<float>(), size.as<double>(), sq.as<double>(),
-             (long)keff, sil.as<double>(), obj.as<double>(), dist.as<double>(), xx.as<double>());
-  EB_LAUNCH("metrics silhouette");
+  // The n x k_eff product: on the tensor cores (the screen's split FP16
+  // products in product mode) for calls large enough to pay, or always in
+  // screen mode 2; FP32 FMA chains on the SIMT cores otherwise.
+  const bool tensor = e->screen_mode == 2 ||
+                      (e->screen_mode == 1 && n >= 4096 && keff >= 64 && d >= 16 && d <= 16384);
+  if (tensor) {
+    Tmp vmax(e, n * 4);
+    screen_products(e, xd, n, d, reuse ? e->bound : nullptr, lab.as<uint32_t>(),
+                    dslot.as<uint32_t>(), c32.as<float>(), inv.as<float>(), keff,
+                    vmax.as<float>());
+    launch_pdl(e, k_row_terms, nblocks(n, 128), 128, 0, xd, (long)n, (int)d, lab.as<uint32_t>(),
+               dslot.as<uint32_t>(), c32.as<float>(), vmax.as<float>(), size.as<double>(),
+               sq.as<double>(), (long)keff, sil.as<double>(), obj.as<double>(),
+               dist.as<double>(), xx.as<double>());
+    EB_LAUNCH("metrics row terms");
+  } else {
+    const unsigned tiles = nblocks(n, BM);
+    const unsigned grid = std::min<unsigned>(tiles, (unsigned)e->num_sms * 4);
+    launch_pdl(e, k_silhouette, grid, NT, 0, xd, (long)n, (int)d, lab.as<uint32_t>(),
+               dslot.as<uint32_t>(), c32.as<float>(), size.as<double>(), sq.as<double>(),
+               (long)keff, sil.as<double>(), obj.as<double>(), dist.as<double>(), xx.as<double>());
+    EB_LAUNCH("metrics silhouette");
+  }
 
   Tmp grand_d(e, d * 8);
   launch_pdl(e, k_grand, nblocks(d, 128), 128, 0, sums.as<double>(), dlive.as<uint32_t>(),

@@ -544,13 +544,22 @@ struct ScreenParams {
   // the screen's first thread.
   uint32_t* zero0;
   uint32_t* zero1;
+  // Product mode (k_screen<true, false, true>, the internal scores' n x k
+  // product): each row's own column pslot[plabels[prow0 + i]], per column the
+  // weight pinv (1 / cluster size), and per (list, row) the largest weighted
+  // product over the other columns (pmax, in accumulator units).
+  const uint32_t* plabels;
+  const uint32_t* pslot;
+  long prow0;
+  const float* pinv;
+  float* pmax;
   // Failure-detection test (eb_test_screen_dead_wait): CTA 0's epilogue waits
   // for its second tile on a barrier that nothing arrives at, so that the
   // wait runs out and the give-up path runs. 0 in normal use.
   int dead_wait;
 };
 
-template <bool IP, bool TOPK = false>
+template <bool IP, bool TOPK = false, bool PROD = false>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_screen(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
              const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
@@ -722,8 +731,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const long i = rt * BM + r;
       const bool live = i < P.m;
       if (stop) {
-        // A wait gave up: this CTA's remaining rows go to the exact fallback.
-        if (live) P.cand_cnt[L * P.m + i] = FALLBACK;
+        // A wait gave up: this CTA's remaining rows go to the exact fallback
+        // (product mode: no result; the call reports the timeout).
+        if (live) {
+          if (PROD)
+            P.pmax[L * P.m + i] = NAN;
+          else
+            P.cand_cnt[L * P.m + i] = FALLBACK;
+        }
         continue;
       }
       const int ex = live ? P.xexp[i] : XEXP_BAD;
@@ -747,6 +762,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       if (!isfinite(off)) fallback = true;
       const bool collect = live && !fallback;
+      // Product mode: this row's own column and the running maximum.
+      const long own_col = PROD && live ? (long)P.pslot[P.plabels[P.prow0 + i]] : -1;
+      float pm = -INFINITY;
       float best = IP ? -INFINITY : INFINITY;
       float thr = best;
       bool overflow = false;
@@ -778,13 +796,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         tc_fence_after();
         const int col0 = nt * BN + hf * HALF;  // first centroid of this warp's half tile
-        if (!IP) {
-          // This half tile's squared centroid norms, staged by each warp for
-          // itself (no barrier across warps, so a timed-out wait strands no warp).
+        if (!IP || PROD) {
+          // This half tile's squared centroid norms (product mode: the
+          // columns' weights), staged by each warp for itself (no barrier
+          // across warps, so a timed-out wait strands no warp).
+          const float* src = PROD ? P.pinv : P.cn;
 #pragma unroll
           for (int u = 0; u < HALF / 32; u++) {
             const int c = u * 32 + lane;
-            cns[c] = col0 + c < P.k ? __ldg(P.cn + col0 + c) : 0.0f;
+            cns[c] = col0 + c < P.k ? __ldg(src + col0 + c) : 0.0f;
           }
           __syncwarp();
         }
@@ -831,6 +851,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // or acc[0] in top-k mode).
         auto score_group = [&](const int g) {
           const uint32_t(&h)[16] = acc[TOPK ? 0 : g];
+          if constexpr (PROD) {
+            // The largest weighted product of the columns other than the own.
+            const long cb = col0 + g * 16;
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+              if (cb + j != own_col && cb + j < P.k)
+                pm = fmaxf(pm, __uint_as_float(h[j]) * cns[g * 16 + j]);
+            return;
+          }
           float s[16];
           if constexpr (TOPK) {
             // Inner product: the accumulator is the screened value.
@@ -969,7 +998,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         }
       }
-      if (live) {
+      if (PROD) {
+        if (live) P.pmax[L * P.m + i] = collect && !stop ? pm : NAN;
+      } else if (live) {
         // A half tile past the last centroid (k <= HALF, or a last part
         // whose one tile has HALF centroids or fewer) holds no centroid at
         // all: its list is empty and its threshold the identity, not a
@@ -1759,6 +1790,35 @@ __global__ void k_scatter_topk(const uint32_t* __restrict__ list, long L, int kk
   sims[o] = tsims[u];
 }
 
+// ---------------------------------------------------------------- product stage
+
+// Product mode: each row's largest weighted product over the columns other
+// than its own (the maximum over its lists), unscaled by the row's and the
+// centroids' powers of two (exact). Rows or centroids with non-finite
+// values, or a screen that gave up: NaN.
+__global__ void k_prod_finish(long p0, long m, int nl, const int* __restrict__ xexp,
+                              const unsigned long long* __restrict__ cinfo, uint32_t cgen,
+                              const float* __restrict__ pmax, float* __restrict__ vmax_out) {
+  pdl_wait();
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= m) return;
+  int ec = 0;
+  frexpf(__uint_as_float(cinfo_word(cinfo, 0, cgen)), &ec);
+  const int ex = xexp[i];
+  float vm = NAN;
+  if (ex != XEXP_BAD && cinfo_word(cinfo, 2, cgen) == 0) {
+    vm = -INFINITY;
+    bool bad = false;
+    for (int h = 0; h < nl; h++) {
+      const float v = pmax[(long)h * m + i];
+      bad = bad || isnan(v);
+      vm = fmaxf(vm, v);
+    }
+    vm = bad ? NAN : ldexpf(vm, ex + ec - 28);
+  }
+  vmax_out[p0 + i] = vm;
+}
+
 // ---------------------------------------------------------------- host side
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1792,11 +1852,11 @@ CUtensorMap make_map(const void* base, size_t rows, size_t dp, uint32_t box_rows
 }
 
 // Dynamic shared memory limits are per-device, per-kernel attributes.
-template <bool IP, bool TOPK>
+template <bool IP, bool TOPK, bool PROD = false>
 void set_smem(int device) {
-  static uint64_t done = 0;  // one instance per kernel: IP, TOPK are template parameters
+  static uint64_t done = 0;  // one instance per kernel: the template parameters
   if (!(done >> device & 1)) {
-    EB_CUDA(cudaFuncSetAttribute(k_screen<IP, TOPK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    EB_CUDA(cudaFuncSetAttribute(k_screen<IP, TOPK, PROD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)SMEM_BYTES));
     done |= 1ull << device;
   }
@@ -1835,11 +1895,11 @@ void set_list_smem(int device) {
   }
 }
 
-template <bool IP, bool TOPK = false>
+template <bool IP, bool TOPK = false, bool PROD = false>
 void launch_screen(eb_engine* e, unsigned grid, const CUtensorMap& ah, const CUtensorMap& al,
                    const CUtensorMap& bh, const CUtensorMap& bl, const ScreenParams& P) {
-  set_smem<IP, TOPK>(e->device);
-  launch_pdl(e, k_screen<IP, TOPK>, grid, NTHREADS, SMEM_BYTES, ah, al, bh, bl, P);
+  set_smem<IP, TOPK, PROD>(e->device);
+  launch_pdl(e, k_screen<IP, TOPK, PROD>, grid, NTHREADS, SMEM_BYTES, ah, al, bh, bl, P);
 }
 
 // Scratch of the exact stage of one pass of m rows.
@@ -2251,6 +2311,91 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
   }
   e->stats.screened_rows += m;
   return true;
+}
+
+// The internal scores' n x k_eff product on the tensor cores (the screen in
+// product mode): for each row i of x (n x d, f32 on the device) with own
+// column slot[labels[i]], vmax_out[i] = the largest x_i . c_s * inv[s] over
+// s != own, from the split FP16 products (xh ch + xh cl + xl ch, FP32
+// accumulation). The bound set's split copy is read in place when xbuf holds
+// one.
+void screen_products(eb_engine* e, const float* x, size_t n, size_t d, eb_buf* xbuf,
+                     const uint32_t* labels, const uint32_t* slot, const float* c,
+                     const float* inv, size_t k, float* vmax_out) {
+  if (n == 0) return;
+  const size_t dp = (d + BKH - 1) / BKH * BKH;
+  const size_t wave = (size_t)e->num_sms * BM;
+  const size_t chunk = std::min(n, PASS_WAVES * wave);
+  float e_rel, e_abs, e_min;
+  screen_bound(d, e_rel, e_abs, e_min);
+  unsigned long long* cinfo = e->scratch_get<unsigned long long>("tc_cinfo", 4, true);
+  __half* ch = e->scratch_get<__half>("tc_ch", k * dp);
+  __half* cl = e->scratch_get<__half>("tc_cl", k * dp);
+  const uint32_t cgen = convert_centroids(e, c, k, d, dp, cinfo, ch, cl);
+  const CUtensorMap mapBh = make_map(ch, k, dp, BN);
+  const CUtensorMap mapBl = make_map(cl, k, dp, BN);
+  const int ntiles = (int)((k + BN - 1) / BN);
+  int max_parts = 1;
+  for (size_t c0 = 0; c0 < n; c0 += chunk)
+    max_parts = std::max(max_parts, screen_parts((std::min(chunk, n - c0) + BM - 1) / BM,
+                                                 ntiles, e->num_sms));
+  const unsigned wpb = 8;
+  __half* xh = e->scratch_get<__half>("tc_xh", chunk * dp);
+  __half* xl = e->scratch_get<__half>("tc_xl", chunk * dp);
+  int* xexp = e->scratch_get<int>("tc_xexp", chunk);
+  float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
+  float* pmax = e->scratch_get<float>("pr_max", 2 * (size_t)max_parts * chunk);
+  Fp16Copy* cache = nullptr;
+  if (xbuf && xbuf->f16 && xbuf->f16->version == xbuf->version && xbuf->f16->n == n &&
+      xbuf->f16->d == d)
+    cache = xbuf->f16;
+
+  ScreenParams P{};
+  P.k = (int)k;
+  P.kblocks = (int)(dp / BKH);
+  P.ntiles = ntiles;
+  P.cinfo = cinfo;
+  P.cgen = cgen;
+  P.e_rel = e_rel;
+  P.e_abs = e_abs;
+  P.e_min = e_min;
+  P.status = e->d_status;
+  P.plabels = labels;
+  P.pslot = slot;
+  P.pinv = inv;
+  P.pmax = pmax;
+  for (size_t c0 = 0; c0 < n; c0 += chunk) {
+    const size_t m = std::min(chunk, n - c0);
+    const __half *ah = xh, *al = xl;
+    const int* pe = xexp;
+    if (cache) {
+      ah = cache->xh + c0 * dp;
+      al = cache->xl + c0 * dp;
+      pe = cache->xexp + c0;
+      P.xexp = pe;
+      P.xnrm = cache->xnrm + c0;
+    } else {
+      launch_pdl(e, k_prep_rows, (unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, x, (long)n,
+                 (int)d, (int)dp, nullptr, (long)c0, (long)m, xh, xl, xexp, xnrm, e->d_status);
+      EB_LAUNCH("product row prep");
+      P.xexp = xexp;
+      P.xnrm = xnrm;
+    }
+    const CUtensorMap mapAh = make_map(ah, m, dp, BM);
+    const CUtensorMap mapAl = make_map(al, m, dp, BM);
+    P.m = (long)m;
+    P.prow0 = (long)c0;
+    const size_t rtiles = (m + BM - 1) / BM;
+    P.parts = screen_parts(rtiles, ntiles, e->num_sms);
+    P.tpp = (ntiles + P.parts - 1) / P.parts;
+    P.units = (int)(rtiles * P.parts);
+    const unsigned grid = (unsigned)std::min<size_t>((size_t)P.units, (size_t)e->num_sms);
+    launch_screen<true, false, true>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
+    EB_LAUNCH("product screen");
+    launch_pdl(e, k_prod_finish, (unsigned)((m + 255) / 256), 256, 0, (long)c0, (long)m,
+               2 * P.parts, pe, cinfo, cgen, pmax, vmax_out);
+    EB_LAUNCH("product finish");
+  }
 }
 
 }  // namespace eb

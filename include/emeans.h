@@ -14,9 +14,11 @@
  * Differences, by design:
  *  - `backend` NULL (and a config without "backend") selects this library's
  *    one backend, the B200 engine on device EMEANS_B200_DEVICE (environment,
- *    default 0); the reference's default is "cpu". "cuda", "cuda-fused" and
- *    "b200" name it too; the reference's other backend names are
- *    EMEANS_ERROR ("not in this library").
+ *    default 0). "cuda", "cuda-fused" and "b200" name it too, and so do
+ *    "cpu" (the reference's default, its fused kernel on x86_64) and
+ *    "cpu-fused": the engine returns that kernel's results bit for bit. The
+ *    reference's other backend names (other float orders) are EMEANS_ERROR
+ *    ("not in this library").
  *  - There is no CPU fallback: with no usable GPU, every call that computes
  *    is EMEANS_ERROR.
  *  - Result JSON numbers are written with 17 significant digits (the same

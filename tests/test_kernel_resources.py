@@ -72,7 +72,8 @@ def test_screen_and_pairs_use_no_local_memory():
     found = _local_memory("top1_tc.cu")
     screens = {k: v for k, v in found.items() if "k_screen" in k}
     pairs = {k: v for k, v in found.items() if "k_pairsILb" in k}
-    assert len(screens) == 3, sorted(found)
+    # top-1 L2, top-1 IP, top-k, and the internal scores' product mode
+    assert len(screens) == 4, sorted(found)
     assert pairs, sorted(found)
     for name, (stack, st, ld) in {**screens, **pairs}.items():
         assert stack == 0 and st == 0 and ld == 0, (name, stack, st, ld)

@@ -4,9 +4,11 @@ CPU (the reference test's tolerance, relative 1e-5), and the device path
 (eb_internal_scores) against the oracle on a GPU.
 
 The n x k_eff product is FP32 on both sides in different addition orders (FMA
-chains on the device, the BLAS order in the oracle, the gemm crate's in the
-reference), so the scores agree to rounding: relative 1e-6 here. Counts and
-k_eff are exact."""
+chains on the device's SIMT path, split FP16 products with FP32 accumulation
+on its tensor-core path, the BLAS order in the oracle, the gemm crate's in the
+reference), so the scores agree to rounding: relative 1e-6 here, on both
+device paths (screen mode 0: SIMT; 2: tensor cores). Counts and k_eff are
+exact."""
 import json
 import os
 
@@ -73,8 +75,10 @@ def check(got, want, rel=1e-6):
 
 
 @pytest.mark.gpu
-def test_device_matches_oracle_and_scikit_learn_on_fixtures():
+@pytest.mark.parametrize("mode", [0, 2], ids=["simt", "tensor"])
+def test_device_matches_oracle_and_scikit_learn_on_fixtures(mode):
     with eb.Engine(0) as e:
+        e.set_screen_mode(mode)
         for c, x in fixtures():
             got = e.internal_scores(x, c["d"], c["labels"], c["k"])
             check(got, oracle_scores(x, c["d"], c["labels"], c["k"]))
@@ -83,8 +87,10 @@ def test_device_matches_oracle_and_scikit_learn_on_fixtures():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("n,d,k", [(1000, 64, 17), (777, 33, 50), (4096, 96, 130), (130, 8, 3)])
-def test_device_matches_oracle(n, d, k):
+@pytest.mark.parametrize("mode", [0, 2], ids=["simt", "tensor"])
+@pytest.mark.parametrize("n,d,k", [(1000, 64, 17), (777, 33, 50), (4096, 96, 130), (130, 8, 3),
+                                   (3000, 48, 700)])
+def test_device_matches_oracle(n, d, k, mode):
     rng = np.random.default_rng(n + d + k)
     x = unit_rows(rng, n, d)
     c = unit_rows(rng, k, d)
@@ -97,6 +103,7 @@ def test_device_matches_oracle(n, d, k):
     # square root of a cancellation of FP32 products, whose value depends on
     # the product's addition order; Davies-Bouldin would compare those.)
     with eb.Engine(0) as e:
+        e.set_screen_mode(mode)
         check(e.internal_scores(x, d, lab, k), oracle_scores(x, d, lab, k))
 
 
@@ -116,13 +123,20 @@ def test_device_degenerate_cases():
 
 
 @pytest.mark.gpu
-def test_device_bound_rows_and_larger_case():
+@pytest.mark.parametrize("mode", [0, 1, 2], ids=["simt", "auto", "tensor"])
+def test_device_bound_rows_and_larger_case(mode):
+    """Rows given, then bound (read in place; after an assign on them, the
+    tensor-core path reads their split copy too)."""
     rng = np.random.default_rng(8)
     n, d, k = 20000, 256, 300
     x = unit_rows(rng, n, d)
-    lab = nearest_labels(x, unit_rows(rng, k, d))
+    c = unit_rows(rng, k, d)
+    lab = nearest_labels(x, c)
     want = oracle_scores(x, d, lab, k)
     with eb.Engine(0) as e:
+        e.set_screen_mode(mode)
         check(e.internal_scores(x, d, lab, k), want)
         e.bind_data(x, d)
+        check(e.internal_scores(x, d, lab, k), want)
+        e.assign(x, d, c, eb.IP, ids=np.arange(n, dtype=np.uint32))
         check(e.internal_scores(x, d, lab, k), want)
