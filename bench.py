@@ -312,24 +312,29 @@ def run_ours(args):
     x = np.ascontiguousarray(xtrain[:n] if n <= xtrain.shape[0] else gen_rows(n, d, 0))
     lo, hi, s = shard(n, world, rank)
 
-    # ---- device-resident assign: this rank's shard of the rows, then the
-    # labels and scores all-gathered so that every rank holds all of them.
-    xb = eng.bind(x, d)
+    # ---- device-resident assign: each rank binds its shard of the rows and
+    # writes its labels and scores into its share of one exchange buffer
+    # (share r = labels then scores of rows r s .. r s + s), which one
+    # all-gather per step gives to every rank.
+    m = hi - lo
+    xb = eng.bind(x[lo:hi], d)
     cb = eng.upload_f32(cent)
     cn = eng.zeros_f32(k)
-    lab = eng.zeros_u32(s * world)
-    sco = eng.zeros_f32(s * world)
+    res_t = torch.zeros(world * 2 * s, dtype=torch.int32, device="cuda")
+    res = eng.wrap(res_t)
+    lab = eng.wrap(res_t[rank * 2 * s:rank * 2 * s + s])
+    sco = eng.wrap(res_t[rank * 2 * s + s:(rank + 1) * 2 * s].view(torch.float32))
 
     def step(ev=None):
         eng.row_norms(cb, k, d, cn)
         if ev:
             ev[0].record(stream)
-        eng.top1(xb, d, None, range(lo, hi), cb, cn, k, eb.L2, lab, sco)
+        if m:
+            eng.top1(xb, d, None, range(0, m), cb, cn, k, eb.L2, lab, sco)
         if ev:
             ev[1].record(stream)
         if world > 1:
-            eng.group_allgather(lab, s)
-            eng.group_allgather(sco, s)
+            eng.group_allgather(res, 2 * s)
 
     # The first call on fresh rows builds their split FP16 copy (kept for later
     # calls on the bound rows, as the reference keeps its per-buffer copy).
@@ -373,11 +378,13 @@ def run_ours(args):
     ms, top1_ms, screen_ms, cold_ms = _max_over_ranks(dist, [ms, top1_ms, screen_ms, cold_ms])
     if dist:
         dist.barrier()
-    glab, gsco = lab.read(0, n), sco.read(0, n)  # every rank holds all rows' results
+    # Every rank holds all rows' results.
+    allres = res.read().reshape(world, 2 * s)
+    glab = np.ascontiguousarray(allres[:, :s]).ravel()[:n]
+    gsco = np.ascontiguousarray(allres[:, s:]).ravel().view(np.float32)[:n]
 
     # ---- end to end through Assigner::assign (eb_assign): this rank's shard
     # from pinned host memory, labels and scores back into pinned host memory.
-    m = hi - lo
     hx = torch.from_numpy(x[lo:hi]).pin_memory()
     hc = torch.from_numpy(np.ascontiguousarray(cent)).pin_memory()
     hl = torch.empty(max(m, 1), dtype=torch.int32).pin_memory()
@@ -410,7 +417,7 @@ def run_ours(args):
     usage = eng.upload_f32(np.full(k, 1.0 / k, np.float32))
 
     def upd_step():
-        eng.scatter_add(xb, d, None, range(lo, hi), lab, k, sums, counts)
+        eng.scatter_add(xb, d, None, range(0, m), lab, k, sums, counts)
         eng.ema_update(pos, usage, sums, counts, k, d, 0.1)
 
     for _ in range(args.warmup):
@@ -559,7 +566,7 @@ def run_ours(args):
                     out["train_s_reduce"]["obj_rel_delta_vs_oracle"] = \
                         abs(tr_red.obj[-1] - otr["obj"][-1]) / abs(otr["obj"][-1])
         print(json.dumps(out), flush=True)
-    del xb, cb, cn, lab, sco, sums, counts, pos, usage
+    del xb, cb, cn, lab, sco, res, sums, counts, pos, usage
     eng.close()
     if dist:
         dist.barrier()

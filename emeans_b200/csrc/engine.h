@@ -288,11 +288,12 @@ void top1_dispatch(eb_engine* e, const Top1Args& a, eb_buf* xbuf);
 // estimated length in centroid-tile times for `rows` rows against k centroids.
 int screen_parts(size_t rtiles, int ntiles, int sms);
 // The internal scores' product on the tensor cores (top1_tc.cu):
-// vmax_out[i] = max over the centroids s other than slot[labels[i]] of
-// x_i . c_s * inv[s] (f32, split FP16 products with FP32 accumulation).
+// best_out[i] = the centroid s other than slot[labels[i]] with the largest
+// x_i . c_s * inv[s] (split FP16 products with FP32 accumulation);
+// 0xFFFFFFFF when there is none, 0xFFFFFFFE when the row could not be scored.
 void screen_products(eb_engine* e, const float* x, size_t n, size_t d, eb_buf* xbuf,
                      const uint32_t* labels, const uint32_t* slot, const float* c,
-                     const float* inv, size_t k, float* vmax_out);
+                     const float* inv, size_t k, uint32_t* best_out);
 size_t screen_tile_times(size_t rows, size_t k, int sms);
 bool top1_screen_supported(eb_engine* e, const Top1Args& a);
 void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf);

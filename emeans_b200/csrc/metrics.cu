@@ -94,19 +94,22 @@ __global__ void k_cluster_prep(const double* __restrict__ sums, const uint32_t* 
   }
 }
 
-// The per-row terms with the tensor-core product (screen_products): vmax =
-// max over s != o of x_i . c32_s / n_s from it; the own cluster's product
-// x_i . c32_o as one FP32 FMA chain in column order (the distance and the
-// silhouette's a cancel it against the row's norm, so it stays the SIMT
-// kernel's exact chain) and the row's f64 sum of squares in column order;
-// then the same formulas as k_silhouette's epilogue. One warp per 32 rows:
-// each 32-column slice of the warp's rows is read coalesced (a row per load,
-// a column per lane) into shared memory, and each lane runs its own row's
+// The per-row terms with the tensor-core product (screen_products), which
+// picks each row's best other cluster b (the largest x_i . c32_s / n_s over
+// s != o). Both products the row needs, x_i . c32_o and x_i . c32_b, are FP32
+// FMA chains in column order, the SIMT kernel's values bit for bit (the
+// distance and the silhouette's a cancel the own product against the row's
+// norm, and the tensor cores' FP32 accumulation leans toward zero), so the
+// scores equal the SIMT path's except where two clusters tie within the
+// screen's rounding. Then the row's f64 sum of squares in column order and
+// the same formulas as k_silhouette's epilogue. One warp per 32 rows: each
+// 32-column slice of the warp's rows is read coalesced (a row per load, a
+// column per lane) into shared memory, and each lane runs its own row's
 // chains.
 __global__ void __launch_bounds__(128) k_row_terms(
     const float* __restrict__ x, long n, int d, const uint32_t* __restrict__ labels,
     const uint32_t* __restrict__ slot, const float* __restrict__ c32,
-    const float* __restrict__ vmax_g, const double* __restrict__ size,
+    const uint32_t* __restrict__ best, const double* __restrict__ size,
     const double* __restrict__ sq, long keff, double* __restrict__ sil, double* __restrict__ obj,
     double* __restrict__ dist, double* __restrict__ xx_out) {
   pdl_wait();
@@ -117,8 +120,11 @@ __global__ void __launch_bounds__(128) k_row_terms(
   float(*t)[33] = tile[w];
   const long myrow = min(r0 + lane, n - 1);
   const float* crow = c32 + (long)slot[labels[myrow]] * d;
+  const uint32_t bcol = best[myrow];
+  const bool has_b = bcol < (uint32_t)keff;
+  const float* brow = c32 + (long)(has_b ? bcol : 0) * d;
   double xv = -0.0;
-  float gf = 0.0f;
+  float gf = 0.0f, gb = 0.0f;
   for (int c0 = 0; c0 < d; c0 += 32) {
     float v[32];
 #pragma unroll
@@ -135,6 +141,7 @@ __global__ void __launch_bounds__(128) k_row_terms(
       const double q = (double)a;
       xv = __dadd_rn(xv, __dmul_rn(q, q));
       gf = __fmaf_rn(a, __ldg(crow + c0 + c), gf);
+      gb = __fmaf_rn(a, __ldg(brow + c0 + c), gb);
     }
     __syncwarp();
   }
@@ -151,7 +158,9 @@ __global__ void __launch_bounds__(128) k_row_terms(
   double sv = 0.0;
   if (keff >= 2 && na >= 2.0) {
     const double a = __dsub_rn(1.0, __ddiv_rn(__dsub_rn(g, xv), __dsub_rn(na, 1.0)));
-    const double bb = __dsub_rn(1.0, (double)vmax_g[row]);
+    const double vm = has_b ? __ddiv_rn((double)gb, size[bcol])
+                            : (bcol == 0xFFFFFFFFu ? -INFINITY : NAN);
+    const double bb = __dsub_rn(1.0, vm);
     const double m = fmax(a, bb);
     sv = m > 0.0 ? __ddiv_rn(__dsub_rn(bb, a), m) : 0.0;
   }
@@ -493,12 +502,12 @@ void internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uin
   const bool tensor = e->screen_mode == 2 ||
                       (e->screen_mode == 1 && n >= 4096 && keff >= 64 && d >= 16 && d <= 16384);
   if (tensor) {
-    Tmp vmax(e, n * 4);
+    Tmp best(e, n * 4);
     screen_products(e, xd, n, d, reuse ? e->bound : nullptr, lab.as<uint32_t>(),
                     dslot.as<uint32_t>(), c32.as<float>(), inv.as<float>(), keff,
-                    vmax.as<float>());
+                    best.as<uint32_t>());
     launch_pdl(e, k_row_terms, nblocks(n, 128), 128, 0, xd, (long)n, (int)d, lab.as<uint32_t>(),
-               dslot.as<uint32_t>(), c32.as<float>(), vmax.as<float>(), size.as<double>(),
+               dslot.as<uint32_t>(), c32.as<float>(), best.as<uint32_t>(), size.as<double>(),
                sq.as<double>(), (long)keff, sil.as<double>(), obj.as<double>(),
                dist.as<double>(), xx.as<double>());
     EB_LAUNCH("metrics row terms");

@@ -547,12 +547,14 @@ struct ScreenParams {
   // Product mode (k_screen<true, false, true>, the internal scores' n x k
   // product): each row's own column pslot[plabels[prow0 + i]], per column the
   // weight pinv (1 / cluster size), and per (list, row) the largest weighted
-  // product over the other columns (pmax, in accumulator units).
+  // product over the other columns (pmax, in accumulator units) and its
+  // column (pcol; the lower column on ties).
   const uint32_t* plabels;
   const uint32_t* pslot;
   long prow0;
   const float* pinv;
   float* pmax;
+  uint32_t* pcol;
   // Failure-detection test (eb_test_screen_dead_wait): CTA 0's epilogue waits
   // for its second tile on a barrier that nothing arrives at, so that the
   // wait runs out and the give-up path runs. 0 in normal use.
@@ -765,6 +767,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // Product mode: this row's own column and the running maximum.
       const long own_col = PROD && live ? (long)P.pslot[P.plabels[P.prow0 + i]] : -1;
       float pm = -INFINITY;
+      uint32_t pc = 0xFFFFFFFFu;
       float best = IP ? -INFINITY : INFINITY;
       float thr = best;
       bool overflow = false;
@@ -855,9 +858,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // The largest weighted product of the columns other than the own.
             const long cb = col0 + g * 16;
 #pragma unroll
-            for (int j = 0; j < 16; j++)
-              if (cb + j != own_col && cb + j < P.k)
-                pm = fmaxf(pm, __uint_as_float(h[j]) * cns[g * 16 + j]);
+            for (int j = 0; j < 16; j++) {
+              const float v = __uint_as_float(h[j]) * cns[g * 16 + j];
+              if (cb + j != own_col && cb + j < P.k && v > pm) {
+                pm = v;
+                pc = (uint32_t)(cb + j);
+              }
+            }
             return;
           }
           float s[16];
@@ -999,7 +1006,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       }
       if (PROD) {
-        if (live) P.pmax[L * P.m + i] = collect && !stop ? pm : NAN;
+        if (live) {
+          P.pmax[L * P.m + i] = collect && !stop ? pm : NAN;
+          P.pcol[L * P.m + i] = pc;
+        }
       } else if (live) {
         // A half tile past the last centroid (k <= HALF, or a last part
         // whose one tile has HALF centroids or fewer) holds no centroid at
@@ -1792,31 +1802,35 @@ __global__ void k_scatter_topk(const uint32_t* __restrict__ list, long L, int kk
 
 // ---------------------------------------------------------------- product stage
 
-// Product mode: each row's largest weighted product over the columns other
-// than its own (the maximum over its lists), unscaled by the row's and the
-// centroids' powers of two (exact). Rows or centroids with non-finite
-// values, or a screen that gave up: NaN.
+// Product mode: each row's column of the largest weighted product over the
+// columns other than its own (over its lists; the lower column on ties), or
+// 0xFFFFFFFF when there is none. Rows or centroids with non-finite values, or
+// a screen that gave up: 0xFFFFFFFE.
 __global__ void k_prod_finish(long p0, long m, int nl, const int* __restrict__ xexp,
                               const unsigned long long* __restrict__ cinfo, uint32_t cgen,
-                              const float* __restrict__ pmax, float* __restrict__ vmax_out) {
+                              const float* __restrict__ pmax, const uint32_t* __restrict__ pcol,
+                              uint32_t* __restrict__ best_out) {
   pdl_wait();
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= m) return;
-  int ec = 0;
-  frexpf(__uint_as_float(cinfo_word(cinfo, 0, cgen)), &ec);
-  const int ex = xexp[i];
-  float vm = NAN;
-  if (ex != XEXP_BAD && cinfo_word(cinfo, 2, cgen) == 0) {
-    vm = -INFINITY;
-    bool bad = false;
+  uint32_t bc = 0xFFFFFFFEu;
+  if (xexp[i] != XEXP_BAD && cinfo_word(cinfo, 2, cgen) == 0) {
+    float vm = -INFINITY;
+    bc = 0xFFFFFFFFu;
     for (int h = 0; h < nl; h++) {
       const float v = pmax[(long)h * m + i];
-      bad = bad || isnan(v);
-      vm = fmaxf(vm, v);
+      const uint32_t c = pcol[(long)h * m + i];
+      if (isnan(v)) {
+        bc = 0xFFFFFFFEu;
+        break;
+      }
+      if (c != 0xFFFFFFFFu && (v > vm || (v == vm && c < bc))) {
+        vm = v;
+        bc = c;
+      }
     }
-    vm = bad ? NAN : ldexpf(vm, ex + ec - 28);
   }
-  vmax_out[p0 + i] = vm;
+  best_out[p0 + i] = bc;
 }
 
 // ---------------------------------------------------------------- host side
@@ -2315,13 +2329,14 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
 
 // The internal scores' n x k_eff product on the tensor cores (the screen in
 // product mode): for each row i of x (n x d, f32 on the device) with own
-// column slot[labels[i]], vmax_out[i] = the largest x_i . c_s * inv[s] over
-// s != own, from the split FP16 products (xh ch + xh cl + xl ch, FP32
-// accumulation). The bound set's split copy is read in place when xbuf holds
-// one.
+// column slot[labels[i]], best_out[i] = the column s != own of the largest
+// x_i . c_s * inv[s], from the split FP16 products (xh ch + xh cl + xl ch,
+// FP32 accumulation); 0xFFFFFFFF when k = 1, 0xFFFFFFFE for rows the screen
+// could not score (non-finite values, a wait that gave up). The bound set's
+// split copy is read in place when xbuf holds one.
 void screen_products(eb_engine* e, const float* x, size_t n, size_t d, eb_buf* xbuf,
                      const uint32_t* labels, const uint32_t* slot, const float* c,
-                     const float* inv, size_t k, float* vmax_out) {
+                     const float* inv, size_t k, uint32_t* best_out) {
   if (n == 0) return;
   const size_t dp = (d + BKH - 1) / BKH * BKH;
   const size_t wave = (size_t)e->num_sms * BM;
@@ -2345,6 +2360,7 @@ void screen_products(eb_engine* e, const float* x, size_t n, size_t d, eb_buf* x
   int* xexp = e->scratch_get<int>("tc_xexp", chunk);
   float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
   float* pmax = e->scratch_get<float>("pr_max", 2 * (size_t)max_parts * chunk);
+  uint32_t* pcol = e->scratch_get<uint32_t>("pr_col", 2 * (size_t)max_parts * chunk);
   Fp16Copy* cache = nullptr;
   if (xbuf && xbuf->f16 && xbuf->f16->version == xbuf->version && xbuf->f16->n == n &&
       xbuf->f16->d == d)
@@ -2364,6 +2380,7 @@ void screen_products(eb_engine* e, const float* x, size_t n, size_t d, eb_buf* x
   P.pslot = slot;
   P.pinv = inv;
   P.pmax = pmax;
+  P.pcol = pcol;
   for (size_t c0 = 0; c0 < n; c0 += chunk) {
     const size_t m = std::min(chunk, n - c0);
     const __half *ah = xh, *al = xl;
@@ -2393,7 +2410,7 @@ void screen_products(eb_engine* e, const float* x, size_t n, size_t d, eb_buf* x
     launch_screen<true, false, true>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
     EB_LAUNCH("product screen");
     launch_pdl(e, k_prod_finish, (unsigned)((m + 255) / 256), 256, 0, (long)c0, (long)m,
-               2 * P.parts, pe, cinfo, cgen, pmax, vmax_out);
+               2 * P.parts, pe, cinfo, cgen, pmax, pcol, best_out);
     EB_LAUNCH("product finish");
   }
 }
