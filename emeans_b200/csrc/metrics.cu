@@ -125,23 +125,47 @@ __global__ void __launch_bounds__(128) k_row_terms(
   const float* brow = c32 + (long)(has_b ? bcol : 0) * d;
   double xv = -0.0;
   float gf = 0.0f, gb = 0.0f;
+  // Each lane reads its two centroid rows' slice as eight 16-byte loads
+  // each (a whole 128-byte line) when the rows allow it.
+  const bool vec = (d & 3) == 0 && ((uintptr_t)c32 & 15) == 0;
   for (int c0 = 0; c0 < d; c0 += 32) {
-    float v[32];
+    {
+      float v[32];
 #pragma unroll
-    for (int r = 0; r < 32; r++) {
-      const long row = r0 + r;
-      v[r] = (row < n && c0 + lane < d) ? __ldg(x + row * d + c0 + lane) : 0.0f;
+      for (int r = 0; r < 32; r++) {
+        const long row = r0 + r;
+        v[r] = (row < n && c0 + lane < d) ? __ldg(x + row * d + c0 + lane) : 0.0f;
+      }
+#pragma unroll
+      for (int r = 0; r < 32; r++) t[r][lane] = v[r];
     }
-#pragma unroll
-    for (int r = 0; r < 32; r++) t[r][lane] = v[r];
     __syncwarp();
     const int cmax = min(32, d - c0);
-    for (int c = 0; c < cmax; c++) {
-      const float a = t[lane][c];
-      const double q = (double)a;
-      xv = __dadd_rn(xv, __dmul_rn(q, q));
-      gf = __fmaf_rn(a, __ldg(crow + c0 + c), gf);
-      gb = __fmaf_rn(a, __ldg(brow + c0 + c), gb);
+    if (vec && cmax == 32) {
+      float cv[32], bv[32];
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        const float4 a4 = __ldg(reinterpret_cast<const float4*>(crow + c0) + q);
+        const float4 b4 = __ldg(reinterpret_cast<const float4*>(brow + c0) + q);
+        cv[4 * q] = a4.x; cv[4 * q + 1] = a4.y; cv[4 * q + 2] = a4.z; cv[4 * q + 3] = a4.w;
+        bv[4 * q] = b4.x; bv[4 * q + 1] = b4.y; bv[4 * q + 2] = b4.z; bv[4 * q + 3] = b4.w;
+      }
+#pragma unroll
+      for (int c = 0; c < 32; c++) {
+        const float a = t[lane][c];
+        const double q = (double)a;
+        xv = __dadd_rn(xv, __dmul_rn(q, q));
+        gf = __fmaf_rn(a, cv[c], gf);
+        gb = __fmaf_rn(a, bv[c], gb);
+      }
+    } else {
+      for (int c = 0; c < cmax; c++) {
+        const float a = t[lane][c];
+        const double q = (double)a;
+        xv = __dadd_rn(xv, __dmul_rn(q, q));
+        gf = __fmaf_rn(a, __ldg(crow + c0 + c), gf);
+        gb = __fmaf_rn(a, __ldg(brow + c0 + c), gb);
+      }
     }
     __syncwarp();
   }
@@ -362,57 +386,95 @@ __global__ void __launch_bounds__(NT) k_silhouette(
 }
 
 // worst[a] = max over b != a of (spread_a + spread_b) / |mean_a - mean_b|
-// (infinite for equal means), folded from 0 (metrics.rs:233-256). Each block
-// takes kDbA clusters a, each thread a cluster b at a time; each distance is
-// a sequential f64 chain over the columns. The means are column-major, so a
-// warp's loads of its 32 b's at one column are one coalesced read, and the
-// kDbA a's share every load of b.
-constexpr int kDbA = 4;
-__global__ void __launch_bounds__(256) k_db(const double* __restrict__ meanT,
-                                            const double* __restrict__ spread, long keff, int d,
-                                            double* __restrict__ worst) {
+// (infinite for equal means), folded from 0 (metrics.rs:233-256); each
+// distance is a sequential f64 chain over the columns. The chain of (a, b)
+// and the one of (b, a) are the same bits ((ma - mb)^2 = (mb - ma)^2, and the
+// spreads' sum commutes), so each pair is computed once, for b > a, and
+// folded into both worst[a] and worst[b]. A block takes kDbA clusters a
+// (their 32-column slices staged in shared memory) and 256 clusters b (one
+// per thread, the means column-major so that a warp's 32 b's at one column
+// are one coalesced read), with kDbA chains per thread; blocks wholly below
+// the diagonal do nothing. The maxima are non-negative doubles (or +inf),
+// whose bit patterns order like their values: atomic maxima on the bits, into
+// worst zeroed by the caller.
+constexpr int kDbA = 16, kDbB = 256, kDbT = 32;
+__device__ __forceinline__ void atomic_max_nonneg(double* p, double v) {
+  atomicMax(reinterpret_cast<unsigned long long*>(p), (unsigned long long)__double_as_longlong(v));
+}
+__global__ void __launch_bounds__(kDbB) k_db(const double* __restrict__ meanT,
+                                             const double* __restrict__ spread, long keff, int d,
+                                             double* __restrict__ worst) {
   pdl_wait();
-  __shared__ double red[kDbA][256];
-  const long a0 = (long)blockIdx.x * kDbA;
-  double w[kDbA];
+  __shared__ double as[kDbT][kDbA];
+  __shared__ double red[kDbB / 32][kDbA];
+  const long a0 = (long)blockIdx.y * kDbA;
+  const long b = (long)blockIdx.x * kDbB + threadIdx.x;
+  if ((long)blockIdx.x * kDbB + kDbB - 1 <= a0) return;  // every b <= every a: nothing here
+  const long bc = min(b, keff - 1);
+  double s[kDbA];
 #pragma unroll
-  for (int q = 0; q < kDbA; q++) w[q] = 0.0;
-  for (long b = threadIdx.x; b < keff; b += blockDim.x) {
-    double s[kDbA];
+  for (int q = 0; q < kDbA; q++) s[q] = -0.0;
+  for (int t0 = 0; t0 < d; t0 += kDbT) {
+    const int tn = min(kDbT, d - t0);
+    __syncthreads();  // the last slice is no longer read
+    for (int u = threadIdx.x; u < kDbT * kDbA; u += kDbB) {
+      const int tt = u / kDbA, q = u % kDbA;
+      as[tt][q] = tt < tn ? __ldg(meanT + (long)(t0 + tt) * keff + min(a0 + q, keff - 1)) : 0.0;
+    }
+    __syncthreads();
+    const double* col = meanT + (long)t0 * keff + bc;
+    if (tn == kDbT) {
+#pragma unroll 8
+      for (int tt = 0; tt < kDbT; tt++) {
+        const double mb = __ldg(col + (long)tt * keff);
 #pragma unroll
-    for (int q = 0; q < kDbA; q++) s[q] = -0.0;
-#pragma unroll 4
-    for (int t = 0; t < d; t++) {
-      const double* col = meanT + (long)t * keff;
-      const double mb = __ldg(col + b);
+        for (int q = 0; q < kDbA; q++) {
+          const double df = __dsub_rn(as[tt][q], mb);
+          s[q] = __dadd_rn(s[q], __dmul_rn(df, df));
+        }
+      }
+    } else {
+      for (int tt = 0; tt < tn; tt++) {
+        const double mb = __ldg(col + (long)tt * keff);
 #pragma unroll
-      for (int q = 0; q < kDbA; q++) {
-        const long a = min(a0 + q, keff - 1);
-        const double df = __dsub_rn(__ldg(col + a), mb);
-        s[q] = __dadd_rn(s[q], __dmul_rn(df, df));
+        for (int q = 0; q < kDbA; q++) {
+          const double df = __dsub_rn(as[tt][q], mb);
+          s[q] = __dadd_rn(s[q], __dmul_rn(df, df));
+        }
       }
     }
-    const double sb = spread[b];
-#pragma unroll
-    for (int q = 0; q < kDbA; q++) {
-      const long a = a0 + q;
-      if (a >= keff || b == a) continue;
-      const double m = __dsqrt_rn(s[q]);
-      const double v = m > 0.0 ? __ddiv_rn(__dadd_rn(spread[a], sb), m) : INFINITY;
-      w[q] = fmax(w[q], v);
-    }
   }
+  const bool bl = b < keff;
+  const double sb = bl ? spread[b] : 0.0;
+  double wb = 0.0;  // this b's maximum over the block's a's
+  double wa[kDbA];
 #pragma unroll
-  for (int q = 0; q < kDbA; q++) red[q][threadIdx.x] = w[q];
+  for (int q = 0; q < kDbA; q++) {
+    const long a = a0 + q;
+    wa[q] = 0.0;
+    if (!bl || a >= keff || b <= a) continue;
+    const double m = __dsqrt_rn(s[q]);
+    const double v = m > 0.0 ? __ddiv_rn(__dadd_rn(spread[a], sb), m) : INFINITY;
+    wa[q] = v;
+    wb = fmax(wb, v);
+  }
+  if (bl && wb > 0.0) atomic_max_nonneg(worst + b, wb);
+  // Each a's maximum over the block's b's: warp shuffles, then across warps.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int q = 0; q < kDbA; q++) {
+    double v = wa[q];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v = fmax(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    if (lane == 0) red[warp][q] = v;
+  }
   __syncthreads();
-  for (int off = blockDim.x / 2; off > 0; off >>= 1) {
-    if (threadIdx.x < off)
+  if (threadIdx.x < kDbA && a0 + threadIdx.x < keff) {
+    double v = 0.0;
 #pragma unroll
-      for (int q = 0; q < kDbA; q++)
-        red[q][threadIdx.x] = fmax(red[q][threadIdx.x], red[q][threadIdx.x + off]);
-    __syncthreads();
+    for (int w = 0; w < kDbB / 32; w++) v = fmax(v, red[w][threadIdx.x]);
+    if (v > 0.0) atomic_max_nonneg(worst + a0 + threadIdx.x, v);
   }
-  if (threadIdx.x < kDbA && a0 + threadIdx.x < keff) worst[a0 + threadIdx.x] = red[threadIdx.x][0];
 }
 
 // grand[t] = sum over the live clusters, in label order, of sums[j][t] from
@@ -422,8 +484,17 @@ __global__ void k_grand(const double* __restrict__ sums, const uint32_t* __restr
   pdl_wait();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= d) return;
+  // One sequential chain per column; sixteen loads in flight ahead of it.
   double g = 0.0;
-  for (long s = 0; s < keff; s++) g = __dadd_rn(g, sums[(long)live[s] * d + t]);
+  long s = 0;
+  for (; s + 16 <= keff; s += 16) {
+    double v[16];
+#pragma unroll
+    for (int q = 0; q < 16; q++) v[q] = __ldg(sums + (long)live[s + q] * d + t);
+#pragma unroll
+    for (int q = 0; q < 16; q++) g = __dadd_rn(g, v[q]);
+  }
+  for (; s < keff; s++) g = __dadd_rn(g, sums[(long)live[s] * d + t]);
   grand[t] = g;
 }
 
@@ -571,8 +642,9 @@ void internal_scores(eb_engine* e, const float* x, size_t n, size_t d, const uin
     for (size_t s = 0; s < keff; s++) spread[s] = scatter[s] / (double)counts[live[s]];
     Tmp dspread(e, keff * 8), dworst(e, keff * 8);
     h2d(e, dspread.p, spread.data(), keff * 8, e->stream);
-    launch_pdl(e, k_db, nblocks(keff, kDbA), 256, 0, mean.as<double>(), dspread.as<double>(),
-               (long)keff, (int)d, dworst.as<double>());
+    EB_CUDA(cudaMemsetAsync(dworst.p, 0, keff * 8, e->stream));
+    launch_pdl(e, k_db, dim3(nblocks(keff, kDbB), nblocks(keff, kDbA)), kDbB, 0,
+               mean.as<double>(), dspread.as<double>(), (long)keff, (int)d, dworst.as<double>());
     EB_LAUNCH("metrics davies-bouldin");
     std::vector<double> worst(keff);
     d2h(e, worst.data(), dworst.p, keff * 8, e->stream);

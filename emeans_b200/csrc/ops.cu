@@ -304,24 +304,26 @@ __global__ void __launch_bounds__(256) k_seg_scan(uint32_t* __restrict__ segcnt,
 }
 
 // Exclusive scan of counts into start[0..k], one block of 1024 threads; and
-// the labels by count, largest first (ties: lower label first), into
-// by_size[0..k), so that the segment sums start the longest chains in the
-// first wave (a chain is sequential, and the largest one sets the kernel's
-// length). Bitonic sort of (count, ~label) keys in shared memory for k up to
-// kSortMax; larger k keep the label order.
-constexpr uint32_t kSortMax = 4096;
+// the labels grouped by the size of their count, largest first (bucket b =
+// bit length of the count), into by_size[0..k), so that the segment sums
+// start the longest chains in the first wave (a chain is sequential, and the
+// largest one sets the kernel's length). Only the launch order of the sum
+// blocks depends on by_size: the order within a bucket is the order of the
+// shared-memory atomics, and every sum comes out the same.
 __global__ void __launch_bounds__(1024) k_label_scan(const uint32_t* __restrict__ counts,
                                                      uint32_t k, uint32_t* __restrict__ start,
                                                      uint32_t* __restrict__ by_size) {
   pdl_wait();
   __shared__ uint32_t part[1024];
-  __shared__ unsigned long long keys[kSortMax];
+  __shared__ uint32_t bins[34];
+  if (threadIdx.x < 34) bins[threadIdx.x] = 0;
   uint32_t per = (k + blockDim.x - 1) / blockDim.x;
   uint32_t lo = threadIdx.x * per, hi = min(lo + per, k);
   uint32_t s = 0;
   for (uint32_t l = lo; l < hi; l++) s += counts[l];
   part[threadIdx.x] = s;
   __syncthreads();
+  for (uint32_t l = lo; l < hi; l++) atomicAdd(&bins[32 - __clz(counts[l])], 1u);
   for (int off = 1; off < (int)blockDim.x; off <<= 1) {
     uint32_t v = threadIdx.x >= (unsigned)off ? part[threadIdx.x - off] : 0;
     __syncthreads();
@@ -334,30 +336,17 @@ __global__ void __launch_bounds__(1024) k_label_scan(const uint32_t* __restrict_
     run += counts[l];
   }
   if (threadIdx.x == blockDim.x - 1) start[k] = part[threadIdx.x];
-  if (k > kSortMax) {
-    for (uint32_t l = threadIdx.x; l < k; l += blockDim.x) by_size[l] = l;
-    return;
-  }
-  uint32_t n2 = 2;
-  while (n2 < k) n2 <<= 1;
-  for (uint32_t l = threadIdx.x; l < n2; l += blockDim.x)
-    keys[l] = l < k ? ((unsigned long long)counts[l] << 32) | (uint32_t)~l : 0ull;
-  __syncthreads();
-  for (uint32_t size = 2; size <= n2; size <<= 1) {
-    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-      for (uint32_t i = threadIdx.x; i < n2 / 2; i += blockDim.x) {
-        const uint32_t a = 2 * i - (i & (stride - 1)), b = a + stride;
-        const bool desc = (a & size) == 0;
-        const unsigned long long ka = keys[a], kb = keys[b];
-        if (desc ? ka < kb : ka > kb) {
-          keys[a] = kb;
-          keys[b] = ka;
-        }
-      }
-      __syncthreads();
+  if (threadIdx.x == 0) {
+    // Bucket starts, largest bucket (32: counts of 2^31 or more) first.
+    uint32_t acc = 0;
+    for (int bb = 32; bb >= 0; bb--) {
+      const uint32_t c = bins[bb];
+      bins[bb] = acc;
+      acc += c;
     }
   }
-  for (uint32_t l = threadIdx.x; l < k; l += blockDim.x) by_size[l] = ~(uint32_t)keys[l];
+  __syncthreads();
+  for (uint32_t l = lo; l < hi; l++) by_size[atomicAdd(&bins[32 - __clz(counts[l])], 1u)] = l;
 }
 
 // Place every position at its sorted slot; the slot holds the data row id.
@@ -444,6 +433,76 @@ __global__ void __launch_bounds__(128) k_seg_sum(const float* __restrict__ x, in
   if (active) {
     sums[j * d + t] = s;
     if (acc) acc[j * d + t] = __fadd_rn(acc[j * d + t], s);
+  }
+}
+
+// The same with four columns per thread (16-byte loads; d % 4 == 0 and
+// 16-byte aligned rows): thread t of the block adds columns 4 t .. 4 t + 3 of
+// the block's 256-column span, four independent chains, each the scalar
+// kernel's chain bit for bit. 64-thread blocks; Q rows' loads in flight.
+template <int Q>
+__device__ __forceinline__ float4 chain_sum4(const float4* __restrict__ xt, const uint32_t* ord,
+                                             uint32_t n, long d4, float4 s) {
+  uint32_t i = 0;
+  auto add = [](float4 a, float4 b) {
+    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
+                       __fadd_rn(a.w, b.w));
+  };
+  float4 v[Q];
+  if (n >= (uint32_t)Q) {
+#pragma unroll
+    for (int q = 0; q < Q; q++) v[q] = __ldg(xt + (long)ord[q] * d4);
+  }
+  for (; i + 2 * Q <= n; i += Q) {
+    float4 w[Q];
+#pragma unroll
+    for (int q = 0; q < Q; q++) w[q] = __ldg(xt + (long)ord[i + Q + q] * d4);
+#pragma unroll
+    for (int q = 0; q < Q; q++) s = add(s, v[q]);
+#pragma unroll
+    for (int q = 0; q < Q; q++) v[q] = w[q];
+  }
+  if (i + Q <= n) {
+#pragma unroll
+    for (int q = 0; q < Q; q++) s = add(s, v[q]);
+    i += Q;
+  }
+  for (; i < n; i++) s = add(s, __ldg(xt + (long)ord[i] * d4));
+  return s;
+}
+
+__global__ void __launch_bounds__(64) k_seg_sum4(const float* __restrict__ x, int d, int cb,
+                                                 const uint32_t* __restrict__ order,
+                                                 const uint32_t* __restrict__ start,
+                                                 const uint32_t* __restrict__ by_size,
+                                                 float* __restrict__ sums,
+                                                 float* __restrict__ acc) {
+  pdl_wait();
+  __shared__ uint32_t ord_s[kSumStage];
+  const long j = by_size[blockIdx.x / cb];
+  const int t4 = (blockIdx.x % cb) * blockDim.x + threadIdx.x;  // float4 column
+  const long d4 = d / 4;
+  const bool active = t4 < d4;
+  const float4* xt = reinterpret_cast<const float4*>(x) + (active ? t4 : 0);
+  const uint32_t b = start[j], e = start[j + 1];
+  float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (uint32_t c0 = b; c0 < e; c0 += kSumStage) {
+    const uint32_t n = min(e - c0, kSumStage);
+    __syncthreads();  // the last chunk's ids are no longer read
+    for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) ord_s[u] = order[c0 + u];
+    __syncthreads();
+    if (!active) continue;
+    s = chain_sum4<16>(xt, ord_s, n, d4, s);
+  }
+  if (active) {
+    float4* so = reinterpret_cast<float4*>(sums + j * d) + t4;
+    *so = s;
+    if (acc) {
+      float4* ao = reinterpret_cast<float4*>(acc + j * d) + t4;
+      const float4 a = *ao;
+      *ao = make_float4(__fadd_rn(a.x, s.x), __fadd_rn(a.y, s.y), __fadd_rn(a.z, s.z),
+                        __fadd_rn(a.w, s.w));
+    }
   }
 }
 
@@ -592,9 +651,17 @@ void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_
                  float* acc) {
   const uint32_t *order, *start, *by_size;
   label_order(e, ids, r0, r1, n, labels, k, counts, &order, &start, &by_size);
-  const unsigned cb = blocks_for(d, 128);
-  launch_pdl(e, k_seg_sum, (unsigned)(k * cb), 128, 0, x, (int)d, (int)cb, order, start, by_size,
-             sums, acc);
+  const bool vec = d % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)sums & 15) == 0 &&
+                   (!acc || ((uintptr_t)acc & 15) == 0);
+  if (vec) {
+    const unsigned cb = blocks_for(d / 4, 64);
+    launch_pdl(e, k_seg_sum4, (unsigned)(k * cb), 64, 0, x, (int)d, (int)cb, order, start,
+               by_size, sums, acc);
+  } else {
+    const unsigned cb = blocks_for(d, 128);
+    launch_pdl(e, k_seg_sum, (unsigned)(k * cb), 128, 0, x, (int)d, (int)cb, order, start,
+               by_size, sums, acc);
+  }
   EB_LAUNCH("scatter sum");
 }
 
