@@ -436,73 +436,77 @@ __global__ void __launch_bounds__(128) k_seg_sum(const float* __restrict__ x, in
   }
 }
 
-// The same with four columns per thread (16-byte loads; d % 4 == 0 and
-// 16-byte aligned rows): thread t of the block adds columns 4 t .. 4 t + 3 of
-// the block's 256-column span, four independent chains, each the scalar
-// kernel's chain bit for bit. 64-thread blocks; Q rows' loads in flight.
-template <int Q>
-__device__ __forceinline__ float4 chain_sum4(const float4* __restrict__ xt, const uint32_t* ord,
-                                             uint32_t n, long d4, float4 s) {
-  uint32_t i = 0;
-  auto add = [](float4 a, float4 b) {
-    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
-                       __fadd_rn(a.w, b.w));
-  };
-  float4 v[Q];
-  if (n >= (uint32_t)Q) {
-#pragma unroll
-    for (int q = 0; q < Q; q++) v[q] = __ldg(xt + (long)ord[q] * d4);
-  }
-  for (; i + 2 * Q <= n; i += Q) {
-    float4 w[Q];
-#pragma unroll
-    for (int q = 0; q < Q; q++) w[q] = __ldg(xt + (long)ord[i + Q + q] * d4);
-#pragma unroll
-    for (int q = 0; q < Q; q++) s = add(s, v[q]);
-#pragma unroll
-    for (int q = 0; q < Q; q++) v[q] = w[q];
-  }
-  if (i + Q <= n) {
-#pragma unroll
-    for (int q = 0; q < Q; q++) s = add(s, v[q]);
-    i += Q;
-  }
-  for (; i < n; i++) s = add(s, __ldg(xt + (long)ord[i] * d4));
-  return s;
-}
-
-__global__ void __launch_bounds__(64) k_seg_sum4(const float* __restrict__ x, int d, int cb,
-                                                 const uint32_t* __restrict__ order,
-                                                 const uint32_t* __restrict__ start,
-                                                 const uint32_t* __restrict__ by_size,
-                                                 float* __restrict__ sums,
-                                                 float* __restrict__ acc) {
+// The same with the rows streamed through shared memory (d % 4 == 0, 16-byte
+// aligned rows): a block takes one centroid and a 128-column slice, copies
+// SS_R rows' slices at a time with cp.async (SS_NS stages in flight, each
+// thread moving 16-byte chunks), and each thread adds its column of every
+// staged row in selection order: the scalar kernel's chain bit for bit. The
+// loads no longer wait on the chain, so the longest centroid's chain (which
+// sets the kernel's length) runs at shared-memory speed.
+constexpr int SS_R = 32, SS_NS = 4, SS_C = 128;
+constexpr size_t SS_SMEM = (size_t)SS_NS * SS_R * SS_C * sizeof(float);
+__global__ void __launch_bounds__(SS_C) k_seg_sum_staged(
+    const float* __restrict__ x, int d, int cb, const uint32_t* __restrict__ order,
+    const uint32_t* __restrict__ start, const uint32_t* __restrict__ by_size,
+    float* __restrict__ sums, float* __restrict__ acc) {
   pdl_wait();
+  extern __shared__ __align__(16) float ss_buf[];  // [SS_NS][SS_R][SS_C]
   __shared__ uint32_t ord_s[kSumStage];
   const long j = by_size[blockIdx.x / cb];
-  const int t4 = (blockIdx.x % cb) * blockDim.x + threadIdx.x;  // float4 column
-  const long d4 = d / 4;
-  const bool active = t4 < d4;
-  const float4* xt = reinterpret_cast<const float4*>(x) + (active ? t4 : 0);
+  const int col0 = (blockIdx.x % cb) * SS_C;
+  const int t = threadIdx.x;
+  const bool active = col0 + t < d;
   const uint32_t b = start[j], e = start[j + 1];
-  float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  float s = 0.0f;
   for (uint32_t c0 = b; c0 < e; c0 += kSumStage) {
     const uint32_t n = min(e - c0, kSumStage);
-    __syncthreads();  // the last chunk's ids are no longer read
-    for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) ord_s[u] = order[c0 + u];
+    __syncthreads();  // the last chunk's ids and rows are no longer read
+    for (uint32_t u = t; u < n; u += SS_C) ord_s[u] = order[c0 + u];
     __syncthreads();
-    if (!active) continue;
-    s = chain_sum4<16>(xt, ord_s, n, d4, s);
+    const int nst = (int)((n + SS_R - 1) / SS_R);
+    auto issue = [&](int st) {
+      if (st < nst) {
+        float* buf = ss_buf + (st % SS_NS) * SS_R * SS_C;
+        const uint32_t r0 = (uint32_t)st * SS_R;
+#pragma unroll
+        for (int u = 0; u < SS_R * SS_C / 4 / SS_C; u++) {  // 8 chunks a thread
+          const int idx = u * SS_C + t;
+          const int r = idx / (SS_C / 4), q = idx % (SS_C / 4);
+          const int col = col0 + q * 4;
+          if (r0 + r < n && col < d) {
+            const float* src = x + (long)ord_s[r0 + r] * d + col;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                             (uint32_t)__cvta_generic_to_shared(buf + r * SS_C + q * 4)),
+                         "l"(src)
+                         : "memory");
+          }
+        }
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+#pragma unroll
+    for (int st = 0; st < SS_NS - 1; st++) issue(st);
+    for (int st = 0; st < nst; st++) {
+      issue(st + SS_NS - 1);
+      asm volatile("cp.async.wait_group %0;" ::"n"(SS_NS - 1) : "memory");
+      __syncthreads();
+      const float* buf = ss_buf + (st % SS_NS) * SS_R * SS_C + t;
+      const int rows = min(SS_R, (int)(n - (uint32_t)st * SS_R));
+      if (active) {
+        if (rows == SS_R) {
+#pragma unroll
+          for (int r = 0; r < SS_R; r++) s = __fadd_rn(s, buf[r * SS_C]);
+        } else {
+          for (int r = 0; r < rows; r++) s = __fadd_rn(s, buf[r * SS_C]);
+        }
+      }
+      __syncthreads();  // the stage is refilled next iteration
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
   }
   if (active) {
-    float4* so = reinterpret_cast<float4*>(sums + j * d) + t4;
-    *so = s;
-    if (acc) {
-      float4* ao = reinterpret_cast<float4*>(acc + j * d) + t4;
-      const float4 a = *ao;
-      *ao = make_float4(__fadd_rn(a.x, s.x), __fadd_rn(a.y, s.y), __fadd_rn(a.z, s.z),
-                        __fadd_rn(a.w, s.w));
-    }
+    sums[j * d + col0 + t] = s;
+    if (acc) acc[j * d + col0 + t] = __fadd_rn(acc[j * d + col0 + t], s);
   }
 }
 
@@ -646,6 +650,15 @@ void label_order(eb_engine* e, const uint32_t* ids, size_t r0, size_t r1, size_t
   if (by_size_out) *by_size_out = by_size;
 }
 
+static void set_seg_sum_smem(int device) {
+  static uint64_t done = 0;
+  if (!(done >> device & 1)) {
+    EB_CUDA(cudaFuncSetAttribute(k_seg_sum_staged, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)SS_SMEM));
+    done |= 1ull << device;
+  }
+}
+
 void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids, size_t r0,
                  size_t r1, const uint32_t* labels, size_t k, float* sums, uint32_t* counts,
                  float* acc) {
@@ -654,9 +667,10 @@ void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_
   const bool vec = d % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)sums & 15) == 0 &&
                    (!acc || ((uintptr_t)acc & 15) == 0);
   if (vec) {
-    const unsigned cb = blocks_for(d / 4, 64);
-    launch_pdl(e, k_seg_sum4, (unsigned)(k * cb), 64, 0, x, (int)d, (int)cb, order, start,
-               by_size, sums, acc);
+    const unsigned cb = blocks_for(d, SS_C);
+    set_seg_sum_smem(e->device);
+    launch_pdl(e, k_seg_sum_staged, (unsigned)(k * cb), SS_C, SS_SMEM, x, (int)d, (int)cb, order,
+               start, by_size, sums, acc);
   } else {
     const unsigned cb = blocks_for(d, 128);
     launch_pdl(e, k_seg_sum, (unsigned)(k * cb), 128, 0, x, (int)d, (int)cb, order, start,
