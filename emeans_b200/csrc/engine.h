@@ -240,6 +240,20 @@ void ema_update(eb_engine* e, float* pos, float* usage, const float* sums, const
                 size_t k, size_t d, float alpha, float decay, bool replace);
 void split(eb_engine* e, float* pos, float* usage, const uint32_t* d_pairs, size_t npairs,
            size_t d);
+// ema_update followed by the next step's readout of the updated centroids
+// (L2: their squared norms into readout[k]; spherical: their normalised rows
+// into readout[k x d]) and the screen's summary of the centroids the next
+// top-1 reads (generation gen of the engine's summary words cinfo), in one
+// kernel; results bit-equal to ema_update + row_norms / normalize_rows. False
+// (nothing launched) when d is too large for the kernel's shared memory.
+bool ema_update_readout(eb_engine* e, float* pos, float* usage, const float* sums,
+                        const uint32_t* counts, size_t k, size_t d, float alpha, float decay,
+                        bool replace, bool spherical, float* readout,
+                        unsigned long long* cinfo, uint32_t gen);
+// The screen's centroid summary words and a fresh generation for them
+// (top1_tc.cu); a Top1Args with summary_gen set to it skips the summary pass.
+unsigned long long* screen_summary_words(eb_engine* e);
+uint32_t screen_next_summary_gen(eb_engine* e);
 void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids, size_t r0,
                  size_t r1, const uint32_t* labels, size_t k, float* sums, uint32_t* counts,
                  float* acc);
@@ -276,6 +290,14 @@ struct Top1Args {
   // The tensor-core screen's split copy of these centroids is already in its
   // scratch (a later slice of the same call): skip the conversion.
   bool centroids_ready = false;
+  // Nonzero: the screen's summary of these centroids (max |c|, norm bound,
+  // non-finite flag) is already in the engine's summary words under this
+  // generation (written by ema_update_readout): only the split copy is made.
+  uint32_t summary_gen = 0;
+  // The selection's rows already in split FP16 in selection order (position
+  // p at row p of the copy; a training epoch's rows): the screen reads it in
+  // place instead of converting or gathering.
+  const Fp16Copy* pre = nullptr;
 };
 // Full exact scan of every selected row.
 void top1_exact(eb_engine* e, const Top1Args& a);
@@ -298,6 +320,16 @@ size_t screen_tile_times(size_t rows, size_t k, int sms);
 bool top1_screen_supported(eb_engine* e, const Top1Args& a);
 void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf);
 void drop_f16(eb_buf* b);
+// The bound set's split copy (made on first use; null if xbuf is not a bound
+// set of that shape or there is no room), and copies indexed by selection
+// position: position_copy allocates one for cap positions (null if there is
+// no room), fill_position_copy gathers src's rows ids[0 .. rows) into it,
+// free_copy releases it (stream-ordered).
+Fp16Copy* bound_copy(eb_engine* e, eb_buf* xbuf, const float* x, size_t n, size_t d);
+Fp16Copy* position_copy(eb_engine* e, size_t cap, size_t d);
+void fill_position_copy(eb_engine* e, Fp16Copy* pc, const Fp16Copy* src, const uint32_t* ids,
+                        size_t rows);
+void free_copy(Fp16Copy* f);
 
 // ---- topk.cu
 void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, size_t d,

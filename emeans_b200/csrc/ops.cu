@@ -172,6 +172,145 @@ __global__ void k_ema(float* __restrict__ pos, float* __restrict__ usage,
   if (threadIdx.x == 0) usage[j] = mass;
 }
 
+// The EMA step (k_ema's arithmetic, bit for bit) fused with the next step's
+// readout of the updated centroid and the screen's summary of the centroids
+// it will read (k_cent_max's words: max |c|, a bound on the row norm, a
+// non-finite flag, under generation gen): the block holds the row in shared
+// memory after the update. L2 (SPH false): readout[j] = the row's squared
+// norm, sequential in column order (row_norms); the summary is of the row.
+// Spherical: readout row j = faiss normalize_into of the row (k_normalize's
+// arithmetic); the summary is of that normalised row. One block of 128
+// threads per centroid; d + 32 floats of dynamic shared memory.
+__device__ __forceinline__ unsigned long long summary_tag(uint32_t gen) {
+  return (unsigned long long)gen << 32;
+}
+template <bool SPH>
+__global__ void __launch_bounds__(128) k_ema_readout(
+    float* __restrict__ pos, float* __restrict__ usage, const float* __restrict__ sums,
+    const uint32_t* __restrict__ counts, int d, float a32, float decay, int replace,
+    float* __restrict__ readout, unsigned long long* __restrict__ cinfo, uint32_t gen) {
+  pdl_wait();
+  extern __shared__ float row_s[];  // [d], then 32 floats of reduction slots
+  float* red = row_s + d;
+  const long j = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float u = usage[j];
+  const uint32_t cnt = counts[j];
+  const float ud = replace ? u : __fmul_rn(u, decay);
+  float mass = ud;
+  float* c = pos + j * d;
+  if (cnt != 0) {
+    const float count = __uint2float_rn(cnt);
+    const float retained = replace ? 0.0f : ud;
+    const float step = __fmul_rn(a32, count);
+    mass = __fadd_rn(retained, step);
+    const float w = __fdiv_rn(step, mass);
+    const float* s = sums + j * d;
+    for (int t = tid; t < d; t += blockDim.x) {
+      const float mean = __fdiv_rn(s[t], count);
+      const float cv = c[t];
+      const float nv = w == 1.0f ? mean : __fadd_rn(cv, __fmul_rn(w, __fsub_rn(mean, cv)));
+      c[t] = nv;
+      row_s[t] = nv;
+    }
+  } else {
+    for (int t = tid; t < d; t += blockDim.x) row_s[t] = c[t];
+  }
+  __syncthreads();  // the row is in shared memory; every thread has read usage[j]
+  if (tid == 0) usage[j] = mass;
+  // Max |v| and finiteness of the row, over the block.
+  float mx = 0.0f;
+  int fin = 1;
+  for (int t = tid; t < d; t += blockDim.x) {
+    const float v = row_s[t];
+    fin &= isfinite(v) ? 1 : 0;
+    mx = fmaxf(mx, fabsf(v));
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+  fin = __all_sync(0xFFFFFFFFu, fin);
+  if (lane == 0) {
+    red[warp] = mx;
+    red[8 + warp] = fin ? 1.0f : 0.0f;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w2 = 1; w2 < (int)(blockDim.x >> 5); w2++) {
+      mx = fmaxf(mx, red[w2]);
+      fin = fin && red[8 + w2] != 0.0f;
+    }
+    red[16] = mx;
+    red[17] = fin ? 1.0f : 0.0f;
+  }
+  __syncthreads();
+  mx = red[16];
+  fin = red[17] != 0.0f;
+  if (!SPH) {
+    if (tid == 0) {
+      float ss = -0.0f;
+      for (int t = 0; t < d; t++) ss = __fadd_rn(ss, __fmul_rn(row_s[t], row_s[t]));
+      readout[j] = ss;
+      const unsigned long long tag = summary_tag(gen);
+      if (!fin) {
+        atomicMax(&cinfo[2], tag | 1ull);
+      } else {
+        atomicMax(&cinfo[0], tag | __float_as_uint(mx));
+        atomicMax(&cinfo[1], tag | __float_as_uint(sqrtf(ss) * (1.0f + 1.0f / 512.0f)));
+      }
+    }
+  } else {
+    const float sc = mx > 0.0f ? mx : 1.0f;
+    if (tid == 0) {
+      float ss = -0.0f;
+      for (int t = 0; t < d; t++) {
+        const float q = __fdiv_rn(row_s[t], sc);
+        ss = __fadd_rn(ss, __fmul_rn(q, q));
+      }
+      const float nrm = __fsqrt_rn(ss);
+      red[18] = nrm > 0.0f ? nrm : 1.0f;
+    }
+    __syncthreads();
+    const float s2 = red[18];
+    float* o = readout + j * d;
+    float omx = 0.0f, oss = 0.0f;
+    int ofin = 1;
+    for (int t = tid; t < d; t += blockDim.x) {
+      const float v = __fdiv_rn(__fdiv_rn(row_s[t], sc), s2);
+      o[t] = v;
+      ofin &= isfinite(v) ? 1 : 0;
+      omx = fmaxf(omx, fabsf(v));
+      oss = fmaf(v, v, oss);
+    }
+#pragma unroll
+    for (int q = 16; q >= 1; q >>= 1) {
+      omx = fmaxf(omx, __shfl_xor_sync(0xFFFFFFFFu, omx, q));
+      oss += __shfl_xor_sync(0xFFFFFFFFu, oss, q);
+    }
+    ofin = __all_sync(0xFFFFFFFFu, ofin);
+    __syncthreads();  // red[16..18] are no longer read
+    if (lane == 0) {
+      red[warp] = omx;
+      red[8 + warp] = oss;
+      red[16 + warp] = ofin ? 1.0f : 0.0f;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      for (int w2 = 1; w2 < (int)(blockDim.x >> 5); w2++) {
+        omx = fmaxf(omx, red[w2]);
+        oss += red[8 + w2];
+        ofin = ofin && red[16 + w2] != 0.0f;
+      }
+      const unsigned long long tag = summary_tag(gen);
+      if (!ofin) {
+        atomicMax(&cinfo[2], tag | 1ull);
+      } else {
+        atomicMax(&cinfo[0], tag | __float_as_uint(omx));
+        atomicMax(&cinfo[1], tag | __float_as_uint(sqrtf(oss) * (1.0f + 1.0f / 512.0f)));
+      }
+    }
+  }
+}
+
 // Revival splits, one block per (donor, dead) pair (core/mod.rs:374-399).
 __global__ void k_split(float* __restrict__ pos, float* __restrict__ usage,
                         const uint32_t* __restrict__ pairs, int d) {
@@ -605,6 +744,22 @@ void ema_update(eb_engine* e, float* pos, float* usage, const float* sums, const
   launch_pdl(e, k_ema, (unsigned)k, 128, 0, pos, usage, sums, counts, (int)d, alpha, decay,
                                            replace ? 1 : 0);
   EB_LAUNCH("ema_update");
+}
+
+bool ema_update_readout(eb_engine* e, float* pos, float* usage, const float* sums,
+                        const uint32_t* counts, size_t k, size_t d, float alpha, float decay,
+                        bool replace, bool spherical, float* readout,
+                        unsigned long long* cinfo, uint32_t gen) {
+  const size_t smem = (d + 32) * sizeof(float);
+  if (k == 0 || smem > 48 * 1024) return false;
+  if (spherical)
+    launch_pdl(e, k_ema_readout<true>, (unsigned)k, 128, smem, pos, usage, sums, counts, (int)d,
+               alpha, decay, replace ? 1 : 0, readout, cinfo, gen);
+  else
+    launch_pdl(e, k_ema_readout<false>, (unsigned)k, 128, smem, pos, usage, sums, counts, (int)d,
+               alpha, decay, replace ? 1 : 0, readout, cinfo, gen);
+  EB_LAUNCH("ema_update + readout");
+  return true;
 }
 
 void split(eb_engine* e, float* pos, float* usage, const uint32_t* d_pairs, size_t npairs,

@@ -64,14 +64,18 @@ struct Fp16Copy {
   cudaStream_t stream = nullptr;
 };
 
+void free_copy(Fp16Copy* f) {
+  if (!f) return;
+  if (f->xh) cudaFreeAsync(f->xh, f->stream);
+  if (f->xl) cudaFreeAsync(f->xl, f->stream);
+  if (f->xexp) cudaFreeAsync(f->xexp, f->stream);
+  if (f->xnrm) cudaFreeAsync(f->xnrm, f->stream);
+  delete f;
+}
+
 void drop_f16(eb_buf* b) {
   if (b && b->f16) {
-    Fp16Copy* f = b->f16;
-    cudaFreeAsync(f->xh, f->stream);
-    cudaFreeAsync(f->xl, f->stream);
-    cudaFreeAsync(f->xexp, f->stream);
-    cudaFreeAsync(f->xnrm, f->stream);
-    delete f;
+    free_copy(b->f16);
     b->f16 = nullptr;
   }
 }
@@ -1992,20 +1996,36 @@ void screen_bound(size_t d, float& e_rel, float& e_abs, float& e_min, bool one_a
 }
 
 
-// The scaled split FP16 copy of k rows of c (centroids, or data rows playing
-// them) and their summary under a new generation, which is returned.
-uint32_t convert_centroids(eb_engine* e, const float* c, size_t k, size_t d, size_t dp,
-                           unsigned long long* cinfo, __half* ch, __half* cl) {
+// A fresh generation of the centroid summary words.
+uint32_t next_gen(eb_engine* e, unsigned long long* cinfo) {
   if (++e->cinfo_gen == 0) {  // wrapped: older tags could compare higher
     EB_CUDA(cudaMemsetAsync(cinfo, 0, 4 * sizeof(unsigned long long), e->stream));
     e->cinfo_gen = 1;
   }
-  const uint32_t gen = e->cinfo_gen;
-  launch_pdl(e, k_cent_max, (unsigned)((k + 1) / 2), 64, 0, c, (long)k, (int)d, cinfo, gen);
-  EB_LAUNCH("screen centroid max");
+  return e->cinfo_gen;
+}
+
+// The scaled split FP16 copy of k rows of c (centroids, or data rows playing
+// them) under summary generation gen; with `summarise`, the summary is made
+// first (else a kernel before wrote it under gen).
+void convert_with(eb_engine* e, const float* c, size_t k, size_t d, size_t dp,
+                  unsigned long long* cinfo, uint32_t gen, bool summarise, __half* ch,
+                  __half* cl) {
+  if (summarise) {
+    launch_pdl(e, k_cent_max, (unsigned)((k + 1) / 2), 64, 0, c, (long)k, (int)d, cinfo, gen);
+    EB_LAUNCH("screen centroid max");
+  }
   launch_pdl(e, k_cent_conv, (unsigned)((k + 1) / 2), 64, 0, c, (long)k, (int)d, (int)dp, cinfo,
-                                                            gen, ch, cl);
+             gen, ch, cl);
   EB_LAUNCH("screen centroid convert");
+}
+
+// The scaled split FP16 copy of k rows of c and their summary under a new
+// generation, which is returned.
+uint32_t convert_centroids(eb_engine* e, const float* c, size_t k, size_t d, size_t dp,
+                           unsigned long long* cinfo, __half* ch, __half* cl) {
+  const uint32_t gen = next_gen(e, cinfo);
+  convert_with(e, c, k, d, dp, cinfo, gen, true, ch, cl);
   return gen;
 }
 
@@ -2040,6 +2060,78 @@ size_t screen_tile_times(size_t rows, size_t k, int sms) {
   return (rtiles * (size_t)p + (size_t)sms - 1) / (size_t)sms * tpp;
 }
 
+unsigned long long* screen_summary_words(eb_engine* e) {
+  return e->scratch_get<unsigned long long>("tc_cinfo", 4, true);
+}
+
+uint32_t screen_next_summary_gen(eb_engine* e) { return next_gen(e, screen_summary_words(e)); }
+
+// The split FP16 copy of a bound data set (n x d rows x, buffer xbuf), made
+// on first use and kept until the buffer is written or freed; null when xbuf
+// is not a bound set of that shape or there is no room for the copy.
+Fp16Copy* bound_copy(eb_engine* e, eb_buf* xbuf, const float* x, size_t n, size_t d) {
+  if (!xbuf || xbuf->d != d || xbuf->len != n * d) return nullptr;
+  const size_t dp = (d + BKH - 1) / BKH * BKH;
+  const unsigned wpb = 8;
+  if (xbuf->f16 && xbuf->f16->version != xbuf->version) drop_f16(xbuf);
+  if (!xbuf->f16) {
+    auto* f = new Fp16Copy;
+    f->n = n;
+    f->d = d;
+    f->version = xbuf->version;
+    f->stream = e->stream;
+    const size_t cells = std::max<size_t>(n * dp, 8);
+    cudaError_t st = cudaMallocAsync(&f->xh, cells * 2, e->stream);
+    if (st == cudaSuccess) st = cudaMallocAsync(&f->xl, cells * 2, e->stream);
+    if (st == cudaSuccess) st = cudaMallocAsync(&f->xexp, std::max<size_t>(n, 1) * 4, e->stream);
+    if (st == cudaSuccess) st = cudaMallocAsync(&f->xnrm, std::max<size_t>(n, 1) * 4, e->stream);
+    e->device_allocs += 4;
+    xbuf->f16 = f;
+    if (st != cudaSuccess) {
+      drop_f16(xbuf);  // no room for the copy: convert per pass instead
+      cudaGetLastError();
+    } else if (n) {
+      launch_pdl(e, k_prep_rows, (unsigned)((n + wpb - 1) / wpb), wpb * 32, 0, x, (long)n,
+                 (int)d, (int)dp, nullptr, 0, (long)n, f->xh, f->xl, f->xexp, f->xnrm,
+                 e->d_status);
+      EB_LAUNCH("screen copy of bound rows");
+    }
+  }
+  return xbuf->f16;
+}
+
+Fp16Copy* position_copy(eb_engine* e, size_t cap, size_t d) {
+  const size_t dp = (d + BKH - 1) / BKH * BKH;
+  auto* f = new Fp16Copy;
+  f->n = cap;
+  f->d = d;
+  f->stream = e->stream;
+  const size_t cells = std::max<size_t>(cap * dp, 8);
+  cudaError_t st = cudaMallocAsync(&f->xh, cells * 2, e->stream);
+  if (st == cudaSuccess) st = cudaMallocAsync(&f->xl, cells * 2, e->stream);
+  if (st == cudaSuccess) st = cudaMallocAsync(&f->xexp, std::max<size_t>(cap, 1) * 4, e->stream);
+  if (st == cudaSuccess) st = cudaMallocAsync(&f->xnrm, std::max<size_t>(cap, 1) * 4, e->stream);
+  e->device_allocs += 4;
+  if (st != cudaSuccess) {
+    free_copy(f);
+    cudaGetLastError();
+    return nullptr;
+  }
+  return f;
+}
+
+void fill_position_copy(eb_engine* e, Fp16Copy* pc, const Fp16Copy* src, const uint32_t* ids,
+                        size_t rows) {
+  if (rows == 0) return;
+  const size_t dp = (pc->d + BKH - 1) / BKH * BKH;
+  const unsigned wpb = 8;
+  launch_pdl(e, k_gather_rows, (unsigned)((rows + wpb - 1) / wpb), wpb * 32, 0, src->xh, src->xl,
+             src->xexp, src->xnrm, (long)src->n, (int)dp, ids, 0L, (long)rows, pc->xh, pc->xl,
+             pc->xexp, pc->xnrm, e->d_status);
+  EB_LAUNCH("epoch row gather");
+  pc->version = 1;
+}
+
 bool top1_screen_supported(eb_engine* e, const Top1Args& a) {
   if (e->screen_mode == 0) return false;
   if (a.d > 16384 || a.k > 0x7FFFFFFF) return false;
@@ -2066,8 +2158,13 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   __half* ch = e->scratch_get<__half>("tc_ch", k * dp);
   __half* cl = e->scratch_get<__half>("tc_cl", k * dp);
   const unsigned wpb = 8;
-  const uint32_t cgen =
-      a.centroids_ready ? e->cinfo_gen : convert_centroids(e, a.c, k, d, dp, cinfo, ch, cl);
+  uint32_t cgen = e->cinfo_gen;
+  if (!a.centroids_ready) {
+    if (a.summary_gen && a.summary_gen == e->cinfo_gen)
+      convert_with(e, a.c, k, d, dp, cinfo, a.summary_gen, false, ch, cl);
+    else
+      cgen = convert_centroids(e, a.c, k, d, dp, cinfo, ch, cl);
+  }
   const CUtensorMap mapBh = make_map(ch, k, dp, BN);
   const CUtensorMap mapBl = make_map(cl, k, dp, BN);
 
@@ -2116,38 +2213,20 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
 
   // A bound data set keeps its split copy across calls (training steps,
   // repeated assigns): converted once, then read in place or gathered by id.
-  Fp16Copy* cache = nullptr;
-  if (xbuf && xbuf->d == d && xbuf->len == a.n * d) {
-    if (xbuf->f16 && xbuf->f16->version != xbuf->version) drop_f16(xbuf);
-    if (!xbuf->f16) {
-      auto* f = new Fp16Copy;
-      f->n = a.n;
-      f->d = d;
-      f->version = xbuf->version;
-      f->stream = e->stream;
-      const size_t cells = std::max<size_t>(a.n * dp, 8);
-      cudaError_t st = cudaMallocAsync(&f->xh, cells * 2, e->stream);
-      if (st == cudaSuccess) st = cudaMallocAsync(&f->xl, cells * 2, e->stream);
-      if (st == cudaSuccess) st = cudaMallocAsync(&f->xexp, std::max<size_t>(a.n, 1) * 4, e->stream);
-      if (st == cudaSuccess) st = cudaMallocAsync(&f->xnrm, std::max<size_t>(a.n, 1) * 4, e->stream);
-      e->device_allocs += 4;
-      xbuf->f16 = f;
-      if (st != cudaSuccess) {
-        drop_f16(xbuf);  // no room for the copy: convert per pass instead
-        cudaGetLastError();
-      } else if (a.n) {
-        launch_pdl(e, k_prep_rows, (unsigned)((a.n + wpb - 1) / wpb), wpb * 32, 0, a.x, (long)a.n, (int)d, (int)dp, nullptr, 0, (long)a.n, f->xh, f->xl, f->xexp,
-            f->xnrm, e->d_status);
-        EB_LAUNCH("screen copy of bound rows");
-      }
-    }
-    cache = xbuf->f16;
-  }
+  Fp16Copy* cache = bound_copy(e, xbuf, a.x, a.n, d);
+  const bool pre = a.pre && a.pre->d == d && a.r1 <= a.pre->n;
 
   for (size_t c0 = a.r0; c0 < a.r1; c0 += chunk) {
     const size_t m = std::min(chunk, a.r1 - c0);
     const __half *ah = xh, *al = xl;
-    if (cache && !a.ids) {
+    if (pre) {
+      // The selection's rows already gathered in selection order (a training
+      // epoch's copy): read in place at the positions.
+      ah = a.pre->xh + c0 * dp;
+      al = a.pre->xl + c0 * dp;
+      P.xexp = a.pre->xexp + c0;
+      P.xnrm = a.pre->xnrm + c0;
+    } else if (cache && !a.ids) {
       // Dense rows of the bound set: the screen reads the cached copy in place.
       ah = cache->xh + c0 * dp;
       al = cache->xl + c0 * dp;

@@ -218,6 +218,22 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   if (out->labels)
     for (size_t i = 0; i < n; i++) out->labels[i] = -1;
 
+  // Nonzero: the readout of dpos and the screen's summary of the next top-1's
+  // centroids were made by the last EMA kernel under this generation.
+  uint32_t readout_gen = 0;
+  // The bound rows' split FP16 copy, and an epoch copy in selection order:
+  // each epoch's rows are gathered from the split copy once, so that the
+  // screen reads every batch of the epoch in place.
+  struct EpochCopy {
+    Fp16Copy* c = nullptr;
+    ~EpochCopy() { free_copy(c); }
+  } epoch_copy;
+  if (e->screen_mode != 0) {
+    size_t cap = 0;
+    for (size_t rows : r.epoch_rows) cap = std::max(cap, rows);
+    if (bound_copy(e, data, static_cast<const float*>(data->ptr), n, d))
+      epoch_copy.c = position_copy(e, cap, d);
+  }
   for (size_t epoch = 0; epoch < n_epochs; epoch++) {
     const size_t rows = r.epoch_rows[epoch];
     next_order.get();
@@ -226,13 +242,18 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
     const bool last = epoch + 1 == n_epochs;
     EB_CUDA(cudaMemcpyAsync(order.u(), ord, rows * 4, cudaMemcpyHostToDevice, e->stream));
     EB_CUDA(cudaEventRecord(done.ev[2 + (epoch & 1)], e->stream));
+    if (epoch_copy.c) fill_position_copy(e, epoch_copy.c, data->f16, order.u(), rows);
     const size_t splits_before = n_splits;
     for (size_t b = 0; b < rows; b += bsz) {
       const size_t end = std::min(b + bsz, rows);
-      if (spherical)
-        normalize_rows(e, dpos.f(), k, d, readout.f());
-      else
-        row_norms(e, dpos.f(), k, d, readout.f());
+      // The readout: made by the last step's EMA kernel when it could (with
+      // the screen's summary of the centroids), else here.
+      if (!readout_gen) {
+        if (spherical)
+          normalize_rows(e, dpos.f(), k, d, readout.f());
+        else
+          row_norms(e, dpos.f(), k, d, readout.f());
+      }
       // In a group, rank q scores positions [b + q s, b + (q + 1) s) of the
       // batch and the slices are all-gathered; alone, the whole batch. By
       // default (group_shard 0) a batch is split only when that shortens
@@ -263,6 +284,8 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
         a.labels = labels_ep.u();
         a.scores = scores_ep.f();
         a.xnorm = data->xnorm;
+        a.summary_gen = readout_gen;
+        a.pre = epoch_copy.c;
         top1_dispatch(e, a, data);
       }
       if (reduce_mode) {
@@ -291,8 +314,16 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
                     labels_ep.u(), k, sums.f(), counts.u(), last ? pass.f() : nullptr);
       }
       const double alpha = host::scheduled_alpha(r.alpha0, step, r.total_steps);
-      ema_update(e, dpos.f(), mass.f(), sums.f(), counts.u(), k, d, (float)alpha,
-                 (float)(1.0 - alpha), alpha == 1.0);
+      // The EMA step, with the next step's readout and the screen's summary
+      // of the centroids it will read, in one kernel where d allows.
+      readout_gen = screen_next_summary_gen(e);
+      if (!ema_update_readout(e, dpos.f(), mass.f(), sums.f(), counts.u(), k, d, (float)alpha,
+                              (float)(1.0 - alpha), alpha == 1.0, spherical, readout.f(),
+                              screen_summary_words(e), readout_gen)) {
+        readout_gen = 0;
+        ema_update(e, dpos.f(), mass.f(), sums.f(), counts.u(), k, d, (float)alpha,
+                   (float)(1.0 - alpha), alpha == 1.0);
+      }
       if ((step + 1) % 5 == 0) {
         read_into(e, mass_h, mass.f(), k * 4);
         std::memcpy(mass_v.data(), mass_h, k * 4);
@@ -304,6 +335,7 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
           EB_CUDA(cudaMemcpyAsync(pairs.u(), plan_h, plan.size() * 4, cudaMemcpyHostToDevice,
                                   e->stream));
           split(e, dpos.f(), mass.f(), pairs.u(), plan.size() / 2, d);
+          readout_gen = 0;  // the split moved centroids: read them out afresh
           n_splits += plan.size() / 2;
         }
       }
