@@ -192,6 +192,7 @@ int eb_engine_destroy(eb_engine* e) {
       if (kv.second.p) cudaFreeAsync(kv.second.p, e->stream);
     cudaStreamSynchronize(e->stream);
     if (e->copy_stream) cudaStreamSynchronize(e->copy_stream);
+    if (e->down_stream) cudaStreamSynchronize(e->down_stream);
     for (cudaEvent_t v : e->stage_ev)
       if (v) cudaEventDestroy(v);
     for (auto& kv : e->pinned)
@@ -200,6 +201,7 @@ int eb_engine_destroy(eb_engine* e) {
     cudaFree(e->d_counters);
     cudaFreeHost(e->h_status);
     if (e->copy_stream) cudaStreamDestroy(e->copy_stream);
+    if (e->down_stream) cudaStreamDestroy(e->down_stream);
     cudaStreamDestroy(e->stream);
     delete e;
   });

@@ -57,7 +57,8 @@ struct Scratch {
   size_t bytes = 0;
 };
 
-struct Fp16Copy;  // FP16 screen copy of a bound data set (top1_tc.cu)
+struct Fp16Copy;  // split FP16 screen copy of a bound data set (top1_tc.cu)
+struct Q8Copy;    // fixed-point screen copy of a bound data set (top1_tc.cu)
 
 }  // namespace eb
 
@@ -69,10 +70,11 @@ struct eb_buf {
   // Bumped by every host write; caches derived from the buffer compare it.
   uint64_t version = 0;
   // For bound data sets: d, the rows' squared norms (CPU float order) and the
-  // FP16 screen copy.
+  // screen copies (split FP16 for top-k and products, fixed point for top-1).
   size_t d = 0;
   float* xnorm = nullptr;
   eb::Fp16Copy* f16 = nullptr;
+  eb::Q8Copy* q8 = nullptr;
 };
 
 struct eb_engine {
@@ -109,9 +111,11 @@ struct eb_engine {
   // Optional CUDA-event timing of the top-1 screen kernel (eb_set_kernel_timing):
   // one (start, end) pair per launch since the last eb_screen_timing read,
   // with the rows of that launch.
-  // Second stream for host-to-device copies that overlap compute (eb_assign),
+  // Second stream for host-to-device copies that overlap compute (eb_assign,
+  // training's epoch orders) and a third for training's epoch read-backs,
   // created on first use.
   cudaStream_t copy_stream = nullptr;
+  cudaStream_t down_stream = nullptr;
   bool time_screen = false;
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> screen_ev;
   std::vector<size_t> screen_ev_rows;
@@ -294,10 +298,6 @@ struct Top1Args {
   // non-finite flag) is already in the engine's summary words under this
   // generation (written by ema_update_readout): only the split copy is made.
   uint32_t summary_gen = 0;
-  // The selection's rows already in split FP16 in selection order (position
-  // p at row p of the copy; a training epoch's rows): the screen reads it in
-  // place instead of converting or gathering.
-  const Fp16Copy* pre = nullptr;
 };
 // Full exact scan of every selected row.
 void top1_exact(eb_engine* e, const Top1Args& a);
@@ -319,17 +319,10 @@ void screen_products(eb_engine* e, const float* x, size_t n, size_t d, eb_buf* x
 size_t screen_tile_times(size_t rows, size_t k, int sms);
 bool top1_screen_supported(eb_engine* e, const Top1Args& a);
 void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf);
-void drop_f16(eb_buf* b);
+void drop_f16(eb_buf* b);  // drops both screen copies
 // The bound set's split copy (made on first use; null if xbuf is not a bound
-// set of that shape or there is no room), and copies indexed by selection
-// position: position_copy allocates one for cap positions (null if there is
-// no room), fill_position_copy gathers src's rows ids[0 .. rows) into it,
-// free_copy releases it (stream-ordered).
+// set of that shape or there is no room).
 Fp16Copy* bound_copy(eb_engine* e, eb_buf* xbuf, const float* x, size_t n, size_t d);
-Fp16Copy* position_copy(eb_engine* e, size_t cap, size_t d);
-void fill_position_copy(eb_engine* e, Fp16Copy* pc, const Fp16Copy* src, const uint32_t* ids,
-                        size_t rows);
-void free_copy(Fp16Copy* f);
 
 // ---- topk.cu
 void topk(eb_engine* e, const float* q, size_t m, const float* data, size_t n, size_t d,

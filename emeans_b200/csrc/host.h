@@ -234,20 +234,34 @@ inline std::vector<uint32_t> plan_revival(const std::vector<float>& usage, doubl
     pre = &own;
   }
   rng = pre->after;
-  std::vector<std::pair<double, uint32_t>> keys;
+  // Keys in IEEE total order (the reference's total_cmp) as unsigned
+  // integers: the sign bit set flips every bit, else only the sign bit.
+  struct Key {
+    uint64_t key;
+    uint32_t j;
+  };
+  std::vector<Key> keys;
+  keys.reserve(n_donor);
   for (size_t j = 0; j < k; j++) {
     float u = usage[j];
-    if (!(u < threshold) && u > 0.0f) keys.emplace_back((double)std::log(u) - pre->g[j], (uint32_t)j);
+    if (!(u < threshold) && u > 0.0f) {
+      const double v = (double)std::log(u) - pre->g[j];
+      uint64_t bits;
+      std::memcpy(&bits, &v, 8);
+      bits = (bits >> 63) ? ~bits : bits | 0x8000000000000000ull;
+      keys.push_back({bits, (uint32_t)j});
+    }
   }
   // Larger key first, then larger index: a strict order (indices differ), so
-  // the first nsplit of a partial sort equal those of a stable sort.
-  std::partial_sort(keys.begin(), keys.begin() + nsplit, keys.end(), [](const auto& a, const auto& b) {
-    return a.first != b.first ? a.first > b.first : a.second > b.second;
-  });
+  // selecting the first nsplit and sorting them equals a stable sort's head.
+  auto before = [](const Key& a, const Key& b) { return a.key != b.key ? a.key > b.key : a.j > b.j; };
+  if (nsplit < keys.size()) std::nth_element(keys.begin(), keys.begin() + nsplit, keys.end(), before);
+  std::sort(keys.begin(), keys.begin() + nsplit, before);
+  plan.reserve(2 * nsplit);
   size_t t = 0;
   for (size_t i = 0; i < nsplit; i++) {
     while (!(usage[t] < threshold)) t++;
-    plan.push_back(keys[i].second);
+    plan.push_back(keys[i].j);
     plan.push_back((uint32_t)t++);
   }
   return plan;

@@ -1,24 +1,26 @@
-// Exact top-1 on the tensor cores: a tcgen05 screen on split FP16 operands,
-// then the exact FP32 chain for the few centroids the screen cannot rule out.
+// Exact top-1 on the tensor cores: a tcgen05 screen on 16-bit fixed-point
+// operands held as two int8 digits, then the exact FP32 chain for the few
+// centroids the screen cannot rule out. Top-k and the internal scores'
+// product use the same kernel on split FP16 operands.
 //
 // The labels and scores are the reference CPU kernel's bit for bit
 // (crates/emeans-core/src/assign/fused.rs:12-16: one sequential FMA chain per
 // dot, lower id on ties). The screen only decides which centroids get that
 // exact chain:
 //
-// 1. prep: rows (per-row exponent) and centroids (one exponent) are scaled by
-//    powers of two so that |v| < 2^14, and split into two FP16 terms,
-//    v' = hi + lo + r with |r| <= 2^-22 |v'| + 2^-24. A bound data set keeps
-//    this copy across calls.
-// 2. screen (tcgen05, persistent: one CTA per SM over 128-row tiles): each
-//    256-centroid tile accumulates xh.ch in one TMEM accumulator and
-//    xh.cl + xl.ch in a second (so the small terms are not rounded against the
-//    large partial sums); operands arrive by TMA in 64-byte-swizzled shared
-//    memory through a 4-stage mbarrier ring. The epilogue (one thread per row)
-//    adds the two accumulators, tracks the running best screened score and
-//    appends every centroid within 2e of it to the row's candidate list, where
-//    e bounds |screen - exact chain|. A centroid more than 2e behind the best
-//    cannot be the exact winner.
+// 1. prep: each row is scaled by its own power of two 2^sx (the centroids by
+//    one, 2^sc) so that its largest value is at most 32639, rounded to
+//    integers v, and kept as digits v = 256 hi + lo (int8 each). A bound data
+//    set keeps this copy across calls.
+// 2. screen (tcgen05 kind::i8, persistent: one CTA per SM over 128-row
+//    tiles): each 256-centroid tile accumulates hi.hi in one TMEM
+//    accumulator and hi.lo + lo.hi in a second, both exact int32 sums;
+//    operands arrive by TMA in 64-byte-swizzled shared memory through a
+//    4-stage mbarrier ring. The epilogue (one thread per row) forms
+//    65536 hi.hi + 256 (hi.lo + lo.hi) in FP32, tracks the running best
+//    screened score and appends every centroid within 2e of it to the row's
+//    candidate list, where e bounds |screen - exact chain|. A centroid more
+//    than 2e behind the best cannot be the exact winner.
 // 3. collect: each row's candidates still inside the final window become
 //    (row, centroid) pairs.
 // 4. pairs: one thread per pair runs the exact FMA chain (operands streamed
@@ -28,7 +30,15 @@
 //    gave up are scanned exactly against every centroid, parallel over
 //    (row, block of centroids) with the same keyed reduction.
 //
-// Error bound in accumulator units (operands scaled, u = 2^-11):
+// Fixed-point error bound (integer units, x' = x 2^sx, c' = c 2^sc): the
+// rounding to integers, sqrt(d) (|x'| + |c'|) / 2 + d / 4; the dropped lo.lo
+// products, |x lo| |c lo|; the FP32 evaluation, 2^-22 (|x'| + 160 sqrt(d))
+// (|c'| + 160 sqrt(d)); and the FP32 chain, gamma_d |x'| |c'|
+// (screen_bound_q8 derives each term).
+//
+// Split FP16 (top-k, products): values scaled by powers of two so that
+// |v| < 2^14 and split into two FP16 terms, v' = hi + lo + r with
+// |r| <= 2^-22 |v'| + 2^-24; its error bound in accumulator units (u = 2^-11):
 //   split operands:   3 2^-22 sum|x'||c'| + 2^-23 (sum|x'| + sum|c'|)
 //   accumulation:     d 2^-21 sum|x'||c'| (four times the per-addition
 //                     truncation bound), the lo accumulator d 2^-30, the final
@@ -73,10 +83,34 @@ void free_copy(Fp16Copy* f) {
   delete f;
 }
 
+// The fixed-point screen copy of a bound data set (top-1), built by the first
+// top-1 on the set and kept like the split copy.
+struct Q8Copy {
+  int8_t* xh = nullptr;  // n x dp, high digits
+  int8_t* xl = nullptr;  // n x dp, low digits
+  int* xexp = nullptr;   // shifts
+  float* xnrm = nullptr;
+  float* xlo = nullptr;  // bounds on the low digits' norms
+  size_t n = 0, d = 0;
+  uint64_t version = 0;
+  cudaStream_t stream = nullptr;
+};
+
+void free_q8(Q8Copy* f) {
+  if (!f) return;
+  for (void* p : {(void*)f->xh, (void*)f->xl, (void*)f->xexp, (void*)f->xnrm, (void*)f->xlo})
+    if (p) cudaFreeAsync(p, f->stream);
+  delete f;
+}
+
 void drop_f16(eb_buf* b) {
   if (b && b->f16) {
     free_copy(b->f16);
     b->f16 = nullptr;
+  }
+  if (b && b->q8) {
+    free_q8(b->q8);
+    b->q8 = nullptr;
   }
 }
 
@@ -85,6 +119,8 @@ namespace {
 constexpr int BM = 128;          // rows per tile (TMEM lanes)
 constexpr int BN = 256;          // centroids per tile (TMEM columns per accumulator)
 constexpr int BKH = 32;          // FP16 columns per k-block: one 64-byte swizzle row
+constexpr int BK8 = 64;          // int8 columns per k-block (top-1): the same 64 bytes
+constexpr float Q8_MAX = 32639.0f;  // largest |v| of a fixed-point value: 256 x 127 + 127
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BKH * 2;                // one of xh / xl
 constexpr int B_BYTES = BN * BKH * 2;                // one of ch / cl
@@ -194,6 +230,20 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate)
+      : "memory");
+}
+
+// kind::i8 instruction descriptor: S8 x S8 -> S32, both K-major, M=128, N=256.
+constexpr uint32_t IDESC_I8 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                              ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(IDESC_I8), "r"(accumulate)
       : "memory");
 }
 
@@ -356,13 +406,144 @@ __global__ void k_prep_rows(const float* __restrict__ x, long n, int d, int dp,
   }
 }
 
-// Rows x[ids[p]] of a cached split copy gathered into the pass's staging rows
-// (one warp per row, 16-byte copies; dp * 2 bytes is a multiple of 64).
-__global__ void k_gather_rows(const __half* __restrict__ src_h, const __half* __restrict__ src_l,
-                              const int* __restrict__ src_e, const float* __restrict__ src_n,
-                              long n, int dp, const uint32_t* __restrict__ ids, long p0, long m,
-                              __half* __restrict__ xh, __half* __restrict__ xl,
-                              int* __restrict__ xexp, float* __restrict__ xnrm, uint32_t* status) {
+// ---- the top-1 screen's fixed-point copies
+//
+// A row (or the centroid set) is scaled by 2^sh, sh the largest shift with
+// max |x| 2^sh <= Q8_MAX, and each value rounded to the integer v = rint(x 2^sh)
+// (|x 2^sh - v| <= 1/2), kept as two int8 digits v = 256 hi + lo, hi in
+// [-127, 127], lo in [-128, 127].
+
+// The shift of a set with largest magnitude mx (15 for mx = 0).
+__device__ __forceinline__ int q8_shift(float mx) {
+  int e = 0;
+  frexpf(mx, &e);  // mx = f 2^e, f in [0.5, 1)
+  int sh = 15 - e;
+  if (ldexpf(mx, sh) > Q8_MAX) sh--;
+  return sh;
+}
+
+// The digits of an integral v with |v| <= Q8_MAX (every step exact).
+__device__ __forceinline__ void split8(float v, int& hi, int& lo) {
+  hi = __float2int_rd((v + 128.0f) * (1.0f / 256.0f));
+  lo = (int)v - 256 * hi;
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return (uint32_t)(a & 0xFF) | (uint32_t)(b & 0xFF) << 8 | (uint32_t)(c & 0xFF) << 16 |
+         (uint32_t)(d & 0xFF) << 24;
+}
+
+// Fixed-point copy of the selected rows (one warp per row): digits xh, xl
+// (dp bytes a row, zero-padded), the row's shift (XEXP_BAD for non-finite
+// rows), an upper bound on its norm and on the norm of its low digits.
+__global__ void k_prep_rows_q8(const float* __restrict__ x, long n, int d, int dp,
+                               const uint32_t* __restrict__ ids, long p0, long m,
+                               int8_t* __restrict__ xh, int8_t* __restrict__ xl,
+                               int* __restrict__ xexp, float* __restrict__ xnrm,
+                               float* __restrict__ xlo, uint32_t* status) {
+  pdl_wait();
+  const long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (i >= m) return;
+  const long p = p0 + i;
+  const long row = ids ? (long)ids[p] : p;
+  int8_t* oh = xh + i * (long)dp;
+  int8_t* ol = xl + i * (long)dp;
+  if (row >= n) {
+    if (lane == 0) {
+      atomicOr(status, ST_BAD_ROW);
+      xexp[i] = XEXP_BAD;
+      xnrm[i] = 0.0f;
+      xlo[i] = 0.0f;
+    }
+    for (int t = lane; t < dp / 4; t += 32)
+      reinterpret_cast<uint32_t*>(oh)[t] = reinterpret_cast<uint32_t*>(ol)[t] = 0u;
+    return;
+  }
+  const float* r = x + row * (long)d;
+  float mx = 0.0f, ss = 0.0f, sl = 0.0f;
+  bool finite = true;
+  int sh = 0;
+  if ((d & 3) == 0 && d <= 1024) {
+    // One read: up to 8 float4 per lane stay in registers.
+    const float4* r4 = reinterpret_cast<const float4*>(r);
+    const int q4 = d / 4;
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int t = lane + 32 * u;
+      v[u] = t < q4 ? __ldg(r4 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
+      finite = finite && isfinite(v[u].x) && isfinite(v[u].y) && isfinite(v[u].z) &&
+               isfinite(v[u].w);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+      ss = fmaf(v[u].x, v[u].x, fmaf(v[u].y, v[u].y, fmaf(v[u].z, v[u].z, fmaf(v[u].w, v[u].w, ss))));
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+      ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    }
+    finite = __all_sync(0xFFFFFFFFu, finite);
+    sh = q8_shift(mx);
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int t = lane + 32 * u;
+      if (t < q4) {
+        const float a[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        int h[4], l[4];
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+          split8(finite ? rintf(ldexpf(a[w], sh)) : 0.0f, h[w], l[w]);
+          sl = fmaf((float)l[w], (float)l[w], sl);
+        }
+        reinterpret_cast<uint32_t*>(oh)[t] = pack4(h[0], h[1], h[2], h[3]);
+        reinterpret_cast<uint32_t*>(ol)[t] = pack4(l[0], l[1], l[2], l[3]);
+      }
+    }
+    for (int t = q4 + lane; t < dp / 4; t += 32)
+      reinterpret_cast<uint32_t*>(oh)[t] = reinterpret_cast<uint32_t*>(ol)[t] = 0u;
+  } else {
+    for (int t = lane; t < d; t += 32) {
+      const float v = __ldg(r + t);
+      finite = finite && isfinite(v);
+      mx = fmaxf(mx, fabsf(v));
+      ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+      ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    }
+    finite = __all_sync(0xFFFFFFFFu, finite);
+    sh = q8_shift(mx);
+    for (int t = lane; t < dp; t += 32) {
+      const float v = (t < d && finite) ? rintf(ldexpf(__ldg(r + t), sh)) : 0.0f;
+      int h, l;
+      split8(v, h, l);
+      oh[t] = (int8_t)h;
+      ol[t] = (int8_t)l;
+      sl = fmaf((float)l, (float)l, sl);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) sl += __shfl_xor_sync(0xFFFFFFFFu, sl, o);
+  if (lane == 0) {
+    xexp[i] = finite ? sh : XEXP_BAD;
+    // Any-order sums of squares: relative error < d 2^-24; inflate by 2^-9.
+    xnrm[i] = finite ? sqrtf(ss) * (1.0f + 1.0f / 512.0f) : 0.0f;
+    xlo[i] = finite ? sqrtf(sl) * (1.0f + 1.0f / 512.0f) : 0.0f;
+  }
+}
+
+// Rows x[ids[p]] of a cached fixed-point copy gathered into the pass's
+// staging rows (one warp per row, 16-byte copies; dp is a multiple of 64).
+__global__ void k_gather_rows_q8(const int8_t* __restrict__ src_h, const int8_t* __restrict__ src_l,
+                                 const int* __restrict__ src_e, const float* __restrict__ src_n,
+                                 const float* __restrict__ src_lo, long n, int dp,
+                                 const uint32_t* __restrict__ ids, long p0, long m,
+                                 int8_t* __restrict__ xh, int8_t* __restrict__ xl,
+                                 int* __restrict__ xexp, float* __restrict__ xnrm,
+                                 float* __restrict__ xlo, uint32_t* status) {
   pdl_wait();
   const long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -370,13 +551,14 @@ __global__ void k_gather_rows(const __half* __restrict__ src_h, const __half* __
   const long row = ids[p0 + i];
   uint4* oh = reinterpret_cast<uint4*>(xh + i * (long)dp);
   uint4* ol = reinterpret_cast<uint4*>(xl + i * (long)dp);
-  const int q = dp / 8;
+  const int q = dp / 16;
   if (row >= n) {
     for (int t = lane; t < q; t += 32) oh[t] = ol[t] = make_uint4(0, 0, 0, 0);
     if (lane == 0) {
       atomicOr(status, ST_BAD_ROW);
       xexp[i] = XEXP_BAD;
       xnrm[i] = 0.0f;
+      xlo[i] = 0.0f;
     }
     return;
   }
@@ -389,11 +571,14 @@ __global__ void k_gather_rows(const __half* __restrict__ src_h, const __half* __
   if (lane == 0) {
     xexp[i] = src_e[row];
     xnrm[i] = src_n[row];
+    xlo[i] = src_lo[row];
   }
 }
 
 // The centroid summary: u64 words (generation << 32 | payload), [0] bits of
-// max |c|, [1] bits of a bound on max |c_j|, [2] non-finite flag. The words
+// max |c|, [1] bits of a bound on max |c_j|, [2] non-finite flag, [3] (the
+// fixed-point conversion) bits of a bound on the largest norm of a
+// centroid's low digits. The words
 // are atomic maxima, so a word from an older generation (a smaller tag) is
 // replaced by the first write of this one; a reader takes a word whose tag is
 // not the current generation as 0.
@@ -493,6 +678,57 @@ __global__ void __launch_bounds__(64) k_cent_conv(const float* __restrict__ c, l
   }
 }
 
+// Fixed-point centroids under the set's one shift (from max |c|): digits ch,
+// cl (dp bytes a centroid, zero-padded), and the largest norm of a centroid's
+// low digits into summary word 3. One warp per centroid, two per block.
+__global__ void __launch_bounds__(64) k_cent_conv_q8(const float* __restrict__ c, long k, int d,
+                                                     int dp,
+                                                     unsigned long long* __restrict__ cinfo,
+                                                     uint32_t gen, int8_t* __restrict__ ch,
+                                                     int8_t* __restrict__ cl) {
+  pdl_wait();
+  const long j = (long)blockIdx.x * 2 + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (j >= k) return;
+  const int sh = q8_shift(__uint_as_float(cinfo_word(cinfo, 0, gen)));
+  const bool bad = cinfo_word(cinfo, 2, gen) != 0;
+  const float* r = c + j * (long)d;
+  int8_t* oh = ch + j * (long)dp;
+  int8_t* ol = cl + j * (long)dp;
+  float sl = 0.0f;
+  if ((d & 3) == 0 && ((uintptr_t)c & 15) == 0) {
+    const float4* r4 = reinterpret_cast<const float4*>(r);
+#pragma unroll 2
+    for (int t = lane; t < dp / 4; t += 32) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (4 * t < d && !bad) v = __ldg(r4 + t);
+      const float a[4] = {v.x, v.y, v.z, v.w};
+      int h[4], l[4];
+#pragma unroll
+      for (int w = 0; w < 4; w++) {
+        split8(rintf(ldexpf(a[w], sh)), h[w], l[w]);
+        sl = fmaf((float)l[w], (float)l[w], sl);
+      }
+      reinterpret_cast<uint32_t*>(oh)[t] = pack4(h[0], h[1], h[2], h[3]);
+      reinterpret_cast<uint32_t*>(ol)[t] = pack4(l[0], l[1], l[2], l[3]);
+    }
+  } else {
+    for (int t = lane; t < dp; t += 32) {
+      const float v = (t < d && !bad) ? rintf(ldexpf(__ldg(r + t), sh)) : 0.0f;
+      int h, l;
+      split8(v, h, l);
+      oh[t] = (int8_t)h;
+      ol[t] = (int8_t)l;
+      sl = fmaf((float)l, (float)l, sl);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) sl += __shfl_xor_sync(0xFFFFFFFFu, sl, o);
+  if (lane == 0)
+    atomicMax(&cinfo[3], (unsigned long long)gen << 32 |
+                             __float_as_uint(sqrtf(sl) * (1.0f + 1.0f / 512.0f)));
+}
+
 // Top-k mode: v (> kv[0]) replaces the smallest of the ascending kv[0 .. KMAX)
 // and takes its place in the order. The slots below v's place each take the
 // next slot's value: independent selects instead of a chain of KMAX - 1
@@ -523,12 +759,14 @@ struct ScreenParams {
   int parts;
   int tpp;             // centroid tiles per part
   int units;           // ceil(m / 128) * parts
-  const int* xexp;     // per staging row
+  const int* xexp;     // per staging row (fixed point: the row's shift)
   const float* xnrm;   // per staging row
+  const float* xlo;    // per staging row, fixed point: a bound on its low digits' norm
   const float* cn;     // k squared centroid norms (L2) or null
   const unsigned long long* cinfo;  // the centroid summary of generation cgen
   uint32_t cgen;
   float e_rel, e_abs, e_min;  // bound coefficients (see the header comment)
+  float e_lo;                 // fixed point: the coefficient of the low-digit term
   // Candidate lists, one per (part, half tile, row): list L = 2 part + half,
   // entry e of row i at (L C + e) m + i (id, screened value bits), C = CAP
   // (CAP_TOPK in top-k mode; top-k mode has one part).
@@ -565,7 +803,7 @@ struct ScreenParams {
   int dead_wait;
 };
 
-template <bool IP, bool TOPK = false, bool PROD = false>
+template <bool IP, bool TOPK = false, bool PROD = false, bool Q8 = false>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_screen(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
              const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
@@ -637,10 +875,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const int nt = t2 / P.kblocks, kb = t2 % P.kblocks;
           uint8_t* st = smem + s * STAGE_BYTES;
           mbar_expect_tx(&full[s], STAGE_BYTES);
-          tma_load_2d(st, &tmAh, &full[s], kb * BKH, (int)(rt * BM));
-          tma_load_2d(st + A_BYTES, &tmAl, &full[s], kb * BKH, (int)(rt * BM));
-          tma_load_2d(st + 2 * A_BYTES, &tmBh, &full[s], kb * BKH, nt * BN);
-          tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[s], kb * BKH, nt * BN);
+          const int kx = kb * (Q8 ? BK8 : BKH);  // 64 bytes of every row either way
+          tma_load_2d(st, &tmAh, &full[s], kx, (int)(rt * BM));
+          tma_load_2d(st + A_BYTES, &tmAl, &full[s], kx, (int)(rt * BM));
+          tma_load_2d(st + 2 * A_BYTES, &tmBh, &full[s], kx, nt * BN);
+          tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[s], kx, nt * BN);
           issued = it + 1;
         }
       }
@@ -690,6 +929,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 umma_f16(dacc, umma_desc(ah + kk * 32), umma_desc(bh + kk * 32), first);
                 umma_f16(dacc, umma_desc(ah + kk * 32), umma_desc(bl + kk * 32), 1u);
                 umma_f16(dacc, umma_desc(al + kk * 32), umma_desc(bh + kk * 32), 1u);
+              } else if constexpr (Q8) {
+                // 32 int8 columns per MMA: hi.hi, and hi.lo + lo.hi (exact int32 sums).
+                umma_i8(tmem, umma_desc(ah + kk * 32), umma_desc(bh + kk * 32), first);
+                umma_i8(tmem + BN, umma_desc(ah + kk * 32), umma_desc(bl + kk * 32), first);
+                umma_i8(tmem + BN, umma_desc(al + kk * 32), umma_desc(bh + kk * 32), 1u);
               } else {
                 umma_f16(tmem, umma_desc(ah + kk * 32), umma_desc(bh + kk * 32), first);
                 umma_f16(tmem + BN, umma_desc(ah + kk * 32), umma_desc(bl + kk * 32), first);
@@ -720,10 +964,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int q = warp & 3;
     const int hf = (warp - 4) >> 2;
     const int r = q * 32 + lane;
+    // The centroids' scale: split FP16, c' = c 2^(14 - ec); fixed point,
+    // c' = c 2^sc (then ec = -sc), and a bound on their low digits' norms.
     int ec = 0;
-    frexpf(__uint_as_float(cinfo_word(P.cinfo, 0, P.cgen)), &ec);
+    if constexpr (Q8)
+      ec = -q8_shift(__uint_as_float(cinfo_word(P.cinfo, 0, P.cgen)));
+    else
+      frexpf(__uint_as_float(cinfo_word(P.cinfo, 0, P.cgen)), &ec);
     const float cmax = __uint_as_float(cinfo_word(P.cinfo, 1, P.cgen));
     const bool c_bad = cinfo_word(P.cinfo, 2, P.cgen) != 0;
+    const float clo = Q8 ? __uint_as_float(cinfo_word(P.cinfo, 3, P.cgen)) : 0.0f;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(hf * HALF);
     float* cns = cn_s + (warp - 4) * HALF;
     float* svs = sv_s + (warp - 4) * 16 * 32 + lane;  // this lane's column of the slab
@@ -750,15 +1000,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int ex = live ? P.xexp[i] : XEXP_BAD;
       bool fallback = !live || ex == XEXP_BAD || c_bad;
       const float xn = live ? P.xnrm[i] : 0.0f;
-      // |x'| and max |c'| in accumulator units, and the bound e there.
-      const float xs = ldexpf(xn, 14 - (fallback ? 0 : ex));
-      const float cs = ldexpf(cmax, 14 - ec);
-      const float e_acc = fmaf(P.e_rel * xs, cs, fmaf(P.e_abs, xs + cs, P.e_min));
+      // |x'| and max |c'| in accumulator units, and the bound e there. Fixed
+      // point: ex holds the row's shift, x' = x 2^ex, and the dropped lo.lo
+      // products add at most |x lo| max |c lo|.
+      const int xsh = Q8 ? (fallback ? 0 : ex) : 14 - (fallback ? 0 : ex);
+      const float xs = ldexpf(xn, xsh);
+      const float cs = ldexpf(cmax, Q8 ? -ec : 14 - ec);
+      float e_acc = fmaf(P.e_rel * xs, cs, fmaf(P.e_abs, xs + cs, P.e_min));
+      if (Q8) e_acc = fmaf(P.e_lo * (live ? P.xlo[i] : 0.0f), clo, e_acc);
       float off, m2f = 1.0f;  // screened value = m2f acc + cn (IP: acc + 0)
       if (IP) {
         off = 2.0f * e_acc;
       } else {
-        const int fe = ex + ec - 28;
+        // The dot is 2^fe acc.
+        const int fe = Q8 ? -xsh + ec : ex + ec - 28;
         if (fe < -100 || fe > 100) fallback = true;
         const float f = ldexpf(1.0f, fallback ? 0 : fe);
         m2f = -2.0f * f;
@@ -843,9 +1098,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int h2 = 0; h2 < LOG; h2++)
 #pragma unroll
-              for (int j = 0; j < 16; j++)
-                acc[LOG * p2 + h2][j] = __float_as_uint(__fadd_rn(
-                    __uint_as_float(acc[LOG * p2 + h2][j]), __uint_as_float(lo[h2][j])));
+              for (int j = 0; j < 16; j++) {
+                uint32_t& a = acc[LOG * p2 + h2][j];
+                if constexpr (Q8)  // 65536 hi + 256 (hi.lo + lo.hi), from the int32 sums
+                  a = __float_as_uint(__fmaf_rn(__int2float_rn((int)a), 65536.0f,
+                                                __int2float_rn((int)lo[h2][j]) * 256.0f));
+                else
+                  a = __float_as_uint(__fadd_rn(__uint_as_float(a), __uint_as_float(lo[h2][j])));
+              }
           }
           tc_fence_before();
           mbar_arrive(tempty);
@@ -1869,13 +2129,29 @@ CUtensorMap make_map(const void* base, size_t rows, size_t dp, uint32_t box_rows
   return m;
 }
 
+// The same for a fixed-point copy: int8 digits, dp8 bytes a row, boxes of
+// 64 columns (64 bytes) by box_rows.
+CUtensorMap make_map_q8(const void* base, size_t rows, size_t dp8, uint32_t box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)dp8, (cuuint64_t)std::max<size_t>(rows, 1)};
+  cuuint64_t strides[1] = {(cuuint64_t)dp8};
+  cuuint32_t box[2] = {(cuuint32_t)BK8, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(EB_ERROR, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  return m;
+}
+
 // Dynamic shared memory limits are per-device, per-kernel attributes.
-template <bool IP, bool TOPK, bool PROD = false>
+template <bool IP, bool TOPK, bool PROD = false, bool Q8 = false>
 void set_smem(int device) {
   static uint64_t done = 0;  // one instance per kernel: the template parameters
   if (!(done >> device & 1)) {
-    EB_CUDA(cudaFuncSetAttribute(k_screen<IP, TOPK, PROD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)SMEM_BYTES));
+    EB_CUDA(cudaFuncSetAttribute(k_screen<IP, TOPK, PROD, Q8>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
     done |= 1ull << device;
   }
 }
@@ -1913,11 +2189,11 @@ void set_list_smem(int device) {
   }
 }
 
-template <bool IP, bool TOPK = false, bool PROD = false>
+template <bool IP, bool TOPK = false, bool PROD = false, bool Q8 = false>
 void launch_screen(eb_engine* e, unsigned grid, const CUtensorMap& ah, const CUtensorMap& al,
                    const CUtensorMap& bh, const CUtensorMap& bl, const ScreenParams& P) {
-  set_smem<IP, TOPK, PROD>(e->device);
-  launch_pdl(e, k_screen<IP, TOPK, PROD>, grid, NTHREADS, SMEM_BYTES, ah, al, bh, bl, P);
+  set_smem<IP, TOPK, PROD, Q8>(e->device);
+  launch_pdl(e, k_screen<IP, TOPK, PROD, Q8>, grid, NTHREADS, SMEM_BYTES, ah, al, bh, bl, P);
 }
 
 // Scratch of the exact stage of one pass of m rows.
@@ -1996,6 +2272,29 @@ void screen_bound(size_t d, float& e_rel, float& e_abs, float& e_min, bool one_a
 }
 
 
+// The fixed-point screen's bound coefficients for this d, with 1% slack, in
+// the integer units of the digits (x' = x 2^sx, c' = c 2^sc real, v = rint(x'),
+// w = rint(c') with |x' - v|, |c' - w| <= 1/2; the MMAs sum 65536 hi.hi +
+// 256 (hi.lo + lo.hi) exactly and drop L = sum lo.lo):
+//   rounding to integers:  |sum x'c' - sum v w| <= (|c'|_1 + |v|_1) / 2
+//                          <= sqrt(d) (|x'| + |c'|) / 2 + d / 4
+//   dropped products:      |L| <= |x lo| |c lo|                      (e_lo)
+//   FP32 evaluation of the two sums and their combination (three roundings,
+//   at most 2^-23 (65536 |hi.hi| + 256 |hi.lo + lo.hi|), where
+//   65536 |hi.hi| <= (|x'| + 128.5 sqrt(d)) (|c'| + 128.5 sqrt(d)) and
+//   256 |hi.lo + lo.hi| <= 128 sqrt(d) (|x'| + |c'|) + 32896 d):
+//                          2^-22 (|x'| + 160 sqrt(d)) (|c'| + 160 sqrt(d))
+//   the FP32 chain:        gamma_d sum|x' c'| <= gamma_d |x'| |c'|
+void screen_bound_q8(size_t d, float& e_rel, float& e_abs, float& e_min, float& e_lo) {
+  const double dd = (double)d, sd = std::sqrt(dd);
+  const double u24 = std::ldexp(1.0, -24), u22 = std::ldexp(1.0, -22);
+  const double gamma_d = dd * u24 / (1.0 - dd * u24);
+  e_rel = (float)((gamma_d + u22) * 1.01);
+  e_abs = (float)((0.5 * sd + u22 * 160.0 * sd) * 1.01);
+  e_min = (float)((0.25 * dd + u22 * 160.0 * 160.0 * dd) * 1.01);
+  e_lo = 1.01f;
+}
+
 // A fresh generation of the centroid summary words.
 uint32_t next_gen(eb_engine* e, unsigned long long* cinfo) {
   if (++e->cinfo_gen == 0) {  // wrapped: older tags could compare higher
@@ -2005,27 +2304,30 @@ uint32_t next_gen(eb_engine* e, unsigned long long* cinfo) {
   return e->cinfo_gen;
 }
 
-// The scaled split FP16 copy of k rows of c (centroids, or data rows playing
-// them) under summary generation gen; with `summarise`, the summary is made
-// first (else a kernel before wrote it under gen).
-void convert_with(eb_engine* e, const float* c, size_t k, size_t d, size_t dp,
-                  unsigned long long* cinfo, uint32_t gen, bool summarise, __half* ch,
-                  __half* cl) {
+// The fixed-point copy of k rows of c under summary generation gen (with
+// `summarise`, the summary is made first).
+void convert_with_q8(eb_engine* e, const float* c, size_t k, size_t d, size_t dp8,
+                     unsigned long long* cinfo, uint32_t gen, bool summarise, int8_t* ch,
+                     int8_t* cl) {
   if (summarise) {
     launch_pdl(e, k_cent_max, (unsigned)((k + 1) / 2), 64, 0, c, (long)k, (int)d, cinfo, gen);
     EB_LAUNCH("screen centroid max");
   }
-  launch_pdl(e, k_cent_conv, (unsigned)((k + 1) / 2), 64, 0, c, (long)k, (int)d, (int)dp, cinfo,
-             gen, ch, cl);
-  EB_LAUNCH("screen centroid convert");
+  launch_pdl(e, k_cent_conv_q8, (unsigned)((k + 1) / 2), 64, 0, c, (long)k, (int)d, (int)dp8,
+             cinfo, gen, ch, cl);
+  EB_LAUNCH("screen centroid fixed-point copy");
 }
 
-// The scaled split FP16 copy of k rows of c and their summary under a new
-// generation, which is returned.
+// The scaled split FP16 copy of k rows of c (centroids, or data rows playing
+// them) and their summary under a new generation, which is returned.
 uint32_t convert_centroids(eb_engine* e, const float* c, size_t k, size_t d, size_t dp,
                            unsigned long long* cinfo, __half* ch, __half* cl) {
   const uint32_t gen = next_gen(e, cinfo);
-  convert_with(e, c, k, d, dp, cinfo, gen, true, ch, cl);
+  launch_pdl(e, k_cent_max, (unsigned)((k + 1) / 2), 64, 0, c, (long)k, (int)d, cinfo, gen);
+  EB_LAUNCH("screen centroid max");
+  launch_pdl(e, k_cent_conv, (unsigned)((k + 1) / 2), 64, 0, c, (long)k, (int)d, (int)dp, cinfo,
+             gen, ch, cl);
+  EB_LAUNCH("screen centroid convert");
   return gen;
 }
 
@@ -2100,36 +2402,41 @@ Fp16Copy* bound_copy(eb_engine* e, eb_buf* xbuf, const float* x, size_t n, size_
   return xbuf->f16;
 }
 
-Fp16Copy* position_copy(eb_engine* e, size_t cap, size_t d) {
-  const size_t dp = (d + BKH - 1) / BKH * BKH;
-  auto* f = new Fp16Copy;
-  f->n = cap;
-  f->d = d;
-  f->stream = e->stream;
-  const size_t cells = std::max<size_t>(cap * dp, 8);
-  cudaError_t st = cudaMallocAsync(&f->xh, cells * 2, e->stream);
-  if (st == cudaSuccess) st = cudaMallocAsync(&f->xl, cells * 2, e->stream);
-  if (st == cudaSuccess) st = cudaMallocAsync(&f->xexp, std::max<size_t>(cap, 1) * 4, e->stream);
-  if (st == cudaSuccess) st = cudaMallocAsync(&f->xnrm, std::max<size_t>(cap, 1) * 4, e->stream);
-  e->device_allocs += 4;
-  if (st != cudaSuccess) {
-    free_copy(f);
-    cudaGetLastError();
-    return nullptr;
-  }
-  return f;
-}
-
-void fill_position_copy(eb_engine* e, Fp16Copy* pc, const Fp16Copy* src, const uint32_t* ids,
-                        size_t rows) {
-  if (rows == 0) return;
-  const size_t dp = (pc->d + BKH - 1) / BKH * BKH;
+// The fixed-point copy of a bound data set, made on first use and kept until
+// the buffer is written or freed; null when xbuf is not a bound set of that
+// shape or there is no room for the copy.
+Q8Copy* bound_copy_q8(eb_engine* e, eb_buf* xbuf, const float* x, size_t n, size_t d) {
+  if (!xbuf || xbuf->d != d || xbuf->len != n * d) return nullptr;
+  const size_t dp8 = (d + BK8 - 1) / BK8 * BK8;
   const unsigned wpb = 8;
-  launch_pdl(e, k_gather_rows, (unsigned)((rows + wpb - 1) / wpb), wpb * 32, 0, src->xh, src->xl,
-             src->xexp, src->xnrm, (long)src->n, (int)dp, ids, 0L, (long)rows, pc->xh, pc->xl,
-             pc->xexp, pc->xnrm, e->d_status);
-  EB_LAUNCH("epoch row gather");
-  pc->version = 1;
+  if (xbuf->q8 && xbuf->q8->version != xbuf->version) drop_f16(xbuf);
+  if (!xbuf->q8) {
+    auto* f = new Q8Copy;
+    f->n = n;
+    f->d = d;
+    f->version = xbuf->version;
+    f->stream = e->stream;
+    const size_t cells = std::max<size_t>(n * dp8, 64);
+    const size_t rows = std::max<size_t>(n, 1);
+    cudaError_t st = cudaMallocAsync(&f->xh, cells, e->stream);
+    if (st == cudaSuccess) st = cudaMallocAsync(&f->xl, cells, e->stream);
+    if (st == cudaSuccess) st = cudaMallocAsync(&f->xexp, rows * 4, e->stream);
+    if (st == cudaSuccess) st = cudaMallocAsync(&f->xnrm, rows * 4, e->stream);
+    if (st == cudaSuccess) st = cudaMallocAsync(&f->xlo, rows * 4, e->stream);
+    e->device_allocs += 5;
+    xbuf->q8 = f;
+    if (st != cudaSuccess) {
+      free_q8(f);  // no room for the copy: convert per pass instead
+      xbuf->q8 = nullptr;
+      cudaGetLastError();
+    } else if (n) {
+      launch_pdl(e, k_prep_rows_q8, (unsigned)((n + wpb - 1) / wpb), wpb * 32, 0, x, (long)n,
+                 (int)d, (int)dp8, nullptr, 0L, (long)n, f->xh, f->xl, f->xexp, f->xnrm, f->xlo,
+                 e->d_status);
+      EB_LAUNCH("screen fixed-point copy of bound rows");
+    }
+  }
+  return xbuf->q8;
 }
 
 bool top1_screen_supported(eb_engine* e, const Top1Args& a) {
@@ -2141,7 +2448,7 @@ bool top1_screen_supported(eb_engine* e, const Top1Args& a) {
 
 void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   const size_t d = a.d, k = a.k;
-  const size_t dp = (d + BKH - 1) / BKH * BKH;
+  const size_t dp = (d + BK8 - 1) / BK8 * BK8;  // bytes of a fixed-point row
   const size_t m_all = a.r1 - a.r0;
   // Rows per pass: eight 128-row tiles per SM, so that each persistent CTA
   // keeps its operand ring running across tiles.
@@ -2149,29 +2456,32 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   const size_t chunk = std::min(m_all, PASS_WAVES * wave);
   const bool ip = a.metric == EB_IP;
 
-  float e_rel, e_abs, e_min;
-  screen_bound(d, e_rel, e_abs, e_min);
+  float e_rel, e_abs, e_min, e_lo;
+  screen_bound_q8(d, e_rel, e_abs, e_min, e_lo);
 
-  // Centroids: one exponent, split FP16 copy (kept from the last call when
-  // the caller says the centroids are unchanged).
+  // Centroids: one shift, fixed-point copy (kept from the last call when the
+  // caller says the centroids are unchanged).
   unsigned long long* cinfo = e->scratch_get<unsigned long long>("tc_cinfo", 4, true);
-  __half* ch = e->scratch_get<__half>("tc_ch", k * dp);
-  __half* cl = e->scratch_get<__half>("tc_cl", k * dp);
+  int8_t* ch = e->scratch_get<int8_t>("tc_ch8", k * dp);
+  int8_t* cl = e->scratch_get<int8_t>("tc_cl8", k * dp);
   const unsigned wpb = 8;
   uint32_t cgen = e->cinfo_gen;
   if (!a.centroids_ready) {
-    if (a.summary_gen && a.summary_gen == e->cinfo_gen)
-      convert_with(e, a.c, k, d, dp, cinfo, a.summary_gen, false, ch, cl);
-    else
-      cgen = convert_centroids(e, a.c, k, d, dp, cinfo, ch, cl);
+    if (a.summary_gen && a.summary_gen == e->cinfo_gen) {
+      convert_with_q8(e, a.c, k, d, dp, cinfo, a.summary_gen, false, ch, cl);
+    } else {
+      cgen = next_gen(e, cinfo);
+      convert_with_q8(e, a.c, k, d, dp, cinfo, cgen, true, ch, cl);
+    }
   }
-  const CUtensorMap mapBh = make_map(ch, k, dp, BN);
-  const CUtensorMap mapBl = make_map(cl, k, dp, BN);
+  const CUtensorMap mapBh = make_map_q8(ch, k, dp, BN);
+  const CUtensorMap mapBl = make_map_q8(cl, k, dp, BN);
 
-  __half* xh = e->scratch_get<__half>("tc_xh", chunk * dp);
-  __half* xl = e->scratch_get<__half>("tc_xl", chunk * dp);
+  int8_t* xh = e->scratch_get<int8_t>("tc_xh8", chunk * dp);
+  int8_t* xl = e->scratch_get<int8_t>("tc_xl8", chunk * dp);
   int* xexp = e->scratch_get<int>("tc_xexp", chunk);
   float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
+  float* xlo = e->scratch_get<float>("tc_xlo", chunk);
   // Parts per row tile for each pass (the pass's row tiles decide them).
   const int ntiles = (int)((k + BN - 1) / BN);
   int max_parts = 1;
@@ -2195,7 +2505,7 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
 
   ScreenParams P{};
   P.k = (int)k;
-  P.kblocks = (int)(dp / BKH);
+  P.kblocks = (int)(dp / BK8);
   P.ntiles = ntiles;
   P.cn = a.cnorm;
   P.cinfo = cinfo;
@@ -2203,6 +2513,7 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   P.e_rel = e_rel;
   P.e_abs = e_abs;
   P.e_min = e_min;
+  P.e_lo = e_lo;
   P.cand = cand;
   P.cand_cnt = cand_cnt;
   P.cand_thr = cand_thr;
@@ -2211,42 +2522,40 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   P.zero1 = list_count;
   P.dead_wait = e->screen_dead_wait;
 
-  // A bound data set keeps its split copy across calls (training steps,
-  // repeated assigns): converted once, then read in place or gathered by id.
-  Fp16Copy* cache = bound_copy(e, xbuf, a.x, a.n, d);
-  const bool pre = a.pre && a.pre->d == d && a.r1 <= a.pre->n;
+  // A bound data set keeps its fixed-point copy across calls (training
+  // steps, repeated assigns): converted once, then read in place or gathered
+  // by id.
+  Q8Copy* cache = bound_copy_q8(e, xbuf, a.x, a.n, d);
 
   for (size_t c0 = a.r0; c0 < a.r1; c0 += chunk) {
     const size_t m = std::min(chunk, a.r1 - c0);
-    const __half *ah = xh, *al = xl;
-    if (pre) {
-      // The selection's rows already gathered in selection order (a training
-      // epoch's copy): read in place at the positions.
-      ah = a.pre->xh + c0 * dp;
-      al = a.pre->xl + c0 * dp;
-      P.xexp = a.pre->xexp + c0;
-      P.xnrm = a.pre->xnrm + c0;
-    } else if (cache && !a.ids) {
+    const int8_t *ah = xh, *al = xl;
+    if (cache && !a.ids) {
       // Dense rows of the bound set: the screen reads the cached copy in place.
       ah = cache->xh + c0 * dp;
       al = cache->xl + c0 * dp;
       P.xexp = cache->xexp + c0;
       P.xnrm = cache->xnrm + c0;
+      P.xlo = cache->xlo + c0;
     } else if (cache) {
-      launch_pdl(e, k_gather_rows, (unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, cache->xh, cache->xl, cache->xexp, cache->xnrm, (long)a.n, (int)dp, a.ids, (long)c0,
-          (long)m, xh, xl, xexp, xnrm, e->d_status);
+      launch_pdl(e, k_gather_rows_q8, (unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, cache->xh,
+                 cache->xl, cache->xexp, cache->xnrm, cache->xlo, (long)a.n, (int)dp, a.ids,
+                 (long)c0, (long)m, xh, xl, xexp, xnrm, xlo, e->d_status);
       EB_LAUNCH("screen row gather");
       P.xexp = xexp;
       P.xnrm = xnrm;
+      P.xlo = xlo;
     } else {
-      launch_pdl(e, k_prep_rows, (unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, a.x, (long)a.n, (int)d, (int)dp, a.ids, (long)c0, (long)m, xh, xl, xexp, xnrm,
-          e->d_status);
+      launch_pdl(e, k_prep_rows_q8, (unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, a.x, (long)a.n,
+                 (int)d, (int)dp, a.ids, (long)c0, (long)m, xh, xl, xexp, xnrm, xlo,
+                 e->d_status);
       EB_LAUNCH("screen row prep");
       P.xexp = xexp;
       P.xnrm = xnrm;
+      P.xlo = xlo;
     }
-    const CUtensorMap mapAh = make_map(ah, m, dp, BM);
-    const CUtensorMap mapAl = make_map(al, m, dp, BM);
+    const CUtensorMap mapAh = make_map_q8(ah, m, dp, BM);
+    const CUtensorMap mapAl = make_map_q8(al, m, dp, BM);
     P.m = (long)m;
     const size_t rtiles = (m + BM - 1) / BM;
     P.parts = screen_parts(rtiles, ntiles, e->num_sms);
@@ -2270,9 +2579,9 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
       ev_end = e->screen_ev[u].second;
     }
     if (ip)
-      launch_screen<true>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
+      launch_screen<true, false, false, true>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
     else
-      launch_screen<false>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
+      launch_screen<false, false, false, true>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
     EB_LAUNCH("screen");
     P.dead_wait = e->screen_dead_wait = 0;  // one launch only
     if (ev_end) EB_CUDA(cudaEventRecord(ev_end, e->stream));

@@ -99,59 +99,90 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   for (size_t rows : r.epoch_rows) ensure(rows > 0, "nepochs gives an empty epoch");
   const auto t0 = std::chrono::steady_clock::now();
 
-  // Events: [0, 1] an epoch's labels and scores landed in pinned set 0 / 1;
-  // [2, 3] an epoch's order left pinned buffer 0 / 1 for the device.
+  // Start state (model.rs:306-349, 772-797), assembled in pinned memory on a
+  // helper thread while the device buffers are set up (the initial pick
+  // draws a permutation of all n rows); its upload is then a plain DMA.
+  float* pos = e->pinned_get<float>("tr_pos", k * d);
+  float* usage = e->pinned_get<float>("tr_usage", k);
+  std::future<void> start = std::async(std::launch::async, [&] {
+    if (job->state_positions) {
+      std::memcpy(pos, job->state_positions, k * d * 4);
+      std::memcpy(usage, job->state_usage, k * 4);
+      for (size_t j = 0; j < k; j++)
+        ensure(std::isfinite(usage[j]) && usage[j] >= 0.0f, "usage must be finite and >= 0");
+    } else {
+      std::fill(usage, usage + k, 1.0f / 65536.0f);
+      if (job->init) {
+        std::memcpy(pos, job->init, k * d * 4);
+      } else if (n == k) {
+        std::memcpy(pos, job->x, k * d * 4);
+      } else {
+        std::vector<uint32_t> perm = host::Mt19937(job->seed).permutation(n);
+        for (size_t j = 0; j < k; j++) std::memcpy(&pos[j * d], job->x + (size_t)perm[j] * d, d * 4);
+      }
+      if (spherical)
+        for (size_t j = 0; j < k; j++) host::normalize_row(&pos[j * d], d);
+    }
+    // Exponent field all ones = inf or NaN; one pass without branches.
+    uint32_t nonfinite = 0;
+    const uint32_t* pb = reinterpret_cast<const uint32_t*>(pos);
+    for (size_t q = 0; q < k * d; q++) nonfinite |= (uint32_t)((pb[q] & 0x7f800000u) == 0x7f800000u);
+    ensure(nonfinite == 0, "initial centroids must be finite");
+  });
+
+  // Events: [0, 1] epoch E's labels and scores landed in pinned set E & 1;
+  // [2, 3] epoch E's order reached device buffer E & 1; [4, 5] epoch E's
+  // steps finished (its order and label buffers are free again).
   struct Events {
-    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     ~Events() {
       for (cudaEvent_t v : ev)
         if (v) cudaEventDestroy(v);
     }
   } done;
   for (auto& v : done.ev) EB_CUDA(cudaEventCreateWithFlags(&v, cudaEventDisableTiming));
+  // Per-epoch device buffers, two sets used by alternate epochs, so that an
+  // epoch's order arrives and the one before's labels and scores leave while
+  // the steps between run.
+  DevBuf order0(e, EB_U32, n), order1(e, EB_U32, n);
+  DevBuf labels0(e, EB_U32, n), labels1(e, EB_U32, n), scores0(e, EB_F32, n), scores1(e, EB_F32, n);
+  uint32_t* order_d[2] = {order0.u(), order1.u()};
+  uint32_t* labels_d[2] = {labels0.u(), labels1.u()};
+  float* scores_d[2] = {scores0.f(), scores1.f()};
+  EB_CUDA(cudaEventRecord(done.ev[4], e->stream));  // the buffers exist
+  EB_CUDA(cudaEventRecord(done.ev[5], e->stream));
+  // Copy streams (the engine's): `up` takes each epoch's order to the
+  // device, `down` brings each epoch's labels and scores back. Declared after
+  // the buffers, so that their copies have ended (the destructor waits)
+  // before the buffers go.
+  if (!e->copy_stream) EB_CUDA(cudaStreamCreateWithFlags(&e->copy_stream, cudaStreamNonBlocking));
+  if (!e->down_stream) EB_CUDA(cudaStreamCreateWithFlags(&e->down_stream, cudaStreamNonBlocking));
+  struct CopyStreams {
+    cudaStream_t up, down;
+    ~CopyStreams() {
+      cudaStreamSynchronize(up);
+      cudaStreamSynchronize(down);
+    }
+  } cs{e->copy_stream, e->down_stream};
   // Each epoch's permutation is drawn on a helper thread, straight into one of
-  // two pinned buffers (so that its upload is a plain DMA), while the previous
-  // epoch runs; the epoch-0 one while the init runs (model.rs:781-784).
+  // two pinned buffers, while the previous epoch runs (the epoch-0 one while
+  // the init runs; model.rs:781-784); the same thread queues its upload on
+  // `up` behind the end of the epoch that last read the device buffer.
   uint32_t* h_ord[2] = {e->pinned_get<uint32_t>("tr_ord0", n), e->pinned_get<uint32_t>("tr_ord1", n)};
   const int dev = e->device;
-  auto perm_of = [n, seed = job->seed, dev, &h_ord, &done](size_t epoch) {
+  auto perm_of = [n, seed = job->seed, dev, &h_ord, &done, &order_d, &cs,
+                  &r](size_t epoch) {
     const int par = (int)(epoch & 1);
-    if (epoch >= 2) {  // the buffer's last upload (epoch - 2) must have left it
-      EB_CUDA(cudaSetDevice(dev));
-      EB_CUDA(cudaEventSynchronize(done.ev[2 + par]));
-    }
+    EB_CUDA(cudaSetDevice(dev));
+    // The pinned buffer's last upload (epoch - 2) must have left it.
+    if (epoch >= 2) EB_CUDA(cudaEventSynchronize(done.ev[2 + par]));
     host::Mt19937(host::epoch_seed(seed, epoch)).permutation_into(h_ord[par], n);
+    EB_CUDA(cudaStreamWaitEvent(cs.up, done.ev[4 + par], 0));
+    EB_CUDA(cudaMemcpyAsync(order_d[par], h_ord[par], r.epoch_rows[epoch] * 4,
+                            cudaMemcpyHostToDevice, cs.up));
+    EB_CUDA(cudaEventRecord(done.ev[2 + par], cs.up));
   };
   std::future<void> next_order = std::async(std::launch::async, perm_of, 0);
-
-  // Start state (model.rs:306-349, 772-797).
-  // The start positions are assembled in pinned memory, so that their upload
-  // runs as a DMA behind the host's remaining set-up.
-  float* pos = e->pinned_get<float>("tr_pos", k * d);
-  std::vector<float> usage(k, 1.0f / 65536.0f);
-  if (job->state_positions) {
-    std::memcpy(pos, job->state_positions, k * d * 4);
-    std::memcpy(usage.data(), job->state_usage, k * 4);
-    for (float u : usage) ensure(std::isfinite(u) && u >= 0.0f, "usage must be finite and >= 0");
-  } else {
-    if (job->init) {
-      std::memcpy(pos, job->init, k * d * 4);
-    } else if (n == k) {
-      std::memcpy(pos, job->x, k * d * 4);
-    } else {
-      std::vector<uint32_t> perm = host::Mt19937(job->seed).permutation(n);
-      for (size_t j = 0; j < k; j++) std::memcpy(&pos[j * d], job->x + (size_t)perm[j] * d, d * 4);
-    }
-    if (spherical)
-      for (size_t j = 0; j < k; j++) host::normalize_row(&pos[j * d], d);
-  }
-  {
-    // Exponent field all ones = inf or NaN; one pass without branches.
-    uint32_t nonfinite = 0;
-    const uint32_t* pb = reinterpret_cast<const uint32_t*>(pos);
-    for (size_t q = 0; q < k * d; q++) nonfinite |= (uint32_t)((pb[q] & 0x7f800000u) == 0x7f800000u);
-    ensure(nonfinite == 0, "initial centroids must be finite");
-  }
 
   const size_t bsz = r.batch_size;
   const size_t chunk = job->chunk > 0 ? (size_t)job->chunk : 65536;
@@ -175,7 +206,6 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
       if (b) free_buf(e, b);
     }
   } unbind{e, reuse ? nullptr : data};
-  DevBuf order(e, EB_U32, n), labels_ep(e, EB_U32, n), scores_ep(e, EB_F32, n);
   DevBuf dpos(e, EB_F32, k * d), mass(e, EB_F32, k), readout(e, EB_F32, spherical ? k * d : k);
   DevBuf sums(e, EB_F32, k * d), counts(e, EB_U32, k), pass(e, EB_F32, k * d);
   DevBuf pairs(e, EB_U32, 2 * k);
@@ -189,8 +219,9 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   const size_t s4 = (sh_max + 3) / 4 * 4, k4 = (k + 3) / 4 * 4;
   const size_t share = reduce_mode ? 2 * s4 + k4 + k * d : 2 * sh_max;
   DevBuf stage(e, EB_U32, e->world > 1 ? share * e->world : 1);
+  start.get();
   EB_CUDA(cudaMemcpyAsync(dpos.f(), pos, k * d * 4, cudaMemcpyHostToDevice, e->stream));
-  EB_CUDA(cudaMemcpyAsync(mass.f(), usage.data(), k * 4, cudaMemcpyHostToDevice, e->stream));
+  EB_CUDA(cudaMemcpyAsync(mass.f(), usage, k * 4, cudaMemcpyHostToDevice, e->stream));
   if (data->d == d && !data->xnorm && !spherical) {
     EB_CUDA(cudaMallocAsync(&data->xnorm, std::max<size_t>(n, 1) * 4, e->stream));
     e->device_allocs++;
@@ -199,10 +230,12 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
 
   host::Mt19937 split_rng(job->seed);
   // The next revival's uniforms, drawn ahead on a helper thread from
-  // split_rng's current state (it changes only when a revival splits).
+  // split_rng's current state (it changes only when a revival splits). After
+  // a split, the helper starts once the next step is queued, so that the
+  // device, idle while the host plans, is fed first.
   std::future<host::RevivalDraws> draws_next;
   std::unique_ptr<host::RevivalDraws> draws;
-  if (tau > 0.0) draws_next = std::async(std::launch::async, host::revival_draws, split_rng, k);
+  bool draws_due = tau > 0.0;
   size_t n_splits = 0, step = 0;
   // Pinned read-backs: two (labels, scores) sets, so that an epoch's copy
   // never overwrites the set whose statistics are still being computed, and
@@ -221,28 +254,20 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   // Nonzero: the readout of dpos and the screen's summary of the next top-1's
   // centroids were made by the last EMA kernel under this generation.
   uint32_t readout_gen = 0;
-  // The bound rows' split FP16 copy, and an epoch copy in selection order:
-  // each epoch's rows are gathered from the split copy once, so that the
-  // screen reads every batch of the epoch in place.
-  struct EpochCopy {
-    Fp16Copy* c = nullptr;
-    ~EpochCopy() { free_copy(c); }
-  } epoch_copy;
-  if (e->screen_mode != 0) {
-    size_t cap = 0;
-    for (size_t rows : r.epoch_rows) cap = std::max(cap, rows);
-    if (bound_copy(e, data, static_cast<const float*>(data->ptr), n, d))
-      epoch_copy.c = position_copy(e, cap, d);
-  }
+
   for (size_t epoch = 0; epoch < n_epochs; epoch++) {
     const size_t rows = r.epoch_rows[epoch];
-    next_order.get();
-    const uint32_t* ord = h_ord[epoch & 1];
+    const int par = (int)(epoch & 1);
+    next_order.get();  // this epoch's upload is queued
+    const uint32_t* ord = h_ord[par];
     if (epoch + 1 < n_epochs) next_order = std::async(std::launch::async, perm_of, epoch + 1);
     const bool last = epoch + 1 == n_epochs;
-    EB_CUDA(cudaMemcpyAsync(order.u(), ord, rows * 4, cudaMemcpyHostToDevice, e->stream));
-    EB_CUDA(cudaEventRecord(done.ev[2 + (epoch & 1)], e->stream));
-    if (epoch_copy.c) fill_position_copy(e, epoch_copy.c, data->f16, order.u(), rows);
+    uint32_t* const order = order_d[par];
+    uint32_t* const labels_ep = labels_d[par];
+    float* const scores_ep = scores_d[par];
+    EB_CUDA(cudaStreamWaitEvent(e->stream, done.ev[2 + par], 0));
+    // Epoch - 2's labels and scores must have left this set of buffers.
+    if (epoch >= 2) EB_CUDA(cudaStreamWaitEvent(e->stream, done.ev[par], 0));
     const size_t splits_before = n_splits;
     for (size_t b = 0; b < rows; b += bsz) {
       const size_t end = std::min(b + bsz, rows);
@@ -274,18 +299,18 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
         a.x = static_cast<const float*>(data->ptr);
         a.n = n;
         a.d = d;
-        a.ids = order.u();
+        a.ids = order;
         a.r0 = c0;
         a.r1 = std::min(c0 + chunk, hi);
         a.c = spherical ? readout.f() : dpos.f();
         a.cnorm = spherical ? nullptr : readout.f();
         a.k = k;
         a.metric = spherical ? EB_IP : EB_L2;
-        a.labels = labels_ep.u();
-        a.scores = scores_ep.f();
+        a.labels = labels_ep;
+        a.scores = scores_ep;
         a.xnorm = data->xnorm;
         a.summary_gen = readout_gen;
-        a.pre = epoch_copy.c;
+
         top1_dispatch(e, a, data);
       }
       if (reduce_mode) {
@@ -295,23 +320,23 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
         // every rank adds the partials in rank order (the same bits on every
         // rank for a given group size; not the single-engine row order).
         uint32_t* mine = stage.u() + (size_t)e->rank * share;
-        shard_pack(e, labels_ep.u() + lo, scores_ep.f() + lo, hi - lo, s4, share, stage.u());
-        scatter_add(e, static_cast<const float*>(data->ptr), n, d, order.u(), lo, hi,
-                    labels_ep.u(), k, reinterpret_cast<float*>(mine + 2 * s4 + k4),
+        shard_pack(e, labels_ep + lo, scores_ep + lo, hi - lo, s4, share, stage.u());
+        scatter_add(e, static_cast<const float*>(data->ptr), n, d, order, lo, hi,
+                    labels_ep, k, reinterpret_cast<float*>(mine + 2 * s4 + k4),
                     mine + 2 * s4, nullptr);
         group_allgather(e, stage.u(), share);
-        shard_unpack(e, stage.u(), end - b, sh, s4, share, labels_ep.u() + b, scores_ep.f() + b);
+        shard_unpack(e, stage.u(), end - b, sh, s4, share, labels_ep + b, scores_ep + b);
         reduce_partials(e, stage.u(), share, e->world, 2 * s4, 2 * s4 + k4, k, d, sums.f(),
                         counts.u(), last ? pass.f() : nullptr);
       } else {
         if (split_batch) {
-          shard_pack(e, labels_ep.u() + lo, scores_ep.f() + lo, hi - lo, sh, 2 * sh, stage.u());
+          shard_pack(e, labels_ep + lo, scores_ep + lo, hi - lo, sh, 2 * sh, stage.u());
           group_allgather(e, stage.u(), 2 * sh);
-          shard_unpack(e, stage.u(), end - b, sh, sh, 2 * sh, labels_ep.u() + b,
-                       scores_ep.f() + b);
+          shard_unpack(e, stage.u(), end - b, sh, sh, 2 * sh, labels_ep + b,
+                       scores_ep + b);
         }
-        scatter_add(e, static_cast<const float*>(data->ptr), n, d, order.u(), b, end,
-                    labels_ep.u(), k, sums.f(), counts.u(), last ? pass.f() : nullptr);
+        scatter_add(e, static_cast<const float*>(data->ptr), n, d, order, b, end,
+                    labels_ep, k, sums.f(), counts.u(), last ? pass.f() : nullptr);
       }
       const double alpha = host::scheduled_alpha(r.alpha0, step, r.total_steps);
       // The EMA step, with the next step's readout and the screen's summary
@@ -324,30 +349,37 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
         ema_update(e, dpos.f(), mass.f(), sums.f(), counts.u(), k, d, (float)alpha,
                    (float)(1.0 - alpha), alpha == 1.0);
       }
-      if ((step + 1) % 5 == 0) {
+      if (draws_due) {
+        draws_next = std::async(std::launch::async, host::revival_draws, split_rng, k);
+        draws_due = false;
+      }
+      // Revival (a threshold of tau <= 0 marks nothing dead: no plan).
+      if (tau > 0.0 && (step + 1) % 5 == 0) {
         read_into(e, mass_h, mass.f(), k * 4);
         std::memcpy(mass_v.data(), mass_h, k * 4);
         if (draws_next.valid()) draws.reset(new host::RevivalDraws(draws_next.get()));
         std::vector<uint32_t> plan = host::plan_revival(mass_v, tau, split_rng, draws.get());
         if (!plan.empty()) {
-          draws_next = std::async(std::launch::async, host::revival_draws, split_rng, k);
           std::memcpy(plan_h, plan.data(), plan.size() * 4);
           EB_CUDA(cudaMemcpyAsync(pairs.u(), plan_h, plan.size() * 4, cudaMemcpyHostToDevice,
                                   e->stream));
           split(e, dpos.f(), mass.f(), pairs.u(), plan.size() / 2, d);
           readout_gen = 0;  // the split moved centroids: read them out afresh
           n_splits += plan.size() / 2;
+          draws.reset();  // drawn from the generator's state before this split
+          draws_due = true;
         }
       }
       step++;
     }
-    // Epoch end: labels and scores come down behind the epoch's work; a
-    // helper thread computes the statistics once they have landed.
-    const int par = (int)(epoch & 1);
+    // Epoch end: labels and scores come down on `down` while the next epoch
+    // runs; a helper thread computes the statistics once they have landed.
+    EB_CUDA(cudaEventRecord(done.ev[4 + par], e->stream));
     if (epoch >= 2) stats[epoch - 2].get();  // the set it read is reused now
-    EB_CUDA(cudaMemcpyAsync(h_lab[par], labels_ep.u(), rows * 4, cudaMemcpyDeviceToHost, e->stream));
-    EB_CUDA(cudaMemcpyAsync(h_sc[par], scores_ep.f(), rows * 4, cudaMemcpyDeviceToHost, e->stream));
-    EB_CUDA(cudaEventRecord(done.ev[par], e->stream));
+    EB_CUDA(cudaStreamWaitEvent(cs.down, done.ev[4 + par], 0));
+    EB_CUDA(cudaMemcpyAsync(h_lab[par], labels_ep, rows * 4, cudaMemcpyDeviceToHost, cs.down));
+    EB_CUDA(cudaMemcpyAsync(h_sc[par], scores_ep, rows * 4, cudaMemcpyDeviceToHost, cs.down));
+    EB_CUDA(cudaEventRecord(done.ev[par], cs.down));
     out->nsplit[epoch] = (int64_t)(n_splits - splits_before);
     const cudaEvent_t ev = done.ev[par];
     const uint32_t* hl = h_lab[par];
@@ -370,7 +402,7 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
     if (last) {
       // Closing means (core/mod.rs:404-429) on the device: the closing pass's
       // label counts, sums / count, renormalised when spherical.
-      label_counts(e, labels_ep.u(), rows, k, counts.u());
+      label_counts(e, labels_ep, rows, k, counts.u());
       closing_means(e, dpos.f(), pass.f(), counts.u(), k, d, sums.f());
       const float* closing = sums.f();
       if (spherical) {

@@ -71,3 +71,68 @@ def test_permutation_matches_golden(driver):
             assert got[len(got) - len(c["tail"]):].tolist() == c["tail"]
         m = min(c["n"], 5000)
         assert int(got[:m] @ np.arange(m)) == c["sum"]
+
+
+PLAN_DRIVER = r"""
+#include <cstdio>
+#include <cstdlib>
+#include "host.h"
+// argv: seed tau rounds k; stdin: rounds x k float32 usage vectors. Plans each
+// round in turn with one generator, drawing the uniforms ahead on odd rounds
+// (as the training loop does) and inside plan_revival on even ones.
+int main(int argc, char** argv) {
+  const uint32_t seed = (uint32_t)strtoul(argv[1], nullptr, 10);
+  const double tau = strtod(argv[2], nullptr);
+  const size_t rounds = (size_t)strtoull(argv[3], nullptr, 10);
+  const size_t k = (size_t)strtoull(argv[4], nullptr, 10);
+  eb::host::Mt19937 rng(seed);
+  std::vector<float> u(k);
+  for (size_t r = 0; r < rounds; r++) {
+    if (fread(u.data(), 4, k, stdin) != k) return 2;
+    eb::host::RevivalDraws pre = eb::host::revival_draws(rng, k);
+    std::vector<uint32_t> plan = eb::host::plan_revival(u, tau, rng, (r & 1) ? &pre : nullptr);
+    printf("%zu", plan.size() / 2);
+    for (uint32_t v : plan) printf(" %u", v);
+    printf("\n");
+  }
+  return 0;
+}
+"""
+
+
+@pytest.fixture(scope="module")
+def plan_driver(tmp_path_factory):
+    if shutil.which("g++") is None:
+        pytest.skip("g++ not found")
+    d = tmp_path_factory.mktemp("host_plan")
+    src, exe = d / "plan.cpp", d / "plan"
+    src.write_text(PLAN_DRIVER)
+    subprocess.run(["g++", "-O2", "-std=c++17", "-I", CSRC, str(src), "-o", str(exe)], check=True)
+    return str(exe)
+
+
+@pytest.mark.parametrize("k", [1, 2, 7, 64, 1024, 5000])
+def test_revival_plan_matches_oracle(plan_driver, k):
+    """The engine's host revival plan (csrc/host.h) against the oracle's
+    restatement of core/mod.rs:339-370 over a run of revivals sharing one
+    generator: the same pairs in the same order, and the same draws."""
+    rs = np.random.default_rng(k)
+    rounds, tau, seed = 8, 0.5, 4321
+    usage = []
+    for r in range(rounds):
+        u = rs.exponential(1.0, k).astype(np.float32) * np.float32(10.0 ** rs.uniform(-6, 2))
+        dead = rs.random(k) < [0.0, 0.05, 0.4, 0.9, 0.3, 0.6, 0.0, 0.2][r]
+        u[dead] = np.float32(0.0) if r % 2 else u[dead] * np.float32(1e-6)
+        if r == 5:
+            u[: k // 2] = u[0]  # ties in usage: equal log terms
+        usage.append(u)
+    out = subprocess.run([plan_driver, str(seed), repr(tau), str(rounds), str(k)],
+                         input=np.concatenate(usage).tobytes(), check=True,
+                         capture_output=True).stdout.decode().splitlines()
+    ref = oracle.Rng(seed)
+    for r in range(rounds):
+        want = ref.plan_revival(usage[r], tau)
+        got = [int(v) for v in out[r].split()]
+        assert got[0] == len(want), (r, got[0], len(want))
+        pairs = list(zip(got[1::2], got[2::2]))
+        assert pairs == want, r
