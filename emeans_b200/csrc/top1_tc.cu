@@ -8,10 +8,10 @@
 // dot, lower id on ties). The screen only decides which centroids get that
 // exact chain:
 //
-// 1. prep: each row is scaled by its own power of two 2^sx (the centroids by
-//    one, 2^sc) so that its largest value is at most 32639, rounded to
-//    integers v, and kept as digits v = 256 hi + lo (int8 each). A bound data
-//    set keeps this copy across calls.
+// 1. prep: each row is scaled by its own factor (the centroids by one) so
+//    that its largest value is 32638, rounded to integers v, and kept as
+//    digits v = 256 hi + lo (int8 each). A bound data set keeps this copy
+//    across calls.
 // 2. screen (tcgen05 kind::i8, persistent: one CTA per SM over 128-row
 //    tiles): each 256-centroid tile accumulates hi.hi in one TMEM
 //    accumulator and hi.lo + lo.hi in a second, both exact int32 sums;
@@ -30,10 +30,10 @@
 //    gave up are scanned exactly against every centroid, parallel over
 //    (row, block of centroids) with the same keyed reduction.
 //
-// Fixed-point error bound (integer units, x' = x 2^sx, c' = c 2^sc): the
-// rounding to integers, sqrt(d) (|x'| + |c'|) / 2 + d / 4; the dropped lo.lo
-// products, |x lo| |c lo|; the FP32 evaluation, 2^-22 (|x'| + 160 sqrt(d))
-// (|c'| + 160 sqrt(d)); and the FP32 chain, gamma_d |x'| |c'|
+// Fixed-point error bound (integer units, x' and c' the scaled values): the
+// rounding to integers, 0.502 sqrt(d) (|x'| + |c'|) + 0.252 d; the dropped
+// lo.lo products, |x lo| |c lo|; the FP32 evaluation, 2^-22 (|x'| +
+// 160 sqrt(d)) (|c'| + 160 sqrt(d)); and the FP32 chain, gamma_d |x'| |c'|
 // (screen_bound_q8 derives each term).
 //
 // Split FP16 (top-k, products): values scaled by powers of two so that
@@ -88,7 +88,7 @@ void free_copy(Fp16Copy* f) {
 struct Q8Copy {
   int8_t* xh = nullptr;  // n x dp, high digits
   int8_t* xl = nullptr;  // n x dp, low digits
-  int* xexp = nullptr;   // shifts
+  float* xscl = nullptr;  // scales (0: not screened)
   float* xnrm = nullptr;
   float* xlo = nullptr;  // bounds on the low digits' norms
   size_t n = 0, d = 0;
@@ -98,7 +98,7 @@ struct Q8Copy {
 
 void free_q8(Q8Copy* f) {
   if (!f) return;
-  for (void* p : {(void*)f->xh, (void*)f->xl, (void*)f->xexp, (void*)f->xnrm, (void*)f->xlo})
+  for (void* p : {(void*)f->xh, (void*)f->xl, (void*)f->xscl, (void*)f->xnrm, (void*)f->xlo})
     if (p) cudaFreeAsync(p, f->stream);
   delete f;
 }
@@ -120,7 +120,6 @@ constexpr int BM = 128;          // rows per tile (TMEM lanes)
 constexpr int BN = 256;          // centroids per tile (TMEM columns per accumulator)
 constexpr int BKH = 32;          // FP16 columns per k-block: one 64-byte swizzle row
 constexpr int BK8 = 64;          // int8 columns per k-block (top-1): the same 64 bytes
-constexpr float Q8_MAX = 32639.0f;  // largest |v| of a fixed-point value: 256 x 127 + 127
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BKH * 2;                // one of xh / xl
 constexpr int B_BYTES = BN * BKH * 2;                // one of ch / cl
@@ -408,21 +407,20 @@ __global__ void k_prep_rows(const float* __restrict__ x, long n, int d, int dp,
 
 // ---- the top-1 screen's fixed-point copies
 //
-// A row (or the centroid set) is scaled by 2^sh, sh the largest shift with
-// max |x| 2^sh <= Q8_MAX, and each value rounded to the integer v = rint(x 2^sh)
-// (|x 2^sh - v| <= 1/2), kept as two int8 digits v = 256 hi + lo, hi in
-// [-127, 127], lo in [-128, 127].
+// A row (or the centroid set) is scaled by s = 32638 / max |x| (FP32, so
+// that the largest scaled value rounds to at most 32638.01), and each value
+// rounded to the integer v = rint(fl(x s)) (|x s - v| <= 1/2 + 2^-24 32639
+// < 0.502), kept as two int8 digits v = 256 hi + lo, hi in [-127, 127], lo
+// in [-128, 127].
 
-// The shift of a set with largest magnitude mx (15 for mx = 0).
-__device__ __forceinline__ int q8_shift(float mx) {
-  int e = 0;
-  frexpf(mx, &e);  // mx = f 2^e, f in [0.5, 1)
-  int sh = 15 - e;
-  if (ldexpf(mx, sh) > Q8_MAX) sh--;
-  return sh;
+// The scale of a set with largest magnitude mx (1 for mx = 0; not finite
+// when mx is too small for 32638 / mx).
+__device__ __forceinline__ float q8_scale(float mx) {
+  return mx > 0.0f ? __fdiv_rn(32638.0f, mx) : 1.0f;
 }
 
-// The digits of an integral v with |v| <= Q8_MAX (every step exact).
+// The digits of an integral v with |v| <= 32639 = 256 x 127 + 127 (every
+// step exact).
 __device__ __forceinline__ void split8(float v, int& hi, int& lo) {
   hi = __float2int_rd((v + 128.0f) * (1.0f / 256.0f));
   lo = (int)v - 256 * hi;
@@ -434,12 +432,13 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
 }
 
 // Fixed-point copy of the selected rows (one warp per row): digits xh, xl
-// (dp bytes a row, zero-padded), the row's shift (XEXP_BAD for non-finite
-// rows), an upper bound on its norm and on the norm of its low digits.
+// (dp bytes a row, zero-padded), the row's scale (0 for rows with a
+// non-finite value or no finite scale), an upper bound on its norm and on
+// the norm of its low digits.
 __global__ void k_prep_rows_q8(const float* __restrict__ x, long n, int d, int dp,
                                const uint32_t* __restrict__ ids, long p0, long m,
                                int8_t* __restrict__ xh, int8_t* __restrict__ xl,
-                               int* __restrict__ xexp, float* __restrict__ xnrm,
+                               float* __restrict__ xscl, float* __restrict__ xnrm,
                                float* __restrict__ xlo, uint32_t* status) {
   pdl_wait();
   const long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
@@ -452,7 +451,7 @@ __global__ void k_prep_rows_q8(const float* __restrict__ x, long n, int d, int d
   if (row >= n) {
     if (lane == 0) {
       atomicOr(status, ST_BAD_ROW);
-      xexp[i] = XEXP_BAD;
+      xscl[i] = 0.0f;
       xnrm[i] = 0.0f;
       xlo[i] = 0.0f;
     }
@@ -463,7 +462,7 @@ __global__ void k_prep_rows_q8(const float* __restrict__ x, long n, int d, int d
   const float* r = x + row * (long)d;
   float mx = 0.0f, ss = 0.0f, sl = 0.0f;
   bool finite = true;
-  int sh = 0;
+  float sc = 1.0f;
   if ((d & 3) == 0 && d <= 1024) {
     // One read: up to 8 float4 per lane stay in registers.
     const float4* r4 = reinterpret_cast<const float4*>(r);
@@ -484,7 +483,8 @@ __global__ void k_prep_rows_q8(const float* __restrict__ x, long n, int d, int d
       ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
     }
     finite = __all_sync(0xFFFFFFFFu, finite);
-    sh = q8_shift(mx);
+    sc = q8_scale(mx);
+    finite = finite && isfinite(sc);
 #pragma unroll
     for (int u = 0; u < 8; u++) {
       const int t = lane + 32 * u;
@@ -493,7 +493,7 @@ __global__ void k_prep_rows_q8(const float* __restrict__ x, long n, int d, int d
         int h[4], l[4];
 #pragma unroll
         for (int w = 0; w < 4; w++) {
-          split8(finite ? rintf(ldexpf(a[w], sh)) : 0.0f, h[w], l[w]);
+          split8(finite ? rintf(__fmul_rn(a[w], sc)) : 0.0f, h[w], l[w]);
           sl = fmaf((float)l[w], (float)l[w], sl);
         }
         reinterpret_cast<uint32_t*>(oh)[t] = pack4(h[0], h[1], h[2], h[3]);
@@ -515,9 +515,10 @@ __global__ void k_prep_rows_q8(const float* __restrict__ x, long n, int d, int d
       ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
     }
     finite = __all_sync(0xFFFFFFFFu, finite);
-    sh = q8_shift(mx);
+    sc = q8_scale(mx);
+    finite = finite && isfinite(sc);
     for (int t = lane; t < dp; t += 32) {
-      const float v = (t < d && finite) ? rintf(ldexpf(__ldg(r + t), sh)) : 0.0f;
+      const float v = (t < d && finite) ? rintf(__fmul_rn(__ldg(r + t), sc)) : 0.0f;
       int h, l;
       split8(v, h, l);
       oh[t] = (int8_t)h;
@@ -528,7 +529,7 @@ __global__ void k_prep_rows_q8(const float* __restrict__ x, long n, int d, int d
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) sl += __shfl_xor_sync(0xFFFFFFFFu, sl, o);
   if (lane == 0) {
-    xexp[i] = finite ? sh : XEXP_BAD;
+    xscl[i] = finite ? sc : 0.0f;
     // Any-order sums of squares: relative error < d 2^-24; inflate by 2^-9.
     xnrm[i] = finite ? sqrtf(ss) * (1.0f + 1.0f / 512.0f) : 0.0f;
     xlo[i] = finite ? sqrtf(sl) * (1.0f + 1.0f / 512.0f) : 0.0f;
@@ -538,11 +539,11 @@ __global__ void k_prep_rows_q8(const float* __restrict__ x, long n, int d, int d
 // Rows x[ids[p]] of a cached fixed-point copy gathered into the pass's
 // staging rows (one warp per row, 16-byte copies; dp is a multiple of 64).
 __global__ void k_gather_rows_q8(const int8_t* __restrict__ src_h, const int8_t* __restrict__ src_l,
-                                 const int* __restrict__ src_e, const float* __restrict__ src_n,
+                                 const float* __restrict__ src_s, const float* __restrict__ src_n,
                                  const float* __restrict__ src_lo, long n, int dp,
                                  const uint32_t* __restrict__ ids, long p0, long m,
                                  int8_t* __restrict__ xh, int8_t* __restrict__ xl,
-                                 int* __restrict__ xexp, float* __restrict__ xnrm,
+                                 float* __restrict__ xscl, float* __restrict__ xnrm,
                                  float* __restrict__ xlo, uint32_t* status) {
   pdl_wait();
   const long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
@@ -556,7 +557,7 @@ __global__ void k_gather_rows_q8(const int8_t* __restrict__ src_h, const int8_t*
     for (int t = lane; t < q; t += 32) oh[t] = ol[t] = make_uint4(0, 0, 0, 0);
     if (lane == 0) {
       atomicOr(status, ST_BAD_ROW);
-      xexp[i] = XEXP_BAD;
+      xscl[i] = 0.0f;
       xnrm[i] = 0.0f;
       xlo[i] = 0.0f;
     }
@@ -569,7 +570,7 @@ __global__ void k_gather_rows_q8(const int8_t* __restrict__ src_h, const int8_t*
     ol[t] = __ldg(il + t);
   }
   if (lane == 0) {
-    xexp[i] = src_e[row];
+    xscl[i] = src_s[row];
     xnrm[i] = src_n[row];
     xlo[i] = src_lo[row];
   }
@@ -678,7 +679,7 @@ __global__ void __launch_bounds__(64) k_cent_conv(const float* __restrict__ c, l
   }
 }
 
-// Fixed-point centroids under the set's one shift (from max |c|): digits ch,
+// Fixed-point centroids under the set's one scale (from max |c|): digits ch,
 // cl (dp bytes a centroid, zero-padded), and the largest norm of a centroid's
 // low digits into summary word 3. One warp per centroid, two per block.
 __global__ void __launch_bounds__(64) k_cent_conv_q8(const float* __restrict__ c, long k, int d,
@@ -690,8 +691,8 @@ __global__ void __launch_bounds__(64) k_cent_conv_q8(const float* __restrict__ c
   const long j = (long)blockIdx.x * 2 + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (j >= k) return;
-  const int sh = q8_shift(__uint_as_float(cinfo_word(cinfo, 0, gen)));
-  const bool bad = cinfo_word(cinfo, 2, gen) != 0;
+  const float sc = q8_scale(__uint_as_float(cinfo_word(cinfo, 0, gen)));
+  const bool bad = cinfo_word(cinfo, 2, gen) != 0 || !isfinite(sc);
   const float* r = c + j * (long)d;
   int8_t* oh = ch + j * (long)dp;
   int8_t* ol = cl + j * (long)dp;
@@ -706,7 +707,7 @@ __global__ void __launch_bounds__(64) k_cent_conv_q8(const float* __restrict__ c
       int h[4], l[4];
 #pragma unroll
       for (int w = 0; w < 4; w++) {
-        split8(rintf(ldexpf(a[w], sh)), h[w], l[w]);
+        split8(rintf(__fmul_rn(a[w], sc)), h[w], l[w]);
         sl = fmaf((float)l[w], (float)l[w], sl);
       }
       reinterpret_cast<uint32_t*>(oh)[t] = pack4(h[0], h[1], h[2], h[3]);
@@ -714,7 +715,7 @@ __global__ void __launch_bounds__(64) k_cent_conv_q8(const float* __restrict__ c
     }
   } else {
     for (int t = lane; t < dp; t += 32) {
-      const float v = (t < d && !bad) ? rintf(ldexpf(__ldg(r + t), sh)) : 0.0f;
+      const float v = (t < d && !bad) ? rintf(__fmul_rn(__ldg(r + t), sc)) : 0.0f;
       int h, l;
       split8(v, h, l);
       oh[t] = (int8_t)h;
@@ -759,7 +760,8 @@ struct ScreenParams {
   int parts;
   int tpp;             // centroid tiles per part
   int units;           // ceil(m / 128) * parts
-  const int* xexp;     // per staging row (fixed point: the row's shift)
+  const int* xexp;     // per staging row (split FP16)
+  const float* xscl;   // per staging row (fixed point: the row's scale, 0 = not screened)
   const float* xnrm;   // per staging row
   const float* xlo;    // per staging row, fixed point: a bound on its low digits' norm
   const float* cn;     // k squared centroid norms (L2) or null
@@ -965,14 +967,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int hf = (warp - 4) >> 2;
     const int r = q * 32 + lane;
     // The centroids' scale: split FP16, c' = c 2^(14 - ec); fixed point,
-    // c' = c 2^sc (then ec = -sc), and a bound on their low digits' norms.
+    // c' = c csc, and a bound on their low digits' norms.
     int ec = 0;
+    float csc = 1.0f;
     if constexpr (Q8)
-      ec = -q8_shift(__uint_as_float(cinfo_word(P.cinfo, 0, P.cgen)));
+      csc = q8_scale(__uint_as_float(cinfo_word(P.cinfo, 0, P.cgen)));
     else
       frexpf(__uint_as_float(cinfo_word(P.cinfo, 0, P.cgen)), &ec);
     const float cmax = __uint_as_float(cinfo_word(P.cinfo, 1, P.cgen));
-    const bool c_bad = cinfo_word(P.cinfo, 2, P.cgen) != 0;
+    const bool c_bad = cinfo_word(P.cinfo, 2, P.cgen) != 0 || !isfinite(csc);
     const float clo = Q8 ? __uint_as_float(cinfo_word(P.cinfo, 3, P.cgen)) : 0.0f;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(hf * HALF);
     float* cns = cn_s + (warp - 4) * HALF;
@@ -997,28 +1000,36 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         continue;
       }
-      const int ex = live ? P.xexp[i] : XEXP_BAD;
-      bool fallback = !live || ex == XEXP_BAD || c_bad;
+      const int ex = live && !Q8 ? P.xexp[i] : XEXP_BAD;
+      const float xsc = live && Q8 ? P.xscl[i] : 0.0f;
+      bool fallback = !live || c_bad || (Q8 ? !(xsc > 0.0f) : ex == XEXP_BAD);
       const float xn = live ? P.xnrm[i] : 0.0f;
       // |x'| and max |c'| in accumulator units, and the bound e there. Fixed
-      // point: ex holds the row's shift, x' = x 2^ex, and the dropped lo.lo
-      // products add at most |x lo| max |c lo|.
-      const int xsh = Q8 ? (fallback ? 0 : ex) : 14 - (fallback ? 0 : ex);
-      const float xs = ldexpf(xn, xsh);
-      const float cs = ldexpf(cmax, Q8 ? -ec : 14 - ec);
+      // point: x' = x xsc, c' = c csc, and the dropped lo.lo products add at
+      // most |x lo| max |c lo|.
+      const float xs = Q8 ? xn * (fallback ? 1.0f : xsc) : ldexpf(xn, 14 - (fallback ? 0 : ex));
+      const float cs = Q8 ? cmax * csc : ldexpf(cmax, 14 - ec);
       float e_acc = fmaf(P.e_rel * xs, cs, fmaf(P.e_abs, xs + cs, P.e_min));
       if (Q8) e_acc = fmaf(P.e_lo * (live ? P.xlo[i] : 0.0f), clo, e_acc);
       float off, m2f = 1.0f;  // screened value = m2f acc + cn (IP: acc + 0)
       if (IP) {
         off = 2.0f * e_acc;
       } else {
-        // The dot is 2^fe acc.
-        const int fe = Q8 ? -xsh + ec : ex + ec - 28;
-        if (fe < -100 || fe > 100) fallback = true;
-        const float f = ldexpf(1.0f, fallback ? 0 : fe);
+        // The dot is f acc: 2^(ex + ec - 28), or 1 / (xsc csc) rounded (its
+        // relative error 2^-22 is a third rounding of the key's dot term).
+        float f;
+        if constexpr (Q8) {
+          f = fallback ? 1.0f : __frcp_rn(__fmul_rn(xsc, csc));
+          if (!(f > 0.0f) || !isfinite(f)) fallback = true;
+        } else {
+          const int fe = ex + ec - 28;
+          if (fe < -100 || fe > 100) fallback = true;
+          f = ldexpf(1.0f, fallback ? 0 : fe);
+        }
         m2f = -2.0f * f;
-        // key error: twice the dot error plus the key's two roundings.
-        const float e_key = fmaf(2.0f * f, e_acc, ldexpf(fmaf(cmax, cmax, 2.0f * xn * cmax), -22));
+        // key error: twice the dot error plus the key's roundings.
+        const float e_key =
+            fmaf(2.0f * f, e_acc, ldexpf(fmaf(cmax, cmax, 2.0f * xn * cmax), Q8 ? -21 : -22));
         off = 2.0f * e_key;
       }
       if (!isfinite(off)) fallback = true;
@@ -2273,11 +2284,11 @@ void screen_bound(size_t d, float& e_rel, float& e_abs, float& e_min, bool one_a
 
 
 // The fixed-point screen's bound coefficients for this d, with 1% slack, in
-// the integer units of the digits (x' = x 2^sx, c' = c 2^sc real, v = rint(x'),
-// w = rint(c') with |x' - v|, |c' - w| <= 1/2; the MMAs sum 65536 hi.hi +
-// 256 (hi.lo + lo.hi) exactly and drop L = sum lo.lo):
-//   rounding to integers:  |sum x'c' - sum v w| <= (|c'|_1 + |v|_1) / 2
-//                          <= sqrt(d) (|x'| + |c'|) / 2 + d / 4
+// the integer units of the digits (x' = x xsc, c' = c csc real, v = rint(fl(x')),
+// w = rint(fl(c')) with |x' - v|, |c' - w| <= r = 0.502; the MMAs sum
+// 65536 hi.hi + 256 (hi.lo + lo.hi) exactly and drop L = sum lo.lo):
+//   rounding to integers:  |sum x'c' - sum v w| <= r (|c'|_1 + |v|_1)
+//                          <= r sqrt(d) (|x'| + |c'|) + r^2 d
 //   dropped products:      |L| <= |x lo| |c lo|                      (e_lo)
 //   FP32 evaluation of the two sums and their combination (three roundings,
 //   at most 2^-23 (65536 |hi.hi| + 256 |hi.lo + lo.hi|), where
@@ -2290,8 +2301,9 @@ void screen_bound_q8(size_t d, float& e_rel, float& e_abs, float& e_min, float& 
   const double u24 = std::ldexp(1.0, -24), u22 = std::ldexp(1.0, -22);
   const double gamma_d = dd * u24 / (1.0 - dd * u24);
   e_rel = (float)((gamma_d + u22) * 1.01);
-  e_abs = (float)((0.5 * sd + u22 * 160.0 * sd) * 1.01);
-  e_min = (float)((0.25 * dd + u22 * 160.0 * 160.0 * dd) * 1.01);
+  const double rr = 0.502;
+  e_abs = (float)((rr * sd + u22 * 160.0 * sd) * 1.01);
+  e_min = (float)((rr * rr * dd + u22 * 160.0 * 160.0 * dd) * 1.01);
   e_lo = 1.01f;
 }
 
@@ -2420,7 +2432,7 @@ Q8Copy* bound_copy_q8(eb_engine* e, eb_buf* xbuf, const float* x, size_t n, size
     const size_t rows = std::max<size_t>(n, 1);
     cudaError_t st = cudaMallocAsync(&f->xh, cells, e->stream);
     if (st == cudaSuccess) st = cudaMallocAsync(&f->xl, cells, e->stream);
-    if (st == cudaSuccess) st = cudaMallocAsync(&f->xexp, rows * 4, e->stream);
+    if (st == cudaSuccess) st = cudaMallocAsync(&f->xscl, rows * 4, e->stream);
     if (st == cudaSuccess) st = cudaMallocAsync(&f->xnrm, rows * 4, e->stream);
     if (st == cudaSuccess) st = cudaMallocAsync(&f->xlo, rows * 4, e->stream);
     e->device_allocs += 5;
@@ -2431,7 +2443,7 @@ Q8Copy* bound_copy_q8(eb_engine* e, eb_buf* xbuf, const float* x, size_t n, size
       cudaGetLastError();
     } else if (n) {
       launch_pdl(e, k_prep_rows_q8, (unsigned)((n + wpb - 1) / wpb), wpb * 32, 0, x, (long)n,
-                 (int)d, (int)dp8, nullptr, 0L, (long)n, f->xh, f->xl, f->xexp, f->xnrm, f->xlo,
+                 (int)d, (int)dp8, nullptr, 0L, (long)n, f->xh, f->xl, f->xscl, f->xnrm, f->xlo,
                  e->d_status);
       EB_LAUNCH("screen fixed-point copy of bound rows");
     }
@@ -2479,7 +2491,7 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
 
   int8_t* xh = e->scratch_get<int8_t>("tc_xh8", chunk * dp);
   int8_t* xl = e->scratch_get<int8_t>("tc_xl8", chunk * dp);
-  int* xexp = e->scratch_get<int>("tc_xexp", chunk);
+  float* xscl = e->scratch_get<float>("tc_xscl", chunk);
   float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
   float* xlo = e->scratch_get<float>("tc_xlo", chunk);
   // Parts per row tile for each pass (the pass's row tiles decide them).
@@ -2534,23 +2546,23 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
       // Dense rows of the bound set: the screen reads the cached copy in place.
       ah = cache->xh + c0 * dp;
       al = cache->xl + c0 * dp;
-      P.xexp = cache->xexp + c0;
+      P.xscl = cache->xscl + c0;
       P.xnrm = cache->xnrm + c0;
       P.xlo = cache->xlo + c0;
     } else if (cache) {
       launch_pdl(e, k_gather_rows_q8, (unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, cache->xh,
-                 cache->xl, cache->xexp, cache->xnrm, cache->xlo, (long)a.n, (int)dp, a.ids,
-                 (long)c0, (long)m, xh, xl, xexp, xnrm, xlo, e->d_status);
+                 cache->xl, cache->xscl, cache->xnrm, cache->xlo, (long)a.n, (int)dp, a.ids,
+                 (long)c0, (long)m, xh, xl, xscl, xnrm, xlo, e->d_status);
       EB_LAUNCH("screen row gather");
-      P.xexp = xexp;
+      P.xscl = xscl;
       P.xnrm = xnrm;
       P.xlo = xlo;
     } else {
       launch_pdl(e, k_prep_rows_q8, (unsigned)((m + wpb - 1) / wpb), wpb * 32, 0, a.x, (long)a.n,
-                 (int)d, (int)dp, a.ids, (long)c0, (long)m, xh, xl, xexp, xnrm, xlo,
+                 (int)d, (int)dp, a.ids, (long)c0, (long)m, xh, xl, xscl, xnrm, xlo,
                  e->d_status);
       EB_LAUNCH("screen row prep");
-      P.xexp = xexp;
+      P.xscl = xscl;
       P.xnrm = xnrm;
       P.xlo = xlo;
     }
