@@ -17,7 +17,8 @@
 //    accumulator and hi.lo + lo.hi in a second, both exact int32 sums;
 //    operands arrive by TMA in 64-byte-swizzled shared memory through a
 //    4-stage mbarrier ring. The epilogue (one thread per row) forms
-//    65536 hi.hi + 256 (hi.lo + lo.hi) in FP32, tracks the running best
+//    hi.hi + floor((hi.lo + lo.hi) / 256) and converts it to FP32 once (in
+//    units of 65536), tracks the running best
 //    screened score and appends every centroid within 2e of it to the row's
 //    candidate list, where e bounds |screen - exact chain|. A centroid more
 //    than 2e behind the best cannot be the exact winner.
@@ -32,9 +33,9 @@
 //
 // Fixed-point error bound (integer units, x' and c' the scaled values): the
 // rounding to integers, 0.502 sqrt(d) (|x'| + |c'|) + 0.252 d; the dropped
-// lo.lo products, |x lo| |c lo|; the FP32 evaluation, 2^-22 (|x'| +
-// 160 sqrt(d)) (|c'| + 160 sqrt(d)); and the FP32 chain, gamma_d |x'| |c'|
-// (screen_bound_q8 derives each term).
+// lo.lo products, |x lo| |c lo|; the epilogue's evaluation, 65536 +
+// 2^-22 (|x'| + 160 sqrt(d)) (|c'| + 160 sqrt(d)); and the FP32 chain,
+// gamma_d |x'| |c'| (screen_bound_q8 derives each term).
 //
 // Split FP16 (top-k, products): values scaled by powers of two so that
 // |v| < 2^14 and split into two FP16 terms, v' = hi + lo + r with
@@ -1010,7 +1011,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const float xs = Q8 ? xn * (fallback ? 1.0f : xsc) : ldexpf(xn, 14 - (fallback ? 0 : ex));
       const float cs = Q8 ? cmax * csc : ldexpf(cmax, 14 - ec);
       float e_acc = fmaf(P.e_rel * xs, cs, fmaf(P.e_abs, xs + cs, P.e_min));
-      if (Q8) e_acc = fmaf(P.e_lo * (live ? P.xlo[i] : 0.0f), clo, e_acc);
+      // Fixed point: the accumulator value is in units of 65536 (hi.hi).
+      if (Q8) e_acc = fmaf(P.e_lo * (live ? P.xlo[i] : 0.0f), clo, e_acc) * (1.0f / 65536.0f);
       float off, m2f = 1.0f;  // screened value = m2f acc + cn (IP: acc + 0)
       if (IP) {
         off = 2.0f * e_acc;
@@ -1019,7 +1021,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // relative error 2^-22 is a third rounding of the key's dot term).
         float f;
         if constexpr (Q8) {
-          f = fallback ? 1.0f : __frcp_rn(__fmul_rn(xsc, csc));
+          f = fallback ? 1.0f : __frcp_rn(__fmul_rn(xsc, csc)) * 65536.0f;
           if (!(f > 0.0f) || !isfinite(f)) fallback = true;
         } else {
           const int fe = ex + ec - 28;
@@ -1058,6 +1060,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t use = TOPK ? (uint32_t)(tc >> 1) : (uint32_t)tc;
         uint64_t* wbar = buf ? tfull1 : tfull;
         uint32_t wpar = use & 1;
+        const int col0 = nt * BN + hf * HALF;  // first centroid of this warp's half tile
+        // This half tile's squared centroid norms (product mode: the columns'
+        // weights), loaded before the wait for the accumulators so that their
+        // latency overlaps the MMAs, and staged in the warp's own shared
+        // memory after the drain (no barrier across warps, so a timed-out
+        // wait strands no warp).
+        float cnv[HALF / 32];
+        if (!IP || PROD) {
+          const float* src = PROD ? P.pinv : P.cn;
+#pragma unroll
+          for (int u = 0; u < HALF / 32; u++) {
+            const int c = u * 32 + lane;
+            cnv[u] = col0 + c < P.k ? __ldg(src + col0 + c) : 0.0f;
+          }
+        }
         if (P.dead_wait && blockIdx.x == 0 && tc == 1) {
           wbar = dead;  // phase 0 never completes: the wait runs out after WAIT_NS
           wpar = 0;
@@ -1068,19 +1085,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           break;
         }
         tc_fence_after();
-        const int col0 = nt * BN + hf * HALF;  // first centroid of this warp's half tile
-        if (!IP || PROD) {
-          // This half tile's squared centroid norms (product mode: the
-          // columns' weights), staged by each warp for itself (no barrier
-          // across warps, so a timed-out wait strands no warp).
-          const float* src = PROD ? P.pinv : P.cn;
-#pragma unroll
-          for (int u = 0; u < HALF / 32; u++) {
-            const int c = u * 32 + lane;
-            cns[c] = col0 + c < P.k ? __ldg(src + col0 + c) : 0.0f;
-          }
-          __syncwarp();
-        }
         const int ngr = max(0, min(HALF / 16, (P.k - col0 + 15) / 16));
         // Drain: this thread's half-tile row (hi in acc, lo added group pair by
         // group pair) comes into registers and the accumulators are released
@@ -1111,15 +1115,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
               for (int j = 0; j < 16; j++) {
                 uint32_t& a = acc[LOG * p2 + h2][j];
-                if constexpr (Q8)  // 65536 hi + 256 (hi.lo + lo.hi), from the int32 sums
-                  a = __float_as_uint(__fmaf_rn(__int2float_rn((int)a), 65536.0f,
-                                                __int2float_rn((int)lo[h2][j]) * 256.0f));
+                if constexpr (Q8)  // hi.hi + floor((hi.lo + lo.hi) / 256), still an integer
+                  a = (uint32_t)((int)a + ((int)lo[h2][j] >> 8));
                 else
                   a = __float_as_uint(__fadd_rn(__uint_as_float(a), __uint_as_float(lo[h2][j])));
               }
           }
           tc_fence_before();
           mbar_arrive(tempty);
+        }
+        if (!IP || PROD) {
+#pragma unroll
+          for (int u = 0; u < HALF / 32; u++) cns[u * 32 + lane] = cnv[u];
+          __syncwarp();
         }
         // Top-k mode scores each group straight from TMEM in a rolled loop
         // (its group code is long: unrolled eight times it no longer fits the
@@ -1155,7 +1163,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
 #pragma unroll
               for (int w = 0; w < 4; w++) {
-                const float v = __uint_as_float(h[j + w]);  // hi + lo, added in the drain
+                // hi + lo, added in the drain (fixed point: an integer in units of
+                // 65536, converted here once)
+                const float v = Q8 ? __int2float_rn((int)h[j + w]) : __uint_as_float(h[j + w]);
                 s[j + w] = __fmaf_rn(m2f, v, cc[w]);
               }
             }
@@ -2290,11 +2300,13 @@ void screen_bound(size_t d, float& e_rel, float& e_abs, float& e_min, bool one_a
 //   rounding to integers:  |sum x'c' - sum v w| <= r (|c'|_1 + |v|_1)
 //                          <= r sqrt(d) (|x'| + |c'|) + r^2 d
 //   dropped products:      |L| <= |x lo| |c lo|                      (e_lo)
-//   FP32 evaluation of the two sums and their combination (three roundings,
-//   at most 2^-23 (65536 |hi.hi| + 256 |hi.lo + lo.hi|), where
+//   the epilogue's value a = hi.hi + floor((hi.lo + lo.hi) / 256) in units
+//   of 65536: the floor loses less than one unit (65536), and the FP32
+//   conversion of a (exact below 2^24) at most 2^-24 65536 |a| <=
+//   2^-23 (65536 |hi.hi| + 256 |hi.lo + lo.hi|), where
 //   65536 |hi.hi| <= (|x'| + 128.5 sqrt(d)) (|c'| + 128.5 sqrt(d)) and
-//   256 |hi.lo + lo.hi| <= 128 sqrt(d) (|x'| + |c'|) + 32896 d):
-//                          2^-22 (|x'| + 160 sqrt(d)) (|c'| + 160 sqrt(d))
+//   256 |hi.lo + lo.hi| <= 128 sqrt(d) (|x'| + |c'|) + 32896 d:
+//                          65536 + 2^-22 (|x'| + 160 sqrt(d)) (|c'| + 160 sqrt(d))
 //   the FP32 chain:        gamma_d sum|x' c'| <= gamma_d |x'| |c'|
 void screen_bound_q8(size_t d, float& e_rel, float& e_abs, float& e_min, float& e_lo) {
   const double dd = (double)d, sd = std::sqrt(dd);
@@ -2303,7 +2315,7 @@ void screen_bound_q8(size_t d, float& e_rel, float& e_abs, float& e_min, float& 
   e_rel = (float)((gamma_d + u22) * 1.01);
   const double rr = 0.502;
   e_abs = (float)((rr * sd + u22 * 160.0 * sd) * 1.01);
-  e_min = (float)((rr * rr * dd + u22 * 160.0 * 160.0 * dd) * 1.01);
+  e_min = (float)((rr * rr * dd + u22 * 160.0 * 160.0 * dd + 65536.0) * 1.01);
   e_lo = 1.01f;
 }
 
