@@ -49,10 +49,10 @@ sys.path.insert(0, ROOT)
 METRIC = "assign Grows/s & k-means train s (200k×768 f32, k=1024) at 1/2/4/8 B200"
 FALLBACK_PEAK_TFLOPS = 1590.0
 # DRAM bytes (read + write) per row of one screen launch, from the ncu capture
-# of k_screen on 65,536 C2 rows in profiles/k_screen_c2_65536rows.md (210.6 MB
-# read + 14.7 MB written): the split FP16 rows (3,072 B/row) plus the centroid
-# tiles and the candidate lists.
-SCREEN_DRAM_BYTES_PER_ROW = (210.6e6 + 14.7e6) / 65_536
+# of k_screen on 65,536 C2 rows in profiles/k_screen_c2_65536rows.md (104.9 MB
+# read + 7.8 MB written): the fixed-point rows (1,536 B/row) plus the centroid
+# digits and the candidate lists.
+SCREEN_DRAM_BYTES_PER_ROW = (104.9e6 + 7.8e6) / 65_536
 TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one 65,536-row screen "
                   "launch (profiles/k_screen_c2_65536rows.md), scaled by rows")
 
