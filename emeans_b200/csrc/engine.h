@@ -182,6 +182,14 @@ namespace eb {
 // training loop slower.)
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// A word of the screen's centroid summary (generation << 32 | payload, only
+// ever raised) raised to at least v. Most contributions do not raise it: the
+// word is read first (from L2) and only a larger v goes to the atomic, so
+// that a thousand blocks do not queue on one address.
+__device__ __forceinline__ void summary_max(unsigned long long* w, unsigned long long v) {
+  if (__ldcg(w) < v) atomicMax(w, v);
+}
+
 template <typename... KArgs, typename... Args>
 void launch_pdl(eb_engine* e, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
                 Args&&... args) {

@@ -252,10 +252,10 @@ __global__ void __launch_bounds__(128) k_ema_readout(
       readout[j] = ss;
       const unsigned long long tag = summary_tag(gen);
       if (!fin) {
-        atomicMax(&cinfo[2], tag | 1ull);
+        summary_max(&cinfo[2], tag | 1ull);
       } else {
-        atomicMax(&cinfo[0], tag | __float_as_uint(mx));
-        atomicMax(&cinfo[1], tag | __float_as_uint(sqrtf(ss) * (1.0f + 1.0f / 512.0f)));
+        summary_max(&cinfo[0], tag | __float_as_uint(mx));
+        summary_max(&cinfo[1], tag | __float_as_uint(sqrtf(ss) * (1.0f + 1.0f / 512.0f)));
       }
     }
   } else {
@@ -302,10 +302,10 @@ __global__ void __launch_bounds__(128) k_ema_readout(
       }
       const unsigned long long tag = summary_tag(gen);
       if (!ofin) {
-        atomicMax(&cinfo[2], tag | 1ull);
+        summary_max(&cinfo[2], tag | 1ull);
       } else {
-        atomicMax(&cinfo[0], tag | __float_as_uint(omx));
-        atomicMax(&cinfo[1], tag | __float_as_uint(sqrtf(oss) * (1.0f + 1.0f / 512.0f)));
+        summary_max(&cinfo[0], tag | __float_as_uint(omx));
+        summary_max(&cinfo[1], tag | __float_as_uint(sqrtf(oss) * (1.0f + 1.0f / 512.0f)));
       }
     }
   }
@@ -577,38 +577,46 @@ __global__ void __launch_bounds__(128) k_seg_sum(const float* __restrict__ x, in
 
 // The same with the rows streamed through shared memory (d % 4 == 0, 16-byte
 // aligned rows): a block takes one centroid and a 128-column slice, copies
-// SS_R rows' slices at a time with cp.async (SS_NS stages in flight, each
-// thread moving 16-byte chunks), and each thread adds its column of every
-// staged row in selection order: the scalar kernel's chain bit for bit. The
-// loads no longer wait on the chain, so the longest centroid's chain (which
-// sets the kernel's length) runs at shared-memory speed.
-constexpr int SS_R = 32, SS_NS = 4, SS_C = 128;
-constexpr size_t SS_SMEM = (size_t)SS_NS * SS_R * SS_C * sizeof(float);
+// R rows' slices at a time with cp.async (NS stages in flight, each thread
+// moving 16-byte chunks; the centroid's row ids staged ID at a time), and
+// each thread adds its column of every staged row in selection order: the
+// scalar kernel's chain bit for bit. The loads no longer wait on the chain,
+// so the longest centroid's chain (which sets the kernel's length) runs at
+// shared-memory speed. Two shapes: 32 rows x 4 stages (64 KB, three blocks
+// an SM) when the centroids average many rows (a full pass), 16 rows x 2
+// stages (16 KB, thirteen blocks an SM) for a training batch, whose
+// centroids average a few rows and whose blocks are mostly start-up.
+constexpr int SS_C = 128;
+template <int R, int NS>
+constexpr size_t ss_smem() {
+  return (size_t)NS * R * SS_C * sizeof(float);
+}
+template <int R, int NS, int ID>
 __global__ void __launch_bounds__(SS_C) k_seg_sum_staged(
     const float* __restrict__ x, int d, int cb, const uint32_t* __restrict__ order,
     const uint32_t* __restrict__ start, const uint32_t* __restrict__ by_size,
     float* __restrict__ sums, float* __restrict__ acc) {
   pdl_wait();
-  extern __shared__ __align__(16) float ss_buf[];  // [SS_NS][SS_R][SS_C]
-  __shared__ uint32_t ord_s[kSumStage];
+  extern __shared__ __align__(16) float ss_buf[];  // [NS][R][SS_C]
+  __shared__ uint32_t ord_s[ID];
   const long j = by_size[blockIdx.x / cb];
   const int col0 = (blockIdx.x % cb) * SS_C;
   const int t = threadIdx.x;
   const bool active = col0 + t < d;
   const uint32_t b = start[j], e = start[j + 1];
   float s = 0.0f;
-  for (uint32_t c0 = b; c0 < e; c0 += kSumStage) {
-    const uint32_t n = min(e - c0, kSumStage);
+  for (uint32_t c0 = b; c0 < e; c0 += ID) {
+    const uint32_t n = min(e - c0, (uint32_t)ID);
     __syncthreads();  // the last chunk's ids and rows are no longer read
     for (uint32_t u = t; u < n; u += SS_C) ord_s[u] = order[c0 + u];
     __syncthreads();
-    const int nst = (int)((n + SS_R - 1) / SS_R);
+    const int nst = (int)((n + R - 1) / R);
     auto issue = [&](int st) {
       if (st < nst) {
-        float* buf = ss_buf + (st % SS_NS) * SS_R * SS_C;
-        const uint32_t r0 = (uint32_t)st * SS_R;
+        float* buf = ss_buf + (st % NS) * R * SS_C;
+        const uint32_t r0 = (uint32_t)st * R;
 #pragma unroll
-        for (int u = 0; u < SS_R * SS_C / 4 / SS_C; u++) {  // 8 chunks a thread
+        for (int u = 0; u < R / 4; u++) {  // R / 4 chunks a thread
           const int idx = u * SS_C + t;
           const int r = idx / (SS_C / 4), q = idx % (SS_C / 4);
           const int col = col0 + q * 4;
@@ -624,17 +632,17 @@ __global__ void __launch_bounds__(SS_C) k_seg_sum_staged(
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
 #pragma unroll
-    for (int st = 0; st < SS_NS - 1; st++) issue(st);
+    for (int st = 0; st < NS - 1; st++) issue(st);
     for (int st = 0; st < nst; st++) {
-      issue(st + SS_NS - 1);
-      asm volatile("cp.async.wait_group %0;" ::"n"(SS_NS - 1) : "memory");
+      issue(st + NS - 1);
+      asm volatile("cp.async.wait_group %0;" ::"n"(NS - 1) : "memory");
       __syncthreads();
-      const float* buf = ss_buf + (st % SS_NS) * SS_R * SS_C + t;
-      const int rows = min(SS_R, (int)(n - (uint32_t)st * SS_R));
+      const float* buf = ss_buf + (st % NS) * R * SS_C + t;
+      const int rows = min(R, (int)(n - (uint32_t)st * R));
       if (active) {
-        if (rows == SS_R) {
+        if (rows == R) {
 #pragma unroll
-          for (int r = 0; r < SS_R; r++) s = __fadd_rn(s, buf[r * SS_C]);
+          for (int r = 0; r < R; r++) s = __fadd_rn(s, buf[r * SS_C]);
         } else {
           for (int r = 0; r < rows; r++) s = __fadd_rn(s, buf[r * SS_C]);
         }
@@ -805,13 +813,19 @@ void label_order(eb_engine* e, const uint32_t* ids, size_t r0, size_t r1, size_t
   if (by_size_out) *by_size_out = by_size;
 }
 
-static void set_seg_sum_smem(int device) {
-  static uint64_t done = 0;
-  if (!(done >> device & 1)) {
-    EB_CUDA(cudaFuncSetAttribute(k_seg_sum_staged, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)SS_SMEM));
-    done |= 1ull << device;
+template <int R, int NS, int ID>
+static void launch_seg_sum_staged(eb_engine* e, unsigned grid, const float* x, size_t d,
+                                  unsigned cb, const uint32_t* order, const uint32_t* start,
+                                  const uint32_t* by_size, float* sums, float* acc) {
+  static uint64_t done = 0;  // one instance per shape
+  if (!(done >> e->device & 1)) {
+    EB_CUDA(cudaFuncSetAttribute(k_seg_sum_staged<R, NS, ID>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)ss_smem<R, NS>()));
+    done |= 1ull << e->device;
   }
+  launch_pdl(e, k_seg_sum_staged<R, NS, ID>, grid, SS_C, ss_smem<R, NS>(), x, (int)d, (int)cb,
+             order, start, by_size, sums, acc);
 }
 
 void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_t* ids, size_t r0,
@@ -823,9 +837,12 @@ void scatter_add(eb_engine* e, const float* x, size_t n, size_t d, const uint32_
                    (!acc || ((uintptr_t)acc & 15) == 0);
   if (vec) {
     const unsigned cb = blocks_for(d, SS_C);
-    set_seg_sum_smem(e->device);
-    launch_pdl(e, k_seg_sum_staged, (unsigned)(k * cb), SS_C, SS_SMEM, x, (int)d, (int)cb, order,
-               start, by_size, sums, acc);
+    if (r1 - r0 <= 48 * k)  // a few rows a centroid on average
+      launch_seg_sum_staged<16, 2, 256>(e, (unsigned)(k * cb), x, d, cb, order, start, by_size,
+                                        sums, acc);
+    else
+      launch_seg_sum_staged<32, 4, 1024>(e, (unsigned)(k * cb), x, d, cb, order, start, by_size,
+                                         sums, acc);
   } else {
     const unsigned cb = blocks_for(d, 128);
     launch_pdl(e, k_seg_sum, (unsigned)(k * cb), 128, 0, x, (int)d, (int)cb, order, start,

@@ -14,8 +14,10 @@ from tests.helpers import bits, mixture
 
 pytestmark = pytest.mark.gpu
 
+# The last two average hundreds of rows a centroid (the staged sum's full-pass
+# shape; the others take its training-batch shape).
 SHAPES = [(1000, 768, 64), (777, 768, 100), (513, 13, 70), (2000, 20, 300), (300, 64, 1),
-          (600, 768, 1024)]
+          (600, 768, 1024), (20000, 96, 32), (12000, 768, 40)]
 
 
 @pytest.mark.parametrize("n,d,k", SHAPES)
