@@ -138,7 +138,8 @@ static_assert(128 * REG_PRODUCER + 256 * REG_EPILOGUE <= NTHREADS * 168, "regist
 constexpr int HALF = BN / 2;     // tile columns per epilogue warp (two warps per TMEM lane quadrant)
 constexpr uint32_t FALLBACK = 0xFFFFFFFFu;
 constexpr int XEXP_BAD = INT_MIN;  // row with a non-finite value
-constexpr size_t PASS_WAVES = 8;   // row tiles per SM in one pass
+constexpr size_t PASS_WAVES = 8;   // row tiles per SM in one pass (top-k, products)
+constexpr size_t PASS_WAVES_TOP1 = 12;  // at most, in one top-1 pass
 constexpr uint64_t WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
 // Operand ring, 256 B of barriers / TMEM slot / flags, the centroid norms of
@@ -2361,10 +2362,12 @@ uint32_t convert_centroids(eb_engine* e, const float* c, size_t k, size_t d, siz
 
 // Parts per row tile: the count (1, 2 or 4, at most the centroid tiles) that
 // minimises the screen's length in centroid-tile times, waves of units times
-// tiles per part (a unit per SM at a time); ties keep fewer parts. With many
-// row tiles every SM is busy at one part; a slice of a few dozen row tiles
-// (a training batch split over GPUs, or a pass's ragged last wave) spreads
-// each row tile's centroid tiles over several SMs.
+// tiles per part (a unit per SM at a time). More parts mean more candidate
+// lists per row for the collect step (two per part), so a larger count is
+// taken only when it shortens the screen by a tenth or more. With many row
+// tiles every SM is busy at one part; a slice of a few dozen row tiles (a
+// training batch split over GPUs) spreads each row tile's centroid tiles over
+// several SMs.
 int screen_parts(size_t rtiles, int ntiles, int sms) {
   int best = 1;
   size_t best_t = (size_t)-1;
@@ -2372,7 +2375,7 @@ int screen_parts(size_t rtiles, int ntiles, int sms) {
     const int tpp = (ntiles + p - 1) / p;
     if ((ntiles + tpp - 1) / tpp != p) continue;  // a part would be empty
     const size_t t = (rtiles * (size_t)p + (size_t)sms - 1) / (size_t)sms * (size_t)tpp;
-    if (t < best_t) {
+    if (best_t == (size_t)-1 || 10 * t <= 9 * best_t) {
       best_t = t;
       best = p;
     }
@@ -2476,10 +2479,15 @@ void top1_screen(eb_engine* e, const Top1Args& a, eb_buf* xbuf) {
   const size_t d = a.d, k = a.k;
   const size_t dp = (d + BK8 - 1) / BK8 * BK8;  // bytes of a fixed-point row
   const size_t m_all = a.r1 - a.r0;
-  // Rows per pass: eight 128-row tiles per SM, so that each persistent CTA
-  // keeps its operand ring running across tiles.
+  // Rows per pass: the call split into equal passes of at most twelve
+  // 128-row tiles per SM (a C2 assign is one pass), so that each persistent
+  // CTA keeps its operand ring running across tiles and the exact stage runs
+  // once per pass.
   const size_t wave = (size_t)e->num_sms * BM;
-  const size_t chunk = std::min(m_all, PASS_WAVES * wave);
+  const size_t max_chunk = PASS_WAVES_TOP1 * wave;
+  const size_t npass = (m_all + max_chunk - 1) / max_chunk;
+  const size_t chunk =
+      std::min(m_all, ((m_all + npass - 1) / std::max<size_t>(npass, 1) + BM - 1) / BM * BM);
   const bool ip = a.metric == EB_IP;
 
   float e_rel, e_abs, e_min, e_lo;
