@@ -1361,19 +1361,21 @@ __device__ __forceinline__ unsigned long long scan_start_key() {
   return result_key<IP>(IP ? -INFINITY : INFINITY, 0u);
 }
 
-// Each row's candidates (from its nl = 2 parts lists, one per part and half
-// tile) still inside its final window become (row, centroid) pairs; the
+// Each row's candidates (from its nl lists, two per part: one per part and
+// half tile) still inside its final window become (row, centroid) pairs; the
 // window is the tightest of the lists' thresholds, the one of the row's
 // overall best. Rows with none, with more than SURV, or marked for the
 // fallback go to the exact list, whose key starts at the scan's starting
 // point. The row's pair key starts at the identity of its reduction. Launched
-// with 256 threads a block. The first eight entries of the first two lists
-// stay in registers between the counting and the writing pass; the pair slots
-// are reserved with one atomic per block (the per-warp atomics on one counter
-// serialised).
+// with 256 threads a block at no more than 40 registers a thread, so that
+// six blocks share an SM and a whole C2 pass's rows are in flight at once (at
+// 107 registers, two blocks an SM made it three waves of dependent loads);
+// the entries are read twice, to count and to write, the second time from
+// L2. The pair slots are reserved with one atomic per block (the per-warp
+// atomics on one counter serialised).
 constexpr int MAX_PARTS = 4;
 template <bool IP>
-__global__ void __launch_bounds__(256) k_collect(
+__global__ void __launch_bounds__(256, 6) k_collect(
     long p0, long m, uint32_t k, int nl, const uint2* __restrict__ cand,
     const uint32_t* __restrict__ cand_cnt, const float* __restrict__ cand_thr,
     uint2* __restrict__ pairs, uint32_t* __restrict__ pair_count,
@@ -1386,52 +1388,46 @@ __global__ void __launch_bounds__(256) k_collect(
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const bool live = i < m;
-  uint32_t cnt[2 * MAX_PARTS];
+  // The lists' counts and thresholds, all loads in flight together (a
+  // fallback list's threshold is not written and not used).
   bool fb = !live;
-#pragma unroll
-  for (int h = 0; h < 2 * MAX_PARTS; h++) {
-    cnt[h] = live && h < nl ? cand_cnt[h * m + i] : 0;
-    if (cnt[h] == FALLBACK) {
-      fb = true;
-    } else if (cnt[h] > CAP) {
-      atomicOr(status, ST_BAD_STATE);
-      fb = true;
-    }
-  }
-  if (fb)
-#pragma unroll
-    for (int h = 0; h < 2 * MAX_PARTS; h++) cnt[h] = 0;
-  uint32_t ns = 0;
   float thr = IP ? -INFINITY : INFINITY;
-  uint2 first[2][8];
-  if (!fb)
+  if (live) {
     for (int h = 0; h < nl; h++) {
-      const float th = cand_thr[h * m + i];
+      const uint32_t c = __ldg(cand_cnt + h * m + i);
+      const float th = __ldg(cand_thr + h * m + i);
+      if (c == FALLBACK) {
+        fb = true;
+      } else if (c > CAP) {
+        atomicOr(status, ST_BAD_STATE);
+        fb = true;
+      }
       thr = IP ? fmaxf(thr, th) : fminf(thr, th);
     }
+  }
+  // Count the entries inside the window, four loads at a time.
+  uint32_t ns = 0;
+  bool bad_entry = false;
+  if (!fb) {
+    for (int h = 0; h < nl; h++) {
+      const uint32_t c = __ldg(cand_cnt + h * m + i);
+      const uint2* lst = cand + (long)h * CAP * m + i;
+      for (uint32_t e0 = 0; e0 < c; e0 += 4) {
+        uint2 en[4];
 #pragma unroll
-  for (int h = 0; h < 2 * MAX_PARTS; h++) {
-    const uint2* lst = cand + (long)h * CAP * m + i;
-    // Loads in batches of eight, so that they are in flight together.
-    for (uint32_t e0 = 0; e0 < cnt[h]; e0 += 8) {
-      uint2 en[8];
+        for (int u = 0; u < 4; u++)
+          en[u] = e0 + u < c ? __ldg(lst + (e0 + u) * m) : make_uint2(0u, __float_as_uint(NAN));
 #pragma unroll
-      for (int u = 0; u < 8; u++)
-        en[u] = e0 + u < cnt[h] ? lst[(e0 + u) * m] : make_uint2(0u, __float_as_uint(NAN));
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const float sv = __uint_as_float(en[u].y);
-        if (en[u].x >= k) fb = true;
-        ns += IP ? (sv >= thr) : (sv <= thr);
-        if (h < 2 && e0 == 0) first[h < 2 ? h : 0][u] = en[u];
+        for (int u = 0; u < 4; u++) {
+          const float sv = __uint_as_float(en[u].y);
+          bad_entry |= en[u].x >= k;
+          ns += IP ? (sv >= thr) : (sv <= thr);
+        }
       }
     }
   }
-  uint32_t listed_entries = 0;
-#pragma unroll
-  for (int h = 0; h < 2 * MAX_PARTS; h++) listed_entries += cnt[h];
-  if (fb && live && listed_entries > 0) atomicOr(status, ST_BAD_STATE);
-  fb = fb || ns == 0 || ns > SURV;
+  if (bad_entry) atomicOr(status, ST_BAD_STATE);
+  fb = fb || bad_entry || ns == 0 || ns > SURV;
   const bool listed = live && fb;
   const uint32_t np = live && !fb ? ns : 0;
   if (live) {
@@ -1468,21 +1464,15 @@ __global__ void __launch_bounds__(256) k_collect(
   __syncthreads();
   uint32_t w = wbase[warp] + incl - np;
   if (np) {
-#pragma unroll
-    for (int h = 0; h < 2 * MAX_PARTS; h++) {
+#pragma unroll 1
+    for (int h = 0; h < nl; h++) {
+      const uint32_t c = __ldg(cand_cnt + h * m + i);
       const uint2* lst = cand + (long)h * CAP * m + i;
-      for (uint32_t e0 = 0; e0 < cnt[h]; e0 += 8) {
-        uint2 en[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++)
-          en[u] = (h < 2 && e0 == 0)
-                      ? first[h < 2 ? h : 0][u]
-                      : (e0 + u < cnt[h] ? lst[(e0 + u) * m] : make_uint2(0u, __float_as_uint(NAN)));
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-          const float sv = __uint_as_float(en[u].y);
-          if (IP ? (sv >= thr) : (sv <= thr)) pairs[w++] = make_uint2((uint32_t)i, en[u].x);
-        }
+#pragma unroll 4
+      for (uint32_t e = 0; e < c; e++) {
+        const uint2 en = __ldg(lst + e * m);
+        const float sv = __uint_as_float(en.y);
+        if (IP ? (sv >= thr) : (sv <= thr)) pairs[w++] = make_uint2((uint32_t)i, en.x);
       }
     }
   }
