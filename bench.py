@@ -445,11 +445,13 @@ def run_ours(args):
         mres = eng.internal_scores(x, d, glab, k)
         met_ms = (time.perf_counter() - t0) * 1e3
 
-    c3 = c4 = None
+    c3 = c4 = c5 = None
     if not args.no_c3:
         c3 = c3_leg(eng, args, world, rank, local, dist)
     if not args.no_c4:
         c4 = c4_leg(eng, args, world, rank, dist)
+    if not args.no_c5 and world == 1:
+        c5 = c5_leg(eng, args)
 
     if rank == 0:
         peak, peak_src = peaks()
@@ -542,6 +544,8 @@ def run_ours(args):
             out["c3"] = c3
         if c4:
             out["c4"] = c4
+        if c5:
+            out["c5_sweep"] = c5
         out["clocks"] = clk.summary()
         if not args.no_cpu:
             # Parity of the scored run: the oracle's labels and scores over the
@@ -763,6 +767,67 @@ def c4_leg(eng, args, world, rank, dist):
     return res
 
 
+def c5_leg(eng, args):
+    """BASELINE config 5's level-1 sweep path (auto::sweep, crates/emeans-cluster/
+    src/auto.rs:455-505) on a C5-shaped sample, one GPU: the rows bound once,
+    then for k in (32, 64, 128) two fits each (spherical training with
+    AutoConfig's 5 epochs, inner-product assignment of every row), the better
+    kept and scored by internal_scores. The oracle runs the first fit (train,
+    assign, internal scores) on the host cores: the parity check and the CPU
+    baseline of that fit."""
+    import oracle
+    from oracle import metrics as ometrics
+
+    n, d = args.c5_n, 768
+    x = gen_c5_rows(n, d)
+    ks, restarts, nepochs, seed, salt = (32, 64, 128), 2, 5.0, 1234, 0
+    eng.bind_data(x, d)
+    eng.sweep(x, d, ks[:1], nepochs, seed, salt, restarts=1)  # warm-up
+    eng.sync()
+    t0 = time.perf_counter()
+    res = eng.sweep(x, d, ks, nepochs, seed, salt, restarts=restarts)
+    sweep_s = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    tr, lab, sco = eng.fit(x, d, ks[0], nepochs, eb_seed_for(seed, salt, ks[0], 0))
+    gmet = eng.internal_scores(x, d, lab, ks[0])
+    fit_s = time.perf_counter() - t0
+    eng.unbind_data()
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    want = oracle.train(x, d, ks[0], nepochs=nepochs, seed=eb_seed_for(seed, salt, ks[0], 0),
+                        spherical=True, threads=threads)
+    wl, ws = oracle.top1(x.ravel(), d, want["centroids"], oracle.IP, threads=threads)
+    wmet = ometrics.internal_scores(x, d, wl, ks[0])
+    cpu_s = time.perf_counter() - t0
+    rel = {key: abs(gmet[key] - wmet[key]) / max(abs(wmet[key]), 1e-30)
+           for key in ("silhouette", "calinski_harabasz", "davies_bouldin", "objective")}
+    return {"workload": f"C5 level-1 sweep: {n:,} x {d} nested-mixture unit rows (64 x 32 "
+                        "sub-means, 2% near-duplicates), k in (32, 64, 128), 2 fits each, "
+                        "spherical, 5 epochs, rows bound once (SharedAssigner)",
+            "rows": n, "d": d, "ks": list(ks), "restarts": restarts,
+            "sweep_s": sweep_s, "fits": len(ks) * restarts,
+            "chosen": [{"k": k, "objective": obj, "silhouette": sc["silhouette"],
+                        "k_eff": sc["k_eff"]} for k, sc, _, _, _, obj in res],
+            "one_fit_s": fit_s,
+            "parity": {"fit": f"k={ks[0]}, restart 0",
+                       "centroids_equal": bool(np.array_equal(
+                           tr.centroids.ravel().view(np.uint32),
+                           want["centroids"].view(np.uint32))),
+                       "labels_equal": bool(np.array_equal(lab, wl)),
+                       "scores_equal": bool(np.array_equal(sco.view(np.uint32),
+                                                           ws.view(np.uint32))),
+                       "internal_scores_max_rel_diff": max(rel.values())},
+            "cpu_baseline": {"value": cpu_s, "unit": "s", "cores": threads, "kind": "port",
+                             "sample": f"the first fit (k={ks[0]}: train, assign, internal "
+                                       "scores) on the host, oracle/"}}
+
+
+def eb_seed_for(seed, salt, k, restart):
+    import emeans_b200 as eb
+
+    return eb.seed_for(seed, salt, k, restart)
+
+
 def run_knn(args):
     """--knn N: the kNN self-join config's shape on N rows (d 384, kk 10, inner
     product, self excluded) through eb_topk with host arrays; one JSON line."""
@@ -807,6 +872,8 @@ def main():
     ap.add_argument("--load-cent", default=None, help="use these centroids instead of training")
     ap.add_argument("--no-c3", action="store_true", help="skip the config-3 assign leg")
     ap.add_argument("--no-c4", action="store_true", help="skip the config-4 kNN leg")
+    ap.add_argument("--no-c5", action="store_true", help="skip the config-5 sweep leg")
+    ap.add_argument("--c5-n", type=int, default=200_000)
     ap.add_argument("--c3-n", type=int, default=10_000_000)
     ap.add_argument("--c3-steps", type=int, default=2)
     ap.add_argument("--c3-check", type=int, default=100_000,

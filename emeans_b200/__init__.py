@@ -75,7 +75,7 @@ class EngineError(RuntimeError):
 class Stats(C.Structure):
     _fields_ = [("screened_rows", C.c_uint64), ("fallback_rows", C.c_uint64),
                 ("rescored_candidates", C.c_uint64), ("exact_rows", C.c_uint64),
-                ("kernel_launches", C.c_uint64)]
+                ("kernel_launches", C.c_uint64), ("h2d_bytes", C.c_uint64)]
 
 
 class TrainJob(C.Structure):
@@ -543,6 +543,72 @@ class Engine:
                        nsplit=list(out.nsplit[:ne]), epoch_time=list(out.epoch_time[:ne]),
                        n_splits=out.n_splits, batch_size=out.batch_size, alpha0=out.alpha0,
                        total_steps=out.total_steps)
+
+
+    def fit(self, x, d: int, k: int, nepochs: float, seed: int, init_rows=None):
+        """``auto::fit`` (crates/emeans-cluster/src/auto.rs:350-375) on the
+        engine: one spherical model (``Config::new(d, k)`` with spherical,
+        nepochs and seed set, assignments not captured) trained on x, from the
+        rows ``init_rows[:k]`` when given (``train_from``), and x assigned to
+        it by inner product (``Emeans::assign``). With x bound
+        (``bind_data``), the training and the assignment both read the bound
+        rows in place: a sweep of fits uploads the data once, as the
+        reference's ``SharedAssigner`` shares one binding across its fits.
+        Returns (Trained, labels, scores)."""
+        x = _f32(x).ravel()
+        cfg = Config(d=d, k=k, nepochs=float(nepochs), seed=int(seed), spherical=True,
+                     capture_assignments=False)
+        init = None
+        if init_rows is not None:
+            r = np.asarray(init_rows, np.int64).ravel()
+            if r.size < k:
+                raise ValueError("need k init rows")
+            init = x.reshape(-1, d)[r[:k]]
+        tr = self.train(x, cfg, init=init)
+        labels, scores = self.assign(x, d, tr.centroids, IP)
+        return tr, labels, scores
+
+    def sweep(self, x, d: int, ks, nepochs: float, seed: int, salt: int = 0, restarts: int = 1,
+              init_rows=None):
+        """``auto::sweep`` (crates/emeans-cluster/src/auto.rs:455-505) on the
+        engine: for every k of ks, ``restarts`` fits (``fit``, seeds from
+        ``seed_for``), the one with the lowest mean objective kept (the first
+        on ties; ``Assignment::mean_objective``, model.rs:127-141: the
+        sequential f64 mean of 2 - 2 cos), and its labels scored by
+        ``internal_scores``. ``init_rows``: one row-id list per restart (the
+        k-means++ picks, whose first k rows seed the fit with k clusters) or
+        None for the seeded random rows. Bind x first (``bind_data``) to keep
+        the rows on the device across the fits. Returns a list of
+        (k, internal scores, Trained, labels, scores, mean objective)."""
+        out = []
+        for k in ks:
+            best = None
+            for r in range(max(int(restarts), 1)):
+                rows = None if init_rows is None else init_rows[r]
+                tr, lab, sco = self.fit(x, d, k, nepochs, seed_for(seed, salt, k, r), rows)
+                obj = mean_objective(sco, spherical=True)
+                if best is None or obj < best[0]:
+                    best = (obj, tr, lab, sco)
+            obj, tr, lab, sco = best
+            out.append((k, self.internal_scores(x, d, lab, k), tr, lab, sco, obj))
+        return out
+
+
+def mean_objective(scores, spherical: bool) -> float:
+    """``Assignment::mean_objective`` (crates/emeans-core/src/model.rs:127-141):
+    the f64 mean, summed in row order, of 2 - 2 cos (spherical) or of the
+    squared distances."""
+    v = np.asarray(scores, np.float32).astype(np.float64)
+    if spherical:
+        v = 2.0 - 2.0 * v
+    return float(np.cumsum(v)[-1]) / max(v.size, 1) if v.size else 0.0
+
+
+def seed_for(seed: int, salt: int, k: int, restart: int) -> int:
+    """A sweep fit's seed (crates/emeans-cluster/src/auto.rs:343-348): u32
+    wrapping arithmetic on the configured seed, a salt, k and the restart."""
+    m = 0xFFFFFFFF
+    return (seed + (salt * 7919 & m) + (k * 131 & m) + (restart * 1_000_003 & m)) & m
 
 
 GROUP_ID_BYTES = 128

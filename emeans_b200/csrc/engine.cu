@@ -703,6 +703,13 @@ int eb_assign(eb_engine* e, const float* rows, size_t n, size_t d, const uint32_
       xb.ptr = xd; xb.len = m * d; xb.dtype = EB_F32;
       rc = eb_top1(e, &xb, d, nullptr, 0, m, &cb, metric == EB_L2 ? &cnb : nullptr, k, metric,
                    &lb, &sb);
+    } else if (e->bound && e->bound_host == rows && e->bound_n == n && e->bound->d == d) {
+      // Dense rows that are the bound data set (the host pointer and shape the
+      // binding is served by, as for indexed rows): read in place with the
+      // binding's norms and screen copy, so that every fit of a sweep over
+      // one bound set assigns without uploading it again.
+      rc = eb_top1(e, e->bound, d, nullptr, 0, m, &cb, metric == EB_L2 ? &cnb : nullptr, k,
+                   metric, &lb, &sb);
     } else {
       // Dense rows: copied in slices on the copy stream, each slice's top-1
       // queued on the engine's stream behind its own copy, so that the copy

@@ -78,6 +78,7 @@ bool host_pinned(const void* p) {
 
 void h2d(eb_engine* e, void* dst, const void* src, size_t bytes, cudaStream_t st) {
   if (!bytes) return;
+  e->stats.h2d_bytes += bytes;
   if (bytes < (1u << 20) || host_pinned(src)) {
     EB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, st));
     return;

@@ -86,13 +86,17 @@ int eb_engine_stream(eb_engine* e, void** stream);
 
 /* Counters since creation: rows top-1 screened on tensor cores, rows that fell
  * back to the exact full scan, candidates re-scored exactly, rows served by the
- * exact SIMT kernel directly, and kernels launched. */
+ * exact SIMT kernel directly, kernels launched, and bytes of caller memory
+ * copied to the device by the buffer, bind, assign, top-k and internal-scores
+ * calls (rows, centroids, labels; not the training loop's own small
+ * uploads). */
 typedef struct {
   uint64_t screened_rows;
   uint64_t fallback_rows;
   uint64_t rescored_candidates;
   uint64_t exact_rows;
   uint64_t kernel_launches;
+  uint64_t h2d_bytes;
 } eb_stats;
 int eb_get_stats(eb_engine* e, eb_stats* out);
 

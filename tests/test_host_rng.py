@@ -136,3 +136,17 @@ def test_revival_plan_matches_oracle(plan_driver, k):
         assert got[0] == len(want), (r, got[0], len(want))
         pairs = list(zip(got[1::2], got[2::2]))
         assert pairs == want, r
+
+
+def test_sweep_seed_wraps_like_u32():
+    """auto.rs:343-348: seed + salt 7919 + k 131 + restart 1,000,003, each
+    product and sum wrapping at 2^32."""
+    import emeans_b200 as eb
+
+    m = 2 ** 32
+    for seed, salt, k, restart in [(7, 3, 64, 2), (2 ** 32 - 1, 1, 1, 1), (123, 2 ** 31, 2 ** 20, 5000),
+                                   (0, 0, 0, 0)]:
+        want = seed
+        for term in (salt * 7919 % m, k * 131 % m, restart * 1_000_003 % m):
+            want = (want + term) % m
+        assert eb.seed_for(seed, salt, k, restart) == want
