@@ -172,6 +172,44 @@ __global__ void k_ema(float* __restrict__ pos, float* __restrict__ usage,
   if (threadIdx.x == 0) usage[j] = mass;
 }
 
+// k_ema with 16-byte loads and stores (d % 4 == 0, aligned rows): one block
+// per centroid, each thread four consecutive columns a round, the same
+// per-element arithmetic.
+__global__ void k_ema4(float* __restrict__ pos, float* __restrict__ usage,
+                       const float* __restrict__ sums, const uint32_t* __restrict__ counts, int d,
+                       float a32, float decay, int replace) {
+  pdl_wait();
+  const long j = blockIdx.x;
+  const float u = usage[j];
+  const uint32_t cnt = counts[j];
+  const float ud = replace ? u : __fmul_rn(u, decay);
+  float mass = ud;
+  if (cnt != 0) {
+    const float count = __uint2float_rn(cnt);
+    const float retained = replace ? 0.0f : ud;
+    const float step = __fmul_rn(a32, count);
+    mass = __fadd_rn(retained, step);
+    const float w = __fdiv_rn(step, mass);
+    float4* c = reinterpret_cast<float4*>(pos + j * d);
+    const float4* s = reinterpret_cast<const float4*>(sums + j * d);
+    for (int q = threadIdx.x; q < d / 4; q += blockDim.x) {
+      const float4 sv = s[q];
+      float4 cv = c[q];
+      auto one = [&](float sx, float cx) {
+        const float mean = __fdiv_rn(sx, count);
+        return w == 1.0f ? mean : __fadd_rn(cx, __fmul_rn(w, __fsub_rn(mean, cx)));
+      };
+      cv.x = one(sv.x, cv.x);
+      cv.y = one(sv.y, cv.y);
+      cv.z = one(sv.z, cv.z);
+      cv.w = one(sv.w, cv.w);
+      c[q] = cv;
+    }
+  }
+  __syncthreads();  // every thread has read usage[j]
+  if (threadIdx.x == 0) usage[j] = mass;
+}
+
 // The EMA step (k_ema's arithmetic, bit for bit) fused with the next step's
 // readout of the updated centroid and the screen's summary of the centroids
 // it will read (k_cent_max's words: max |c|, a bound on the row norm, a
@@ -350,121 +388,130 @@ __global__ void k_split(float* __restrict__ pos, float* __restrict__ usage,
 // ---- deterministic scatter-add: a stable counting sort by label, then one
 // sequential f32 sum per (centroid, column) in selection order.
 
-constexpr int kSeg = 256;  // positions per segment (one warp ranks a segment)
-
-// In-segment stable rank of every position among positions with its label,
-// and the per-(segment, label) counts. With SMEM (k <= kRankSmem) each warp
-// counts in its own shared-memory histogram and writes it out whole at the
-// end (no zeroing pass over segcnt, no global read-modify-writes); otherwise
-// it counts in segcnt, which the caller zeroes.
+// The positions are cut into segments; a segment's positions are ranked
+// among the segment's positions with the same label (stable), the segment's
+// per-label counts are scanned over the segments per label, the labels'
+// totals are scanned over the labels, and each position lands at
+// start[label] + (its label's count in earlier segments) + its rank.
+// Two segment shapes: with k <= kRankSmem a block of eight warps ranks
+// kBlockSeg positions in shared-memory histograms (one per warp, combined
+// in warp order), so the per-(segment, label) table has one row per 2,048
+// positions; with larger k one warp ranks kSeg positions with its counts in
+// global memory (the caller zeroes them).
+constexpr int kSeg = 256;  // positions a warp ranks
+constexpr int kRankWarps = 8;
+constexpr int kBlockSeg = kSeg * kRankWarps;  // positions a block ranks (k <= kRankSmem)
 constexpr uint32_t kRankSmem = 1024;
 
-template <bool SMEM>
-__global__ void __launch_bounds__(256) k_seg_rank(const uint32_t* __restrict__ labels, long r0,
-                                                  long m, uint32_t k,
-                                                  uint32_t* __restrict__ segcnt,
-                                                  uint32_t* __restrict__ rank, uint32_t* status) {
-  pdl_wait();
-  __shared__ uint32_t hist[SMEM ? 8 : 1][SMEM ? kRankSmem : 1];
-  long seg = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  int lane = threadIdx.x & 31;
-  long segs = (m + kSeg - 1) / kSeg;
-  if (seg >= segs) return;
-  uint32_t* cnt = SMEM ? hist[threadIdx.x / 32] : segcnt + seg * (long)k;
-  if (SMEM) {
-    for (uint32_t l = lane; l < k; l += 32) cnt[l] = 0;
-    __syncwarp();
-  }
+// In-warp stable ranks of the warp's kSeg positions starting at p0, counted
+// in cnt (shared or global; only the warp touches it). lab[] receives the
+// labels (0xFFFFFFFF past the end or for a bad label), rk[] the ranks.
+__device__ __forceinline__ void warp_rank(const uint32_t* __restrict__ labels, long r0, long m,
+                                          long p0, uint32_t k, uint32_t* cnt,
+                                          uint32_t (&lab)[kSeg / 32], uint32_t (&rk)[kSeg / 32],
+                                          uint32_t* status) {
+  const int lane = threadIdx.x & 31;
   // The segment's labels for this lane, all loads in flight together.
-  uint32_t lab[kSeg / 32];
 #pragma unroll
   for (int c = 0; c < kSeg / 32; c++) {
-    const long p = seg * kSeg + c * 32 + lane;
+    const long p = p0 + c * 32 + lane;
     lab[c] = p < m ? labels[r0 + p] : 0xFFFFFFFFu;
   }
 #pragma unroll
-  for (int c = 0; c < kSeg; c += 32) {
-    long p = seg * kSeg + c + lane;
-    uint32_t l = lab[c / 32];
-    bool valid = l < k;
+  for (int c = 0; c < kSeg / 32; c++) {
+    const long p = p0 + c * 32 + lane;
+    const uint32_t l = lab[c];
+    const bool valid = l < k;
     if (p < m && !valid) atomicOr(status, ST_BAD_LABEL);
-    uint32_t key = valid ? l : 0xFFFFFFFFu;
-    uint32_t peers = __match_any_sync(0xFFFFFFFFu, key);
-    int leader = __ffs(peers) - 1;
+    if (!valid) lab[c] = 0xFFFFFFFFu;
+    const uint32_t peers = __match_any_sync(0xFFFFFFFFu, valid ? l : 0xFFFFFFFFu);
+    const int leader = __ffs(peers) - 1;
     uint32_t base = 0;
     if (valid && lane == leader) {
       base = cnt[l];
       cnt[l] = base + __popc(peers);
     }
     base = __shfl_sync(0xFFFFFFFFu, base, leader);
-    if (valid) rank[p] = base + __popc(peers & ((1u << lane) - 1u));
+    rk[c] = base + __popc(peers & ((1u << lane) - 1u));
     __syncwarp();
   }
-  if (SMEM)
-    for (uint32_t l = lane; l < k; l += 32) segcnt[seg * (long)k + l] = cnt[l];
 }
 
-// Per label: exclusive prefix of its counts over segments (in place), and
-// the label's total. One warp per label: in each round lane l reads a run of
-// kScanR consecutive segments (all loads in flight together), the warp scans
-// the runs' sums, and each lane writes its run's prefixes.
-constexpr int kScanR = 16;
-__global__ void __launch_bounds__(256) k_seg_scan(uint32_t* __restrict__ segcnt, long segs,
-                                                  uint32_t k, uint32_t* __restrict__ counts) {
+// k > kRankSmem: one warp per kSeg positions, counts in segcnt (zeroed by
+// the caller; only the segment's warp updates its row).
+__global__ void __launch_bounds__(256) k_seg_rank(const uint32_t* __restrict__ labels, long r0,
+                                                  long m, uint32_t k,
+                                                  uint32_t* __restrict__ segcnt,
+                                                  uint32_t* __restrict__ rank, uint32_t* status) {
   pdl_wait();
-  const uint32_t l = (uint32_t)(((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const long seg = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const long segs = (m + kSeg - 1) / kSeg;
+  if (seg >= segs) return;
+  uint32_t lab[kSeg / 32], rk[kSeg / 32];
+  warp_rank(labels, r0, m, seg * kSeg, k, segcnt + seg * (long)k, lab, rk, status);
   const int lane = threadIdx.x & 31;
-  if (l >= k) return;  // the whole warp: its lanes share l
-  uint32_t carry = 0;
-  for (long s0 = 0; s0 < segs; s0 += 32 * kScanR) {
-    const long my0 = s0 + (long)lane * kScanR;
-    uint32_t c[kScanR];
-    uint32_t sum = 0;
 #pragma unroll
-    for (int r = 0; r < kScanR; r++) {
-      c[r] = my0 + r < segs ? segcnt[(my0 + r) * k + l] : 0u;
-      sum += c[r];
-    }
-    uint32_t incl = sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    uint32_t run = carry + incl - sum;
-#pragma unroll
-    for (int r = 0; r < kScanR; r++) {
-      if (my0 + r < segs) segcnt[(my0 + r) * k + l] = run;
-      run += c[r];
-    }
-    carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
-  }
-  if (lane == 0) counts[l] = carry;
+  for (int c = 0; c < kSeg / 32; c++)
+    if (lab[c] != 0xFFFFFFFFu) rank[seg * kSeg + c * 32 + lane] = rk[c];
 }
 
-// Exclusive scan of counts into start[0..k], one block of 1024 threads; and
-// the labels grouped by the size of their count, largest first (bucket b =
-// bit length of the count), into by_size[0..k), so that the segment sums
-// start the longest chains in the first wave (a chain is sequential, and the
-// largest one sets the kernel's length). Only the launch order of the sum
-// blocks depends on by_size: the order within a bucket is the order of the
-// shared-memory atomics, and every sum comes out the same.
-__global__ void __launch_bounds__(1024) k_label_scan(const uint32_t* __restrict__ counts,
-                                                     uint32_t k, uint32_t* __restrict__ start,
-                                                     uint32_t* __restrict__ by_size) {
+// k <= kRankSmem: one block of kRankWarps warps per kBlockSeg positions.
+// Each warp ranks its kSeg positions in its own shared histogram; the
+// histograms are then turned into each warp's offset per label (exclusive,
+// in warp order, so the ranks stay stable) and the block's totals go out as
+// the segment's row of segcnt (every entry written: no zeroing pass).
+__global__ void __launch_bounds__(kRankWarps * 32) k_block_rank(
+    const uint32_t* __restrict__ labels, long r0, long m, uint32_t k,
+    uint32_t* __restrict__ segcnt, uint32_t* __restrict__ rank, uint32_t* status) {
   pdl_wait();
-  __shared__ uint32_t part[1024];
+  __shared__ uint32_t hist[kRankWarps][kRankSmem];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long seg = blockIdx.x;
+  for (uint32_t l = lane; l < k; l += 32) hist[w][l] = 0;
+  __syncwarp();
+  uint32_t lab[kSeg / 32], rk[kSeg / 32];
+  const long p0 = seg * kBlockSeg + (long)w * kSeg;
+  warp_rank(labels, r0, m, p0, k, hist[w], lab, rk, status);
+  __syncthreads();
+  for (uint32_t l = threadIdx.x; l < k; l += blockDim.x) {
+    uint32_t off = 0;
+#pragma unroll
+    for (int v = 0; v < kRankWarps; v++) {
+      const uint32_t t = hist[v][l];
+      hist[v][l] = off;
+      off += t;
+    }
+    segcnt[seg * (long)k + l] = off;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < kSeg / 32; c++)
+    if (lab[c] != 0xFFFFFFFFu) rank[p0 + c * 32 + lane] = rk[c] + hist[w][lab[c]];
+}
+
+// Exclusive scan of counts into start[0..k] by one block of kScanThreads
+// threads, and the labels grouped by the size of their count, largest first
+// (bucket b = bit length of the count), into by_size[0..k), so that the
+// segment sums start the longest chains in the first wave (a chain is
+// sequential, and the largest one sets the kernel's length). Only the launch
+// order of the sum blocks depends on by_size: the order within a bucket is
+// the order of the shared-memory atomics, and every sum comes out the same.
+// counts were written by other blocks of the grid: read through L2.
+constexpr int kScanThreads = 256;
+__device__ void label_scan_block(const uint32_t* counts, uint32_t k, uint32_t* __restrict__ start,
+                                 uint32_t* __restrict__ by_size) {
+  __shared__ uint32_t part[kScanThreads];
   __shared__ uint32_t bins[34];
   if (threadIdx.x < 34) bins[threadIdx.x] = 0;
-  uint32_t per = (k + blockDim.x - 1) / blockDim.x;
-  uint32_t lo = threadIdx.x * per, hi = min(lo + per, k);
+  const uint32_t per = (k + kScanThreads - 1) / kScanThreads;
+  const uint32_t lo = min(threadIdx.x * per, k), hi = min(lo + per, k);
   uint32_t s = 0;
-  for (uint32_t l = lo; l < hi; l++) s += counts[l];
+  for (uint32_t l = lo; l < hi; l++) s += __ldcg(counts + l);
   part[threadIdx.x] = s;
   __syncthreads();
-  for (uint32_t l = lo; l < hi; l++) atomicAdd(&bins[32 - __clz(counts[l])], 1u);
-  for (int off = 1; off < (int)blockDim.x; off <<= 1) {
-    uint32_t v = threadIdx.x >= (unsigned)off ? part[threadIdx.x - off] : 0;
+  for (uint32_t l = lo; l < hi; l++) atomicAdd(&bins[32 - __clz(__ldcg(counts + l))], 1u);
+  for (int off = 1; off < kScanThreads; off <<= 1) {
+    const uint32_t v = threadIdx.x >= (unsigned)off ? part[threadIdx.x - off] : 0;
     __syncthreads();
     part[threadIdx.x] += v;
     __syncthreads();
@@ -472,9 +519,9 @@ __global__ void __launch_bounds__(1024) k_label_scan(const uint32_t* __restrict_
   uint32_t run = threadIdx.x ? part[threadIdx.x - 1] : 0;
   for (uint32_t l = lo; l < hi; l++) {
     start[l] = run;
-    run += counts[l];
+    run += __ldcg(counts + l);
   }
-  if (threadIdx.x == blockDim.x - 1) start[k] = part[threadIdx.x];
+  if (threadIdx.x == kScanThreads - 1) start[k] = part[threadIdx.x];
   if (threadIdx.x == 0) {
     // Bucket starts, largest bucket (32: counts of 2^31 or more) first.
     uint32_t acc = 0;
@@ -485,20 +532,77 @@ __global__ void __launch_bounds__(1024) k_label_scan(const uint32_t* __restrict_
     }
   }
   __syncthreads();
-  for (uint32_t l = lo; l < hi; l++) by_size[atomicAdd(&bins[32 - __clz(counts[l])], 1u)] = l;
+  for (uint32_t l = lo; l < hi; l++)
+    by_size[atomicAdd(&bins[32 - __clz(__ldcg(counts + l))], 1u)] = l;
+}
+
+// Per label: exclusive prefix of its counts over segments (in place), and
+// the label's total. One warp per label: in each round lane l reads a run of
+// kScanR consecutive segments (all loads in flight together), the warp scans
+// the runs' sums, and each lane writes its run's prefixes. The block that
+// finishes last (a ticket taken after each block's counts are fenced; no
+// block waits for another) then runs the label scan, and resets the ticket
+// for the next call.
+constexpr int kScanR = 16;
+__global__ void __launch_bounds__(kScanThreads) k_seg_scan(
+    uint32_t* __restrict__ segcnt, long segs, uint32_t k, uint32_t* counts,
+    uint32_t* __restrict__ start, uint32_t* __restrict__ by_size, uint32_t* ticket) {
+  pdl_wait();
+  const uint32_t l = (uint32_t)(((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (l < k) {  // the whole warp: its lanes share l
+    uint32_t carry = 0;
+    for (long s0 = 0; s0 < segs; s0 += 32 * kScanR) {
+      const long my0 = s0 + (long)lane * kScanR;
+      uint32_t c[kScanR];
+      uint32_t sum = 0;
+#pragma unroll
+      for (int r = 0; r < kScanR; r++) {
+        c[r] = my0 + r < segs ? segcnt[(my0 + r) * k + l] : 0u;
+        sum += c[r];
+      }
+      uint32_t incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      uint32_t run = carry + incl - sum;
+#pragma unroll
+      for (int r = 0; r < kScanR; r++) {
+        if (my0 + r < segs) segcnt[(my0 + r) * k + l] = run;
+        run += c[r];
+      }
+      carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
+    }
+    if (lane == 0) {
+      counts[l] = carry;
+      __threadfence();
+    }
+  }
+  __shared__ uint32_t last;
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  label_scan_block(counts, k, start, by_size);
+  if (threadIdx.x == 0) *ticket = 0;
 }
 
 // Place every position at its sorted slot; the slot holds the data row id.
+// seg_len: positions per segment of segcnt's rows (kSeg or kBlockSeg).
 __global__ void k_place(const uint32_t* __restrict__ labels, const uint32_t* __restrict__ ids,
-                        long r0, long m, long n, uint32_t k, const uint32_t* __restrict__ segcnt,
-                        const uint32_t* __restrict__ start, const uint32_t* __restrict__ rank,
-                        uint32_t* __restrict__ order, uint32_t* status) {
+                        long r0, long m, long n, uint32_t k, int seg_len,
+                        const uint32_t* __restrict__ segcnt, const uint32_t* __restrict__ start,
+                        const uint32_t* __restrict__ rank, uint32_t* __restrict__ order,
+                        uint32_t* status) {
   pdl_wait();
   long p = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= m) return;
   uint32_t l = labels[r0 + p];
   if (l >= k) return;
-  long seg = p / kSeg;
+  long seg = p / seg_len;
   uint32_t row = ids ? ids[r0 + p] : (uint32_t)(r0 + p);
   if ((long)row >= n) {
     atomicOr(status, ST_BAD_ROW);
@@ -749,8 +853,15 @@ void closing_means(eb_engine* e, const float* pos, const float* sums, const uint
 void ema_update(eb_engine* e, float* pos, float* usage, const float* sums, const uint32_t* counts,
                 size_t k, size_t d, float alpha, float decay, bool replace) {
   if (k == 0) return;
-  launch_pdl(e, k_ema, (unsigned)k, 128, 0, pos, usage, sums, counts, (int)d, alpha, decay,
-                                           replace ? 1 : 0);
+  if (d % 4 == 0 && ((uintptr_t)pos & 15) == 0 && ((uintptr_t)sums & 15) == 0) {
+    const unsigned q = (unsigned)(d / 4);
+    const unsigned threads = q >= 256 ? 256 : (q + 31) / 32 * 32;
+    launch_pdl(e, k_ema4, (unsigned)k, threads, 0, pos, usage, sums, counts, (int)d, alpha,
+               decay, replace ? 1 : 0);
+  } else {
+    launch_pdl(e, k_ema, (unsigned)k, 128, 0, pos, usage, sums, counts, (int)d, alpha, decay,
+               replace ? 1 : 0);
+  }
   EB_LAUNCH("ema_update");
 }
 
@@ -781,31 +892,33 @@ void label_order(eb_engine* e, const uint32_t* ids, size_t r0, size_t r1, size_t
                  const uint32_t* labels, size_t k, uint32_t* counts, const uint32_t** order_out,
                  const uint32_t** start_out, const uint32_t** by_size_out) {
   size_t m = r1 - r0;
-  size_t segs = (m + kSeg - 1) / kSeg;
+  const bool block_rank = m > 0 && k <= kRankSmem;
+  const size_t seg_len = block_rank ? kBlockSeg : kSeg;
+  size_t segs = (m + seg_len - 1) / seg_len;
   if (segs == 0) segs = 1;
   uint32_t* segcnt = e->scratch_get<uint32_t>("sc_segcnt", segs * k);
   uint32_t* rank = e->scratch_get<uint32_t>("sc_rank", m ? m : 1);
   uint32_t* start = e->scratch_get<uint32_t>("sc_start", k + 1);
   uint32_t* order = e->scratch_get<uint32_t>("sc_order", m ? m : 1);
   uint32_t* by_size = e->scratch_get<uint32_t>("sc_by_size", k);
-  const bool smem_rank = m > 0 && k <= kRankSmem;
-  if (!smem_rank) EB_CUDA(cudaMemsetAsync(segcnt, 0, segs * k * sizeof(uint32_t), e->stream));
-  if (m > 0) {
+  uint32_t* ticket = e->scratch_get<uint32_t>("sc_ticket", 1, true);
+  if (!block_rank) EB_CUDA(cudaMemsetAsync(segcnt, 0, segs * k * sizeof(uint32_t), e->stream));
+  if (block_rank) {
+    launch_pdl(e, k_block_rank, (unsigned)segs, kRankWarps * 32, 0, labels, (long)r0, (long)m,
+               (uint32_t)k, segcnt, rank, e->d_status);
+    EB_LAUNCH("scatter rank");
+  } else if (m > 0) {
     const int warps = 8;
-    if (smem_rank)
-      launch_pdl(e, k_seg_rank<true>, blocks_for(segs, warps), warps * 32, 0, labels, (long)r0, (long)m, (uint32_t)k, segcnt, rank, e->d_status);
-    else
-      launch_pdl(e, k_seg_rank<false>, blocks_for(segs, warps), warps * 32, 0, labels, (long)r0, (long)m, (uint32_t)k, segcnt, rank, e->d_status);
+    launch_pdl(e, k_seg_rank, blocks_for(segs, warps), warps * 32, 0, labels, (long)r0, (long)m,
+               (uint32_t)k, segcnt, rank, e->d_status);
     EB_LAUNCH("scatter rank");
   }
-  launch_pdl(e, k_seg_scan, blocks_for(k * 32, 256), 256, 0, segcnt, (long)segs, (uint32_t)k, counts);
+  launch_pdl(e, k_seg_scan, blocks_for(k * 32, kScanThreads), kScanThreads, 0, segcnt,
+             (long)segs, (uint32_t)k, counts, start, by_size, ticket);
   EB_LAUNCH("scatter seg scan");
-  launch_pdl(e, k_label_scan, 1, 1024, 0, counts, (uint32_t)k, start, by_size);
-  EB_LAUNCH("scatter label scan");
   if (m > 0) {
     launch_pdl(e, k_place, blocks_for(m, 256), 256, 0, labels, ids, (long)r0, (long)m, (long)n,
-                                                       (uint32_t)k, segcnt, start, rank, order,
-                                                       e->d_status);
+               (uint32_t)k, (int)seg_len, segcnt, start, rank, order, e->d_status);
     EB_LAUNCH("scatter place");
   }
   *order_out = order;

@@ -14,10 +14,15 @@ from tests.helpers import bits, mixture
 
 pytestmark = pytest.mark.gpu
 
-# The last two average hundreds of rows a centroid (the staged sum's full-pass
-# shape; the others take its training-batch shape).
+# (20000, 96, 32) and (12000, 768, 40) average hundreds of rows a centroid
+# (the staged sum's full-pass shape; the others take its training-batch
+# shape). With k <= 1024 the label order ranks 2,048-position blocks
+# ((9000, 40, 700): several blocks and a ragged last one); (5000, 24, 1500)
+# and (3000, 8, 2048) take the larger-k order (256-position warp segments
+# counted in global memory).
 SHAPES = [(1000, 768, 64), (777, 768, 100), (513, 13, 70), (2000, 20, 300), (300, 64, 1),
-          (600, 768, 1024), (20000, 96, 32), (12000, 768, 40)]
+          (600, 768, 1024), (20000, 96, 32), (12000, 768, 40), (9000, 40, 700),
+          (5000, 24, 1500), (3000, 8, 2048)]
 
 
 @pytest.mark.parametrize("n,d,k", SHAPES)
