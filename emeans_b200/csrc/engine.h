@@ -70,7 +70,8 @@ struct eb_buf {
   // Bumped by every host write; caches derived from the buffer compare it.
   uint64_t version = 0;
   // For bound data sets: d, the rows' squared norms (CPU float order) and the
-  // screen copies (split FP16 for top-k and products, fixed point for top-1).
+  // screen copies (split FP16 for the internal scores' products, fixed point
+  // for top-1).
   size_t d = 0;
   float* xnorm = nullptr;
   eb::Fp16Copy* f16 = nullptr;

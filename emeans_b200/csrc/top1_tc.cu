@@ -1,7 +1,9 @@
 // Exact top-1 on the tensor cores: a tcgen05 screen on 16-bit fixed-point
 // operands held as two int8 digits, then the exact FP32 chain for the few
-// centroids the screen cannot rule out. Top-k and the internal scores'
-// product use the same kernel on split FP16 operands.
+// centroids the screen cannot rule out. Top-k uses the same kernel and
+// digits (k_screen<true, true>: the best kk screened values per row and the
+// window below the kk-th); the internal scores' product uses it on split
+// FP16 operands.
 //
 // The labels and scores are the reference CPU kernel's bit for bit
 // (crates/emeans-core/src/assign/fused.rs:12-16: one sequential FMA chain per
@@ -37,7 +39,7 @@
 // 2^-22 (|x'| + 160 sqrt(d)) (|c'| + 160 sqrt(d)); and the FP32 chain,
 // gamma_d |x'| |c'| (screen_bound_q8 derives each term).
 //
-// Split FP16 (top-k, products): values scaled by powers of two so that
+// Split FP16 (the internal scores' products): values scaled by powers of two so that
 // |v| < 2^14 and split into two FP16 terms, v' = hi + lo + r with
 // |r| <= 2^-22 |v'| + 2^-24; its error bound in accumulator units (u = 2^-11):
 //   split operands:   3 2^-22 sum|x'||c'| + 2^-23 (sum|x'| + sum|c'|)
@@ -47,10 +49,10 @@
 //   the FP32 chain:   gamma_d sum|x c| from the exact dot
 // with sum|x'||c'| <= |x'| |c'| and sum|x'| <= sqrt(d) |x'| (Cauchy-Schwarz).
 //
-// Top-k mode (k_screen<true, true>) gives each tile one accumulator that takes
-// all three products and alternates two accumulator buffers, so that the MMAs
-// of the next tile overlap the scoring of this one; its accumulation term
-// counts 3d additions (3 d 2^-21) and has no lo accumulator term.
+// Top-k mode holds the tile in TMEM while it scores: the best-kk state takes
+// the registers that top-1 spends on the drained tile. It votes on each
+// 16-column group first and scores in full only the groups that some row's
+// window reaches, then releases the accumulators.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -820,16 +822,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 1;
   uint64_t* mma_done = tempty + 1;
-  // Top-k mode: the second accumulator buffer's pair.
-  uint64_t* tfull1 = mma_done + 1;
-  uint64_t* tempty1 = tfull1 + 1;
-  uint64_t* dead = tempty1 + 1;  // never arrived at (the dead_wait test)
+  uint64_t* dead = mma_done + 1;  // never arrived at (the dead_wait test)
   uint32_t* tmem_slot = (uint32_t*)(dead + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   float* cn_s = (float*)(smem + STAGES * STAGE_BYTES + 256);  // [8 warps][HALF]
   float* sv_s = cn_s + 8 * HALF;                               // [8 warps][16][32]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Top-k runs on the fixed-point digits only (the split FP16 operands serve
+  // the product mode).
+  static_assert(!TOPK || Q8, "top-k mode reads fixed-point digits");
 
   if (threadIdx.x == 0) {
     if (blockIdx.x == 0) {
@@ -843,8 +845,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(tfull, 1);
     mbar_init(tempty, 256);
     mbar_init(mma_done, 1);
-    mbar_init(tfull1, 1);
-    mbar_init(tempty1, 256);
     mbar_init(dead, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -904,12 +904,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int u = blockIdx.x; u < P.units && !stop; u += gridDim.x) {
         const int nt0 = (u % P.parts) * P.tpp, nt1 = min(nt0 + P.tpp, P.ntiles);
         for (int nt = nt0; nt < nt1; nt++, tc++) {
-          // Top-1 mode: the epilogue must have read both accumulators of the
-          // last tile. Top-k mode: one accumulator per tile, two buffers in
-          // turn; the epilogue must have read this buffer's last tile.
-          const int buf = TOPK ? (tc & 1) : 0;
-          const uint32_t use = TOPK ? (uint32_t)(tc >> 1) : (uint32_t)tc;
-          if (!mbar_wait(buf ? tempty1 : tempty, (use & 1) ^ 1, abort_flag)) {
+          // The epilogue must have read both accumulators of the last tile.
+          if (!mbar_wait(tempty, (tc & 1) ^ 1, abort_flag)) {
             stop = true;
             break;
           }
@@ -927,13 +923,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int kk = 0; kk < BKH / 16; kk++) {
               const uint32_t first = (kb > 0 || kk > 0) ? 1u : 0u;
-              if constexpr (TOPK) {
-                // All three products into the buffer's one accumulator.
-                const uint32_t dacc = tmem + (uint32_t)(buf * BN);
-                umma_f16(dacc, umma_desc(ah + kk * 32), umma_desc(bh + kk * 32), first);
-                umma_f16(dacc, umma_desc(ah + kk * 32), umma_desc(bl + kk * 32), 1u);
-                umma_f16(dacc, umma_desc(al + kk * 32), umma_desc(bh + kk * 32), 1u);
-              } else if constexpr (Q8) {
+              if constexpr (Q8) {
                 // 32 int8 columns per MMA: hi.hi, and hi.lo + lo.hi (exact int32 sums).
                 umma_i8(tmem, umma_desc(ah + kk * 32), umma_desc(bh + kk * 32), first);
                 umma_i8(tmem + BN, umma_desc(ah + kk * 32), umma_desc(bl + kk * 32), first);
@@ -950,7 +940,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             stop = true;
             break;
           }
-          umma_commit(buf ? tfull1 : tfull);
+          umma_commit(tfull);
         }
       }
       // Every MMA this thread issued has completed once mma_done flips.
@@ -1057,10 +1047,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
       for (int nt = nt0; nt < nt1; nt++, tc++) {
         // Warp-uniform: the TMEM loads below are .sync.aligned.
-        const int buf = TOPK ? (tc & 1) : 0;
-        const uint32_t use = TOPK ? (uint32_t)(tc >> 1) : (uint32_t)tc;
-        uint64_t* wbar = buf ? tfull1 : tfull;
-        uint32_t wpar = use & 1;
+        uint64_t* wbar = tfull;
+        uint32_t wpar = tc & 1;
         const int col0 = nt * BN + hf * HALF;  // first centroid of this warp's half tile
         // This half tile's squared centroid norms (product mode: the columns'
         // weights), loaded before the wait for the accumulators so that their
@@ -1130,14 +1118,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int u = 0; u < HALF / 32; u++) cns[u * 32 + lane] = cnv[u];
           __syncwarp();
         }
-        // Top-k mode scores each group straight from TMEM in a rolled loop
-        // (its group code is long: unrolled eight times it no longer fits the
-        // instruction cache) and frees TMEM after the tile; top-1 mode scores
-        // the drained registers in an unrolled loop.
-        // The scoring of group g of this half tile (its 16 values in acc[g],
-        // or acc[0] in top-k mode).
-        auto score_group = [&](const int g) {
-          const uint32_t(&h)[16] = acc[TOPK ? 0 : g];
+        // Top-k mode scores the groups its vote selects straight from TMEM
+        // in a rolled loop (its group code is long: unrolled eight times it
+        // no longer fits the instruction cache) and frees TMEM after the
+        // tile; top-1 mode scores the drained registers in an unrolled loop.
+        // The scoring of group g of this half tile, its 16 values in h.
+        auto score_group = [&](const uint32_t(&h)[16], const int g) {
           if constexpr (PROD) {
             // The largest weighted product of the columns other than the own.
             const long cb = col0 + g * 16;
@@ -1153,9 +1139,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           float s[16];
           if constexpr (TOPK) {
-            // Inner product: the accumulator is the screened value.
+            // Inner product: the accumulator is the screened value (fixed
+            // point: an integer in units of 65536, converted here).
 #pragma unroll
-            for (int j = 0; j < 16; j++) s[j] = __uint_as_float(h[j]);
+            for (int j = 0; j < 16; j++)
+              s[j] = Q8 ? __int2float_rn((int)h[j]) : __uint_as_float(h[j]);
           } else {
             const float4* c4 = reinterpret_cast<const float4*>(cns + g * 16);
 #pragma unroll
@@ -1272,22 +1260,52 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         };
         if constexpr (TOPK) {
-          // One accumulator per tile (all three products), in buffer buf.
-#pragma unroll 1
+          // Fixed-point top-k: the groups are voted on first, one at a time
+          // straight from TMEM (each group's largest value hi + floor(lo /
+          // 256), an integer maximum and one conversion, against the row's
+          // threshold as the tile began; thresholds only rise, so a group no
+          // lane votes for would be skipped by the full scoring as well).
+          // Only the groups some lane wants are scored in full, each read
+          // again from TMEM in a rolled loop, and TMEM is released after
+          // them (the best-kk state leaves no room to hold the tile in
+          // registers).
+          uint32_t need = 0;
+#pragma unroll
           for (int g = 0; g < HALF / 16; g++) {
-            if (g >= ngr) break;
-            tmem_ld16(lane_base + (uint32_t)(buf * BN + g * 16), acc[0]);
+            if (g < ngr) {
+              uint32_t h[16], l[16];
+              tmem_ld16(lane_base + (uint32_t)(g * 16), h);
+              tmem_ld16(lane_base + (uint32_t)(BN + g * 16), l);
+              tmem_wait();
+              tmem_tie(h);
+              tmem_tie(l);
+              int mx = (int)h[0] + ((int)l[0] >> 8);
+#pragma unroll
+              for (int j = 1; j < 16; j++) mx = max(mx, (int)h[j] + ((int)l[j] >> 8));
+              need |= (uint32_t)__any_sync(0xFFFFFFFFu, collect && __int2float_rn(mx) >= thr) << g;
+            }
+          }
+#pragma unroll 1
+          while (need) {
+            const int g = __ffs(need) - 1;
+            need &= need - 1;
+            uint32_t h[16], l[16];
+            tmem_ld16(lane_base + (uint32_t)(g * 16), h);
+            tmem_ld16(lane_base + (uint32_t)(BN + g * 16), l);
             tmem_wait();
-            tmem_tie(acc[0]);
-            score_group(g);
+            tmem_tie(h);
+            tmem_tie(l);
+#pragma unroll
+            for (int j = 0; j < 16; j++) h[j] = (uint32_t)((int)h[j] + ((int)l[j] >> 8));
+            score_group(h, g);
           }
           tc_fence_before();
-          mbar_arrive(buf ? tempty1 : tempty);
+          mbar_arrive(tempty);
         } else {
 #pragma unroll
           for (int g = 0; g < HALF / 16; g++) {
             if (g >= ngr) break;
-            score_group(g);
+            score_group(acc[g], g);
           }
         }
       }
@@ -2269,20 +2287,17 @@ void launch_exact(eb_engine* e, const Top1Args& a, long c0, long m, const ExactS
 
 namespace {
 
-// The bound coefficients of the header comment for this d, with 1% slack.
-// With one accumulator (top-k mode) all 3d products are added into it, so
-// the accumulation term counts 3d additions and the lo accumulator's term
-// falls away.
-void screen_bound(size_t d, float& e_rel, float& e_abs, float& e_min, bool one_acc = false) {
+// The split FP16 bound coefficients of the header comment for this d, with
+// 1% slack.
+void screen_bound(size_t d, float& e_rel, float& e_abs, float& e_min) {
   const double dd = (double)d;
-  const double adds = one_acc ? 3.0 * dd : dd;
   const double u24 = std::ldexp(1.0, -24);
   const double gamma_d = dd * u24 / (1.0 - dd * u24);
-  e_rel = (float)((3.0 * std::ldexp(1.0, -22) + adds * std::ldexp(1.0, -21) * (1.0 + std::ldexp(1.0, -9)) +
-                   (one_acc ? 0.0 : dd * std::ldexp(1.0, -30)) + std::ldexp(1.0, -23) + gamma_d) *
+  e_rel = (float)((3.0 * std::ldexp(1.0, -22) + dd * std::ldexp(1.0, -21) * (1.0 + std::ldexp(1.0, -9)) +
+                   dd * std::ldexp(1.0, -30) + std::ldexp(1.0, -23) + gamma_d) *
                   1.01);
   e_abs = (float)(std::ldexp(1.0, -23) * std::sqrt(dd) * 1.01);
-  e_min = (float)(adds * std::ldexp(1.0, -48));
+  e_min = (float)(dd * std::ldexp(1.0, -48));
 }
 
 
@@ -2627,25 +2642,28 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
                  size_t kk, bool exclude_self, uint32_t* ids, float* sims, size_t id0) {
   if (e->screen_mode == 0 || d > 16384 || n > 0x7FFFFFFFull || kk > (size_t)KMAX) return false;
   if (e->screen_mode == 1 && (n < 256 || m < 128 || d < 16)) return false;
-  const size_t dp = (d + BKH - 1) / BKH * BKH;
+  const size_t dp = (d + BK8 - 1) / BK8 * BK8;  // bytes of a fixed-point row
   const size_t wave = (size_t)e->num_sms * BM;
   const size_t chunk = std::min(m, PASS_WAVES * wave);
-  float e_rel, e_abs, e_min;
-  screen_bound(d, e_rel, e_abs, e_min, true);
+  float e_rel, e_abs, e_min, e_lo;
+  screen_bound_q8(d, e_rel, e_abs, e_min, e_lo);
 
-  // The data rows play the centroids: one exponent, split FP16 copy.
+  // The data rows play the centroids: one scale, fixed-point copy (the two
+  // int8 digits of each value, as in the top-1 screen).
   unsigned long long* cinfo = e->scratch_get<unsigned long long>("tc_cinfo", 4, true);
-  __half* ch = e->scratch_get<__half>("tc_ch", n * dp);
-  __half* cl = e->scratch_get<__half>("tc_cl", n * dp);
-  const uint32_t cgen = convert_centroids(e, data, n, d, dp, cinfo, ch, cl);
-  const CUtensorMap mapBh = make_map(ch, n, dp, BN);
-  const CUtensorMap mapBl = make_map(cl, n, dp, BN);
+  int8_t* ch = e->scratch_get<int8_t>("tc_ch8", n * dp);
+  int8_t* cl = e->scratch_get<int8_t>("tc_cl8", n * dp);
+  const uint32_t cgen = next_gen(e, cinfo);
+  convert_with_q8(e, data, n, d, dp, cinfo, cgen, true, ch, cl);
+  const CUtensorMap mapBh = make_map_q8(ch, n, dp, BN);
+  const CUtensorMap mapBl = make_map_q8(cl, n, dp, BN);
 
   const unsigned wpb = 8;
-  __half* xh = e->scratch_get<__half>("tc_xh", chunk * dp);
-  __half* xl = e->scratch_get<__half>("tc_xl", chunk * dp);
-  int* xexp = e->scratch_get<int>("tc_xexp", chunk);
+  int8_t* xh = e->scratch_get<int8_t>("tc_xh8", chunk * dp);
+  int8_t* xl = e->scratch_get<int8_t>("tc_xl8", chunk * dp);
+  float* xscl = e->scratch_get<float>("tc_xscl", chunk);
   float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
+  float* xlo = e->scratch_get<float>("tc_xlo", chunk);
   uint2* cand = e->scratch_get<uint2>("tc_cand", 2 * chunk * CAP_TOPK);
   uint32_t* cand_cnt = e->scratch_get<uint32_t>("tc_cnt", 2 * chunk);
   float* cand_thr = e->scratch_get<float>("tc_thr", 2 * chunk);
@@ -2663,7 +2681,7 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
 
   ScreenParams P{};
   P.k = (int)n;
-  P.kblocks = (int)(dp / BKH);
+  P.kblocks = (int)(dp / BK8);
   P.ntiles = (int)((n + BN - 1) / BN);
   P.parts = 1;  // the top-k collect merges the two halves' best-kk lists
   P.tpp = P.ntiles;
@@ -2673,6 +2691,7 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
   P.e_rel = e_rel;
   P.e_abs = e_abs;
   P.e_min = e_min;
+  P.e_lo = e_lo;
   P.cand = cand;
   P.cand_cnt = cand_cnt;
   P.cand_thr = cand_thr;
@@ -2687,18 +2706,20 @@ bool topk_screen(eb_engine* e, const float* q, size_t m, const float* data, size
 
   for (size_t c0 = 0; c0 < m; c0 += chunk) {
     const size_t mc = std::min(chunk, m - c0);
-    launch_pdl(e, k_prep_rows, (unsigned)((mc + wpb - 1) / wpb), wpb * 32, 0, q, (long)m, (int)d, (int)dp, nullptr, (long)c0, (long)mc, xh, xl, xexp, xnrm,
-        e->d_status);
+    launch_pdl(e, k_prep_rows_q8, (unsigned)((mc + wpb - 1) / wpb), wpb * 32, 0, q, (long)m,
+               (int)d, (int)dp, nullptr, (long)c0, (long)mc, xh, xl, xscl, xnrm, xlo,
+               e->d_status);
     EB_LAUNCH("topk query prep");
-    const CUtensorMap mapAh = make_map(xh, mc, dp, BM);
-    const CUtensorMap mapAl = make_map(xl, mc, dp, BM);
+    const CUtensorMap mapAh = make_map_q8(xh, mc, dp, BM);
+    const CUtensorMap mapAl = make_map_q8(xl, mc, dp, BM);
     P.m = (long)mc;
     P.units = (int)((mc + BM - 1) / BM);
-    P.xexp = xexp;
+    P.xscl = xscl;
     P.xnrm = xnrm;
+    P.xlo = xlo;
     P.row_gid0 = (long)c0;
     const unsigned grid = (unsigned)std::min<size_t>((mc + BM - 1) / BM, (size_t)e->num_sms);
-    launch_screen<true, true>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
+    launch_screen<true, true, false, true>(e, grid, mapAh, mapAl, mapBh, mapBl, P);
     EB_LAUNCH("topk screen");
     const unsigned rgrid = (unsigned)((mc + 255) / 256);
     launch_pdl(e, k_collect_topk, rgrid, 256, 0, (long)c0, (long)mc, (uint32_t)n, (int)kk, cand,
