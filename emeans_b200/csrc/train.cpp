@@ -282,16 +282,23 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
       // In a group, rank q scores positions [b + q s, b + (q + 1) s) of the
       // batch and the slices are all-gathered; alone, the whole batch. By
       // default (group_shard 0) a batch is split only when that shortens
-      // the screen (its length in centroid-tile times, the slice's row tiles
-      // spread over the SMs with their centroid tiles in parts); otherwise
-      // every rank scores all of it and nothing is exchanged (the same
-      // result either way).
+      // the screen by more than the exchange costs: the screen's length in
+      // centroid-tile times (the slice's row tiles spread over the SMs with
+      // their centroid tiles in parts), a tile time about 0.52 µs per 64
+      // columns of d (72 int8 MMAs at d = 768 take 6.2 µs), against about
+      // 40 µs for the exchange (pack, all-gather, unpack, and the launch
+      // chain broken around the collective; measured on two B200s, a C2
+      // step with its batch split took longer than one GPU's whole step).
+      // Otherwise every rank scores all of it and nothing is exchanged (the
+      // same result either way).
       const size_t sh = (end - b + e->world - 1) / e->world;
+      const double tile_us = 0.52 * (double)((d + 63) / 64);
+      const double saved_us =
+          tile_us * ((double)screen_tile_times(end - b, k, e->num_sms) -
+                     (double)screen_tile_times(sh, k, e->num_sms));
       const bool split_batch =
           e->world > 1 &&
-          (reduce_mode || e->group_shard == 1 ||
-           (e->group_shard == 0 &&
-            screen_tile_times(sh, k, e->num_sms) < screen_tile_times(end - b, k, e->num_sms)));
+          (reduce_mode || e->group_shard == 1 || (e->group_shard == 0 && saved_us > 40.0));
       const size_t lo = split_batch ? std::min(b + (size_t)e->rank * sh, end) : b;
       const size_t hi = split_batch ? std::min(lo + sh, end) : end;
       for (size_t c0 = lo; c0 < hi; c0 += chunk) {

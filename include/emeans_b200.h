@@ -266,11 +266,13 @@ int eb_engine_join(eb_engine* e, int rank, int world, const unsigned char* id);
 int eb_engine_group(eb_engine* e, int* rank, int* world);
 /* No counterpart in the reference. How eb_train on a joined engine divides a
  * batch (the data-parallel step of core/train.rs:60-303 over several GPUs):
- *  0 (default) splits its top-1 across the ranks only when that cuts the
- *    screen's waves of 128-row tiles (a batch of one wave or less is scored
- *    whole by every rank, with no exchange); 1 always splits it; 2 never
- *    does. Modes 0-2 exchange (label, score) slices and give the model of one
- *    engine alone, bit for bit.
+ *  0 (default) splits its top-1 across the ranks only when the screen time
+ *    that saves (its length in 128-row x 256-centroid tile times, about
+ *    0.52 us per 64 columns of d each) exceeds about 40 us, the cost of the
+ *    exchange; otherwise every rank scores the batch whole, with no
+ *    exchange (a C2 batch, 16,384 rows with k = 1024, is not split). 1
+ *    always splits it; 2 never does. Modes 0-2 give the model of one engine
+ *    alone, bit for bit.
  *  3 splits the top-1 and the scatter-add: each rank sums its slice's rows
  *    into partial k x d sums and k counts, one all-gather per step carries
  *    every rank's slice results and partials, and every rank adds the
