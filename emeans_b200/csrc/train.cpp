@@ -220,6 +220,24 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   const size_t share = reduce_mode ? 2 * s4 + k4 + k * d : 2 * sh_max;
   DevBuf stage(e, EB_U32, e->world > 1 ? share * e->world : 1);
   start.get();
+  // The caller's result buffers are touched page by page on a helper thread
+  // while the device trains (a read and a write back of one byte a page, so
+  // the contents are unchanged even where a buffer aliases an input): memory
+  // the caller has just allocated takes its first-touch page faults here,
+  // not in the copies of the results after the last step (about 1.4 ms for
+  // a C2 run's 3 MB centroids, 3 MB positions and 800 KB labels).
+  std::future<void> prefault = std::async(std::launch::async, [out, k, d, n] {
+    auto touch = [](void* p, size_t bytes) {
+      if (!p || !bytes) return;
+      volatile unsigned char* c = static_cast<volatile unsigned char*>(p);
+      for (size_t o = 0; o < bytes; o += 4096) c[o] = c[o];
+      c[bytes - 1] = c[bytes - 1];
+    };
+    touch(out->centroids, k * d * 4);
+    touch(out->positions, k * d * 4);
+    touch(out->usage, k * 4);
+    touch(out->labels, n * 4);
+  });
   EB_CUDA(cudaMemcpyAsync(dpos.f(), pos, k * d * 4, cudaMemcpyHostToDevice, e->stream));
   EB_CUDA(cudaMemcpyAsync(mass.f(), usage, k * 4, cudaMemcpyHostToDevice, e->stream));
   if (data->d == d && !data->xnorm && !spherical) {
@@ -237,11 +255,29 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
   std::unique_ptr<host::RevivalDraws> draws;
   bool draws_due = tau > 0.0;
   size_t n_splits = 0, step = 0;
-  // Pinned read-backs: two (labels, scores) sets, so that an epoch's copy
-  // never overwrites the set whose statistics are still being computed, and
-  // the masses and revival plan.
-  uint32_t* h_lab[2] = {e->pinned_get<uint32_t>("tr_lab0", n), e->pinned_get<uint32_t>("tr_lab1", n)};
-  float* h_sc[2] = {e->pinned_get<float>("tr_sc0", n), e->pinned_get<float>("tr_sc1", n)};
+  // Pinned read-backs of each epoch's labels and scores: a set of its own
+  // for every epoch of runs up to 8 epochs (C2: 5 sets of 1.6 MB), else two
+  // sets in turn, an epoch's copy waiting for the statistics of the epoch
+  // that last read its set. Measured on C2: copies into a set the host had
+  // just read (the statistics two epochs back) ran at about 4.4 GB/s instead
+  // of 44, and the last epoch's held up the copy of the results behind them.
+  // Then the masses and revival plan.
+  const size_t nsets = n_epochs <= 8 ? n_epochs : 2;
+  std::vector<uint32_t*> h_lab(nsets);
+  std::vector<float*> h_sc(nsets);
+  for (size_t q = 0; q < nsets; q++) {
+    h_lab[q] = e->pinned_get<uint32_t>(("tr_lab" + std::to_string(q)).c_str(), n);
+    h_sc[q] = e->pinned_get<float>(("tr_sc" + std::to_string(q)).c_str(), n);
+  }
+  // One "copies landed" event per set.
+  struct SetEvents {
+    std::vector<cudaEvent_t> ev;
+    ~SetEvents() {
+      for (cudaEvent_t v : ev)
+        if (v) cudaEventDestroy(v);
+    }
+  } landed{std::vector<cudaEvent_t>(nsets, nullptr)};
+  for (auto& v : landed.ev) EB_CUDA(cudaEventCreateWithFlags(&v, cudaEventDisableTiming));
   float* mass_h = e->pinned_get<float>("tr_mass", k);
   float* h_cent = e->pinned_get<float>("tr_cent", k * d);
   uint32_t* plan_h = e->pinned_get<uint32_t>("tr_plan", 2 * k);
@@ -382,16 +418,18 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
     // Epoch end: labels and scores come down on `down` while the next epoch
     // runs; a helper thread computes the statistics once they have landed.
     EB_CUDA(cudaEventRecord(done.ev[4 + par], e->stream));
-    if (epoch >= 2) stats[epoch - 2].get();  // the set it read is reused now
+    const size_t set = epoch % nsets;
+    if (epoch >= nsets) stats[epoch - nsets].get();  // the set it read is reused now
     EB_CUDA(cudaStreamWaitEvent(cs.down, done.ev[4 + par], 0));
-    EB_CUDA(cudaMemcpyAsync(h_lab[par], labels_ep, rows * 4, cudaMemcpyDeviceToHost, cs.down));
-    EB_CUDA(cudaMemcpyAsync(h_sc[par], scores_ep, rows * 4, cudaMemcpyDeviceToHost, cs.down));
-    EB_CUDA(cudaEventRecord(done.ev[par], cs.down));
+    EB_CUDA(cudaMemcpyAsync(h_lab[set], labels_ep, rows * 4, cudaMemcpyDeviceToHost, cs.down));
+    EB_CUDA(cudaMemcpyAsync(h_sc[set], scores_ep, rows * 4, cudaMemcpyDeviceToHost, cs.down));
+    EB_CUDA(cudaEventRecord(landed.ev[set], cs.down));
     out->nsplit[epoch] = (int64_t)(n_splits - splits_before);
-    const cudaEvent_t ev = done.ev[par];
-    const uint32_t* hl = h_lab[par];
-    const float* hs = h_sc[par];
+    const cudaEvent_t ev = landed.ev[set];
+    const uint32_t* hl = h_lab[set];
+    const float* hs = h_sc[set];
     const bool verbose = job->verbose != 0;
+    if (last) prefault.get();  // the last epoch's statistics write the labels
     stats[epoch] = std::async(std::launch::async, [=]() {
       EB_CUDA(cudaSetDevice(dev));
       EB_CUDA(cudaEventSynchronize(ev));
@@ -403,8 +441,20 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
       if (verbose)
         fprintf(stderr, "  Epoch %zu / %zu (%zu rows), iteration %zu (%.2f s): objective=%.17g\n",
                 epoch + 1, n_epochs, rows, step, out->epoch_time[epoch], st.obj);
-      if (last && out->labels)
-        for (size_t i = 0; i < rows; i++) out->labels[ord[i]] = (int32_t)hl[i];
+      if (last && out->labels) {
+        // The captured assignments in row order, in four slices at once
+        // (ord is a permutation: the slices write disjoint entries).
+        const size_t q4 = (rows + 3) / 4;
+        auto place = [&](size_t a, size_t b) {
+          for (size_t i = a; i < b; i++) out->labels[ord[i]] = (int32_t)hl[i];
+        };
+        std::future<void> parts[3];
+        for (int q = 1; q < 4; q++)
+          parts[q - 1] = std::async(std::launch::async, place, std::min(rows, q * q4),
+                                    std::min(rows, (q + 1) * q4));
+        place(0, std::min(rows, q4));
+        for (auto& f : parts) f.get();
+      }
     });
     if (last) {
       // Closing means (core/mod.rs:404-429) on the device: the closing pass's
@@ -420,16 +470,27 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
     }
   }
   // Results through pinned staging (a DMA at full speed), then into the
-  // caller's buffers on two threads.
+  // caller's buffers on four threads (each buffer in two halves).
   EB_CUDA(cudaMemcpyAsync(pos, dpos.f(), k * d * 4, cudaMemcpyDeviceToHost, e->stream));
   EB_CUDA(cudaMemcpyAsync(mass_h, mass.f(), k * 4, cudaMemcpyDeviceToHost, e->stream));
   sync(e);
   {
-    auto cp = std::async(std::launch::async,
-                         [&] { std::memcpy(out->centroids, h_cent, k * d * 4); });
-    if (out->positions) std::memcpy(out->positions, pos, k * d * 4);
+    const size_t half = k * d / 2;
+    auto copy = [](float* dst, const float* src, size_t count) {
+      std::memcpy(dst, src, count * 4);
+    };
+    auto c0 = std::async(std::launch::async, copy, out->centroids, h_cent, half);
+    auto c1 = std::async(std::launch::async, copy, out->centroids + half, h_cent + half,
+                         k * d - half);
+    std::future<void> p1;
+    if (out->positions) {
+      p1 = std::async(std::launch::async, copy, out->positions + half, pos + half, k * d - half);
+      copy(out->positions, pos, half);
+    }
     if (out->usage) std::memcpy(out->usage, mass_h, k * 4);
-    cp.get();
+    c0.get();
+    c1.get();
+    if (p1.valid()) p1.get();
   }
   for (auto& f : stats)
     if (f.valid()) f.get();
