@@ -48,32 +48,57 @@ struct EpochStat {
 };
 
 // Epoch statistics (train.rs:224-279): f64 objective per chunk, imbalance.
+// With threads > 1 the batches are split into contiguous ranges summed at
+// once, each batch's sum still in its own sequential order, and the batch
+// sums are then added in batch order: the same bits as one thread. The
+// label counts are integers (any order).
 EpochStat epoch_stats(const uint32_t* lab, const float* sc, size_t rows, size_t bsz, size_t chunk,
-                      size_t k, bool spherical) {
-  double obj_epoch = 0.0;
-  for (size_t b = 0; b < rows; b += bsz) {
-    size_t e = std::min(b + bsz, rows);
-    double obj_batch = 0.0;
-    for (size_t c0 = b; c0 < e; c0 += chunk) {
-      size_t c1 = std::min(c0 + chunk, e);
-      double obj = 0.0;
-      if (spherical) {
-        obj += 2.0 * (double)(c1 - c0);
-        for (size_t i = c0; i < c1; i++) obj += (double)(-2.0f * sc[i]);
-      } else {
-        for (size_t i = c0; i < c1; i++) obj += (double)sc[i];
+                      size_t k, bool spherical, int threads = 1) {
+  const size_t nb = (rows + bsz - 1) / bsz;
+  std::vector<double> batch_obj(nb, 0.0);
+  std::vector<std::vector<uint64_t>> hists(std::max(threads, 1), std::vector<uint64_t>(k, 0));
+  auto part = [&](int q) {
+    const size_t b0 = nb * (size_t)q / (size_t)threads, b1 = nb * (size_t)(q + 1) / (size_t)threads;
+    for (size_t bi = b0; bi < b1; bi++) {
+      const size_t b = bi * bsz, e = std::min(b + bsz, rows);
+      double obj_batch = 0.0;
+      for (size_t c0 = b; c0 < e; c0 += chunk) {
+        size_t c1 = std::min(c0 + chunk, e);
+        double obj = 0.0;
+        if (spherical) {
+          obj += 2.0 * (double)(c1 - c0);
+          for (size_t i = c0; i < c1; i++) obj += (double)(-2.0f * sc[i]);
+        } else {
+          for (size_t i = c0; i < c1; i++) obj += (double)sc[i];
+        }
+        obj_batch += obj;
       }
-      obj_batch += obj;
+      batch_obj[bi] = obj_batch;
     }
-    obj_epoch += obj_batch;
+    std::vector<uint64_t>& hist = hists[q];
+    const size_t r0 = std::min(rows, b0 * bsz), r1 = std::min(rows, b1 * bsz);
+    for (size_t i = r0; i < r1; i++) {
+      ensure(lab[i] < k, "device returned a label >= k");
+      hist[lab[i]]++;
+    }
+  };
+  if (threads <= 1) {
+    threads = 1;
+    part(0);
+  } else {
+    std::vector<std::future<void>> fs;
+    for (int q = 1; q < threads; q++) fs.push_back(std::async(std::launch::async, part, q));
+    part(0);
+    for (auto& f : fs) f.get();
   }
-  std::vector<uint64_t> hist(k, 0);
-  for (size_t i = 0; i < rows; i++) {
-    ensure(lab[i] < k, "device returned a label >= k");
-    hist[lab[i]]++;
-  }
+  double obj_epoch = 0.0;
+  for (size_t bi = 0; bi < nb; bi++) obj_epoch += batch_obj[bi];
   double sq = 0.0;
-  for (size_t j = 0; j < k; j++) sq += (double)hist[j] * (double)hist[j];
+  for (size_t j = 0; j < k; j++) {
+    uint64_t c = 0;
+    for (int q = 0; q < threads; q++) c += hists[q][j];
+    sq += (double)c * (double)c;
+  }
   return {obj_epoch, (double)k * sq / ((double)rows * (double)rows)};
 }
 
@@ -433,7 +458,21 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
     stats[epoch] = std::async(std::launch::async, [=]() {
       EB_CUDA(cudaSetDevice(dev));
       EB_CUDA(cudaEventSynchronize(ev));
-      const EpochStat st = epoch_stats(hl, hs, rows, bsz, chunk, k, spherical);
+      // The last epoch's statistics and its labels put in row order are the
+      // end of the call: both run on several threads, at once. The other
+      // epochs' statistics run on one thread while the device works.
+      std::future<void> parts[2];
+      if (last && out->labels) {
+        // The captured assignments in row order, in two slices (ord is a
+        // permutation: the slices write disjoint entries).
+        const size_t h2 = rows / 2;
+        auto place = [out, ord, hl](size_t a, size_t b) {
+          for (size_t i = a; i < b; i++) out->labels[ord[i]] = (int32_t)hl[i];
+        };
+        parts[0] = std::async(std::launch::async, place, (size_t)0, h2);
+        parts[1] = std::async(std::launch::async, place, h2, rows);
+      }
+      const EpochStat st = epoch_stats(hl, hs, rows, bsz, chunk, k, spherical, last ? 4 : 1);
       out->obj[epoch] = st.obj;
       out->imbalance[epoch] = st.imbalance;
       out->epoch_time[epoch] =
@@ -441,20 +480,8 @@ void train(eb_engine* e, const eb_train_job* job, eb_train_out* out) {
       if (verbose)
         fprintf(stderr, "  Epoch %zu / %zu (%zu rows), iteration %zu (%.2f s): objective=%.17g\n",
                 epoch + 1, n_epochs, rows, step, out->epoch_time[epoch], st.obj);
-      if (last && out->labels) {
-        // The captured assignments in row order, in four slices at once
-        // (ord is a permutation: the slices write disjoint entries).
-        const size_t q4 = (rows + 3) / 4;
-        auto place = [&](size_t a, size_t b) {
-          for (size_t i = a; i < b; i++) out->labels[ord[i]] = (int32_t)hl[i];
-        };
-        std::future<void> parts[3];
-        for (int q = 1; q < 4; q++)
-          parts[q - 1] = std::async(std::launch::async, place, std::min(rows, q * q4),
-                                    std::min(rows, (q + 1) * q4));
-        place(0, std::min(rows, q4));
-        for (auto& f : parts) f.get();
-      }
+      for (auto& f : parts)
+        if (f.valid()) f.get();
     });
     if (last) {
       // Closing means (core/mod.rs:404-429) on the device: the closing pass's

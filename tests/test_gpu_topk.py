@@ -96,3 +96,30 @@ def test_self_join_config_shape(engine):
     wi, ws = oracle.topk(x, x, d, kk, exclude_self=True)
     assert np.array_equal(gi, wi) and np.array_equal(bits(gs), bits(ws))
     assert s1["screened_rows"] - s0["screened_rows"] == n
+
+
+@pytest.mark.parametrize("case", ["scaled", "zero_rows", "nonfinite_queries", "nonfinite_data"])
+def test_edge_values(eng, case):
+    """Rows whose norms span six decades (the screen gives the database rows
+    one scale, so small rows keep few digits and their windows widen), zero
+    rows, and non-finite values in queries or data (rows the screen cannot
+    certify go to the exact scan): ids and scores equal to the oracle's."""
+    m, n, d, kk = 300, 2000, 100, 8
+    rng = np.random.default_rng(11)
+    data = mixture(n, d, 9, 0.5, False, 31)
+    q = mixture(m, d, 9, 0.5, False, 32)
+    if case == "scaled":
+        data *= (10.0 ** rng.uniform(-3, 3, n)).astype(np.float32)[:, None]
+        q *= (10.0 ** rng.uniform(-3, 3, m)).astype(np.float32)[:, None]
+    elif case == "zero_rows":
+        q[7] = 0.0
+        data[[11, 12, 500]] = 0.0
+    elif case == "nonfinite_queries":
+        q[5, 3] = np.nan
+        q[17, 0] = np.inf
+        q[100] = -np.inf
+    else:
+        data[40, 2] = np.nan
+    gi, gs = eng.topk(q, data, d, kk)
+    wi, ws = oracle.topk(q, data, d, kk)
+    assert np.array_equal(gi, wi) and np.array_equal(bits(gs), bits(ws))
