@@ -558,6 +558,24 @@ def run_ours(args):
                              "scores_equal": bool(np.array_equal(gsco[:r].view(np.uint32),
                                                                  osc.view(np.uint32))),
                              "oracle": "oracle/oracle.cpp (reference cpu-fused order)"}
+            if mres is not None:
+                # The internal scores of the same labels by the oracle's
+                # restatement (numpy, f64 sums, an f32 matrix product: the
+                # reference agrees with it to rounding).
+                from oracle import metrics as ometrics
+
+                t0 = time.perf_counter()
+                ores = ometrics.internal_scores(x, d, glab, k)
+                o_s = time.perf_counter() - t0
+                out["metrics"]["oracle"] = {
+                    name: float(ores[name]) for name in
+                    ("silhouette", "calinski_harabasz", "davies_bouldin", "objective")}
+                out["metrics"]["rel_delta_vs_oracle"] = {
+                    name: abs(float(mres[name]) - float(ores[name])) / max(abs(float(ores[name])),
+                                                                           1e-300)
+                    for name in ("silhouette", "calinski_harabasz", "davies_bouldin",
+                                 "objective")}
+                out["metrics"]["oracle_s"] = o_s
             if world == 1:
                 out["cpu_baseline"] = cpu
             if tr is not None:
