@@ -450,8 +450,11 @@ def run_ours(args):
         c3 = c3_leg(eng, args, world, rank, local, dist)
     if not args.no_c4:
         c4 = c4_leg(eng, args, world, rank, dist)
+    c5d = None
     if not args.no_c5 and world == 1:
         c5 = c5_leg(eng, args)
+        if args.c5_dedup_n:
+            c5d = c5_dedup_leg(eng, args)
 
     if rank == 0:
         peak, peak_src = peaks()
@@ -546,6 +549,8 @@ def run_ours(args):
             out["c4"] = c4
         if c5:
             out["c5_sweep"] = c5
+        if c5d:
+            out["c5_dedup"] = c5d
         out["clocks"] = clk.summary()
         if not args.no_cpu:
             # Parity of the scored run: the oracle's labels and scores over the
@@ -626,8 +631,16 @@ def gen_c5_rows(n, d, seed=5, tops=64, subs=32, sub_sigma=0.3, row_sigma=0.2, du
     sub = (np.repeat(top, subs, axis=0) +
            np.float32(sub_sigma) * rng.standard_normal((tops * subs, d), dtype=np.float32))
     x = sub[rng.integers(0, tops * subs, n)]
-    x += np.float32(row_sigma) * rng.standard_normal((n, d), dtype=np.float32)
-    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    # The row noise and the normalisation in row chunks (the generator's
+    # stream is drawn in the same order: the same rows as one draw), so that
+    # millions of rows need no full-size temporaries.
+    step = 1 << 17
+    for c0 in range(0, n, step):
+        c1 = min(c0 + step, n)
+        x[c0:c1] += np.float32(row_sigma) * rng.standard_normal((c1 - c0, d), dtype=np.float32)
+    for c0 in range(0, n, step):
+        c1 = min(c0 + step, n)
+        x[c0:c1] /= np.linalg.norm(x[c0:c1], axis=1, keepdims=True)
     nd = int(n * dup_frac)
     dup = rng.choice(n, nd, replace=False)
     x[dup] = x[rng.integers(0, n, nd)] + np.float32(dup_sigma) * rng.standard_normal(
@@ -840,6 +853,57 @@ def c5_leg(eng, args):
                                        "scores) on the host, oracle/"}}
 
 
+def c5_dedup_leg(eng, args):
+    """BASELINE config 5's dedup at full size on one GPU: 2,000,000 x 768 nested-
+    mixture unit rows with 2% near-duplicates, dedup::dedup (crates/emeans-cluster/
+    src/dedup.rs:160-183) at sim_threshold 0.97 and k 10 through the host-array
+    API (the rows copied to the device, the exact kNN self-join on the engine,
+    the grouping stages on the host), after a 50,000-row warm-up call. Parity:
+    the nearest-neighbour similarity (self excluded) of the first rows, bit for
+    bit against the oracle's exact self-join over all rows (the oracle's time
+    on them is the CPU baseline)."""
+    import oracle
+    import emeans_b200 as eb
+
+    n, d, kk = args.c5_dedup_n, 768, 10
+    x = gen_c5_rows(n, d)
+    cfg = eb.DedupConfig(k=kk, sim_threshold=0.97)
+    eng.dedup(x[:50_000], d, cfg=cfg)  # warm-up
+    eng.sync()
+    s0 = eng.stats()
+    t0 = time.perf_counter()
+    res = eng.dedup(x, d, cfg=cfg)
+    dedup_s = time.perf_counter() - t0
+    s1 = eng.stats()
+    threads = os.cpu_count() or 1
+    q = min(args.c5_dedup_check, n)
+    t0 = time.perf_counter()
+    _, wsims = oracle.topk_self_rows(x, d, 0, q, kk, threads=threads)
+    cpu_s = time.perf_counter() - t0
+    want = wsims.reshape(q, kk)[:, 0]
+    return {"workload": f"C5 dedup: {n:,} x {d} nested-mixture unit rows (64 x 32 sub-means, "
+                        "2% near-duplicates, sigma 0.005), sim_threshold 0.97, k 10, host "
+                        "arrays in and out (eb_dedup)",
+            "rows": n, "d": d, "k": kk, "sim_threshold": 0.97,
+            "s_per_dedup": dedup_s,
+            "self_join_useful_tflops": 2.0 * n * n * d / dedup_s / 1e12,
+            "groups": res.n_groups(), "rows_in_groups_of_two_or_more":
+                int(np.sum(res.sizes[res.sizes > 1])),
+            "linked_pairs": res.linked_pairs,
+            "largest_group": int(res.sizes.max()) if res.sizes.size else 0,
+            "self_join_stats": {key: s1[key] - s0[key] for key in
+                                ("screened_rows", "fallback_rows", "rescored_candidates",
+                                 "exact_rows")},
+            "parity": {"rows": q,
+                       "nn_sim_equal": bool(np.array_equal(res.nn_sim[:q].view(np.uint32),
+                                                           want.view(np.uint32))),
+                       "oracle": "FMA-chain exact self-join (oracle/oracle.cpp)"},
+            "cpu_baseline": {"value": q / cpu_s, "unit": "queries/s", "cores": threads,
+                             "kind": "port",
+                             "sample": f"the self-join of the first {q:,} rows against all "
+                                       f"{n:,}, {cpu_s:.1f} s"}}
+
+
 def eb_seed_for(seed, salt, k, restart):
     import emeans_b200 as eb
 
@@ -892,6 +956,10 @@ def main():
     ap.add_argument("--no-c4", action="store_true", help="skip the config-4 kNN leg")
     ap.add_argument("--no-c5", action="store_true", help="skip the config-5 sweep leg")
     ap.add_argument("--c5-n", type=int, default=200_000)
+    ap.add_argument("--c5-dedup-n", type=int, default=2_000_000,
+                    help="rows of the config-5 dedup leg (0: skip it)")
+    ap.add_argument("--c5-dedup-check", type=int, default=1000,
+                    help="config-5 dedup rows whose nearest neighbour the oracle checks")
     ap.add_argument("--c3-n", type=int, default=10_000_000)
     ap.add_argument("--c3-steps", type=int, default=2)
     ap.add_argument("--c3-check", type=int, default=100_000,

@@ -19,9 +19,13 @@
 // rounded products added in column order (no contraction: the library is
 // built with -ffp-contract=off), so every threshold test sees the same bits.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
+#include <exception>
 #include <map>
+#include <mutex>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -53,6 +57,35 @@ float dot(const float* a, const float* b, size_t d) {
   float s = -0.0f;
   for (size_t t = 0; t < d; t++) s += a[t] * b[t];
   return s;
+}
+
+// f(i) for i in [0, count) on the host's threads, items handed out one at a
+// time (their costs differ by orders of magnitude). The first exception
+// thrown by f is rethrown once every thread has stopped.
+template <class F>
+void parallel_for(size_t count, F&& f) {
+  if (count == 0) return;
+  const size_t hw = std::max<unsigned>(1u, std::thread::hardware_concurrency());
+  const size_t nt = std::min<size_t>(std::min<size_t>(hw, 64), count);
+  std::atomic<size_t> next{0};
+  std::exception_ptr err;
+  std::mutex mu;
+  auto work = [&] {
+    for (size_t i = next++; i < count; i = next++) {
+      try {
+        f(i);
+      } catch (...) {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!err) err = std::current_exception();
+        next = count;
+      }
+    }
+  };
+  std::vector<std::thread> ts;
+  for (size_t t = 1; t < nt; t++) ts.emplace_back(work);
+  work();
+  for (auto& t : ts) t.join();
+  if (err) std::rethrow_exception(err);
 }
 
 }  // namespace
@@ -140,15 +173,9 @@ void dedup_with_neighbors(const float* x, size_t n, size_t d, const uint32_t* id
     std::vector<uint32_t> rows;
     uint32_t anchor;
   };
-  std::vector<Group> groups;
-  uint64_t split_components = 0;
-  for (size_t c = 0; c < n; c++) {
-    const uint32_t b = start[c], e = start[c + 1];
-    if (b == e) continue;
-    if (e - b == 1) {
-      groups.push_back({{members[b]}, members[b]});
-      continue;
-    }
+  // The star cover of one component (its members in row order at
+  // members[b, e)), appended to gs.
+  auto cover = [&](uint32_t b, uint32_t e, std::vector<Group>& gs) {
     // Units of the component, by unit root (their rows in row order).
     std::map<uint32_t, std::vector<uint32_t>> units;
     for (uint32_t q = b; q < e; q++) units[unit_of[members[q]]].push_back(members[q]);
@@ -158,7 +185,6 @@ void dedup_with_neighbors(const float* x, size_t n, size_t d, const uint32_t* id
     });
     std::map<uint32_t, bool> taken;
     for (auto& u : units) taken[u.first] = false;
-    const size_t before = groups.size();
     for (uint32_t a : order) {
       const uint32_t au = unit_of[a];
       if (taken[au]) continue;
@@ -181,16 +207,40 @@ void dedup_with_neighbors(const float* x, size_t n, size_t d, const uint32_t* id
         g.insert(g.end(), units[u].begin(), units[u].end());
       }
       std::sort(g.begin(), g.end());
-      groups.push_back({std::move(g), a});
+      gs.push_back({std::move(g), a});
     }
-    if (groups.size() - before > 1) split_components++;
+  };
+  // Components of two or more rows are covered on all host threads at once
+  // (each on its own: the dots of a large component dominate the host
+  // stages), their groups kept per component and then taken in component
+  // order, as one thread would produce them.
+  std::vector<uint32_t> multi;
+  for (size_t c = 0; c < n; c++)
+    if (start[c + 1] - start[c] > 1) multi.push_back((uint32_t)c);
+  std::vector<std::vector<Group>> covered(multi.size());
+  parallel_for(multi.size(), [&](size_t q) {
+    cover(start[multi[q]], start[multi[q] + 1], covered[q]);
+  });
+  std::vector<Group> groups;
+  uint64_t split_components = 0;
+  for (size_t c = 0, q = 0; c < n; c++) {
+    const uint32_t b = start[c], e = start[c + 1];
+    if (b == e) continue;
+    if (e - b == 1) {
+      groups.push_back({{members[b]}, members[b]});
+      continue;
+    }
+    std::vector<Group>& gs = covered[q++];
+    if (gs.size() > 1) split_components++;
+    for (Group& g : gs) groups.push_back(std::move(g));
   }
   std::stable_sort(groups.begin(), groups.end(),
                    [](const Group& p, const Group& q) { return p.rows[0] < q.rows[0]; });
 
   // Representatives: priority, then mean similarity to the other members
-  // (f64, added in member order), then the lowest id.
-  for (size_t gi = 0; gi < groups.size(); gi++) {
+  // (f64, added in member order), then the lowest id; the groups on all host
+  // threads at once (each group's sums in its own order).
+  parallel_for(groups.size(), [&](size_t gi) {
     const std::vector<uint32_t>& g = groups[gi].rows;
     uint32_t rep = g[0];
     if (g.size() > 1) {
@@ -214,7 +264,7 @@ void dedup_with_neighbors(const float* x, size_t n, size_t d, const uint32_t* id
     out->anchors[gi] = groups[gi].anchor;
     out->sizes[gi] = (uint32_t)g.size();
     for (uint32_t r : g) out->group_of[r] = (uint32_t)gi;
-  }
+  });
   for (size_t i = 0; i < n; i++) out->nn_sim[i] = sims[i * kk];
   out->n_groups = groups.size();
   out->linked_pairs = linked;
