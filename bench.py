@@ -450,11 +450,17 @@ def run_ours(args):
         c3 = c3_leg(eng, args, world, rank, local, dist)
     if not args.no_c4:
         c4 = c4_leg(eng, args, world, rank, dist)
-    c5d = None
+    c5d = c5a = None
     if not args.no_c5 and world == 1:
-        c5 = c5_leg(eng, args)
+        # BASELINE config 5's rows once: the sweep (auto_cluster's level 1) on
+        # the first c5_n rows, the incremental add of the rest, dedup on all.
+        x5 = gen_c5_rows(max(args.c5_n, args.c5_dedup_n), 768)
+        best, c5 = c5_leg(eng, args, x5[:args.c5_n])
+        if args.c5_dedup_n > args.c5_n:
+            c5a = c5_add_leg(eng, x5[args.c5_n:args.c5_dedup_n], best)
         if args.c5_dedup_n:
-            c5d = c5_dedup_leg(eng, args)
+            c5d = c5_dedup_leg(eng, args, x5[:args.c5_dedup_n])
+        del x5
 
     if rank == 0:
         peak, peak_src = peaks()
@@ -549,6 +555,8 @@ def run_ours(args):
             out["c4"] = c4
         if c5:
             out["c5_sweep"] = c5
+        if c5a:
+            out["c5_add"] = c5a
         if c5d:
             out["c5_dedup"] = c5d
         out["clocks"] = clk.summary()
@@ -798,7 +806,7 @@ def c4_leg(eng, args, world, rank, dist):
     return res
 
 
-def c5_leg(eng, args):
+def c5_leg(eng, args, x):
     """BASELINE config 5's level-1 sweep path (auto::sweep, crates/emeans-cluster/
     src/auto.rs:455-505) on a C5-shaped sample, one GPU: the rows bound once,
     then for k in (32, 64, 128) two fits each (spherical training with
@@ -809,8 +817,7 @@ def c5_leg(eng, args):
     import oracle
     from oracle import metrics as ometrics
 
-    n, d = args.c5_n, 768
-    x = gen_c5_rows(n, d)
+    n, d = x.shape
     ks, restarts, nepochs, seed, salt = (32, 64, 128), 2, 5.0, 1234, 0
     eng.bind_data(x, d)
     eng.sweep(x, d, ks[:1], nepochs, seed, salt, restarts=1)  # warm-up
@@ -832,7 +839,8 @@ def c5_leg(eng, args):
     cpu_s = time.perf_counter() - t0
     rel = {key: abs(gmet[key] - wmet[key]) / max(abs(wmet[key]), 1e-30)
            for key in ("silhouette", "calinski_harabasz", "davies_bouldin", "objective")}
-    return {"workload": f"C5 level-1 sweep: {n:,} x {d} nested-mixture unit rows (64 x 32 "
+    best = max(res, key=lambda r: r[1]["silhouette"])
+    return best, {"workload": f"C5 level-1 sweep: {n:,} x {d} nested-mixture unit rows (64 x 32 "
                         "sub-means, 2% near-duplicates), k in (32, 64, 128), 2 fits each, "
                         "spherical, 5 epochs, rows bound once (SharedAssigner)",
             "rows": n, "d": d, "ks": list(ks), "restarts": restarts,
@@ -853,7 +861,37 @@ def c5_leg(eng, args):
                                        "scores) on the host, oracle/"}}
 
 
-def c5_dedup_leg(eng, args):
+def c5_add_leg(eng, x_add, best):
+    """BASELINE config 5's incremental add (Hierarchy::add's device work, the
+    new rows' inner-product assignment to the chosen model's centroids) on the
+    rows after the sweep's, through the host-array assign (eb_assign), after a
+    warm-up call; the first rows checked against the oracle bit for bit."""
+    import oracle
+    import emeans_b200 as eb
+
+    k, _, tr, _, _, _ = best
+    m, d = x_add.shape
+    cent = np.ascontiguousarray(tr.centroids, dtype=np.float32)
+    eng.assign(x_add[:20_000], d, cent, eb.IP)  # warm-up
+    t0 = time.perf_counter()
+    lab, sco = eng.assign(x_add, d, cent, eb.IP)
+    add_s = time.perf_counter() - t0
+    q = min(2000, m)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    wl, ws = oracle.top1(x_add[:q].ravel(), d, cent.ravel(), oracle.IP, threads=threads)
+    cpu_s = time.perf_counter() - t0
+    return {"workload": f"C5 incremental add: {m:,} new rows assigned (inner product) to the "
+                        f"chosen model's k={k} centroids, host arrays in and out (eb_assign)",
+            "rows": m, "k": k, "s": add_s, "rows_per_s": m / add_s,
+            "parity": {"rows": q, "labels_equal": bool(np.array_equal(lab[:q], wl)),
+                       "scores_equal": bool(np.array_equal(sco[:q].view(np.uint32),
+                                                           ws.view(np.uint32)))},
+            "cpu_baseline": {"value": q / cpu_s, "unit": "rows/s", "cores": threads,
+                             "kind": "port", "sample": f"the first {q:,} added rows"}}
+
+
+def c5_dedup_leg(eng, args, x):
     """BASELINE config 5's dedup at full size on one GPU: 2,000,000 x 768 nested-
     mixture unit rows with 2% near-duplicates, dedup::dedup (crates/emeans-cluster/
     src/dedup.rs:160-183) at sim_threshold 0.97 and k 10 through the host-array
@@ -865,8 +903,8 @@ def c5_dedup_leg(eng, args):
     import oracle
     import emeans_b200 as eb
 
-    n, d, kk = args.c5_dedup_n, 768, 10
-    x = gen_c5_rows(n, d)
+    n, d = x.shape
+    kk = 10
     cfg = eb.DedupConfig(k=kk, sim_threshold=0.97)
     eng.dedup(x[:50_000], d, cfg=cfg)  # warm-up
     eng.sync()
@@ -955,9 +993,11 @@ def main():
     ap.add_argument("--no-c3", action="store_true", help="skip the config-3 assign leg")
     ap.add_argument("--no-c4", action="store_true", help="skip the config-4 kNN leg")
     ap.add_argument("--no-c5", action="store_true", help="skip the config-5 sweep leg")
-    ap.add_argument("--c5-n", type=int, default=200_000)
+    ap.add_argument("--c5-n", type=int, default=1_600_000,
+                    help="rows of the config-5 sweep (the first rows of the config-5 set)")
     ap.add_argument("--c5-dedup-n", type=int, default=2_000_000,
-                    help="rows of the config-5 dedup leg (0: skip it)")
+                    help="rows of the config-5 set: the rows after the sweep's are added "
+                         "(assigned to the chosen model), dedup runs on all (0: neither)")
     ap.add_argument("--c5-dedup-check", type=int, default=1000,
                     help="config-5 dedup rows whose nearest neighbour the oracle checks")
     ap.add_argument("--c3-n", type=int, default=10_000_000)
