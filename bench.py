@@ -820,7 +820,7 @@ def c5_leg(eng, args, x):
     n, d = x.shape
     ks, restarts, nepochs, seed, salt = (32, 64, 128), 2, 5.0, 1234, 0
     eng.bind_data(x, d)
-    eng.sweep(x, d, ks[:1], nepochs, seed, salt, restarts=1)  # warm-up
+    eng.sweep(x, d, ks, nepochs, seed, salt, restarts=1)  # warm-up: every k's shapes
     eng.sync()
     t0 = time.perf_counter()
     res = eng.sweep(x, d, ks, nepochs, seed, salt, restarts=restarts)
@@ -872,7 +872,7 @@ def c5_add_leg(eng, x_add, best):
     k, _, tr, _, _, _ = best
     m, d = x_add.shape
     cent = np.ascontiguousarray(tr.centroids, dtype=np.float32)
-    eng.assign(x_add[:20_000], d, cent, eb.IP)  # warm-up
+    eng.assign(x_add, d, cent, eb.IP)  # warm-up (the same shape)
     t0 = time.perf_counter()
     lab, sco = eng.assign(x_add, d, cent, eb.IP)
     add_s = time.perf_counter() - t0
