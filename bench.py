@@ -9,7 +9,9 @@ schedule), so the assign sees trained geometry. One step = one full assign
 pass over the 200,000 rows (``Device::top1`` preceded by the centroid norms,
 as ``core::assign_on`` does). With N GPUs the rows are sharded over the ranks
 (strong scaling: the total work is fixed), centroids replicated, and each
-step ends with the labels and scores all-gathered over NCCL to every rank.
+step ends with the labels and scores all-gathered to every rank (one kernel
+pushing each rank's share into every peer's copy of the group's exchange
+region over NVLink).
 
 Reported:
 - value: rows assigned per second (Grows/s), device-resident inputs, CUDA
@@ -166,7 +168,8 @@ def c2_config(args, world):
             "centroids": "trained on the C2 rows, seed 0, nepochs 5 (bit-equal on both arms)",
             "l2_flush": "inputs larger than L2 (rows are 614 MB)",
             "parallelism": f"rows sharded over {world} GPU(s), centroids replicated; "
-                           "labels and scores all-gathered to every rank"}
+                           "labels and scores all-gathered to every rank (peer memory "
+                           "over NVLink)"}
 
 
 def cpu_assign(x, d, cent, budget_s):
@@ -313,17 +316,19 @@ def run_ours(args):
     lo, hi, s = shard(n, world, rank)
 
     # ---- device-resident assign: each rank binds its shard of the rows and
-    # writes its labels and scores into its share of one exchange buffer
-    # (share r = labels then scores of rows r s .. r s + s), which one
-    # all-gather per step gives to every rank.
+    # writes its labels and scores into its share of the group's exchange
+    # region (share r = labels then scores of rows r s .. r s + s, each s4
+    # words), which one all-gather per step, over NVLink peer memory, gives
+    # to every rank.
     m = hi - lo
     xb = eng.bind(x[lo:hi], d)
     cb = eng.upload_f32(cent)
     cn = eng.zeros_f32(k)
-    res_t = torch.zeros(world * 2 * s, dtype=torch.int32, device="cuda")
-    res = eng.wrap(res_t)
-    lab = eng.wrap(res_t[rank * 2 * s:rank * 2 * s + s])
-    sco = eng.wrap(res_t[rank * 2 * s + s:(rank + 1) * 2 * s].view(torch.float32))
+    s4 = (s + 3) // 4 * 4
+    res = eng.group_exchange(world * 2 * s4)
+    xch_mapped, xch_why = eng.group_exchange_info()
+    lab = eng.view(res, rank * 2 * s4, s4, eb.U32)
+    sco = eng.view(res, rank * 2 * s4 + s4, s4, eb.F32)
 
     def step(ev=None):
         eng.row_norms(cb, k, d, cn)
@@ -334,7 +339,7 @@ def run_ours(args):
         if ev:
             ev[1].record(stream)
         if world > 1:
-            eng.group_allgather(res, 2 * s)
+            eng.group_allgather(res, 2 * s4)
 
     # The first call on fresh rows builds their fixed-point copy (kept for later
     # calls on the bound rows, as the reference keeps its per-buffer copy).
@@ -379,9 +384,9 @@ def run_ours(args):
     if dist:
         dist.barrier()
     # Every rank holds all rows' results.
-    allres = res.read().reshape(world, 2 * s)
+    allres = res.read().reshape(world, 2 * s4)
     glab = np.ascontiguousarray(allres[:, :s]).ravel()[:n]
-    gsco = np.ascontiguousarray(allres[:, s:]).ravel().view(np.float32)[:n]
+    gsco = np.ascontiguousarray(allres[:, s4:s4 + s]).ravel().view(np.float32)[:n]
 
     # ---- end to end through Assigner::assign (eb_assign): this rank's shard
     # from pinned host memory, labels and scores back into pinned host memory.
@@ -481,6 +486,7 @@ def run_ours(args):
             "dtype": "f32", "data": "synthetic",
             "config": c2_config(args, world),
             "engine": eng.name(),
+            "exchange": {"peer_memory": xch_mapped, "why_not": xch_why} if world > 1 else None,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
                          "kernel": "k_screen (tcgen05 kind::i8 screen on 16-bit fixed point in "

@@ -156,6 +156,8 @@ def load():
         "eb_set_group_shard": (I, [P, I]),
         "eb_device_allocations": (I, [P, C.POINTER(C.c_uint64)]),
         "eb_group_allgather": (I, [P, P, S]),
+        "eb_group_exchange": (I, [P, S, P]),
+        "eb_group_exchange_info": (I, [P, P, P, S]),
         "eb_test_screen_dead_wait": (I, [P, I]),
         "eb_dedup_with_neighbors": (I, [P, S, S, P, P, S, P, P, P, C.POINTER(_DedupConfig),
                                         C.POINTER(_DedupOut)]),
@@ -506,6 +508,27 @@ class Engine:
         """eb_group_allgather: in-place all-gather of buf's rank shares
         (words_per_rank 32-bit words each); collective over the group."""
         _check(load().eb_group_allgather(self.h, buf.h, int(words_per_rank)))
+
+    def group_exchange(self, words: int) -> "Buffer":
+        """eb_group_exchange: a buffer of ``words`` 32-bit words in the group's
+        exchange region (collective), whose all-gather runs over NVLink peer
+        memory; a plain buffer when alone. The region is the engine's: keep the
+        view only while the group lasts."""
+        return self._new(load().eb_group_exchange, int(words), dtype=U32)
+
+    def group_exchange_info(self):
+        """(mapped, why): whether the exchange region is mapped over peer memory,
+        and the reason the last set-up mapped none."""
+        m = C.c_int()
+        why = C.create_string_buffer(512)
+        _check(load().eb_group_exchange_info(self.h, C.byref(m), why, 512))
+        return bool(m.value), why.value.decode()
+
+    def view(self, buf: "Buffer", offset: int, length: int, dtype: int) -> "Buffer":
+        """A non-owning view of buf's elements offset .. offset + length
+        (4-byte elements; the view's start must be 16-byte aligned)."""
+        return self._new(load().eb_buf_wrap, dtype, buf.ptr + 4 * int(offset), int(length),
+                         dtype=dtype, owner=buf)
 
     def group(self):
         r, w = C.c_int(), C.c_int()

@@ -58,6 +58,10 @@ struct Scratch {
 };
 
 struct Fp16Copy;  // split FP16 screen copy of a bound data set (top1_tc.cu)
+struct PeerExchange;  // a group's symmetric exchange region (nccl.cpp)
+// Words of flags before the data of an exchange region (ready [0, 64), done
+// [64, 128), a block ticket at 128; 1 KB, so the data is 16-byte aligned).
+constexpr size_t kPxFlagWords = 256;
 struct Q8Copy;    // fixed-point screen copy of a bound data set (top1_tc.cu)
 
 }  // namespace eb
@@ -109,6 +113,10 @@ struct eb_engine {
   // shortens it, 1 always, 2 never, 3 splits the top-1 and the scatter-add
   // and sums the ranks' partial sums (eb_set_group_shard).
   int group_shard = 0;
+  // The group's symmetric exchange region (eb_group_exchange), or null, and
+  // why the last set-up did not map one.
+  eb::PeerExchange* px = nullptr;
+  std::string px_why;
   // Optional CUDA-event timing of the top-1 screen kernel (eb_set_kernel_timing):
   // one (start, end) pair per launch since the last eb_screen_timing read,
   // with the rows of that launch.
@@ -225,6 +233,10 @@ void set_last_error(const std::string& msg);
 // buf[r * words ..). Release of the engine's communicator.
 void group_allgather(eb_engine* e, uint32_t* buf, size_t words);
 void group_leave(eb_engine* e);
+// ops.cu: the all-gather over the group's exchange regions (peers_d: every
+// rank's region on this GPU, own included); words per rank, a multiple of 4.
+void px_allgather(eb_engine* e, uint32_t* const* peers_d, int world, int rank, size_t words,
+                  uint32_t epoch);
 // Pack this rank's (labels, scores) slice of len <= soff entries into
 // stage[rank * stride ..) (labels, then scores soff words later; the words
 // past len zero) and unpack every rank's slice after the exchange into

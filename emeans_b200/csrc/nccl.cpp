@@ -10,9 +10,11 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "engine.h"
 
@@ -58,6 +60,144 @@ void nccl_check(ncclResult_t r, const char* what) {
 
 }  // namespace
 
+// The group's symmetric exchange region: on every rank one cudaMalloc of
+// kPxFlagWords flag words and then the data, mapped on every other rank
+// through CUDA IPC, so that a kernel can store into any rank's copy over
+// NVLink (ops.cu's k_px_allgather).
+struct PeerExchange {
+  uint32_t* base = nullptr;       // this rank's region
+  size_t words = 0;               // its data words
+  std::vector<uint32_t*> peers;   // every rank's region as mapped here (own at rank)
+  uint32_t** peers_d = nullptr;   // the same on the device
+  uint32_t epoch = 0;             // calls so far (the flags' values)
+};
+
+namespace {
+
+// The ranks' words w (one per rank) all-gathered; blocking.
+std::vector<uint32_t> allgather_words(eb_engine* e, uint32_t w) {
+  uint32_t* d = nullptr;
+  EB_CUDA(cudaMalloc(&d, (size_t)e->world * 4));
+  std::vector<uint32_t> all(e->world);
+  try {
+    EB_CUDA(cudaMemcpy(d + e->rank, &w, 4, cudaMemcpyHostToDevice));
+    nccl_check(nccl().all_gather(d + e->rank, d, 1, ncclUint32, static_cast<ncclComm_t>(e->comm),
+                                 e->stream),
+               "ncclAllGather");
+    EB_CUDA(cudaStreamSynchronize(e->stream));
+    EB_CUDA(cudaMemcpy(all.data(), d, (size_t)e->world * 4, cudaMemcpyDeviceToHost));
+  } catch (...) {
+    cudaFree(d);
+    throw;
+  }
+  cudaFree(d);
+  return all;
+}
+
+// Closes and frees the region. Collective: every rank's stream has finished
+// its calls and a round over the group has passed before any region goes,
+// so no peer still stores into it.
+void px_free(eb_engine* e) {
+  PeerExchange* px = e->px;
+  if (!px) return;
+  e->px = nullptr;
+  cudaStreamSynchronize(e->stream);
+  try {
+    allgather_words(e, 1);
+  } catch (...) {
+  }
+  for (int q = 0; q < (int)px->peers.size(); q++)
+    if (q != e->rank && px->peers[q]) cudaIpcCloseMemHandle(px->peers[q]);
+  if (px->peers_d) cudaFree(px->peers_d);
+  if (px->base) cudaFree(px->base);
+  delete px;
+}
+
+// Sets up a region of `words` data words on every rank, or none (e->px stays
+// null) when any rank cannot export or map one: the ranks agree on the
+// outcome in two rounds over the group, so all take the same path.
+void px_create(eb_engine* e, size_t words) {
+  auto* px = new PeerExchange;
+  px->words = words;
+  px->peers.assign(e->world, nullptr);
+  const size_t bytes = (kPxFlagWords + words) * 4;
+  cudaIpcMemHandle_t h{};
+  cudaError_t st = cudaMalloc(&px->base, bytes);
+  if (st == cudaSuccess) st = cudaMemsetAsync(px->base, 0, bytes, e->stream);
+  if (st == cudaSuccess) st = cudaStreamSynchronize(e->stream);
+  if (st == cudaSuccess) st = cudaIpcGetMemHandle(&h, px->base);
+  std::string why;
+  if (st != cudaSuccess) {
+    why = std::string("exporting the region: ") + cudaGetErrorString(st);
+    cudaGetLastError();
+  }
+  // Round 1: every rank's handle and whether it has one (32 words each).
+  constexpr size_t kRec = 32;
+  static_assert(sizeof(cudaIpcMemHandle_t) <= (kRec - 1) * 4, "IPC handle size");
+  std::vector<uint32_t> rec(kRec, 0);
+  std::memcpy(rec.data(), &h, sizeof h);
+  rec[kRec - 1] = st == cudaSuccess ? 1u : 0u;
+  uint32_t* d = nullptr;
+  EB_CUDA(cudaMalloc(&d, kRec * 4 * (size_t)e->world));
+  std::vector<uint32_t> all(kRec * (size_t)e->world);
+  try {
+    EB_CUDA(cudaMemcpy(d + kRec * (size_t)e->rank, rec.data(), kRec * 4, cudaMemcpyHostToDevice));
+    nccl_check(nccl().all_gather(d + kRec * (size_t)e->rank, d, kRec, ncclUint32,
+                                 static_cast<ncclComm_t>(e->comm), e->stream),
+               "ncclAllGather");
+    EB_CUDA(cudaStreamSynchronize(e->stream));
+    EB_CUDA(cudaMemcpy(all.data(), d, all.size() * 4, cudaMemcpyDeviceToHost));
+  } catch (...) {
+    cudaFree(d);
+    throw;
+  }
+  cudaFree(d);
+  bool ok = true;
+  for (int q = 0; q < e->world; q++) ok = ok && all[kRec * (size_t)q + kRec - 1] == 1u;
+  if (!ok && why.empty()) why = "a peer could not export its region";
+  // Round 2: whether every peer's region could be mapped here.
+  uint32_t mapped = ok ? 1u : 0u;
+  if (ok) {
+    for (int q = 0; q < e->world; q++) {
+      if (q == e->rank) {
+        px->peers[q] = px->base;
+        continue;
+      }
+      cudaIpcMemHandle_t hq;
+      std::memcpy(&hq, all.data() + kRec * (size_t)q, sizeof hq);
+      void* p = nullptr;
+      const cudaError_t so = cudaIpcOpenMemHandle(&p, hq, cudaIpcMemLazyEnablePeerAccess);
+      if (so != cudaSuccess) {
+        why = "mapping rank " + std::to_string(q) + "'s region: " + cudaGetErrorString(so);
+        cudaGetLastError();
+        mapped = 0;
+        break;
+      }
+      px->peers[q] = static_cast<uint32_t*>(p);
+    }
+  }
+  if (mapped && cudaMalloc(&px->peers_d, sizeof(uint32_t*) * (size_t)e->world) == cudaSuccess) {
+    if (cudaMemcpy(px->peers_d, px->peers.data(), sizeof(uint32_t*) * (size_t)e->world,
+                   cudaMemcpyHostToDevice) != cudaSuccess)
+      mapped = 0;
+  } else {
+    mapped = 0;
+  }
+  cudaGetLastError();
+  std::vector<uint32_t> agree = allgather_words(e, mapped);
+  bool all_mapped = true;
+  for (uint32_t v : agree) all_mapped = all_mapped && v == 1u;
+  e->px = px;
+  if (!all_mapped) {
+    px_free(e);  // every rank frees: NCCL stays the path
+    e->px_why = why.empty() ? "a peer could not map the regions" : why;
+  } else {
+    e->px_why.clear();
+  }
+}
+
+}  // namespace
+
 void group_allgather(eb_engine* e, uint32_t* buf, size_t words) {
   ensure(e->comm != nullptr, "engine is not in a group");
   nccl_check(nccl().all_gather(buf + (size_t)e->rank * words, buf, words, ncclUint32,
@@ -67,6 +207,7 @@ void group_allgather(eb_engine* e, uint32_t* buf, size_t words) {
 
 void group_leave(eb_engine* e) {
   if (e->comm) {
+    px_free(e);
     nccl().destroy(static_cast<ncclComm_t>(e->comm));
     e->comm = nullptr;
   }
@@ -137,7 +278,12 @@ extern "C" int eb_group_allgather(eb_engine* e, eb_buf* b, size_t words_per_rank
       cudaGetDevice(&prev);
       if (prev != e->device) EB_CUDA(cudaSetDevice(e->device));
       try {
-        eb::group_allgather(e, static_cast<uint32_t*>(b->ptr), words_per_rank);
+        eb::PeerExchange* px = e->px;
+        if (px && b->ptr == px->base + eb::kPxFlagWords && words_per_rank % 4 == 0 &&
+            words_per_rank * (size_t)e->world <= px->words)
+          eb::px_allgather(e, px->peers_d, e->world, e->rank, words_per_rank, ++px->epoch);
+        else
+          eb::group_allgather(e, static_cast<uint32_t*>(b->ptr), words_per_rank);
       } catch (...) {
         if (prev >= 0 && prev != e->device) cudaSetDevice(prev);
         throw;
@@ -150,6 +296,57 @@ extern "C" int eb_group_allgather(eb_engine* e, eb_buf* b, size_t words_per_rank
     eb::set_last_error(err.what());
     return err.code;
   }
+}
+
+extern "C" int eb_group_exchange(eb_engine* e, size_t words, eb_buf** out) {
+  try {
+    eb::ensure(e != nullptr && out != nullptr, "engine and out are required");
+    eb::ensure(words > 0 && words < ((size_t)1 << 40), "words must be in 1 .. 2^40 - 1");
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != e->device) EB_CUDA(cudaSetDevice(e->device));
+    struct Restore {
+      int prev, dev;
+      ~Restore() {
+        if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+      }
+    } restore{prev, e->device};
+    // The flag words hold 64 ranks; larger groups take NCCL.
+    if (e->world > 1 && e->world <= 64 && e->comm && (!e->px || e->px->words < words)) {
+      eb::px_free(e);
+      eb::px_create(e, words);
+    }
+    if (e->world > 1 && e->px) {
+      auto* b = new eb_buf;
+      b->ptr = e->px->base + eb::kPxFlagWords;
+      b->len = words;
+      b->dtype = EB_U32;
+      b->owned = false;
+      *out = b;
+    } else {
+      *out = eb::new_buf(e, EB_U32, words);
+    }
+    eb::set_last_error("");
+    return EB_OK;
+  } catch (const eb::Error& err) {
+    eb::set_last_error(err.what());
+    return err.code;
+  }
+}
+
+extern "C" int eb_group_exchange_info(eb_engine* e, int* mapped, char* why, size_t cap) {
+  if (!e || !mapped) {
+    eb::set_last_error("engine and mapped are required");
+    return EB_INVALID_ARGUMENT;
+  }
+  *mapped = e->px != nullptr ? 1 : 0;
+  if (why && cap) {
+    const std::string& w = e->px_why;
+    const size_t len = std::min(cap - 1, w.size());
+    std::memcpy(why, w.data(), len);
+    why[len] = 0;
+  }
+  return EB_OK;
 }
 
 extern "C" int eb_engine_group(eb_engine* e, int* rank, int* world) {

@@ -1075,3 +1075,109 @@ void reduce_partials(eb_engine* e, const uint32_t* stage, size_t stride, int wor
 }
 
 }  // namespace eb
+
+// ---- the group's peer-memory all-gather (a compute step's results pushed
+// straight into every rank's copy of a symmetric exchange region over
+// NVLink; nccl.cpp sets the regions up).
+
+namespace eb {
+namespace {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t px_now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Flag v has reached epoch (32-bit wrap-around order).
+__device__ __forceinline__ bool px_reached(uint32_t v, uint32_t epoch) {
+  return (int32_t)(v - epoch) >= 0;
+}
+constexpr uint64_t kPxWaitNs = 2000000000ull;  // every wait gives up after 2 s
+
+// Region of rank q (peers[q], mapped on this GPU): flag words, then data.
+// ready[r] (word r) and done[r] (word 64 + r) are written by rank r with the
+// call's epoch; word 128 counts this kernel's finished blocks.
+// 1. Block 0 posts ready to every peer; every block waits (bounded) until
+//    every peer has posted it: all ranks have reached this call, so no rank
+//    still reads a region's previous contents.
+// 2. The blocks push this rank's share (data words rank * words .. + words)
+//    into the same place of every peer's region (16-byte stores).
+// 3. Each block fences its stores at system scope and takes a ticket; the
+//    last block posts done to every peer and waits (bounded) until every
+//    peer has posted done here: then every share is in this rank's region.
+// A wait that runs out sets ST_WAIT_TIMEOUT (the next sync reports it) and
+// the block returns.
+__global__ void __launch_bounds__(256) k_px_allgather(uint32_t* const* __restrict__ peers,
+                                                      int world, int rank, long words,
+                                                      uint32_t epoch, uint32_t* status) {
+  pdl_wait();
+  uint32_t* const mine = peers[rank];
+  __shared__ int ok, last;
+  if (blockIdx.x == 0 && (int)threadIdx.x < world && (int)threadIdx.x != rank)
+    st_release_sys(peers[threadIdx.x] + rank, epoch);
+  if (threadIdx.x == 0) {
+    ok = 1;
+    const uint64_t t0 = px_now_ns();
+    for (int q = 0; q < world && ok; q++) {
+      if (q == rank) continue;
+      while (!px_reached(ld_acquire_sys(mine + q), epoch)) {
+        if (px_now_ns() - t0 > kPxWaitNs) {
+          ok = 0;
+          break;
+        }
+      }
+    }
+    if (!ok) atomicOr(status, ST_WAIT_TIMEOUT);
+  }
+  __syncthreads();
+  if (!ok) return;
+  const long off = kPxFlagWords + (long)rank * words;
+  const long nvec = words / 4;  // words is a multiple of 4 (the host checks)
+  const uint4* src = reinterpret_cast<const uint4*>(mine + off);
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
+       i += (long)gridDim.x * blockDim.x) {
+    const uint4 v = src[i];
+    for (int q = 0; q < world; q++)
+      if (q != rank) reinterpret_cast<uint4*>(peers[q] + off)[i] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(mine + 128, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  mine[128] = 0;  // the ticket of the next call
+  for (int q = 0; q < world; q++)
+    if (q != rank) st_release_sys(peers[q] + 64 + rank, epoch);
+  const uint64_t t0 = px_now_ns();
+  for (int q = 0; q < world; q++) {
+    if (q == rank) continue;
+    while (!px_reached(ld_acquire_sys(mine + 64 + q), epoch)) {
+      if (px_now_ns() - t0 > kPxWaitNs) {
+        atomicOr(status, ST_WAIT_TIMEOUT);
+        return;
+      }
+    }
+  }
+}
+
+}  // namespace
+
+void px_allgather(eb_engine* e, uint32_t* const* peers_d, int world, int rank, size_t words,
+                  uint32_t epoch) {
+  const size_t nvec = words / 4;
+  const unsigned grid = (unsigned)std::min<size_t>(
+      std::max<size_t>(1, (nvec + 255) / 256), (size_t)e->num_sms);
+  launch_pdl(e, k_px_allgather, grid, 256, 0, peers_d, world, rank, (long)words, epoch,
+             e->d_status);
+  EB_LAUNCH("peer all-gather");
+}
+
+}  // namespace eb

@@ -291,6 +291,24 @@ int eb_set_group_shard(eb_engine* e, int mode);
  * A no-op on an engine that is not in a group. */
 int eb_group_allgather(eb_engine* e, eb_buf* b, size_t words_per_rank);
 
+/* No counterpart in the reference. Collective: all ranks call it with the
+ * same words. A buffer of `words` 32-bit words in the group's exchange
+ * region: one allocation per rank, mapped on every other rank through CUDA
+ * IPC. eb_group_allgather on this buffer (the whole of it, words_per_rank a
+ * multiple of 4) pushes each rank's share straight into every peer's copy
+ * over NVLink in one kernel (an entry and an exit round of flags, every wait
+ * bounded: a peer that does not arrive within 2 s is reported as EB_ERROR at
+ * the next sync) instead of NCCL. The region is the engine's: the buffer is a
+ * view, valid until a larger region is requested or the group is left, and
+ * eb_buf_free releases only the view. Alone, or when any rank cannot map the
+ * regions (the ranks agree), a plain device buffer (NCCL serves the
+ * all-gather). */
+int eb_group_exchange(eb_engine* e, size_t words, eb_buf** out);
+/* No counterpart in the reference. Whether the engine's exchange region is
+ * mapped (1) or its all-gathers go through NCCL (0), and in `why` (cap bytes,
+ * NUL-terminated; may be null) the reason the last set-up mapped none. */
+int eb_group_exchange_info(eb_engine* e, int* mapped, char* why, size_t cap);
+
 /* Device::topk over a database sharded across a group (knn_self over several
  * GPUs, crates/emeans-cluster/src/knn.rs:17-64): every rank passes the same m
  * queries and its own shard, rows shard_offset .. shard_offset + n_shard of an

@@ -5,7 +5,8 @@ ranks a sharded database with eb_topk_group; both must equal, bit for bit, a
 lone engine's results on the same GPU. In group mode 3 (the top-1 and the
 scatter-add split, partial sums exchanged) every rank must hold the same
 model, within rounding of the lone engine's; and a sharded assign with its
-labels and scores all-gathered (eb_group_allgather) equals one engine's."""
+labels and scores all-gathered (eb_group_allgather) equals one engine's, over
+NCCL and through the group's exchange region (peer memory over NVLink)."""
 
 import datetime
 import os
@@ -92,7 +93,37 @@ def main():
     assert np.array_equal(lab.read(0, n), sl), f"rank {rank}: gathered labels differ"
     assert np.array_equal(sco.read(0, n).view(np.uint32), ss.view(np.uint32)), \
         f"rank {rank}: gathered scores differ"
-    del xb, cb, cn, lab, sco
+    # The same sharded assign through the group's exchange region: labels and
+    # scores of rank r's rows in its share (labels then scores), pushed into
+    # every rank's copy over peer memory by eb_group_allgather.
+    s4 = (s + 3) // 4 * 4
+    res = group.group_exchange(world * 2 * s4)
+    mapped, why = group.group_exchange_info()
+    assert mapped, f"rank {rank}: the exchange region is not mapped: {why}"
+    plab = group.view(res, rank * 2 * s4, s4, eb.U32)
+    psco = group.view(res, rank * 2 * s4 + s4, s4, eb.F32)
+    xs = group.bind(x[lo:hi], d)  # this rank's rows: its selection starts at 0
+    group.top1(xs, d, None, range(0, hi - lo), cb, cn, k, eb.L2, plab, psco)
+    for step in range(3):  # successive calls: the exchange's flags move on
+        group.group_allgather(res, 2 * s4)
+    got = res.read().reshape(world, 2, s4)
+    glab = np.concatenate([got[q, 0, :min(s, n - q * s)] for q in range(world)])
+    gsco = np.concatenate([got[q, 1, :min(s, n - q * s)] for q in range(world)]).view(np.float32)
+    assert np.array_equal(glab, sl), f"rank {rank}: exchanged labels differ"
+    assert np.array_equal(gsco.view(np.uint32), ss.view(np.uint32)), \
+        f"rank {rank}: exchanged scores differ"
+    # Every rank's share, written with its own pattern, reaches every rank.
+    words = 1000
+    res2 = group.group_exchange(world * words)
+    mine = group.view(res2, rank * words, words, eb.U32)
+    mine.write(0, (np.arange(words, dtype=np.uint64) * 2654435761 + rank).astype(np.uint32))
+    group.group_allgather(res2, words)
+    got2 = res2.read().reshape(world, words)
+    for q in range(world):
+        want = (np.arange(words, dtype=np.uint64) * 2654435761 + q).astype(np.uint32)
+        assert np.array_equal(got2[q], want), f"rank {rank}: share {q} did not arrive"
+    group.sync()
+    del xb, xs, cb, cn, lab, sco, plab, psco, mine, res, res2
     group.close()
     solo.close()
     dist.barrier()
