@@ -198,3 +198,23 @@ def test_one_row_and_argument_errors():
     bad[0] = 99
     with pytest.raises(eb.EngineError, match="past the rows"):
         eb.dedup_with_neighbors(x, 8, bad, sims, kk)
+
+
+def test_matches_the_restatement_with_large_components():
+    """Clustered rows (a few hundred per mean, unit norm) at a threshold that
+    links most of a cluster: components of hundreds of rows, whose star covers
+    and representatives the library computes on several host threads at once,
+    whole and split into several stars; every field equal to the
+    restatement's."""
+    rng = np.random.default_rng(17)
+    d, means, per = 24, 6, 250
+    mu = rng.standard_normal((means, d)).astype(np.float32)
+    x = np.repeat(mu, per, axis=0) + np.float32(0.12) * rng.standard_normal(
+        (means * per, d)).astype(np.float32)
+    x = (x / np.linalg.norm(x, axis=1, keepdims=True)).astype(np.float32)
+    x = x[rng.permutation(x.shape[0])]
+    got = run_both(x, d, eb.DedupConfig(k=10, sim_threshold=0.95))
+    assert got.sizes.max() >= 50  # the case exercises large components
+    # A stricter representative threshold splits the components' star covers.
+    got = run_both(x, d, eb.DedupConfig(k=10, sim_threshold=0.95, rep_threshold=0.985))
+    assert got.split_components >= 2 and got.sizes.max() >= 50
