@@ -1104,7 +1104,8 @@ constexpr uint64_t kPxWaitNs = 2000000000ull;  // every wait gives up after 2 s
 
 // Region of rank q (peers[q], mapped on this GPU): flag words, then data.
 // ready[r] (word r) and done[r] (word 64 + r) are written by rank r with the
-// call's epoch; word 128 counts this kernel's finished blocks.
+// call's epoch; word 128 counts this kernel's finished blocks, word 129 is
+// set by a block whose wait ran out.
 // 1. Block 0 posts ready to every peer; every block waits (bounded) until
 //    every peer has posted it: all ranks have reached this call, so no rank
 //    still reads a region's previous contents.
@@ -1113,8 +1114,11 @@ constexpr uint64_t kPxWaitNs = 2000000000ull;  // every wait gives up after 2 s
 // 3. Each block fences its stores at system scope and takes a ticket; the
 //    last block posts done to every peer and waits (bounded) until every
 //    peer has posted done here: then every share is in this rank's region.
-// A wait that runs out sets ST_WAIT_TIMEOUT (the next sync reports it) and
-// the block returns.
+// A wait that runs out sets ST_WAIT_TIMEOUT (the next sync reports it). A
+// block whose entry wait ran out pushes nothing but still takes its ticket
+// (so the count is whole for the next call), and then the last block posts
+// no done: the peers' exit waits run out and report it too, rather than
+// reading shares that were never sent.
 __global__ void __launch_bounds__(256) k_px_allgather(uint32_t* const* __restrict__ peers,
                                                       int world, int rank, long words,
                                                       uint32_t epoch, uint32_t* status) {
@@ -1135,14 +1139,16 @@ __global__ void __launch_bounds__(256) k_px_allgather(uint32_t* const* __restric
         }
       }
     }
-    if (!ok) atomicOr(status, ST_WAIT_TIMEOUT);
+    if (!ok) {
+      atomicOr(status, ST_WAIT_TIMEOUT);
+      atomicOr(mine + 129, 1u);
+    }
   }
   __syncthreads();
-  if (!ok) return;
   const long off = kPxFlagWords + (long)rank * words;
   const long nvec = words / 4;  // words is a multiple of 4 (the host checks)
   const uint4* src = reinterpret_cast<const uint4*>(mine + off);
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; ok && i < nvec;
        i += (long)gridDim.x * blockDim.x) {
     const uint4 v = src[i];
     for (int q = 0; q < world; q++)
@@ -1154,6 +1160,7 @@ __global__ void __launch_bounds__(256) k_px_allgather(uint32_t* const* __restric
   __syncthreads();
   if (!last || threadIdx.x != 0) return;
   mine[128] = 0;  // the ticket of the next call
+  if (atomicExch(mine + 129, 0u) != 0u) return;  // a block's wait ran out: no done
   for (int q = 0; q < world; q++)
     if (q != rank) st_release_sys(peers[q] + 64 + rank, epoch);
   const uint64_t t0 = px_now_ns();
