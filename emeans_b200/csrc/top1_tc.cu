@@ -2424,7 +2424,8 @@ Fp16Copy* bound_copy(eb_engine* e, eb_buf* xbuf, const float* x, size_t n, size_
     e->device_allocs += 4;
     xbuf->f16 = f;
     if (st != cudaSuccess) {
-      drop_f16(xbuf);  // no room for the copy: convert per pass instead
+      free_copy(f);  // no room for the copy: convert per pass instead
+      xbuf->f16 = nullptr;
       cudaGetLastError();
     } else if (n) {
       launch_pdl(e, k_prep_rows, (unsigned)((n + wpb - 1) / wpb), wpb * 32, 0, x, (long)n,
@@ -2794,10 +2795,10 @@ void screen_products(eb_engine* e, const float* x, size_t n, size_t d, eb_buf* x
   float* xnrm = e->scratch_get<float>("tc_xnrm", chunk);
   float* pmax = e->scratch_get<float>("pr_max", 2 * (size_t)max_parts * chunk);
   uint32_t* pcol = e->scratch_get<uint32_t>("pr_col", 2 * (size_t)max_parts * chunk);
-  Fp16Copy* cache = nullptr;
-  if (xbuf && xbuf->f16 && xbuf->f16->version == xbuf->version && xbuf->f16->n == n &&
-      xbuf->f16->d == d)
-    cache = xbuf->f16;
+  // A bound data set keeps its split FP16 copy (made by the first product
+  // call, kept until the buffer is written or freed): later calls on it,
+  // such as a sweep's internal scores, read it in place.
+  Fp16Copy* cache = bound_copy(e, xbuf, x, n, d);
 
   ScreenParams P{};
   P.k = (int)k;
