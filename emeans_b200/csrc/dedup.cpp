@@ -59,6 +59,47 @@ float dot(const float* a, const float* b, size_t d) {
   return s;
 }
 
+// out[l] = dot(a, b[l], d) for l < 8, computed together: eight independent
+// chains, each the same rounded products added in column order from -0 as
+// dot's (no contraction), so each result has dot's bits.
+void dots8(const float* a, const float* const* b, size_t d, float* out) {
+  float s0 = -0.0f, s1 = -0.0f, s2 = -0.0f, s3 = -0.0f;
+  float s4 = -0.0f, s5 = -0.0f, s6 = -0.0f, s7 = -0.0f;
+  const float *b0 = b[0], *b1 = b[1], *b2 = b[2], *b3 = b[3];
+  const float *b4 = b[4], *b5 = b[5], *b6 = b[6], *b7 = b[7];
+  for (size_t t = 0; t < d; t++) {
+    const float v = a[t];
+    s0 += v * b0[t];
+    s1 += v * b1[t];
+    s2 += v * b2[t];
+    s3 += v * b3[t];
+    s4 += v * b4[t];
+    s5 += v * b5[t];
+    s6 += v * b6[t];
+    s7 += v * b7[t];
+  }
+  out[0] = s0;
+  out[1] = s1;
+  out[2] = s2;
+  out[3] = s3;
+  out[4] = s4;
+  out[5] = s5;
+  out[6] = s6;
+  out[7] = s7;
+}
+
+// dot(a, rows[i]) for every i, eight at a time (the last group padded with a).
+void dots_many(const float* a, const std::vector<const float*>& rows, size_t d, float* out) {
+  const float* b[8];
+  float o[8];
+  for (size_t i0 = 0; i0 < rows.size(); i0 += 8) {
+    const size_t m = std::min<size_t>(8, rows.size() - i0);
+    for (size_t l = 0; l < 8; l++) b[l] = l < m ? rows[i0 + l] : a;
+    dots8(a, b, d, o);
+    for (size_t l = 0; l < m; l++) out[i0 + l] = o[l];
+  }
+}
+
 // f(i) for i in [0, count) on the host's threads, items handed out one at a
 // time (their costs differ by orders of magnitude). The first exception
 // thrown by f is rethrown once every thread has stopped.
@@ -190,16 +231,24 @@ void dedup_with_neighbors(const float* x, size_t n, size_t d, const uint32_t* id
       if (taken[au]) continue;
       taken[au] = true;
       std::vector<uint32_t> g = units[au];
-      // Each untaken unit joins when every one of its rows fits the anchor.
+      // Each untaken unit joins when every one of its rows fits the anchor
+      // (time rule, and dot >= rep_threshold); the rows' dots with the anchor
+      // are computed eight at a time.
+      std::vector<const float*> cand;
+      for (auto& u : units)
+        if (!taken[u.first])
+          for (uint32_t r : u.second) cand.push_back(row(r));
+      std::vector<float> dv(cand.size());
+      dots_many(row(a), cand, d, dv.data());
       std::vector<uint32_t> joins;
+      size_t ci = 0;
       for (auto& u : units) {
         if (taken[u.first]) continue;
         bool all = true;
-        for (uint32_t r : u.second)
-          if (!(time_ok(r, a) && dot(row(r), row(a), d) >= rep_t)) {
-            all = false;
-            break;
-          }
+        for (uint32_t r : u.second) {
+          const float v = dv[ci++];  // every row's dot, in the order computed
+          all = all && time_ok(r, a) && v >= rep_t;
+        }
         if (all) joins.push_back(u.first);
       }
       for (uint32_t u : joins) {
@@ -247,10 +296,17 @@ void dedup_with_neighbors(const float* x, size_t n, size_t d, const uint32_t* id
       float best_p = -INFINITY;
       double best_m = -INFINITY;
       rep = 0xFFFFFFFFu;
+      std::vector<const float*> others;
+      std::vector<float> dv(g.size());
       for (uint32_t a : g) {
-        double sum = -0.0;
+        // The other members' dots with a (eight at a time), added in f64 in
+        // member order.
+        others.clear();
         for (uint32_t bb : g)
-          if (bb != a) sum += (double)dot(row(a), row(bb), d);
+          if (bb != a) others.push_back(row(bb));
+        dots_many(row(a), others, d, dv.data());
+        double sum = -0.0;
+        for (size_t i = 0; i < others.size(); i++) sum += (double)dv[i];
         const double mean = sum / (double)(g.size() - 1);
         const float p = priority ? priority[a] : 0.0f;
         if (p > best_p || (p == best_p && mean > best_m)) {
