@@ -25,6 +25,7 @@
 #include <exception>
 #include <map>
 #include <mutex>
+#include <system_error>
 #include <thread>
 #include <unordered_map>
 #include <vector>
@@ -123,7 +124,11 @@ void parallel_for(size_t count, F&& f) {
     }
   };
   std::vector<std::thread> ts;
-  for (size_t t = 1; t < nt; t++) ts.emplace_back(work);
+  // A thread the system refuses leaves its share to the threads that started.
+  try {
+    for (size_t t = 1; t < nt; t++) ts.emplace_back(work);
+  } catch (const std::system_error&) {
+  }
   work();
   for (auto& t : ts) t.join();
   if (err) std::rethrow_exception(err);
