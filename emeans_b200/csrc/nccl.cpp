@@ -113,11 +113,10 @@ void px_free(eb_engine* e) {
   delete px;
 }
 
-// Sets up a region of `words` data words on every rank, or none (e->px stays
-// null) when any rank cannot export or map one: the ranks agree on the
-// outcome in two rounds over the group, so all take the same path.
-void px_create(eb_engine* e, size_t words) {
-  auto* px = new PeerExchange;
+// Exports this rank's region, maps every peer's and reports whether every
+// rank mapped all of them (two rounds over the group; `why` says what failed
+// here). Everything it opened or allocated is recorded in px.
+bool px_setup(eb_engine* e, PeerExchange* px, size_t words, std::string& why) {
   px->words = words;
   px->peers.assign(e->world, nullptr);
   const size_t bytes = (kPxFlagWords + words) * 4;
@@ -126,7 +125,6 @@ void px_create(eb_engine* e, size_t words) {
   if (st == cudaSuccess) st = cudaMemsetAsync(px->base, 0, bytes, e->stream);
   if (st == cudaSuccess) st = cudaStreamSynchronize(e->stream);
   if (st == cudaSuccess) st = cudaIpcGetMemHandle(&h, px->base);
-  std::string why;
   if (st != cudaSuccess) {
     why = std::string("exporting the region: ") + cudaGetErrorString(st);
     cudaGetLastError();
@@ -187,6 +185,29 @@ void px_create(eb_engine* e, size_t words) {
   std::vector<uint32_t> agree = allgather_words(e, mapped);
   bool all_mapped = true;
   for (uint32_t v : agree) all_mapped = all_mapped && v == 1u;
+  return all_mapped;
+}
+
+// Sets up a region of `words` data words on every rank, or none (e->px stays
+// null) when any rank cannot export or map one: the ranks agree on the
+// outcome in two rounds over the group, so all take the same path.
+void px_create(eb_engine* e, size_t words) {
+  auto* px = new PeerExchange;
+  std::string why;
+  bool all_mapped = false;
+  try {
+    all_mapped = px_setup(e, px, words, why);
+  } catch (...) {
+    // An error before the ranks agreed: no kernel has stored into any
+    // region, so this rank's mappings and memory go at once.
+    for (int q = 0; q < (int)px->peers.size(); q++)
+      if (q != e->rank && px->peers[q]) cudaIpcCloseMemHandle(px->peers[q]);
+    if (px->peers_d) cudaFree(px->peers_d);
+    if (px->base) cudaFree(px->base);
+    delete px;
+    cudaGetLastError();
+    throw;
+  }
   e->px = px;
   if (!all_mapped) {
     px_free(e);  // every rank frees: NCCL stays the path
