@@ -526,8 +526,15 @@ class Engine:
 
     def view(self, buf: "Buffer", offset: int, length: int, dtype: int) -> "Buffer":
         """A non-owning view of buf's elements offset .. offset + length
-        (4-byte elements; the view's start must be 16-byte aligned)."""
-        return self._new(load().eb_buf_wrap, dtype, buf.ptr + 4 * int(offset), int(length),
+        (4-byte elements; the view's start must be 16-byte aligned). A range
+        past buf's end is refused (INVALID_ARGUMENT), as the C calls refuse
+        one."""
+        offset, length = int(offset), int(length)
+        if offset < 0 or length < 0 or offset + length > len(buf):
+            raise EngineError(INVALID_ARGUMENT,
+                              f"view {offset} .. {offset + length} is outside the buffer's "
+                              f"{len(buf)} elements")
+        return self._new(load().eb_buf_wrap, dtype, buf.ptr + 4 * offset, length,
                          dtype=dtype, owner=buf)
 
     def group(self):

@@ -59,3 +59,19 @@ def test_load_fails_loudly_when_library_missing(monkeypatch, tmp_path):
     monkeypatch.setattr(emeans_b200, "HERE", str(tmp_path))
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         emeans_b200.load()
+
+
+def test_view_outside_its_buffer_is_refused():
+    """Engine.view checks its range before any C call: a view past the
+    buffer's end, or a negative one, is INVALID_ARGUMENT."""
+
+    class FakeBuffer:
+        ptr = 4096
+
+        def __len__(self):
+            return 64
+
+    for offset, length in [(60, 8), (-4, 4), (0, 65), (8, -1)]:
+        with pytest.raises(emeans_b200.EngineError) as err:
+            emeans_b200.Engine.view(None, FakeBuffer(), offset, length, emeans_b200.U32)
+        assert err.value.code == emeans_b200.INVALID_ARGUMENT
